@@ -1,0 +1,457 @@
+#!/usr/bin/env python
+"""Decode throughput of the Qwen3-0.6B-shaped Q8_0 model on B200.
+
+Workload: the full 28-layer model with a tied
+151936 x 1024 Q8_0 embedding/head and seeded synthetic Q8_0 weights, a
+64-token prompt (ids uniform in [0, 151936)), then greedy batch-1 decode.  A
+step is one decode token (embedding -> 28 layers -> output_norm -> head ->
+argmax); K steps cover positions 64 .. 64+K-1 (K = 256 reproduces config 2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl flock|reference]
+
+`value`: tokens/s with the token fed back on the device (one CUDA graph per
+token, no host round trip), CUDA-event timed, max over ranks.
+`e2e`:   the same decode through the public API, one Model.step([id]) per
+token (4-byte H2D of the id, 4-byte D2H of the next id, host loop).
+N > 1: layer-range pipeline (4 layers + head on rank 0, the rest split
+evenly), hidden state passed with NCCL send/recv; per-token work is fixed,
+so scaling is "strong".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = "decode tok/s (bs1, Qwen3-0.6B-shape Q8_0)"
+PROMPT = 64
+SEED = 0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ----------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return int(vis.split(",")[local_rank])
+        except (ValueError, IndexError):
+            pass
+    return local_rank
+
+
+def peaks() -> dict:
+    p = os.path.join(HERE, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+def traffic_from_profile() -> float | None:
+    """dram bytes per head launch from the committed ncu summary, if any."""
+    p = os.path.join(HERE, "profiles", "gemv_lm_head_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("dram_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+# ----------------------------------------------------------------- bytes
+def bytes_per_token(shape, keys: float) -> float:
+    """Algorithmic HBM bytes of one decode token: every Q8_0 weight byte
+    (1.0625 B/weight), the f32 K/V rows read, plus the token's small vectors."""
+    h, f, q, kv = shape.hidden, shape.ffn, shape.n_heads * shape.head_dim, \
+        shape.n_kv_heads * shape.head_dim
+    layer_w = (q * h + 2 * kv * h + h * q + 2 * f * h + h * f) * 1.0625
+    head_w = shape.vocab * h * 1.0625
+    kv_bytes = 2 * kv * 4 * keys
+    return shape.n_layers * (layer_w + kv_bytes) + head_w
+
+
+# ------------------------------------------------------------ cpu baseline
+def cpu_baseline(m, shape, n_tokens: int = 2) -> dict:
+    """The oracle (C restatement of layer_ref.ts / model.ts) decoding
+    n_tokens at position 64 on all host cores."""
+    import oracle
+    cores = len(os.sched_getaffinity(0))
+    oracle.set_threads(cores)
+    cfg = dict(hidden=shape.hidden, n_heads=shape.n_heads, n_kv_heads=shape.n_kv_heads,
+               head_dim=shape.head_dim, ffn=shape.ffn)
+    kvw = shape.n_kv_heads * shape.head_dim
+    layers = []
+    for i, w in enumerate(m.layers):
+        L = oracle.RefLayer(w, cfg, PROMPT + n_tokens + 1)
+        L.fill_cache(np.random.default_rng(i).standard_normal(PROMPT * kvw).astype(np.float32),
+                     np.random.default_rng(100 + i).standard_normal(PROMPT * kvw).astype(np.float32))
+        layers.append(L)
+    tok = 1
+    t0 = time.perf_counter()
+    for _ in range(n_tokens):
+        h = oracle.embed(m.embd["packed"], [tok], shape.hidden)
+        for L in layers:
+            h = L.forward(h, 1)
+        tok, _, _ = oracle.head(h, m.output_norm, m.embd["packed"], shape.vocab, shape.hidden)
+    dt = time.perf_counter() - t0
+    return {"value": n_tokens / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n_tokens} decode tokens of the 28-layer model at position {PROMPT} "
+                      f"(oracle/flock_oracle.c, OpenMP over rows, {cores} threads)"}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    """--impl reference: the reference's CPU path (its strict-f32 TS oracle,
+    restated in C: Deno is absent) on this config, on the host cores."""
+    if rank != 0:
+        return
+    from flock_b200 import synth
+    import oracle
+    shape = synth.QWEN3_06B
+    m = synth.model(SEED, shape)
+    cores = len(os.sched_getaffinity(0))
+    oracle.set_threads(cores)
+    cfg = dict(hidden=shape.hidden, n_heads=shape.n_heads, n_kv_heads=shape.n_kv_heads,
+               head_dim=shape.head_dim, ffn=shape.ffn)
+    kvw = shape.n_kv_heads * shape.head_dim
+    n_layers = shape.n_layers
+    # a step is one decoder layer of one decode token; every 28th also runs the
+    # head, so 28 steps are one full token (bounded so K=256 stays ~minutes)
+    total = args.warmup + args.steps
+    layers = []
+    for i, w in enumerate(m.layers):
+        L = oracle.RefLayer(w, cfg, PROMPT + total // n_layers + 2)
+        L.fill_cache(np.random.default_rng(i).standard_normal(PROMPT * kvw).astype(np.float32),
+                     np.random.default_rng(100 + i).standard_normal(PROMPT * kvw).astype(np.float32))
+        layers.append(L)
+    h = oracle.embed(m.embd["packed"], [1], shape.hidden)
+
+    def step(s):
+        nonlocal h
+        h = layers[s % n_layers].forward(h, 1)
+        if s % n_layers == n_layers - 1:
+            tok, _, _ = oracle.head(h, m.output_norm, m.embd["packed"], shape.vocab, shape.hidden)
+            h = oracle.embed(m.embd["packed"], [tok], shape.hidden)
+
+    for s in range(args.warmup):
+        step(s)
+    t0 = time.perf_counter()
+    for s in range(args.warmup, total):
+        step(s)
+    dt = time.perf_counter() - t0
+    tok_s = (args.steps / n_layers) / dt
+    sample = (f"{args.steps} decoder-layer steps ({args.steps / n_layers:.2f} tokens) of the "
+              f"28-layer model at position {PROMPT}, oracle/flock_oracle.c on {cores} threads")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1000 / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config 2: Qwen3-0.6B-shape Q8_0, 28 layers, tied 151936x1024 "
+                               "head, prompt 64, greedy bs1 decode", "seed": SEED},
+        "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference's own CPU path is TypeScript under Deno; Deno and every JS engine "
+                "are absent here, so its C restatement (same operation order) is timed",
+    }), flush=True)
+
+
+# --------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="flock", choices=["flock", "reference"])
+    ap.add_argument("--attention", default="fast", choices=["fast", "exact"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    from flock_b200 import synth
+    from flock_b200.layer import QWEN3_06B
+    from flock_b200.lib import get_device
+    from flock_b200.model import Model
+    from flock_b200 import ops
+
+    shape = synth.QWEN3_06B
+    t_gen = time.perf_counter()
+    m = synth.model(SEED, shape)
+    log(f"[rank {rank}] synthetic model generated in {time.perf_counter() - t_gen:.1f}s")
+    max_keys = PROMPT + args.warmup + args.steps + 8
+    cfg = QWEN3_06B.with_(max_keys=max(max_keys, 512), attention=args.attention)
+    prompt = synth.uniform_ids(SEED, "prompt", PROMPT, shape.vocab)
+    dev = get_device(local)
+    pk = peaks()
+
+    if world > 1:
+        run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk)
+        return
+
+    M = Model.create(dev, m, cfg)
+    first = M.step(prompt)                # prefill (untimed)
+    M.decode_device(args.warmup)          # warm-up steps
+    M.rewind(PROMPT)
+    M.set_token(first)
+    dev.sync()
+
+    clk = Clocks(gpu_index(local))
+    clk.start()
+    dev.timer_start()
+    ids_dev = M.decode_device(args.steps)
+    ms = dev.timer_stop()
+    clocks = clk.stop()
+    tok_s = args.steps / (ms / 1000.0)
+    log(f"decode: {args.steps} tokens in {ms:.2f} ms -> {tok_s:.1f} tok/s; clocks {clocks}")
+
+    # end to end through the public API, host loop
+    e2e = None
+    if not args.no_e2e:
+        M.rewind(PROMPT)
+        prev = first
+        ids_api = []
+        dev.timer_start()
+        for _ in range(args.steps):
+            prev = M.step([prev])
+            ids_api.append(prev)
+        ms_e2e = dev.timer_stop()
+        e2e = {"value": args.steps / (ms_e2e / 1000.0), "unit": "tok/s",
+               "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+               "ids_match_device_loop": ids_api == ids_dev.tolist()}
+        log(f"e2e: {e2e}")
+
+    # roofline of the dominant kernel: the Q8_0 GEMV, as its largest launch
+    # (the tied 151936 x 1024 LM head), timed alone with CUDA events
+    embd_t = M._keep[1]
+    head_ms = ops.matvec_timed(dev, embd_t, 1, 50)
+    head_bytes = shape.vocab * shape.hidden * 1.0625 + 4 * shape.hidden + 4 * shape.vocab
+    achieved = head_bytes / (head_ms / 1000.0) / 1e9
+    traffic = traffic_from_profile()
+    avg_keys = PROMPT + (args.steps - 1) / 2.0 + 1
+    tok_bytes = bytes_per_token(shape, avg_keys)
+    token_gbs = tok_bytes * tok_s / 1e9
+    launches_per_token = 1 + shape.n_layers * (5 if args.attention == "fast" else 6) + 2
+
+    out = {
+        "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config 2: Qwen3-0.6B-shape Q8_0, 28 layers, tied 151936x1024 "
+                               "head, prompt 64 then greedy bs1 decode at positions 64..",
+                   "seed": SEED, "prompt": PROMPT, "attention": args.attention,
+                   "l2": "inputs larger than L2: 692 MB of weights streamed per token",
+                   "timing": "CUDA events around K device-fed decode steps"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
+                     "kernel": "k_gemv<Q8,R2,STORE> on the 151936x1024 head, 165.3 MB per launch",
+                     "ms_per_launch": head_ms, "peak_src": pk["src"]},
+        "token_roofline": {"achieved": token_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                           "frac": token_gbs / pk["hbm_gbs"],
+                           "bytes_per_token": tok_bytes, "avg_keys": avg_keys},
+        "clocks": clocks,
+        "gpu_launches": launches_per_token * args.steps,
+    }
+    if e2e:
+        out["e2e"] = e2e
+    if not args.no_cpu_baseline:
+        try:
+            out["cpu_baseline"] = cpu_baseline(m, shape)
+        except Exception as e:  # reported, not fatal
+            out["cpu_baseline"] = {"value": None, "error": str(e)}
+    print(json.dumps(out), flush=True)
+
+
+def stage_layers(n_layers: int, world: int) -> list[tuple[int, int]]:
+    """4 layers on rank 0, the remaining split evenly (earlier ranks take the
+    remainder), as BASELINE config 2 asks."""
+    if world == 1:
+        return [(0, n_layers)]
+    first = min(4, n_layers - (world - 1))
+    rest = n_layers - first
+    base, extra = divmod(rest, world - 1)
+    out, at = [(0, first)], first
+    for r in range(world - 1):
+        c = base + (1 if r < extra else 0)
+        out.append((at, at + c))
+        at += c
+    return out
+
+
+def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
+    import ctypes
+    import torch.distributed as dist
+    from datetime import timedelta
+    from flock_b200 import _abi
+    from flock_b200.layer import upload_layer
+    from flock_b200.lib import GpuTensor
+    from flock_b200.model import Model
+
+    dist.init_process_group("gloo", timeout=timedelta(seconds=120))
+    uid = np.zeros(128, np.uint8)
+    if rank == 0:
+        _abi.call("flock_comm_unique_id", _abi.ptr(uid, _abi._u8p))
+    obj = [uid.tobytes()]
+    dist.broadcast_object_list(obj, src=0)
+    uid = np.frombuffer(obj[0], np.uint8).copy()
+    comm = ctypes.c_void_p()
+    _abi.call("flock_comm_init", dev.handle, world, rank, _abi.ptr(uid, _abi._u8p), 60000,
+              ctypes.byref(comm))
+    a, b = stage_layers(shape.n_layers, world)[rank]
+    layer_ts = [upload_layer(dev, m.layers[i]) for i in range(a, b)]
+    if rank == 0:
+        embd = GpuTensor.from_packed(dev, m.embd["packed"], m.embd["rows"], m.embd["cols"])
+        onorm = GpuTensor.from_f32(dev, m.output_norm)
+        M = Model.from_tensors(dev, cfg, shape.vocab, b - a, layer_ts, embd, onorm)
+    else:
+        M = Model.from_tensors(dev, cfg, shape.vocab, b - a, layer_ts, None, None)
+    nxt = ctypes.c_int32()
+
+    def pstep(ids, n, sync):
+        p = None
+        if ids is not None:
+            arr = np.ascontiguousarray(ids, np.int32)
+            pstep.keep = arr
+            p = _abi.ptr(arr, _abi._i32p)
+        _abi.call("flock_pipeline_step", M.handle, comm, p, n, sync, ctypes.byref(nxt))
+
+    pstep(prompt if rank == 0 else None, PROMPT, 1)
+    first = nxt.value
+    for _ in range(args.warmup):
+        pstep(None, 1, 0)
+    dev.sync()
+    M.rewind(PROMPT)
+    if rank == 0:
+        M.set_token(first)
+    dist.barrier()
+    clk = Clocks(gpu_index(local))
+    clk.start()
+    dev.timer_start()
+    for _ in range(args.steps):
+        pstep(None, 1, 0)
+    ms = dev.timer_stop()
+    clocks = clk.stop()
+    t = np.array([ms], np.float64)
+    import torch
+    tt = torch.tensor(t)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms_max = float(tt[0])
+    # e2e: host loop through the API, id read back on rank 0 every token
+    M.rewind(PROMPT)
+    if rank == 0:
+        M.set_token(first)
+    dist.barrier()
+    dev.timer_start()
+    prev = first
+    for _ in range(args.steps):
+        pstep([prev] if rank == 0 else None, 1, 1)
+        prev = nxt.value
+    ms_e2e = dev.timer_stop()
+    tt = torch.tensor([ms_e2e], dtype=torch.float64)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms_e2e = float(tt[0])
+    if rank == 0:
+        tok_s = args.steps / (ms_max / 1000.0)
+        out = {
+            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "config 2 pipelined: contiguous layer ranges "
+                                   f"{stage_layers(shape.n_layers, world)}, hidden state over "
+                                   "NCCL send/recv", "seed": SEED, "prompt": PROMPT,
+                       "attention": args.attention, "parallelism": f"pp{world}",
+                       "l2": "inputs larger than L2"},
+            "clocks": clocks,
+            "e2e": {"value": args.steps / (ms_e2e / 1000.0), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": (1 + shape.n_layers * (5 if args.attention == "fast" else 6) + 2)
+            * args.steps,
+        }
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    _abi.lib().flock_comm_free(comm)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

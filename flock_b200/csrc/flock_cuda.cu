@@ -1,0 +1,1110 @@
+// libflock_cuda.so: devices, tensors, launch planning and the op-level,
+// Layer and range entry points of include/flock_cuda.h.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "attn_fast.cuh"
+#include "flock_internal.h"
+#include "gemv.cuh"
+#include "ops.cuh"
+
+namespace flock {
+
+static thread_local std::string g_err;
+
+void set_error(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+}
+
+int DBuf::alloc(size_t n) {
+  release();
+  if (n == 0) n = 16;
+  cudaError_t e = cudaMalloc(&p, n);
+  if (e != cudaSuccess) {
+    p = nullptr;
+    set_error("cudaMalloc(%zu) failed: %s", n, cudaGetErrorString(e));
+    return FLOCK_E_NOMEM;
+  }
+  bytes = n;
+  return FLOCK_OK;
+}
+
+void DBuf::release() {
+  if (p) cudaFree(p);
+  p = nullptr;
+  bytes = 0;
+}
+
+const char* const kTensorNames[W_COUNT] = {
+    "attn_q.weight",   "attn_k.weight",    "attn_v.weight",      "attn_output.weight",
+    "ffn_gate.weight", "ffn_up.weight",    "ffn_down.weight",    "attn_norm.weight",
+    "attn_q_norm.weight", "attn_k_norm.weight", "ffn_norm.weight"};
+
+// ------------------------------------------------------------- launching
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_ex(cudaStream_t st, void (*k)(KArgs...), dim3 grid, dim3 block,
+                             size_t smem, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
+template <int QT, int R, int EPI, int MX>
+static cudaError_t gemv_go(flock_dev* d, const GemvArgs& a, int ctas, bool pdl) {
+  auto k = k_gemv<QT, R, EPI, MX>;
+  const size_t smem = gemv_smem_bytes(a.K);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  return launch_ex(d->stream, k, dim3(ctas, a.n_tokens), dim3(GEMV_THREADS), smem, pdl, a);
+}
+
+int gemv_grid(flock_dev* d, int total_groups) {
+  int ctas = (total_groups + GEMV_WARPS - 1) / GEMV_WARPS;
+  const int cap = 2 * d->sm_count;
+  return ctas < 1 ? 1 : (ctas > cap ? cap : ctas);
+}
+
+int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl) {
+  if (a.K % 32 != 0 || a.K > 24576) {
+    set_error("matvec cols %d must be a multiple of 32 and <= 24576", a.K);
+    return FLOCK_E_ARG;
+  }
+  const int M = (a.K / 32 + 31) / 32;
+  const int MX = M >= 2 ? 2 : 1;
+  int rows = 0;
+  for (int s = 0; s < a.nseg; s++) rows += a.seg[s].rows;
+  int R = 1;
+  if (EPI == EPI_SWIGLU || EPI == EPI_ARGMAX) R = 2;
+  else if (EPI == EPI_STORE && rows >= 16384) R = 2;
+  int groups;
+  if (EPI == EPI_SWIGLU) groups = a.seg[0].rows;
+  else {
+    groups = 0;
+    for (int s = 0; s < a.nseg; s++) groups += (a.seg[s].rows + R - 1) / R;
+  }
+  const int ctas = gemv_grid(d, groups);
+  cudaError_t e = cudaErrorInvalidValue;
+#define GO(qt, r, epi, mx) e = gemv_go<qt, r, epi, mx>(d, a, ctas, pdl)
+  if (QT == QT_Q8) {
+    switch (EPI) {
+      case EPI_STORE:
+        if (R == 2) { if (MX == 1) GO(QT_Q8, 2, EPI_STORE, 1); else GO(QT_Q8, 2, EPI_STORE, 2); }
+        else { if (MX == 1) GO(QT_Q8, 1, EPI_STORE, 1); else GO(QT_Q8, 1, EPI_STORE, 2); }
+        break;
+      case EPI_RESIDUAL:
+        if (MX == 1) GO(QT_Q8, 1, EPI_RESIDUAL, 1); else GO(QT_Q8, 1, EPI_RESIDUAL, 2);
+        break;
+      case EPI_SWIGLU:
+        if (MX == 1) GO(QT_Q8, 2, EPI_SWIGLU, 1); else GO(QT_Q8, 2, EPI_SWIGLU, 2);
+        break;
+      case EPI_ARGMAX:
+        if (MX == 1) GO(QT_Q8, 2, EPI_ARGMAX, 1); else GO(QT_Q8, 2, EPI_ARGMAX, 2);
+        break;
+    }
+  } else {
+    if (EPI != EPI_STORE) {
+      set_error("Q4_0 matvec supports the plain store epilogue only");
+      return FLOCK_E_UNSUPPORTED;
+    }
+    if (R == 2) { if (MX == 1) GO(QT_Q4, 2, EPI_STORE, 1); else GO(QT_Q4, 2, EPI_STORE, 2); }
+    else { if (MX == 1) GO(QT_Q4, 1, EPI_STORE, 1); else GO(QT_Q4, 1, EPI_STORE, 2); }
+  }
+#undef GO
+  if (e != cudaSuccess) {
+    set_error("matvec launch failed: %s", cudaGetErrorString(e));
+    return FLOCK_E_CUDA;
+  }
+  return FLOCK_OK;
+}
+
+static GemvSeg seg_of(const flock_tensor* t, float* out, int out_stride) {
+  GemvSeg s;
+  s.qs = t->qs.as<uint8_t>();
+  s.sc = t->sc.as<uint16_t>();
+  s.out = out;
+  s.rows = (int)t->rows;
+  s.sc_stride = t->sc_stride;
+  s.out_stride = out_stride;
+  return s;
+}
+
+static void pf_add(PrefetchList& pf, const flock_tensor* t) {
+  if (!t) return;
+  if (pf.n + 2 > 4) return;
+  pf.ptr[pf.n] = t->qs.as<uint8_t>();
+  pf.bytes[pf.n] = t->qs.bytes & ~(uint64_t)15;
+  pf.n++;
+  pf.ptr[pf.n] = t->sc.as<uint8_t>();
+  pf.bytes[pf.n] = t->sc.bytes & ~(uint64_t)15;
+  pf.n++;
+}
+
+// ------------------------------------------------------------- workspace
+
+int Workspace::alloc(const flock_layer_config& c) {
+  P = c.max_prefill < 1 ? 1 : c.max_prefill;
+  H = c.hidden;
+  nH = c.n_heads;
+  nKV = c.n_kv_heads;
+  hd = c.head_dim;
+  F = c.ffn;
+  const size_t f = sizeof(float);
+  FLOCK_TRY(h.alloc((size_t)P * H * f));
+  FLOCK_TRY(q.alloc((size_t)P * nH * hd * f));
+  FLOCK_TRY(k.alloc((size_t)P * nKV * hd * f));
+  FLOCK_TRY(v.alloc((size_t)P * nKV * hd * f));
+  FLOCK_TRY(qn.alloc((size_t)P * nH * hd * f));
+  FLOCK_TRY(attn.alloc((size_t)P * nH * hd * f));
+  FLOCK_TRY(act.alloc((size_t)P * F * f));
+  FLOCK_TRY(attn_part.alloc((size_t)nH * attn_splits * (hd + 2) * f));
+  FLOCK_TRY(attn_count.alloc((size_t)nKV * 4));
+  FLOCK_CK(cudaMemset(attn_count.p, 0, attn_count.bytes));
+  return FLOCK_OK;
+}
+
+// --------------------------------------------------------------- layer
+
+static int check_cfg(const flock_layer_config& c) {
+  if (c.head_dim != 128) {
+    set_error("head_dim %d: the kernels are built for head_dim 128", c.head_dim);
+    return FLOCK_E_UNSUPPORTED;
+  }
+  if (c.hidden % 32 || c.ffn % 32 || c.hidden < 32 || c.ffn < 32) {
+    set_error("hidden %d and ffn %d must be multiples of 32", c.hidden, c.ffn);
+    return FLOCK_E_ARG;
+  }
+  if (c.n_kv_heads < 1 || c.n_heads % c.n_kv_heads) {
+    set_error("n_heads %d must be a multiple of n_kv_heads %d", c.n_heads, c.n_kv_heads);
+    return FLOCK_E_ARG;
+  }
+  if (c.n_heads / c.n_kv_heads > 4) {
+    set_error("GQA group size %d > 4 is not supported", c.n_heads / c.n_kv_heads);
+    return FLOCK_E_UNSUPPORTED;
+  }
+  if (c.max_keys < 1 || c.max_prefill < 1) {
+    set_error("max_keys and max_prefill must be >= 1");
+    return FLOCK_E_ARG;
+  }
+  if (c.attention == FLOCK_ATTN_EXACT && c.max_keys > 48 * 1024) {
+    set_error("exact decode attention holds every score on chip: max_keys %d > 49152; use "
+              "FLOCK_ATTN_FAST", c.max_keys);
+    return FLOCK_E_UNSUPPORTED;
+  }
+  return FLOCK_OK;
+}
+
+int layer_init(flock_layer* L, flock_dev* dev, const flock_layer_config& cfg, Workspace* ws,
+               int* shared_ctl) {
+  FLOCK_TRY(check_cfg(cfg));
+  L->dev = dev;
+  L->cfg = cfg;
+  const size_t kv = (size_t)cfg.max_keys * cfg.n_kv_heads * cfg.head_dim * sizeof(float);
+  FLOCK_TRY(L->kcache.alloc(kv));
+  FLOCK_TRY(L->vcache.alloc(kv));
+  std::vector<float> inv(cfg.head_dim / 2);
+  // layer.ts:180 invFreqOf: fr(1 / base^(2j/headDim)), on the host.
+  for (int j = 0; j < cfg.head_dim / 2; j++)
+    inv[j] = (float)(1.0 / std::pow(cfg.rope_base, (double)(2 * j) / (double)cfg.head_dim));
+  FLOCK_TRY(L->inv_freq.alloc(inv.size() * sizeof(float)));
+  FLOCK_CK(cudaMemcpy(L->inv_freq.p, inv.data(), inv.size() * sizeof(float),
+                      cudaMemcpyHostToDevice));
+  if (shared_ctl) {
+    L->ctl = shared_ctl;
+  } else {
+    FLOCK_TRY(L->ctl_own.alloc(2 * sizeof(int)));
+    FLOCK_CK(cudaMemset(L->ctl_own.p, 0, 2 * sizeof(int)));
+    L->ctl = L->ctl_own.as<int>();
+  }
+  if (ws) {
+    L->ws = ws;
+  } else {
+    FLOCK_TRY(L->ws_own.alloc(cfg));
+    L->ws = &L->ws_own;
+    L->owns_ws = true;
+  }
+  return FLOCK_OK;
+}
+
+int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_next, bool pdl) {
+  flock_dev* d = L->dev;
+  Workspace* ws = L->ws;
+  const flock_layer_config& c = L->cfg;
+  const int qw = c.n_heads * c.head_dim, kvw = c.n_kv_heads * c.head_dim;
+  const float* g_attn = L->w[W_ATTN_NORM]->data.as<float>();
+  const float* g_q = L->w[W_Q_NORM]->data.as<float>();
+  const float* g_k = L->w[W_K_NORM]->data.as<float>();
+  const float* g_ffn = L->w[W_FFN_NORM]->data.as<float>();
+
+  // 1. attn_norm + q/k/v projections (one launch, three outputs)
+  {
+    GemvArgs a = {};
+    a.seg[0] = seg_of(L->w[W_Q], ws->q.as<float>(), qw);
+    a.seg[1] = seg_of(L->w[W_K], ws->k.as<float>(), kvw);
+    a.seg[2] = seg_of(L->w[W_V], ws->v.as<float>(), kvw);
+    a.nseg = 3;
+    a.K = c.hidden;
+    a.n_tokens = n;
+    a.x = ws->h.as<float>();
+    a.x_stride = c.hidden;
+    a.norm_gain = g_attn;
+    a.eps = c.eps;
+    if (advance) {
+      a.ctl = L->ctl;
+      a.ctl_n = n;
+    }
+    pf_add(a.pf, L->w[W_O]);
+    FLOCK_TRY(launch_gemv(d, QT_Q8, EPI_STORE, a, pdl));
+  }
+  // 2-3. q/k norm + RoPE + KV append, attention
+  if (n == 1 && c.attention == FLOCK_ATTN_FAST) {
+    AttnFastArgs a = {};
+    a.q = ws->q.as<float>();
+    a.k = ws->k.as<float>();
+    a.v = ws->v.as<float>();
+    a.q_norm = g_q;
+    a.k_norm = g_k;
+    a.inv_freq = L->inv_freq.as<float>();
+    a.kcache = L->kcache.as<float>();
+    a.vcache = L->vcache.as<float>();
+    a.ctl = L->ctl;
+    a.out = ws->attn.as<float>();
+    a.part = ws->attn_part.as<float>();
+    a.count = ws->attn_count.as<uint32_t>();
+    a.n_heads = c.n_heads;
+    a.n_kv_heads = c.n_kv_heads;
+    a.head_dim = c.head_dim;
+    a.splits = ws->attn_splits;
+    a.eps = c.eps;
+    a.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
+    a.chunk_cap = (c.max_keys + a.splits - 1) / a.splits;
+    pf_add(a.pf, L->w[W_GATE]);
+    const size_t smem = attn_fast_smem(a.chunk_cap);
+    static bool attr = false;
+    if (!attr) {
+      FLOCK_CK(cudaFuncSetAttribute(k_attn_decode_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    200 * 1024));
+      attr = true;
+    }
+    FLOCK_CK(launch_ex(d->stream, k_attn_decode_fast, dim3(c.n_kv_heads, a.splits),
+                       dim3(ATTN_FAST_THREADS), smem, pdl, a));
+  } else {
+    QkArgs qa = {};
+    qa.q = ws->q.as<float>();
+    qa.k = ws->k.as<float>();
+    qa.v = ws->v.as<float>();
+    qa.q_norm = g_q;
+    qa.k_norm = g_k;
+    qa.inv_freq = L->inv_freq.as<float>();
+    qa.qn = ws->qn.as<float>();
+    qa.kcache = L->kcache.as<float>();
+    qa.vcache = L->vcache.as<float>();
+    qa.ctl = L->ctl;
+    qa.n_tokens = n;
+    qa.n_heads = c.n_heads;
+    qa.n_kv_heads = c.n_kv_heads;
+    qa.head_dim = c.head_dim;
+    qa.eps = c.eps;
+    qa.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
+    pf_add(qa.pf, L->w[W_GATE]);
+    FLOCK_CK(launch_ex(d->stream, k_qk_norm_rope_append, dim3(n * (c.n_heads + c.n_kv_heads)),
+                       dim3(128), 0, pdl, qa));
+    AttnArgs aa = {};
+    aa.q = ws->qn.as<float>();
+    aa.kcache = L->kcache.as<float>();
+    aa.vcache = L->vcache.as<float>();
+    aa.out = ws->attn.as<float>();
+    aa.ctl = L->ctl;
+    aa.n_tokens = n;
+    aa.n_heads = c.n_heads;
+    aa.n_kv_heads = c.n_kv_heads;
+    aa.head_dim = c.head_dim;
+    pf_add(aa.pf, L->w[W_UP]);
+    if (n == 1) {
+      const size_t smem = (size_t)c.max_keys * sizeof(float);
+      static bool attr = false;
+      if (!attr) {
+        FLOCK_CK(cudaFuncSetAttribute(k_attn_decode_exact,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr = true;
+      }
+      FLOCK_CK(launch_ex(d->stream, k_attn_decode_exact, dim3(c.n_heads), dim3(256), smem, pdl,
+                         aa));
+    } else {
+      FLOCK_CK(launch_ex(d->stream, k_attn_prefill_exact, dim3(c.n_heads, n), dim3(128), 0, pdl,
+                         aa));
+    }
+  }
+  // 4. o_proj + residual, in place on h
+  {
+    GemvArgs a = {};
+    a.seg[0] = seg_of(L->w[W_O], ws->h.as<float>(), c.hidden);
+    a.nseg = 1;
+    a.K = qw;
+    a.n_tokens = n;
+    a.x = ws->attn.as<float>();
+    a.x_stride = qw;
+    a.res = ws->h.as<float>();
+    a.res_stride = c.hidden;
+    pf_add(a.pf, L->w[W_DOWN]);
+    FLOCK_TRY(launch_gemv(d, QT_Q8, EPI_RESIDUAL, a, pdl));
+  }
+  // 5. ffn_norm + gate/up + SwiGLU
+  {
+    GemvArgs a = {};
+    a.seg[0] = seg_of(L->w[W_GATE], ws->act.as<float>(), c.ffn);
+    a.seg[1] = seg_of(L->w[W_UP], ws->act.as<float>(), c.ffn);
+    a.nseg = 2;
+    a.K = c.hidden;
+    a.n_tokens = n;
+    a.x = ws->h.as<float>();
+    a.x_stride = c.hidden;
+    a.norm_gain = g_ffn;
+    a.eps = c.eps;
+    a.pf = pf_next;
+    FLOCK_TRY(launch_gemv(d, QT_Q8, EPI_SWIGLU, a, pdl));
+  }
+  // 6. down + residual, in place on h
+  {
+    GemvArgs a = {};
+    a.seg[0] = seg_of(L->w[W_DOWN], ws->h.as<float>(), c.hidden);
+    a.nseg = 1;
+    a.K = c.ffn;
+    a.n_tokens = n;
+    a.x = ws->act.as<float>();
+    a.x_stride = c.ffn;
+    a.res = ws->h.as<float>();
+    a.res_stride = c.hidden;
+    FLOCK_TRY(launch_gemv(d, QT_Q8, EPI_RESIDUAL, a, pdl));
+  }
+  return FLOCK_OK;
+}
+
+}  // namespace flock
+
+using namespace flock;
+
+// ================================================================ C ABI
+
+extern "C" {
+
+const char* flock_last_error(void) { return g_err.c_str(); }
+const char* flock_version(void) { return "flock_b200 0.1 sm_100a"; }
+
+int flock_dev_open(int ordinal, flock_dev** out) {
+  if (!out) return FLOCK_E_ARG;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    set_error("no CUDA device");
+    return FLOCK_E_CUDA;
+  }
+  if (ordinal < 0 || ordinal >= n) {
+    set_error("device %d out of range (%d devices)", ordinal, n);
+    return FLOCK_E_ARG;
+  }
+  FLOCK_CK(cudaSetDevice(ordinal));
+  cudaDeviceProp prop;
+  FLOCK_CK(cudaGetDeviceProperties(&prop, ordinal));
+  if (prop.major != 10) {
+    set_error("device %d is sm_%d%d; this library is built for sm_100a (B200)", ordinal,
+              prop.major, prop.minor);
+    return FLOCK_E_UNSUPPORTED;
+  }
+  flock_dev* d = new flock_dev();
+  d->ordinal = ordinal;
+  d->sm_count = prop.multiProcessorCount;
+  FLOCK_CK(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+  FLOCK_CK(cudaEventCreate(&d->t0));
+  FLOCK_CK(cudaEventCreate(&d->t1));
+  int rc;
+  if ((rc = d->am_val.alloc(4096 * 4)) || (rc = d->am_idx.alloc(4096 * 4)) ||
+      (rc = d->am_count.alloc(16)) || (rc = d->am_best_val.alloc(16)) ||
+      (rc = d->am_best_idx.alloc(16))) {
+    delete d;
+    return rc;
+  }
+  FLOCK_CK(cudaMemset(d->am_count.p, 0, 16));
+  *out = d;
+  return FLOCK_OK;
+}
+
+int flock_dev_close(flock_dev* d) {
+  if (!d) return FLOCK_OK;
+  cudaSetDevice(d->ordinal);
+  cudaStreamSynchronize(d->stream);
+  cudaEventDestroy(d->t0);
+  cudaEventDestroy(d->t1);
+  cudaStreamDestroy(d->stream);
+  delete d;
+  return FLOCK_OK;
+}
+
+int flock_dev_sync(flock_dev* d) {
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  return FLOCK_OK;
+}
+
+int flock_dev_sm_count(flock_dev* d, int* out) {
+  *out = d->sm_count;
+  return FLOCK_OK;
+}
+
+int flock_dev_timer_start(flock_dev* d) {
+  FLOCK_CK(cudaEventRecord(d->t0, d->stream));
+  return FLOCK_OK;
+}
+
+int flock_dev_timer_stop(flock_dev* d, float* ms) {
+  FLOCK_CK(cudaEventRecord(d->t1, d->stream));
+  FLOCK_CK(cudaEventSynchronize(d->t1));
+  FLOCK_CK(cudaEventElapsedTime(ms, d->t0, d->t1));
+  return FLOCK_OK;
+}
+
+// ---------------------------------------------------------------- repack
+
+int flock_repack_q8(const uint8_t* packed, int64_t rows, int64_t cols, uint8_t* qs,
+                    uint8_t* scales) {
+  if (!packed || !qs || !scales || rows < 0 || cols % 32) {
+    set_error("repack_q8: cols %lld must be a multiple of 32", (long long)cols);
+    return FLOCK_E_ARG;
+  }
+  const int64_t nb = cols / 32;
+  for (int64_t r = 0; r < rows; r++)
+    for (int64_t b = 0; b < nb; b++) {
+      const uint8_t* src = packed + (r * nb + b) * 34;
+      scales[(r * nb + b) * 2] = src[0];
+      scales[(r * nb + b) * 2 + 1] = src[1];
+      memcpy(qs + r * cols + b * 32, src + 2, 32);
+    }
+  return FLOCK_OK;
+}
+
+int flock_repack_q4(const uint8_t* packed, int64_t rows, int64_t cols, uint8_t* qs,
+                    uint8_t* scales) {
+  if (!packed || !qs || !scales || rows < 0 || cols % 32) {
+    set_error("repack_q4: cols %lld must be a multiple of 32", (long long)cols);
+    return FLOCK_E_ARG;
+  }
+  const int64_t nb = cols / 32;
+  for (int64_t r = 0; r < rows; r++)
+    for (int64_t b = 0; b < nb; b++) {
+      const uint8_t* src = packed + (r * nb + b) * 18;
+      scales[(r * nb + b) * 2] = src[0];
+      scales[(r * nb + b) * 2 + 1] = src[1];
+      memcpy(qs + (r * nb + b) * 16, src + 2, 16);
+    }
+  return FLOCK_OK;
+}
+
+// --------------------------------------------------------------- tensors
+
+int flock_tensor_from_split(flock_dev* dev, int dtype, const uint8_t* qs, const uint8_t* scales,
+                            int64_t rows, int64_t cols, flock_tensor** out) {
+  if (!dev || !qs || !scales || !out || rows < 1 || cols < 32 || cols % 32 ||
+      (dtype != FLOCK_Q8_0 && dtype != FLOCK_Q4_0)) {
+    set_error("tensor: bad split tensor %lldx%lld dtype %d", (long long)rows, (long long)cols,
+              dtype);
+    return FLOCK_E_ARG;
+  }
+  FLOCK_CK(cudaSetDevice(dev->ordinal));
+  flock_tensor* t = new flock_tensor();
+  t->dev = dev;
+  t->dtype = dtype;
+  t->rows = rows;
+  t->cols = cols;
+  const int64_t nb = cols / 32;
+  t->sc_stride = (int)((nb + 7) / 8 * 8);
+  const int64_t qs_bytes = dtype == FLOCK_Q8_0 ? rows * cols : rows * nb * 16;
+  int rc;
+  if ((rc = t->qs.alloc(qs_bytes)) || (rc = t->sc.alloc(rows * t->sc_stride * 2))) {
+    delete t;
+    return rc;
+  }
+  cudaError_t e = cudaMemcpy(t->qs.p, qs, qs_bytes, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    if (t->sc_stride == nb) {
+      e = cudaMemcpy(t->sc.p, scales, rows * nb * 2, cudaMemcpyHostToDevice);
+    } else {
+      e = cudaMemset(t->sc.p, 0, t->sc.bytes);
+      if (e == cudaSuccess)
+        e = cudaMemcpy2D(t->sc.p, t->sc_stride * 2, scales, nb * 2, nb * 2, rows,
+                         cudaMemcpyHostToDevice);
+    }
+  }
+  if (e != cudaSuccess) {
+    set_error("tensor upload failed: %s", cudaGetErrorString(e));
+    delete t;
+    return FLOCK_E_CUDA;
+  }
+  *out = t;
+  return FLOCK_OK;
+}
+
+int flock_tensor_from_packed(flock_dev* dev, int dtype, const uint8_t* packed, int64_t rows,
+                             int64_t cols, flock_tensor** out) {
+  if (!packed || cols % 32 || rows < 1) {
+    set_error("tensor: cols %lld must be a multiple of 32", (long long)cols);
+    return FLOCK_E_ARG;
+  }
+  const int64_t nb = cols / 32;
+  std::vector<uint8_t> qs(dtype == FLOCK_Q8_0 ? rows * cols : rows * nb * 16);
+  std::vector<uint8_t> sc(rows * nb * 2);
+  int rc = dtype == FLOCK_Q8_0 ? flock_repack_q8(packed, rows, cols, qs.data(), sc.data())
+                               : flock_repack_q4(packed, rows, cols, qs.data(), sc.data());
+  if (rc) return rc;
+  return flock_tensor_from_split(dev, dtype, qs.data(), sc.data(), rows, cols, out);
+}
+
+int flock_tensor_from_f32(flock_dev* dev, const float* data, int64_t n, flock_tensor** out) {
+  if (!dev || !data || n < 1 || !out) return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(dev->ordinal));
+  flock_tensor* t = new flock_tensor();
+  t->dev = dev;
+  t->dtype = FLOCK_F32;
+  t->rows = 1;
+  t->cols = n;
+  int rc = t->data.alloc(n * 4);
+  if (rc) {
+    delete t;
+    return rc;
+  }
+  FLOCK_CK(cudaMemcpy(t->data.p, data, n * 4, cudaMemcpyHostToDevice));
+  *out = t;
+  return FLOCK_OK;
+}
+
+int flock_tensor_free(flock_tensor* t) {
+  if (t) {
+    cudaSetDevice(t->dev->ordinal);
+    delete t;
+  }
+  return FLOCK_OK;
+}
+
+int flock_tensor_bytes(const flock_tensor* t, int64_t* out) {
+  *out = t->dtype == FLOCK_F32 ? (int64_t)t->data.bytes : (int64_t)(t->qs.bytes + t->sc.bytes);
+  return FLOCK_OK;
+}
+
+// ------------------------------------------------------------ op level
+
+}  // extern "C"
+
+namespace {
+struct Tmp {
+  DBuf b;
+  template <typename T>
+  int put(const T* host, size_t n) {
+    FLOCK_TRY(b.alloc(n * sizeof(T)));
+    if (host) FLOCK_CK(cudaMemcpy(b.p, host, n * sizeof(T), cudaMemcpyHostToDevice));
+    return FLOCK_OK;
+  }
+};
+}  // namespace
+
+extern "C" {
+
+int flock_op_matvec(flock_dev* d, const flock_tensor* w, const float* x, int n_tokens,
+                    float* out) {
+  if (!d || !w || !x || !out || n_tokens < 1 || w->dtype == FLOCK_F32) return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  Tmp tx, to;
+  FLOCK_TRY(tx.put(x, (size_t)n_tokens * w->cols));
+  FLOCK_TRY(to.put<float>(nullptr, (size_t)n_tokens * w->rows));
+  GemvArgs a = {};
+  a.seg[0] = seg_of(w, to.b.as<float>(), (int)w->rows);
+  a.nseg = 1;
+  a.K = (int)w->cols;
+  a.n_tokens = n_tokens;
+  a.x = tx.b.as<float>();
+  a.x_stride = (int)w->cols;
+  FLOCK_TRY(launch_gemv(d, w->dtype == FLOCK_Q8_0 ? QT_Q8 : QT_Q4, EPI_STORE, a, false));
+  FLOCK_CK(cudaMemcpyAsync(out, to.b.p, (size_t)n_tokens * w->rows * 4, cudaMemcpyDeviceToHost,
+                           d->stream));
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  return FLOCK_OK;
+}
+
+int flock_op_matvec_timed(flock_dev* d, const flock_tensor* w, int n_tokens, int iters,
+                          float* ms_per_call) {
+  if (!d || !w || n_tokens < 1 || iters < 1 || !ms_per_call || w->dtype == FLOCK_F32)
+    return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  std::vector<float> hx((size_t)n_tokens * w->cols);
+  uint32_t s = 12345u;
+  for (auto& v : hx) {  // xorshift32 in [-1, 1)
+    s ^= s << 13;
+    s ^= s >> 17;
+    s ^= s << 5;
+    v = (float)((double)s / 2147483648.0 - 1.0);
+  }
+  Tmp tx, to;
+  FLOCK_TRY(tx.put(hx.data(), hx.size()));
+  FLOCK_TRY(to.put<float>(nullptr, (size_t)n_tokens * w->rows));
+  GemvArgs a = {};
+  a.seg[0] = seg_of(w, to.b.as<float>(), (int)w->rows);
+  a.nseg = 1;
+  a.K = (int)w->cols;
+  a.n_tokens = n_tokens;
+  a.x = tx.b.as<float>();
+  a.x_stride = (int)w->cols;
+  const int qt = w->dtype == FLOCK_Q8_0 ? QT_Q8 : QT_Q4;
+  FLOCK_TRY(launch_gemv(d, qt, EPI_STORE, a, false));  // warm-up
+  FLOCK_CK(cudaEventRecord(d->t0, d->stream));
+  for (int i = 0; i < iters; i++) FLOCK_TRY(launch_gemv(d, qt, EPI_STORE, a, true));
+  FLOCK_CK(cudaEventRecord(d->t1, d->stream));
+  FLOCK_CK(cudaEventSynchronize(d->t1));
+  float ms = 0;
+  FLOCK_CK(cudaEventElapsedTime(&ms, d->t0, d->t1));
+  *ms_per_call = ms / iters;
+  return FLOCK_OK;
+}
+
+int flock_op_rmsnorm(flock_dev* d, const float* x, const float* g, int n, int n_vecs, float eps,
+                     float* out) {
+  if (!d || !x || !g || !out || n < 1 || n_vecs < 1) return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  Tmp tx, tg, to;
+  FLOCK_TRY(tx.put(x, (size_t)n * n_vecs));
+  FLOCK_TRY(tg.put(g, (size_t)n));
+  FLOCK_TRY(to.put<float>(nullptr, (size_t)n * n_vecs));
+  k_rmsnorm<<<n_vecs, 128, 0, d->stream>>>(tx.b.as<float>(), tg.b.as<float>(), to.b.as<float>(),
+                                           n, n_vecs, eps);
+  FLOCK_CK(cudaGetLastError());
+  FLOCK_CK(cudaMemcpyAsync(out, to.b.p, (size_t)n * n_vecs * 4, cudaMemcpyDeviceToHost,
+                           d->stream));
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  return FLOCK_OK;
+}
+
+}  // extern "C"
+
+namespace flock {
+// kernels/rope.wgsl:50: one thread per rotated pair, in place.
+static __global__ void k_rope(float* x, const float* inv_freq, int n_tokens, int n_heads, int head_dim,
+                       int pos0, int neox) {
+  const int half = head_dim / 2;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= (int64_t)n_tokens * n_heads * half) return;
+  const int j = gid % half;
+  const int head = (gid / half) % n_heads;
+  const int tok = gid / ((int64_t)half * n_heads);
+  const float theta = fmul((float)(pos0 + tok), inv_freq[j]);
+  const float c = __double2float_rn(cos((double)theta));
+  const float s = __double2float_rn(sin((double)theta));
+  float* hb = x + ((int64_t)tok * n_heads + head) * head_dim;
+  const int ia = neox ? j : 2 * j, ib = neox ? j + half : 2 * j + 1;
+  const float a = hb[ia], b = hb[ib];
+  hb[ia] = ffma(-b, s, fmul(a, c));
+  hb[ib] = ffma(b, c, fmul(a, s));
+}
+}  // namespace flock
+
+extern "C" {
+
+int flock_op_rope(flock_dev* d, const float* x, int n_tokens, int n_heads, int head_dim,
+                  int pos0, const float* inv_freq, int pairing, float* out) {
+  if (!d || !x || !inv_freq || !out || head_dim % 2) return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  const size_t n = (size_t)n_tokens * n_heads * head_dim;
+  Tmp tx, ti;
+  FLOCK_TRY(tx.put(x, n));
+  FLOCK_TRY(ti.put(inv_freq, (size_t)head_dim / 2));
+  const int64_t pairs = (int64_t)n_tokens * n_heads * (head_dim / 2);
+  k_rope<<<(unsigned)((pairs + 63) / 64), 64, 0, d->stream>>>(
+      tx.b.as<float>(), ti.b.as<float>(), n_tokens, n_heads, head_dim, pos0,
+      pairing == FLOCK_ROPE_NEOX);
+  FLOCK_CK(cudaGetLastError());
+  FLOCK_CK(cudaMemcpyAsync(out, tx.b.p, n * 4, cudaMemcpyDeviceToHost, d->stream));
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  return FLOCK_OK;
+}
+
+static int ew_op(flock_dev* d, const float* a, const float* b, int64_t n, float* out, bool swiglu) {
+  if (!d || !a || !b || !out || n < 1) return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  Tmp ta, tb, to;
+  FLOCK_TRY(ta.put(a, (size_t)n));
+  FLOCK_TRY(tb.put(b, (size_t)n));
+  FLOCK_TRY(to.put<float>(nullptr, (size_t)n));
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  if (swiglu)
+    k_swiglu<<<blocks, 256, 0, d->stream>>>(ta.b.as<float>(), tb.b.as<float>(), to.b.as<float>(), n);
+  else
+    k_add<<<blocks, 256, 0, d->stream>>>(ta.b.as<float>(), tb.b.as<float>(), to.b.as<float>(), n);
+  FLOCK_CK(cudaGetLastError());
+  FLOCK_CK(cudaMemcpyAsync(out, to.b.p, n * 4, cudaMemcpyDeviceToHost, d->stream));
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  return FLOCK_OK;
+}
+
+int flock_op_swiglu(flock_dev* d, const float* g, const float* u, int64_t n, float* out) {
+  return ew_op(d, g, u, n, out, true);
+}
+
+int flock_op_add(flock_dev* d, const float* a, const float* b, int64_t n, float* out) {
+  return ew_op(d, a, b, n, out, false);
+}
+
+int flock_op_attention(flock_dev* d, const float* q, const float* k, const float* v, int n_heads,
+                       int n_kv_heads, int head_dim, int n_keys, int mode, float* out) {
+  if (!d || !q || !k || !v || !out || head_dim != 128 || n_keys < 1 || n_kv_heads < 1 ||
+      n_heads % n_kv_heads) {
+    set_error("attention: head_dim must be 128 and n_heads a multiple of n_kv_heads");
+    return FLOCK_E_ARG;
+  }
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  const size_t kvn = (size_t)n_keys * n_kv_heads * head_dim;
+  Tmp tq, tk, tv, to, tc;
+  FLOCK_TRY(tq.put(q, (size_t)n_heads * head_dim));
+  FLOCK_TRY(tk.put(k, kvn));
+  FLOCK_TRY(tv.put(v, kvn));
+  FLOCK_TRY(to.put<float>(nullptr, (size_t)n_heads * head_dim));
+  int ctl[2] = {n_keys - 1, 0};
+  FLOCK_TRY(tc.put(ctl, 2));
+  if (mode == FLOCK_ATTN_EXACT) {
+    if ((size_t)n_keys * 4 > 200 * 1024) {
+      set_error("exact attention: %d keys exceed the on-chip score buffer", n_keys);
+      return FLOCK_E_UNSUPPORTED;
+    }
+    AttnArgs aa = {};
+    aa.q = tq.b.as<float>();
+    aa.kcache = tk.b.as<float>();
+    aa.vcache = tv.b.as<float>();
+    aa.out = to.b.as<float>();
+    aa.ctl = tc.b.as<int>();
+    aa.n_tokens = 1;
+    aa.n_heads = n_heads;
+    aa.n_kv_heads = n_kv_heads;
+    aa.head_dim = head_dim;
+    FLOCK_CK(cudaFuncSetAttribute(k_attn_decode_exact, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  200 * 1024));
+    k_attn_decode_exact<<<n_heads, 256, (size_t)n_keys * 4, d->stream>>>(aa);
+    FLOCK_CK(cudaGetLastError());
+  } else {
+    // split-K core on already-final q/k (the layer path fuses norm + RoPE)
+    if (n_heads / n_kv_heads > 4) return FLOCK_E_UNSUPPORTED;
+    Tmp tp, tcount;
+    const int splits = 16;
+    FLOCK_TRY(tp.put<float>(nullptr, (size_t)n_heads * splits * (head_dim + 2)));
+    FLOCK_TRY(tcount.put<uint32_t>(nullptr, (size_t)n_kv_heads));
+    FLOCK_CK(cudaMemset(tcount.b.p, 0, tcount.b.bytes));
+    AttnFastArgs a = {};
+    a.q = tq.b.as<float>();
+    a.kcache = tk.b.as<float>();
+    a.vcache = tv.b.as<float>();
+    a.ctl = tc.b.as<int>();
+    a.out = to.b.as<float>();
+    a.part = tp.b.as<float>();
+    a.count = tcount.b.as<uint32_t>();
+    a.n_heads = n_heads;
+    a.n_kv_heads = n_kv_heads;
+    a.head_dim = head_dim;
+    a.splits = splits;
+    a.chunk_cap = (n_keys + splits - 1) / splits;
+    const size_t smem = attn_fast_smem(a.chunk_cap);
+    if (smem > 200 * 1024) return FLOCK_E_UNSUPPORTED;
+    FLOCK_CK(cudaFuncSetAttribute(k_attn_decode_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  200 * 1024));
+    k_attn_decode_fast<<<dim3(n_kv_heads, splits), ATTN_FAST_THREADS, smem, d->stream>>>(a);
+    FLOCK_CK(cudaGetLastError());
+  }
+  FLOCK_CK(cudaMemcpyAsync(out, to.b.p, (size_t)n_heads * head_dim * 4, cudaMemcpyDeviceToHost,
+                           d->stream));
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  return FLOCK_OK;
+}
+
+int flock_op_attention_prefill(flock_dev* d, const float* q, const float* k, const float* v,
+                               int n_heads, int n_kv_heads, int head_dim, int n_queries, int pos0,
+                               float* out) {
+  if (!d || !q || !k || !v || !out || head_dim != 128 || n_queries < 1 || pos0 < 0 ||
+      n_kv_heads < 1 || n_heads % n_kv_heads) {
+    set_error("attention_prefill: head_dim must be 128");
+    return FLOCK_E_ARG;
+  }
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  const int n_keys = pos0 + n_queries;
+  const size_t kvn = (size_t)n_keys * n_kv_heads * head_dim;
+  const size_t qn = (size_t)n_queries * n_heads * head_dim;
+  Tmp tq, tk, tv, to, tc;
+  FLOCK_TRY(tq.put(q, qn));
+  FLOCK_TRY(tk.put(k, kvn));
+  FLOCK_TRY(tv.put(v, kvn));
+  FLOCK_TRY(to.put<float>(nullptr, qn));
+  int ctl[2] = {pos0, 0};
+  FLOCK_TRY(tc.put(ctl, 2));
+  AttnArgs aa = {};
+  aa.q = tq.b.as<float>();
+  aa.kcache = tk.b.as<float>();
+  aa.vcache = tv.b.as<float>();
+  aa.out = to.b.as<float>();
+  aa.ctl = tc.b.as<int>();
+  aa.n_tokens = n_queries;
+  aa.n_heads = n_heads;
+  aa.n_kv_heads = n_kv_heads;
+  aa.head_dim = head_dim;
+  k_attn_prefill_exact<<<dim3(n_heads, n_queries), 128, 0, d->stream>>>(aa);
+  FLOCK_CK(cudaGetLastError());
+  FLOCK_CK(cudaMemcpyAsync(out, to.b.p, qn * 4, cudaMemcpyDeviceToHost, d->stream));
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  return FLOCK_OK;
+}
+
+int flock_op_embed(flock_dev* d, const flock_tensor* table, const int32_t* ids, int n,
+                   float* out) {
+  if (!d || !table || !ids || !out || n < 1 || table->dtype != FLOCK_Q8_0) return FLOCK_E_ARG;
+  for (int i = 0; i < n; i++)
+    if (ids[i] < 0 || ids[i] >= table->rows) {
+      set_error("embed: id %d out of range 0..%lld", ids[i], (long long)table->rows - 1);
+      return FLOCK_E_ARG;
+    }
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  Tmp ti, to;
+  FLOCK_TRY(ti.put(ids, (size_t)n));
+  FLOCK_TRY(to.put<float>(nullptr, (size_t)n * table->cols));
+  EmbedArgs a = {};
+  a.qs = table->qs.as<uint8_t>();
+  a.sc = table->sc.as<uint16_t>();
+  a.ids = ti.b.as<int32_t>();
+  a.out = to.b.as<float>();
+  a.n_tokens = n;
+  a.hidden = (int)table->cols;
+  a.sc_stride = table->sc_stride;
+  a.vocab = (int)table->rows;
+  k_embed<<<n, 256, 0, d->stream>>>(a);
+  FLOCK_CK(cudaGetLastError());
+  FLOCK_CK(cudaMemcpyAsync(out, to.b.p, (size_t)n * table->cols * 4, cudaMemcpyDeviceToHost,
+                           d->stream));
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  return FLOCK_OK;
+}
+
+int flock_op_argmax(flock_dev* d, const float* x, int64_t n, int64_t* index, float* value) {
+  if (!d || !x || n < 1 || !index) return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  Tmp tx;
+  FLOCK_TRY(tx.put(x, (size_t)n));
+  int blocks = (int)((n + 255) / 256);
+  if (blocks > 2 * d->sm_count) blocks = 2 * d->sm_count;
+  k_argmax<<<blocks, 256, 0, d->stream>>>(tx.b.as<float>(), n, d->am_val.as<float>(),
+                                          d->am_idx.as<uint32_t>(), d->am_count.as<uint32_t>(),
+                                          d->am_best_val.as<float>(), d->am_best_idx.as<int32_t>(),
+                                          0);
+  FLOCK_CK(cudaGetLastError());
+  int32_t idx = 0;
+  float val = 0;
+  FLOCK_CK(cudaMemcpyAsync(&idx, d->am_best_idx.p, 4, cudaMemcpyDeviceToHost, d->stream));
+  FLOCK_CK(cudaMemcpyAsync(&val, d->am_best_val.p, 4, cudaMemcpyDeviceToHost, d->stream));
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  *index = (int64_t)(uint32_t)idx;
+  if (value) *value = val;
+  return FLOCK_OK;
+}
+
+// ------------------------------------------------------------------ layer
+
+}  // extern "C"
+
+namespace flock {
+// Layer.fromBuffers (layer.ts:228) body: bind tensors by name, check the
+// required set (requireWeights, :269) and shapes, allocate the KV cache.
+// ws / ctl == nullptr -> the layer owns its workspace / position block.
+int layer_build(flock_dev* dev, const flock_layer_config* cfg, int n_tensors,
+                const char* const* names, flock_tensor* const* tensors, Workspace* ws,
+                int* ctl, flock_layer** out) {
+  if (!dev || !cfg || !names || !tensors || !out) return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(dev->ordinal));
+  flock_layer* L = new flock_layer();
+  for (int i = 0; i < n_tensors; i++) {
+    int slot = -1;
+    for (int s = 0; s < W_COUNT; s++)
+      if (names[i] && strcmp(names[i], kTensorNames[s]) == 0) slot = s;
+    if (slot < 0) continue;  // extra tensors are ignored, as the reference ignores them
+    const flock_tensor* t = tensors[i];
+    const bool is_norm = slot >= W_ATTN_NORM;
+    if (!t || (is_norm ? t->dtype != FLOCK_F32 : t->dtype != FLOCK_Q8_0)) {
+      set_error("%s: neither a split Q8_0 tensor nor f32 data", names[i]);
+      delete L;
+      return FLOCK_E_ARG;
+    }
+    L->w[slot] = t;
+  }
+  std::string missing;
+  int n_missing = 0;
+  for (int s = 0; s < W_COUNT; s++)
+    if (!L->w[s]) {
+      missing += (n_missing ? ", " : "");
+      missing += kTensorNames[s];
+      n_missing++;
+    }
+  if (n_missing) {
+    set_error("layer is missing %d tensor(s): %s", n_missing, missing.c_str());
+    delete L;
+    return FLOCK_E_MISSING;
+  }
+  // shapes
+  const int qw = cfg->n_heads * cfg->head_dim, kvw = cfg->n_kv_heads * cfg->head_dim;
+  struct { int s; int64_t r, c; } want[] = {
+      {W_Q, qw, cfg->hidden},         {W_K, kvw, cfg->hidden},        {W_V, kvw, cfg->hidden},
+      {W_O, cfg->hidden, qw},         {W_GATE, cfg->ffn, cfg->hidden}, {W_UP, cfg->ffn, cfg->hidden},
+      {W_DOWN, cfg->hidden, cfg->ffn}};
+  for (auto& w : want)
+    if (L->w[w.s]->rows != w.r || L->w[w.s]->cols != w.c) {
+      set_error("%s is %lldx%lld, config wants %lldx%lld", kTensorNames[w.s],
+                (long long)L->w[w.s]->rows, (long long)L->w[w.s]->cols, (long long)w.r,
+                (long long)w.c);
+      delete L;
+      return FLOCK_E_ARG;
+    }
+  int rc = layer_init(L, dev, *cfg, ws, ctl);
+  if (rc) {
+    delete L;
+    return rc;
+  }
+  *out = L;
+  return FLOCK_OK;
+}
+}  // namespace flock
+
+extern "C" {
+
+int flock_layer_create(flock_dev* dev, const flock_layer_config* cfg, int n_tensors,
+                       const char* const* names, flock_tensor* const* tensors,
+                       flock_layer** out) {
+  return layer_build(dev, cfg, n_tensors, names, tensors, nullptr, nullptr, out);
+}
+
+
+int flock_layer_free(flock_layer* L) {
+  if (L) {
+    cudaSetDevice(L->dev->ordinal);
+    cudaStreamSynchronize(L->dev->stream);
+    delete L;
+  }
+  return FLOCK_OK;
+}
+
+int flock_layer_encode(flock_layer* L, const float* hidden, int n) {
+  if (!L) return FLOCK_E_ARG;
+  const flock_layer_config& c = L->cfg;
+  if (n < 1) {
+    set_error("nTokens must be >= 1, got %d", n);
+    return FLOCK_E_ARG;
+  }
+  if (n > c.max_prefill) {
+    set_error("prefill of %d exceeds maxPrefill %d; chunk it", n, c.max_prefill);
+    return FLOCK_E_STATE;
+  }
+  if (L->n_keys + n > c.max_keys) {
+    if (n == 1) set_error("KV cache full at %d keys", c.max_keys);
+    else set_error("KV cache would exceed %d keys (%d + %d)", c.max_keys, L->n_keys, n);
+    return FLOCK_E_STATE;
+  }
+  FLOCK_CK(cudaSetDevice(L->dev->ordinal));
+  if (hidden)
+    FLOCK_CK(cudaMemcpyAsync(L->ws->h.p, hidden, (size_t)n * c.hidden * 4, cudaMemcpyHostToDevice,
+                             L->dev->stream));
+  PrefetchList none = {};
+  FLOCK_TRY(layer_enqueue(L, n, true, none, true));
+  L->n_keys += n;
+  return FLOCK_OK;
+}
+
+int flock_layer_read_output(flock_layer* L, int n, float* out) {
+  if (!L || !out || n < 1 || n > L->cfg.max_prefill) return FLOCK_E_ARG;
+  FLOCK_CK(cudaMemcpyAsync(out, L->ws->h.p, (size_t)n * L->cfg.hidden * 4, cudaMemcpyDeviceToHost,
+                           L->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(L->dev->stream));
+  return FLOCK_OK;
+}
+
+int flock_layer_rewind(flock_layer* L, int n_keys) {
+  if (!L || n_keys < 0 || n_keys > L->cfg.max_keys) return FLOCK_E_ARG;
+  int ctl[2] = {n_keys, 0};
+  FLOCK_CK(cudaMemcpyAsync(L->ctl, ctl, sizeof ctl, cudaMemcpyHostToDevice, L->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(L->dev->stream));
+  L->n_keys = n_keys;
+  return FLOCK_OK;
+}
+
+int flock_layer_reset(flock_layer* L) { return flock_layer_rewind(L, 0); }
+
+int flock_layer_n_keys(const flock_layer* L, int* out) {
+  *out = L->n_keys;
+  return FLOCK_OK;
+}
+
+int flock_layer_read_cache(flock_layer* L, float* k, float* v) {
+  const size_t bytes = (size_t)L->n_keys * L->cfg.n_kv_heads * L->cfg.head_dim * 4;
+  if (bytes) {
+    FLOCK_CK(cudaMemcpyAsync(k, L->kcache.p, bytes, cudaMemcpyDeviceToHost, L->dev->stream));
+    FLOCK_CK(cudaMemcpyAsync(v, L->vcache.p, bytes, cudaMemcpyDeviceToHost, L->dev->stream));
+  }
+  FLOCK_CK(cudaStreamSynchronize(L->dev->stream));
+  return FLOCK_OK;
+}
+
+int flock_layer_write_cache(flock_layer* L, const float* k, const float* v, int n_keys) {
+  if (!L || !k || !v || n_keys < 0 || L->n_keys + n_keys > L->cfg.max_keys) return FLOCK_E_ARG;
+  const size_t row = (size_t)L->cfg.n_kv_heads * L->cfg.head_dim * 4;
+  FLOCK_CK(cudaMemcpyAsync(L->kcache.as<uint8_t>() + L->n_keys * row, k, n_keys * row,
+                           cudaMemcpyHostToDevice, L->dev->stream));
+  FLOCK_CK(cudaMemcpyAsync(L->vcache.as<uint8_t>() + L->n_keys * row, v, n_keys * row,
+                           cudaMemcpyHostToDevice, L->dev->stream));
+  return flock_layer_rewind(L, L->n_keys + n_keys);
+}
+
+int flock_range_forward(flock_layer* const* layers, int n_layers, const float* x, int seq,
+                        int offset, int reset, float* out) {
+  if (!layers || n_layers < 1 || !x || !out || seq < 1) return FLOCK_E_ARG;
+  for (int i = 0; i < n_layers; i++) {
+    if (!layers[i] || layers[i]->dev != layers[0]->dev ||
+        layers[i]->cfg.hidden != layers[0]->cfg.hidden) {
+      set_error("range_forward: layers must share one device and hidden size");
+      return FLOCK_E_ARG;
+    }
+    if (reset) FLOCK_TRY(flock_layer_reset(layers[i]));
+    if (layers[i]->n_keys != offset) {
+      set_error("offset %d does not match this cache's position %d", offset, layers[i]->n_keys);
+      return FLOCK_E_STATE;
+    }
+  }
+  flock_dev* d = layers[0]->dev;
+  const size_t bytes = (size_t)seq * layers[0]->cfg.hidden * 4;
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  FLOCK_TRY(flock_layer_encode(layers[0], x, seq));
+  for (int i = 1; i < n_layers; i++) {
+    // chain on the device: previous output -> this layer's input buffer
+    if (layers[i]->ws != layers[i - 1]->ws)
+      FLOCK_CK(cudaMemcpyAsync(layers[i]->ws->h.p, layers[i - 1]->ws->h.p, bytes,
+                               cudaMemcpyDeviceToDevice, d->stream));
+    FLOCK_TRY(flock_layer_encode(layers[i], nullptr, seq));
+  }
+  return flock_layer_read_output(layers[n_layers - 1], seq, out);
+}
+
+}  // extern "C"

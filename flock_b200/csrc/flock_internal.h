@@ -1,0 +1,115 @@
+// Internal host-side structures of libflock_cuda.so (not part of the ABI).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "../../include/flock_cuda.h"
+#include "gemv.cuh"
+
+namespace flock {
+
+void set_error(const char* fmt, ...);
+
+#define FLOCK_CK(call)                                                              \
+  do {                                                                              \
+    cudaError_t e_ = (call);                                                        \
+    if (e_ != cudaSuccess) {                                                        \
+      ::flock::set_error("CUDA error %s at %s:%d (%s)", cudaGetErrorString(e_),     \
+                         __FILE__, __LINE__, #call);                                \
+      return FLOCK_E_CUDA;                                                          \
+    }                                                                               \
+  } while (0)
+
+#define FLOCK_TRY(expr)        \
+  do {                         \
+    int rc_ = (expr);          \
+    if (rc_ != FLOCK_OK) return rc_; \
+  } while (0)
+
+// A device allocation owned by its holder.
+struct DBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  int alloc(size_t n);
+  void release();
+  template <typename T>
+  T* as() const { return reinterpret_cast<T*>(p); }
+  ~DBuf() { release(); }
+  DBuf() = default;
+  DBuf(const DBuf&) = delete;
+  DBuf& operator=(const DBuf&) = delete;
+};
+
+}  // namespace flock
+
+struct flock_dev {
+  int ordinal = 0;
+  int sm_count = 148;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t t0 = nullptr, t1 = nullptr;
+  // scratch for op-level calls and argmax partials
+  flock::DBuf am_val, am_idx, am_count, am_best_val, am_best_idx;
+};
+
+struct flock_tensor {
+  flock_dev* dev = nullptr;
+  int dtype = 0;
+  int64_t rows = 0, cols = 0;
+  int sc_stride = 0;  // f16 scales per row, padded to a multiple of 8
+  flock::DBuf qs, sc, data;
+};
+
+struct flock_comm;
+
+namespace flock {
+
+// Activation buffers one layer step needs; a Model shares one across layers.
+struct Workspace {
+  int P = 0, H = 0, nH = 0, nKV = 0, hd = 0, F = 0;
+  DBuf h, q, k, v, qn, attn, act;
+  DBuf attn_part, attn_count;  // fast decode attention partials
+  int attn_splits = 16;
+  int alloc(const flock_layer_config& c);
+};
+
+enum { W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_ATTN_NORM, W_Q_NORM, W_K_NORM, W_FFN_NORM,
+       W_COUNT };
+extern const char* const kTensorNames[W_COUNT];
+
+// Launch plan pieces
+int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl);
+int gemv_grid(flock_dev* d, int total_groups);
+
+}  // namespace flock
+
+struct flock_layer {
+  flock_dev* dev = nullptr;
+  flock_layer_config cfg{};
+  const flock_tensor* w[flock::W_COUNT] = {};
+  flock::DBuf kcache, vcache, ctl_own, inv_freq;
+  int* ctl = nullptr;          // {pos, n_last} on the device (own or the model's)
+  int n_keys = 0;              // host mirror
+  flock::Workspace* ws = nullptr;
+  flock::Workspace ws_own;     // standalone layers own their workspace
+  bool owns_ws = false;
+};
+
+namespace flock {
+// Enqueue one layer step over ws->h (in place): n tokens at the layer's pos.
+// `advance` = this launch advances the layer's ctl; pf_next = L2 prefetch
+// hint for whatever follows the layer (may be empty).
+int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_next, bool pdl);
+int layer_init(flock_layer* L, flock_dev* dev, const flock_layer_config& cfg, Workspace* ws,
+               int* shared_ctl);
+int comm_send(flock_comm* c, const void* p, size_t n_f32, int peer);
+int comm_recv(flock_comm* c, void* p, size_t n_f32, int peer);
+int comm_wait(flock_comm* c);
+int comm_rank(const flock_comm* c, int* rank, int* n_ranks);
+int layer_build(flock_dev* dev, const flock_layer_config* cfg, int n_tensors,
+                const char* const* names, flock_tensor* const* tensors, Workspace* ws, int* ctl,
+                flock_layer** out);
+}  // namespace flock

@@ -1,0 +1,534 @@
+// Model: kernels/model.ts on B200.  ids -> embedding gather -> held layers ->
+// output_norm -> tied (or untied) Q8_0 head -> argmax, everything on the
+// device; the host sees one int32 per generated token.
+//
+// Device-side state makes a decode step replayable as one CUDA graph: the
+// position lives in a {pos, n_last} control block that layer 0's first
+// kernel advances, the head's last CTA writes the chosen id into ids[0]
+// (the next step's embedding input) and into a per-position history, so a
+// greedy decode loop needs no host round trip at all.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <vector>
+
+#include "flock_internal.h"
+#include "gemv.cuh"
+#include "ops.cuh"
+
+using namespace flock;
+
+struct flock_model {
+  flock_dev* dev = nullptr;
+  flock_layer_config cfg{};
+  int vocab = 0, n_layers = 0, held = 0;
+  std::vector<flock_layer*> layers;
+  const flock_tensor* embd = nullptr;
+  const flock_tensor* out_norm = nullptr;
+  const flock_tensor* head = nullptr;  // lm-head: embd when tied
+  Workspace ws;
+  DBuf ctl, ids, hist, logits, normed, am_val, am_idx, am_count, am_best_val;
+  int pos = 0;  // host mirror of ctl[0] after the last step
+  cudaGraphExec_t decode_graph = nullptr;
+};
+
+namespace {
+
+int enqueue_embed(flock_model* m, int n) {
+  EmbedArgs a = {};
+  a.qs = m->embd->qs.as<uint8_t>();
+  a.sc = m->embd->sc.as<uint16_t>();
+  a.ids = m->ids.as<int32_t>();
+  a.out = m->ws.h.as<float>();
+  a.n_tokens = n;
+  a.hidden = m->cfg.hidden;
+  a.sc_stride = m->embd->sc_stride;
+  a.vocab = (int)m->embd->rows;
+  if (m->held > 0) {
+    const flock_tensor* q = m->layers[0]->w[W_Q];
+    a.pf.ptr[0] = q->qs.as<uint8_t>();
+    a.pf.bytes[0] = q->qs.bytes & ~(uint64_t)15;
+    a.pf.n = 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n);
+  cfg.blockDim = dim3(256);
+  cfg.stream = m->dev->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FLOCK_CK(cudaLaunchKernelEx(&cfg, k_embed, a));
+  return FLOCK_OK;
+}
+
+// Layers over ws.h ([n][hidden]); layer 0 advances the shared position.
+int enqueue_layers(flock_model* m, int n) {
+  for (int i = 0; i < m->held; i++) {
+    PrefetchList pf = {};
+    if (i + 1 < m->held) {
+      const flock_tensor* q = m->layers[i + 1]->w[W_Q];
+      pf.ptr[0] = q->qs.as<uint8_t>();
+      pf.bytes[0] = q->qs.bytes & ~(uint64_t)15;
+      const flock_tensor* k = m->layers[i + 1]->w[W_K];
+      pf.ptr[1] = k->qs.as<uint8_t>();
+      pf.bytes[1] = k->qs.bytes & ~(uint64_t)15;
+      const flock_tensor* v = m->layers[i + 1]->w[W_V];
+      pf.ptr[2] = v->qs.as<uint8_t>();
+      pf.bytes[2] = v->qs.bytes & ~(uint64_t)15;
+      pf.n = 3;
+    }
+    FLOCK_TRY(layer_enqueue(m->layers[i], n, i == 0, pf, true));
+  }
+  return FLOCK_OK;
+}
+
+// output_norm + lm-head + argmax on row `row` of ws.h.
+int enqueue_head(flock_model* m, int row) {
+  GemvArgs a = {};
+  GemvSeg s;
+  s.qs = m->head->qs.as<uint8_t>();
+  s.sc = m->head->sc.as<uint16_t>();
+  s.out = m->logits.as<float>();
+  s.rows = (int)m->head->rows;
+  s.sc_stride = m->head->sc_stride;
+  s.out_stride = (int)m->head->rows;
+  a.seg[0] = s;
+  a.nseg = 1;
+  a.K = m->cfg.hidden;
+  a.n_tokens = 1;
+  a.x = m->ws.h.as<float>() + (size_t)row * m->cfg.hidden;
+  a.x_stride = m->cfg.hidden;
+  a.norm_gain = m->out_norm->data.as<float>();
+  a.eps = m->cfg.eps;
+  a.am_val = m->am_val.as<float>();
+  a.am_idx = m->am_idx.as<uint32_t>();
+  a.am_count = m->am_count.as<uint32_t>();
+  a.am_best_val = m->am_best_val.as<float>();
+  a.am_best_idx = m->ids.as<int32_t>();
+  return launch_gemv(m->dev, QT_Q8, EPI_ARGMAX, a, true);
+}
+
+// Copy ids[0] (the chosen token) into hist[pos_last] on the device.
+static __global__ void k_record(const int32_t* ids, const int* ctl, int32_t* hist, int cap) {
+  pdl_wait();
+  const int p = ctl[0] + ctl[1] - 1;
+  if (p >= 0 && p < cap) hist[p] = ids[0];
+}
+
+int enqueue_record(flock_model* m) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(1);
+  cfg.stream = m->dev->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FLOCK_CK(cudaLaunchKernelEx(&cfg, k_record, (const int32_t*)m->ids.as<int32_t>(),
+                              (const int*)m->ctl.as<int>(), m->hist.as<int32_t>(),
+                              m->cfg.max_keys));
+  return FLOCK_OK;
+}
+
+int check_room(flock_model* m, int n) {
+  if (m->pos + n > m->cfg.max_keys) {
+    set_error("sequence would exceed maxKeys %d at %d", m->cfg.max_keys, m->pos + n);
+    return FLOCK_E_STATE;
+  }
+  return FLOCK_OK;
+}
+
+int upload_ids(flock_model* m, const int32_t* ids, int n) {
+  for (int i = 0; i < n; i++)
+    if (ids[i] < 0 || ids[i] >= m->vocab) {
+      set_error("token id %d out of range 0..%d", ids[i], m->vocab - 1);
+      return FLOCK_E_ARG;
+    }
+  FLOCK_CK(cudaMemcpyAsync(m->ids.p, ids, (size_t)n * 4, cudaMemcpyHostToDevice, m->dev->stream));
+  return FLOCK_OK;
+}
+
+// model.ts:235 encodeTokens: chunks of maxPrefill; leaves the last chunk's
+// rows in ws.h.  Returns the size of the last chunk.
+int encode_tokens(flock_model* m, const int32_t* ids, int n, int* last_chunk) {
+  if (n < 1) {
+    set_error("no tokens");
+    return FLOCK_E_ARG;
+  }
+  FLOCK_TRY(check_room(m, n));
+  for (int off = 0; off < n; off += m->cfg.max_prefill) {
+    const int c = (n - off) < m->cfg.max_prefill ? (n - off) : m->cfg.max_prefill;
+    FLOCK_TRY(upload_ids(m, ids + off, c));
+    FLOCK_TRY(enqueue_embed(m, c));
+    FLOCK_TRY(enqueue_layers(m, c));
+    m->pos += c;
+    *last_chunk = c;
+  }
+  return FLOCK_OK;
+}
+
+int capture_decode(flock_model* m) {
+  if (m->decode_graph) return FLOCK_OK;
+  cudaStream_t st = m->dev->stream;
+  cudaGraph_t g = nullptr;
+  FLOCK_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  int rc = enqueue_embed(m, 1);
+  if (!rc) rc = enqueue_layers(m, 1);
+  if (!rc) rc = enqueue_head(m, 0);
+  if (!rc) rc = enqueue_record(m);
+  cudaError_t e = cudaStreamEndCapture(st, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) {
+    set_error("decode graph capture failed: %s", cudaGetErrorString(e));
+    return FLOCK_E_CUDA;
+  }
+  e = cudaGraphInstantiate(&m->decode_graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    m->decode_graph = nullptr;
+    set_error("decode graph instantiate failed: %s", cudaGetErrorString(e));
+    return FLOCK_E_CUDA;
+  }
+  return FLOCK_OK;
+}
+
+int need_head(flock_model* m) {
+  if (!m->embd || !m->head) {
+    set_error("this model holds no embedding/head (a layer-range stage)");
+    return FLOCK_E_STATE;
+  }
+  return FLOCK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_layers,
+                       flock_tensor* const* lt, const flock_tensor* embd,
+                       const flock_tensor* output_norm, const flock_tensor* output, int cut,
+                       flock_model** out) {
+  if (!dev || !cfg || !out || n_layers < 0 || (n_layers > 0 && !lt)) return FLOCK_E_ARG;
+  if (cut < 0) cut = n_layers;
+  if (cut > n_layers) {
+    set_error("cut %d is not in 0..%d", cut, n_layers);
+    return FLOCK_E_ARG;
+  }
+  if (embd && (embd->cols != cfg->hidden || embd->dtype != FLOCK_Q8_0)) {
+    set_error("token_embd cols %lld != hidden %d", (long long)embd->cols, cfg->hidden);
+    return FLOCK_E_ARG;
+  }
+  if (embd && (!output_norm || output_norm->dtype != FLOCK_F32 || output_norm->cols != cfg->hidden)) {
+    set_error("output_norm.weight missing or not %d f32", cfg->hidden);
+    return FLOCK_E_MISSING;
+  }
+  FLOCK_CK(cudaSetDevice(dev->ordinal));
+  flock_model* m = new flock_model();
+  m->dev = dev;
+  m->cfg = *cfg;
+  m->vocab = vocab;
+  m->n_layers = n_layers;
+  m->embd = embd;
+  m->out_norm = output_norm;
+  m->head = output ? output : embd;
+  int rc = FLOCK_OK;
+  auto fail = [&](int r) {
+    flock_model_free(m);
+    return r;
+  };
+  if ((rc = m->ws.alloc(*cfg))) return fail(rc);
+  if ((rc = m->ctl.alloc(16))) return fail(rc);
+  if (cudaMemset(m->ctl.p, 0, 16) != cudaSuccess) return fail(FLOCK_E_CUDA);
+  if ((rc = m->ids.alloc((size_t)m->ws.P * 4 + 16))) return fail(rc);
+  if ((rc = m->hist.alloc((size_t)cfg->max_keys * 4))) return fail(rc);
+  if ((rc = m->logits.alloc((size_t)(vocab > 0 ? vocab : 1) * 4))) return fail(rc);
+  if ((rc = m->normed.alloc((size_t)cfg->hidden * 4))) return fail(rc);
+  if ((rc = m->am_val.alloc(4096 * 4)) || (rc = m->am_idx.alloc(4096 * 4)) ||
+      (rc = m->am_count.alloc(16)) || (rc = m->am_best_val.alloc(16)))
+    return fail(rc);
+  if (cudaMemset(m->am_count.p, 0, 16) != cudaSuccess) return fail(FLOCK_E_CUDA);
+  if (m->head && (m->head->cols != cfg->hidden || m->head->rows != vocab)) {
+    set_error("lm-head is %lldx%lld, want %dx%d", (long long)m->head->rows,
+              (long long)m->head->cols, vocab, cfg->hidden);
+    return fail(FLOCK_E_ARG);
+  }
+  for (int i = 0; i < cut; i++) {
+    const char* names[W_COUNT];
+    flock_tensor* ts[W_COUNT];
+    for (int s = 0; s < W_COUNT; s++) {
+      names[s] = kTensorNames[s];
+      ts[s] = lt[(size_t)i * W_COUNT + s];
+    }
+    flock_layer* L = nullptr;
+    // all held layers share the model's workspace and position block
+    if ((rc = layer_build(dev, cfg, W_COUNT, names, ts, &m->ws, m->ctl.as<int>(), &L)))
+      return fail(rc);
+    m->layers.push_back(L);
+  }
+  m->held = cut;
+  *out = m;
+  return FLOCK_OK;
+}
+
+int flock_model_free(flock_model* m) {
+  if (!m) return FLOCK_OK;
+  cudaSetDevice(m->dev->ordinal);
+  cudaStreamSynchronize(m->dev->stream);
+  if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
+  for (auto* L : m->layers) flock_layer_free(L);
+  delete m;
+  return FLOCK_OK;
+}
+
+int flock_model_reset(flock_model* m) { return flock_model_rewind(m, 0); }
+
+int flock_model_rewind(flock_model* m, int n_keys) {
+  if (!m || n_keys < 0 || n_keys > m->cfg.max_keys) return FLOCK_E_ARG;
+  int ctl[4] = {n_keys, 0, 0, 0};
+  FLOCK_CK(cudaMemcpyAsync(m->ctl.p, ctl, sizeof ctl, cudaMemcpyHostToDevice, m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  m->pos = n_keys;
+  for (auto* L : m->layers) L->n_keys = n_keys;
+  return FLOCK_OK;
+}
+
+int flock_model_pos(const flock_model* m, int* out) {
+  *out = m->pos;
+  return FLOCK_OK;
+}
+
+int flock_model_held(const flock_model* m, int* out) {
+  *out = m->held;
+  return FLOCK_OK;
+}
+
+int flock_model_step(flock_model* m, const int32_t* ids, int n, int32_t* next_id) {
+  if (!m || !ids || !next_id) return FLOCK_E_ARG;
+  FLOCK_TRY(need_head(m));
+  FLOCK_CK(cudaSetDevice(m->dev->ordinal));
+  if (n == 1 && m->held > 0) {
+    FLOCK_TRY(check_room(m, 1));
+    FLOCK_TRY(upload_ids(m, ids, 1));
+    FLOCK_TRY(capture_decode(m));
+    FLOCK_CK(cudaGraphLaunch(m->decode_graph, m->dev->stream));
+    m->pos += 1;
+  } else {
+    int last = 0;
+    FLOCK_TRY(encode_tokens(m, ids, n, &last));
+    FLOCK_TRY(enqueue_head(m, last - 1));
+    FLOCK_TRY(enqueue_record(m));
+  }
+  for (auto* L : m->layers) L->n_keys = m->pos;
+  FLOCK_CK(cudaMemcpyAsync(next_id, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
+}
+
+int flock_model_decode_device(flock_model* m, int n_steps, int32_t* out_ids) {
+  if (!m || n_steps < 0 || (n_steps > 0 && !out_ids)) return FLOCK_E_ARG;
+  FLOCK_TRY(need_head(m));
+  if (m->held == 0) return FLOCK_E_STATE;
+  FLOCK_TRY(check_room(m, n_steps));
+  FLOCK_CK(cudaSetDevice(m->dev->ordinal));
+  FLOCK_TRY(capture_decode(m));
+  const int start = m->pos;
+  for (int i = 0; i < n_steps; i++) FLOCK_CK(cudaGraphLaunch(m->decode_graph, m->dev->stream));
+  m->pos += n_steps;
+  for (auto* L : m->layers) L->n_keys = m->pos;
+  if (n_steps)
+    FLOCK_CK(cudaMemcpyAsync(out_ids, m->hist.as<int32_t>() + start, (size_t)n_steps * 4,
+                             cudaMemcpyDeviceToHost, m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
+}
+
+int flock_model_generate(flock_model* m, const int32_t* prompt, int n_prompt, int max_tokens,
+                         const int32_t* eos, int n_eos, int32_t* out_ids, int* n_out) {
+  if (!m || !prompt || n_prompt < 1 || max_tokens < 0 || !n_out) return FLOCK_E_ARG;
+  *n_out = 0;
+  int32_t next = 0;
+  FLOCK_TRY(flock_model_step(m, prompt, n_prompt, &next));
+  for (int i = 0; i < max_tokens; i++) {
+    bool stop = false;
+    for (int e = 0; e < n_eos; e++) stop |= (eos[e] == next);
+    if (stop) break;
+    out_ids[(*n_out)++] = next;
+    if (*n_out >= max_tokens) break;
+    FLOCK_TRY(flock_model_step(m, &next, 1, &next));
+  }
+  return FLOCK_OK;
+}
+
+int flock_model_logits(flock_model* m, const int32_t* ids, int n, float* logits) {
+  int32_t tok;
+  FLOCK_TRY(flock_model_step(m, ids, n, &tok));
+  FLOCK_CK(cudaMemcpy(logits, m->logits.p, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost));
+  return FLOCK_OK;
+}
+
+int flock_model_hidden_state(flock_model* m, const int32_t* ids, int n, float* out) {
+  if (!m || !ids || !out) return FLOCK_E_ARG;
+  if (!m->embd) return need_head(m);
+  FLOCK_CK(cudaSetDevice(m->dev->ordinal));
+  int last = 0;
+  FLOCK_TRY(encode_tokens(m, ids, n, &last));
+  for (auto* L : m->layers) L->n_keys = m->pos;
+  FLOCK_CK(cudaMemcpyAsync(out, m->ws.h.as<float>() + (size_t)(last - 1) * m->cfg.hidden,
+                           (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost, m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
+}
+
+int flock_model_normed_state(flock_model* m, const int32_t* ids, int n, float* out) {
+  if (!m || !ids || !out) return FLOCK_E_ARG;
+  FLOCK_TRY(need_head(m));
+  FLOCK_CK(cudaSetDevice(m->dev->ordinal));
+  int last = 0;
+  FLOCK_TRY(encode_tokens(m, ids, n, &last));
+  for (auto* L : m->layers) L->n_keys = m->pos;
+  k_rmsnorm<<<1, 128, 0, m->dev->stream>>>(
+      m->ws.h.as<float>() + (size_t)(last - 1) * m->cfg.hidden, m->out_norm->data.as<float>(),
+      m->normed.as<float>(), m->cfg.hidden, 1, m->cfg.eps);
+  FLOCK_CK(cudaGetLastError());
+  FLOCK_TRY(enqueue_head(m, last - 1));
+  FLOCK_CK(cudaMemcpyAsync(out, m->normed.p, (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost,
+                           m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
+}
+
+int flock_model_embed(flock_model* m, const int32_t* ids, int n, float* out) {
+  if (!m || !ids || !out || n < 1 || n > m->ws.P) return FLOCK_E_ARG;
+  FLOCK_TRY(need_head(m));
+  FLOCK_CK(cudaSetDevice(m->dev->ordinal));
+  FLOCK_TRY(upload_ids(m, ids, n));
+  FLOCK_TRY(enqueue_embed(m, n));
+  FLOCK_CK(cudaMemcpyAsync(out, m->ws.h.p, (size_t)n * m->cfg.hidden * 4, cudaMemcpyDeviceToHost,
+                           m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
+}
+
+int flock_model_encode_partial(flock_model* m, const int32_t* ids, int n, int offset, float* out) {
+  if (!m || !ids || !out) return FLOCK_E_ARG;
+  if (offset >= 0 && offset != m->pos) {
+    set_error("offset %d does not match this cache's position %d", offset, m->pos);
+    return FLOCK_E_STATE;
+  }
+  if (n > m->cfg.max_prefill) {
+    set_error("a lap of %d tokens exceeds maxPrefill %d", n, m->cfg.max_prefill);
+    return FLOCK_E_STATE;
+  }
+  if (!m->embd) return need_head(m);
+  FLOCK_CK(cudaSetDevice(m->dev->ordinal));
+  int last = 0;
+  FLOCK_TRY(encode_tokens(m, ids, n, &last));
+  for (auto* L : m->layers) L->n_keys = m->pos;
+  FLOCK_CK(cudaMemcpyAsync(out, m->ws.h.p, (size_t)n * m->cfg.hidden * 4, cudaMemcpyDeviceToHost,
+                           m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
+}
+
+int flock_model_project_hidden(flock_model* m, const float* flat, int seq, int32_t* next_id) {
+  if (!m || !flat || seq < 1 || !next_id) return FLOCK_E_ARG;
+  FLOCK_TRY(need_head(m));
+  FLOCK_CK(cudaSetDevice(m->dev->ordinal));
+  FLOCK_CK(cudaMemcpyAsync(m->ws.h.p, flat + (size_t)(seq - 1) * m->cfg.hidden,
+                           (size_t)m->cfg.hidden * 4, cudaMemcpyHostToDevice, m->dev->stream));
+  FLOCK_TRY(enqueue_head(m, 0));
+  FLOCK_CK(cudaMemcpyAsync(next_id, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
+}
+
+int flock_model_set_token(flock_model* m, int32_t id) {
+  if (!m || id < 0 || id >= m->vocab) return FLOCK_E_ARG;
+  FLOCK_CK(cudaMemcpyAsync(m->ids.p, &id, 4, cudaMemcpyHostToDevice, m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
+}
+
+int flock_model_current_token(flock_model* m, int32_t* out) {
+  FLOCK_CK(cudaMemcpyAsync(out, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
+}
+
+}  // extern "C"
+
+// ============================================================ pipeline
+//
+// server/mesh.js:679 Flock.lap + web/bird.html:544 runFrame on one box: the
+// coordinator rank (embedding, layers 0..cut-1, output_norm, head) sends the
+// hidden state [n][hidden] to the next rank over NCCL, each stage runs its
+// contiguous layer range and passes it on, the last stage sends it back to
+// the coordinator, which projects the last row.  Every hop is stream-ordered
+// on the GPUs; the host only sees the token id.
+
+extern "C" {
+
+int flock_comm_send_hidden(flock_comm* c, flock_model* m, int n_tokens, int peer) {
+  if (!c || !m || n_tokens < 1 || n_tokens > m->ws.P) return FLOCK_E_ARG;
+  FLOCK_TRY(comm_send(c, m->ws.h.p, (size_t)n_tokens * m->cfg.hidden, peer));
+  return comm_wait(c);
+}
+
+int flock_comm_recv_hidden(flock_comm* c, flock_model* m, int n_tokens, int peer) {
+  if (!c || !m || n_tokens < 1 || n_tokens > m->ws.P) return FLOCK_E_ARG;
+  FLOCK_TRY(comm_recv(c, m->ws.h.p, (size_t)n_tokens * m->cfg.hidden, peer));
+  return comm_wait(c);
+}
+
+int flock_pipeline_step(flock_model* m, flock_comm* c, const int32_t* ids, int n, int sync,
+                        int32_t* next_id) {
+  if (!m || n < 1 || n > m->cfg.max_prefill) {
+    set_error("pipeline step of %d tokens: 1..maxPrefill %d", n, m ? m->cfg.max_prefill : 0);
+    return FLOCK_E_ARG;
+  }
+  int rank = 0, nr = 1;
+  if (c) FLOCK_TRY(comm_rank(c, &rank, &nr));
+  FLOCK_CK(cudaSetDevice(m->dev->ordinal));
+  FLOCK_TRY(check_room(m, n));
+  const size_t nf = (size_t)n * m->cfg.hidden;
+  if (rank == 0) {
+    FLOCK_TRY(need_head(m));
+    if (ids) FLOCK_TRY(upload_ids(m, ids, n));
+    FLOCK_TRY(enqueue_embed(m, n));
+    FLOCK_TRY(enqueue_layers(m, n));
+    if (nr > 1) {
+      FLOCK_TRY(comm_send(c, m->ws.h.p, nf, 1));
+      FLOCK_TRY(comm_recv(c, m->ws.h.p, nf, nr - 1));
+    }
+    FLOCK_TRY(enqueue_head(m, n - 1));
+    FLOCK_TRY(enqueue_record(m));
+  } else {
+    FLOCK_TRY(comm_recv(c, m->ws.h.p, nf, rank - 1));
+    FLOCK_TRY(enqueue_layers(m, n));
+    FLOCK_TRY(comm_send(c, m->ws.h.p, nf, (rank + 1) % nr));
+  }
+  m->pos += n;
+  for (auto* L : m->layers) L->n_keys = m->pos;
+  if (rank == 0 && next_id)
+    FLOCK_CK(cudaMemcpyAsync(next_id, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
+  if (sync) return c ? comm_wait(c) : (cudaStreamSynchronize(m->dev->stream) == cudaSuccess
+                                           ? FLOCK_OK : FLOCK_E_CUDA);
+  return FLOCK_OK;
+}
+
+int flock_model_history(flock_model* m, int start, int n, int32_t* out) {
+  if (!m || start < 0 || n < 0 || start + n > m->cfg.max_keys || (n && !out)) return FLOCK_E_ARG;
+  if (n)
+    FLOCK_CK(cudaMemcpyAsync(out, m->hist.as<int32_t>() + start, (size_t)n * 4,
+                             cudaMemcpyDeviceToHost, m->dev->stream));
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
+}
+
+}  // extern "C"

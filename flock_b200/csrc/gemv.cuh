@@ -1,0 +1,403 @@
+// Q8_0 / Q4_0 dequantising matvec for B200, in the reference's exact f32 order.
+//
+// What it computes (kernels/q8_coop.wgsl:76, kernels/q4_coop.wgsl:48, CPU
+// model kernels/lib.ts:213 matmulF32 with coop(64)): for row r,
+//   logical lane l in [0,64) walks blocks b = l, l+64, l+128, ... and folds
+//   scale_b * (dot4(q[8g..8g+3], x) + dot4(q[8g+4..8g+7], x)) into its own
+//   accumulator for g = 0..3 (Q4_0: q[4g..4g+3] / q[4g+16..4g+19]);
+//   the 64 accumulators are then summed by the pairwise tree.
+// The result is bit-identical to cpuMatmulQ8F32(coop(64)) / cpuMatmulQ4F32.
+//
+// How it is laid out on the GPU (not how the WGSL is): one warp owns a group
+// of R rows; lane t of the warp plays logical lanes t and t+32, i.e. blocks
+// t + 32m with m even (lane t) and m odd (lane t+32).  A warp therefore reads
+// each row as contiguous 1 KiB runs of qs -- fully coalesced 128-bit streams
+// straight from HBM -- and the tree's first level (stride 32) is a register
+// add, the remaining five are warp shuffles.  x lives in shared memory (with
+// the attn/ffn/output RMSNorm optionally fused into the load) and the first
+// MX of each thread's x blocks are held in registers for the whole kernel.
+//
+// Launch: persistent-style grid of <= 2 CTAs per SM; each warp strides over
+// row groups.  Before griddepcontrol.wait the kernel only touches weights: it
+// issues the L2 prefetch list for the NEXT kernel and the loads of its own
+// first row group, so both overlap the previous kernel's tail.
+#pragma once
+#include "common.cuh"
+
+namespace flock {
+
+enum { QT_Q8 = 0, QT_Q4 = 1 };
+enum { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+
+struct GemvSeg {
+  const uint8_t* qs;   // Q8: [rows][K] int8; Q4: [rows][K/32][16] nibble pairs
+  const uint16_t* sc;  // [rows][sc_stride] f16 scales
+  float* out;          // [n_tokens][out_stride]
+  int rows;
+  int sc_stride;
+  int out_stride;
+};
+
+struct GemvArgs {
+  GemvSeg seg[3];
+  int nseg;
+  int K;
+  int n_tokens;
+  // input: x [n_tokens][x_stride] or rmsnorm(norm_src[t], norm_gain)
+  const float* x;
+  int x_stride;
+  const float* norm_gain;  // non-null -> fused rmsnorm prologue (ops_ref.ts:20, WG=128)
+  float eps;
+  // epilogue inputs
+  const float* res;  // EPI_RESIDUAL: [n_tokens][res_stride]
+  int res_stride;
+  // EPI_ARGMAX: per-CTA partials, arrival counter, final (value, index)
+  float* am_val;
+  uint32_t* am_idx;
+  uint32_t* am_count;
+  float* am_best_val;
+  int32_t* am_best_idx;
+  int am_row_offset;  // added to the reported index (a row shard's first row)
+  // step control {pos, n_last}: advanced once by CTA (0,0) when non-null
+  int* ctl;
+  int ctl_n;
+  PrefetchList pf;
+};
+
+// Weights of one row in one 32-weight block, as loaded for one thread.
+template <int QT>
+struct BlockW;
+template <>
+struct BlockW<QT_Q8> {
+  uint4 w0, w1;
+  uint16_t s;
+};
+template <>
+struct BlockW<QT_Q4> {
+  uint4 w;
+  uint16_t s;
+};
+
+template <int QT>
+FLOCK_DEV void load_block(BlockW<QT>& bw, const GemvSeg& sg, int row, int b, int K);
+template <>
+FLOCK_DEV void load_block<QT_Q8>(BlockW<QT_Q8>& bw, const GemvSeg& sg, int row, int b, int K) {
+  const uint8_t* p = sg.qs + (size_t)row * K + (size_t)b * 32;
+  bw.w0 = ldg_stream(p);
+  bw.w1 = ldg_stream(p + 16);
+  bw.s = __ldg(sg.sc + (size_t)row * sg.sc_stride + b);
+}
+template <>
+FLOCK_DEV void load_block<QT_Q4>(BlockW<QT_Q4>& bw, const GemvSeg& sg, int row, int b, int K) {
+  const uint8_t* p = sg.qs + ((size_t)row * (K / 32) + b) * 16;
+  bw.w = ldg_stream(p);
+  bw.s = __ldg(sg.sc + (size_t)row * sg.sc_stride + b);
+}
+
+// Fold one block into acc in the reference order.  xb points at the block's
+// 32 x values (registers or shared memory).
+template <int QT>
+FLOCK_DEV float fold_block(const BlockW<QT>& bw, const float* xb, float acc);
+template <>
+FLOCK_DEV float fold_block<QT_Q8>(const BlockW<QT_Q8>& bw, const float* xb, float acc) {
+  const float s = scale_f16(bw.s);
+  const uint32_t w[8] = {bw.w0.x, bw.w0.y, bw.w0.z, bw.w0.w, bw.w1.x, bw.w1.y, bw.w1.z, bw.w1.w};
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    float a0, a1, a2, a3, c0, c1, c2, c3;
+    dec_i8x4(w[2 * g], a0, a1, a2, a3);
+    dec_i8x4(w[2 * g + 1], c0, c1, c2, c3);
+    const float* xa = xb + 8 * g;
+    float d0 = dot4(a0, a1, a2, a3, xa[0], xa[1], xa[2], xa[3]);
+    float d1 = dot4(c0, c1, c2, c3, xa[4], xa[5], xa[6], xa[7]);
+    acc = ffma(s, fadd(d0, d1), acc);
+  }
+  return acc;
+}
+template <>
+FLOCK_DEV float fold_block<QT_Q4>(const BlockW<QT_Q4>& bw, const float* xb, float acc) {
+  const float s = scale_f16(bw.s);
+  const uint32_t w[4] = {bw.w.x, bw.w.y, bw.w.z, bw.w.w};
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    float a0, a1, a2, a3, c0, c1, c2, c3;
+    dec_nib4(w[g] & 0x0F0F0F0Fu, a0, a1, a2, a3);
+    dec_nib4((w[g] >> 4) & 0x0F0F0F0Fu, c0, c1, c2, c3);
+    float d0 = dot4(a0, a1, a2, a3, xb[4 * g], xb[4 * g + 1], xb[4 * g + 2], xb[4 * g + 3]);
+    float d1 =
+        dot4(c0, c1, c2, c3, xb[16 + 4 * g], xb[17 + 4 * g], xb[18 + 4 * g], xb[19 + 4 * g]);
+    acc = ffma(s, fadd(d0, d1), acc);
+  }
+  return acc;
+}
+
+// kernels/argmax.wgsl:57 better(): strictly larger, or equal with lower index.
+FLOCK_DEV bool am_better(float va, uint32_t ia, float vb, uint32_t ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+// Fused RMSNorm prologue, exact ops_ref.ts:20 order with WG = 128:
+// part[t] = serial fma over i = t, t+128, ...; pairwise tree over 128;
+// scale = fr(1/sqrt(fr(fr(sum/n) + eps))); y = fr(fr(x*scale)*g).
+// Called by all GEMV_THREADS threads; writes y into xs[0..n).
+FLOCK_DEV void rmsnorm_to_smem(const float* __restrict__ src, const float* __restrict__ gain,
+                               int n, float eps, float* xs, float* red) {
+  const int t = threadIdx.x;
+  if (t < 128) {
+    float acc = 0.0f;
+    for (int i = t; i < n; i += 128) {
+      float v = src[i];
+      acc = ffma(v, v, acc);
+    }
+    red[t] = acc;
+  }
+  __syncthreads();
+  if (t < 64) red[t] = fadd(red[t], red[t + 64]);
+  __syncthreads();
+  if (t < 32) {
+    float v = fadd(red[t], red[t + 32]);
+    v = warp_tree_sum(v);
+    if (t == 0) red[128] = rsqrt_f64r(fadd(fdiv(v, (float)n), eps));
+  }
+  __syncthreads();
+  const float scale = red[128];
+  for (int i = t; i < n; i += GEMV_THREADS) xs[i] = fmul(fmul(src[i], scale), gain[i]);
+}
+
+// Resolve global row-group index -> (segment, first row).  Row groups never
+// straddle segments; each segment has ceil(rows / R) groups.
+template <int R>
+FLOCK_DEV bool group_of(const GemvArgs& a, int g, int& seg, int& row0) {
+#pragma unroll
+  for (int s = 0; s < 3; s++) {
+    if (s >= a.nseg) return false;
+    const int ng = (a.seg[s].rows + R - 1) / R;
+    if (g < ng) {
+      seg = s;
+      row0 = g * R;
+      return true;
+    }
+    g -= ng;
+  }
+  return false;
+}
+
+// MX: how many of each thread's x blocks stay in registers (0 = reload from
+// shared memory per row group).  For K <= 1024*MX every block is resident.
+template <int QT, int R, int EPI, int MX>
+__global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  float* xs = smem;                          // [K]
+  float* red = smem + a.K;                   // [132] reduction scratch
+  float* cta_val = red + 136;                // [GEMV_WARPS]
+  uint32_t* cta_idx = (uint32_t*)(cta_val + GEMV_WARPS);
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int tok = blockIdx.y;
+  const int nb = a.K / 32;
+  const int M = (nb + 31) / 32;
+
+  // Row groups: for SWIGLU segment 0 (gate) and 1 (up) are walked together,
+  // R/2 rows of each per group.
+  int n_groups;
+  if (EPI == EPI_SWIGLU) {
+    n_groups = (a.seg[0].rows + R / 2 - 1) / (R / 2);
+  } else {
+    n_groups = 0;
+    for (int s = 0; s < a.nseg; s++) n_groups += (a.seg[s].rows + R - 1) / R;
+  }
+  const int gwarp = blockIdx.x * GEMV_WARPS + warp;
+  const int nwarps = gridDim.x * GEMV_WARPS;
+
+  issue_prefetch(a.pf);
+  pdl_launch_dependents();
+  pdl_wait();
+
+  if (a.ctl && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+    a.ctl[0] += a.ctl[1];
+    a.ctl[1] = a.ctl_n;
+  }
+
+  // ---- x into shared memory (optionally normalised) ----
+  if (a.norm_gain) {
+    rmsnorm_to_smem(a.x + (size_t)tok * a.x_stride, a.norm_gain, a.K, a.eps, xs, red);
+  } else {
+    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)tok * a.x_stride);
+    for (int i = threadIdx.x; i < a.K / 4; i += GEMV_THREADS)
+      reinterpret_cast<float4*>(xs)[i] = src[i];
+  }
+  __syncthreads();
+
+  // Resident x blocks: block lane + 32m for m < MX.
+  float xr[MX > 0 ? MX : 1][32];
+#pragma unroll
+  for (int m = 0; m < MX; m++) {
+    const int b = lane + 32 * m;
+#pragma unroll
+    for (int i = 0; i < 32; i++) xr[m][i] = (b < nb) ? xs[b * 32 + i] : 0.0f;
+  }
+
+  float best_v = -FLT_MAX;
+  uint32_t best_i = 0xFFFFFFFFu;
+
+  for (int g = gwarp; g < n_groups; g += nwarps) {
+    // Rows of this group: pointers per slot.
+    int rseg[R], rrow[R];
+    bool rok[R];
+    if (EPI == EPI_SWIGLU) {
+      const int r0 = g * (R / 2);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        rseg[r] = r < R / 2 ? 0 : 1;
+        rrow[r] = r0 + (r % (R / 2));
+        rok[r] = rrow[r] < a.seg[0].rows;
+      }
+    } else {
+      int s, row0;
+      group_of<R>(a, g, s, row0);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        rseg[r] = s;
+        rrow[r] = row0 + r;
+        rok[r] = rrow[r] < a.seg[s].rows;
+      }
+    }
+
+    float accA[R], accB[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) accA[r] = accB[r] = 0.0f;
+
+    // One 32-weight column block of the group: load R rows, fold into the
+    // accumulator of logical lane (lane + 32 * (m & 1)).
+    auto step = [&](int m, const float* xb) {
+      const int b = lane + 32 * m;
+      if (b >= nb) return;
+      BlockW<QT> bw[R];
+#pragma unroll
+      for (int r = 0; r < R; r++)
+        if (rok[r]) load_block<QT>(bw[r], a.seg[rseg[r]], rrow[r], b, a.K);
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        if (!rok[r]) continue;
+        if (m & 1)
+          accB[r] = fold_block<QT>(bw[r], xb, accB[r]);
+        else
+          accA[r] = fold_block<QT>(bw[r], xb, accA[r]);
+      }
+    };
+#pragma unroll
+    for (int m = 0; m < MX; m++) step(m, xr[m]);
+    for (int m = MX; m < M; m++) step(m, xs + (lane + 32 * m) * 32);
+
+    float y[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) y[r] = warp_tree_sum(fadd(accA[r], accB[r]));
+
+    if (lane == 0) {
+      if (EPI == EPI_SWIGLU) {
+#pragma unroll
+        for (int r = 0; r < R / 2; r++) {
+          if (!rok[r]) continue;
+          // ops_ref.ts:103 swigluRef: fr(fr(g / fr(1 + fr(exp(-g)))) * up)
+          const float gt = y[r], up = y[r + R / 2];
+          const float e = exp_f64r(-gt);
+          const float sg = fdiv(gt, fadd(1.0f, e));
+          a.seg[0].out[(size_t)tok * a.seg[0].out_stride + rrow[r]] = fmul(sg, up);
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          if (!rok[r]) continue;
+          const GemvSeg& sg = a.seg[rseg[r]];
+          float v = y[r];
+          if (EPI == EPI_RESIDUAL) v = fadd(a.res[(size_t)tok * a.res_stride + rrow[r]], v);
+          sg.out[(size_t)tok * sg.out_stride + rrow[r]] = v;
+          if (EPI == EPI_ARGMAX) {
+            const uint32_t idx = (uint32_t)(rrow[r] + a.am_row_offset);
+            if (am_better(v, idx, best_v, best_i)) {
+              best_v = v;
+              best_i = idx;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  if (EPI == EPI_ARGMAX) {
+    // CTA reduction of the per-warp bests, then the last CTA to arrive
+    // reduces the per-CTA partials (kernels/argmax.wgsl pass1/pass2 fused).
+    if (lane == 0) {
+      cta_val[warp] = best_v;
+      cta_idx[warp] = best_i;
+    }
+    __syncthreads();
+    __shared__ bool last;
+    if (threadIdx.x == 0) {
+      float bv = cta_val[0];
+      uint32_t bi = cta_idx[0];
+      for (int w = 1; w < GEMV_WARPS; w++)
+        if (am_better(cta_val[w], cta_idx[w], bv, bi)) {
+          bv = cta_val[w];
+          bi = cta_idx[w];
+        }
+      a.am_val[blockIdx.x] = bv;
+      a.am_idx[blockIdx.x] = bi;
+      __threadfence();
+      const uint32_t prev = atomicAdd(a.am_count, 1u);
+      last = (prev == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (last) {
+      __threadfence();
+      float bv = -FLT_MAX;
+      uint32_t bi = 0xFFFFFFFFu;
+      for (int i = threadIdx.x; i < (int)gridDim.x; i += GEMV_THREADS) {
+        const float v = ((volatile float*)a.am_val)[i];
+        const uint32_t ix = ((volatile uint32_t*)a.am_idx)[i];
+        if (am_better(v, ix, bv, bi)) {
+          bv = v;
+          bi = ix;
+        }
+      }
+      // block reduce
+#pragma unroll
+      for (int s = 16; s > 0; s >>= 1) {
+        const float ov = __shfl_down_sync(0xffffffffu, bv, s);
+        const uint32_t oi = __shfl_down_sync(0xffffffffu, bi, s);
+        if (am_better(ov, oi, bv, bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (lane == 0) {
+        cta_val[warp] = bv;
+        cta_idx[warp] = bi;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        bv = cta_val[0];
+        bi = cta_idx[0];
+        for (int w = 1; w < GEMV_WARPS; w++)
+          if (am_better(cta_val[w], cta_idx[w], bv, bi)) {
+            bv = cta_val[w];
+            bi = cta_idx[w];
+          }
+        *a.am_best_val = bv;
+        *a.am_best_idx = (int32_t)bi;
+        *a.am_count = 0;  // re-arm for the next launch
+      }
+    }
+  }
+}
+
+// Shared-memory bytes a k_gemv launch needs.
+inline size_t gemv_smem_bytes(int K) {
+  return (size_t)K * 4 + (136 + GEMV_WARPS * 2) * 4 + 16;
+}
+
+}  // namespace flock

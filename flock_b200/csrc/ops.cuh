@@ -1,0 +1,388 @@
+// The non-matmul kernels of the decoder layer, in the reference's f32 order.
+//
+//   k_qk_norm_rope_append  kernels/rmsnorm.wgsl + rope.wgsl + the KV copies of
+//                          layer.ts:620-622, fused: per-head RMSNorm (q_norm /
+//                          k_norm, ops_ref.ts:20), RoPE (ops_ref.ts:65) at
+//                          position pos0 + token, k and v appended to the cache.
+//   k_attn_decode_exact    kernels/attention.wgsl / ops_ref.ts:135 attnRef:
+//                          two-pass softmax, serial sums in key order.
+//   k_attn_prefill_exact   kernels/attention_prefill.wgsl / head_ref.ts:99:
+//                          streaming softmax over 64-key tiles, WG = 128 trees.
+//   k_embed                kernels/embed.wgsl / head_ref.ts:34.
+//   k_rmsnorm, k_add, k_swiglu, k_argmax  the standalone forms used by the
+//                          op-level API (rmsnorm.wgsl, elementwise.wgsl,
+//                          argmax.wgsl).
+#pragma once
+#include "common.cuh"
+
+namespace flock {
+
+// Tree over 128 values in shared memory (kernels/lib.ts:312 order); all 128
+// threads of the block call it; returns the sum to every thread.
+FLOCK_DEV float block128_tree_sum(float v, float* red) {
+  const int t = threadIdx.x;
+  red[t] = v;
+  __syncthreads();
+  if (t < 64) red[t] = fadd(red[t], red[t + 64]);
+  __syncthreads();
+  if (t < 32) {
+    float w = fadd(red[t], red[t + 32]);
+    w = warp_tree_sum(w);
+    if (t == 0) red[128] = w;
+  }
+  __syncthreads();
+  const float r = red[128];
+  __syncthreads();
+  return r;
+}
+
+FLOCK_DEV float fmax_js(float a, float b) { return a > b ? a : b; }
+
+// Tree max over 128 values (head_ref.ts:186 treeReduce(part, Math.max)).
+FLOCK_DEV float block128_tree_max(float v, float* red) {
+  const int t = threadIdx.x;
+  red[t] = v;
+  __syncthreads();
+  if (t < 64) red[t] = fmax_js(red[t], red[t + 64]);
+  __syncthreads();
+  if (t < 32) {
+    float w = fmax_js(red[t], red[t + 32]);
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) w = fmax_js(w, __shfl_down_sync(0xffffffffu, w, s));
+    if (t == 0) red[128] = w;
+  }
+  __syncthreads();
+  const float r = red[128];
+  __syncthreads();
+  return r;
+}
+
+struct QkArgs {
+  const float* q;   // [n][nH][hd] raw projections
+  const float* k;   // [n][nKV][hd]
+  const float* v;   // [n][nKV][hd]
+  const float* q_norm;
+  const float* k_norm;
+  const float* inv_freq;  // [hd/2]
+  float* qn;        // [n][nH][hd] out
+  float* kcache;    // [maxKeys][nKV][hd]
+  float* vcache;
+  const int* ctl;   // ctl[0] = pos0
+  int n_tokens, n_heads, n_kv_heads, head_dim;
+  float eps;
+  int neox;
+  PrefetchList pf;
+};
+
+// One block of 128 threads per (token, head-vector); head_dim must be 128.
+static __global__ void __launch_bounds__(128) k_qk_norm_rope_append(const QkArgs a) {
+  __shared__ float red[132];
+  __shared__ float y[128];
+  issue_prefetch(a.pf);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int nvec = a.n_heads + a.n_kv_heads;
+  const int tok = blockIdx.x / nvec, hv = blockIdx.x % nvec;
+  const int t = threadIdx.x, hd = a.head_dim;
+  const bool is_q = hv < a.n_heads;
+  const int kvh = hv - a.n_heads;
+  const int pos0 = a.ctl[0];
+  const float* src = is_q ? a.q + ((size_t)tok * a.n_heads + hv) * hd
+                          : a.k + ((size_t)tok * a.n_kv_heads + kvh) * hd;
+  const float* gain = is_q ? a.q_norm : a.k_norm;
+  // rmsnorm over one head (n = WG = 128: each partial is one fma32(x, x, 0))
+  const float x = src[t];
+  const float sum = block128_tree_sum(ffma(x, x, 0.0f), red);
+  const float scale = rsqrt_f64r(fadd(fdiv(sum, (float)hd), a.eps));
+  y[t] = fmul(fmul(x, scale), gain[t]);
+  __syncthreads();
+  // RoPE at absolute position pos0 + tok
+  const int half = hd / 2;
+  float* dst = is_q ? a.qn + ((size_t)tok * a.n_heads + hv) * hd
+                    : a.kcache + ((size_t)(pos0 + tok) * a.n_kv_heads + kvh) * hd;
+  if (t < half) {
+    const int j = t;
+    const float theta = fmul((float)(pos0 + tok), a.inv_freq[j]);
+    const float c = __double2float_rn(cos((double)theta));
+    const float s = __double2float_rn(sin((double)theta));
+    const int ia = a.neox ? j : 2 * j, ib = a.neox ? j + half : 2 * j + 1;
+    const float av = y[ia], bv = y[ib];
+    dst[ia] = ffma(-bv, s, fmul(av, c));
+    dst[ib] = ffma(bv, c, fmul(av, s));
+  }
+  if (!is_q) {
+    a.vcache[((size_t)(pos0 + tok) * a.n_kv_heads + kvh) * hd + t] =
+        a.v[((size_t)tok * a.n_kv_heads + kvh) * hd + t];
+  }
+}
+
+struct AttnArgs {
+  const float* q;  // [n][nH][hd] normalised + rotated
+  const float* kcache;
+  const float* vcache;
+  float* out;      // [n][nH][hd]
+  const int* ctl;  // ctl[0] = pos0 (keys before this batch)
+  int n_tokens, n_heads, n_kv_heads, head_dim;
+  PrefetchList pf;
+};
+
+// ops_ref.ts:135 attnRef for ONE query per head: one CTA per head, 256
+// threads.  Scores are serial FMA chains over head_dim (one key per thread),
+// the softmax sum is one serial chain in key order (thread 128), and each of
+// the 128 output channels is one serial chain over keys (threads 0..127), all
+// exactly as the reference orders them.  Dynamic smem: n_keys floats.
+static __global__ void __launch_bounds__(256) k_attn_decode_exact(const AttnArgs a) {
+  extern __shared__ float sc[];  // [n_keys] scores, then exp values
+  __shared__ float qs[128];
+  __shared__ float red[260];
+  __shared__ float inv_s;
+  issue_prefetch(a.pf);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int h = blockIdx.x, t = threadIdx.x, hd = a.head_dim;
+  const int kvh = h / (a.n_heads / a.n_kv_heads);
+  const int n_keys = a.ctl[0] + 1;
+  const float scale = __double2float_rn(1.0 / sqrt((double)hd));
+  if (t < hd) qs[t] = a.q[(size_t)h * hd + t];
+  __syncthreads();
+  for (int key = t; key < n_keys; key += blockDim.x) {
+    const float4* kr =
+        reinterpret_cast<const float4*>(a.kcache + ((size_t)key * a.n_kv_heads + kvh) * hd);
+    float acc = 0.0f;
+    for (int i4 = 0; i4 < hd / 4; i4++) {
+      const float4 kv = kr[i4];
+      acc = ffma(qs[4 * i4 + 0], kv.x, acc);
+      acc = ffma(qs[4 * i4 + 1], kv.y, acc);
+      acc = ffma(qs[4 * i4 + 2], kv.z, acc);
+      acc = ffma(qs[4 * i4 + 3], kv.w, acc);
+    }
+    sc[key] = fmul(acc, scale);
+  }
+  __syncthreads();
+  // max (exact in any order)
+  float m = -INFINITY;
+  for (int key = t; key < n_keys; key += blockDim.x) m = fmax_js(m, sc[key]);
+  red[t] = m;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if (t < s) red[t] = fmax_js(red[t], red[t + s]);
+    __syncthreads();
+  }
+  const float mx = red[0];
+  __syncthreads();
+  for (int key = t; key < n_keys; key += blockDim.x) sc[key] = exp_f64r(fsub(sc[key], mx));
+  __syncthreads();
+  if (t == 128) {
+    float sum = 0.0f;
+    for (int key = 0; key < n_keys; key++) sum = fadd(sum, sc[key]);
+    inv_s = __double2float_rn(1.0 / (double)sum);
+  }
+  float acc = 0.0f;
+  if (t < hd) {
+    const float* vr = a.vcache + (size_t)kvh * hd + t;
+    const size_t vstride = (size_t)a.n_kv_heads * hd;
+    for (int key = 0; key < n_keys; key++) acc = ffma(sc[key], vr[key * vstride], acc);
+  }
+  __syncthreads();
+  if (t < hd) a.out[(size_t)h * hd + t] = fmul(acc, inv_s);
+}
+
+// head_ref.ts:99 attnPrefillRef / attention_prefill.wgsl: one CTA of 128
+// threads per (head, query); TILE = 64 keys; tree reductions over WG = 128.
+static __global__ void __launch_bounds__(128) k_attn_prefill_exact(const AttnArgs a) {
+  constexpr int TILE = 64, WG = 128;
+  __shared__ float tile_s[TILE];
+  __shared__ float red[132];
+  __shared__ float qs[128];
+  issue_prefetch(a.pf);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int h = blockIdx.x, qi = blockIdx.y, t = threadIdx.x, hd = a.head_dim;
+  const int kvh = h / (a.n_heads / a.n_kv_heads);
+  const float scale = __double2float_rn(1.0 / sqrt((double)hd));
+  const int pos0 = a.ctl[0];
+  const int n_keys = pos0 + qi + 1;
+  const size_t qbase = ((size_t)qi * a.n_heads + h) * hd;
+  if (t < hd) qs[t] = a.q[qbase + t];
+  __syncthreads();
+  float m = -INFINITY, l = 0.0f, acc = 0.0f;
+  const size_t kvstride = (size_t)a.n_kv_heads * hd;
+  for (int base = 0; base < n_keys; base += TILE) {
+    const int n_this = min(TILE, n_keys - base);
+    if (t < n_this) {
+      const float4* kr = reinterpret_cast<const float4*>(a.kcache + (base + t) * kvstride +
+                                                         (size_t)kvh * hd);
+      float s = 0.0f;
+      for (int i4 = 0; i4 < hd / 4; i4++) {
+        const float4 kv = kr[i4];
+        s = ffma(qs[4 * i4 + 0], kv.x, s);
+        s = ffma(qs[4 * i4 + 1], kv.y, s);
+        s = ffma(qs[4 * i4 + 2], kv.z, s);
+        s = ffma(qs[4 * i4 + 3], kv.w, s);
+      }
+      tile_s[t] = fmul(s, scale);
+    }
+    __syncthreads();
+    // tile max: thread t owns j = t (n_this <= TILE < WG)
+    const float tmax = block128_tree_max(t < n_this ? tile_s[t] : -INFINITY, red);
+    const float m_new = fmax_js(m, tmax);
+    const float corr = exp_f64r(fsub(m, m_new));
+    float e = 0.0f;
+    if (t < n_this) {
+      e = exp_f64r(fsub(tile_s[t], m_new));
+    }
+    __syncthreads();
+    if (t < n_this) tile_s[t] = e;
+    const float tsum = block128_tree_sum(fadd(0.0f, e), red);  // ts = fr(0 + e)
+    if (t < hd) {
+      float av = fmul(acc, corr);
+      const float* vr = a.vcache + (size_t)base * kvstride + (size_t)kvh * hd + t;
+      for (int j = 0; j < n_this; j++) av = ffma(tile_s[j], vr[j * kvstride], av);
+      acc = av;
+    }
+    l = ffma(l, corr, tsum);
+    m = m_new;
+    __syncthreads();
+  }
+  if (t < hd) a.out[qbase + t] = fdiv(acc, l);
+}
+
+struct EmbedArgs {
+  const uint8_t* qs;   // [vocab][hidden] int8
+  const uint16_t* sc;  // [vocab][sc_stride]
+  const int32_t* ids;
+  float* out;          // [n][hidden]
+  int n_tokens, hidden, sc_stride;
+  int vocab;           // rows of the table; an id outside it embeds as zeros
+  PrefetchList pf;
+};
+
+// kernels/embed.wgsl:52: gather one Q8_0 row per token and dequantise it.
+static __global__ void __launch_bounds__(256) k_embed(const EmbedArgs a) {
+  issue_prefetch(a.pf);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tok = blockIdx.x;
+  const int64_t row = a.ids[tok];
+  const int n4 = a.hidden / 4;
+  if (row < 0 || row >= a.vocab) {  // never read outside the table
+    for (int g = threadIdx.x; g < n4; g += blockDim.x)
+      reinterpret_cast<float4*>(a.out + (size_t)tok * a.hidden)[g] = make_float4(0, 0, 0, 0);
+    return;
+  }
+  for (int g = threadIdx.x; g < n4; g += blockDim.x) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(a.qs + row * a.hidden + 4 * g);
+    const float s = scale_f16(a.sc[row * a.sc_stride + g / 8]);
+    float q0, q1, q2, q3;
+    dec_i8x4(w, q0, q1, q2, q3);
+    float4 o = make_float4(fmul(q0, s), fmul(q1, s), fmul(q2, s), fmul(q3, s));
+    reinterpret_cast<float4*>(a.out + (size_t)tok * a.hidden)[g] = o;
+  }
+}
+
+// kernels/rmsnorm.wgsl:41 standalone: one 128-thread block per vector.
+static __global__ void __launch_bounds__(128) k_rmsnorm(const float* x, const float* g, float* out, int n,
+                                                 int n_vecs, float eps) {
+  __shared__ float red[132];
+  const int v = blockIdx.x, t = threadIdx.x;
+  const float* xv = x + (size_t)v * n;
+  float acc = 0.0f;
+  for (int i = t; i < n; i += 128) acc = ffma(xv[i], xv[i], acc);
+  const float sum = block128_tree_sum(acc, red);
+  const float scale = rsqrt_f64r(fadd(fdiv(sum, (float)n), eps));
+  for (int i = t; i < n; i += 128) out[(size_t)v * n + i] = fmul(fmul(xv[i], scale), g[i]);
+}
+
+// kernels/elementwise.wgsl:31 add / :23 swiglu
+static __global__ void k_add(const float* a, const float* b, float* o, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) o[i] = fadd(a[i], b[i]);
+}
+static __global__ void k_swiglu(const float* g, const float* u, float* o, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float gv = g[i];
+    o[i] = fmul(fdiv(gv, fadd(1.0f, exp_f64r(-gv))), u[i]);
+  }
+}
+
+// kernels/argmax.wgsl pass1+pass2 as one launch: per-CTA (value, index)
+// partials, and the last CTA to arrive reduces them.  Same better() rule.
+static __global__ void __launch_bounds__(256) k_argmax(const float* x, int64_t n, float* pval,
+                                                uint32_t* pidx, uint32_t* count, float* best_val,
+                                                int32_t* best_idx, int64_t index_offset) {
+  __shared__ float wv[8];
+  __shared__ uint32_t wi[8];
+  __shared__ bool last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float bv = -FLT_MAX;
+  uint32_t bi = 0xFFFFFFFFu;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const uint32_t ix = (uint32_t)(i + index_offset);
+    if (v > bv || (v == bv && ix < bi)) {
+      bv = v;
+      bi = ix;
+    }
+  }
+  auto reduce = [&](float& v, uint32_t& ix) {
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+      const float ov = __shfl_down_sync(0xffffffffu, v, s);
+      const uint32_t oi = __shfl_down_sync(0xffffffffu, ix, s);
+      if (ov > v || (ov == v && oi < ix)) {
+        v = ov;
+        ix = oi;
+      }
+    }
+    if (lane == 0) {
+      wv[warp] = v;
+      wi[warp] = ix;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < (int)(blockDim.x / 32); w++)
+        if (wv[w] > wv[0] || (wv[w] == wv[0] && wi[w] < wi[0])) {
+          wv[0] = wv[w];
+          wi[0] = wi[w];
+        }
+    }
+    __syncthreads();
+  };
+  reduce(bv, bi);
+  if (threadIdx.x == 0) {
+    pval[blockIdx.x] = wv[0];
+    pidx[blockIdx.x] = wi[0];
+    __threadfence();
+    last = atomicAdd(count, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  bv = -FLT_MAX;
+  bi = 0xFFFFFFFFu;
+  for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
+    const float v = ((volatile float*)pval)[i];
+    const uint32_t ix = ((volatile uint32_t*)pidx)[i];
+    if (v > bv || (v == bv && ix < bi)) {
+      bv = v;
+      bi = ix;
+    }
+  }
+  reduce(bv, bi);
+  if (threadIdx.x == 0) {
+    *best_val = wv[0];
+    *best_idx = (int32_t)wi[0];
+    *count = 0;
+  }
+}
+
+// Advance a step-control block {pos, n_last} without any other work
+// (used where no GEMV precedes attention, e.g. an attention-only op call).
+static __global__ void k_ctl_advance(int* ctl, int n) {
+  ctl[0] += ctl[1];
+  ctl[1] = n;
+}
+
+}  // namespace flock

@@ -1,0 +1,298 @@
+/*
+ * flock_cuda.h -- C ABI of libflock_cuda.so, the B200 (sm_100a) replacement
+ * for flock's per-token Qwen3 hot path (the kernels/ module of
+ * ethanhinson/flock).  Plain C types only: a Deno.dlopen / ctypes / cgo
+ * binding can bind every symbol below without a C++ or CUDA header.
+ *
+ * Conventions
+ *  - Every call returns an int status: FLOCK_OK (0) or a negative FLOCK_E_*
+ *    code; flock_last_error() returns the calling thread's message, worded
+ *    like the reference's thrown Error where one exists.
+ *  - Host pointers passed in are read during the call and not retained;
+ *    host output pointers are written before the call returns (the call
+ *    synchronises the handle's stream when it returns data to the host).
+ *  - Handles are opaque.  A handle is bound to one device and one CUDA
+ *    stream and is not thread-safe (the reference is single-threaded: one JS
+ *    event loop, one conversation, docs/ARCHITECTURE.md:295-296).
+ *  - Matrices are [rows][cols] row-major, rows = output size, cols = input
+ *    size (GGUF lists the shape as [cols, rows]; kernels/layer.ts:20-22).
+ *
+ * Reference interfaces are cited as file:line within ethanhinson/flock.
+ */
+#ifndef FLOCK_CUDA_H
+#define FLOCK_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(FLOCK_BUILD)
+#define FLOCK_API __attribute__((visibility("default")))
+#else
+#define FLOCK_API
+#endif
+
+#define FLOCK_OK 0
+#define FLOCK_E_ARG (-1)     /* bad argument / shape (reference: throw new Error) */
+#define FLOCK_E_CUDA (-2)    /* CUDA runtime error */
+#define FLOCK_E_STATE (-3)   /* KV cache full, offset mismatch, maxPrefill exceeded */
+#define FLOCK_E_MISSING (-4) /* a required tensor is missing (layer.ts:269-287) */
+#define FLOCK_E_LIMIT (-5)   /* a shard does not fit its binding/memory limit (shard.ts:229-243) */
+#define FLOCK_E_NCCL (-6)    /* NCCL error or timeout */
+#define FLOCK_E_NOMEM (-7)   /* device allocation failed */
+#define FLOCK_E_UNSUPPORTED (-8)
+
+#define FLOCK_Q8_0 8  /* 34-byte blocks: f16 scale + 32 int8 (lib.ts:25-26) */
+#define FLOCK_Q4_0 4  /* 18-byte blocks: f16 scale + 16 nibble pairs (lib.ts:27-28) */
+#define FLOCK_F32 32  /* plain f32 (norm gains) */
+
+#define FLOCK_ROPE_NEOX 0 /* pairs (j, j+hd/2): HuggingFace halves (lib.ts:526) */
+#define FLOCK_ROPE_NORM 1 /* pairs (2j, 2j+1): GGUF adjacent */
+
+#define FLOCK_ATTN_EXACT 0 /* decode attention in attnRef's exact order (ops_ref.ts:135) */
+#define FLOCK_ATTN_FAST 1  /* split-K flash-decode; no key cap; tolerance 1e-5 rel */
+
+typedef struct flock_dev flock_dev;
+typedef struct flock_tensor flock_tensor;
+typedef struct flock_layer flock_layer;
+typedef struct flock_model flock_model;
+typedef struct flock_shard flock_shard;
+typedef struct flock_head flock_head;
+typedef struct flock_comm flock_comm;
+
+/* kernels/layer.ts:87-112 LayerConfig (+ the decode-attention choice). */
+typedef struct flock_layer_config {
+  int32_t hidden;       /* 1024 */
+  int32_t n_heads;      /* 16 */
+  int32_t n_kv_heads;   /* 8 */
+  int32_t head_dim;     /* 128 (the kernels require 128) */
+  int32_t ffn;          /* 3072 */
+  float eps;            /* f32(1e-6) */
+  double rope_base;     /* 1e6 */
+  int32_t max_keys;     /* KV cache capacity */
+  int32_t max_prefill;  /* largest prefill batch (sizes activations) */
+  int32_t rope_pairing; /* FLOCK_ROPE_NEOX | FLOCK_ROPE_NORM */
+  int32_t attention;    /* FLOCK_ATTN_EXACT | FLOCK_ATTN_FAST */
+} flock_layer_config;
+
+/* ------------------------------------------------------------- errors/dev */
+
+/* The calling thread's last error message ("" if none). */
+FLOCK_API const char* flock_last_error(void);
+/* Library version string, e.g. "flock_b200 0.1 sm_100a". */
+FLOCK_API const char* flock_version(void);
+
+/* kernels/lib.ts:385 getDevice(): open GPU `ordinal` with its own stream. */
+FLOCK_API int flock_dev_open(int ordinal, flock_dev** out);
+FLOCK_API int flock_dev_close(flock_dev* dev);
+/* Wait for all work queued on the device handle's stream. */
+FLOCK_API int flock_dev_sync(flock_dev* dev);
+/* Number of SMs, for launch planning by callers. */
+FLOCK_API int flock_dev_sm_count(flock_dev* dev, int* out);
+/* Device-event timing around the handle's stream: start, stop, elapsed ms. */
+FLOCK_API int flock_dev_timer_start(flock_dev* dev);
+FLOCK_API int flock_dev_timer_stop(flock_dev* dev, float* ms);
+
+/* --------------------------------------------------------------- repack */
+
+/* kernels/lib.ts:126 splitQ8: 34-byte blocks -> qs [rows*cols] + scales
+ * [rows*cols/32*2], byte for byte.  Pure host code, no device needed. */
+FLOCK_API int flock_repack_q8(const uint8_t* packed, int64_t rows, int64_t cols, uint8_t* qs_out,
+                    uint8_t* scales_out);
+/* kernels/lib.ts:142 splitQ4: 18-byte blocks -> qs [rows*cols/2] + scales. */
+FLOCK_API int flock_repack_q4(const uint8_t* packed, int64_t rows, int64_t cols, uint8_t* qs_out,
+                    uint8_t* scales_out);
+
+/* -------------------------------------------------------------- tensors */
+
+/* kernels/layer.ts:289 Layer.create's per-tensor path: split the packed GGUF
+ * blocks on the host and upload (dtype FLOCK_Q8_0 or FLOCK_Q4_0). */
+FLOCK_API int flock_tensor_from_packed(flock_dev* dev, int dtype, const uint8_t* packed, int64_t rows,
+                             int64_t cols, flock_tensor** out);
+/* web/js/gguf-stream.mjs:281 streamTensorToGPU / layer.ts:73 GpuTensor
+ * {qs, scales}: upload planes that are already split (fromBuffers path). */
+FLOCK_API int flock_tensor_from_split(flock_dev* dev, int dtype, const uint8_t* qs, const uint8_t* scales,
+                            int64_t rows, int64_t cols, flock_tensor** out);
+/* layer.ts:73 GpuTensor {data}: an f32 tensor (norm gains). */
+FLOCK_API int flock_tensor_from_f32(flock_dev* dev, const float* data, int64_t n, flock_tensor** out);
+FLOCK_API int flock_tensor_free(flock_tensor* t);
+/* Bytes resident on the device for the tensor (qs + scales, or data). */
+FLOCK_API int flock_tensor_bytes(const flock_tensor* t, int64_t* out);
+
+/* ---------------------------------------------------- op-level kernels
+ * The individually validated kernels, with host inputs/outputs, as the
+ * reference's kernel tests drive them (kernels/test_coop.ts, test_ops.ts,
+ * test_head.ts, test_prefill.ts). */
+
+/* kernels/q8_coop.wgsl:76 / q4_coop.wgsl:48: out[t][r] = W x[t] for n_tokens
+ * rows of x ([n_tokens][cols] -> [n_tokens][rows]). */
+FLOCK_API int flock_op_matvec(flock_dev* dev, const flock_tensor* w, const float* x, int n_tokens,
+                    float* out);
+/* Device-resident timing of the matvec (bench.ts:195 timeBatched's role):
+ * `iters` back-to-back launches on a seeded device x, CUDA-event timed;
+ * writes the mean milliseconds per launch. */
+FLOCK_API int flock_op_matvec_timed(flock_dev* dev, const flock_tensor* w, int n_tokens, int iters,
+                                    float* ms_per_call);
+/* kernels/rmsnorm.wgsl:41: n_vecs vectors of width n. */
+FLOCK_API int flock_op_rmsnorm(flock_dev* dev, const float* x, const float* g, int n, int n_vecs, float eps,
+                     float* out);
+/* kernels/rope.wgsl:50 on [n_tokens][n_heads][head_dim] at pos0 + token. */
+FLOCK_API int flock_op_rope(flock_dev* dev, const float* x, int n_tokens, int n_heads, int head_dim,
+                  int pos0, const float* inv_freq, int pairing, float* out);
+/* kernels/elementwise.wgsl:23 swiglu / :31 add. */
+FLOCK_API int flock_op_swiglu(flock_dev* dev, const float* gate, const float* up, int64_t n, float* out);
+FLOCK_API int flock_op_add(flock_dev* dev, const float* a, const float* b, int64_t n, float* out);
+/* kernels/attention.wgsl:58: one query per head over n_keys keys of
+ * [n_keys][n_kv_heads][head_dim]; mode FLOCK_ATTN_EXACT | FLOCK_ATTN_FAST. */
+FLOCK_API int flock_op_attention(flock_dev* dev, const float* q, const float* k, const float* v,
+                       int n_heads, int n_kv_heads, int head_dim, int n_keys, int mode,
+                       float* out);
+/* kernels/attention_prefill.wgsl:75: n_queries causal queries at pos0. */
+FLOCK_API int flock_op_attention_prefill(flock_dev* dev, const float* q, const float* k, const float* v,
+                               int n_heads, int n_kv_heads, int head_dim, int n_queries,
+                               int pos0, float* out);
+/* kernels/embed.wgsl:52: gather + dequantise rows of a Q8_0 tensor. */
+FLOCK_API int flock_op_embed(flock_dev* dev, const flock_tensor* table, const int32_t* ids, int n,
+                   float* out);
+/* kernels/argmax.wgsl:83,112: lowest index among the maxima. */
+FLOCK_API int flock_op_argmax(flock_dev* dev, const float* x, int64_t n, int64_t* index, float* value);
+
+/* ---------------------------------------------------------------- layer */
+
+/* kernels/layer.ts:228 Layer.fromBuffers: `names` are the GGUF suffixes
+ * ("attn_q.weight", ..., "ffn_norm.weight"); the layer borrows the tensors
+ * (they must outlive it).  Missing tensors -> FLOCK_E_MISSING naming them. */
+FLOCK_API int flock_layer_create(flock_dev* dev, const flock_layer_config* cfg, int n_tensors,
+                       const char* const* names, flock_tensor* const* tensors,
+                       flock_layer** out);
+FLOCK_API int flock_layer_free(flock_layer* layer);
+/* kernels/layer.ts:571 encode (n_tokens == 1) / :685 encodePrefill
+ * (n_tokens > 1): consume `hidden` ([n_tokens][hidden]; NULL = the previous
+ * output, already on the device), append n_tokens keys, leave the output on
+ * the device.  Throws-equivalents: KV full, maxPrefill exceeded. */
+FLOCK_API int flock_layer_encode(flock_layer* layer, const float* hidden, int n_tokens);
+/* kernels/layer.ts:801 readOutput(nTokens). */
+FLOCK_API int flock_layer_read_output(flock_layer* layer, int n_tokens, float* out);
+/* kernels/layer.ts:451 reset(); Layer.nKeys. */
+FLOCK_API int flock_layer_reset(flock_layer* layer);
+FLOCK_API int flock_layer_n_keys(const flock_layer* layer, int* out);
+/* Drop the cache back to n_keys (model.ts:529 rewind, per layer). */
+FLOCK_API int flock_layer_rewind(flock_layer* layer, int n_keys);
+/* kernels/layer.ts:792 cacheBuffers(): copy keys/values [n_keys][nKV][hd]. */
+FLOCK_API int flock_layer_read_cache(flock_layer* layer, float* k_out, float* v_out);
+/* Preload keys/values at the current position (a synthetic cache). */
+FLOCK_API int flock_layer_write_cache(flock_layer* layer, const float* k, const float* v, int n_keys);
+
+/* web/bird.html:544-620 runFrame / tools/sim_bird.mjs:326-340: run `x`
+ * ([seq][hidden]) through `n_layers` held layers in order at cache offset
+ * `offset` (checked against every layer's nKeys unless `reset`, which
+ * clears the caches first, wire.mjs FLAG_RESET), write [seq][hidden]. */
+FLOCK_API int flock_range_forward(flock_layer* const* layers, int n_layers, const float* x, int seq,
+                        int offset, int reset, float* out);
+
+/* ---------------------------------------------------------------- model */
+
+/* kernels/model.ts:109 Model.create(dev, m, cfg, {cut}): `layer_tensors` is
+ * n_layers * 11 tensors in the order attn_q, attn_k, attn_v, attn_output,
+ * ffn_gate, ffn_up, ffn_down, attn_norm, attn_q_norm, attn_k_norm,
+ * ffn_norm; `embd` the tied [vocab][hidden] Q8_0 table; `output` the untied
+ * lm-head or NULL (tied).  Holds layers 0..cut-1 (cut < 0: all). */
+FLOCK_API int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_layers,
+                       flock_tensor* const* layer_tensors, const flock_tensor* embd,
+                       const flock_tensor* output_norm, const flock_tensor* output, int cut,
+                       flock_model** out);
+FLOCK_API int flock_model_free(flock_model* m);
+/* kernels/model.ts:387 step(ids): prefill/decode ids, return the greedy id. */
+FLOCK_API int flock_model_step(flock_model* m, const int32_t* ids, int n, int32_t* next_id);
+/* kernels/model.ts:400 logits(ids): the [vocab] logits of the last position. */
+FLOCK_API int flock_model_logits(flock_model* m, const int32_t* ids, int n, float* logits);
+/* kernels/model.ts:409 hiddenState / :491 normedState. */
+FLOCK_API int flock_model_hidden_state(flock_model* m, const int32_t* ids, int n, float* out);
+FLOCK_API int flock_model_normed_state(flock_model* m, const int32_t* ids, int n, float* out);
+/* kernels/model.ts:546 embed(ids). */
+FLOCK_API int flock_model_embed(flock_model* m, const int32_t* ids, int n, float* out);
+/* kernels/model.ts:437 encodePartial(ids, offset): [n][hidden] after the held
+ * layers; offset < 0 skips the check. */
+FLOCK_API int flock_model_encode_partial(flock_model* m, const int32_t* ids, int n, int offset, float* out);
+/* kernels/model.ts:474 projectHidden(flat, seq): head on the last row. */
+FLOCK_API int flock_model_project_hidden(flock_model* m, const float* flat, int seq, int32_t* next_id);
+/* kernels/model.ts:572 generate(prompt, maxTokens, {eos}): host loop of
+ * step(), one 4-byte readback per token, stopping at an eos id. */
+FLOCK_API int flock_model_generate(flock_model* m, const int32_t* prompt, int n_prompt, int max_tokens,
+                         const int32_t* eos, int n_eos, int32_t* out_ids, int* n_out);
+/* Greedy decode with the token fed back on the device (no per-token host
+ * round trip): `n_steps` decode steps from the token the last step chose,
+ * replayed from one captured CUDA graph; ids are read back at the end. */
+FLOCK_API int flock_model_decode_device(flock_model* m, int n_steps, int32_t* out_ids);
+/* kernels/model.ts:199 reset() / :529 rewind(nKeys) / pos / held. */
+FLOCK_API int flock_model_reset(flock_model* m);
+FLOCK_API int flock_model_rewind(flock_model* m, int n_keys);
+FLOCK_API int flock_model_pos(const flock_model* m, int* out);
+FLOCK_API int flock_model_held(const flock_model* m, int* out);
+/* Set the token the next device-fed decode step consumes (ids[0]). */
+FLOCK_API int flock_model_set_token(flock_model* m, int32_t id);
+/* kernels/model.ts:541 currentToken(). */
+FLOCK_API int flock_model_current_token(flock_model* m, int32_t* out);
+
+/* --------------------------------------------------------------- shards */
+
+/* kernels/shard.ts:214 ShardedMatvec.create over a Q8_0 tensor given in the
+ * split layout ([rows][cols] qs + scales), direction 0 = row (output-split),
+ * 1 = col (input-split); binding_limit <= 0 means no limit.  All shards live
+ * on `dev` (the reference's single-device validation form). */
+FLOCK_API int flock_shard_matvec_create(flock_dev* dev, const uint8_t* qs, const uint8_t* scales,
+                              int64_t rows, int64_t cols, int n_shards, int direction,
+                              int64_t binding_limit, flock_shard** out);
+FLOCK_API int flock_shard_matvec_free(flock_shard* s);
+/* shard.ts:320 setInput + :340 encode + :400 output: y = W x. */
+FLOCK_API int flock_shard_matvec_run(flock_shard* s, const float* x, float* y);
+/* shard.ts:405 partials(): [n_shards][rows] (col direction only). */
+FLOCK_API int flock_shard_matvec_partials(flock_shard* s, float* parts);
+/* shard.ts:411 wireBytesPerCall(). */
+FLOCK_API int flock_shard_matvec_wire_bytes(const flock_shard* s, int64_t* out);
+
+/* kernels/shard.ts:502 ShardedHead.create: row-sharded LM head with
+ * per-shard argmax and the cross-shard reduce (shard_ref.ts:437). */
+FLOCK_API int flock_sharded_head_create(flock_dev* dev, const uint8_t* qs, const uint8_t* scales,
+                              int64_t vocab, int64_t hidden, int n_shards, flock_head** out);
+FLOCK_API int flock_sharded_head_free(flock_head* h);
+/* shard.ts:582 setInput + :595 encode: logits [vocab] (optional) and token. */
+FLOCK_API int flock_sharded_head_run(flock_head* h, const float* x, float* logits, int32_t* token);
+/* shard.ts:632 argmaxBuffers(): per-shard (value, local index, row offset). */
+FLOCK_API int flock_sharded_head_shard_argmax(flock_head* h, float* values, int64_t* index,
+                                    int64_t* row_offset);
+
+/* ------------------------------------------------- multi-GPU (NCCL) */
+
+/* NCCL unique id (128 bytes) for rank 0 to broadcast to the others. */
+FLOCK_API int flock_comm_unique_id(uint8_t id_out[128]);
+/* One communicator per process/GPU; timeout_ms bounds every collective. */
+FLOCK_API int flock_comm_init(flock_dev* dev, int n_ranks, int rank, const uint8_t id[128], int timeout_ms,
+                    flock_comm** out);
+FLOCK_API int flock_comm_free(flock_comm* c);
+/* Pipeline hop (replaces server/mesh.js:679 Flock.lap's wire hop): send /
+ * receive `n` f32 of device-resident hidden state to/from `peer`. */
+FLOCK_API int flock_comm_send_hidden(flock_comm* c, flock_model* m, int n_tokens, int peer);
+FLOCK_API int flock_comm_recv_hidden(flock_comm* c, flock_model* m, int n_tokens, int peer);
+/* One pipeline step on this rank (kernels/model.ts encodeTokens + encodeHead
+ * split across ranks, server/mesh.js:679 lap): rank 0 embeds `ids` (NULL =
+ * the id its head chose last step, already on the device), runs its layers,
+ * sends the hidden state on, receives it back from the last rank and runs
+ * the head; rank r > 0 receives, runs its layer range and sends on.  With
+ * sync = 0 nothing waits on the host (a device-resident decode loop).  A
+ * NULL communicator is the single-GPU case. */
+FLOCK_API int flock_pipeline_step(flock_model* m, flock_comm* c, const int32_t* ids, int n,
+                                  int sync, int32_t* next_id);
+/* Token ids the head chose at positions [start, start+n) (rank 0). */
+FLOCK_API int flock_model_history(flock_model* m, int start, int n, int32_t* out);
+/* Host-buffer all-reduce (sum, f32) and all-gather, for tests and planners. */
+FLOCK_API int flock_comm_allreduce_f32(flock_comm* c, const float* in, float* out, int64_t n);
+FLOCK_API int flock_comm_allgather_bytes(flock_comm* c, const void* in, void* out, int64_t bytes_per_rank);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLOCK_CUDA_H */

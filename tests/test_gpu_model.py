@@ -1,0 +1,136 @@
+"""Whole-model greedy decode vs the oracle composed the way kernels/model.ts
+wires it (embed -> layers -> output_norm -> tied head -> argmax), and the
+coordinator split (kernels/test_split.ts)."""
+import numpy as np
+import pytest
+
+from flock_b200 import lib as flib
+from flock_b200 import synth
+from flock_b200._abi import FlockError
+from flock_b200.layer import QWEN3_06B, Layer, range_forward
+from flock_b200.model import Model
+from gpu_util import n_mismatch
+
+pytestmark = pytest.mark.gpu
+
+S = synth.QWEN3_06B
+CFG = dict(hidden=S.hidden, n_heads=S.n_heads, n_kv_heads=S.n_kv_heads, head_dim=S.head_dim,
+           ffn=S.ffn)
+
+
+@pytest.fixture(scope="module")
+def dev():
+    d = flib.get_device(0)
+    yield d
+    d.close()
+
+
+class OracleModel:
+    """model.ts step() on the CPU oracle."""
+
+    def __init__(self, oracle, m, ieee=False):
+        self.o, self.m, self.ieee = oracle, m, ieee
+        self.layers = [oracle.RefLayer(w, CFG, 4096) for w in m.layers]
+
+    def step(self, ids):
+        o = self.o
+        o.set_fma_mode(self.ieee)
+        try:
+            n = len(ids)
+            h = o.embed(self.m.embd["packed"], ids, S.hidden)
+            for L in self.layers:
+                h = L.forward(h, n)
+            last = h[(n - 1) * S.hidden:]
+            tok, normed, logits = o.head(last, self.m.output_norm, self.m.embd["packed"],
+                                         self.m.vocab, S.hidden)
+        finally:
+            o.set_fma_mode(False)
+        self.logits = logits
+        return tok
+
+
+@pytest.fixture(scope="module")
+def small():
+    return synth.model(200, n_layers=2, vocab=4096)
+
+
+@pytest.mark.parametrize("mode", ["exact", "fast"])
+def test_small_model_greedy_ids(dev, oracle, small, mode):
+    M = Model.create(dev, small, QWEN3_06B.with_(attention=mode))
+    ref = OracleModel(oracle, small, ieee=True)
+    prompt = [5, 99, 4000, 17, 17, 3]
+    got = [M.step(prompt)]
+    want = [ref.step(prompt)]
+    for _ in range(6):
+        got.append(M.step([got[-1]]))
+        want.append(ref.step([want[-1]]))
+    assert got == want
+
+
+def test_small_model_logits_exact(dev, oracle, small):
+    M = Model.create(dev, small, QWEN3_06B)
+    ref = OracleModel(oracle, small, ieee=True)
+    prompt = [7, 8, 9, 10]
+    lg = M.logits(prompt)
+    ref.step(prompt)
+    assert n_mismatch(lg, ref.logits) == 0
+    assert int(np.argmax(lg)) == int(np.argmax(ref.logits))
+
+
+def test_decode_device_matches_host_loop(dev, small):
+    A = Model.create(dev, small)
+    B = Model.create(dev, small)
+    prompt = [1, 2, 3, 4, 5]
+    first = A.step(prompt)
+    assert B.step(prompt) == first
+    host = [first]
+    for _ in range(10):
+        host.append(A.step([host[-1]]))
+    dev_ids = B.decode_device(10)
+    assert [first] + dev_ids.tolist() == host
+    assert A.pos == B.pos == len(prompt) + 10
+
+
+def test_coordinator_split_equals_whole(dev, small):
+    # kernels/test_split.ts:42-195: cut model + layer range == whole model
+    whole = Model.create(dev, small)
+    coord = Model.create(dev, small, cut=1)
+    bird = [Layer.create(dev, small.layers[1])]
+    prompt = [11, 22, 33, 44]
+    want = whole.generate(prompt, 6)
+    got = []
+    ids, offset = prompt, 0
+    for _ in range(6):
+        flat = coord.encode_partial(ids, offset)
+        flat = range_forward(bird, flat, len(ids), offset)
+        tok = coord.project_hidden(flat, len(ids))
+        got.append(tok)
+        offset += len(ids)
+        ids = [tok]
+    assert got == want
+    with pytest.raises(FlockError, match="offset"):
+        coord.encode_partial([1], 0)
+
+
+def test_generate_eos_and_rewind(dev, small):
+    M = Model.create(dev, small)
+    out = M.generate([1, 2, 3], 5)
+    assert len(out) == 5
+    M.reset()
+    assert M.pos == 0
+    out2 = M.generate([1, 2, 3], 5, eos=[out[2]])
+    assert out2 == out[:out.index(out[2])]
+
+
+def test_full_06b_model_greedy_ids(dev, oracle):
+    """BASELINE config 2 shape (28 layers, vocab 151936, tied head), short run."""
+    m = synth.model(300)
+    M = Model.create(dev, m, QWEN3_06B)
+    ref = OracleModel(oracle, m, ieee=False)
+    prompt = synth.uniform_ids(300, "prompt", 8, S.vocab).tolist()
+    got = [M.step(prompt)]
+    want = [ref.step(prompt)]
+    for _ in range(2):
+        got.append(M.step([got[-1]]))
+        want.append(ref.step([want[-1]]))
+    assert got == want
