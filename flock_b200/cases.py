@@ -1,0 +1,66 @@
+"""Small, fixed GPU workloads for profiling one kernel family at a time.
+
+    python -m flock_b200.cases layer [--time]   # one decode layer (config 0 shape, 256-key cache)
+    python -m flock_b200.cases head  [--time]   # the 151936 x 1024 Q8_0 head matvec
+    python -m flock_b200.cases gemv  [--time]   # the config 1 matvec sweep (M = 1)
+
+Each case builds seeded synthetic weights, runs a few warm launches and, with
+--time, prints CUDA-event timings.  They are small enough (< 0.5 GB on the
+device) to run under ncu.
+"""
+from __future__ import annotations
+
+import sys
+
+from . import ops, synth
+from . import lib as flib
+from .layer import QWEN3_06B, Layer
+
+SWEEP = [(2048, 1024), (1024, 1024), (1024, 2048), (3072, 1024), (1024, 3072), (151936, 1024)]
+
+
+def layer_case(timed: bool, attention: str = "fast") -> None:
+    dev = flib.get_device(0)
+    L = Layer.create(dev, synth.layer_weights(100, 24), QWEN3_06B.with_(attention=attention))
+    kvw = 1024
+    L.write_cache(synth.normal(1, "k", 256 * kvw), synth.normal(1, "v", 256 * kvw))
+    x = synth.normal(1, "x", 1024)
+    for i in range(5):
+        L.encode(x if i == 0 else None)
+    dev.sync()
+    if timed:
+        dev.timer_start()
+        for _ in range(50):
+            L.encode(None)
+        ms = dev.timer_stop()
+        print(f"layer decode ({attention}): {ms / 50 * 1000:.2f} us/step")
+
+
+def head_case(timed: bool) -> None:
+    dev = flib.get_device(0)
+    t = flib.GpuTensor.from_packed(dev, synth.q8_tensor(6, "head", 151936, 1024), 151936, 1024)
+    ms = ops.matvec_timed(dev, t, 1, 50 if timed else 3)
+    if timed:
+        b = 151936 * 1024 * 1.0625 + 4 * (1024 + 151936)
+        print(f"head matvec: {ms * 1000:.2f} us, {b / ms / 1e6:.1f} GB/s")
+
+
+def gemv_case(timed: bool) -> None:
+    dev = flib.get_device(0)
+    for q8 in (True, False):
+        for rows, cols in SWEEP:
+            make = synth.q8_tensor if q8 else synth.q4_tensor
+            t = flib.GpuTensor.from_packed(dev, make(2, "t", rows, cols), rows, cols,
+                                           flib.FLOCK_Q8_0 if q8 else flib.FLOCK_Q4_0)
+            ms = ops.matvec_timed(dev, t, 1, 100 if timed else 2)
+            if timed:
+                b = rows * cols * (1.0625 if q8 else 0.5625) + 4 * (rows + cols)
+                print(f"{'Q8_0' if q8 else 'Q4_0'} {rows}x{cols}: {ms * 1000:.2f} us "
+                      f"{b / ms / 1e6:.1f} GB/s")
+
+
+if __name__ == "__main__":
+    case = sys.argv[1] if len(sys.argv) > 1 else "layer"
+    timed = "--time" in sys.argv
+    {"layer": layer_case, "head": head_case, "gemv": gemv_case}[case](timed)
+    print("ok")

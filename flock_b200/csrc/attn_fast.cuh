@@ -42,7 +42,7 @@ struct AttnFastArgs {
   int n_heads, n_kv_heads, head_dim, splits;
   float eps;
   int neox;
-  int chunk_cap;   // max keys per split this launch was sized for
+  int chunk_cap;   // max keys per split (informational; tiles of 64 are staged)
   PrefetchList pf;
 };
 
@@ -80,114 +80,188 @@ FLOCK_DEV void norm_rope_half(const float* src, const float* gain, float eps, in
 }
 
 constexpr int ATTN_FAST_THREADS = 256;
+constexpr int ATTN_TILE = 64;  // keys staged in shared memory per pass
+
+// Shared-memory layout (floats): raw q [4][128], raw k/v [2][128], gains
+// [2][128], inv_freq [64], normalised q [4][128], new k/v [2][128], norm
+// scratch tmp [2][128] + red [2][132], scores/probabilities [4][TILE],
+// running softmax state [4][4], K and V tiles [2][TILE][128].
+constexpr int AF_QRAW = 0, AF_KRAW = 512, AF_VRAW = 640, AF_GQ = 768, AF_GK = 896,
+              AF_INV = 1024, AF_QV = 1088, AF_KNEW = 1600, AF_VNEW = 1728, AF_TMP = 1856,
+              AF_RED = 2112, AF_SC = 2376, AF_ML = AF_SC + 4 * ATTN_TILE, AF_KT = AF_ML + 16,
+              AF_VT = AF_KT + ATTN_TILE * 128, AF_END = AF_VT + ATTN_TILE * 128;
 
 static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(const AttnFastArgs a) {
   extern __shared__ __align__(16) float dsm[];
-  const int G = a.n_heads / a.n_kv_heads;  // <= 4
-  float* qv = dsm;                          // [G][128]
-  float* knew = qv + 4 * 128;               // [128]
-  float* vnew = knew + 128;                 // [128]
-  float* tmp = vnew + 128;                  // [2][128]
-  float* red = tmp + 256;                   // [2][132]
-  float* ml = red + 264;                    // [G][2] (m, l)
-  float* sc = ml + 8;                       // [G][chunk_cap]
   __shared__ bool last;
+  const int G = a.n_heads / a.n_kv_heads;  // <= 4
+  const int g = blockIdx.x, s = blockIdx.y, t = threadIdx.x;
+  const int half = t >> 7, lane = t & 31, warp = t >> 5;
+  const int hd = 128;
+  const size_t kvs = (size_t)a.n_kv_heads * hd;
 
   issue_prefetch(a.pf);
   pdl_launch_dependents();
   pdl_wait();
 
-  const int g = blockIdx.x, s = blockIdx.y, t = threadIdx.x;
-  const int half = t >> 7, lane = t & 31, warp = t >> 5;
   const int pos = a.ctl[0];
   const int n_keys = pos + 1;
-  const int hd = 128;
-
-  if (a.q_norm) {
-    // Normalise + rotate the G query heads and the new key (G+1 vectors, two
-    // per pass over the two 128-thread halves of the block).
-    for (int base = 0; base < G + 1; base += 2) {
-      const int vi = base + half;
-      const bool active = vi <= G;
-      const bool is_k = vi == G;
-      const float* src = is_k ? a.k + (size_t)g * hd : a.q + (size_t)(g * G + vi) * hd;
-      float* dst = is_k ? knew : qv + vi * 128;
-      norm_rope_half(src, is_k ? a.k_norm : a.q_norm, a.eps, pos, a.inv_freq, a.neox, dst,
-                     red + half * 132, tmp + half * 128, active);
-    }
-    if (t < 128) vnew[t] = a.v[(size_t)g * hd + t];
-  } else {
-    // Pre-normalised form (op-level attention): q is final and the key and
-    // value of position pos are already in the cache.
-    for (int i = t; i < G * 128; i += ATTN_FAST_THREADS) qv[i] = a.q[(size_t)g * G * hd + i];
-    if (t < 128) {
-      knew[t] = a.kcache[((size_t)pos * a.n_kv_heads + g) * hd + t];
-      vnew[t] = a.vcache[((size_t)pos * a.n_kv_heads + g) * hd + t];
-    }
-  }
-  __syncthreads();
-  if (a.q_norm && s == 0 && t < 128) {
-    a.kcache[((size_t)pos * a.n_kv_heads + g) * hd + t] = knew[t];
-    a.vcache[((size_t)pos * a.n_kv_heads + g) * hd + t] = vnew[t];
-  }
-
   const int chunk = (n_keys + a.splits - 1) / a.splits;
   const int k0 = s * chunk;
   const int k1 = min(n_keys, k0 + chunk);
   const int nk = max(0, k1 - k0);
-  const float scale = __double2float_rn(1.0 / sqrt((double)hd));
-  const size_t kvs = (size_t)a.n_kv_heads * hd;
+  const bool fused = a.q_norm != nullptr;
 
-  // Scores: one warp per key, float4 per lane, all G heads per K read.
-  for (int j = warp; j < nk; j += ATTN_FAST_THREADS / 32) {
-    const int key = k0 + j;
-    const float4 kv = key == pos ? reinterpret_cast<const float4*>(knew)[lane]
-                                 : reinterpret_cast<const float4*>(a.kcache + key * kvs +
-                                                                   (size_t)g * hd)[lane];
-    for (int hq = 0; hq < G; hq++) {
-      const float4 qq = reinterpret_cast<const float4*>(qv + hq * 128)[lane];
-      float p = qq.x * kv.x + qq.y * kv.y + qq.z * kv.z + qq.w * kv.w;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-      if (lane == 0) sc[hq * a.chunk_cap + j] = p * scale;
+  // ---- one round trip: the token's raw q/k/v, gains, and the first K/V tile
+  auto stage_tile = [&](int t0, int nt) {
+    // keys [t0, t0 + nt) of kv head g; position pos is filled from knew/vnew
+    for (int i = t; i < nt * 32; i += ATTN_FAST_THREADS) {
+      const int j = i >> 5, c4 = i & 31, key = t0 + j;
+      if (key == pos) continue;
+      const float4* kr = reinterpret_cast<const float4*>(a.kcache + key * kvs + (size_t)g * hd);
+      const float4* vr = reinterpret_cast<const float4*>(a.vcache + key * kvs + (size_t)g * hd);
+      reinterpret_cast<float4*>(dsm + AF_KT)[i] = kr[c4];
+      reinterpret_cast<float4*>(dsm + AF_VT)[i] = vr[c4];
     }
+  };
+  {
+    const float* qsrc = a.q + (size_t)g * G * hd;
+    for (int i = t; i < G * 32; i += ATTN_FAST_THREADS)
+      reinterpret_cast<float4*>(dsm + AF_QRAW)[i] = reinterpret_cast<const float4*>(qsrc)[i];
+    if (t < 32) {
+      if (fused) {
+        reinterpret_cast<float4*>(dsm + AF_KRAW)[t] =
+            reinterpret_cast<const float4*>(a.k + (size_t)g * hd)[t];
+        reinterpret_cast<float4*>(dsm + AF_VRAW)[t] =
+            reinterpret_cast<const float4*>(a.v + (size_t)g * hd)[t];
+        reinterpret_cast<float4*>(dsm + AF_GQ)[t] = reinterpret_cast<const float4*>(a.q_norm)[t];
+        reinterpret_cast<float4*>(dsm + AF_GK)[t] = reinterpret_cast<const float4*>(a.k_norm)[t];
+        if (t < 16)
+          reinterpret_cast<float4*>(dsm + AF_INV)[t] =
+              reinterpret_cast<const float4*>(a.inv_freq)[t];
+      } else {
+        reinterpret_cast<float4*>(dsm + AF_KNEW)[t] =
+            reinterpret_cast<const float4*>(a.kcache + (size_t)pos * kvs + (size_t)g * hd)[t];
+        reinterpret_cast<float4*>(dsm + AF_VNEW)[t] =
+            reinterpret_cast<const float4*>(a.vcache + (size_t)pos * kvs + (size_t)g * hd)[t];
+      }
+    }
+    stage_tile(k0, min(nk, ATTN_TILE));
   }
   __syncthreads();
-  // Local softmax statistics per head (warp hq).
-  if (warp < G) {
-    const int hq = warp;
-    float m = -INFINITY;
-    for (int j = lane; j < nk; j += 32) m = fmaxf(m, sc[hq * a.chunk_cap + j]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.0f;
-    for (int j = lane; j < nk; j += 32) {
-      const float p = expf(sc[hq * a.chunk_cap + j] - m);
-      sc[hq * a.chunk_cap + j] = p;
-      l += p;
+
+  float* qv = dsm + AF_QV;
+  float* knew = dsm + AF_KNEW;
+  float* vnew = dsm + AF_VNEW;
+  if (fused) {
+    // exact per-head RMSNorm + RoPE of the G query heads and the new key,
+    // two 128-wide vectors per pass (k_qk_norm_rope_append's arithmetic)
+    for (int base = 0; base < G + 1; base += 2) {
+      const int vi = base + half;
+      const bool active = vi <= G;
+      const bool is_k = vi == G;
+      const float* src = is_k ? dsm + AF_KRAW : dsm + AF_QRAW + (active ? vi : 0) * 128;
+      float* dst = is_k ? knew : qv + (active ? vi : 0) * 128;
+      norm_rope_half(src, is_k ? dsm + AF_GK : dsm + AF_GQ, a.eps, pos, dsm + AF_INV, a.neox,
+                     dst, dsm + AF_RED + half * 132, dsm + AF_TMP + half * 128, active);
     }
+    if (t < 128) vnew[t] = dsm[AF_VRAW + t];
+    __syncthreads();
+    if (s == 0 && t < 128) {
+      a.kcache[(size_t)pos * kvs + (size_t)g * hd + t] = knew[t];
+      a.vcache[(size_t)pos * kvs + (size_t)g * hd + t] = vnew[t];
+    }
+  } else {
+    for (int i = t; i < G * 128; i += ATTN_FAST_THREADS) qv[i] = dsm[AF_QRAW + i];
+    __syncthreads();
+  }
+
+  const float scale = __double2float_rn(1.0 / sqrt((double)hd));
+  float* sc = dsm + AF_SC;
+  float* ml = dsm + AF_ML;  // per head: m, l, correction
+  float* kt = dsm + AF_KT;
+  float* vt = dsm + AF_VT;
+  if (t < G) {
+    ml[4 * t] = -INFINITY;
+    ml[4 * t + 1] = 0.0f;
+  }
+  float o[2] = {0.0f, 0.0f};  // outputs oi = t, t + 256 (G * 128 <= 512)
+
+  for (int t0 = k0; t0 < k1; t0 += ATTN_TILE) {
+    const int nt = min(ATTN_TILE, k1 - t0);
+    if (t0 != k0) {
+      __syncthreads();
+      stage_tile(t0, nt);
+    }
+    // the new key/value live in shared memory, not (yet) in the cache
+    if (pos >= t0 && pos < t0 + nt && t < 128) {
+      kt[(pos - t0) * 128 + t] = knew[t];
+      vt[(pos - t0) * 128 + t] = vnew[t];
+    }
+    __syncthreads();
+    // scores: one warp per key, all G heads per K row
+    for (int j = warp; j < nt; j += ATTN_FAST_THREADS / 32) {
+      const float4 kv = reinterpret_cast<const float4*>(kt + j * 128)[lane];
+      for (int hq = 0; hq < G; hq++) {
+        const float4 qq = reinterpret_cast<const float4*>(qv + hq * 128)[lane];
+        float p = fmaf(qq.x, kv.x, fmaf(qq.y, kv.y, fmaf(qq.z, kv.z, qq.w * kv.w)));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) {
-      ml[2 * hq] = m;
-      ml[2 * hq + 1] = l;
+        for (int o2 = 16; o2 > 0; o2 >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o2);
+        if (lane == 0) sc[hq * ATTN_TILE + j] = p * scale;
+      }
+    }
+    __syncthreads();
+    // online softmax per head (warp hq): new max, correction, probabilities
+    if (warp < G) {
+      const int hq = warp;
+      float mt = -INFINITY;
+      for (int j = lane; j < nt; j += 32) mt = fmaxf(mt, sc[hq * ATTN_TILE + j]);
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o2));
+      const float m_old = ml[4 * hq];
+      const float m_new = fmaxf(m_old, mt);
+      float lt = 0.0f;
+      for (int j = lane; j < nt; j += 32) {
+        const float p = expf(sc[hq * ATTN_TILE + j] - m_new);
+        sc[hq * ATTN_TILE + j] = p;
+        lt += p;
+      }
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o2);
+      __syncwarp();
+      if (lane == 0) {
+        const float c = expf(m_old - m_new);
+        ml[4 * hq] = m_new;
+        ml[4 * hq + 1] = fmaf(ml[4 * hq + 1], c, lt);
+        ml[4 * hq + 2] = c;
+      }
+    }
+    __syncthreads();
+    // unnormalised output: thread owns outputs (hq, i) = t, t + 256
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int oi = t + u * ATTN_FAST_THREADS;
+      if (oi < G * hd) {
+        const int hq = oi / hd, i = oi % hd;
+        float acc = o[u] * ml[4 * hq + 2];
+        for (int j = 0; j < nt; j++) acc = fmaf(sc[hq * ATTN_TILE + j], vt[j * 128 + i], acc);
+        o[u] = acc;
+      }
     }
   }
-  __syncthreads();
-  // Unnormalised output of this split.
-  for (int oi = t; oi < G * hd; oi += ATTN_FAST_THREADS) {
-    const int hq = oi / hd, i = oi % hd;
-    float acc = 0.0f;
-    for (int j = 0; j < nk; j++) {
-      const int key = k0 + j;
-      const float vv = key == pos ? vnew[i] : a.vcache[key * kvs + (size_t)g * hd + i];
-      acc = fmaf(sc[hq * a.chunk_cap + j], vv, acc);
-    }
-    float* pp = a.part + ((size_t)(g * G + hq) * a.splits + s) * (hd + 2);
-    pp[i] = acc;
-    if (i == 0) {
-      pp[hd] = ml[2 * hq];
-      pp[hd + 1] = ml[2 * hq + 1];
+
+  // this split's partial: unnormalised o, running max m, sum l
+#pragma unroll
+  for (int u = 0; u < 2; u++) {
+    const int oi = t + u * ATTN_FAST_THREADS;
+    if (oi < G * hd) {
+      const int hq = oi / hd, i = oi % hd;
+      float* pp = a.part + ((size_t)(g * G + hq) * a.splits + s) * (hd + 2);
+      pp[i] = o[u];
+      if (i == 0) {
+        pp[hd] = ml[4 * hq];
+        pp[hd + 1] = ml[4 * hq + 1];
+      }
     }
   }
   __threadfence();
@@ -212,8 +286,6 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
   if (t == 0) a.count[g] = 0;
 }
 
-inline size_t attn_fast_smem(int chunk_cap) {
-  return (size_t)(4 * 128 + 128 + 128 + 256 + 264 + 8 + 4 * chunk_cap) * 4;
-}
+inline size_t attn_fast_smem(int /*chunk_cap*/) { return (size_t)AF_END * 4; }
 
 }  // namespace flock

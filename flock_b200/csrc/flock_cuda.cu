@@ -71,10 +71,10 @@ static cudaError_t launch_ex(cudaStream_t st, void (*k)(KArgs...), dim3 grid, di
 template <int QT, int R, int EPI, int MX>
 static cudaError_t gemv_go(flock_dev* d, const GemvArgs& a, int ctas, bool pdl) {
   auto k = k_gemv<QT, R, EPI, MX>;
-  const size_t smem = gemv_smem_bytes(a.K);
+  const size_t smem = gemv_smem_bytes(a.K, a.norm_gain != nullptr);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -88,17 +88,20 @@ int gemv_grid(flock_dev* d, int total_groups) {
 }
 
 int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl) {
-  if (a.K % 32 != 0 || a.K > 24576) {
-    set_error("matvec cols %d must be a multiple of 32 and <= 24576", a.K);
+  if (a.K % 32 != 0 || a.K > 24576 || (a.norm_gain && a.K > 12288)) {
+    set_error("matvec cols %d must be a multiple of 32 and <= 24576 (12288 with a fused norm)",
+              a.K);
     return FLOCK_E_ARG;
   }
   const int M = (a.K / 32 + 31) / 32;
   const int MX = M >= 2 ? 2 : 1;
   int rows = 0;
   for (int s = 0; s < a.nseg; s++) rows += a.seg[s].rows;
+  // rows per warp step: 2 where that keeps one wave of <= 2 CTAs per SM busy
+  // with about one row group per warp, 1 for the small matrices
   int R = 1;
   if (EPI == EPI_SWIGLU || EPI == EPI_ARGMAX) R = 2;
-  else if (EPI == EPI_STORE && rows >= 16384) R = 2;
+  else if (EPI == EPI_STORE && rows > 2 * GEMV_WARPS * d->sm_count) R = 2;
   int groups;
   if (EPI == EPI_SWIGLU) groups = a.seg[0].rows;
   else {

@@ -51,7 +51,7 @@ int enqueue_embed(flock_model* m, int n) {
     a.pf.n = 1;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(n);
+  cfg.gridDim = dim3(n < 64 ? 64 : n);
   cfg.blockDim = dim3(256);
   cfg.stream = m->dev->stream;
   cudaLaunchAttribute attr[1];

@@ -98,11 +98,11 @@ FLOCK_DEV void load_block<QT_Q4>(BlockW<QT_Q4>& bw, const GemvSeg& sg, int row, 
 }
 
 // Fold one block into acc in the reference order.  xb points at the block's
-// 32 x values (registers or shared memory).
+// 32 x values as 8 float4 (registers, or a padded shared-memory row).
 template <int QT>
-FLOCK_DEV float fold_block(const BlockW<QT>& bw, const float* xb, float acc);
+FLOCK_DEV float fold_block(const BlockW<QT>& bw, const float4* xb, float acc);
 template <>
-FLOCK_DEV float fold_block<QT_Q8>(const BlockW<QT_Q8>& bw, const float* xb, float acc) {
+FLOCK_DEV float fold_block<QT_Q8>(const BlockW<QT_Q8>& bw, const float4* xb, float acc) {
   const float s = scale_f16(bw.s);
   const uint32_t w[8] = {bw.w0.x, bw.w0.y, bw.w0.z, bw.w0.w, bw.w1.x, bw.w1.y, bw.w1.z, bw.w1.w};
 #pragma unroll
@@ -110,15 +110,15 @@ FLOCK_DEV float fold_block<QT_Q8>(const BlockW<QT_Q8>& bw, const float* xb, floa
     float a0, a1, a2, a3, c0, c1, c2, c3;
     dec_i8x4(w[2 * g], a0, a1, a2, a3);
     dec_i8x4(w[2 * g + 1], c0, c1, c2, c3);
-    const float* xa = xb + 8 * g;
-    float d0 = dot4(a0, a1, a2, a3, xa[0], xa[1], xa[2], xa[3]);
-    float d1 = dot4(c0, c1, c2, c3, xa[4], xa[5], xa[6], xa[7]);
+    const float4 xa = xb[2 * g], xc = xb[2 * g + 1];
+    float d0 = dot4(a0, a1, a2, a3, xa.x, xa.y, xa.z, xa.w);
+    float d1 = dot4(c0, c1, c2, c3, xc.x, xc.y, xc.z, xc.w);
     acc = ffma(s, fadd(d0, d1), acc);
   }
   return acc;
 }
 template <>
-FLOCK_DEV float fold_block<QT_Q4>(const BlockW<QT_Q4>& bw, const float* xb, float acc) {
+FLOCK_DEV float fold_block<QT_Q4>(const BlockW<QT_Q4>& bw, const float4* xb, float acc) {
   const float s = scale_f16(bw.s);
   const uint32_t w[4] = {bw.w.x, bw.w.y, bw.w.z, bw.w.w};
 #pragma unroll
@@ -126,13 +126,18 @@ FLOCK_DEV float fold_block<QT_Q4>(const BlockW<QT_Q4>& bw, const float* xb, floa
     float a0, a1, a2, a3, c0, c1, c2, c3;
     dec_nib4(w[g] & 0x0F0F0F0Fu, a0, a1, a2, a3);
     dec_nib4((w[g] >> 4) & 0x0F0F0F0Fu, c0, c1, c2, c3);
-    float d0 = dot4(a0, a1, a2, a3, xb[4 * g], xb[4 * g + 1], xb[4 * g + 2], xb[4 * g + 3]);
-    float d1 =
-        dot4(c0, c1, c2, c3, xb[16 + 4 * g], xb[17 + 4 * g], xb[18 + 4 * g], xb[19 + 4 * g]);
+    const float4 xa = xb[g], xc = xb[4 + g];  // cols 4g.. and 16+4g..
+    float d0 = dot4(a0, a1, a2, a3, xa.x, xa.y, xa.z, xa.w);
+    float d1 = dot4(c0, c1, c2, c3, xc.x, xc.y, xc.z, xc.w);
     acc = ffma(s, fadd(d0, d1), acc);
   }
   return acc;
 }
+
+// x lives in shared memory with each 32-float block padded to 36 floats, so
+// lane l reading block l (float4 at a time) touches distinct banks.
+constexpr int XPAD = 36;
+FLOCK_DEV int xpad(int i) { return (i >> 5) * XPAD + (i & 31); }
 
 // kernels/argmax.wgsl:57 better(): strictly larger, or equal with lower index.
 FLOCK_DEV bool am_better(float va, uint32_t ia, float vb, uint32_t ib) {
@@ -142,14 +147,26 @@ FLOCK_DEV bool am_better(float va, uint32_t ia, float vb, uint32_t ib) {
 // Fused RMSNorm prologue, exact ops_ref.ts:20 order with WG = 128:
 // part[t] = serial fma over i = t, t+128, ...; pairwise tree over 128;
 // scale = fr(1/sqrt(fr(fr(sum/n) + eps))); y = fr(fr(x*scale)*g).
-// Called by all GEMV_THREADS threads; writes y into xs[0..n).
+// x and the gain are staged into shared memory with ONE round trip of
+// 128-bit loads (all issued before any is consumed); the rest runs on chip.
+// Called by all GEMV_THREADS threads; leaves y in xs (padded layout).
 FLOCK_DEV void rmsnorm_to_smem(const float* __restrict__ src, const float* __restrict__ gain,
-                               int n, float eps, float* xs, float* red) {
+                               int n, float eps, float* xs, float* gs, float* red) {
   const int t = threadIdx.x;
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  const float4* g4 = reinterpret_cast<const float4*>(gain);
+#pragma unroll 4
+  for (int i = t; i < n / 4; i += GEMV_THREADS) {
+    const float4 v = s4[i];
+    const float4 g = g4[i];
+    reinterpret_cast<float4*>(xs)[(i >> 3) * (XPAD / 4) + (i & 7)] = v;
+    reinterpret_cast<float4*>(gs)[i] = g;
+  }
+  __syncthreads();
   if (t < 128) {
     float acc = 0.0f;
     for (int i = t; i < n; i += 128) {
-      float v = src[i];
+      const float v = xs[xpad(i)];
       acc = ffma(v, v, acc);
     }
     red[t] = acc;
@@ -164,34 +181,59 @@ FLOCK_DEV void rmsnorm_to_smem(const float* __restrict__ src, const float* __res
   }
   __syncthreads();
   const float scale = red[128];
-  for (int i = t; i < n; i += GEMV_THREADS) xs[i] = fmul(fmul(src[i], scale), gain[i]);
+  for (int i = t; i < n; i += GEMV_THREADS) xs[xpad(i)] = fmul(fmul(xs[xpad(i)], scale), gs[i]);
 }
 
-// Resolve global row-group index -> (segment, first row).  Row groups never
-// straddle segments; each segment has ceil(rows / R) groups.
+// The R rows a row group covers.
 template <int R>
-FLOCK_DEV bool group_of(const GemvArgs& a, int g, int& seg, int& row0) {
+struct Rows {
+  int seg[R], row[R];
+  bool ok[R];
+};
+
+template <int R, int EPI>
+FLOCK_DEV void rows_of(const GemvArgs& a, int g, Rows<R>& rs) {
+  if (EPI == EPI_SWIGLU) {
+    // R/2 gate rows (segment 0) and the same R/2 up rows (segment 1)
+    const int r0 = g * (R / 2);
 #pragma unroll
-  for (int s = 0; s < 3; s++) {
-    if (s >= a.nseg) return false;
-    const int ng = (a.seg[s].rows + R - 1) / R;
-    if (g < ng) {
-      seg = s;
-      row0 = g * R;
-      return true;
+    for (int r = 0; r < R; r++) {
+      rs.seg[r] = r < R / 2 ? 0 : 1;
+      rs.row[r] = r0 + (r % (R / 2));
+      rs.ok[r] = rs.row[r] < a.seg[0].rows;
     }
-    g -= ng;
+  } else {
+    int s = 0, row0 = 0;
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+      if (q >= a.nseg) break;
+      const int ng = (a.seg[q].rows + R - 1) / R;
+      if (g < ng) {
+        s = q;
+        row0 = g * R;
+        break;
+      }
+      g -= ng;
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      rs.seg[r] = s;
+      rs.row[r] = row0 + r;
+      rs.ok[r] = rs.row[r] < a.seg[s].rows;
+    }
   }
-  return false;
 }
 
-// MX: how many of each thread's x blocks stay in registers (0 = reload from
-// shared memory per row group).  For K <= 1024*MX every block is resident.
+// MX: how many of each thread's x blocks (lane + 32m, m < MX) stay in
+// registers; the rest are read from shared memory.
 template <int QT, int R, int EPI, int MX>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(16) float smem[];
-  float* xs = smem;                          // [K]
-  float* red = smem + a.K;                   // [132] reduction scratch
+  const bool norm = a.norm_gain != nullptr;
+  const int kpad = a.K / 32 * XPAD;
+  float* xs = smem;                          // [K/32][36] the (normalised) input
+  float* gs = smem + kpad;                   // [K] gain staging (norm only)
+  float* red = gs + (norm ? a.K : 0);        // [136] reduction scratch
   float* cta_val = red + 136;                // [GEMV_WARPS]
   uint32_t* cta_idx = (uint32_t*)(cta_val + GEMV_WARPS);
 
@@ -201,8 +243,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   const int nb = a.K / 32;
   const int M = (nb + 31) / 32;
 
-  // Row groups: for SWIGLU segment 0 (gate) and 1 (up) are walked together,
-  // R/2 rows of each per group.
   int n_groups;
   if (EPI == EPI_SWIGLU) {
     n_groups = (a.seg[0].rows + R / 2 - 1) / (R / 2);
@@ -210,8 +250,23 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     n_groups = 0;
     for (int s = 0; s < a.nseg; s++) n_groups += (a.seg[s].rows + R - 1) / R;
   }
-  const int gwarp = blockIdx.x * GEMV_WARPS + warp;
   const int nwarps = gridDim.x * GEMV_WARPS;
+
+  // The warp walks steps (g, m): row group g = gwarp, gwarp + nwarps, ...,
+  // column block m = 0..M-1.  Weights do not depend on any earlier kernel,
+  // so the first step's loads are issued before griddepcontrol.wait.
+  int g = blockIdx.x * GEMV_WARPS + warp, m = 0;
+  bool have = g < n_groups;
+  Rows<R> rs;
+  BlockW<QT> cur[R];
+  if (have) {
+    rows_of<R, EPI>(a, g, rs);
+    if (lane < nb) {
+#pragma unroll
+      for (int r = 0; r < R; r++)
+        if (rs.ok[r]) load_block<QT>(cur[r], a.seg[rs.seg[r]], rs.row[r], lane, a.K);
+    }
+  }
 
   issue_prefetch(a.pf);
   pdl_launch_dependents();
@@ -223,109 +278,116 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   }
 
   // ---- x into shared memory (optionally normalised) ----
-  if (a.norm_gain) {
-    rmsnorm_to_smem(a.x + (size_t)tok * a.x_stride, a.norm_gain, a.K, a.eps, xs, red);
+  if (norm) {
+    rmsnorm_to_smem(a.x + (size_t)tok * a.x_stride, a.norm_gain, a.K, a.eps, xs, gs, red);
   } else {
     const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)tok * a.x_stride);
+#pragma unroll 4
     for (int i = threadIdx.x; i < a.K / 4; i += GEMV_THREADS)
-      reinterpret_cast<float4*>(xs)[i] = src[i];
+      reinterpret_cast<float4*>(xs)[(i >> 3) * (XPAD / 4) + (i & 7)] = src[i];
   }
   __syncthreads();
 
-  // Resident x blocks: block lane + 32m for m < MX.
-  float xr[MX > 0 ? MX : 1][32];
+  const float4* xs4 = reinterpret_cast<const float4*>(xs);
+  float4 xr[MX][8];
 #pragma unroll
-  for (int m = 0; m < MX; m++) {
-    const int b = lane + 32 * m;
+  for (int mm = 0; mm < MX; mm++) {
+    const int b = lane + 32 * mm;
 #pragma unroll
-    for (int i = 0; i < 32; i++) xr[m][i] = (b < nb) ? xs[b * 32 + i] : 0.0f;
+    for (int j = 0; j < 8; j++)
+      xr[mm][j] = (b < nb) ? xs4[b * (XPAD / 4) + j] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 
+  float accA[R], accB[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) accA[r] = accB[r] = 0.0f;
   float best_v = -FLT_MAX;
   uint32_t best_i = 0xFFFFFFFFu;
 
-  for (int g = gwarp; g < n_groups; g += nwarps) {
-    // Rows of this group: pointers per slot.
-    int rseg[R], rrow[R];
-    bool rok[R];
-    if (EPI == EPI_SWIGLU) {
-      const int r0 = g * (R / 2);
+  while (have) {
+    // issue the next step's loads before folding this one
+    int g2 = g, m2 = m + 1;
+    if (m2 == M) {
+      m2 = 0;
+      g2 = g + nwarps;
+    }
+    const bool have2 = g2 < n_groups;
+    Rows<R> rs2 = rs;
+    if (have2 && m2 == 0) rows_of<R, EPI>(a, g2, rs2);
+    BlockW<QT> nxt[R];
+    const int b2 = lane + 32 * m2;
+    if (have2 && b2 < nb) {
 #pragma unroll
-      for (int r = 0; r < R; r++) {
-        rseg[r] = r < R / 2 ? 0 : 1;
-        rrow[r] = r0 + (r % (R / 2));
-        rok[r] = rrow[r] < a.seg[0].rows;
-      }
-    } else {
-      int s, row0;
-      group_of<R>(a, g, s, row0);
+      for (int r = 0; r < R; r++)
+        if (rs2.ok[r]) load_block<QT>(nxt[r], a.seg[rs2.seg[r]], rs2.row[r], b2, a.K);
+    }
+
+    const int b = lane + 32 * m;
+    if (b < nb) {
+      auto fold_all = [&](const float4* xb) {
 #pragma unroll
-      for (int r = 0; r < R; r++) {
-        rseg[r] = s;
-        rrow[r] = row0 + r;
-        rok[r] = rrow[r] < a.seg[s].rows;
+        for (int r = 0; r < R; r++) {
+          if (!rs.ok[r]) continue;
+          if (m & 1)
+            accB[r] = fold_block<QT>(cur[r], xb, accB[r]);
+          else
+            accA[r] = fold_block<QT>(cur[r], xb, accA[r]);
+        }
+      };
+      if constexpr (MX >= 2) {
+        if (m == 0) fold_all(xr[0]);
+        else if (m == 1) fold_all(xr[MX >= 2 ? 1 : 0]);
+        else fold_all(xs4 + b * (XPAD / 4));
+      } else {
+        if (m == 0) fold_all(xr[0]);
+        else fold_all(xs4 + b * (XPAD / 4));
       }
     }
 
-    float accA[R], accB[R];
-#pragma unroll
-    for (int r = 0; r < R; r++) accA[r] = accB[r] = 0.0f;
-
-    // One 32-weight column block of the group: load R rows, fold into the
-    // accumulator of logical lane (lane + 32 * (m & 1)).
-    auto step = [&](int m, const float* xb) {
-      const int b = lane + 32 * m;
-      if (b >= nb) return;
-      BlockW<QT> bw[R];
-#pragma unroll
-      for (int r = 0; r < R; r++)
-        if (rok[r]) load_block<QT>(bw[r], a.seg[rseg[r]], rrow[r], b, a.K);
+    if (m == M - 1) {
+      float y[R];
 #pragma unroll
       for (int r = 0; r < R; r++) {
-        if (!rok[r]) continue;
-        if (m & 1)
-          accB[r] = fold_block<QT>(bw[r], xb, accB[r]);
-        else
-          accA[r] = fold_block<QT>(bw[r], xb, accA[r]);
+        y[r] = warp_tree_sum(fadd(accA[r], accB[r]));
+        accA[r] = accB[r] = 0.0f;
       }
-    };
+      if (lane == 0) {
+        if (EPI == EPI_SWIGLU) {
 #pragma unroll
-    for (int m = 0; m < MX; m++) step(m, xr[m]);
-    for (int m = MX; m < M; m++) step(m, xs + (lane + 32 * m) * 32);
-
-    float y[R];
+          for (int r = 0; r < R / 2; r++) {
+            if (!rs.ok[r]) continue;
+            // ops_ref.ts:103 swigluRef: fr(fr(g / fr(1 + fr(exp(-g)))) * up)
+            const float gt = y[r], up = y[r + R / 2];
+            const float e = exp_f64r(-gt);
+            const float sg = fdiv(gt, fadd(1.0f, e));
+            a.seg[0].out[(size_t)tok * a.seg[0].out_stride + rs.row[r]] = fmul(sg, up);
+          }
+        } else {
 #pragma unroll
-    for (int r = 0; r < R; r++) y[r] = warp_tree_sum(fadd(accA[r], accB[r]));
-
-    if (lane == 0) {
-      if (EPI == EPI_SWIGLU) {
-#pragma unroll
-        for (int r = 0; r < R / 2; r++) {
-          if (!rok[r]) continue;
-          // ops_ref.ts:103 swigluRef: fr(fr(g / fr(1 + fr(exp(-g)))) * up)
-          const float gt = y[r], up = y[r + R / 2];
-          const float e = exp_f64r(-gt);
-          const float sg = fdiv(gt, fadd(1.0f, e));
-          a.seg[0].out[(size_t)tok * a.seg[0].out_stride + rrow[r]] = fmul(sg, up);
-        }
-      } else {
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-          if (!rok[r]) continue;
-          const GemvSeg& sg = a.seg[rseg[r]];
-          float v = y[r];
-          if (EPI == EPI_RESIDUAL) v = fadd(a.res[(size_t)tok * a.res_stride + rrow[r]], v);
-          sg.out[(size_t)tok * sg.out_stride + rrow[r]] = v;
-          if (EPI == EPI_ARGMAX) {
-            const uint32_t idx = (uint32_t)(rrow[r] + a.am_row_offset);
-            if (am_better(v, idx, best_v, best_i)) {
-              best_v = v;
-              best_i = idx;
+          for (int r = 0; r < R; r++) {
+            if (!rs.ok[r]) continue;
+            const GemvSeg& sg = a.seg[rs.seg[r]];
+            float v = y[r];
+            if (EPI == EPI_RESIDUAL) v = fadd(a.res[(size_t)tok * a.res_stride + rs.row[r]], v);
+            sg.out[(size_t)tok * sg.out_stride + rs.row[r]] = v;
+            if (EPI == EPI_ARGMAX) {
+              const uint32_t idx = (uint32_t)(rs.row[r] + a.am_row_offset);
+              if (am_better(v, idx, best_v, best_i)) {
+                best_v = v;
+                best_i = idx;
+              }
             }
           }
         }
       }
     }
+
+#pragma unroll
+    for (int r = 0; r < R; r++) cur[r] = nxt[r];
+    g = g2;
+    m = m2;
+    rs = rs2;
+    have = have2;
   }
 
   if (EPI == EPI_ARGMAX) {
@@ -364,7 +426,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
           bi = ix;
         }
       }
-      // block reduce
 #pragma unroll
       for (int s = 16; s > 0; s >>= 1) {
         const float ov = __shfl_down_sync(0xffffffffu, bv, s);
@@ -396,8 +457,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
 }
 
 // Shared-memory bytes a k_gemv launch needs.
-inline size_t gemv_smem_bytes(int K) {
-  return (size_t)K * 4 + (136 + GEMV_WARPS * 2) * 4 + 16;
+inline size_t gemv_smem_bytes(int K, bool norm) {
+  return (size_t)(K / 32 * XPAD + (norm ? K : 0) + 136 + GEMV_WARPS * 2) * 4 + 16;
 }
 
 }  // namespace flock

@@ -258,11 +258,14 @@ struct EmbedArgs {
 };
 
 // kernels/embed.wgsl:52: gather one Q8_0 row per token and dequantise it.
+// The grid may be wider than n_tokens: the extra CTAs only share the L2
+// prefetch of the next kernel's weights, which one CTA would issue slowly.
 static __global__ void __launch_bounds__(256) k_embed(const EmbedArgs a) {
   issue_prefetch(a.pf);
   pdl_launch_dependents();
   pdl_wait();
   const int tok = blockIdx.x;
+  if (tok >= a.n_tokens) return;
   const int64_t row = a.ids[tok];
   const int n4 = a.hidden / 4;
   if (row < 0 || row >= a.vocab) {  // never read outside the table

@@ -145,7 +145,7 @@ class SynthModel:
 
     @property
     def vocab(self) -> int:
-        return self.shape.vocab
+        return int(self.embd["rows"])
 
     @property
     def n_layers(self) -> int:

@@ -154,8 +154,10 @@ def test_attention_fast(dev, oracle, nk):
     v = synth.normal(11, f"v{nk}", nk * nKV * hd)
     got = ops.attention(dev, q, k, v, nH, nKV, hd, nk, "fast")
     want = oracle.attn(q, k, v, nH, nKV, hd, nk)
+    # stated tolerance of the reassociated path: 1e-5 of the output scale, and
+    # the north star's f32-decode bound (max rel err <= 1e-3, 1e-3 floor)
     assert abs_err_scaled(got, want) < 1e-5
-    assert rel_err(got, want, 1e-3) < 1e-4
+    assert rel_err(got, want, 1e-3) < 1e-3
 
 
 def test_attention_gqa_map(dev):
