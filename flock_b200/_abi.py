@@ -83,6 +83,7 @@ SIGNATURES = {
     "flock_op_attention_prefill": [_vp, _fp, _fp, _fp, _i, _i, _i, _i, _i, _fp],
     "flock_op_embed": [_vp, _vp, _i32p, _i, _fp],
     "flock_op_argmax": [_vp, _fp, _i64, _i64p, _fp],
+    "flock_argmax_noalloc": [_vp, _i64, _vp, _vp, _vp],
     "flock_layer_create": [_vp, _cfgp, _i, _ccp, _pp, _pp],
     "flock_layer_free": [_vp],
     "flock_layer_encode": [_vp, _fp, _i],

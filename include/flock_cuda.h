@@ -160,6 +160,21 @@ FLOCK_API int flock_op_embed(flock_dev* dev, const flock_tensor* table, const in
 /* kernels/argmax.wgsl:83,112: lowest index among the maxima. */
 FLOCK_API int flock_op_argmax(flock_dev* dev, const float* x, int64_t n, int64_t* index, float* value);
 
+/* No counterpart in the reference.  Greedy argmax (lowest index among the
+ * maxima) over n device-resident f32 logits, for callers that cannot
+ * allocate device memory: a serving framework that owns the GPU's memory,
+ * a decode loop that must not call cudaMalloc (it synchronises the device),
+ * an FFI caller holding only raw device pointers.  x, index_out and
+ * value_out are device pointers; stream may be NULL (the default stream).
+ * Nothing is allocated: the per-CTA partials live in a fixed 8.25 KiB
+ * device array inside the library, present on every GPU that loads it
+ * until exit.  n must be <= 4194304 (FLOCK_E_LIMIT otherwise).  The first
+ * call on a device resolves that array's address (cudaGetSymbolAddress) --
+ * make it before any stream capture.  Calls share the array: calls whose
+ * kernels overlap on the GPU race, so order them on one stream. */
+FLOCK_API int flock_argmax_noalloc(const float* x, int64_t n, int32_t* index_out, float* value_out,
+                                   void* stream);
+
 /* ---------------------------------------------------------------- layer */
 
 /* kernels/layer.ts:228 Layer.fromBuffers: `names` are the GGUF suffixes
