@@ -25,6 +25,7 @@ FLOCK_E_UNSUPPORTED = -8
 FLOCK_Q8_0, FLOCK_Q4_0, FLOCK_F32 = 8, 4, 32
 FLOCK_ROPE_NEOX, FLOCK_ROPE_NORM = 0, 1
 FLOCK_ATTN_EXACT, FLOCK_ATTN_FAST = 0, 1
+FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT = 0, 1
 
 
 class FlockError(RuntimeError):
@@ -110,6 +111,8 @@ SIGNATURES = {
     "flock_model_pos": [_vp, _ip],
     "flock_model_held": [_vp, _ip],
     "flock_model_set_token": [_vp, ctypes.c_int32],
+    "flock_model_set_decode_mode": [_vp, _i],
+    "flock_model_get_decode_mode": [_vp, _ip],
     "flock_model_current_token": [_vp, _i32p],
     "flock_shard_matvec_create": [_vp, _u8p, _u8p, _i64, _i64, _i, _i, _i64, _pp],
     "flock_shard_matvec_free": [_vp],

@@ -3,10 +3,14 @@
     python -m flock_b200.cases layer [--time]   # one decode layer (config 0 shape, 256-key cache)
     python -m flock_b200.cases head  [--time]   # the 151936 x 1024 Q8_0 head matvec
     python -m flock_b200.cases gemv  [--time]   # the config 1 matvec sweep (M = 1)
+    python -m flock_b200.cases model [--time] [--kernels]
+                                                # 28-layer 0.6B-shape decode, persistent
+                                                # kernel (default) or per-op kernel graph
 
 Each case builds seeded synthetic weights, runs a few warm launches and, with
---time, prints CUDA-event timings.  They are small enough (< 0.5 GB on the
-device) to run under ncu.
+--time, prints CUDA-event timings.  They are small enough (< 1 GB on the
+device) to run under ncu; the model case decodes 3 warm tokens after a
+64-token prompt, then (with --time) 64 timed tokens.
 """
 from __future__ import annotations
 
@@ -59,8 +63,25 @@ def gemv_case(timed: bool) -> None:
                       f"{b / ms / 1e6:.1f} GB/s")
 
 
+def model_case(timed: bool) -> None:
+    from .model import Model
+    dev = flib.get_device(0)
+    m = synth.model(300)
+    M = Model.create(dev, m, QWEN3_06B.with_(attention="fast"))
+    M.decode_mode = "kernels" if "--kernels" in sys.argv else "persistent"
+    M.step(synth.uniform_ids(300, "prompt", 64, synth.QWEN3_06B.vocab).tolist())
+    M.decode_device(3)
+    dev.sync()
+    if timed:
+        dev.timer_start()
+        M.decode_device(64)
+        ms = dev.timer_stop()
+        print(f"model decode ({M.decode_mode}): {ms / 64 * 1000:.1f} us/token, "
+              f"{64 / ms * 1000:.1f} tok/s")
+
+
 if __name__ == "__main__":
     case = sys.argv[1] if len(sys.argv) > 1 else "layer"
     timed = "--time" in sys.argv
-    {"layer": layer_case, "head": head_case, "gemv": gemv_case}[case](timed)
+    {"layer": layer_case, "head": head_case, "gemv": gemv_case, "model": model_case}[case](timed)
     print("ok")

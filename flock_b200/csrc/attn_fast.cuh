@@ -49,24 +49,25 @@ struct AttnFastArgs {
 // Exact RMSNorm (WG = 128) + RoPE of one 128-vector by one 128-thread half
 // of the block; `red` is that half's reduction scratch.  Mirrors
 // k_qk_norm_rope_append.  All threads of the block must call it together.
+template <typename Sync>
 FLOCK_DEV void norm_rope_half(const float* src, const float* gain, float eps, int pos,
                               const float* inv_freq, int neox, float* dst, float* red,
-                              float* tmp, bool active) {
+                              float* tmp, bool active, Sync sync) {
   const int t = threadIdx.x & 127;
   const float x = active ? src[t] : 0.0f;
   red[t] = ffma(x, x, 0.0f);
-  __syncthreads();
+  sync();
   if (t < 64) red[t] = fadd(red[t], red[t + 64]);
-  __syncthreads();
+  sync();
   if (t < 32) {
     float w = fadd(red[t], red[t + 32]);
     w = warp_tree_sum(w);
     if (t == 0) red[128] = w;
   }
-  __syncthreads();
+  sync();
   const float scale = rsqrt_f64r(fadd(fdiv(red[128], 128.0f), eps));
   if (active) tmp[t] = fmul(fmul(x, scale), gain[t]);
-  __syncthreads();
+  sync();
   if (active && t < 64) {
     const float theta = fmul((float)pos, inv_freq[t]);
     const float c = __double2float_rn(cos((double)theta));
@@ -76,7 +77,7 @@ FLOCK_DEV void norm_rope_half(const float* src, const float* gain, float eps, in
     dst[ia] = ffma(-bv, s, fmul(av, c));
     dst[ib] = ffma(bv, c, fmul(av, s));
   }
-  __syncthreads();
+  sync();
 }
 
 constexpr int ATTN_FAST_THREADS = 256;
@@ -91,20 +92,18 @@ constexpr int AF_QRAW = 0, AF_KRAW = 512, AF_VRAW = 640, AF_GQ = 768, AF_GK = 89
               AF_RED = 2112, AF_SC = 2376, AF_ML = AF_SC + 4 * ATTN_TILE, AF_KT = AF_ML + 16,
               AF_VT = AF_KT + ATTN_TILE * 128, AF_END = AF_VT + ATTN_TILE * 128;
 
-static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(const AttnFastArgs a) {
-  extern __shared__ __align__(16) float dsm[];
-  __shared__ bool last;
+// One (kv head g, split s) work item, run by ATTN_FAST_THREADS threads that
+// synchronise with `sync()`; `dsm` holds AF_END floats; `last` is a shared
+// flag.  `pos` is the position of the token being decoded.
+template <typename Sync>
+FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, float* dsm,
+                              bool* last_flag, Sync sync) {
   const int G = a.n_heads / a.n_kv_heads;  // <= 4
-  const int g = blockIdx.x, s = blockIdx.y, t = threadIdx.x;
+  const int t = threadIdx.x;
   const int half = t >> 7, lane = t & 31, warp = t >> 5;
   const int hd = 128;
   const size_t kvs = (size_t)a.n_kv_heads * hd;
 
-  issue_prefetch(a.pf);
-  pdl_launch_dependents();
-  pdl_wait();
-
-  const int pos = a.ctl[0];
   const int n_keys = pos + 1;
   const int chunk = (n_keys + a.splits - 1) / a.splits;
   const int k0 = s * chunk;
@@ -148,7 +147,7 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
     }
     stage_tile(k0, min(nk, ATTN_TILE));
   }
-  __syncthreads();
+  sync();
 
   float* qv = dsm + AF_QV;
   float* knew = dsm + AF_KNEW;
@@ -163,17 +162,17 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
       const float* src = is_k ? dsm + AF_KRAW : dsm + AF_QRAW + (active ? vi : 0) * 128;
       float* dst = is_k ? knew : qv + (active ? vi : 0) * 128;
       norm_rope_half(src, is_k ? dsm + AF_GK : dsm + AF_GQ, a.eps, pos, dsm + AF_INV, a.neox,
-                     dst, dsm + AF_RED + half * 132, dsm + AF_TMP + half * 128, active);
+                     dst, dsm + AF_RED + half * 132, dsm + AF_TMP + half * 128, active, sync);
     }
     if (t < 128) vnew[t] = dsm[AF_VRAW + t];
-    __syncthreads();
+    sync();
     if (s == 0 && t < 128) {
       a.kcache[(size_t)pos * kvs + (size_t)g * hd + t] = knew[t];
       a.vcache[(size_t)pos * kvs + (size_t)g * hd + t] = vnew[t];
     }
   } else {
     for (int i = t; i < G * 128; i += ATTN_FAST_THREADS) qv[i] = dsm[AF_QRAW + i];
-    __syncthreads();
+    sync();
   }
 
   const float scale = __double2float_rn(1.0 / sqrt((double)hd));
@@ -190,7 +189,7 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
   for (int t0 = k0; t0 < k1; t0 += ATTN_TILE) {
     const int nt = min(ATTN_TILE, k1 - t0);
     if (t0 != k0) {
-      __syncthreads();
+      sync();
       stage_tile(t0, nt);
     }
     // the new key/value live in shared memory, not (yet) in the cache
@@ -198,7 +197,7 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
       kt[(pos - t0) * 128 + t] = knew[t];
       vt[(pos - t0) * 128 + t] = vnew[t];
     }
-    __syncthreads();
+    sync();
     // scores: one warp per key, all G heads per K row
     for (int j = warp; j < nt; j += ATTN_FAST_THREADS / 32) {
       const float4 kv = reinterpret_cast<const float4*>(kt + j * 128)[lane];
@@ -210,7 +209,7 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
         if (lane == 0) sc[hq * ATTN_TILE + j] = p * scale;
       }
     }
-    __syncthreads();
+    sync();
     // online softmax per head (warp hq): new max, correction, probabilities
     if (warp < G) {
       const int hq = warp;
@@ -236,7 +235,7 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
         ml[4 * hq + 2] = c;
       }
     }
-    __syncthreads();
+    sync();
     // unnormalised output: thread owns outputs (hq, i) = t, t + 256
 #pragma unroll
     for (int u = 0; u < 2; u++) {
@@ -265,10 +264,10 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
     }
   }
   __threadfence();
-  __syncthreads();
-  if (t == 0) last = atomicAdd(a.count + g, 1u) == (uint32_t)(a.splits - 1);
-  __syncthreads();
-  if (!last) return;
+  sync();
+  if (t == 0) *last_flag = atomicAdd(a.count + g, 1u) == (uint32_t)(a.splits - 1);
+  sync();
+  if (!*last_flag) return;
   __threadfence();
   for (int oi = t; oi < G * hd; oi += ATTN_FAST_THREADS) {
     const int hq = oi / hd, i = oi % hd;
@@ -284,6 +283,19 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
     a.out[(size_t)(g * G + hq) * hd + i] = O / L;
   }
   if (t == 0) a.count[g] = 0;
+}
+
+struct BlockSync {
+  FLOCK_DEV void operator()() const { __syncthreads(); }
+};
+
+static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(const AttnFastArgs a) {
+  extern __shared__ __align__(16) float dsm[];
+  __shared__ bool last;
+  issue_prefetch(a.pf);
+  pdl_launch_dependents();
+  pdl_wait();
+  attn_fast_item(a, blockIdx.x, blockIdx.y, a.ctl[0], dsm, &last, BlockSync{});
 }
 
 inline size_t attn_fast_smem(int /*chunk_cap*/) { return (size_t)AF_END * 4; }

@@ -165,10 +165,30 @@ static void pf_add(PrefetchList& pf, const flock_tensor* t) {
   pf.n++;
 }
 
+// ------------------------------------------------------------ device refs
+
+flock_dev* dev_retain(flock_dev* d) {
+  if (d) d->refs.fetch_add(1, std::memory_order_relaxed);
+  return d;
+}
+
+void dev_release(flock_dev* d) {
+  if (!d || d->refs.fetch_sub(1, std::memory_order_acq_rel) != 1) return;
+  cudaSetDevice(d->ordinal);
+  cudaStreamSynchronize(d->stream);
+  cudaEventDestroy(d->t0);
+  cudaEventDestroy(d->t1);
+  cudaStreamDestroy(d->stream);
+  delete d;
+}
+
 // ------------------------------------------------------------- workspace
 
-int Workspace::alloc(const flock_layer_config& c) {
+int Workspace::alloc(const flock_layer_config& c, int sm_count) {
   P = c.max_prefill < 1 ? 1 : c.max_prefill;
+  attn_splits = c.n_kv_heads > 0 ? sm_count / c.n_kv_heads : 1;
+  if (attn_splits < 1) attn_splits = 1;
+  if (attn_splits > attn_split_cap) attn_splits = attn_split_cap;
   H = c.hidden;
   nH = c.n_heads;
   nKV = c.n_kv_heads;
@@ -182,7 +202,7 @@ int Workspace::alloc(const flock_layer_config& c) {
   FLOCK_TRY(qn.alloc((size_t)P * nH * hd * f));
   FLOCK_TRY(attn.alloc((size_t)P * nH * hd * f));
   FLOCK_TRY(act.alloc((size_t)P * F * f));
-  FLOCK_TRY(attn_part.alloc((size_t)nH * attn_splits * (hd + 2) * f));
+  FLOCK_TRY(attn_part.alloc((size_t)nH * attn_split_cap * (hd + 2) * f));
   FLOCK_TRY(attn_count.alloc((size_t)nKV * 4));
   FLOCK_CK(cudaMemset(attn_count.p, 0, attn_count.bytes));
   return FLOCK_OK;
@@ -222,7 +242,7 @@ static int check_cfg(const flock_layer_config& c) {
 int layer_init(flock_layer* L, flock_dev* dev, const flock_layer_config& cfg, Workspace* ws,
                int* shared_ctl) {
   FLOCK_TRY(check_cfg(cfg));
-  L->dev = dev;
+  L->dev = dev_retain(dev);
   L->cfg = cfg;
   const size_t kv = (size_t)cfg.max_keys * cfg.n_kv_heads * cfg.head_dim * sizeof(float);
   FLOCK_TRY(L->kcache.alloc(kv));
@@ -244,7 +264,7 @@ int layer_init(flock_layer* L, flock_dev* dev, const flock_layer_config& cfg, Wo
   if (ws) {
     L->ws = ws;
   } else {
-    FLOCK_TRY(L->ws_own.alloc(cfg));
+    FLOCK_TRY(L->ws_own.alloc(cfg, dev->sm_count));
     L->ws = &L->ws_own;
     L->owns_ws = true;
   }
@@ -454,13 +474,7 @@ int flock_dev_open(int ordinal, flock_dev** out) {
 }
 
 int flock_dev_close(flock_dev* d) {
-  if (!d) return FLOCK_OK;
-  cudaSetDevice(d->ordinal);
-  cudaStreamSynchronize(d->stream);
-  cudaEventDestroy(d->t0);
-  cudaEventDestroy(d->t1);
-  cudaStreamDestroy(d->stream);
-  delete d;
+  flock::dev_release(d);
   return FLOCK_OK;
 }
 
@@ -534,7 +548,7 @@ int flock_tensor_from_split(flock_dev* dev, int dtype, const uint8_t* qs, const 
   }
   FLOCK_CK(cudaSetDevice(dev->ordinal));
   flock_tensor* t = new flock_tensor();
-  t->dev = dev;
+  t->dev = flock::dev_retain(dev);
   t->dtype = dtype;
   t->rows = rows;
   t->cols = cols;
@@ -543,7 +557,7 @@ int flock_tensor_from_split(flock_dev* dev, int dtype, const uint8_t* qs, const 
   const int64_t qs_bytes = dtype == FLOCK_Q8_0 ? rows * cols : rows * nb * 16;
   int rc;
   if ((rc = t->qs.alloc(qs_bytes)) || (rc = t->sc.alloc(rows * t->sc_stride * 2))) {
-    delete t;
+    flock_tensor_free(t);
     return rc;
   }
   cudaError_t e = cudaMemcpy(t->qs.p, qs, qs_bytes, cudaMemcpyHostToDevice);
@@ -559,7 +573,7 @@ int flock_tensor_from_split(flock_dev* dev, int dtype, const uint8_t* qs, const 
   }
   if (e != cudaSuccess) {
     set_error("tensor upload failed: %s", cudaGetErrorString(e));
-    delete t;
+    flock_tensor_free(t);
     return FLOCK_E_CUDA;
   }
   *out = t;
@@ -585,13 +599,13 @@ int flock_tensor_from_f32(flock_dev* dev, const float* data, int64_t n, flock_te
   if (!dev || !data || n < 1 || !out) return FLOCK_E_ARG;
   FLOCK_CK(cudaSetDevice(dev->ordinal));
   flock_tensor* t = new flock_tensor();
-  t->dev = dev;
+  t->dev = flock::dev_retain(dev);
   t->dtype = FLOCK_F32;
   t->rows = 1;
   t->cols = n;
   int rc = t->data.alloc(n * 4);
   if (rc) {
-    delete t;
+    flock_tensor_free(t);
     return rc;
   }
   FLOCK_CK(cudaMemcpy(t->data.p, data, n * 4, cudaMemcpyHostToDevice));
@@ -601,8 +615,10 @@ int flock_tensor_from_f32(flock_dev* dev, const float* data, int64_t n, flock_te
 
 int flock_tensor_free(flock_tensor* t) {
   if (t) {
-    cudaSetDevice(t->dev->ordinal);
+    flock_dev* d = t->dev;
+    if (d) cudaSetDevice(d->ordinal);
     delete t;
+    flock::dev_release(d);
   }
   return FLOCK_OK;
 }
@@ -985,7 +1001,7 @@ int layer_build(flock_dev* dev, const flock_layer_config* cfg, int n_tensors,
     }
   int rc = layer_init(L, dev, *cfg, ws, ctl);
   if (rc) {
-    delete L;
+    flock_layer_free(L);
     return rc;
   }
   *out = L;
@@ -1004,9 +1020,13 @@ int flock_layer_create(flock_dev* dev, const flock_layer_config* cfg, int n_tens
 
 int flock_layer_free(flock_layer* L) {
   if (L) {
-    cudaSetDevice(L->dev->ordinal);
-    cudaStreamSynchronize(L->dev->stream);
+    flock_dev* d = L->dev;
+    if (d) {
+      cudaSetDevice(d->ordinal);
+      cudaStreamSynchronize(d->stream);
+    }
     delete L;
+    flock::dev_release(d);
   }
   return FLOCK_OK;
 }

@@ -2,6 +2,8 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include <cstdint>
 #include <cstdio>
 #include <string>
@@ -13,6 +15,10 @@
 namespace flock {
 
 void set_error(const char* fmt, ...);
+
+// Device references (see flock_dev): retain returns its argument.
+flock_dev* dev_retain(flock_dev* d);
+void dev_release(flock_dev* d);
 
 #define FLOCK_CK(call)                                                              \
   do {                                                                              \
@@ -46,7 +52,11 @@ struct DBuf {
 
 }  // namespace flock
 
+// Every object created on a device (tensor, layer, model, shard, head,
+// communicator) holds a reference, so flock_dev_close only drops the
+// caller's reference and the device lives until the last object is freed.
 struct flock_dev {
+  std::atomic<int> refs{1};
   int ordinal = 0;
   int sm_count = 148;
   cudaStream_t stream = nullptr;
@@ -72,8 +82,9 @@ struct Workspace {
   int P = 0, H = 0, nH = 0, nKV = 0, hd = 0, F = 0;
   DBuf h, q, k, v, qn, attn, act;
   DBuf attn_part, attn_count;  // fast decode attention partials
-  int attn_splits = 16;
-  int alloc(const flock_layer_config& c);
+  int attn_splits = 16;         // splits: SMs / kv heads, so one wave covers them
+  int attn_split_cap = 64;      // partial slots allocated (the persistent kernel uses more)
+  int alloc(const flock_layer_config& c, int sm_count);
 };
 
 enum { W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_ATTN_NORM, W_Q_NORM, W_K_NORM, W_FFN_NORM,

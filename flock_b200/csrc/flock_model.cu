@@ -12,6 +12,7 @@
 #include <cstring>
 #include <vector>
 
+#include "decode_mk.cuh"
 #include "flock_internal.h"
 #include "gemv.cuh"
 #include "ops.cuh"
@@ -30,6 +31,13 @@ struct flock_model {
   DBuf ctl, ids, hist, logits, normed, am_val, am_idx, am_count, am_best_val;
   int pos = 0;  // host mirror of ctl[0] after the last step
   cudaGraphExec_t decode_graph = nullptr;
+  // persistent decode kernel
+  int decode_mode = FLOCK_DECODE_KERNELS;
+  bool mk_ok = false;       // shape fits the persistent kernel
+  DBuf mk_layers, mk_bar, mk_err;
+  MkArgs mk{};
+  size_t mk_smem = 0;
+  int mk_grid = 0;
 };
 
 namespace {
@@ -170,15 +178,148 @@ int encode_tokens(flock_model* m, const int32_t* ids, int n, int* last_chunk) {
   return FLOCK_OK;
 }
 
+// The persistent decode kernel's tables and launch shape (once per model).
+int mk_prepare(flock_model* m) {
+  const flock_layer_config& c = m->cfg;
+  m->mk_ok = false;
+  if (c.attention != FLOCK_ATTN_FAST || !m->embd || !m->head || m->held < 1 || c.head_dim != 128 ||
+      c.n_heads / c.n_kv_heads > 4 || c.hidden > 4096)
+    return FLOCK_OK;
+  int dev = m->dev->ordinal, coop = 0, smem_optin = 0;
+  FLOCK_CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+  FLOCK_CK(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  if (!coop) return FLOCK_OK;
+  const int grid = m->dev->sm_count;
+  const int splits = grid / c.n_kv_heads;
+  if (splits < 1 || splits > m->ws.attn_split_cap) return FLOCK_OK;
+  MkArgs& a = m->mk;
+  a = MkArgs{};
+  a.n_stages = 4;
+  a.stage_bytes = 32 * 1024;
+  const size_t smem = mk_smem_bytes(a.stage_bytes, a.n_stages, c.hidden, c.n_heads * c.head_dim,
+                                    c.ffn) + 1024;  // + static shared
+  if (smem > (size_t)smem_optin) return FLOCK_OK;
+  // every unit of every phase must fit one stage
+  const int kmax = c.hidden > c.ffn ? c.hidden : c.ffn;
+  if (2 * (kmax + ((kmax / 32 + 7) / 8 * 8) * 2) > a.stage_bytes) return FLOCK_OK;
+  if (m->embd->dtype != FLOCK_Q8_0 || m->head->dtype != FLOCK_Q8_0) return FLOCK_OK;
+  for (int i = 0; i < m->held; i++)
+    for (int t = 0; t < 7; t++)
+      if (m->layers[i]->w[t]->dtype != FLOCK_Q8_0) return FLOCK_OK;
+  std::vector<MkLayer> tab(m->held);
+  for (int i = 0; i < m->held; i++) {
+    flock_layer* L = m->layers[i];
+    for (int t = 0; t < 7; t++) {
+      tab[i].qs[t] = L->w[t]->qs.as<uint8_t>();
+      tab[i].sc[t] = L->w[t]->sc.as<uint16_t>();
+      tab[i].sc_stride[t] = L->w[t]->sc_stride;
+    }
+    tab[i].attn_norm = L->w[W_ATTN_NORM]->data.as<float>();
+    tab[i].q_norm = L->w[W_Q_NORM]->data.as<float>();
+    tab[i].k_norm = L->w[W_K_NORM]->data.as<float>();
+    tab[i].ffn_norm = L->w[W_FFN_NORM]->data.as<float>();
+    tab[i].kcache = L->kcache.as<float>();
+    tab[i].vcache = L->vcache.as<float>();
+  }
+  FLOCK_TRY(m->mk_layers.alloc(tab.size() * sizeof(MkLayer)));
+  FLOCK_CK(cudaMemcpy(m->mk_layers.p, tab.data(), tab.size() * sizeof(MkLayer),
+                      cudaMemcpyHostToDevice));
+  FLOCK_TRY(m->mk_bar.alloc(16));
+  FLOCK_TRY(m->mk_err.alloc(16));
+  FLOCK_CK(cudaMemset(m->mk_err.p, 0, 16));
+  a.layers = m->mk_layers.as<MkLayer>();
+  a.n_layers = m->held;
+  a.H = c.hidden;
+  a.nH = c.n_heads;
+  a.nKV = c.n_kv_heads;
+  a.hd = c.head_dim;
+  a.F = c.ffn;
+  a.vocab = m->vocab;
+  a.eps = c.eps;
+  a.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
+  a.inv_freq = m->layers[0]->inv_freq.as<float>();
+  a.embd_qs = m->embd->qs.as<uint8_t>();
+  a.embd_sc = m->embd->sc.as<uint16_t>();
+  a.embd_sc_stride = m->embd->sc_stride;
+  a.head_qs = m->head->qs.as<uint8_t>();
+  a.head_sc = m->head->sc.as<uint16_t>();
+  a.head_sc_stride = m->head->sc_stride;
+  a.out_norm = m->out_norm->data.as<float>();
+  a.h = m->ws.h.as<float>();
+  a.q = m->ws.q.as<float>();
+  a.k = m->ws.k.as<float>();
+  a.v = m->ws.v.as<float>();
+  a.attn = m->ws.attn.as<float>();
+  a.act = m->ws.act.as<float>();
+  a.logits = m->logits.as<float>();
+  a.ids = m->ids.as<int32_t>();
+  a.hist = m->hist.as<int32_t>();
+  a.hist_cap = c.max_keys;
+  a.attn_part = m->ws.attn_part.as<float>();
+  a.attn_count = m->ws.attn_count.as<uint32_t>();
+  a.splits = splits;
+  a.am_val = m->am_val.as<float>();
+  a.am_idx = m->am_idx.as<uint32_t>();
+  a.am_count = m->am_count.as<uint32_t>();
+  a.am_best_val = m->am_best_val.as<float>();
+  a.ctl = m->ctl.as<int>();
+  a.bar = m->mk_bar.as<unsigned>();
+  a.err = m->mk_err.as<int>();
+  FLOCK_CK(cudaFuncSetAttribute(k_decode_mk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)smem));
+  int per_sm = 0;
+  FLOCK_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mk, MK_THREADS, smem));
+  if (per_sm < 1) return FLOCK_OK;
+  m->mk_smem = smem;
+  m->mk_grid = grid;
+  m->mk_ok = true;
+  return FLOCK_OK;
+}
+
+int enqueue_mk(flock_model* m) {
+  FLOCK_CK(cudaMemsetAsync(m->mk_bar.p, 0, 4, m->dev->stream));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(m->mk_grid);
+  cfg.blockDim = dim3(MK_THREADS);
+  cfg.dynamicSmemBytes = m->mk_smem;
+  cfg.stream = m->dev->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FLOCK_CK(cudaLaunchKernelEx(&cfg, k_decode_mk, m->mk));
+  return FLOCK_OK;
+}
+
+int check_mk_error(flock_model* m) {
+  if (!m->mk_ok || m->decode_mode != FLOCK_DECODE_PERSISTENT) return FLOCK_OK;
+  int err = 0;
+  FLOCK_CK(cudaMemcpy(&err, m->mk_err.p, 4, cudaMemcpyDeviceToHost));
+  if (err) {
+    set_error("persistent decode kernel gave up waiting (%s timeout)",
+              err == 2 ? "grid barrier" : "weight stream");
+    cudaMemset(m->mk_err.p, 0, 4);
+    return FLOCK_E_CUDA;
+  }
+  return FLOCK_OK;
+}
+
 int capture_decode(flock_model* m) {
   if (m->decode_graph) return FLOCK_OK;
   cudaStream_t st = m->dev->stream;
   cudaGraph_t g = nullptr;
+  const bool mk = m->decode_mode == FLOCK_DECODE_PERSISTENT && m->mk_ok;
   FLOCK_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-  int rc = enqueue_embed(m, 1);
-  if (!rc) rc = enqueue_layers(m, 1);
-  if (!rc) rc = enqueue_head(m, 0);
-  if (!rc) rc = enqueue_record(m);
+  int rc = FLOCK_OK;
+  if (mk) {
+    rc = enqueue_mk(m);
+  } else {
+    rc = enqueue_embed(m, 1);
+    if (!rc) rc = enqueue_layers(m, 1);
+    if (!rc) rc = enqueue_head(m, 0);
+    if (!rc) rc = enqueue_record(m);
+  }
   cudaError_t e = cudaStreamEndCapture(st, &g);
   if (rc) {
     if (g) cudaGraphDestroy(g);
@@ -230,7 +371,7 @@ int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab,
   }
   FLOCK_CK(cudaSetDevice(dev->ordinal));
   flock_model* m = new flock_model();
-  m->dev = dev;
+  m->dev = dev_retain(dev);
   m->cfg = *cfg;
   m->vocab = vocab;
   m->n_layers = n_layers;
@@ -242,7 +383,7 @@ int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab,
     flock_model_free(m);
     return r;
   };
-  if ((rc = m->ws.alloc(*cfg))) return fail(rc);
+  if ((rc = m->ws.alloc(*cfg, dev->sm_count))) return fail(rc);
   if ((rc = m->ctl.alloc(16))) return fail(rc);
   if (cudaMemset(m->ctl.p, 0, 16) != cudaSuccess) return fail(FLOCK_E_CUDA);
   if ((rc = m->ids.alloc((size_t)m->ws.P * 4 + 16))) return fail(rc);
@@ -272,17 +413,38 @@ int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab,
     m->layers.push_back(L);
   }
   m->held = cut;
+  if ((rc = mk_prepare(m))) return fail(rc);
   *out = m;
+  return FLOCK_OK;
+}
+
+int flock_model_set_decode_mode(flock_model* m, int mode) {
+  if (!m || (mode != FLOCK_DECODE_KERNELS && mode != FLOCK_DECODE_PERSISTENT)) return FLOCK_E_ARG;
+  if (mode != m->decode_mode && m->decode_graph) {
+    cudaStreamSynchronize(m->dev->stream);
+    cudaGraphExecDestroy(m->decode_graph);
+    m->decode_graph = nullptr;
+  }
+  m->decode_mode = mode;
+  return FLOCK_OK;
+}
+
+int flock_model_get_decode_mode(const flock_model* m, int* mode) {
+  if (!m || !mode) return FLOCK_E_ARG;
+  *mode = (m->decode_mode == FLOCK_DECODE_PERSISTENT && m->mk_ok) ? FLOCK_DECODE_PERSISTENT
+                                                                  : FLOCK_DECODE_KERNELS;
   return FLOCK_OK;
 }
 
 int flock_model_free(flock_model* m) {
   if (!m) return FLOCK_OK;
-  cudaSetDevice(m->dev->ordinal);
-  cudaStreamSynchronize(m->dev->stream);
+  flock_dev* d = m->dev;
+  cudaSetDevice(d->ordinal);
+  cudaStreamSynchronize(d->stream);
   if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
   for (auto* L : m->layers) flock_layer_free(L);
   delete m;
+  dev_release(d);
   return FLOCK_OK;
 }
 
@@ -327,7 +489,7 @@ int flock_model_step(flock_model* m, const int32_t* ids, int n, int32_t* next_id
   for (auto* L : m->layers) L->n_keys = m->pos;
   FLOCK_CK(cudaMemcpyAsync(next_id, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return FLOCK_OK;
+  return check_mk_error(m);
 }
 
 int flock_model_decode_device(flock_model* m, int n_steps, int32_t* out_ids) {
@@ -345,7 +507,7 @@ int flock_model_decode_device(flock_model* m, int n_steps, int32_t* out_ids) {
     FLOCK_CK(cudaMemcpyAsync(out_ids, m->hist.as<int32_t>() + start, (size_t)n_steps * 4,
                              cudaMemcpyDeviceToHost, m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return FLOCK_OK;
+  return check_mk_error(m);
 }
 
 int flock_model_generate(flock_model* m, const int32_t* prompt, int n_prompt, int max_tokens,

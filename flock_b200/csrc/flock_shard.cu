@@ -181,7 +181,7 @@ int flock_shard_matvec_create(flock_dev* dev, const uint8_t* qs, const uint8_t* 
   }
   FLOCK_CK(cudaSetDevice(dev->ordinal));
   flock_shard* s = new flock_shard();
-  s->dev = dev;
+  s->dev = flock::dev_retain(dev);
   s->rows = rows;
   s->cols = cols;
   s->n = n;
@@ -209,7 +209,9 @@ int flock_shard_matvec_create(flock_dev* dev, const uint8_t* qs, const uint8_t* 
 int flock_shard_matvec_free(flock_shard* s) {
   if (!s) return FLOCK_OK;
   for (auto* t : s->shards) flock_tensor_free(t);
+  flock_dev* d = s->dev;
   delete s;
+  flock::dev_release(d);
   return FLOCK_OK;
 }
 
@@ -262,7 +264,7 @@ int flock_sharded_head_create(flock_dev* dev, const uint8_t* qs, const uint8_t* 
   FLOCK_TRY(shard_ranges(vocab, n, 1, st, ct));
   FLOCK_CK(cudaSetDevice(dev->ordinal));
   flock_head* h = new flock_head();
-  h->dev = dev;
+  h->dev = flock::dev_retain(dev);
   h->vocab = vocab;
   h->hidden = hidden;
   h->n = n;
@@ -289,7 +291,9 @@ int flock_sharded_head_create(flock_dev* dev, const uint8_t* qs, const uint8_t* 
 int flock_sharded_head_free(flock_head* h) {
   if (!h) return FLOCK_OK;
   for (auto* t : h->shards) flock_tensor_free(t);
+  flock_dev* d = h->dev;
   delete h;
+  flock::dev_release(d);
   return FLOCK_OK;
 }
 
@@ -458,7 +462,7 @@ int flock_comm_init(flock_dev* dev, int n_ranks, int rank, const uint8_t id[128]
   if (!g_nccl.load()) return FLOCK_E_NCCL;
   FLOCK_CK(cudaSetDevice(dev->ordinal));
   flock_comm* c = new flock_comm();
-  c->dev = dev;
+  c->dev = flock::dev_retain(dev);
   c->n_ranks = n_ranks;
   c->rank = rank;
   c->timeout_ms = timeout_ms > 0 ? timeout_ms : 30000;
@@ -469,7 +473,9 @@ int flock_comm_init(flock_dev* dev, int n_ranks, int rank, const uint8_t id[128]
   ncclResult_t r = g_nccl.CommInitRankConfig(&c->comm, n_ranks, uid, rank, &cfg);
   if (r != ncclSuccess && r != ncclInProgress) {
     set_error("ncclCommInitRankConfig: %s", g_nccl.GetErrorString(r));
+    flock_dev* d = c->dev;
     delete c;
+    flock::dev_release(d);
     return FLOCK_E_NCCL;
   }
   auto t0 = std::chrono::steady_clock::now();
@@ -480,14 +486,18 @@ int flock_comm_init(flock_dev* dev, int n_ranks, int rank, const uint8_t id[128]
     if (st != ncclInProgress) {
       set_error("NCCL init failed: %s", g_nccl.GetErrorString(st));
       g_nccl.CommAbort(c->comm);
+      flock_dev* d = c->dev;
       delete c;
+      flock::dev_release(d);
       return FLOCK_E_NCCL;
     }
     if (std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count() >
         c->timeout_ms) {
       set_error("NCCL init timed out after %d ms", c->timeout_ms);
       g_nccl.CommAbort(c->comm);
+      flock_dev* d = c->dev;
       delete c;
+      flock::dev_release(d);
       return FLOCK_E_NCCL;
     }
     std::this_thread::sleep_for(std::chrono::milliseconds(1));
@@ -502,7 +512,9 @@ int flock_comm_free(flock_comm* c) {
     cudaStreamSynchronize(c->dev->stream);
     g_nccl.CommDestroy(c->comm);
   }
+  flock_dev* d = c->dev;
   delete c;
+  flock::dev_release(d);
   return FLOCK_OK;
 }
 

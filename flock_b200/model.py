@@ -180,6 +180,18 @@ class Model:
         _abi.call("flock_model_held", self.handle, ctypes.byref(n))
         return n.value
 
+    @property
+    def decode_mode(self) -> str:
+        """"persistent" (one cooperative kernel per token) or "kernels"."""
+        n = ctypes.c_int()
+        _abi.call("flock_model_get_decode_mode", self.handle, ctypes.byref(n))
+        return "persistent" if n.value == _abi.FLOCK_DECODE_PERSISTENT else "kernels"
+
+    @decode_mode.setter
+    def decode_mode(self, mode: str) -> None:
+        _abi.call("flock_model_set_decode_mode", self.handle,
+                  _abi.FLOCK_DECODE_PERSISTENT if mode == "persistent" else _abi.FLOCK_DECODE_KERNELS)
+
     def set_token(self, token: int) -> None:
         """The id the next device-fed decode step consumes."""
         _abi.call("flock_model_set_token", self.handle, int(token))

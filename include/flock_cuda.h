@@ -247,6 +247,14 @@ FLOCK_API int flock_model_reset(flock_model* m);
 FLOCK_API int flock_model_rewind(flock_model* m, int n_keys);
 FLOCK_API int flock_model_pos(const flock_model* m, int* out);
 FLOCK_API int flock_model_held(const flock_model* m, int* out);
+#define FLOCK_DECODE_KERNELS 0    /* one kernel per op, CUDA graph + PDL */
+#define FLOCK_DECODE_PERSISTENT 1 /* one cooperative persistent kernel per token */
+/* Choose the decode engine for single-token steps (default: the kernel
+ * graph).  The persistent kernel needs fast attention, Q8_0 weights, head_dim
+ * 128 and a resident embedding/head; otherwise the kernel graph runs and
+ * flock_model_get_decode_mode reports it.  Both give bit-identical results. */
+FLOCK_API int flock_model_set_decode_mode(flock_model* m, int mode);
+FLOCK_API int flock_model_get_decode_mode(const flock_model* m, int* mode);
 /* Set the token the next device-fed decode step consumes (ids[0]). */
 FLOCK_API int flock_model_set_token(flock_model* m, int32_t id);
 /* kernels/model.ts:541 currentToken(). */

@@ -122,6 +122,19 @@ def test_generate_eos_and_rewind(dev, small):
     assert out2 == out[:out.index(out[2])]
 
 
+def test_objects_outlive_device_close(small):
+    """Closing a device drops only the caller's reference: models and tensors
+    made on it keep working and free cleanly afterwards."""
+    d = flib.get_device(0)
+    t = flib.GpuTensor.from_f32(d, np.ones(64, np.float32))
+    M = Model.create(d, small)
+    first = M.step([1, 2, 3])
+    d.close()
+    assert M.step([first]) >= 0
+    M.free()
+    t.free()
+
+
 def test_full_06b_model_greedy_ids(dev, oracle):
     """BASELINE config 2 shape (28 layers, vocab 151936, tied head), short run."""
     m = synth.model(300)
