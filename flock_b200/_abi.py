@@ -113,6 +113,8 @@ SIGNATURES = {
     "flock_model_set_token": [_vp, ctypes.c_int32],
     "flock_model_set_decode_mode": [_vp, _i],
     "flock_model_get_decode_mode": [_vp, _ip],
+    "flock_model_trace": [_vp, _i],
+    "flock_model_trace_read": [_vp, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int64, _ip, _ip],
     "flock_model_current_token": [_vp, _i32p],
     "flock_shard_matvec_create": [_vp, _u8p, _u8p, _i64, _i64, _i, _i, _i64, _pp],
     "flock_shard_matvec_free": [_vp],

@@ -3,7 +3,7 @@
     python -m flock_b200.cases layer [--time]   # one decode layer (config 0 shape, 256-key cache)
     python -m flock_b200.cases head  [--time]   # the 151936 x 1024 Q8_0 head matvec
     python -m flock_b200.cases gemv  [--time]   # the config 1 matvec sweep (M = 1)
-    python -m flock_b200.cases model [--time] [--kernels]
+    python -m flock_b200.cases model [--time] [--kernels] [--trace]
                                                 # 28-layer 0.6B-shape decode, persistent
                                                 # kernel (default) or per-op kernel graph
 
@@ -63,6 +63,39 @@ def gemv_case(timed: bool) -> None:
                       f"{b / ms / 1e6:.1f} GB/s")
 
 
+PHASES = ("qkv", "attention", "o_proj", "gate/up", "down")
+
+
+def trace_summary(tr, n_layers: int) -> str:
+    """Per phase of the persistent kernel, averaged over layers: compute time
+    (mean and slowest CTA) and time spent in the grid barrier after it."""
+    import numpy as np
+    t = (tr[:, :4 + 10 * n_layers].astype(np.int64) - int(tr[:, 0].min())) / 1000.0
+    lines = [f"token: {t[:, 3 + 10 * n_layers].max():.1f} us; start skew {t[:, 0].max():.2f} us; "
+             f"embed {np.mean(t[:, 1] - t[:, 0]):.2f} us"]
+    for p, name in enumerate(PHASES):
+        comp, slow, wait = [], [], []
+        for l in range(n_layers):
+            c = 2 + 10 * l + 2 * p
+            d = t[:, c] - t[:, c - 1]
+            comp.append(d.mean())
+            slow.append(d.max())
+            wait.append((t[:, c + 1] - t[:, c]).mean())
+        lines.append(f"{name:>9}: compute {np.mean(comp):6.2f} us (slowest CTA {np.mean(slow):6.2f}), "
+                     f"barrier {np.mean(wait):5.2f} us; x{n_layers} = "
+                     f"{(np.mean(comp) + np.mean(wait)) * n_layers:7.1f} us")
+    h = 2 + 10 * n_layers
+    lines.append(f"     head: compute {np.mean(t[:, h] - t[:, h - 1]):6.2f} us "
+                 f"(slowest {np.max(t[:, h] - t[:, h - 1]):.2f}), argmax "
+                 f"{np.max(t[:, h + 1] - t[:, h]):.2f} us")
+    w = tr[:, 4 + 10 * n_layers:].astype(np.float64) / 1000.0
+    lines.append("weight waits (warp 0, per token): " + ", ".join(
+        f"{n} {w[:, i].mean():.1f} us" for i, n in enumerate(("qkv", "o_proj", "gate/up", "down",
+                                                                "head"))) +
+        f"; producer waited for free stages {w[:, 5].mean():.1f} us")
+    return "\n".join(lines)
+
+
 def model_case(timed: bool) -> None:
     from .model import Model
     dev = flib.get_device(0)
@@ -78,6 +111,11 @@ def model_case(timed: bool) -> None:
         ms = dev.timer_stop()
         print(f"model decode ({M.decode_mode}): {ms / 64 * 1000:.1f} us/token, "
               f"{64 / ms * 1000:.1f} tok/s")
+    if "--trace" in sys.argv:
+        M.trace(True)
+        M.decode_device(4)
+        print(trace_summary(M.read_trace(), M.held))
+        M.trace(False)
 
 
 if __name__ == "__main__":

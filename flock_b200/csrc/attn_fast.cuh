@@ -9,8 +9,15 @@
 //    row is read from HBM once per token, not once per query head;
 //  * per split: scores by warp-parallel dot products, local max m_s, local
 //    sum l_s and unnormalised output o_s (online-softmax partials);
-//  * the last CTA of a group to finish (arrival counter) combines the splits:
-//    out = sum_s o_s e^(m_s-M) / sum_s l_s e^(m_s-M).
+//  * the splits are combined, one warp per query head:
+//    out = sum_s o_s e^(m_s-M) / sum_s l_s e^(m_s-M), by the last CTA of a
+//    group to finish (arrival counter) -- or, inside the persistent decode
+//    kernel, by every CTA of the next phase after a grid barrier;
+//  * a step over n keys uses ceil(n / 16) splits, at most
+//    attn_max_splits(SMs, kv heads): short contexts keep few partials;
+//  * scores: one thread per (key, query head), a 128-long dot product over
+//    a K tile whose rows are padded to 132 floats (conflict-free 128-bit
+//    reads).
 //
 // There is no key cap (the WGSL decode kernel stops at maxKeys = 2048).  The
 // reassociation changes rounding, so parity with attnRef is a tolerance
@@ -43,54 +50,121 @@ struct AttnFastArgs {
   float eps;
   int neox;
   int chunk_cap;   // max keys per split (informational; tiles of 64 are staged)
+  int combine;     // 1: the last split of a group combines into out; 0: leave partials
   PrefetchList pf;
 };
-
-// Exact RMSNorm (WG = 128) + RoPE of one 128-vector by one 128-thread half
-// of the block; `red` is that half's reduction scratch.  Mirrors
-// k_qk_norm_rope_append.  All threads of the block must call it together.
-template <typename Sync>
-FLOCK_DEV void norm_rope_half(const float* src, const float* gain, float eps, int pos,
-                              const float* inv_freq, int neox, float* dst, float* red,
-                              float* tmp, bool active, Sync sync) {
-  const int t = threadIdx.x & 127;
-  const float x = active ? src[t] : 0.0f;
-  red[t] = ffma(x, x, 0.0f);
-  sync();
-  if (t < 64) red[t] = fadd(red[t], red[t + 64]);
-  sync();
-  if (t < 32) {
-    float w = fadd(red[t], red[t + 32]);
-    w = warp_tree_sum(w);
-    if (t == 0) red[128] = w;
-  }
-  sync();
-  const float scale = rsqrt_f64r(fadd(fdiv(red[128], 128.0f), eps));
-  if (active) tmp[t] = fmul(fmul(x, scale), gain[t]);
-  sync();
-  if (active && t < 64) {
-    const float theta = fmul((float)pos, inv_freq[t]);
-    const float c = __double2float_rn(cos((double)theta));
-    const float s = __double2float_rn(sin((double)theta));
-    const int ia = neox ? t : 2 * t, ib = neox ? t + 64 : 2 * t + 1;
-    const float av = tmp[ia], bv = tmp[ib];
-    dst[ia] = ffma(-bv, s, fmul(av, c));
-    dst[ib] = ffma(bv, c, fmul(av, s));
-  }
-  sync();
-}
 
 constexpr int ATTN_FAST_THREADS = 256;
 constexpr int ATTN_TILE = 64;  // keys staged in shared memory per pass
 
+// Most splits a decode step may use: one wave of CTAs over the kv heads, and
+// at most 32 so a warp holds one split per lane when combining.
+__host__ __device__ inline int attn_max_splits(int sm_count, int n_kv_heads) {
+  int s = n_kv_heads > 0 ? sm_count / n_kv_heads : 1;
+  return s < 1 ? 1 : (s > 32 ? 32 : s);
+}
+
+// Splits a step over n_keys keys uses: one per ATTN_SPLIT_KEYS keys, at most
+// max_splits.  Both decode engines use this rule, so their partials and
+// results are identical.
+constexpr int ATTN_SPLIT_KEYS = 16;
+FLOCK_DEV int attn_splits_for(int n_keys, int max_splits) {
+  const int s = (n_keys + ATTN_SPLIT_KEYS - 1) / ATTN_SPLIT_KEYS;
+  return s < 1 ? 1 : (s > max_splits ? max_splits : s);
+}
+
+// One query head's output from its split partials ([splits][hd + 2]:
+// unnormalised o, running max m, sum l) by one warp; lane s holds split s's
+// (m, l).  out = sum_s o_s w_s / sum_s l_s w_s with w_s = e^(m_s - M), both
+// sums in split order.  store(i, value) receives element i.
+template <typename Store>
+FLOCK_DEV void attn_combine_warp(const float* pp, int splits, int hd, int lane, Store store) {
+  const float m = lane < splits ? __ldcg(pp + lane * (hd + 2) + hd) : -INFINITY;
+  const float l = lane < splits ? __ldcg(pp + lane * (hd + 2) + hd + 1) : 0.0f;
+  float M = m;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float w = lane < splits ? expf(m - M) : 0.0f;
+  float L = 0.0f;
+  for (int sp = 0; sp < splits; sp++)
+    L = fmaf(__shfl_sync(0xffffffffu, l, sp), __shfl_sync(0xffffffffu, w, sp), L);
+  constexpr int B = 8;  // splits whose loads are in flight together
+  for (int i0 = 0; i0 < hd; i0 += 128) {
+    float O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int sp0 = 0; sp0 < splits; sp0 += B) {
+      float ov[B][4];
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const float* o = pp + (sp0 + u) * (hd + 2) + i0 + lane;
+#pragma unroll
+        for (int e = 0; e < 4; e++) ov[u][e] = sp0 + u < splits ? __ldcg(o + 32 * e) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const float ws = __shfl_sync(0xffffffffu, w, (sp0 + u) & 31);
+        if (sp0 + u < splits) {
+#pragma unroll
+          for (int e = 0; e < 4; e++) O[e] = fmaf(ov[u][e], ws, O[e]);
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; e++) store(i0 + lane + 32 * e, O[e] / L);
+  }
+}
+
+// Exact RMSNorm (WG = 128) + RoPE of one 128-vector by one warp, with no
+// block synchronisation: lane l holds elements l, l+32, l+64, l+96 -- the
+// grouping the WG = 128 tree folds (partials t and t+64, t+32 and t+96, then
+// the shuffle tree) -- so NEOX pairs (i, i+64) are lane-local and NORM pairs
+// (2i, 2i+1) are neighbouring lanes.  k_qk_norm_rope_append's arithmetic.
+FLOCK_DEV void norm_rope_warp(const float* src, const float* gain, float eps, int pos,
+                              const float* inv_freq, int neox, float* dst, int lane) {
+  float x[4], y[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++) x[q] = src[lane + 32 * q];
+  float v = fadd(fadd(ffma(x[0], x[0], 0.0f), ffma(x[2], x[2], 0.0f)),
+                 fadd(ffma(x[1], x[1], 0.0f), ffma(x[3], x[3], 0.0f)));
+  v = warp_tree_sum(v);
+  v = __shfl_sync(0xffffffffu, v, 0);
+  const float scale = rsqrt_f64r(fadd(fdiv(v, 128.0f), eps));
+#pragma unroll
+  for (int q = 0; q < 4; q++) y[q] = fmul(fmul(x[q], scale), gain[lane + 32 * q]);
+  if (neox) {
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const int i = lane + 32 * q;
+      const float theta = fmul((float)pos, inv_freq[i]);
+      const float c = __double2float_rn(cos((double)theta));
+      const float s = __double2float_rn(sin((double)theta));
+      const float av = y[q], bv = y[q + 2];
+      dst[i] = ffma(-bv, s, fmul(av, c));
+      dst[i + 64] = ffma(bv, c, fmul(av, s));
+    }
+  } else {
+    const bool odd = lane & 1;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int e = lane + 32 * q;
+      const float other = __shfl_xor_sync(0xffffffffu, y[q], 1);
+      const float av = odd ? other : y[q], bv = odd ? y[q] : other;
+      const float theta = fmul((float)pos, inv_freq[e >> 1]);
+      const float c = __double2float_rn(cos((double)theta));
+      const float s = __double2float_rn(sin((double)theta));
+      dst[e] = odd ? ffma(bv, c, fmul(av, s)) : ffma(-bv, s, fmul(av, c));
+    }
+  }
+}
+
 // Shared-memory layout (floats): raw q [4][128], raw k/v [2][128], gains
 // [2][128], inv_freq [64], normalised q [4][128], new k/v [2][128], norm
 // scratch tmp [2][128] + red [2][132], scores/probabilities [4][TILE],
-// running softmax state [4][4], K and V tiles [2][TILE][128].
+// running softmax state [4][4], K tile [TILE][AF_KSTRIDE], V tile [TILE][128].
+constexpr int AF_KSTRIDE = 132;
 constexpr int AF_QRAW = 0, AF_KRAW = 512, AF_VRAW = 640, AF_GQ = 768, AF_GK = 896,
-              AF_INV = 1024, AF_QV = 1088, AF_KNEW = 1600, AF_VNEW = 1728, AF_TMP = 1856,
-              AF_RED = 2112, AF_SC = 2376, AF_ML = AF_SC + 4 * ATTN_TILE, AF_KT = AF_ML + 16,
-              AF_VT = AF_KT + ATTN_TILE * 128, AF_END = AF_VT + ATTN_TILE * 128;
+              AF_INV = 1024, AF_QV = 1088, AF_KNEW = 1600, AF_VNEW = 1728,
+              AF_SC = 1856, AF_ML = AF_SC + 4 * ATTN_TILE, AF_KT = AF_ML + 16,
+              AF_VT = AF_KT + ATTN_TILE * AF_KSTRIDE, AF_END = AF_VT + ATTN_TILE * 128;
 
 // One (kv head g, split s) work item, run by ATTN_FAST_THREADS threads that
 // synchronise with `sync()`; `dsm` holds AF_END floats; `last` is a shared
@@ -100,12 +174,14 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
                               bool* last_flag, Sync sync) {
   const int G = a.n_heads / a.n_kv_heads;  // <= 4
   const int t = threadIdx.x;
-  const int half = t >> 7, lane = t & 31, warp = t >> 5;
+  const int lane = t & 31, warp = t >> 5;
   const int hd = 128;
   const size_t kvs = (size_t)a.n_kv_heads * hd;
 
   const int n_keys = pos + 1;
-  const int chunk = (n_keys + a.splits - 1) / a.splits;
+  const int splits = attn_splits_for(n_keys, a.splits);
+  if (s >= splits) return;  // uniform over the CTA, before any synchronisation
+  const int chunk = (n_keys + splits - 1) / splits;
   const int k0 = s * chunk;
   const int k1 = min(n_keys, k0 + chunk);
   const int nk = max(0, k1 - k0);
@@ -119,20 +195,20 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
       if (key == pos) continue;
       const float4* kr = reinterpret_cast<const float4*>(a.kcache + key * kvs + (size_t)g * hd);
       const float4* vr = reinterpret_cast<const float4*>(a.vcache + key * kvs + (size_t)g * hd);
-      reinterpret_cast<float4*>(dsm + AF_KT)[i] = kr[c4];
+      reinterpret_cast<float4*>(dsm + AF_KT)[j * (AF_KSTRIDE / 4) + c4] = kr[c4];
       reinterpret_cast<float4*>(dsm + AF_VT)[i] = vr[c4];
     }
   };
   {
     const float* qsrc = a.q + (size_t)g * G * hd;
     for (int i = t; i < G * 32; i += ATTN_FAST_THREADS)
-      reinterpret_cast<float4*>(dsm + AF_QRAW)[i] = reinterpret_cast<const float4*>(qsrc)[i];
+      reinterpret_cast<float4*>(dsm + AF_QRAW)[i] = __ldcg(reinterpret_cast<const float4*>(qsrc) + i);
     if (t < 32) {
       if (fused) {
         reinterpret_cast<float4*>(dsm + AF_KRAW)[t] =
-            reinterpret_cast<const float4*>(a.k + (size_t)g * hd)[t];
+            __ldcg(reinterpret_cast<const float4*>(a.k + (size_t)g * hd) + t);
         reinterpret_cast<float4*>(dsm + AF_VRAW)[t] =
-            reinterpret_cast<const float4*>(a.v + (size_t)g * hd)[t];
+            __ldcg(reinterpret_cast<const float4*>(a.v + (size_t)g * hd) + t);
         reinterpret_cast<float4*>(dsm + AF_GQ)[t] = reinterpret_cast<const float4*>(a.q_norm)[t];
         reinterpret_cast<float4*>(dsm + AF_GK)[t] = reinterpret_cast<const float4*>(a.k_norm)[t];
         if (t < 16)
@@ -153,18 +229,15 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   float* knew = dsm + AF_KNEW;
   float* vnew = dsm + AF_VNEW;
   if (fused) {
-    // exact per-head RMSNorm + RoPE of the G query heads and the new key,
-    // two 128-wide vectors per pass (k_qk_norm_rope_append's arithmetic)
-    for (int base = 0; base < G + 1; base += 2) {
-      const int vi = base + half;
-      const bool active = vi <= G;
-      const bool is_k = vi == G;
-      const float* src = is_k ? dsm + AF_KRAW : dsm + AF_QRAW + (active ? vi : 0) * 128;
-      float* dst = is_k ? knew : qv + (active ? vi : 0) * 128;
-      norm_rope_half(src, is_k ? dsm + AF_GK : dsm + AF_GQ, a.eps, pos, dsm + AF_INV, a.neox,
-                     dst, dsm + AF_RED + half * 132, dsm + AF_TMP + half * 128, active, sync);
-    }
-    if (t < 128) vnew[t] = dsm[AF_VRAW + t];
+    // exact per-head RMSNorm + RoPE (k_qk_norm_rope_append's arithmetic):
+    // warps 0..G-1 the query heads, warp G the new key, warp G+1 copies v
+    if (warp < G)
+      norm_rope_warp(dsm + AF_QRAW + warp * 128, dsm + AF_GQ, a.eps, pos, dsm + AF_INV, a.neox,
+                     qv + warp * 128, lane);
+    else if (warp == G)
+      norm_rope_warp(dsm + AF_KRAW, dsm + AF_GK, a.eps, pos, dsm + AF_INV, a.neox, knew, lane);
+    else if (warp == G + 1)
+      for (int i = lane; i < 128; i += 32) vnew[i] = dsm[AF_VRAW + i];
     sync();
     if (s == 0 && t < 128) {
       a.kcache[(size_t)pos * kvs + (size_t)g * hd + t] = knew[t];
@@ -194,20 +267,26 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
     }
     // the new key/value live in shared memory, not (yet) in the cache
     if (pos >= t0 && pos < t0 + nt && t < 128) {
-      kt[(pos - t0) * 128 + t] = knew[t];
+      kt[(pos - t0) * AF_KSTRIDE + t] = knew[t];
       vt[(pos - t0) * 128 + t] = vnew[t];
     }
     sync();
-    // scores: one warp per key, all G heads per K row
-    for (int j = warp; j < nt; j += ATTN_FAST_THREADS / 32) {
-      const float4 kv = reinterpret_cast<const float4*>(kt + j * 128)[lane];
-      for (int hq = 0; hq < G; hq++) {
-        const float4 qq = reinterpret_cast<const float4*>(qv + hq * 128)[lane];
-        float p = fmaf(qq.x, kv.x, fmaf(qq.y, kv.y, fmaf(qq.z, kv.z, qq.w * kv.w)));
-#pragma unroll
-        for (int o2 = 16; o2 > 0; o2 >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o2);
-        if (lane == 0) sc[hq * ATTN_TILE + j] = p * scale;
+    // scores: one thread per (query head, key), four partial sums over the
+    // components of the 128-bit reads
+    for (int idx = t; idx < G * nt; idx += ATTN_FAST_THREADS) {
+      const int hq = idx / nt, j = idx - hq * nt;
+      const float4* kr = reinterpret_cast<const float4*>(kt + j * AF_KSTRIDE);
+      const float4* qr = reinterpret_cast<const float4*>(qv + hq * 128);
+      float p0 = 0.0f, p1 = 0.0f, p2 = 0.0f, p3 = 0.0f;
+#pragma unroll 8
+      for (int c4 = 0; c4 < 32; c4++) {
+        const float4 kk = kr[c4], qq = qr[c4];
+        p0 = fmaf(qq.x, kk.x, p0);
+        p1 = fmaf(qq.y, kk.y, p1);
+        p2 = fmaf(qq.z, kk.z, p2);
+        p3 = fmaf(qq.w, kk.w, p3);
       }
+      sc[hq * ATTN_TILE + j] = ((p0 + p1) + (p2 + p3)) * scale;
     }
     sync();
     // online softmax per head (warp hq): new max, correction, probabilities
@@ -255,7 +334,7 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
     const int oi = t + u * ATTN_FAST_THREADS;
     if (oi < G * hd) {
       const int hq = oi / hd, i = oi % hd;
-      float* pp = a.part + ((size_t)(g * G + hq) * a.splits + s) * (hd + 2);
+      float* pp = a.part + ((size_t)(g * G + hq) * a.splits + s) * (hd + 2);  // stride: max splits
       pp[i] = o[u];
       if (i == 0) {
         pp[hd] = ml[4 * hq];
@@ -263,24 +342,18 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
       }
     }
   }
+  if (!a.combine) return;  // combined by the caller after a grid-wide barrier
   __threadfence();
   sync();
-  if (t == 0) *last_flag = atomicAdd(a.count + g, 1u) == (uint32_t)(a.splits - 1);
+  if (t == 0) *last_flag = atomicAdd(a.count + g, 1u) == (uint32_t)(splits - 1);
   sync();
   if (!*last_flag) return;
   __threadfence();
-  for (int oi = t; oi < G * hd; oi += ATTN_FAST_THREADS) {
-    const int hq = oi / hd, i = oi % hd;
-    const volatile float* pp = a.part + (size_t)(g * G + hq) * a.splits * (hd + 2);
-    float M = -INFINITY;
-    for (int sp = 0; sp < a.splits; sp++) M = fmaxf(M, pp[sp * (hd + 2) + hd]);
-    float L = 0.0f, O = 0.0f;
-    for (int sp = 0; sp < a.splits; sp++) {
-      const float w = expf(pp[sp * (hd + 2) + hd] - M);
-      L = fmaf(pp[sp * (hd + 2) + hd + 1], w, L);
-      O = fmaf(pp[sp * (hd + 2) + i], w, O);
-    }
-    a.out[(size_t)(g * G + hq) * hd + i] = O / L;
+  if (warp < G) {
+    const int h = g * G + warp;
+    float* out = a.out + (size_t)h * hd;
+    attn_combine_warp(a.part + (size_t)h * a.splits * (hd + 2), splits, hd, lane,
+                      [&](int i, float v) { out[i] = v; });
   }
   if (t == 0) a.count[g] = 0;
 }

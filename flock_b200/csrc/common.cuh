@@ -68,6 +68,35 @@ FLOCK_DEV float dot4(float q0, float q1, float q2, float q3, float x0, float x1,
   return s;
 }
 
+// ------------------------------------------------- packed f32 pairs (sm_100a)
+// f32x2 arithmetic rounds each half exactly as the scalar instruction does,
+// so two independent chains can share one instruction stream.
+FLOCK_DEV uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+FLOCK_DEV float2 unpack2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+FLOCK_DEV uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+FLOCK_DEV uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+FLOCK_DEV uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 // ------------------------------------------------------------ memory helpers
 FLOCK_DEV uint4 ldg_stream(const void* p) {
   uint4 r;

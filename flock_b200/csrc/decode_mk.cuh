@@ -78,7 +78,16 @@ struct MkArgs {
   int* err;        // set non-zero on a timed-out wait
   int stage_bytes; // bytes per ring stage
   int n_stages;
+  // optional phase trace: per CTA, mk_trace_stride(n_layers) entries of
+  // global-timer nanoseconds -- stamps (start, embedded, then per layer and
+  // phase: computed, released; head computed, done), then the time warp 0
+  // waited for weights in the QKV, o_proj, gate/up, down and head phases
+  // (summed over layers) and the time the producer waited for a free stage;
+  // nullptr when off
+  unsigned long long* trace;
 };
+
+__host__ __device__ inline int mk_trace_stride(int n_layers) { return 10 + 10 * n_layers; }
 
 constexpr int MK_CONSUMERS = 8;                   // consumer warps
 constexpr int MK_THREADS = (MK_CONSUMERS + 1) * 32;
@@ -115,12 +124,28 @@ FLOCK_DEV uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// try_wait that lets the hardware suspend the thread for up to `hint_ns`
+// while the phase is incomplete (it resumes as soon as the phase completes),
+// so a waiting warp stops taking issue slots from the warps that compute.
+FLOCK_DEV bool mbar_try_wait_sleep(uint64_t* b, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: false after MK_WAIT_NS of global time (or MK_MAX_POLLS polls),
-// or as soon as *err is set when `watch_err`.
+// or as soon as *err is set when `watch_err`.  Each poll may sleep up to
+// MK_SLEEP_NS.
+constexpr uint32_t MK_SLEEP_NS = 20000;
 FLOCK_DEV bool mbar_wait(uint64_t* b, uint32_t parity, const int* err, bool watch_err = true) {
   uint64_t t0 = 0;
   for (uint32_t i = 0; i < MK_MAX_POLLS; i++) {
-    if (mbar_try_wait(b, parity)) return true;
+    if (mbar_try_wait_sleep(b, parity, MK_SLEEP_NS)) return true;
     if ((i & 63) == 63) {
       if (watch_err && *(volatile const int*)err) return false;
       const uint64_t now = globaltimer_ns();
@@ -306,133 +331,263 @@ struct ConsumerSync {
   FLOCK_DEV void operator()() const { consumers_sync(); }
 };
 
-// x for the next phase into the padded shared layout, RMSNorm fused when
-// `gain` is given: the same one-round-trip staging and exact ops_ref.ts:20
-// order as rmsnorm_to_smem, synchronised over the consumer warps only.
-// `src` may point to global or shared memory.
-FLOCK_DEV void mk_stage_x(const float* src, int K, const float* gain, float eps, float* xs,
-                          float* gs, float* red) {
-  const int t = threadIdx.x;
-  for (int i = t; i < K / 4; i += MK_CONSUMERS * 32) {
-    const float4 v = reinterpret_cast<const float4*>(src)[i];
-    reinterpret_cast<float4*>(xs)[(i >> 3) * (XPAD / 4) + (i & 7)] = v;
-    if (gain) reinterpret_cast<float4*>(gs)[i] = reinterpret_cast<const float4*>(gain)[i];
-  }
-  consumers_sync();
-  if (!gain) return;
-  if (t < 128) {
-    float acc = 0.0f;
-    for (int i = t; i < K; i += 128) {
-      const float v = xs[xpad(i)];
-      acc = ffma(v, v, acc);
-    }
-    red[t] = acc;
-  }
-  consumers_sync();
-  if (t < 64) red[t] = fadd(red[t], red[t + 64]);
-  consumers_sync();
-  if (t < 32) {
-    float v = fadd(red[t], red[t + 32]);
-    v = warp_tree_sum(v);
-    if (t == 0) red[128] = rsqrt_f64r(fadd(fdiv(v, (float)K), eps));
-  }
-  consumers_sync();
-  const float scale = red[128];
-  for (int i = t; i < K; i += MK_CONSUMERS * 32)
-    xs[xpad(i)] = fmul(fmul(xs[xpad(i)], scale), gs[i]);
-  consumers_sync();
+// x in shared memory: 32-float blocks padded to XPAD floats (lane l reading
+// block l touches distinct banks), and inside each 8-float group the pairs
+// (x_k, x_k+4) adjacent, so one 128-bit read yields two f32x2 operands for
+// fold_q8_packed.  The norm gains are staged in the same layout.
+FLOCK_DEV int xperm(int i) {
+  const int j = i & 31;
+  return (i >> 5) * XPAD + (j & ~7) + 2 * (j & 3) + ((j >> 2) & 1);
 }
 
-// One row held in shared memory against the staged x: the reference's
-// coop(64) order (lane plays logical lanes lane and lane+32), block 0 of x
-// from registers, the rest from the padded shared copy.  Lane 0 gets y.
-FLOCK_DEV float mk_row_dot(const uint8_t* rq, const uint16_t* rs, int nb, const float4 (&xr0)[8],
-                           const float4* xs4, int lane) {
-  float accA = 0.0f, accB = 0.0f;
+// One Q8_0 block against x in packed pairs: xp[4g + k] = (x[8g+k], x[8g+4+k]).
+// The two dot4 chains of a group (weights 8g..8g+3 and 8g+4..8g+7) run as
+// the halves of one f32x2 chain: the same rounded product and three FMAs
+// each (lib.ts:196), then acc = fma(scale, d0 + d1, acc) as fold_block.
+FLOCK_DEV float fold_q8_packed(const BlockW<QT_Q8>& bw, const uint64_t (&xp)[16], float acc) {
+  const float s = scale_f16(bw.s);
+  const uint32_t w[8] = {bw.w0.x, bw.w0.y, bw.w0.z, bw.w0.w, bw.w1.x, bw.w1.y, bw.w1.z, bw.w1.w};
+  const uint64_t k2 = pack2(8388736.0f, 8388736.0f);  // 2^23 + 128
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    const uint32_t ua = w[2 * g] ^ 0x80808080u, uc = w[2 * g + 1] ^ 0x80808080u;
+    uint64_t q[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+      q[k] = fsub2(pack2(__uint_as_float(__byte_perm(ua, 0x4B000000u, 0x7540u + k)),
+                         __uint_as_float(__byte_perm(uc, 0x4B000000u, 0x7540u + k))),
+                   k2);
+    uint64_t d = fmul2(q[0], xp[4 * g]);
+    d = ffma2(q[1], xp[4 * g + 1], d);
+    d = ffma2(q[2], xp[4 * g + 2], d);
+    d = ffma2(q[3], xp[4 * g + 3], d);
+    const float2 dd = unpack2(d);
+    acc = ffma(s, fadd(dd.x, dd.y), acc);
+  }
+  return acc;
+}
+
+FLOCK_DEV void load_pairs(const float* xs, int b, uint64_t (&xp)[16]) {
+  const ulonglong2* q = reinterpret_cast<const ulonglong2*>(xs + b * XPAD);
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const ulonglong2 v = q[j];
+    xp[2 * j] = v.x;
+    xp[2 * j + 1] = v.y;
+  }
+}
+
+// x for a GEMV phase: one round trip of 128-bit loads into the packed shared
+// layout, then each lane's block 0 of x into registers (xp).  With `gain`,
+// RMSNorm is fused in the exact ops_ref.ts:20 order (WG = 128: partial t
+// folds elements t, t+128, ...; partials t and t+64, then t+32, then the
+// shuffle tree): every warp computes the scale itself from shared memory, so
+// one consumer barrier suffices when a row's x fits lane-resident blocks
+// (K <= 1024); larger K also rescales the shared copy.  `src` is global
+// memory written before the last grid barrier, or shared memory.
+FLOCK_DEV void mk_stage(const float* src, bool src_shared, int K, const float* gain, float eps,
+                        float* xs, float* gs, uint64_t (&xp)[16]) {
+  const int t = threadIdx.x, lane = t & 31;
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  const float4* g4 = reinterpret_cast<const float4*>(gain);
+  for (int i = t; i < K / 8; i += MK_CONSUMERS * 32) {
+    const float4 a = src_shared ? s4[2 * i] : __ldcg(s4 + 2 * i);
+    const float4 b = src_shared ? s4[2 * i + 1] : __ldcg(s4 + 2 * i + 1);
+    float4* d = reinterpret_cast<float4*>(xs + (i >> 2) * XPAD + (i & 3) * 8);
+    d[0] = make_float4(a.x, b.x, a.y, b.y);
+    d[1] = make_float4(a.z, b.z, a.w, b.w);
+    if (gain) {
+      const float4 ga = __ldg(g4 + 2 * i), gb = __ldg(g4 + 2 * i + 1);
+      float4* e = reinterpret_cast<float4*>(gs + (i >> 2) * XPAD + (i & 3) * 8);
+      e[0] = make_float4(ga.x, gb.x, ga.y, gb.y);
+      e[1] = make_float4(ga.z, gb.z, ga.w, gb.w);
+    }
+  }
+  consumers_sync();
+  const int nb = K / 32;
+  if (!gain) {
+    if (lane < nb) load_pairs(xs, lane, xp);
+    return;
+  }
+  float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int q = 0; q < 4; q++)
+    for (int i = lane + 32 * q; i < K; i += 128) {
+      const float v = xs[xperm(i)];
+      p[q] = ffma(v, v, p[q]);
+    }
+  float v = fadd(fadd(p[0], p[2]), fadd(p[1], p[3]));
+  v = warp_tree_sum(v);
+  v = __shfl_sync(0xffffffffu, v, 0);
+  const float scale = rsqrt_f64r(fadd(fdiv(v, (float)K), eps));
+  if (nb <= 32) {
+    if (lane < nb) {
+      const float4* x4 = reinterpret_cast<const float4*>(xs + lane * XPAD);
+      const float4* w4 = reinterpret_cast<const float4*>(gs + lane * XPAD);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float4 x = x4[j], g = w4[j];
+        xp[2 * j] = pack2(fmul(fmul(x.x, scale), g.x), fmul(fmul(x.y, scale), g.y));
+        xp[2 * j + 1] = pack2(fmul(fmul(x.z, scale), g.z), fmul(fmul(x.w, scale), g.w));
+      }
+    }
+    return;
+  }
+  consumers_sync();  // every warp has read the unscaled copy
+  for (int i = t; i < K; i += MK_CONSUMERS * 32) {
+    const int o = xperm(i);
+    xs[o] = fmul(fmul(xs[o], scale), gs[o]);
+  }
+  consumers_sync();
+  load_pairs(xs, lane, xp);
+}
+
+// x for o_proj: the attention output, combined here from the split partials
+// the attention phase left (attn_combine_warp, one warp per query head --
+// the same arithmetic as the kernel graph's last-split combine).
+FLOCK_DEV void mk_stage_attn(const MkArgs& a, int pos, float* xs, uint64_t (&xp)[16]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int splits = attn_splits_for(pos + 1, a.splits);
+  for (int h = warp; h < a.nH; h += MK_CONSUMERS)
+    attn_combine_warp(a.attn_part + (size_t)h * a.splits * (a.hd + 2), splits, a.hd, lane,
+                      [&](int i, float v) { xs[xperm(h * a.hd + i)] = v; });
+  consumers_sync();
+  if (lane < a.nH * a.hd / 32) load_pairs(xs, lane, xp);
+}
+
+// R rows held in shared memory against the staged x, interleaved so their
+// dependency chains overlap: the reference's coop(64) order per row (lane
+// plays logical lanes lane and lane+32; block 0 of x from registers, the rest
+// from the packed shared copy), then the 64-lane tree.  Lane 0 gets y[r].
+template <int R>
+FLOCK_DEV void mk_rows_dot(const uint8_t* const* rq, const uint16_t* const* rs, int nb,
+                           const uint64_t (&xp)[16], const float* xs, int lane, float* y) {
+  float accA[R], accB[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) accA[r] = accB[r] = 0.0f;
   const int M = (nb + 31) / 32;
   for (int m = 0; m < M; m++) {
     const int b = lane + 32 * m;
     if (b >= nb) break;
-    BlockW<QT_Q8> bw;
-    load_block_smem(bw, rq, rs, b);
-    if (m == 0)
-      accA = fold_block<QT_Q8>(bw, xr0, accA);
-    else if (m & 1)
-      accB = fold_block<QT_Q8>(bw, xs4 + b * (XPAD / 4), accB);
-    else
-      accA = fold_block<QT_Q8>(bw, xs4 + b * (XPAD / 4), accA);
+    BlockW<QT_Q8> bw[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) load_block_smem(bw[r], rq[r], rs[r], b);
+    if (m == 0) {
+#pragma unroll
+      for (int r = 0; r < R; r++) accA[r] = fold_q8_packed(bw[r], xp, accA[r]);
+    } else {
+      uint64_t xb[16];
+      load_pairs(xs, b, xb);
+      if (m & 1) {
+#pragma unroll
+        for (int r = 0; r < R; r++) accB[r] = fold_q8_packed(bw[r], xb, accB[r]);
+      } else {
+#pragma unroll
+        for (int r = 0; r < R; r++) accA[r] = fold_q8_packed(bw[r], xb, accA[r]);
+      }
+    }
   }
-  return warp_tree_sum(fadd(accA, accB));
+#pragma unroll
+  for (int r = 0; r < R; r++) y[r] = fadd(accA[r], accB[r]);
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) {
+#pragma unroll
+    for (int r = 0; r < R; r++) y[r] = fadd(y[r], __shfl_down_sync(0xffffffffu, y[r], s));
+  }
 }
 
 struct MkShared {
   float* xs;      // padded x
   float* gs;      // gain staging
-  float* red;     // [136]
   float* raw;     // [H] embedded row (layer 0)
   float* wv;      // [MK_CONSUMERS] argmax values
   uint32_t* wi;   // [MK_CONSUMERS] argmax indices
   float* att;     // AF_END floats for the attention phase (aliases the above)
 };
 
-// A GEMV phase over this CTA's chunks.  Returns false if a wait gave up.
-template <int P>
-FLOCK_DEV void mk_gemv_phase(const MkArgs& a, int layer, uint8_t* ring, uint64_t* full,
-                             uint64_t* empty, int& cidx, const MkShared& sm, float& best_v,
-                             uint32_t& best_i) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float4* xs4 = reinterpret_cast<const float4*>(sm.xs);
-  float4 xr0[8];
-  {
-    const PhaseGeo g = phase_geo(a, P);
-    const int nb = g.K / 32;
+// A warp's group of units (rows; gate/up: row pairs) within a chunk.  The
+// group grows with the chunk (1, 2 or 4 units) so small chunks still spread
+// over all consumer warps and large ones overlap several rows' chains.
+template <int P, int U>
+FLOCK_DEV void mk_group(const MkArgs& a, const Chunk& c, const uint8_t* q0, const uint8_t* q1,
+                        const uint16_t* s0, const uint16_t* s1, int scs, int u0,
+                        const uint64_t (&xp)[16], const float* xs, int lane, float& best_v,
+                        uint32_t& best_i) {
+  constexpr int R = P == PH_GU ? 2 * U : U;  // row dots
+  const uint8_t* rq[R];
+  const uint16_t* rs[R];
 #pragma unroll
-    for (int j = 0; j < 8; j++)
-      xr0[j] = lane < nb ? xs4[lane * (XPAD / 4) + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r = 0; r < U; r++) {
+    const int u = min(u0 + r, c.rows - 1);  // a short group repeats its last unit
+    rq[r] = q0 + (size_t)u * c.K;
+    rs[r] = s0 + (size_t)u * scs;
+    if (P == PH_GU) {
+      rq[U + r] = q1 + (size_t)u * c.K;
+      rs[U + r] = s1 + (size_t)u * scs;
+    }
   }
-  const MkLayer* L = P == PH_HEAD ? nullptr : a.layers + layer;
+  float y[R];
+  mk_rows_dot<R>(rq, rs, c.K / 32, xp, xs, lane, y);
+  if (lane != 0) return;
+#pragma unroll
+  for (int r = 0; r < U; r++) {
+    if (u0 + r >= c.rows) break;
+    const int row = c.row0 + u0 + r;
+    if (P == PH_GU) {
+      // ops_ref.ts:103 swigluRef: fr(fr(g / fr(1 + fr(exp(-g)))) * up)
+      const float e = exp_f64r(-y[r]);
+      a.act[row] = fmul(fdiv(y[r], fadd(1.0f, e)), y[U + r]);
+    } else if (P == PH_QKV) {
+      float* dst = c.seg == 0 ? a.q : (c.seg == 1 ? a.k : a.v);
+      dst[row] = y[r];
+    } else if (P == PH_O || P == PH_DOWN) {
+      a.h[row] = fadd(__ldcg(a.h + row), y[r]);
+    } else if (P == PH_HEAD) {
+      a.logits[row] = y[r];
+      if (am_better(y[r], (uint32_t)row, best_v, best_i)) {
+        best_v = y[r];
+        best_i = (uint32_t)row;
+      }
+    }
+  }
+}
+
+// A GEMV phase over this CTA's chunks.  A weight wait that gives up sets *err.
+template <int P>
+FLOCK_DEV void mk_gemv_phase(const MkArgs& a, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                             int& cidx, const float* xs, const uint64_t (&xp)[16], float& best_v,
+                             uint32_t& best_i, unsigned long long* wait_acc) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int UMAX = P == PH_GU ? 2 : 4;
+  unsigned long long waited = 0;
   for_each_chunk(a, P, [&](const Chunk& c) {
     const int st = cidx % a.n_stages;
+    const unsigned long long w0 = wait_acc ? globaltimer_ns() : 0;
     if (!mbar_wait(&full[st], (uint32_t)((cidx / a.n_stages) & 1), a.err)) atomicCAS(a.err, 0, 1);
+    if (wait_acc) waited += globaltimer_ns() - w0;
     const uint8_t* stage = ring + (size_t)st * a.stage_bytes;
-    const int nb = c.K / 32;
-    const int scs = (nb + 7) / 8 * 8;
+    const int scs = (c.K / 32 + 7) / 8 * 8;
     const int nsrc = P == PH_GU ? 2 : 1;
     const uint32_t qbytes = (uint32_t)c.rows * c.K;
     const uint8_t* q0 = stage;
     const uint8_t* q1 = stage + qbytes;
     const uint16_t* s0 = reinterpret_cast<const uint16_t*>(stage + nsrc * qbytes);
     const uint16_t* s1 = s0 + (size_t)c.rows * scs;
-    for (int u = warp; u < c.rows; u += MK_CONSUMERS) {
-      const int row = c.row0 + u;
-      const float y = mk_row_dot(q0 + (size_t)u * c.K, s0 + (size_t)u * scs, nb, xr0, xs4, lane);
-      if (P == PH_GU) {
-        const float yu = mk_row_dot(q1 + (size_t)u * c.K, s1 + (size_t)u * scs, nb, xr0, xs4, lane);
-        if (lane == 0) {
-          // ops_ref.ts:103 swigluRef: fr(fr(g / fr(1 + fr(exp(-g)))) * up)
-          const float e = exp_f64r(-y);
-          a.act[row] = fmul(fdiv(y, fadd(1.0f, e)), yu);
-        }
-      } else if (lane == 0) {
-        if (P == PH_QKV) {
-          float* dst = c.seg == 0 ? a.q : (c.seg == 1 ? a.k : a.v);
-          dst[row] = y;
-        } else if (P == PH_O || P == PH_DOWN) {
-          a.h[row] = fadd(a.h[row], y);
-        } else if (P == PH_HEAD) {
-          a.logits[row] = y;
-          if (am_better(y, (uint32_t)row, best_v, best_i)) {
-            best_v = y;
-            best_i = (uint32_t)row;
-          }
-        }
-      }
+    int U = (c.rows + MK_CONSUMERS - 1) / MK_CONSUMERS;
+    U = U > 2 ? UMAX : U;
+    for (int u0 = warp * U; u0 < c.rows; u0 += MK_CONSUMERS * U) {
+      if (U == 1)
+        mk_group<P, 1>(a, c, q0, q1, s0, s1, scs, u0, xp, xs, lane, best_v, best_i);
+      else if (U == 2)
+        mk_group<P, 2>(a, c, q0, q1, s0, s1, scs, u0, xp, xs, lane, best_v, best_i);
+      else
+        mk_group<P, UMAX>(a, c, q0, q1, s0, s1, scs, u0, xp, xs, lane, best_v, best_i);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     cidx++;
   });
-  (void)L;
+  if (wait_acc) *wait_acc += waited;
 }
 
 // The per-token kernel.  grid = one CTA per SM (cooperative), block =
@@ -447,8 +602,7 @@ static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs
   MkShared sm;
   sm.xs = xregion;
   sm.gs = sm.xs + kmax / 32 * XPAD;
-  sm.red = sm.gs + a.H;
-  sm.raw = sm.red + 136;
+  sm.raw = sm.gs + a.H / 32 * XPAD;
   sm.wv = sm.raw + a.H;
   sm.wi = reinterpret_cast<uint32_t*>(sm.wv + MK_CONSUMERS);
   sm.att = xregion;
@@ -466,6 +620,16 @@ static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs
   }
   __syncthreads();
 
+  unsigned long long* tr =
+      a.trace ? a.trace + (size_t)blockIdx.x * mk_trace_stride(a.n_layers) : nullptr;
+  auto stamp = [&](int i) {
+    if (tr && threadIdx.x == 0) tr[i] = globaltimer_ns();
+  };
+  stamp(0);
+  // weight-wait accumulators (thread 0) and the producer's stage wait
+  unsigned long long* wacc = tr && threadIdx.x == 0 ? tr + 4 + 10 * a.n_layers : nullptr;
+  if (wacc)
+    for (int i = 0; i < 5; i++) wacc[i] = 0;
   const int pos = a.ctl[0] + a.ctl[1];  // this token's position
   const int token = a.ids[0];
 
@@ -474,15 +638,18 @@ static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs
     if (lane == 0) {
       int cidx = 0;
       bool stop = false;
+      unsigned long long waited = 0;
       auto produce = [&](int layer, int p) {
         for_each_chunk(a, p, [&](const Chunk& c) {
           if (stop) return;
           const int st = cidx % a.n_stages;
+          const unsigned long long w0 = tr ? globaltimer_ns() : 0;
           if (cidx >= a.n_stages &&
               !mbar_wait(&empty[st], (uint32_t)(((cidx / a.n_stages) - 1) & 1), a.err)) {
             stop = true;
             return;
           }
+          if (tr) waited += globaltimer_ns() - w0;
           if (*(volatile int*)a.err) {
             stop = true;
             return;
@@ -499,6 +666,7 @@ static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs
         produce(l, PH_DOWN);
       }
       if (!stop) produce(0, PH_HEAD);
+      if (tr) tr[9 + 10 * a.n_layers] = waited;
     }
   } else {
     // ------------------------------------------------------------ consumers
@@ -523,6 +691,7 @@ static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs
     consumers_sync();
     if (blockIdx.x == 0)
       for (int i = threadIdx.x; i < a.H; i += MK_CONSUMERS * 32) a.h[i] = sm.raw[i];
+    stamp(1);
 
     AttnFastArgs aa = {};
     aa.q = a.q;
@@ -538,14 +707,19 @@ static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs
     aa.splits = a.splits;
     aa.eps = a.eps;
     aa.neox = a.neox;
+    aa.combine = 0;  // the o_proj staging combines the partials
+    uint64_t xr0[16];
 
     bool ok = true;
     for (int l = 0; l < a.n_layers && ok; l++) {
       const MkLayer& L = a.layers[l];
       // QKV (attn_norm fused)
-      mk_stage_x(l == 0 ? sm.raw : a.h, a.H, L.attn_norm, a.eps, sm.xs, sm.gs, sm.red);
-      mk_gemv_phase<PH_QKV>(a, l, ring, full, empty, cidx, sm, best_v, best_i);
+      mk_stage(l == 0 ? sm.raw : a.h, l == 0, a.H, L.attn_norm, a.eps, sm.xs, sm.gs, xr0);
+      mk_gemv_phase<PH_QKV>(a, ring, full, empty, cidx, sm.xs, xr0, best_v, best_i,
+                              wacc ? wacc + 0 : nullptr);
+      stamp(2 + l * 10 + 0);
       if (!(ok = grid_barrier(a, epoch))) break;
+      stamp(2 + l * 10 + 1);
       // attention (q/k norm + RoPE + KV append fused)
       aa.q_norm = L.q_norm;
       aa.k_norm = L.k_norm;
@@ -554,24 +728,37 @@ static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs
       if ((int)blockIdx.x < a.nKV * a.splits)
         attn_fast_item(aa, blockIdx.x / a.splits, blockIdx.x % a.splits, pos, sm.att, &att_last,
                        ConsumerSync{});
+      stamp(2 + l * 10 + 2);
       if (!(ok = grid_barrier(a, epoch))) break;
+      stamp(2 + l * 10 + 3);
       // o_proj + residual
-      mk_stage_x(a.attn, a.nH * a.hd, nullptr, a.eps, sm.xs, sm.gs, sm.red);
-      mk_gemv_phase<PH_O>(a, l, ring, full, empty, cidx, sm, best_v, best_i);
+      mk_stage_attn(a, pos, sm.xs, xr0);
+      mk_gemv_phase<PH_O>(a, ring, full, empty, cidx, sm.xs, xr0, best_v, best_i,
+                              wacc ? wacc + 1 : nullptr);
+      stamp(2 + l * 10 + 4);
       if (!(ok = grid_barrier(a, epoch))) break;
+      stamp(2 + l * 10 + 5);
       // gate/up + SwiGLU (ffn_norm fused)
-      mk_stage_x(a.h, a.H, L.ffn_norm, a.eps, sm.xs, sm.gs, sm.red);
-      mk_gemv_phase<PH_GU>(a, l, ring, full, empty, cidx, sm, best_v, best_i);
+      mk_stage(a.h, false, a.H, L.ffn_norm, a.eps, sm.xs, sm.gs, xr0);
+      mk_gemv_phase<PH_GU>(a, ring, full, empty, cidx, sm.xs, xr0, best_v, best_i,
+                              wacc ? wacc + 2 : nullptr);
+      stamp(2 + l * 10 + 6);
       if (!(ok = grid_barrier(a, epoch))) break;
+      stamp(2 + l * 10 + 7);
       // down + residual
-      mk_stage_x(a.act, a.F, nullptr, a.eps, sm.xs, sm.gs, sm.red);
-      mk_gemv_phase<PH_DOWN>(a, l, ring, full, empty, cidx, sm, best_v, best_i);
+      mk_stage(a.act, false, a.F, nullptr, a.eps, sm.xs, sm.gs, xr0);
+      mk_gemv_phase<PH_DOWN>(a, ring, full, empty, cidx, sm.xs, xr0, best_v, best_i,
+                              wacc ? wacc + 3 : nullptr);
+      stamp(2 + l * 10 + 8);
       ok = grid_barrier(a, epoch);
+      stamp(2 + l * 10 + 9);
     }
     if (ok) {
     // output_norm + head + argmax
-    mk_stage_x(a.h, a.H, a.out_norm, a.eps, sm.xs, sm.gs, sm.red);
-    mk_gemv_phase<PH_HEAD>(a, 0, ring, full, empty, cidx, sm, best_v, best_i);
+    mk_stage(a.h, false, a.H, a.out_norm, a.eps, sm.xs, sm.gs, xr0);
+    mk_gemv_phase<PH_HEAD>(a, ring, full, empty, cidx, sm.xs, xr0, best_v, best_i,
+                              wacc ? wacc + 4 : nullptr);
+    stamp(2 + a.n_layers * 10);
     if (lane == 0) {
       sm.wv[warp] = best_v;
       sm.wi[warp] = best_i;
@@ -592,25 +779,38 @@ static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs
       last = atomicAdd(a.am_count, 1u) == gridDim.x - 1;
     }
     consumers_sync();
-    if (last && threadIdx.x == 0) {
+    if (last && warp == 0) {
+      // the CTA partials, one per lane at a time, then the shuffle tree
       __threadfence();
       float bv = -FLT_MAX;
       uint32_t bi = 0xFFFFFFFFu;
-      for (int i = 0; i < (int)gridDim.x; i++) {
-        const float v = ((volatile float*)a.am_val)[i];
-        const uint32_t ix = ((volatile uint32_t*)a.am_idx)[i];
+      for (int i = lane; i < (int)gridDim.x; i += 32) {
+        const float v = __ldcg(a.am_val + i);
+        const uint32_t ix = __ldcg(a.am_idx + i);
         if (am_better(v, ix, bv, bi)) {
           bv = v;
           bi = ix;
         }
       }
-      *a.am_best_val = bv;
-      a.ids[0] = (int32_t)bi;
-      if (pos >= 0 && pos < a.hist_cap) a.hist[pos] = (int32_t)bi;
-      a.ctl[0] = pos;
-      a.ctl[1] = 1;
-      *a.am_count = 0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+        const uint32_t oi = __shfl_down_sync(0xffffffffu, bi, o);
+        if (am_better(ov, oi, bv, bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (lane == 0) {
+        *a.am_best_val = bv;
+        a.ids[0] = (int32_t)bi;
+        if (pos >= 0 && pos < a.hist_cap) a.hist[pos] = (int32_t)bi;
+        a.ctl[0] = pos;
+        a.ctl[1] = 1;
+        *a.am_count = 0;
+      }
     }
+    stamp(3 + a.n_layers * 10);
     }  // ok
   }
   __syncthreads();
@@ -625,7 +825,7 @@ static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs
 // Dynamic shared memory of a k_decode_mk launch.
 inline size_t mk_smem_bytes(int stage_bytes, int n_stages, int H, int qw, int F) {
   const int kmax = H > qw ? (H > F ? H : F) : (qw > F ? qw : F);
-  const size_t xfloats = (size_t)kmax / 32 * XPAD + H + 136 + H + 2 * MK_CONSUMERS;
+  const size_t xfloats = (size_t)kmax / 32 * XPAD + (size_t)H / 32 * XPAD + H + 2 * MK_CONSUMERS;
   const size_t region = xfloats > (size_t)AF_END ? xfloats : (size_t)AF_END;
   return (size_t)n_stages * stage_bytes + 2 * MK_MAX_STAGES * 8 + region * 4;
 }

@@ -186,9 +186,7 @@ void dev_release(flock_dev* d) {
 
 int Workspace::alloc(const flock_layer_config& c, int sm_count) {
   P = c.max_prefill < 1 ? 1 : c.max_prefill;
-  attn_splits = c.n_kv_heads > 0 ? sm_count / c.n_kv_heads : 1;
-  if (attn_splits < 1) attn_splits = 1;
-  if (attn_splits > attn_split_cap) attn_splits = attn_split_cap;
+  attn_splits = attn_max_splits(sm_count, c.n_kv_heads);
   H = c.hidden;
   nH = c.n_heads;
   nKV = c.n_kv_heads;
@@ -323,6 +321,7 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.eps = c.eps;
     a.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
     a.chunk_cap = (c.max_keys + a.splits - 1) / a.splits;
+    a.combine = 1;
     pf_add(a.pf, L->w[W_GATE]);
     const size_t smem = attn_fast_smem(a.chunk_cap);
     static bool attr = false;
@@ -844,6 +843,7 @@ int flock_op_attention(flock_dev* d, const float* q, const float* k, const float
     a.head_dim = head_dim;
     a.splits = splits;
     a.chunk_cap = (n_keys + splits - 1) / splits;
+    a.combine = 1;
     const size_t smem = attn_fast_smem(a.chunk_cap);
     if (smem > 200 * 1024) return FLOCK_E_UNSUPPORTED;
     FLOCK_CK(cudaFuncSetAttribute(k_attn_decode_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,

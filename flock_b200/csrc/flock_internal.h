@@ -83,7 +83,7 @@ struct Workspace {
   DBuf h, q, k, v, qn, attn, act;
   DBuf attn_part, attn_count;  // fast decode attention partials
   int attn_splits = 16;         // splits: SMs / kv heads, so one wave covers them
-  int attn_split_cap = 64;      // partial slots allocated (the persistent kernel uses more)
+  int attn_split_cap = 32;      // partial slots allocated per head (attn_max_splits' bound)
   int alloc(const flock_layer_config& c, int sm_count);
 };
 

@@ -34,7 +34,7 @@ struct flock_model {
   // persistent decode kernel
   int decode_mode = FLOCK_DECODE_KERNELS;
   bool mk_ok = false;       // shape fits the persistent kernel
-  DBuf mk_layers, mk_bar, mk_err;
+  DBuf mk_layers, mk_bar, mk_err, mk_trace;
   MkArgs mk{};
   size_t mk_smem = 0;
   int mk_grid = 0;
@@ -190,8 +190,8 @@ int mk_prepare(flock_model* m) {
   FLOCK_CK(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
   if (!coop) return FLOCK_OK;
   const int grid = m->dev->sm_count;
-  const int splits = grid / c.n_kv_heads;
-  if (splits < 1 || splits > m->ws.attn_split_cap) return FLOCK_OK;
+  const int splits = attn_max_splits(grid, c.n_kv_heads);  // = the kernel graph's
+  if (splits != m->ws.attn_splits) return FLOCK_OK;
   MkArgs& a = m->mk;
   a = MkArgs{};
   a.n_stages = 4;
@@ -309,17 +309,11 @@ int capture_decode(flock_model* m) {
   if (m->decode_graph) return FLOCK_OK;
   cudaStream_t st = m->dev->stream;
   cudaGraph_t g = nullptr;
-  const bool mk = m->decode_mode == FLOCK_DECODE_PERSISTENT && m->mk_ok;
   FLOCK_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-  int rc = FLOCK_OK;
-  if (mk) {
-    rc = enqueue_mk(m);
-  } else {
-    rc = enqueue_embed(m, 1);
-    if (!rc) rc = enqueue_layers(m, 1);
-    if (!rc) rc = enqueue_head(m, 0);
-    if (!rc) rc = enqueue_record(m);
-  }
+  int rc = enqueue_embed(m, 1);
+  if (!rc) rc = enqueue_layers(m, 1);
+  if (!rc) rc = enqueue_head(m, 0);
+  if (!rc) rc = enqueue_record(m);
   cudaError_t e = cudaStreamEndCapture(st, &g);
   if (rc) {
     if (g) cudaGraphDestroy(g);
@@ -336,6 +330,16 @@ int capture_decode(flock_model* m) {
     set_error("decode graph instantiate failed: %s", cudaGetErrorString(e));
     return FLOCK_E_CUDA;
   }
+  return FLOCK_OK;
+}
+
+// One single-token decode step on the stream: the persistent kernel (a
+// barrier reset plus one cooperative launch; no graph, so profilers see the
+// kernel) or the captured kernel graph.
+int launch_decode(flock_model* m) {
+  if (m->decode_mode == FLOCK_DECODE_PERSISTENT && m->mk_ok) return enqueue_mk(m);
+  FLOCK_TRY(capture_decode(m));
+  FLOCK_CK(cudaGraphLaunch(m->decode_graph, m->dev->stream));
   return FLOCK_OK;
 }
 
@@ -429,6 +433,33 @@ int flock_model_set_decode_mode(flock_model* m, int mode) {
   return FLOCK_OK;
 }
 
+int flock_model_trace(flock_model* m, int enable) {
+  if (!m) return FLOCK_E_ARG;
+  if (!m->mk_ok) {
+    set_error("phase tracing needs the persistent decode kernel, which this model cannot run");
+    return FLOCK_E_UNSUPPORTED;
+  }
+  if (enable && !m->mk_trace.p) {
+    const size_t n = (size_t)m->mk_grid * mk_trace_stride(m->held);
+    FLOCK_TRY(m->mk_trace.alloc(n * 8));
+    FLOCK_CK(cudaMemset(m->mk_trace.p, 0, n * 8));
+  }
+  m->mk.trace = enable ? m->mk_trace.as<unsigned long long>() : nullptr;
+  return FLOCK_OK;
+}
+
+int flock_model_trace_read(flock_model* m, uint64_t* out, int64_t cap, int* n_ctas, int* stride) {
+  if (!m || !n_ctas || !stride) return FLOCK_E_ARG;
+  *n_ctas = m->mk_grid;
+  *stride = mk_trace_stride(m->held);
+  const int64_t n = (int64_t)m->mk_grid * *stride;
+  if (!m->mk_trace.p) return FLOCK_E_STATE;
+  if (!out || cap < n) return FLOCK_E_LIMIT;
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_CK(cudaMemcpy(out, m->mk_trace.p, (size_t)n * 8, cudaMemcpyDeviceToHost));
+  return FLOCK_OK;
+}
+
 int flock_model_get_decode_mode(const flock_model* m, int* mode) {
   if (!m || !mode) return FLOCK_E_ARG;
   *mode = (m->decode_mode == FLOCK_DECODE_PERSISTENT && m->mk_ok) ? FLOCK_DECODE_PERSISTENT
@@ -477,8 +508,7 @@ int flock_model_step(flock_model* m, const int32_t* ids, int n, int32_t* next_id
   if (n == 1 && m->held > 0) {
     FLOCK_TRY(check_room(m, 1));
     FLOCK_TRY(upload_ids(m, ids, 1));
-    FLOCK_TRY(capture_decode(m));
-    FLOCK_CK(cudaGraphLaunch(m->decode_graph, m->dev->stream));
+    FLOCK_TRY(launch_decode(m));
     m->pos += 1;
   } else {
     int last = 0;
@@ -498,9 +528,8 @@ int flock_model_decode_device(flock_model* m, int n_steps, int32_t* out_ids) {
   if (m->held == 0) return FLOCK_E_STATE;
   FLOCK_TRY(check_room(m, n_steps));
   FLOCK_CK(cudaSetDevice(m->dev->ordinal));
-  FLOCK_TRY(capture_decode(m));
   const int start = m->pos;
-  for (int i = 0; i < n_steps; i++) FLOCK_CK(cudaGraphLaunch(m->decode_graph, m->dev->stream));
+  for (int i = 0; i < n_steps; i++) FLOCK_TRY(launch_decode(m));
   m->pos += n_steps;
   for (auto* L : m->layers) L->n_keys = m->pos;
   if (n_steps)

@@ -192,6 +192,22 @@ class Model:
         _abi.call("flock_model_set_decode_mode", self.handle,
                   _abi.FLOCK_DECODE_PERSISTENT if mode == "persistent" else _abi.FLOCK_DECODE_KERNELS)
 
+    def trace(self, enable: bool = True) -> None:
+        """Record per-CTA phase timestamps in the persistent decode kernel."""
+        _abi.call("flock_model_trace", self.handle, 1 if enable else 0)
+
+    def read_trace(self) -> np.ndarray:
+        """The last traced token's entries, [n_ctas, 10 + 10 * held] uint64 ns."""
+        n, s = ctypes.c_int(), ctypes.c_int()
+        rc = _abi.lib().flock_model_trace_read(self.handle, None, 0, ctypes.byref(n), ctypes.byref(s))
+        if rc not in (0, _abi.FLOCK_E_LIMIT):
+            _abi.check(rc)
+        out = np.zeros((n.value, s.value), np.uint64)
+        _abi.call("flock_model_trace_read", self.handle,
+                  out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), out.size,
+                  ctypes.byref(n), ctypes.byref(s))
+        return out
+
     def set_token(self, token: int) -> None:
         """The id the next device-fed decode step consumes."""
         _abi.call("flock_model_set_token", self.handle, int(token))

@@ -120,3 +120,21 @@ def test_persistent_full_06b(dev):
     la, lb = a.logits([ta]), b.logits([tb])
     assert np.array_equal(_bits(la), _bits(lb))
     assert a.decode_device(16).tolist() == b.decode_device(16).tolist()
+
+
+def test_phase_trace(dev, small):
+    a, b = _pair(dev, small)
+    for M in (a, b):
+        M.step([2, 4, 6])
+    a.trace(True)
+    got = a.decode_device(3)
+    tr = a.read_trace().astype(np.int64)
+    a.trace(False)
+    assert got.tolist() == b.decode_device(3).tolist()
+    assert tr.shape == (dev.sm_count, 10 + 10 * a.held)
+    tr = tr[:, :4 + 10 * a.held]                      # the stamps
+    assert (tr > 0).all()
+    assert (np.diff(tr, axis=1) >= 0).all()          # stamps in program order per CTA
+    # no CTA leaves a grid barrier before every CTA has reached it
+    for c in range(3, tr.shape[1] - 2, 2):
+        assert tr[:, c].min() >= tr[:, c - 1].max()
