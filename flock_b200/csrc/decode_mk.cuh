@@ -27,6 +27,7 @@
 #include "attn_fast.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
+#include "mbar.cuh"
 
 namespace flock {
 
@@ -92,75 +93,6 @@ __host__ __device__ inline int mk_trace_stride(int n_layers) { return 10 + 10 * 
 constexpr int MK_CONSUMERS = 8;                   // consumer warps
 constexpr int MK_THREADS = (MK_CONSUMERS + 1) * 32;
 constexpr int MK_MAX_STAGES = 8;
-constexpr uint64_t MK_WAIT_NS = 2000000000ull;    // a wait gives up after 2 s
-constexpr uint32_t MK_MAX_POLLS = 1u << 26;       // backstop on the poll count
-
-// ------------------------------------------------------------- primitives
-FLOCK_DEV uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-FLOCK_DEV void mbar_init(uint64_t* b, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
-}
-FLOCK_DEV void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
-               "r"(bytes) : "memory");
-}
-FLOCK_DEV void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-FLOCK_DEV bool mbar_try_wait(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-FLOCK_DEV uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// try_wait that lets the hardware suspend the thread for up to `hint_ns`
-// while the phase is incomplete (it resumes as soon as the phase completes),
-// so a waiting warp stops taking issue slots from the warps that compute.
-FLOCK_DEV bool mbar_try_wait_sleep(uint64_t* b, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: false after MK_WAIT_NS of global time (or MK_MAX_POLLS polls),
-// or as soon as *err is set when `watch_err`.  Each poll may sleep up to
-// MK_SLEEP_NS.
-constexpr uint32_t MK_SLEEP_NS = 20000;
-FLOCK_DEV bool mbar_wait(uint64_t* b, uint32_t parity, const int* err, bool watch_err = true) {
-  uint64_t t0 = 0;
-  for (uint32_t i = 0; i < MK_MAX_POLLS; i++) {
-    if (mbar_try_wait_sleep(b, parity, MK_SLEEP_NS)) return true;
-    if ((i & 63) == 63) {
-      if (watch_err && *(volatile const int*)err) return false;
-      const uint64_t now = globaltimer_ns();
-      if (!t0) t0 = now;
-      else if (now - t0 > MK_WAIT_NS) return false;
-    }
-  }
-  return false;
-}
-FLOCK_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 FLOCK_DEV unsigned ld_acquire_u32(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -314,7 +246,7 @@ FLOCK_DEV bool grid_barrier(const MkArgs& a, unsigned& epoch) {
       if (*(volatile int*)a.err) { ok = 0; break; }
       const uint64_t now = globaltimer_ns();
       if (!t0) t0 = now;
-      if (now - t0 > MK_WAIT_NS || i >= MK_MAX_POLLS) {
+      if (now - t0 > WAIT_NS || i >= WAIT_MAX_POLLS) {
         atomicExch(a.err, 2);
         ok = 0;
         break;

@@ -1,0 +1,179 @@
+// Host side of the tensor-core prefill GEMM (gemm_tc.cuh): the activation
+// image, launches, and the op-level entry points that the M > 1 sweep and
+// the parity tests call.
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "flock_internal.h"
+#include "gemm_tc.cuh"
+
+namespace flock {
+
+size_t act_image_bytes(int M, int K) {
+  const int nt = tc_token_tile(M);
+  const size_t n_mb = (size_t)(M + nt - 1) / nt;
+  return n_mb * (size_t)(K / TC_KT) * (size_t)nt * 128;
+}
+
+int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float* gain, float eps,
+                      int M, int K, uint8_t* img) {
+  if (K % TC_KT || K > 12288 || M < 1) {
+    set_error("tensor-core GEMM needs K a multiple of 64 and at most 12288 (K = %d)", K);
+    return FLOCK_E_ARG;
+  }
+  ActImgArgs a = {};
+  a.x = x;
+  a.x_stride = x_stride;
+  a.gain = gain;
+  a.eps = eps;
+  a.M = M;
+  a.K = K;
+  a.Nt = tc_token_tile(M);
+  a.img = img;
+  const int rows = (M + a.Nt - 1) / a.Nt * a.Nt;
+  k_act_image<<<rows, ACT_IMG_THREADS, (size_t)K * 4, st>>>(a);
+  FLOCK_CK(cudaGetLastError());
+  return FLOCK_OK;
+}
+
+TcSeg tc_seg_of(const flock_tensor* t, float* out, int out_stride) {
+  TcSeg s;
+  s.qs = t->qs.as<uint8_t>();
+  s.sc = t->sc.as<uint16_t>();
+  s.sc_stride = t->sc_stride;
+  s.rows = (int)t->rows;
+  s.out = out;
+  s.out_stride = out_stride;
+  return s;
+}
+
+void tc_finish_tiles(TcArgs& a) {
+  int tiles = 0;
+  for (int i = 0; i < a.nseg; i++) {
+    a.tile0[i] = tiles;
+    tiles += (a.seg[i].rows + TC_ROWS - 1) / TC_ROWS;
+  }
+  a.tile0[a.nseg] = tiles;
+}
+
+template <int QT, int EPI>
+static int launch_tc(cudaStream_t st, const TcArgs& a) {
+  const size_t smem = gemm_tc_smem_bytes(a.Nt);
+  FLOCK_CK(cudaFuncSetAttribute(k_gemm_tc<QT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)gemm_tc_smem_bytes(TC_MAX_NT)));
+  const dim3 grid((unsigned)a.tile0[a.nseg], (unsigned)((a.M + a.Nt - 1) / a.Nt));
+  k_gemm_tc<QT, EPI><<<grid, TC_THREADS, smem, st>>>(a);
+  FLOCK_CK(cudaGetLastError());
+  return FLOCK_OK;
+}
+
+// Y = X . W^T for the segments of `a` on the tensor cores; `a.img` must hold
+// the activation image of the same M and K.
+int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a) {
+  if (a.K % TC_KT || a.M < 1 || a.nseg < 1 || a.nseg > 3) return FLOCK_E_ARG;
+  a.Nt = tc_token_tile(a.M);
+  tc_finish_tiles(a);
+  if (qt == QT_Q8)
+    return epi == EPI_RESIDUAL ? launch_tc<QT_Q8, EPI_RESIDUAL>(st, a)
+                               : launch_tc<QT_Q8, EPI_STORE>(st, a);
+  return epi == EPI_RESIDUAL ? launch_tc<QT_Q4, EPI_RESIDUAL>(st, a)
+                             : launch_tc<QT_Q4, EPI_STORE>(st, a);
+}
+
+}  // namespace flock
+
+using namespace flock;
+
+namespace {
+
+// One op-level GEMM on device buffers: image + tensor-core GEMM.
+int gemm_once(flock_dev* d, const flock_tensor* w, const float* x, int M, float* y, int* err,
+              uint8_t* img) {
+  const int K = (int)w->cols;
+  FLOCK_TRY(act_image_enqueue(d->stream, x, K, nullptr, 0.0f, M, K, img));
+  TcArgs a = {};
+  a.seg[0] = tc_seg_of(w, y, (int)w->rows);
+  a.nseg = 1;
+  a.K = K;
+  a.M = M;
+  a.img = img;
+  a.err = err;
+  return gemm_tc_enqueue(d->stream, w->dtype == FLOCK_Q8_0 ? QT_Q8 : QT_Q4, EPI_STORE, a);
+}
+
+int check_tc_err(const DBuf& err) {
+  int e = 0;
+  FLOCK_CK(cudaMemcpy(&e, err.p, 4, cudaMemcpyDeviceToHost));
+  if (e) {
+    set_error("tensor-core GEMM gave up waiting (code %d)", e);
+    return FLOCK_E_CUDA;
+  }
+  return FLOCK_OK;
+}
+
+int gemm_check_args(const flock_tensor* w, int M) {
+  if (!w || M < 1 || w->dtype == FLOCK_F32) return FLOCK_E_ARG;
+  if (w->cols % TC_KT || w->cols > 12288) {
+    set_error("tensor-core GEMM needs cols a multiple of 64 and at most 12288 (cols = %lld)",
+              (long long)w->cols);
+    return FLOCK_E_ARG;
+  }
+  return FLOCK_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int flock_op_gemm(flock_dev* d, const flock_tensor* w, const float* x, int M, float* y) {
+  if (!d || !x || !y) return FLOCK_E_ARG;
+  FLOCK_TRY(gemm_check_args(w, M));
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  DBuf dx, dy, img, err;
+  FLOCK_TRY(dx.alloc((size_t)M * w->cols * 4));
+  FLOCK_TRY(dy.alloc((size_t)M * w->rows * 4));
+  FLOCK_TRY(img.alloc(act_image_bytes(M, (int)w->cols)));
+  FLOCK_TRY(err.alloc(16));
+  FLOCK_CK(cudaMemset(err.p, 0, 16));
+  FLOCK_CK(cudaMemcpy(dx.p, x, dx.bytes, cudaMemcpyHostToDevice));
+  FLOCK_TRY(gemm_once(d, w, dx.as<float>(), M, dy.as<float>(), err.as<int>(), img.as<uint8_t>()));
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  FLOCK_TRY(check_tc_err(err));
+  FLOCK_CK(cudaMemcpy(y, dy.p, dy.bytes, cudaMemcpyDeviceToHost));
+  return FLOCK_OK;
+}
+
+int flock_op_gemm_timed(flock_dev* d, const flock_tensor* w, int M, int iters, float* ms_per_call) {
+  if (!d || iters < 1 || !ms_per_call) return FLOCK_E_ARG;
+  FLOCK_TRY(gemm_check_args(w, M));
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  std::vector<float> hx((size_t)M * w->cols);
+  uint32_t s = 777u;
+  for (auto& v : hx) {  // xorshift32 in [-1, 1)
+    s ^= s << 13;
+    s ^= s >> 17;
+    s ^= s << 5;
+    v = (float)((double)s / 2147483648.0 - 1.0);
+  }
+  DBuf dx, dy, img, err;
+  FLOCK_TRY(dx.alloc(hx.size() * 4));
+  FLOCK_TRY(dy.alloc((size_t)M * w->rows * 4));
+  FLOCK_TRY(img.alloc(act_image_bytes(M, (int)w->cols)));
+  FLOCK_TRY(err.alloc(16));
+  FLOCK_CK(cudaMemset(err.p, 0, 16));
+  FLOCK_CK(cudaMemcpy(dx.p, hx.data(), dx.bytes, cudaMemcpyHostToDevice));
+  FLOCK_TRY(gemm_once(d, w, dx.as<float>(), M, dy.as<float>(), err.as<int>(), img.as<uint8_t>()));
+  FLOCK_CK(cudaEventRecord(d->t0, d->stream));
+  for (int i = 0; i < iters; i++)
+    FLOCK_TRY(gemm_once(d, w, dx.as<float>(), M, dy.as<float>(), err.as<int>(),
+                        img.as<uint8_t>()));
+  FLOCK_CK(cudaEventRecord(d->t1, d->stream));
+  FLOCK_CK(cudaEventSynchronize(d->t1));
+  float ms = 0;
+  FLOCK_CK(cudaEventElapsedTime(&ms, d->t0, d->t1));
+  *ms_per_call = ms / iters;
+  return check_tc_err(err);
+}
+
+}  // extern "C"

@@ -93,6 +93,14 @@ extern const char* const kTensorNames[W_COUNT];
 
 // Launch plan pieces
 int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl);
+// tensor-core prefill GEMM (flock_gemm.cu)
+struct TcArgs;
+struct TcSeg;
+size_t act_image_bytes(int M, int K);
+int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float* gain, float eps,
+                      int M, int K, uint8_t* img);
+int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a);
+TcSeg tc_seg_of(const flock_tensor* t, float* out, int out_stride);
 int gemv_grid(flock_dev* d, int total_groups);
 
 }  // namespace flock

@@ -1,0 +1,397 @@
+// Prefill GEMM on the 5th-generation tensor cores (tcgen05) for Q8_0 / Q4_0
+// weights -- kernels/q8_coop.wgsl:76 / q4_coop.wgsl:48 at M > 1 tokens
+// (layer.ts:685 encodePrefill), re-designed for B200:
+//
+//   Y[m][n] = sum_k X[m][k] * W[n][k],  X f32 -> bf16, W = s * q -> bf16,
+//   f32 accumulation in tensor memory.
+//
+//  * Operands are swapped for small M: 128 weight rows form the MMA's M and
+//    up to 256 tokens its N, so a 16-token prefill still issues full-height
+//    tcgen05.mma.cta_group::1.kind::f16 (128 x Nt x 16) instructions.
+//  * Producers (4 warps, one weight row per thread) keep 4 K-tiles of raw
+//    int8 / nibble weights in flight in registers, dequantise q * s in f32,
+//    round to bf16 and write the K-major 128-byte-swizzled layout the UMMA
+//    shared-memory descriptor names (8-row x 128-byte atoms, 16-byte chunk
+//    c of row r at (c ^ r % 8)).  int8 values are exact in bf16, so the only
+//    weight rounding is that of the scaled value.
+//  * Activations come from an image the caller builds once per GEMM
+//    (k_act_image: RMSNorm fused, bf16, same swizzled layout, Nt rows per
+//    K-tile contiguous), so each stage's B tile is one bulk copy.
+//  * One thread issues the MMAs; tcgen05.commit returns each stage to the
+//    producers through an mbarrier and signals the epilogue after the last
+//    K-tile.  The epilogue warps read the accumulator with tcgen05.ld
+//    (32 lanes x 32 bit: one weight row per thread, one token per column)
+//    and store coalesced rows of Y, optionally adding a residual.
+//
+// Every wait is bounded (mbar_wait); on a timeout the kernel sets *err,
+// still releases its tensor memory and returns.  No multicast is used.
+#pragma once
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "mbar.cuh"
+
+namespace flock {
+
+constexpr int TC_ROWS = 128;              // weight rows per CTA: the MMA's M
+constexpr int TC_KT = 64;                 // K per stage: one 128-byte bf16 swizzle atom row
+constexpr int TC_STAGES = 4;
+constexpr int TC_MAX_NT = 256;            // tokens per CTA: the MMA's N
+constexpr int TC_PRODUCERS = 128;         // 4 warps: producers, then the epilogue
+constexpr int TC_THREADS = TC_PRODUCERS + 32;  // + the MMA warp
+constexpr int TC_A_BYTES = TC_ROWS * TC_KT * 2;  // 16 KiB of bf16 per stage
+constexpr int TC_PREFETCH = 4;            // K-tiles of raw weights in flight per thread
+
+struct TcSeg {
+  const uint8_t* qs;
+  const uint16_t* sc;
+  int sc_stride;   // f16 scales per row
+  int rows;
+  float* out;      // [m][out_stride]
+  int out_stride;
+};
+
+struct TcArgs {
+  TcSeg seg[3];
+  int nseg;
+  int tile0[4];      // first 128-row tile of each segment; tile0[nseg] = all tiles
+  int K, M, Nt;      // Nt: tokens per CTA (multiple of 16, <= 256)
+  const uint8_t* img;  // activation image: [M / Nt][K / 64][Nt][128 B] bf16, swizzled
+  const float* res;    // EPI_RESIDUAL: y += res[m][n] (res may alias the output)
+  int res_stride;
+  int* err;
+};
+
+// ------------------------------------------------------------------ tcgen05
+FLOCK_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+FLOCK_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+FLOCK_DEV void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+}
+FLOCK_DEV void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+FLOCK_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// D[tmem] (+)= A[smem desc] . B[smem desc]^T, bf16 inputs, f32 accumulator.
+FLOCK_DEV void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// The mbarrier arrives once every tcgen05 operation this thread issued before
+// has completed.
+FLOCK_DEV void umma_commit(uint64_t* mbar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(mbar))
+      : "memory");
+}
+// 16 consecutive f32 columns of this warp's 32 tensor-memory lanes.
+FLOCK_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms
+// 1024 bytes apart (stride byte offset); the leading byte offset is unused
+// for swizzled K-major operands.  Bits 46-47 hold the sm_100 descriptor
+// version (1), bits 61-63 the layout (2 = 128-byte swizzle).
+FLOCK_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: f32 D (bits 4-5 = 1), bf16 A and B
+// (bits 7-9, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+FLOCK_DEV uint32_t umma_idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
+// Byte offset of 16-byte chunk c (8 bf16, K elements 8c..8c+7 of a K-tile)
+// of row r inside a K-tile block of 128-byte rows.
+FLOCK_DEV uint32_t sw128_off(int r, int c) { return (uint32_t)r * 128u + (uint32_t)((c ^ (r & 7)) << 4); }
+
+FLOCK_DEV uint32_t bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Raw weights of one row for one K-tile (64 weights) and their two scales.
+struct TcRaw {
+  uint4 q[4];   // Q8: 64 int8; Q4: q[0..1] = two 16-byte nibble blocks
+  uint32_t s;   // two f16 scales
+};
+
+template <int QT>
+FLOCK_DEV void tc_load_raw(TcRaw& r, const TcSeg& sg, int K, int row, int kt) {
+  const uint4* p;
+  if (QT == QT_Q8) {
+    p = reinterpret_cast<const uint4*>(sg.qs + (size_t)row * K + (size_t)kt * TC_KT);
+    r.q[0] = ldg_stream(p);
+    r.q[1] = ldg_stream(p + 1);
+    r.q[2] = ldg_stream(p + 2);
+    r.q[3] = ldg_stream(p + 3);
+  } else {
+    p = reinterpret_cast<const uint4*>(sg.qs + (size_t)row * (K / 2) + (size_t)kt * (TC_KT / 2));
+    r.q[0] = ldg_stream(p);
+    r.q[1] = ldg_stream(p + 1);
+  }
+  r.s = __ldg(reinterpret_cast<const uint32_t*>(sg.sc + (size_t)row * sg.sc_stride + kt * 2));
+}
+
+// Dequantise one row's K-tile into its 128-byte swizzled row of the A stage.
+template <int QT>
+FLOCK_DEV void tc_store_row(const TcRaw& r, uint8_t* A, int t) {
+  const float s0 = scale_f16((uint16_t)(r.s & 0xFFFFu)), s1 = scale_f16((uint16_t)(r.s >> 16));
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    float v[8];
+    if (QT == QT_Q8) {
+      const uint4 w = r.q[c >> 1];
+      const uint32_t w0 = (c & 1) ? w.z : w.x, w1 = (c & 1) ? w.w : w.y;
+      dec_i8x4(w0, v[0], v[1], v[2], v[3]);
+      dec_i8x4(w1, v[4], v[5], v[6], v[7]);
+    } else {
+      // block c / 4; weights j0..j0+7 of it: low nibbles of bytes j0.. (j0 < 16)
+      // or high nibbles of bytes j0-16.. (q4_coop.wgsl: byte i = weights i, i+16)
+      const uint4 w = r.q[c >> 2];
+      const int j0 = (c & 3) * 8;
+      const uint32_t b0 = (j0 & 15) == 0 ? w.x : w.z, b1 = (j0 & 15) == 0 ? w.y : w.w;
+      const int sh = j0 < 16 ? 0 : 4;
+      dec_nib4((b0 >> sh) & 0x0F0F0F0Fu, v[0], v[1], v[2], v[3]);
+      dec_nib4((b1 >> sh) & 0x0F0F0F0Fu, v[4], v[5], v[6], v[7]);
+    }
+    const float s = c < 4 ? s0 : s1;
+    uint4 o;
+    o.x = bf16x2(v[0] * s, v[1] * s);
+    o.y = bf16x2(v[2] * s, v[3] * s);
+    o.z = bf16x2(v[4] * s, v[5] * s);
+    o.w = bf16x2(v[6] * s, v[7] * s);
+    *reinterpret_cast<uint4*>(A + sw128_off(t, c)) = o;
+  }
+}
+
+FLOCK_DEV int tc_tmem_cols(int nt) {
+  int c = 32;
+  while (c < nt) c <<= 1;
+  return c;
+}
+
+template <int QT, int EPI>
+static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a) {
+  extern __shared__ __align__(16) uint8_t tsm_raw[];
+  // the swizzle atoms must sit on 1024-byte boundaries: round the dynamic
+  // shared memory up (the launch reserves 1 KiB of slack for this)
+  uint8_t* tsm = tsm_raw + ((1024u - (smem_u32(tsm_raw) & 1023u)) & 1023u);
+  const int Nt = a.Nt;
+  const int b_bytes = Nt * 128;
+  const int stage_bytes = TC_A_BYTES + b_bytes;  // a multiple of 1024
+  uint64_t* full = reinterpret_cast<uint64_t*>(tsm + TC_STAGES * stage_bytes);
+  uint64_t* empty = full + TC_STAGES;
+  uint64_t* done = empty + TC_STAGES;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; s++) {
+      mbar_init(&full[s], TC_PRODUCERS);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const uint32_t ncols = (uint32_t)tc_tmem_cols(Nt);
+  if (warp == 4) {
+    tmem_alloc(tslot, ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  int sgi = 0;
+  while (sgi + 1 < a.nseg && (int)blockIdx.x >= a.tile0[sgi + 1]) sgi++;
+  const TcSeg& sg = a.seg[sgi];
+  const int row0 = ((int)blockIdx.x - a.tile0[sgi]) * TC_ROWS;
+  const int mb = blockIdx.y, m0 = mb * Nt;
+  const int KT = a.K / TC_KT;
+
+  if (warp < 4) {
+    // ------------------------------------------------------------ producers
+    const int t = threadIdx.x;
+    const int row = row0 + t;
+    const bool rv = row < sg.rows;
+    const int lrow = rv ? row : sg.rows - 1;  // rows past the end load a real row, store nothing
+    TcRaw ring[TC_PREFETCH];
+#pragma unroll
+    for (int j = 0; j < TC_PREFETCH; j++)
+      if (j < KT) tc_load_raw<QT>(ring[j], sg, a.K, lrow, j);
+    bool ok = true;
+    for (int kt0 = 0; kt0 < KT && ok; kt0 += TC_PREFETCH) {
+#pragma unroll
+      for (int j = 0; j < TC_PREFETCH; j++) {
+        const int kt = kt0 + j;
+        if (kt >= KT || !ok) break;
+        const int st = kt % TC_STAGES;
+        if (kt >= TC_STAGES &&
+            !mbar_wait(&empty[st], (uint32_t)(((kt / TC_STAGES) - 1) & 1), a.err)) {
+          atomicCAS(a.err, 0, 1);
+          ok = false;
+          break;
+        }
+        uint8_t* A = tsm + (size_t)st * stage_bytes;
+        if (t == 0) {
+          mbar_expect_tx_only(&full[st], (uint32_t)b_bytes);
+          bulk_g2s(A + TC_A_BYTES, a.img + ((size_t)mb * KT + kt) * (size_t)b_bytes,
+                   (uint32_t)b_bytes, &full[st]);
+        }
+        tc_store_row<QT>(ring[j], A, t);
+        if (kt + TC_PREFETCH < KT) tc_load_raw<QT>(ring[j], sg, a.K, lrow, kt + TC_PREFETCH);
+        fence_proxy_async_smem();
+        mbar_arrive(&full[st]);
+      }
+    }
+    // ------------------------------------------------------------- epilogue
+    if (!mbar_wait(done, 0, a.err)) atomicCAS(a.err, 0, 1);
+    tc_fence_after();
+    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    for (int c0 = 0; c0 < Nt; c0 += 16) {
+      float v[16];
+      tmem_ld16(tmem + lane_base + (uint32_t)c0, v);
+      if (rv) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const int m = m0 + c0 + j;
+          if (m < a.M) {
+            float y = v[j];
+            if (EPI == EPI_RESIDUAL) y = a.res[(size_t)m * a.res_stride + row] + y;
+            sg.out[(size_t)m * sg.out_stride + row] = y;
+          }
+        }
+      }
+    }
+  } else if (lane == 0) {
+    // ----------------------------------------------------------- MMA issuer
+    const uint32_t idesc = umma_idesc_bf16(TC_ROWS, Nt);
+    for (int kt = 0; kt < KT; kt++) {
+      const int st = kt % TC_STAGES;
+      if (!mbar_wait(&full[st], (uint32_t)((kt / TC_STAGES) & 1), a.err)) {
+        atomicCAS(a.err, 0, 1);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t A = smem_u32(tsm + (size_t)st * stage_bytes), B = A + TC_A_BYTES;
+#pragma unroll
+      for (int k16 = 0; k16 < TC_KT / 16; k16++)
+        umma_bf16(tmem, umma_desc_sw128(A + 32 * k16), umma_desc_sw128(B + 32 * k16), idesc,
+                  (kt | k16) != 0);
+      umma_commit(&empty[st]);
+    }
+    umma_commit(done);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, ncols);
+  }
+}
+
+inline size_t gemm_tc_smem_bytes(int nt) {
+  return (size_t)TC_STAGES * (TC_A_BYTES + nt * 128) + (2 * TC_STAGES + 1) * 8 + 16 + 1024;
+}
+
+// ------------------------------------------------------- activation image
+// X (f32 [M][x_stride]) -> bf16 image [M / Nt][K / 64][Nt][128 B] in the
+// swizzled K-major layout, RMSNorm fused when `gain` is set (ops_ref.ts:20
+// order: WG = 128 strided partials, the pairwise tree, 1/sqrt in f64 rounded
+// once, then x * scale * gain rounded per multiply).  One CTA per image row;
+// rows >= M are written as zeros.
+struct ActImgArgs {
+  const float* x;
+  int x_stride;
+  const float* gain;
+  float eps;
+  int M, K, Nt;
+  uint8_t* img;
+};
+
+constexpr int ACT_IMG_THREADS = 128;
+
+static __global__ void __launch_bounds__(ACT_IMG_THREADS) k_act_image(const ActImgArgs a) {
+  extern __shared__ __align__(16) float xrow[];
+  __shared__ float red[132];
+  const int m = blockIdx.x, t = threadIdx.x;
+  const int r = m % a.Nt, mb = m / a.Nt, KT = a.K / TC_KT;
+  uint8_t* base = a.img + (size_t)mb * KT * a.Nt * 128 + (size_t)r * 128;
+  if (m >= a.M) {
+    for (int i = t; i < a.K / 8; i += ACT_IMG_THREADS)
+      *reinterpret_cast<uint4*>(base + (size_t)(i >> 3) * a.Nt * 128 + ((i & 7) << 4)) =
+          make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)m * a.x_stride);
+  for (int i = t; i < a.K / 4; i += ACT_IMG_THREADS) reinterpret_cast<float4*>(xrow)[i] = src[i];
+  __syncthreads();
+  float scale = 1.0f;
+  if (a.gain) {
+    float acc = 0.0f;
+    for (int i = t; i < a.K; i += 128) acc = ffma(xrow[i], xrow[i], acc);
+    red[t] = acc;
+    __syncthreads();
+    if (t < 64) red[t] = fadd(red[t], red[t + 64]);
+    __syncthreads();
+    if (t < 32) {
+      float v = fadd(red[t], red[t + 32]);
+      v = warp_tree_sum(v);
+      if (t == 0) red[128] = rsqrt_f64r(fadd(fdiv(v, (float)a.K), a.eps));
+    }
+    __syncthreads();
+    scale = red[128];
+  }
+  for (int i = t; i < a.K / 8; i += ACT_IMG_THREADS) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int k = 8 * i + e;
+      v[e] = a.gain ? fmul(fmul(xrow[k], scale), __ldg(a.gain + k)) : xrow[k];
+    }
+    uint4 o;
+    o.x = bf16x2(v[0], v[1]);
+    o.y = bf16x2(v[2], v[3]);
+    o.z = bf16x2(v[4], v[5]);
+    o.w = bf16x2(v[6], v[7]);
+    const int kt = i >> 3, c = i & 7;
+    *reinterpret_cast<uint4*>(base + (size_t)kt * a.Nt * 128 - (size_t)r * 128 +
+                              sw128_off(r, c)) = o;
+  }
+}
+
+inline int tc_token_tile(int M) {
+  const int nt = (M + 15) / 16 * 16;
+  return nt < TC_MAX_NT ? nt : TC_MAX_NT;
+}
+
+}  // namespace flock

@@ -44,6 +44,23 @@ def matvec_timed(dev: Device, w: GpuTensor, n_tokens: int = 1, iters: int = 50) 
     return ms.value
 
 
+def gemm(dev: Device, w: GpuTensor, x: np.ndarray, m: int) -> np.ndarray:
+    """[m][cols] x W^T on the tensor cores (bf16 operands, f32 accumulation)."""
+    x = _f32(x)
+    if x.size != m * w.cols:
+        raise ValueError(f"x is {x.size} floats, want {m * w.cols}")
+    out = np.empty(m * w.rows, np.float32)
+    _abi.call("flock_op_gemm", dev.handle, w.handle, _abi.ptr(x, _f), m, _abi.ptr(out, _f))
+    return out
+
+
+def gemm_timed(dev: Device, w: GpuTensor, m: int, iters: int = 20) -> float:
+    """Mean ms per device-resident tensor-core GEMM (activation image + GEMM)."""
+    ms = ctypes.c_float()
+    _abi.call("flock_op_gemm_timed", dev.handle, w.handle, m, iters, ctypes.byref(ms))
+    return ms.value
+
+
 def rmsnorm(dev: Device, x, g, n: int, n_vecs: int, eps: float) -> np.ndarray:
     x, g = _f32(x), _f32(g)
     out = np.empty(n * n_vecs, np.float32)

@@ -136,6 +136,16 @@ FLOCK_API int flock_op_matvec(flock_dev* dev, const flock_tensor* w, const float
  * writes the mean milliseconds per launch. */
 FLOCK_API int flock_op_matvec_timed(flock_dev* dev, const flock_tensor* w, int n_tokens, int iters,
                                     float* ms_per_call);
+/* The prefill matmul of layer.ts:685 encodePrefill (q8_coop.wgsl:76 /
+ * q4_coop.wgsl:48 over M tokens) on the tcgen05 tensor cores: y[m][r] =
+ * W x[m] with x and s * q rounded to bf16 and f32 accumulation (the bf16
+ * prefill path: max relative error <= 1e-2).  x is [M][cols],
+ * y [M][rows]; cols must be a multiple of 64 and at most 12288. */
+FLOCK_API int flock_op_gemm(flock_dev* dev, const flock_tensor* w, const float* x, int M, float* y);
+/* Device-resident timing of flock_op_gemm (activation conversion + GEMM per
+ * call), `iters` calls on a seeded device x; mean milliseconds per call. */
+FLOCK_API int flock_op_gemm_timed(flock_dev* dev, const flock_tensor* w, int M, int iters,
+                                  float* ms_per_call);
 /* kernels/rmsnorm.wgsl:41: n_vecs vectors of width n. */
 FLOCK_API int flock_op_rmsnorm(flock_dev* dev, const float* x, const float* g, int n, int n_vecs, float eps,
                      float* out);
