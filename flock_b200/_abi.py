@@ -26,6 +26,7 @@ FLOCK_Q8_0, FLOCK_Q4_0, FLOCK_F32 = 8, 4, 32
 FLOCK_ROPE_NEOX, FLOCK_ROPE_NORM = 0, 1
 FLOCK_ATTN_EXACT, FLOCK_ATTN_FAST = 0, 1
 FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT = 0, 1
+FLOCK_PREFILL_EXACT, FLOCK_PREFILL_BF16 = 0, 1
 
 
 class FlockError(RuntimeError):
@@ -41,7 +42,8 @@ class LayerConfigC(ctypes.Structure):
                 ("n_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
                 ("ffn", ctypes.c_int32), ("eps", ctypes.c_float), ("rope_base", ctypes.c_double),
                 ("max_keys", ctypes.c_int32), ("max_prefill", ctypes.c_int32),
-                ("rope_pairing", ctypes.c_int32), ("attention", ctypes.c_int32)]
+                ("rope_pairing", ctypes.c_int32), ("attention", ctypes.c_int32),
+                ("prefill", ctypes.c_int32)]
 
 
 _vp = ctypes.c_void_p
@@ -77,7 +79,7 @@ SIGNATURES = {
     "flock_op_matvec": [_vp, _vp, _fp, _i, _fp],
     "flock_op_matvec_timed": [_vp, _vp, _i, _i, _fp],
     "flock_op_gemm": [_vp, _vp, _fp, _i, _fp],
-    "flock_op_gemm_timed": [_vp, _vp, _i, _i, _fp],
+    "flock_op_gemm_timed": [_vp, _vp, _i, _i, _fp, _fp],
     "flock_op_rmsnorm": [_vp, _fp, _fp, _i, _i, _f, _fp],
     "flock_op_rope": [_vp, _fp, _i, _i, _i, _i, _fp, _i, _fp],
     "flock_op_swiglu": [_vp, _fp, _fp, _i64, _fp],

@@ -3,7 +3,13 @@
     python -m flock_b200.cases layer [--time]   # one decode layer (config 0 shape, 256-key cache)
     python -m flock_b200.cases head  [--time]   # the 151936 x 1024 Q8_0 head matvec
     python -m flock_b200.cases gemv  [--time]   # the config 1 matvec sweep (M = 1)
+    python -m flock_b200.cases sweep [--time]   # config 1: Q8_0/Q4_0 x shapes x M in {1,16,128,512}
+    python -m flock_b200.cases gemm  [--time]   # one M = 512 tensor-core GEMM (3072 x 1024)
     python -m flock_b200.cases model [--time] [--kernels] [--trace]
+    python -m flock_b200.cases prefill [--time] [--exact]
+                                                # config 3: 512-token prompt TTFT on the
+                                                # 28-layer model, tensor-core (default) or
+                                                # exact prefill, then 32 decode tokens
                                                 # 28-layer 0.6B-shape decode, persistent
                                                 # kernel (default) or per-op kernel graph
 
@@ -61,6 +67,67 @@ def gemv_case(timed: bool) -> None:
                 b = rows * cols * (1.0625 if q8 else 0.5625) + 4 * (rows + cols)
                 print(f"{'Q8_0' if q8 else 'Q4_0'} {rows}x{cols}: {ms * 1000:.2f} us "
                       f"{b / ms / 1e6:.1f} GB/s")
+
+
+def sweep_case(timed: bool) -> None:
+    """Config 1: M = 1 through the GEMV, M > 1 through the tensor-core GEMM
+    (activation conversion included); the per-token GEMV at M = 16 beside it."""
+    dev = flib.get_device(0)
+    if timed:
+        print("| wt | K x N | M | engine | us | GB/s | TFLOP/s |")
+        print("|---|---|---|---|---|---|---|")
+    for q8 in (True, False):
+        for rows, cols in SWEEP:
+            make = synth.q8_tensor if q8 else synth.q4_tensor
+            t = flib.GpuTensor.from_packed(dev, make(2, "t", rows, cols), rows, cols,
+                                           flib.FLOCK_Q8_0 if q8 else flib.FLOCK_Q4_0)
+            bpw = 1.0625 if q8 else 0.5625
+            runs = [(1, "gemv", lambda: (ops.matvec_timed(dev, t, 1, 50 if timed else 2), 0.0)),
+                    (16, "gemv", lambda: (ops.matvec_timed(dev, t, 16, 10 if timed else 1), 0.0))]
+            for m in (16, 128, 512):
+                runs.append((m, "tcgen05", lambda m=m: ops.gemm_timed(dev, t, m, 20 if timed else 1)))
+            for m, eng, f in runs:
+                ms, img = f()
+                if timed:
+                    b = rows * cols * bpw + 4 * cols * m + 4 * rows * m
+                    tf = 2.0 * m * rows * cols / (ms * 1e-3) / 1e12
+                    extra = f" (+{img * 1000:.1f} us x->bf16)" if img else ""
+                    print(f"| {'Q8_0' if q8 else 'Q4_0'} | {cols} x {rows} | {m} | {eng} | "
+                          f"{ms * 1000:.1f}{extra} | {b / ms / 1e6:.0f} | {tf:.1f} |")
+            t.free()
+
+
+def gemm_case(timed: bool) -> None:
+    dev = flib.get_device(0)
+    t = flib.GpuTensor.from_packed(dev, synth.q8_tensor(2, "t", 3072, 1024), 3072, 1024)
+    ms, _ = ops.gemm_timed(dev, t, 512, 20 if timed else 2)
+    if timed:
+        print(f"gemm 512 x 1024 x 3072: {ms * 1000:.1f} us, "
+              f"{2 * 512 * 1024 * 3072 / (ms * 1e-3) / 1e12:.1f} TFLOP/s")
+
+
+def prefill_case(timed: bool) -> None:
+    from .model import Model
+    dev = flib.get_device(0)
+    m = synth.model(300)
+    exact = "--exact" in sys.argv
+    cfg = QWEN3_06B.with_(attention="fast", max_keys=1024,
+                          prefill="exact" if exact else "bf16")
+    M = Model.create(dev, m, cfg)
+    prompt = synth.uniform_ids(300, "p512", 512, synth.QWEN3_06B.vocab).tolist()
+    M.step(prompt[:64])  # warm-up: kernels loaded, workspaces touched
+    M.reset()
+    dev.sync()
+    dev.timer_start()
+    first = M.step(prompt)
+    ttft = dev.timer_stop()
+    dev.timer_start()
+    M.decode_device(32)
+    dec = dev.timer_stop()
+    if timed:
+        print(f"prefill ({'exact' if exact else 'bf16 tensor cores'}): TTFT {ttft:.2f} ms for 512 "
+              f"tokens ({512 / ttft * 1000:.0f} tok/s), first id {first}; 32 decode tokens "
+              f"{dec / 32 * 1000:.1f} us/token")
 
 
 PHASES = ("qkv", "attention", "o_proj", "gate/up", "down")
@@ -121,5 +188,6 @@ def model_case(timed: bool) -> None:
 if __name__ == "__main__":
     case = sys.argv[1] if len(sys.argv) > 1 else "layer"
     timed = "--time" in sys.argv
-    {"layer": layer_case, "head": head_case, "gemv": gemv_case, "model": model_case}[case](timed)
+    {"layer": layer_case, "head": head_case, "gemv": gemv_case, "model": model_case,
+     "sweep": sweep_case, "gemm": gemm_case, "prefill": prefill_case}[case](timed)
     print("ok")

@@ -6,9 +6,12 @@
 #include <cstdarg>
 #include <cstring>
 #include <string>
+#include <mutex>
+#include <set>
 #include <vector>
 
 #include "attn_fast.cuh"
+#include "gemm_tc.cuh"
 #include "flock_internal.h"
 #include "gemv.cuh"
 #include "ops.cuh"
@@ -52,6 +55,19 @@ const char* const kTensorNames[W_COUNT] = {
 
 // ------------------------------------------------------------- launching
 
+int kernel_setup(const void* func, int max_dyn_smem) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  FLOCK_CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({func, dev})) return FLOCK_OK;
+  if (max_dyn_smem > 0)
+    FLOCK_CK(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn_smem));
+  done.insert({func, dev});
+  return FLOCK_OK;
+}
+
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_ex(cudaStream_t st, void (*k)(KArgs...), dim3 grid, dim3 block,
                              size_t smem, bool pdl, Args&&... args) {
@@ -72,12 +88,7 @@ template <int QT, int R, int EPI, int MX>
 static cudaError_t gemv_go(flock_dev* d, const GemvArgs& a, int ctas, bool pdl) {
   auto k = k_gemv<QT, R, EPI, MX>;
   const size_t smem = gemv_smem_bytes(a.K, a.norm_gain != nullptr);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  if (kernel_setup((const void*)k, 200 * 1024)) return cudaErrorInvalidValue;
   return launch_ex(d->stream, k, dim3(ctas, a.n_tokens), dim3(GEMV_THREADS), smem, pdl, a);
 }
 
@@ -203,6 +214,16 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count) {
   FLOCK_TRY(attn_part.alloc((size_t)nH * attn_split_cap * (hd + 2) * f));
   FLOCK_TRY(attn_count.alloc((size_t)nKV * 4));
   FLOCK_CK(cudaMemset(attn_count.p, 0, attn_count.bytes));
+  if (c.prefill == FLOCK_PREFILL_BF16) {
+    size_t ib = act_image_bytes(P, H);
+    const size_t iq = act_image_bytes(P, nH * hd), iff = act_image_bytes(P, F);
+    ib = ib > iq ? ib : iq;
+    ib = ib > iff ? ib : iff;
+    FLOCK_TRY(img.alloc(ib));
+    FLOCK_TRY(gu.alloc((size_t)P * 2 * F * f));
+    FLOCK_TRY(tc_err.alloc(16));
+    FLOCK_CK(cudaMemset(tc_err.p, 0, 16));
+  }
   return FLOCK_OK;
 }
 
@@ -228,6 +249,16 @@ static int check_cfg(const flock_layer_config& c) {
   if (c.max_keys < 1 || c.max_prefill < 1) {
     set_error("max_keys and max_prefill must be >= 1");
     return FLOCK_E_ARG;
+  }
+  if (c.prefill != FLOCK_PREFILL_EXACT && c.prefill != FLOCK_PREFILL_BF16) {
+    set_error("prefill mode %d is neither FLOCK_PREFILL_EXACT nor FLOCK_PREFILL_BF16", c.prefill);
+    return FLOCK_E_ARG;
+  }
+  if (c.prefill == FLOCK_PREFILL_BF16 &&
+      (c.hidden % 64 || c.ffn % 64 || c.hidden > 12288 || c.ffn > 12288)) {
+    set_error("bf16 prefill needs hidden %d and ffn %d multiples of 64, at most 12288", c.hidden,
+              c.ffn);
+    return FLOCK_E_UNSUPPORTED;
   }
   if (c.attention == FLOCK_ATTN_EXACT && c.max_keys > 48 * 1024) {
     set_error("exact decode attention holds every score on chip: max_keys %d > 49152; use "
@@ -269,7 +300,155 @@ int layer_init(flock_layer* L, flock_dev* dev, const flock_layer_config& cfg, Wo
   return FLOCK_OK;
 }
 
+// q/k norm + RoPE + KV append, then attention over n >= 1 queries in
+// attnRef / attnPrefillRef order (exact decode and all prefill steps).
+static int enqueue_qk_attn_exact(flock_layer* L, int n, bool pdl) {
+  flock_dev* d = L->dev;
+  Workspace* ws = L->ws;
+  const flock_layer_config& c = L->cfg;
+  QkArgs qa = {};
+  qa.q = ws->q.as<float>();
+  qa.k = ws->k.as<float>();
+  qa.v = ws->v.as<float>();
+  qa.q_norm = L->w[W_Q_NORM]->data.as<float>();
+  qa.k_norm = L->w[W_K_NORM]->data.as<float>();
+  qa.inv_freq = L->inv_freq.as<float>();
+  qa.qn = ws->qn.as<float>();
+  qa.kcache = L->kcache.as<float>();
+  qa.vcache = L->vcache.as<float>();
+  qa.ctl = L->ctl;
+  qa.n_tokens = n;
+  qa.n_heads = c.n_heads;
+  qa.n_kv_heads = c.n_kv_heads;
+  qa.head_dim = c.head_dim;
+  qa.eps = c.eps;
+  qa.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
+  pf_add(qa.pf, L->w[W_GATE]);
+  FLOCK_CK(launch_ex(d->stream, k_qk_norm_rope_append, dim3(n * (c.n_heads + c.n_kv_heads)),
+                     dim3(128), 0, pdl, qa));
+  AttnArgs aa = {};
+  aa.q = ws->qn.as<float>();
+  aa.kcache = L->kcache.as<float>();
+  aa.vcache = L->vcache.as<float>();
+  aa.out = ws->attn.as<float>();
+  aa.ctl = L->ctl;
+  aa.n_tokens = n;
+  aa.n_heads = c.n_heads;
+  aa.n_kv_heads = c.n_kv_heads;
+  aa.head_dim = c.head_dim;
+  pf_add(aa.pf, L->w[W_UP]);
+  if (n == 1) {
+    const size_t smem = (size_t)c.max_keys * sizeof(float);
+    FLOCK_TRY(kernel_setup((const void*)k_attn_decode_exact, 200 * 1024));
+    FLOCK_CK(launch_ex(d->stream, k_attn_decode_exact, dim3(c.n_heads), dim3(256), smem, pdl,
+                       aa));
+  } else {
+    FLOCK_CK(launch_ex(d->stream, k_attn_prefill_exact, dim3(c.n_heads, n), dim3(128), 0, pdl,
+                       aa));
+  }
+  return FLOCK_OK;
+}
+
+// SwiGLU over rows of [gate | up] (ops_ref.ts:103 swigluRef order).
+static __global__ void k_swiglu_rows(const float* gu, float* act, int n, int F) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)n * F) return;
+  const int64_t m = i / F, f = i - m * F;
+  const float g = gu[m * 2 * F + f], u = gu[m * 2 * F + F + f];
+  act[i] = fmul(fdiv(g, fadd(1.0f, exp_f64r(-g))), u);
+}
+
+// One prefill step of n > 1 tokens with the four weight matmuls on the
+// tcgen05 tensor cores (FLOCK_PREFILL_BF16); norms, RoPE, attention and the
+// residual adds keep their f32 arithmetic.
+static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
+  flock_dev* d = L->dev;
+  Workspace* ws = L->ws;
+  const flock_layer_config& c = L->cfg;
+  cudaStream_t st = d->stream;
+  const int qw = c.n_heads * c.head_dim, kvw = c.n_kv_heads * c.head_dim, H = c.hidden,
+            F = c.ffn;
+  uint8_t* img = ws->img.as<uint8_t>();
+  int* err = ws->tc_err.as<int>();
+  if (advance) {
+    k_ctl_advance<<<1, 1, 0, st>>>(L->ctl, n);
+    FLOCK_CK(cudaGetLastError());
+  }
+  {  // attn_norm + q/k/v
+    FLOCK_TRY(act_image_enqueue(st, ws->h.as<float>(), H, L->w[W_ATTN_NORM]->data.as<float>(),
+                                c.eps, n, H, img));
+    TcArgs a = {};
+    a.seg[0] = tc_seg_of(L->w[W_Q], ws->q.as<float>(), qw);
+    a.seg[1] = tc_seg_of(L->w[W_K], ws->k.as<float>(), kvw);
+    a.seg[2] = tc_seg_of(L->w[W_V], ws->v.as<float>(), kvw);
+    a.nseg = 3;
+    a.K = H;
+    a.M = n;
+    a.img = img;
+    a.err = err;
+    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_STORE, a));
+  }
+  FLOCK_TRY(enqueue_qk_attn_exact(L, n, false));
+  {  // o_proj + residual on h
+    FLOCK_TRY(act_image_enqueue(st, ws->attn.as<float>(), qw, nullptr, 0.0f, n, qw, img));
+    TcArgs a = {};
+    a.seg[0] = tc_seg_of(L->w[W_O], ws->h.as<float>(), H);
+    a.nseg = 1;
+    a.K = qw;
+    a.M = n;
+    a.img = img;
+    a.res = ws->h.as<float>();
+    a.res_stride = H;
+    a.err = err;
+    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_RESIDUAL, a));
+  }
+  {  // ffn_norm + gate | up, SwiGLU
+    FLOCK_TRY(act_image_enqueue(st, ws->h.as<float>(), H, L->w[W_FFN_NORM]->data.as<float>(),
+                                c.eps, n, H, img));
+    TcArgs a = {};
+    a.seg[0] = tc_seg_of(L->w[W_GATE], ws->gu.as<float>(), 2 * F);
+    a.seg[1] = tc_seg_of(L->w[W_UP], ws->gu.as<float>() + F, 2 * F);
+    a.nseg = 2;
+    a.K = H;
+    a.M = n;
+    a.img = img;
+    a.err = err;
+    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_STORE, a));
+    const int64_t total = (int64_t)n * F;
+    k_swiglu_rows<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(ws->gu.as<float>(),
+                                                                    ws->act.as<float>(), n, F);
+    FLOCK_CK(cudaGetLastError());
+  }
+  {  // down + residual on h
+    FLOCK_TRY(act_image_enqueue(st, ws->act.as<float>(), F, nullptr, 0.0f, n, F, img));
+    TcArgs a = {};
+    a.seg[0] = tc_seg_of(L->w[W_DOWN], ws->h.as<float>(), H);
+    a.nseg = 1;
+    a.K = F;
+    a.M = n;
+    a.img = img;
+    a.res = ws->h.as<float>();
+    a.res_stride = H;
+    a.err = err;
+    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_RESIDUAL, a));
+  }
+  return FLOCK_OK;
+}
+
+int ws_check_errors(Workspace* ws) {
+  if (!ws->tc_err.p) return FLOCK_OK;
+  int e = 0;
+  FLOCK_CK(cudaMemcpy(&e, ws->tc_err.p, 4, cudaMemcpyDeviceToHost));
+  if (e) {
+    cudaMemset(ws->tc_err.p, 0, 4);
+    set_error("tensor-core prefill GEMM gave up waiting (code %d)", e);
+    return FLOCK_E_CUDA;
+  }
+  return FLOCK_OK;
+}
+
 int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_next, bool pdl) {
+  if (n > 1 && L->cfg.prefill == FLOCK_PREFILL_BF16) return layer_enqueue_tc(L, n, advance);
   flock_dev* d = L->dev;
   Workspace* ws = L->ws;
   const flock_layer_config& c = L->cfg;
@@ -324,60 +503,11 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.combine = 1;
     pf_add(a.pf, L->w[W_GATE]);
     const size_t smem = attn_fast_smem(a.chunk_cap);
-    static bool attr = false;
-    if (!attr) {
-      FLOCK_CK(cudaFuncSetAttribute(k_attn_decode_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    200 * 1024));
-      attr = true;
-    }
+    FLOCK_TRY(kernel_setup((const void*)k_attn_decode_fast, 200 * 1024));
     FLOCK_CK(launch_ex(d->stream, k_attn_decode_fast, dim3(c.n_kv_heads, a.splits),
                        dim3(ATTN_FAST_THREADS), smem, pdl, a));
   } else {
-    QkArgs qa = {};
-    qa.q = ws->q.as<float>();
-    qa.k = ws->k.as<float>();
-    qa.v = ws->v.as<float>();
-    qa.q_norm = g_q;
-    qa.k_norm = g_k;
-    qa.inv_freq = L->inv_freq.as<float>();
-    qa.qn = ws->qn.as<float>();
-    qa.kcache = L->kcache.as<float>();
-    qa.vcache = L->vcache.as<float>();
-    qa.ctl = L->ctl;
-    qa.n_tokens = n;
-    qa.n_heads = c.n_heads;
-    qa.n_kv_heads = c.n_kv_heads;
-    qa.head_dim = c.head_dim;
-    qa.eps = c.eps;
-    qa.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
-    pf_add(qa.pf, L->w[W_GATE]);
-    FLOCK_CK(launch_ex(d->stream, k_qk_norm_rope_append, dim3(n * (c.n_heads + c.n_kv_heads)),
-                       dim3(128), 0, pdl, qa));
-    AttnArgs aa = {};
-    aa.q = ws->qn.as<float>();
-    aa.kcache = L->kcache.as<float>();
-    aa.vcache = L->vcache.as<float>();
-    aa.out = ws->attn.as<float>();
-    aa.ctl = L->ctl;
-    aa.n_tokens = n;
-    aa.n_heads = c.n_heads;
-    aa.n_kv_heads = c.n_kv_heads;
-    aa.head_dim = c.head_dim;
-    pf_add(aa.pf, L->w[W_UP]);
-    if (n == 1) {
-      const size_t smem = (size_t)c.max_keys * sizeof(float);
-      static bool attr = false;
-      if (!attr) {
-        FLOCK_CK(cudaFuncSetAttribute(k_attn_decode_exact,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr = true;
-      }
-      FLOCK_CK(launch_ex(d->stream, k_attn_decode_exact, dim3(c.n_heads), dim3(256), smem, pdl,
-                         aa));
-    } else {
-      FLOCK_CK(launch_ex(d->stream, k_attn_prefill_exact, dim3(c.n_heads, n), dim3(128), 0, pdl,
-                         aa));
-    }
+    FLOCK_TRY(enqueue_qk_attn_exact(L, n, pdl));
   }
   // 4. o_proj + residual, in place on h
   {
@@ -1062,7 +1192,7 @@ int flock_layer_read_output(flock_layer* L, int n, float* out) {
   FLOCK_CK(cudaMemcpyAsync(out, L->ws->h.p, (size_t)n * L->cfg.hidden * 4, cudaMemcpyDeviceToHost,
                            L->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(L->dev->stream));
-  return FLOCK_OK;
+  return ws_check_errors(L->ws);
 }
 
 int flock_layer_rewind(flock_layer* L, int n_keys) {
@@ -1088,7 +1218,7 @@ int flock_layer_read_cache(flock_layer* L, float* k, float* v) {
     FLOCK_CK(cudaMemcpyAsync(v, L->vcache.p, bytes, cudaMemcpyDeviceToHost, L->dev->stream));
   }
   FLOCK_CK(cudaStreamSynchronize(L->dev->stream));
-  return FLOCK_OK;
+  return ws_check_errors(L->ws);
 }
 
 int flock_layer_write_cache(flock_layer* L, const float* k, const float* v, int n_keys) {

@@ -59,9 +59,8 @@ void tc_finish_tiles(TcArgs& a) {
 
 template <int QT, int EPI>
 static int launch_tc(cudaStream_t st, const TcArgs& a) {
+  FLOCK_TRY(kernel_setup((const void*)k_gemm_tc<QT, EPI>, (int)gemm_tc_smem_bytes(TC_MAX_NT)));
   const size_t smem = gemm_tc_smem_bytes(a.Nt);
-  FLOCK_CK(cudaFuncSetAttribute(k_gemm_tc<QT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)gemm_tc_smem_bytes(TC_MAX_NT)));
   const dim3 grid((unsigned)a.tile0[a.nseg], (unsigned)((a.M + a.Nt - 1) / a.Nt));
   k_gemm_tc<QT, EPI><<<grid, TC_THREADS, smem, st>>>(a);
   FLOCK_CK(cudaGetLastError());
@@ -87,11 +86,13 @@ using namespace flock;
 
 namespace {
 
-// One op-level GEMM on device buffers: image + tensor-core GEMM.
+// One op-level GEMM on device buffers: image + tensor-core GEMM; `mid`, when
+// given, is recorded between the two kernels.
 int gemm_once(flock_dev* d, const flock_tensor* w, const float* x, int M, float* y, int* err,
-              uint8_t* img) {
+              uint8_t* img, cudaEvent_t mid = nullptr) {
   const int K = (int)w->cols;
   FLOCK_TRY(act_image_enqueue(d->stream, x, K, nullptr, 0.0f, M, K, img));
+  if (mid) FLOCK_CK(cudaEventRecord(mid, d->stream));
   TcArgs a = {};
   a.seg[0] = tc_seg_of(w, y, (int)w->rows);
   a.nseg = 1;
@@ -144,8 +145,9 @@ int flock_op_gemm(flock_dev* d, const flock_tensor* w, const float* x, int M, fl
   return FLOCK_OK;
 }
 
-int flock_op_gemm_timed(flock_dev* d, const flock_tensor* w, int M, int iters, float* ms_per_call) {
-  if (!d || iters < 1 || !ms_per_call) return FLOCK_E_ARG;
+int flock_op_gemm_timed(flock_dev* d, const flock_tensor* w, int M, int iters, float* ms_per_call,
+                        float* ms_image) {
+  if (!d || iters < 1 || !ms_per_call || !ms_image) return FLOCK_E_ARG;
   FLOCK_TRY(gemm_check_args(w, M));
   FLOCK_CK(cudaSetDevice(d->ordinal));
   std::vector<float> hx((size_t)M * w->cols);
@@ -164,15 +166,31 @@ int flock_op_gemm_timed(flock_dev* d, const flock_tensor* w, int M, int iters, f
   FLOCK_CK(cudaMemset(err.p, 0, 16));
   FLOCK_CK(cudaMemcpy(dx.p, hx.data(), dx.bytes, cudaMemcpyHostToDevice));
   FLOCK_TRY(gemm_once(d, w, dx.as<float>(), M, dy.as<float>(), err.as<int>(), img.as<uint8_t>()));
-  FLOCK_CK(cudaEventRecord(d->t0, d->stream));
-  for (int i = 0; i < iters; i++)
-    FLOCK_TRY(gemm_once(d, w, dx.as<float>(), M, dy.as<float>(), err.as<int>(),
-                        img.as<uint8_t>()));
-  FLOCK_CK(cudaEventRecord(d->t1, d->stream));
-  FLOCK_CK(cudaEventSynchronize(d->t1));
-  float ms = 0;
-  FLOCK_CK(cudaEventElapsedTime(&ms, d->t0, d->t1));
-  *ms_per_call = ms / iters;
+  // per call: [start] image [mid] GEMM [end], each pair timed on the device
+  std::vector<cudaEvent_t> ev(3 * (size_t)iters, nullptr);
+  for (auto& e : ev) FLOCK_CK(cudaEventCreate(&e));
+  int rc = FLOCK_OK;
+  for (int i = 0; i < iters && !rc; i++) {
+    FLOCK_CK(cudaEventRecord(ev[3 * i], d->stream));
+    rc = gemm_once(d, w, dx.as<float>(), M, dy.as<float>(), err.as<int>(), img.as<uint8_t>(),
+                   ev[3 * i + 1]);
+    if (!rc) FLOCK_CK(cudaEventRecord(ev[3 * i + 2], d->stream));
+  }
+  float gemm = 0, image = 0;
+  if (!rc) {
+    FLOCK_CK(cudaStreamSynchronize(d->stream));
+    for (int i = 0; i < iters; i++) {
+      float a = 0, b = 0;
+      FLOCK_CK(cudaEventElapsedTime(&a, ev[3 * i], ev[3 * i + 1]));
+      FLOCK_CK(cudaEventElapsedTime(&b, ev[3 * i + 1], ev[3 * i + 2]));
+      image += a;
+      gemm += b;
+    }
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  FLOCK_TRY(rc);
+  *ms_per_call = gemm / iters;
+  *ms_image = image / iters;
   return check_tc_err(err);
 }
 

@@ -16,6 +16,11 @@ namespace flock {
 
 void set_error(const char* fmt, ...);
 
+// Per (kernel, current device), once: when max_dyn_smem > 0, opt in to that
+// much dynamic shared memory (the attribute is per device, so a process
+// driving several GPUs needs it on each).
+int kernel_setup(const void* func, int max_dyn_smem);
+
 // Device references (see flock_dev): retain returns its argument.
 flock_dev* dev_retain(flock_dev* d);
 void dev_release(flock_dev* d);
@@ -84,6 +89,7 @@ struct Workspace {
   DBuf attn_part, attn_count;  // fast decode attention partials
   int attn_splits = 16;         // splits: SMs / kv heads, so one wave covers them
   int attn_split_cap = 32;      // partial slots allocated per head (attn_max_splits' bound)
+  DBuf img, gu, tc_err;         // bf16 prefill: activation image, gate|up rows, error word
   int alloc(const flock_layer_config& c, int sm_count);
 };
 
@@ -101,6 +107,9 @@ int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float
                       int M, int K, uint8_t* img);
 int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a);
 TcSeg tc_seg_of(const flock_tensor* t, float* out, int out_stride);
+// bf16 prefill's device error word: FLOCK_E_CUDA (and cleared) if a tensor-core
+// GEMM gave up waiting since the last check; call after a synchronisation.
+int ws_check_errors(Workspace* ws);
 int gemv_grid(flock_dev* d, int total_groups);
 
 }  // namespace flock

@@ -265,8 +265,7 @@ int mk_prepare(flock_model* m) {
   a.ctl = m->ctl.as<int>();
   a.bar = m->mk_bar.as<unsigned>();
   a.err = m->mk_err.as<int>();
-  FLOCK_CK(cudaFuncSetAttribute(k_decode_mk, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)smem));
+  FLOCK_TRY(kernel_setup((const void*)k_decode_mk, (int)smem));
   int per_sm = 0;
   FLOCK_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mk, MK_THREADS, smem));
   if (per_sm < 1) return FLOCK_OK;
@@ -292,7 +291,10 @@ int enqueue_mk(flock_model* m) {
   return FLOCK_OK;
 }
 
-int check_mk_error(flock_model* m) {
+// The device error words of the persistent kernel and the bf16 prefill
+// GEMMs; call after a synchronisation.
+int check_device_errors(flock_model* m) {
+  FLOCK_TRY(ws_check_errors(&m->ws));
   if (!m->mk_ok || m->decode_mode != FLOCK_DECODE_PERSISTENT) return FLOCK_OK;
   int err = 0;
   FLOCK_CK(cudaMemcpy(&err, m->mk_err.p, 4, cudaMemcpyDeviceToHost));
@@ -519,7 +521,7 @@ int flock_model_step(flock_model* m, const int32_t* ids, int n, int32_t* next_id
   for (auto* L : m->layers) L->n_keys = m->pos;
   FLOCK_CK(cudaMemcpyAsync(next_id, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return check_mk_error(m);
+  return check_device_errors(m);
 }
 
 int flock_model_decode_device(flock_model* m, int n_steps, int32_t* out_ids) {
@@ -536,7 +538,7 @@ int flock_model_decode_device(flock_model* m, int n_steps, int32_t* out_ids) {
     FLOCK_CK(cudaMemcpyAsync(out_ids, m->hist.as<int32_t>() + start, (size_t)n_steps * 4,
                              cudaMemcpyDeviceToHost, m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return check_mk_error(m);
+  return check_device_errors(m);
 }
 
 int flock_model_generate(flock_model* m, const int32_t* prompt, int n_prompt, int max_tokens,
@@ -573,7 +575,7 @@ int flock_model_hidden_state(flock_model* m, const int32_t* ids, int n, float* o
   FLOCK_CK(cudaMemcpyAsync(out, m->ws.h.as<float>() + (size_t)(last - 1) * m->cfg.hidden,
                            (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost, m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return FLOCK_OK;
+  return check_device_errors(m);
 }
 
 int flock_model_normed_state(flock_model* m, const int32_t* ids, int n, float* out) {
@@ -591,7 +593,7 @@ int flock_model_normed_state(flock_model* m, const int32_t* ids, int n, float* o
   FLOCK_CK(cudaMemcpyAsync(out, m->normed.p, (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost,
                            m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return FLOCK_OK;
+  return check_device_errors(m);
 }
 
 int flock_model_embed(flock_model* m, const int32_t* ids, int n, float* out) {
@@ -603,7 +605,7 @@ int flock_model_embed(flock_model* m, const int32_t* ids, int n, float* out) {
   FLOCK_CK(cudaMemcpyAsync(out, m->ws.h.p, (size_t)n * m->cfg.hidden * 4, cudaMemcpyDeviceToHost,
                            m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return FLOCK_OK;
+  return check_device_errors(m);
 }
 
 int flock_model_encode_partial(flock_model* m, const int32_t* ids, int n, int offset, float* out) {
@@ -624,7 +626,7 @@ int flock_model_encode_partial(flock_model* m, const int32_t* ids, int n, int of
   FLOCK_CK(cudaMemcpyAsync(out, m->ws.h.p, (size_t)n * m->cfg.hidden * 4, cudaMemcpyDeviceToHost,
                            m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return FLOCK_OK;
+  return check_device_errors(m);
 }
 
 int flock_model_project_hidden(flock_model* m, const float* flat, int seq, int32_t* next_id) {
@@ -636,20 +638,20 @@ int flock_model_project_hidden(flock_model* m, const float* flat, int seq, int32
   FLOCK_TRY(enqueue_head(m, 0));
   FLOCK_CK(cudaMemcpyAsync(next_id, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return FLOCK_OK;
+  return check_device_errors(m);
 }
 
 int flock_model_set_token(flock_model* m, int32_t id) {
   if (!m || id < 0 || id >= m->vocab) return FLOCK_E_ARG;
   FLOCK_CK(cudaMemcpyAsync(m->ids.p, &id, 4, cudaMemcpyHostToDevice, m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return FLOCK_OK;
+  return check_device_errors(m);
 }
 
 int flock_model_current_token(flock_model* m, int32_t* out) {
   FLOCK_CK(cudaMemcpyAsync(out, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return FLOCK_OK;
+  return check_device_errors(m);
 }
 
 }  // extern "C"
@@ -719,7 +721,7 @@ int flock_model_history(flock_model* m, int start, int n, int32_t* out) {
     FLOCK_CK(cudaMemcpyAsync(out, m->hist.as<int32_t>() + start, (size_t)n * 4,
                              cudaMemcpyDeviceToHost, m->dev->stream));
   FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
-  return FLOCK_OK;
+  return check_device_errors(m);
 }
 
 }  // extern "C"

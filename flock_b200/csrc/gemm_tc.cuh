@@ -8,9 +8,10 @@
 //  * Operands are swapped for small M: 128 weight rows form the MMA's M and
 //    up to 256 tokens its N, so a 16-token prefill still issues full-height
 //    tcgen05.mma.cta_group::1.kind::f16 (128 x Nt x 16) instructions.
-//  * Producers (4 warps, one weight row per thread) keep 4 K-tiles of raw
-//    int8 / nibble weights in flight in registers, dequantise q * s in f32,
-//    round to bf16 and write the K-major 128-byte-swizzled layout the UMMA
+//  * Producers (8 warps, two threads per weight row: one 32-weight block each
+//    per K-tile) keep 6 K-tiles of raw int8 / nibble weights in flight in
+//    registers, dequantise q * s in f32 (packed f32x2), round to bf16 and
+//    write the K-major 128-byte-swizzled layout the UMMA
 //    shared-memory descriptor names (8-row x 128-byte atoms, 16-byte chunk
 //    c of row r at (c ^ r % 8)).  int8 values are exact in bf16, so the only
 //    weight rounding is that of the scaled value.
@@ -19,9 +20,10 @@
 //    K-tile contiguous), so each stage's B tile is one bulk copy.
 //  * One thread issues the MMAs; tcgen05.commit returns each stage to the
 //    producers through an mbarrier and signals the epilogue after the last
-//    K-tile.  The epilogue warps read the accumulator with tcgen05.ld
-//    (32 lanes x 32 bit: one weight row per thread, one token per column)
-//    and store coalesced rows of Y, optionally adding a residual.
+//    K-tile.  The 8 producer warps then read the accumulator with tcgen05.ld
+//    (32 lanes x 32 bit: one weight row per thread, one token per column;
+//    warps w and w+4 share a lane quarter and split the columns) and store
+//    coalesced rows of Y, optionally adding a residual.
 //
 // Every wait is bounded (mbar_wait); on a timeout the kernel sets *err,
 // still releases its tensor memory and returns.  No multicast is used.
@@ -38,10 +40,10 @@ constexpr int TC_ROWS = 128;              // weight rows per CTA: the MMA's M
 constexpr int TC_KT = 64;                 // K per stage: one 128-byte bf16 swizzle atom row
 constexpr int TC_STAGES = 4;
 constexpr int TC_MAX_NT = 256;            // tokens per CTA: the MMA's N
-constexpr int TC_PRODUCERS = 128;         // 4 warps: producers, then the epilogue
+constexpr int TC_PRODUCERS = 256;         // 8 warps: producers, then the epilogue
 constexpr int TC_THREADS = TC_PRODUCERS + 32;  // + the MMA warp
 constexpr int TC_A_BYTES = TC_ROWS * TC_KT * 2;  // 16 KiB of bf16 per stage
-constexpr int TC_PREFETCH = 4;            // K-tiles of raw weights in flight per thread
+constexpr int TC_PREFETCH = 6;            // K-tiles of raw weights in flight per thread
 
 struct TcSeg {
   const uint8_t* qs;
@@ -136,58 +138,69 @@ FLOCK_DEV uint32_t bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Raw weights of one row for one K-tile (64 weights) and their two scales.
+// Raw weights of one block (32 weights) of a row for one K-tile.
 struct TcRaw {
-  uint4 q[4];   // Q8: 64 int8; Q4: q[0..1] = two 16-byte nibble blocks
-  uint32_t s;   // two f16 scales
+  uint4 q[2];   // Q8: 32 int8; Q4: q[0] = the 16-byte nibble block
+  uint32_t s;   // the f16 scale (low 16 bits)
 };
 
+// Block `half` (0/1) of row `row` in K-tile kt.
 template <int QT>
-FLOCK_DEV void tc_load_raw(TcRaw& r, const TcSeg& sg, int K, int row, int kt) {
-  const uint4* p;
+FLOCK_DEV void tc_load_raw(TcRaw& r, const TcSeg& sg, int K, int row, int half, int kt) {
   if (QT == QT_Q8) {
-    p = reinterpret_cast<const uint4*>(sg.qs + (size_t)row * K + (size_t)kt * TC_KT);
+    const uint4* p = reinterpret_cast<const uint4*>(sg.qs + (size_t)row * K + (size_t)kt * TC_KT +
+                                                    half * 32);
     r.q[0] = ldg_stream(p);
     r.q[1] = ldg_stream(p + 1);
-    r.q[2] = ldg_stream(p + 2);
-    r.q[3] = ldg_stream(p + 3);
   } else {
-    p = reinterpret_cast<const uint4*>(sg.qs + (size_t)row * (K / 2) + (size_t)kt * (TC_KT / 2));
-    r.q[0] = ldg_stream(p);
-    r.q[1] = ldg_stream(p + 1);
+    r.q[0] = ldg_stream(reinterpret_cast<const uint4*>(sg.qs + (size_t)row * (K / 2) +
+                                                       (size_t)kt * (TC_KT / 2) + half * 16));
   }
-  r.s = __ldg(reinterpret_cast<const uint32_t*>(sg.sc + (size_t)row * sg.sc_stride + kt * 2));
+  r.s = __ldg(sg.sc + (size_t)row * sg.sc_stride + kt * 2 + half);
 }
 
-// Dequantise one row's K-tile into its 128-byte swizzled row of the A stage.
+// bf16(q * s) for the four int8 / nibble values of word u, two per packed op.
+FLOCK_DEV uint2 tc_dequant4(uint32_t u, uint64_t bias2, uint64_t s2) {
+  const uint64_t a = fmul2(fsub2(pack2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u)),
+                                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541u))),
+                                 bias2),
+                           s2);
+  const uint64_t b = fmul2(fsub2(pack2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542u)),
+                                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543u))),
+                                 bias2),
+                           s2);
+  const float2 fa = unpack2(a), fb = unpack2(b);
+  return make_uint2(bf16x2(fa.x, fa.y), bf16x2(fb.x, fb.y));
+}
+
+// Dequantise one block into chunks 4*half .. 4*half+3 of row t's swizzled
+// 128-byte row of the A stage.  The integers come out exact (2^23 + bias
+// trick), then q * s rounds once in f32 and once to bf16.
 template <int QT>
-FLOCK_DEV void tc_store_row(const TcRaw& r, uint8_t* A, int t) {
-  const float s0 = scale_f16((uint16_t)(r.s & 0xFFFFu)), s1 = scale_f16((uint16_t)(r.s >> 16));
+FLOCK_DEV void tc_store_block(const TcRaw& r, uint8_t* A, int t, int half) {
+  const float s = scale_f16((uint16_t)(r.s & 0xFFFFu));
+  const uint64_t s2 = pack2(s, s);
 #pragma unroll
-  for (int c = 0; c < 8; c++) {
-    float v[8];
+  for (int cc = 0; cc < 4; cc++) {
+    uint32_t w0, w1;
+    uint64_t bias2;
     if (QT == QT_Q8) {
-      const uint4 w = r.q[c >> 1];
-      const uint32_t w0 = (c & 1) ? w.z : w.x, w1 = (c & 1) ? w.w : w.y;
-      dec_i8x4(w0, v[0], v[1], v[2], v[3]);
-      dec_i8x4(w1, v[4], v[5], v[6], v[7]);
+      // weights 8cc..8cc+7 of the block; int8 -> u8 by flipping the sign bit
+      const uint4 w = r.q[cc >> 1];
+      w0 = ((cc & 1) ? w.z : w.x) ^ 0x80808080u;
+      w1 = ((cc & 1) ? w.w : w.y) ^ 0x80808080u;
+      bias2 = pack2(8388736.0f, 8388736.0f);  // 2^23 + 128
     } else {
-      // block c / 4; weights j0..j0+7 of it: low nibbles of bytes j0.. (j0 < 16)
-      // or high nibbles of bytes j0-16.. (q4_coop.wgsl: byte i = weights i, i+16)
-      const uint4 w = r.q[c >> 2];
-      const int j0 = (c & 3) * 8;
-      const uint32_t b0 = (j0 & 15) == 0 ? w.x : w.z, b1 = (j0 & 15) == 0 ? w.y : w.w;
-      const int sh = j0 < 16 ? 0 : 4;
-      dec_nib4((b0 >> sh) & 0x0F0F0F0Fu, v[0], v[1], v[2], v[3]);
-      dec_nib4((b1 >> sh) & 0x0F0F0F0Fu, v[4], v[5], v[6], v[7]);
+      // q4_coop.wgsl: byte i holds weights i (low nibble) and i+16 (high);
+      // weights 8cc..8cc+7 are nibbles of bytes 8(cc&1).. , high for cc >= 2
+      const uint4 w = r.q[0];
+      const int sh = cc < 2 ? 0 : 4;
+      w0 = (((cc & 1) ? w.z : w.x) >> sh) & 0x0F0F0F0Fu;
+      w1 = (((cc & 1) ? w.w : w.y) >> sh) & 0x0F0F0F0Fu;
+      bias2 = pack2(8388616.0f, 8388616.0f);  // 2^23 + 8
     }
-    const float s = c < 4 ? s0 : s1;
-    uint4 o;
-    o.x = bf16x2(v[0] * s, v[1] * s);
-    o.y = bf16x2(v[2] * s, v[3] * s);
-    o.z = bf16x2(v[4] * s, v[5] * s);
-    o.w = bf16x2(v[6] * s, v[7] * s);
-    *reinterpret_cast<uint4*>(A + sw128_off(t, c)) = o;
+    const uint2 lo = tc_dequant4(w0, bias2, s2), hi = tc_dequant4(w1, bias2, s2);
+    *reinterpret_cast<uint4*>(A + sw128_off(t, 4 * half + cc)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
   }
 }
 
@@ -222,7 +235,7 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
   }
   __syncthreads();
   const uint32_t ncols = (uint32_t)tc_tmem_cols(Nt);
-  if (warp == 4) {
+  if (warp == TC_PRODUCERS / 32) {
     tmem_alloc(tslot, ncols);
     tmem_relinquish();
   }
@@ -238,16 +251,16 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
   const int mb = blockIdx.y, m0 = mb * Nt;
   const int KT = a.K / TC_KT;
 
-  if (warp < 4) {
+  if (warp < TC_PRODUCERS / 32) {
     // ------------------------------------------------------------ producers
-    const int t = threadIdx.x;
+    const int t = threadIdx.x & (TC_ROWS - 1), half = threadIdx.x >> 7;
     const int row = row0 + t;
     const bool rv = row < sg.rows;
     const int lrow = rv ? row : sg.rows - 1;  // rows past the end load a real row, store nothing
     TcRaw ring[TC_PREFETCH];
 #pragma unroll
     for (int j = 0; j < TC_PREFETCH; j++)
-      if (j < KT) tc_load_raw<QT>(ring[j], sg, a.K, lrow, j);
+      if (j < KT) tc_load_raw<QT>(ring[j], sg, a.K, lrow, half, j);
     bool ok = true;
     for (int kt0 = 0; kt0 < KT && ok; kt0 += TC_PREFETCH) {
 #pragma unroll
@@ -262,13 +275,14 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
           break;
         }
         uint8_t* A = tsm + (size_t)st * stage_bytes;
-        if (t == 0) {
+        if (threadIdx.x == 0) {
           mbar_expect_tx_only(&full[st], (uint32_t)b_bytes);
           bulk_g2s(A + TC_A_BYTES, a.img + ((size_t)mb * KT + kt) * (size_t)b_bytes,
                    (uint32_t)b_bytes, &full[st]);
         }
-        tc_store_row<QT>(ring[j], A, t);
-        if (kt + TC_PREFETCH < KT) tc_load_raw<QT>(ring[j], sg, a.K, lrow, kt + TC_PREFETCH);
+        tc_store_block<QT>(ring[j], A, t, half);
+        if (kt + TC_PREFETCH < KT)
+          tc_load_raw<QT>(ring[j], sg, a.K, lrow, half, kt + TC_PREFETCH);
         fence_proxy_async_smem();
         mbar_arrive(&full[st]);
       }
@@ -276,8 +290,8 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
     // ------------------------------------------------------------- epilogue
     if (!mbar_wait(done, 0, a.err)) atomicCAS(a.err, 0, 1);
     tc_fence_after();
-    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-    for (int c0 = 0; c0 < Nt; c0 += 16) {
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    for (int c0 = 16 * half; c0 < Nt; c0 += 32) {
       float v[16];
       tmem_ld16(tmem + lane_base + (uint32_t)c0, v);
       if (rv) {
@@ -313,7 +327,7 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == TC_PRODUCERS / 32) {
     tc_fence_after();
     tmem_dealloc(tmem, ncols);
   }

@@ -60,13 +60,16 @@ FLOCK_DEV bool mbar_try_wait_sleep(uint64_t* b, uint32_t parity, uint32_t hint_n
 }
 
 // Bounded wait: false after WAIT_NS of global time (or WAIT_MAX_POLLS polls),
-// or as soon as *err is set when `watch_err`.  Each poll may sleep up to
-// WAIT_SLEEP_NS.
+// or as soon as *err is set when `watch_err`.  The first WAIT_SPIN polls
+// return at once (short waits stay short); later polls may sleep up to
+// WAIT_SLEEP_NS so a long-waiting warp yields its issue slots.
 constexpr uint32_t WAIT_SLEEP_NS = 20000;
+constexpr uint32_t WAIT_SPIN = 4096;
 FLOCK_DEV bool mbar_wait(uint64_t* b, uint32_t parity, const int* err, bool watch_err = true) {
   uint64_t t0 = 0;
   for (uint32_t i = 0; i < WAIT_MAX_POLLS; i++) {
-    if (mbar_try_wait_sleep(b, parity, WAIT_SLEEP_NS)) return true;
+    if (i < WAIT_SPIN ? mbar_try_wait(b, parity) : mbar_try_wait_sleep(b, parity, WAIT_SLEEP_NS))
+      return true;
     if ((i & 63) == 63) {
       if (watch_err && *(volatile const int*)err) return false;
       const uint64_t now = globaltimer_ns();

@@ -54,11 +54,13 @@ def gemm(dev: Device, w: GpuTensor, x: np.ndarray, m: int) -> np.ndarray:
     return out
 
 
-def gemm_timed(dev: Device, w: GpuTensor, m: int, iters: int = 20) -> float:
-    """Mean ms per device-resident tensor-core GEMM (activation image + GEMM)."""
-    ms = ctypes.c_float()
-    _abi.call("flock_op_gemm_timed", dev.handle, w.handle, m, iters, ctypes.byref(ms))
-    return ms.value
+def gemm_timed(dev: Device, w: GpuTensor, m: int, iters: int = 20) -> tuple:
+    """(GEMM kernel ms, activation-conversion ms), means over device-resident
+    calls timed with CUDA events around each kernel."""
+    ms, img = ctypes.c_float(), ctypes.c_float()
+    _abi.call("flock_op_gemm_timed", dev.handle, w.handle, m, iters, ctypes.byref(ms),
+              ctypes.byref(img))
+    return ms.value, img.value
 
 
 def rmsnorm(dev: Device, x, g, n: int, n_vecs: int, eps: float) -> np.ndarray:

@@ -55,6 +55,10 @@ extern "C" {
 #define FLOCK_ATTN_EXACT 0 /* decode attention in attnRef's exact order (ops_ref.ts:135) */
 #define FLOCK_ATTN_FAST 1  /* split-K flash-decode; no key cap; tolerance 1e-5 rel */
 
+#define FLOCK_PREFILL_EXACT 0 /* prefill matmuls in the reference's f32 order (bit-exact) */
+#define FLOCK_PREFILL_BF16 1  /* prefill matmuls on the tcgen05 tensor cores: bf16 operands,
+                                 f32 accumulation, max relative error 1e-2 */
+
 typedef struct flock_dev flock_dev;
 typedef struct flock_tensor flock_tensor;
 typedef struct flock_layer flock_layer;
@@ -76,6 +80,7 @@ typedef struct flock_layer_config {
   int32_t max_prefill;  /* largest prefill batch (sizes activations) */
   int32_t rope_pairing; /* FLOCK_ROPE_NEOX | FLOCK_ROPE_NORM */
   int32_t attention;    /* FLOCK_ATTN_EXACT | FLOCK_ATTN_FAST */
+  int32_t prefill;      /* FLOCK_PREFILL_EXACT | FLOCK_PREFILL_BF16 (multi-token steps) */
 } flock_layer_config;
 
 /* ------------------------------------------------------------- errors/dev */
@@ -142,10 +147,11 @@ FLOCK_API int flock_op_matvec_timed(flock_dev* dev, const flock_tensor* w, int n
  * prefill path: max relative error <= 1e-2).  x is [M][cols],
  * y [M][rows]; cols must be a multiple of 64 and at most 12288. */
 FLOCK_API int flock_op_gemm(flock_dev* dev, const flock_tensor* w, const float* x, int M, float* y);
-/* Device-resident timing of flock_op_gemm (activation conversion + GEMM per
- * call), `iters` calls on a seeded device x; mean milliseconds per call. */
+/* Device-resident timing of flock_op_gemm over `iters` calls on a seeded
+ * device x, CUDA events around each kernel: mean milliseconds of the GEMM
+ * kernel and of the activation conversion before it. */
 FLOCK_API int flock_op_gemm_timed(flock_dev* dev, const flock_tensor* w, int M, int iters,
-                                  float* ms_per_call);
+                                  float* ms_per_call, float* ms_image);
 /* kernels/rmsnorm.wgsl:41: n_vecs vectors of width n. */
 FLOCK_API int flock_op_rmsnorm(flock_dev* dev, const float* x, const float* g, int n, int n_vecs, float eps,
                      float* out);
