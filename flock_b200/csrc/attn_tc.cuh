@@ -1,0 +1,241 @@
+// Causal GQA prefill attention on the tcgen05 tensor cores, for the bf16
+// prefill path -- kernels/attention_prefill.wgsl:75 / head_ref.ts:99
+// attnPrefillRef (queries at positions pos0 .. pos0+n-1, query i sees keys
+// 0 .. pos0+i, scale 1/sqrt(head_dim), max-subtracted softmax), re-designed:
+//
+//  * one CTA per (128-query tile, query head); 4 warps; thread t owns query
+//    row t of the tile, which is TMEM lane t of every accumulator, so a row's
+//    max and sum need no cross-thread reduction (tcgen05.ld 32x32b);
+//  * q, K and V are staged as bf16 in the K-major 128-byte-swizzled layout
+//    (head_dim 128 = two 64-wide swizzle chunks); V is transposed while it is
+//    staged ([head_dim][keys]) so both products read K-major operands;
+//  * pass 1: S = q K^T per 128-key tile (tcgen05.mma 128x128x16, f32 in
+//    TMEM) -> exact row max m;  pass 2: S again, P = e^(S*scale - m) written
+//    as bf16 into shared memory, O += P V^T accumulated in TMEM, l += sum P;
+//    the extra q K^T replaces any rescaling of O;
+//  * out = O / l in f32.
+//
+// Waits are bounded (mbar_wait); on a timeout the kernel sets *err, frees its
+// tensor memory and returns.  No multicast is used.
+#pragma once
+#include "gemm_tc.cuh"
+
+namespace flock {
+
+constexpr int ATC_Q = 128;        // queries per CTA
+constexpr int ATC_K = 128;        // keys per tile
+constexpr int ATC_HD = 128;       // head_dim (two 64-wide swizzle chunks)
+constexpr int ATC_THREADS = 128;
+constexpr int ATC_OPND = ATC_Q * ATC_HD * 2;  // bytes of one 128 x 128 bf16 operand (32 KiB)
+
+struct AttnTcArgs {
+  const float* q;  // [n][nH][hd] normalised + rotated
+  const float* kcache;
+  const float* vcache;
+  float* out;      // [n][nH][hd]
+  const int* ctl;  // ctl[0] = pos0 (keys before this batch)
+  int n_tokens, n_heads, n_kv_heads;
+  int* err;
+};
+
+// Byte offset of element (row r, column c) -- c < 128 -- in a 128-row operand
+// of two 64-column swizzled chunks (16 KiB each).
+FLOCK_DEV uint32_t atc_off(int r, int chunk16) {
+  return (uint32_t)(chunk16 >> 3) * (ATC_Q * 128) + sw128_off(r, chunk16 & 7);
+}
+
+// Row r of a 128 x 128 bf16 operand from 128 f32 values at `src` (global),
+// or zeros.
+FLOCK_DEV void atc_stage_row(uint8_t* op, int r, const float* src) {
+#pragma unroll 4
+  for (int c = 0; c < 16; c++) {
+    uint4 o = make_uint4(0, 0, 0, 0);
+    if (src) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(src) + 2 * c);
+      const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 2 * c + 1);
+      o = make_uint4(bf16x2(a.x, a.y), bf16x2(a.z, a.w), bf16x2(b.x, b.y), bf16x2(b.z, b.w));
+    }
+    *reinterpret_cast<uint4*>(op + atc_off(r, c)) = o;
+  }
+}
+
+// D (TMEM, 128 lanes x 128 columns) (+)= A . B^T over 128 K elements, both
+// 128 x 128 bf16 operands in the two-chunk swizzled layout.
+FLOCK_DEV void atc_mma(uint32_t d, uint32_t a, uint32_t b, bool accumulate) {
+  const uint32_t idesc = umma_idesc_bf16(128, 128);
+#pragma unroll
+  for (int k16 = 0; k16 < 8; k16++) {
+    const uint32_t off = (uint32_t)(k16 >> 2) * (ATC_Q * 128) + (uint32_t)(k16 & 3) * 32;
+    umma_bf16(d, umma_desc_sw128(a + off), umma_desc_sw128(b + off), idesc,
+              (accumulate || k16 > 0) ? 1u : 0u);
+  }
+}
+
+static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const AttnTcArgs a) {
+  extern __shared__ __align__(16) uint8_t asm_raw[];
+  uint8_t* base = asm_raw + ((1024u - (smem_u32(asm_raw) & 1023u)) & 1023u);
+  uint8_t* sQ = base;
+  uint8_t* sK = sQ + ATC_OPND;
+  uint8_t* sV = sK + ATC_OPND;  // V^T: [head_dim][keys]
+  uint8_t* sP = sV + ATC_OPND;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + ATC_OPND);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+  __shared__ int s_stop;
+
+  const int t = threadIdx.x, warp = t >> 5;
+  const int h = blockIdx.y, q0 = blockIdx.x * ATC_Q;
+  const int G = a.n_heads / a.n_kv_heads, g = h / G;
+  const size_t kvs = (size_t)a.n_kv_heads * ATC_HD;
+  const int pos0 = a.ctl[0];
+  const int qi = q0 + t;                   // this thread's query
+  const int qpos = pos0 + qi;              // its position: sees keys 0..qpos
+  const int last_q = min(q0 + ATC_Q, a.n_tokens) - 1;
+  const int kend = pos0 + last_q + 1;      // keys any query of the tile sees
+  const int n_tiles = (kend + ATC_K - 1) / ATC_K;
+  const float scale = __double2float_rn(1.0 / sqrt((double)ATC_HD));
+
+  if (t == 0) {
+    mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_stop = 0;
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 256);
+    tmem_relinquish();
+  }
+  // q tile (rows past n are zeros)
+  atc_stage_row(sQ, t, qi < a.n_tokens ? a.q + ((size_t)qi * a.n_heads + h) * ATC_HD : nullptr);
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+  uint32_t phase = 0;
+  bool ok = true;
+
+  auto stage_k = [&](int k0) {
+    const int key = k0 + t;
+    atc_stage_row(sK, t, key < kend ? a.kcache + (size_t)key * kvs + (size_t)g * ATC_HD : nullptr);
+  };
+  auto stage_vt = [&](int k0) {
+    // thread t = head_dim column t: keys k0.. of that column, 8 per chunk
+    const float* src = a.vcache + (size_t)g * ATC_HD + t;
+#pragma unroll 2
+    for (int c = 0; c < 16; c++) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const int key = k0 + 8 * c + e;
+        v[e] = key < kend ? __ldg(src + (size_t)key * kvs) : 0.0f;
+      }
+      *reinterpret_cast<uint4*>(sV + atc_off(t, c)) =
+          make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]), bf16x2(v[6], v[7]));
+    }
+  };
+  // issue S = q K^T (thread 0) and wait for it (everyone)
+  auto scores = [&]() {
+    if (t == 0) {
+      tc_fence_after();
+      atc_mma(tS, smem_u32(sQ), smem_u32(sK), false);
+      umma_commit(bar);
+    }
+    if (!mbar_wait(bar, phase, a.err)) {
+      atomicCAS(a.err, 0, 1);
+      s_stop = 1;
+    }
+    phase ^= 1;
+    tc_fence_after();
+  };
+
+  // ---------------------------------------------------------------- pass 1
+  float m = -INFINITY;
+  for (int kt = 0; kt < n_tiles && ok; kt++) {
+    const int k0 = kt * ATC_K;
+    stage_k(k0);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    scores();
+    for (int c0 = 0; c0 < ATC_K; c0 += 16) {
+      float s[16];
+      tmem_ld16(tS + lane_base + (uint32_t)c0, s);
+#pragma unroll
+      for (int j = 0; j < 16; j++)
+        if (k0 + c0 + j <= qpos) m = fmaxf(m, s[j] * scale);
+    }
+    tc_fence_before();
+    __syncthreads();
+    ok = !s_stop;
+  }
+  // ---------------------------------------------------------------- pass 2
+  float l = 0.0f;
+  for (int kt = 0; kt < n_tiles && ok; kt++) {
+    const int k0 = kt * ATC_K;
+    stage_k(k0);
+    stage_vt(k0);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    scores();
+    for (int c0 = 0; c0 < ATC_K; c0 += 16) {
+      float s[16];
+      tmem_ld16(tS + lane_base + (uint32_t)c0, s);
+      float p[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        p[j] = k0 + c0 + j <= qpos ? expf(s[j] * scale - m) : 0.0f;
+        l += p[j];
+      }
+#pragma unroll
+      for (int half = 0; half < 2; half++)
+        *reinterpret_cast<uint4*>(sP + atc_off(t, (c0 >> 3) + half)) =
+            make_uint4(bf16x2(p[8 * half], p[8 * half + 1]), bf16x2(p[8 * half + 2], p[8 * half + 3]),
+                       bf16x2(p[8 * half + 4], p[8 * half + 5]),
+                       bf16x2(p[8 * half + 6], p[8 * half + 7]));
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (t == 0) {
+      tc_fence_after();
+      atc_mma(tO, smem_u32(sP), smem_u32(sV), kt > 0);
+      umma_commit(bar);
+    }
+    if (!mbar_wait(bar, phase, a.err)) {
+      atomicCAS(a.err, 0, 1);
+      s_stop = 1;
+    }
+    phase ^= 1;
+    tc_fence_after();
+    __syncthreads();
+    ok = !s_stop;
+  }
+  // --------------------------------------------------------------- epilogue
+  if (ok) {
+    // every lane takes part in the warp-collective loads; rows past n store nothing
+    float* dst = a.out + ((size_t)qi * a.n_heads + h) * ATC_HD;
+    const float inv = 1.0f / l;
+    for (int c0 = 0; c0 < ATC_HD; c0 += 16) {
+      float o[16];
+      tmem_ld16(tO + lane_base + (uint32_t)c0, o);
+      if (qi < a.n_tokens) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<float4*>(dst + c0 + j) =
+              make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+inline size_t attn_tc_smem_bytes() { return 4 * (size_t)ATC_OPND + 16 + 1024; }
+
+}  // namespace flock

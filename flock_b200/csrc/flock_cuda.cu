@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "attn_fast.cuh"
+#include "attn_tc.cuh"
 #include "gemm_tc.cuh"
 #include "flock_internal.h"
 #include "gemv.cuh"
@@ -300,9 +301,9 @@ int layer_init(flock_layer* L, flock_dev* dev, const flock_layer_config& cfg, Wo
   return FLOCK_OK;
 }
 
-// q/k norm + RoPE + KV append, then attention over n >= 1 queries in
-// attnRef / attnPrefillRef order (exact decode and all prefill steps).
-static int enqueue_qk_attn_exact(flock_layer* L, int n, bool pdl) {
+// q/k norm + RoPE + KV append, then attention over n >= 1 queries: in
+// attnRef / attnPrefillRef order, or (tensor_cores, n > 1) on tcgen05.
+static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   flock_dev* d = L->dev;
   Workspace* ws = L->ws;
   const flock_layer_config& c = L->cfg;
@@ -337,7 +338,22 @@ static int enqueue_qk_attn_exact(flock_layer* L, int n, bool pdl) {
   aa.n_kv_heads = c.n_kv_heads;
   aa.head_dim = c.head_dim;
   pf_add(aa.pf, L->w[W_UP]);
-  if (n == 1) {
+  if (n > 1 && tensor_cores) {
+    AttnTcArgs ta = {};
+    ta.q = ws->qn.as<float>();
+    ta.kcache = L->kcache.as<float>();
+    ta.vcache = L->vcache.as<float>();
+    ta.out = ws->attn.as<float>();
+    ta.ctl = L->ctl;
+    ta.n_tokens = n;
+    ta.n_heads = c.n_heads;
+    ta.n_kv_heads = c.n_kv_heads;
+    ta.err = ws->tc_err.as<int>();
+    FLOCK_TRY(kernel_setup((const void*)k_attn_prefill_tc, (int)attn_tc_smem_bytes()));
+    k_attn_prefill_tc<<<dim3((n + ATC_Q - 1) / ATC_Q, c.n_heads), ATC_THREADS,
+                        attn_tc_smem_bytes(), d->stream>>>(ta);
+    FLOCK_CK(cudaGetLastError());
+  } else if (n == 1) {
     const size_t smem = (size_t)c.max_keys * sizeof(float);
     FLOCK_TRY(kernel_setup((const void*)k_attn_decode_exact, 200 * 1024));
     FLOCK_CK(launch_ex(d->stream, k_attn_decode_exact, dim3(c.n_heads), dim3(256), smem, pdl,
@@ -388,7 +404,7 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.err = err;
     FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_STORE, a));
   }
-  FLOCK_TRY(enqueue_qk_attn_exact(L, n, false));
+  FLOCK_TRY(enqueue_qk_attn(L, n, false, true));
   {  // o_proj + residual on h
     FLOCK_TRY(act_image_enqueue(st, ws->attn.as<float>(), qw, nullptr, 0.0f, n, qw, img));
     TcArgs a = {};
@@ -507,7 +523,7 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     FLOCK_CK(launch_ex(d->stream, k_attn_decode_fast, dim3(c.n_kv_heads, a.splits),
                        dim3(ATTN_FAST_THREADS), smem, pdl, a));
   } else {
-    FLOCK_TRY(enqueue_qk_attn_exact(L, n, pdl));
+    FLOCK_TRY(enqueue_qk_attn(L, n, pdl, false));
   }
   // 4. o_proj + residual, in place on h
   {

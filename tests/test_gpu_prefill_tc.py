@@ -85,3 +85,22 @@ def test_bf16_prefill_chunks_past_max_prefill(dev):
     prompt = synth.uniform_ids(6, "long", 150, 4096).tolist()
     assert abs_err_scaled(a.logits(prompt), b.logits(prompt)) <= 1e-2
     assert a.pos == 150
+
+
+def test_bf16_prefill_over_long_cache(dev, oracle, weights):
+    """pos0 = 900: 130 queries over 1030 keys (two query tiles, nine key tiles)."""
+    kvw = S.n_kv_heads * S.head_dim
+    kc = synth.normal(105, "k900", 900 * kvw)
+    vc = synth.normal(105, "v900", 900 * kvw)
+    L = Layer.create(dev, weights, BF16)
+    L.write_cache(kc, vc)
+    oracle.set_fma_mode(False)
+    ref = oracle.RefLayer(weights, CFG, 4096)
+    ref.fill_cache(kc, vc)
+    n = 130
+    x = synth.normal(106, "p130", n * S.hidden).astype(np.float32)
+    L.encode_prefill(n, x)
+    got = L.read_output(n)
+    want = ref.forward(x, n)
+    assert abs_err_scaled(got - x, want - x) <= 1e-2
+    assert L.n_keys == 1030
