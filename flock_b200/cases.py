@@ -4,7 +4,8 @@
     python -m flock_b200.cases head  [--time]   # the 151936 x 1024 Q8_0 head matvec
     python -m flock_b200.cases gemv  [--time]   # the config 1 matvec sweep (M = 1)
     python -m flock_b200.cases sweep [--time]   # config 1: Q8_0/Q4_0 x shapes x M in {1,16,128,512}
-    python -m flock_b200.cases gemm  [--time]   # one M = 512 tensor-core GEMM (3072 x 1024)
+    python -m flock_b200.cases gemm  [--time] [rows cols [M]]
+                                                # one tensor-core GEMM (default 3072 x 1024, M 512)
     python -m flock_b200.cases model [--time] [--kernels] [--trace]
     python -m flock_b200.cases prefill [--time] [--exact]
                                                 # config 3: 512-token prompt TTFT on the
@@ -99,11 +100,13 @@ def sweep_case(timed: bool) -> None:
 
 def gemm_case(timed: bool) -> None:
     dev = flib.get_device(0)
-    t = flib.GpuTensor.from_packed(dev, synth.q8_tensor(2, "t", 3072, 1024), 3072, 1024)
-    ms, _ = ops.gemm_timed(dev, t, 512, 20 if timed else 2)
+    nums = [int(a) for a in sys.argv[2:] if a.isdigit()]
+    rows, cols, m = (nums + [3072, 1024, 512][len(nums):])[:3]
+    t = flib.GpuTensor.from_packed(dev, synth.q8_tensor(2, "t", rows, cols), rows, cols)
+    ms, _ = ops.gemm_timed(dev, t, m, 20 if timed else 2)
     if timed:
-        print(f"gemm 512 x 1024 x 3072: {ms * 1000:.1f} us, "
-              f"{2 * 512 * 1024 * 3072 / (ms * 1e-3) / 1e12:.1f} TFLOP/s")
+        print(f"gemm M {m} x K {cols} x N {rows}: {ms * 1000:.1f} us, "
+              f"{2 * m * rows * cols / (ms * 1e-3) / 1e12:.1f} TFLOP/s")
 
 
 def prefill_case(timed: bool) -> None:

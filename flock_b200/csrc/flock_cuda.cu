@@ -224,6 +224,7 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count) {
     FLOCK_TRY(gu.alloc((size_t)P * 2 * F * f));
     FLOCK_TRY(tc_err.alloc(16));
     FLOCK_CK(cudaMemset(tc_err.p, 0, 16));
+    FLOCK_TRY(part.alloc((size_t)8 * P * H * f));
   }
   return FLOCK_OK;
 }
@@ -402,7 +403,7 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.M = n;
     a.img = img;
     a.err = err;
-    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_STORE, a));
+    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_STORE, a, d->sm_count, ws->part.bytes / 4));
   }
   FLOCK_TRY(enqueue_qk_attn(L, n, false, true));
   {  // o_proj + residual on h
@@ -416,7 +417,8 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.res = ws->h.as<float>();
     a.res_stride = H;
     a.err = err;
-    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_RESIDUAL, a));
+    a.part = ws->part.as<float>();
+    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_RESIDUAL, a, d->sm_count, ws->part.bytes / 4));
   }
   {  // ffn_norm + gate | up, SwiGLU
     FLOCK_TRY(act_image_enqueue(st, ws->h.as<float>(), H, L->w[W_FFN_NORM]->data.as<float>(),
@@ -429,7 +431,7 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.M = n;
     a.img = img;
     a.err = err;
-    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_STORE, a));
+    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_STORE, a, d->sm_count, ws->part.bytes / 4));
     const int64_t total = (int64_t)n * F;
     k_swiglu_rows<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(ws->gu.as<float>(),
                                                                     ws->act.as<float>(), n, F);
@@ -446,7 +448,8 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.res = ws->h.as<float>();
     a.res_stride = H;
     a.err = err;
-    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_RESIDUAL, a));
+    a.part = ws->part.as<float>();
+    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_RESIDUAL, a, d->sm_count, ws->part.bytes / 4));
   }
   return FLOCK_OK;
 }

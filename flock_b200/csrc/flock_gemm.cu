@@ -61,18 +61,42 @@ template <int QT, int EPI>
 static int launch_tc(cudaStream_t st, const TcArgs& a) {
   FLOCK_TRY(kernel_setup((const void*)k_gemm_tc<QT, EPI>, (int)gemm_tc_smem_bytes(TC_MAX_NT)));
   const size_t smem = gemm_tc_smem_bytes(a.Nt);
-  const dim3 grid((unsigned)a.tile0[a.nseg], (unsigned)((a.M + a.Nt - 1) / a.Nt));
+  const dim3 grid((unsigned)a.tile0[a.nseg], (unsigned)((a.M + a.Nt - 1) / a.Nt),
+                  (unsigned)a.ksplit);
   k_gemm_tc<QT, EPI><<<grid, TC_THREADS, smem, st>>>(a);
   FLOCK_CK(cudaGetLastError());
+  if (a.ksplit > 1) {
+    const TcSeg& s = a.seg[0];
+    const int64_t total = (int64_t)a.M * s.rows;
+    k_splitk_reduce<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+        a.part, a.ksplit, a.M, s.rows, EPI == EPI_RESIDUAL ? a.res : nullptr, a.res_stride, s.out,
+        s.out_stride);
+    FLOCK_CK(cudaGetLastError());
+  }
   return FLOCK_OK;
 }
 
 // Y = X . W^T for the segments of `a` on the tensor cores; `a.img` must hold
-// the activation image of the same M and K.
-int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a) {
+// the activation image of the same M and K.  With `part` (room for
+// part_floats) and one segment, a grid too small for the GPU is split along
+// K (at least 8 K-tiles per CTA) and reduced by k_splitk_reduce.
+int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a, int sm_count,
+                    size_t part_floats) {
   if (a.K % TC_KT || a.M < 1 || a.nseg < 1 || a.nseg > 3) return FLOCK_E_ARG;
   a.Nt = tc_token_tile(a.M);
   tc_finish_tiles(a);
+  a.ksplit = 1;
+  const int ctas = a.tile0[a.nseg] * ((a.M + a.Nt - 1) / a.Nt);
+  const int KT = a.K / TC_KT;
+  if (a.part && a.nseg == 1 && 2 * ctas <= sm_count) {
+    for (int s = 8; s >= 2; s--) {
+      if (KT % s || KT / s < 8 || ctas * s > sm_count ||
+          (size_t)s * a.M * a.seg[0].rows > part_floats)
+        continue;
+      a.ksplit = s;
+      break;
+    }
+  }
   if (qt == QT_Q8)
     return epi == EPI_RESIDUAL ? launch_tc<QT_Q8, EPI_RESIDUAL>(st, a)
                                : launch_tc<QT_Q8, EPI_STORE>(st, a);
@@ -100,7 +124,8 @@ int gemm_once(flock_dev* d, const flock_tensor* w, const float* x, int M, float*
   a.M = M;
   a.img = img;
   a.err = err;
-  return gemm_tc_enqueue(d->stream, w->dtype == FLOCK_Q8_0 ? QT_Q8 : QT_Q4, EPI_STORE, a);
+  return gemm_tc_enqueue(d->stream, w->dtype == FLOCK_Q8_0 ? QT_Q8 : QT_Q4, EPI_STORE, a,
+                         d->sm_count, 0);
 }
 
 int check_tc_err(const DBuf& err) {

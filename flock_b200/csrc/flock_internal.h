@@ -89,7 +89,8 @@ struct Workspace {
   DBuf attn_part, attn_count;  // fast decode attention partials
   int attn_splits = 16;         // splits: SMs / kv heads, so one wave covers them
   int attn_split_cap = 32;      // partial slots allocated per head (attn_max_splits' bound)
-  DBuf img, gu, tc_err;         // bf16 prefill: activation image, gate|up rows, error word
+  DBuf img, gu, tc_err, part;   // bf16 prefill: activation image, gate|up rows, error word,
+                                // split-K partials
   int alloc(const flock_layer_config& c, int sm_count);
 };
 
@@ -105,7 +106,8 @@ struct TcSeg;
 size_t act_image_bytes(int M, int K);
 int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float* gain, float eps,
                       int M, int K, uint8_t* img);
-int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a);
+int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a, int sm_count,
+                    size_t part_floats);
 TcSeg tc_seg_of(const flock_tensor* t, float* out, int out_stride);
 // bf16 prefill's device error word: FLOCK_E_CUDA (and cleared) if a tensor-core
 // GEMM gave up waiting since the last check; call after a synchronisation.

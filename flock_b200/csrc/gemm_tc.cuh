@@ -63,6 +63,10 @@ struct TcArgs {
   const float* res;    // EPI_RESIDUAL: y += res[m][n] (res may alias the output)
   int res_stride;
   int* err;
+  // split-K (one segment): CTA z covers K-tiles [z * KT / ksplit, (z+1) * KT / ksplit)
+  // and writes its partial to part[z][m][row]; k_splitk_reduce sums them
+  int ksplit;
+  float* part;
 };
 
 // ------------------------------------------------------------------ tcgen05
@@ -249,7 +253,8 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
   const TcSeg& sg = a.seg[sgi];
   const int row0 = ((int)blockIdx.x - a.tile0[sgi]) * TC_ROWS;
   const int mb = blockIdx.y, m0 = mb * Nt;
-  const int KT = a.K / TC_KT;
+  const int KT = a.K / TC_KT / a.ksplit;       // K-tiles of this CTA
+  const int kt_base = (int)blockIdx.z * KT;     // its first K-tile
 
   if (warp < TC_PRODUCERS / 32) {
     // ------------------------------------------------------------ producers
@@ -260,7 +265,7 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
     TcRaw ring[TC_PREFETCH];
 #pragma unroll
     for (int j = 0; j < TC_PREFETCH; j++)
-      if (j < KT) tc_load_raw<QT>(ring[j], sg, a.K, lrow, half, j);
+      if (j < KT) tc_load_raw<QT>(ring[j], sg, a.K, lrow, half, kt_base + j);
     bool ok = true;
     for (int kt0 = 0; kt0 < KT && ok; kt0 += TC_PREFETCH) {
 #pragma unroll
@@ -277,12 +282,13 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
         uint8_t* A = tsm + (size_t)st * stage_bytes;
         if (threadIdx.x == 0) {
           mbar_expect_tx_only(&full[st], (uint32_t)b_bytes);
-          bulk_g2s(A + TC_A_BYTES, a.img + ((size_t)mb * KT + kt) * (size_t)b_bytes,
+          bulk_g2s(A + TC_A_BYTES,
+                   a.img + ((size_t)mb * (a.K / TC_KT) + kt_base + kt) * (size_t)b_bytes,
                    (uint32_t)b_bytes, &full[st]);
         }
         tc_store_block<QT>(ring[j], A, t, half);
         if (kt + TC_PREFETCH < KT)
-          tc_load_raw<QT>(ring[j], sg, a.K, lrow, half, kt + TC_PREFETCH);
+          tc_load_raw<QT>(ring[j], sg, a.K, lrow, half, kt_base + kt + TC_PREFETCH);
         fence_proxy_async_smem();
         mbar_arrive(&full[st]);
       }
@@ -291,7 +297,17 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
     if (!mbar_wait(done, 0, a.err)) atomicCAS(a.err, 0, 1);
     tc_fence_after();
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const bool split = a.ksplit > 1;
     for (int c0 = 16 * half; c0 < Nt; c0 += 32) {
+      // the residual (which may alias the output) is read before any store
+      float r[16];
+      if (EPI == EPI_RESIDUAL && !split && rv) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const int m = m0 + c0 + j;
+          r[j] = m < a.M ? a.res[(size_t)m * a.res_stride + row] : 0.0f;
+        }
+      }
       float v[16];
       tmem_ld16(tmem + lane_base + (uint32_t)c0, v);
       if (rv) {
@@ -299,9 +315,12 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
         for (int j = 0; j < 16; j++) {
           const int m = m0 + c0 + j;
           if (m < a.M) {
-            float y = v[j];
-            if (EPI == EPI_RESIDUAL) y = a.res[(size_t)m * a.res_stride + row] + y;
-            sg.out[(size_t)m * sg.out_stride + row] = y;
+            if (split) {
+              a.part[((size_t)blockIdx.z * a.M + m) * sg.rows + row] = v[j];
+            } else {
+              const float y = EPI == EPI_RESIDUAL ? r[j] + v[j] : v[j];
+              sg.out[(size_t)m * sg.out_stride + row] = y;
+            }
           }
         }
       }
@@ -331,6 +350,20 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
     tc_fence_after();
     tmem_dealloc(tmem, ncols);
   }
+}
+
+// out[m][n] = (res[m][n] +) sum_z part[z][m][n], the splits added in order.
+static __global__ void k_splitk_reduce(const float* part, int ksplit, int M, int N,
+                                       const float* res, int res_stride, float* out,
+                                       int out_stride) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)M * N) return;
+  const int64_t m = i / N, n = i - m * N;
+  const size_t plane = (size_t)M * N;
+  float s = part[i];
+  for (int z = 1; z < ksplit; z++) s = s + part[z * plane + i];
+  if (res) s = res[m * res_stride + n] + s;
+  out[m * out_stride + n] = s;
 }
 
 inline size_t gemm_tc_smem_bytes(int nt) {
