@@ -113,49 +113,6 @@ FLOCK_DEV void attn_combine_warp(const float* pp, int splits, int hd, int lane, 
   }
 }
 
-// Exact RMSNorm (WG = 128) + RoPE of one 128-vector by one warp, with no
-// block synchronisation: lane l holds elements l, l+32, l+64, l+96 -- the
-// grouping the WG = 128 tree folds (partials t and t+64, t+32 and t+96, then
-// the shuffle tree) -- so NEOX pairs (i, i+64) are lane-local and NORM pairs
-// (2i, 2i+1) are neighbouring lanes.  k_qk_norm_rope_append's arithmetic.
-FLOCK_DEV void norm_rope_warp(const float* src, const float* gain, float eps, int pos,
-                              const float* inv_freq, int neox, float* dst, int lane) {
-  float x[4], y[4];
-#pragma unroll
-  for (int q = 0; q < 4; q++) x[q] = src[lane + 32 * q];
-  float v = fadd(fadd(ffma(x[0], x[0], 0.0f), ffma(x[2], x[2], 0.0f)),
-                 fadd(ffma(x[1], x[1], 0.0f), ffma(x[3], x[3], 0.0f)));
-  v = warp_tree_sum(v);
-  v = __shfl_sync(0xffffffffu, v, 0);
-  const float scale = rsqrt_f64r(fadd(fdiv(v, 128.0f), eps));
-#pragma unroll
-  for (int q = 0; q < 4; q++) y[q] = fmul(fmul(x[q], scale), gain[lane + 32 * q]);
-  if (neox) {
-#pragma unroll
-    for (int q = 0; q < 2; q++) {
-      const int i = lane + 32 * q;
-      const float theta = fmul((float)pos, inv_freq[i]);
-      const float c = __double2float_rn(cos((double)theta));
-      const float s = __double2float_rn(sin((double)theta));
-      const float av = y[q], bv = y[q + 2];
-      dst[i] = ffma(-bv, s, fmul(av, c));
-      dst[i + 64] = ffma(bv, c, fmul(av, s));
-    }
-  } else {
-    const bool odd = lane & 1;
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int e = lane + 32 * q;
-      const float other = __shfl_xor_sync(0xffffffffu, y[q], 1);
-      const float av = odd ? other : y[q], bv = odd ? y[q] : other;
-      const float theta = fmul((float)pos, inv_freq[e >> 1]);
-      const float c = __double2float_rn(cos((double)theta));
-      const float s = __double2float_rn(sin((double)theta));
-      dst[e] = odd ? ffma(bv, c, fmul(av, s)) : ffma(-bv, s, fmul(av, c));
-    }
-  }
-}
-
 // Shared-memory layout (floats): raw q [4][128], raw k/v [2][128], gains
 // [2][128], inv_freq [64], normalised q [4][128], new k/v [2][128], norm
 // scratch tmp [2][128] + red [2][132], scores/probabilities [4][TILE],

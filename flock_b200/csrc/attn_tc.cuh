@@ -6,9 +6,11 @@
 //  * one CTA per (128-query tile, query head); 4 warps; thread t owns query
 //    row t of the tile, which is TMEM lane t of every accumulator, so a row's
 //    max and sum need no cross-thread reduction (tcgen05.ld 32x32b);
-//  * q, K and V are staged as bf16 in the K-major 128-byte-swizzled layout
-//    (head_dim 128 = two 64-wide swizzle chunks); V is transposed while it is
-//    staged ([head_dim][keys]) so both products read K-major operands;
+//  * q is staged as bf16 in the K-major 128-byte-swizzled layout (head_dim
+//    128 = two 64-wide swizzle chunks); K and V come from a bf16 image of the
+//    cache that k_kv_image builds once per step (per kv head, 128-key tiles
+//    of K and of V transposed to [head_dim][keys], already in that layout),
+//    one bulk copy per tile, so both products read K-major operands;
 //  * pass 1: S = q K^T per 128-key tile (tcgen05.mma 128x128x16, f32 in
 //    TMEM) -> exact row max m;  pass 2: S again, P = e^(S*scale - m) written
 //    as bf16 into shared memory, O += P V^T accumulated in TMEM, l += sum P;
@@ -30,8 +32,8 @@ constexpr int ATC_OPND = ATC_Q * ATC_HD * 2;  // bytes of one 128 x 128 bf16 ope
 
 struct AttnTcArgs {
   const float* q;  // [n][nH][hd] normalised + rotated
-  const float* kcache;
-  const float* vcache;
+  const uint8_t* kv_img;  // [nKV][tiles][K tile | V^T tile], ATC_OPND bytes each
+  int img_tiles;          // key tiles per kv head in the image
   float* out;      // [n][nH][hd]
   const int* ctl;  // ctl[0] = pos0 (keys before this batch)
   int n_tokens, n_heads, n_kv_heads;
@@ -79,13 +81,13 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
   uint8_t* sV = sK + ATC_OPND;  // V^T: [head_dim][keys]
   uint8_t* sP = sV + ATC_OPND;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sP + ATC_OPND);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+  uint64_t* ldbar = bar + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 2);
   __shared__ int s_stop;
 
   const int t = threadIdx.x, warp = t >> 5;
   const int h = blockIdx.y, q0 = blockIdx.x * ATC_Q;
   const int G = a.n_heads / a.n_kv_heads, g = h / G;
-  const size_t kvs = (size_t)a.n_kv_heads * ATC_HD;
   const int pos0 = a.ctl[0];
   const int qi = q0 + t;                   // this thread's query
   const int qpos = pos0 + qi;              // its position: sees keys 0..qpos
@@ -96,6 +98,7 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
 
   if (t == 0) {
     mbar_init(bar, 1);
+    mbar_init(ldbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_stop = 0;
   }
@@ -112,27 +115,22 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
   const uint32_t tmem = *tslot;
   const uint32_t tS = tmem, tO = tmem + 128;
   const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-  uint32_t phase = 0;
+  uint32_t phase = 0, ldphase = 0;
   bool ok = true;
 
-  auto stage_k = [&](int k0) {
-    const int key = k0 + t;
-    atc_stage_row(sK, t, key < kend ? a.kcache + (size_t)key * kvs + (size_t)g * ATC_HD : nullptr);
-  };
-  auto stage_vt = [&](int k0) {
-    // thread t = head_dim column t: keys k0.. of that column, 8 per chunk
-    const float* src = a.vcache + (size_t)g * ATC_HD + t;
-#pragma unroll 2
-    for (int c = 0; c < 16; c++) {
-      float v[8];
-#pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const int key = k0 + 8 * c + e;
-        v[e] = key < kend ? __ldg(src + (size_t)key * kvs) : 0.0f;
-      }
-      *reinterpret_cast<uint4*>(sV + atc_off(t, c)) =
-          make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]), bf16x2(v[6], v[7]));
+  // K tile kt (and its V^T tile) from the image by bulk copy; everyone waits
+  auto stage = [&](int kt, bool with_v) {
+    if (t == 0) {
+      const uint8_t* src = a.kv_img + ((size_t)g * a.img_tiles + kt) * 2 * ATC_OPND;
+      mbar_expect_tx(ldbar, (uint32_t)(with_v ? 2 : 1) * ATC_OPND);
+      bulk_g2s(sK, src, ATC_OPND, ldbar);
+      if (with_v) bulk_g2s(sV, src + ATC_OPND, ATC_OPND, ldbar);
     }
+    if (!mbar_wait(ldbar, ldphase, a.err)) {
+      atomicCAS(a.err, 0, 1);
+      s_stop = 1;
+    }
+    ldphase ^= 1;
   };
   // issue S = q K^T (thread 0) and wait for it (everyone)
   auto scores = [&]() {
@@ -153,8 +151,7 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
   float m = -INFINITY;
   for (int kt = 0; kt < n_tiles && ok; kt++) {
     const int k0 = kt * ATC_K;
-    stage_k(k0);
-    fence_proxy_async_smem();
+    stage(kt, false);
     tc_fence_before();
     __syncthreads();
     scores();
@@ -173,9 +170,7 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
   float l = 0.0f;
   for (int kt = 0; kt < n_tiles && ok; kt++) {
     const int k0 = kt * ATC_K;
-    stage_k(k0);
-    stage_vt(k0);
-    fence_proxy_async_smem();
+    stage(kt, true);
     tc_fence_before();
     __syncthreads();
     scores();
@@ -236,6 +231,49 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
   }
 }
 
-inline size_t attn_tc_smem_bytes() { return 4 * (size_t)ATC_OPND + 16 + 1024; }
+inline size_t attn_tc_smem_bytes() { return 4 * (size_t)ATC_OPND + 24 + 1024; }
+
+// The bf16 image of keys [0, kend) of the cache for k_attn_prefill_tc, kend =
+// ctl[0] + n (the position block already advanced for this step): per (key
+// tile, kv head) one CTA writes the K tile ([key][head_dim], rows past kend
+// zero) and the V^T tile ([head_dim][key]), transposed through shared memory
+// so every global load is a coalesced row.  The grid covers the cache's
+// capacity; tiles past kend return at once.
+constexpr int KVI_STRIDE = 132;  // f32 row stride of the transposition buffer
+static __global__ void __launch_bounds__(ATC_THREADS) k_kv_image(const float* kcache,
+                                                                const float* vcache,
+                                                                int n_kv_heads, const int* ctl,
+                                                                int n, int img_tiles,
+                                                                uint8_t* img) {
+  extern __shared__ __align__(16) float vbuf[];  // [128 keys][KVI_STRIDE]
+  const int kt = blockIdx.x, g = blockIdx.y, t = threadIdx.x;
+  const int kend = ctl[0] + n;
+  if (kt * ATC_K >= kend) return;
+  const size_t kvs = (size_t)n_kv_heads * ATC_HD;
+  const int key = kt * ATC_K + t;
+  uint8_t* kdst = img + ((size_t)g * img_tiles + kt) * 2 * ATC_OPND;
+  uint8_t* vdst = kdst + ATC_OPND;
+  atc_stage_row(kdst, t, key < kend ? kcache + (size_t)key * kvs + (size_t)g * ATC_HD : nullptr);
+  const float4* vr = reinterpret_cast<const float4*>(vcache + (size_t)key * kvs + (size_t)g * ATC_HD);
+#pragma unroll 8
+  for (int c = 0; c < 32; c++)
+    reinterpret_cast<float4*>(vbuf + t * KVI_STRIDE)[c] =
+        key < kend ? __ldg(vr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  // thread t = head_dim column t of the tile
+#pragma unroll 4
+  for (int c = 0; c < 16; c++) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = vbuf[(8 * c + e) * KVI_STRIDE + t];
+    *reinterpret_cast<uint4*>(vdst + atc_off(t, c)) =
+        make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]), bf16x2(v[6], v[7]));
+  }
+}
+
+inline size_t kv_image_smem_bytes() { return (size_t)ATC_K * KVI_STRIDE * 4; }
+inline size_t kv_image_bytes(int max_keys, int n_kv_heads) {
+  return (size_t)n_kv_heads * ((max_keys + ATC_K - 1) / ATC_K) * 2 * ATC_OPND;
+}
 
 }  // namespace flock

@@ -225,6 +225,7 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count) {
     FLOCK_TRY(tc_err.alloc(16));
     FLOCK_CK(cudaMemset(tc_err.p, 0, 16));
     FLOCK_TRY(part.alloc((size_t)8 * P * H * f));
+    FLOCK_TRY(kv_img.alloc(kv_image_bytes(c.max_keys, nKV)));
   }
   return FLOCK_OK;
 }
@@ -326,8 +327,8 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   qa.eps = c.eps;
   qa.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
   pf_add(qa.pf, L->w[W_GATE]);
-  FLOCK_CK(launch_ex(d->stream, k_qk_norm_rope_append, dim3(n * (c.n_heads + c.n_kv_heads)),
-                     dim3(128), 0, pdl, qa));
+  FLOCK_CK(launch_ex(d->stream, k_qk_norm_rope_append,
+                     dim3((n * (c.n_heads + c.n_kv_heads) + 7) / 8), dim3(256), 0, pdl, qa));
   AttnArgs aa = {};
   aa.q = ws->qn.as<float>();
   aa.kcache = L->kcache.as<float>();
@@ -340,10 +341,17 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   aa.head_dim = c.head_dim;
   pf_add(aa.pf, L->w[W_UP]);
   if (n > 1 && tensor_cores) {
+    // the bf16 image of keys [0, ctl[0] + n) (pos0 is read on the device)
+    const int img_tiles = (c.max_keys + ATC_K - 1) / ATC_K;
+    FLOCK_TRY(kernel_setup((const void*)k_kv_image, (int)kv_image_smem_bytes()));
+    k_kv_image<<<dim3(img_tiles, c.n_kv_heads), ATC_THREADS, kv_image_smem_bytes(),
+                 d->stream>>>(L->kcache.as<float>(), L->vcache.as<float>(), c.n_kv_heads, L->ctl,
+                              n, img_tiles, ws->kv_img.as<uint8_t>());
+    FLOCK_CK(cudaGetLastError());
     AttnTcArgs ta = {};
     ta.q = ws->qn.as<float>();
-    ta.kcache = L->kcache.as<float>();
-    ta.vcache = L->vcache.as<float>();
+    ta.kv_img = ws->kv_img.as<uint8_t>();
+    ta.img_tiles = img_tiles;
     ta.out = ws->attn.as<float>();
     ta.ctl = L->ctl;
     ta.n_tokens = n;

@@ -32,7 +32,9 @@ int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float
   a.Nt = tc_token_tile(M);
   a.img = img;
   const int rows = (M + a.Nt - 1) / a.Nt * a.Nt;
-  k_act_image<<<rows, ACT_IMG_THREADS, (size_t)K * 4, st>>>(a);
+  const size_t smem = (size_t)ACT_IMG_ROWS * K * 4;
+  FLOCK_TRY(kernel_setup((const void*)k_act_image, ACT_IMG_ROWS * 12288 * 4));
+  k_act_image<<<(rows + ACT_IMG_ROWS - 1) / ACT_IMG_ROWS, ACT_IMG_THREADS, smem, st>>>(a);
   FLOCK_CK(cudaGetLastError());
   return FLOCK_OK;
 }

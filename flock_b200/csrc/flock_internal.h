@@ -91,6 +91,7 @@ struct Workspace {
   int attn_split_cap = 32;      // partial slots allocated per head (attn_max_splits' bound)
   DBuf img, gu, tc_err, part;   // bf16 prefill: activation image, gate|up rows, error word,
                                 // split-K partials
+  DBuf kv_img;                  // bf16 prefill: bf16 K / V^T tiles of the cache
   int alloc(const flock_layer_config& c, int sm_count);
 };
 

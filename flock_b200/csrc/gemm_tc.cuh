@@ -360,8 +360,13 @@ static __global__ void k_splitk_reduce(const float* part, int ksplit, int M, int
   if (i >= (int64_t)M * N) return;
   const int64_t m = i / N, n = i - m * N;
   const size_t plane = (size_t)M * N;
-  float s = part[i];
-  for (int z = 1; z < ksplit; z++) s = s + part[z * plane + i];
+  float p[8];  // every split's load in flight before the ordered adds
+#pragma unroll
+  for (int z = 0; z < 8; z++) p[z] = z < ksplit ? part[z * plane + i] : 0.0f;
+  float s = p[0];
+#pragma unroll
+  for (int z = 1; z < 8; z++)
+    if (z < ksplit) s = s + p[z];
   if (res) s = res[m * res_stride + n] + s;
   out[m * out_stride + n] = s;
 }
@@ -373,9 +378,10 @@ inline size_t gemm_tc_smem_bytes(int nt) {
 // ------------------------------------------------------- activation image
 // X (f32 [M][x_stride]) -> bf16 image [M / Nt][K / 64][Nt][128 B] in the
 // swizzled K-major layout, RMSNorm fused when `gain` is set (ops_ref.ts:20
-// order: WG = 128 strided partials, the pairwise tree, 1/sqrt in f64 rounded
-// once, then x * scale * gain rounded per multiply).  One CTA per image row;
-// rows >= M are written as zeros.
+// order: WG = 128 strided partials -- lane l of the warp folds partials l,
+// l+32, l+64, l+96 -- the pairwise tree, 1/sqrt in f64 rounded once, then
+// x * scale * gain rounded per multiply).  One warp per image row, no block
+// barriers; rows >= M are written as zeros.
 struct ActImgArgs {
   const float* x;
   int x_stride;
@@ -386,53 +392,46 @@ struct ActImgArgs {
 };
 
 constexpr int ACT_IMG_THREADS = 128;
+constexpr int ACT_IMG_ROWS = ACT_IMG_THREADS / 32;  // rows per CTA
 
 static __global__ void __launch_bounds__(ACT_IMG_THREADS) k_act_image(const ActImgArgs a) {
-  extern __shared__ __align__(16) float xrow[];
-  __shared__ float red[132];
-  const int m = blockIdx.x, t = threadIdx.x;
+  extern __shared__ __align__(16) float xrows[];  // [ACT_IMG_ROWS][K]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.x * ACT_IMG_ROWS + warp;
+  const int n_mb = (a.M + a.Nt - 1) / a.Nt;
+  if (m >= n_mb * a.Nt) return;
   const int r = m % a.Nt, mb = m / a.Nt, KT = a.K / TC_KT;
-  uint8_t* base = a.img + (size_t)mb * KT * a.Nt * 128 + (size_t)r * 128;
+  uint8_t* base = a.img + (size_t)mb * KT * a.Nt * 128;
   if (m >= a.M) {
-    for (int i = t; i < a.K / 8; i += ACT_IMG_THREADS)
-      *reinterpret_cast<uint4*>(base + (size_t)(i >> 3) * a.Nt * 128 + ((i & 7) << 4)) =
+    for (int i = lane; i < a.K / 8; i += 32)
+      *reinterpret_cast<uint4*>(base + (size_t)(i >> 3) * a.Nt * 128 + sw128_off(r, i & 7)) =
           make_uint4(0, 0, 0, 0);
     return;
   }
+  float* xr = xrows + (size_t)warp * a.K;
   const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)m * a.x_stride);
-  for (int i = t; i < a.K / 4; i += ACT_IMG_THREADS) reinterpret_cast<float4*>(xrow)[i] = src[i];
-  __syncthreads();
+  for (int i = lane; i < a.K / 4; i += 32) reinterpret_cast<float4*>(xr)[i] = src[i];
+  __syncwarp();
   float scale = 1.0f;
   if (a.gain) {
-    float acc = 0.0f;
-    for (int i = t; i < a.K; i += 128) acc = ffma(xrow[i], xrow[i], acc);
-    red[t] = acc;
-    __syncthreads();
-    if (t < 64) red[t] = fadd(red[t], red[t + 64]);
-    __syncthreads();
-    if (t < 32) {
-      float v = fadd(red[t], red[t + 32]);
-      v = warp_tree_sum(v);
-      if (t == 0) red[128] = rsqrt_f64r(fadd(fdiv(v, (float)a.K), a.eps));
-    }
-    __syncthreads();
-    scale = red[128];
+    float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+      for (int i = lane + 32 * q; i < a.K; i += 128) p[q] = ffma(xr[i], xr[i], p[q]);
+    float v = fadd(fadd(p[0], p[2]), fadd(p[1], p[3]));
+    v = warp_tree_sum(v);
+    v = __shfl_sync(0xffffffffu, v, 0);
+    scale = rsqrt_f64r(fadd(fdiv(v, (float)a.K), a.eps));
   }
-  for (int i = t; i < a.K / 8; i += ACT_IMG_THREADS) {
+  for (int i = lane; i < a.K / 8; i += 32) {
     float v[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) {
       const int k = 8 * i + e;
-      v[e] = a.gain ? fmul(fmul(xrow[k], scale), __ldg(a.gain + k)) : xrow[k];
+      v[e] = a.gain ? fmul(fmul(xr[k], scale), __ldg(a.gain + k)) : xr[k];
     }
-    uint4 o;
-    o.x = bf16x2(v[0], v[1]);
-    o.y = bf16x2(v[2], v[3]);
-    o.z = bf16x2(v[4], v[5]);
-    o.w = bf16x2(v[6], v[7]);
-    const int kt = i >> 3, c = i & 7;
-    *reinterpret_cast<uint4*>(base + (size_t)kt * a.Nt * 128 - (size_t)r * 128 +
-                              sw128_off(r, c)) = o;
+    *reinterpret_cast<uint4*>(base + (size_t)(i >> 3) * a.Nt * 128 + sw128_off(r, i & 7)) =
+        make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]), bf16x2(v[6], v[7]));
   }
 }
 

@@ -75,44 +75,74 @@ struct QkArgs {
 };
 
 // One block of 128 threads per (token, head-vector); head_dim must be 128.
-static __global__ void __launch_bounds__(128) k_qk_norm_rope_append(const QkArgs a) {
-  __shared__ float red[132];
-  __shared__ float y[128];
+// Exact RMSNorm (WG = 128) + RoPE of one 128-vector by one warp, with no
+// block synchronisation: lane l holds elements l, l+32, l+64, l+96 -- the
+// grouping the WG = 128 tree folds (partials t and t+64, t+32 and t+96, then
+// the shuffle tree) -- so NEOX pairs (i, i+64) are lane-local and NORM pairs
+// (2i, 2i+1) are neighbouring lanes.  k_qk_norm_rope_append's arithmetic.
+FLOCK_DEV void norm_rope_warp(const float* src, const float* gain, float eps, int pos,
+                              const float* inv_freq, int neox, float* dst, int lane) {
+  float x[4], y[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++) x[q] = src[lane + 32 * q];
+  float v = fadd(fadd(ffma(x[0], x[0], 0.0f), ffma(x[2], x[2], 0.0f)),
+                 fadd(ffma(x[1], x[1], 0.0f), ffma(x[3], x[3], 0.0f)));
+  v = warp_tree_sum(v);
+  v = __shfl_sync(0xffffffffu, v, 0);
+  const float scale = rsqrt_f64r(fadd(fdiv(v, 128.0f), eps));
+#pragma unroll
+  for (int q = 0; q < 4; q++) y[q] = fmul(fmul(x[q], scale), gain[lane + 32 * q]);
+  if (neox) {
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const int i = lane + 32 * q;
+      const float theta = fmul((float)pos, inv_freq[i]);
+      const float c = __double2float_rn(cos((double)theta));
+      const float s = __double2float_rn(sin((double)theta));
+      const float av = y[q], bv = y[q + 2];
+      dst[i] = ffma(-bv, s, fmul(av, c));
+      dst[i + 64] = ffma(bv, c, fmul(av, s));
+    }
+  } else {
+    const bool odd = lane & 1;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int e = lane + 32 * q;
+      const float other = __shfl_xor_sync(0xffffffffu, y[q], 1);
+      const float av = odd ? other : y[q], bv = odd ? y[q] : other;
+      const float theta = fmul((float)pos, inv_freq[e >> 1]);
+      const float c = __double2float_rn(cos((double)theta));
+      const float s = __double2float_rn(sin((double)theta));
+      dst[e] = odd ? ffma(bv, c, fmul(av, s)) : ffma(-bv, s, fmul(av, c));
+    }
+  }
+}
+
+// One warp per 128-vector (8 per CTA): q heads -> qn, k heads -> the cache at
+// position pos0 + token with v copied beside it.  norm_rope_warp's arithmetic
+// is the WG = 128 RMSNorm and RoPE above, bit for bit.
+static __global__ void __launch_bounds__(256) k_qk_norm_rope_append(const QkArgs a) {
   issue_prefetch(a.pf);
   pdl_launch_dependents();
   pdl_wait();
   const int nvec = a.n_heads + a.n_kv_heads;
-  const int tok = blockIdx.x / nvec, hv = blockIdx.x % nvec;
-  const int t = threadIdx.x, hd = a.head_dim;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int vidx = blockIdx.x * 8 + warp;
+  if (vidx >= a.n_tokens * nvec) return;
+  const int tok = vidx / nvec, hv = vidx % nvec, hd = a.head_dim;
   const bool is_q = hv < a.n_heads;
   const int kvh = hv - a.n_heads;
-  const int pos0 = a.ctl[0];
-  const float* src = is_q ? a.q + ((size_t)tok * a.n_heads + hv) * hd
-                          : a.k + ((size_t)tok * a.n_kv_heads + kvh) * hd;
-  const float* gain = is_q ? a.q_norm : a.k_norm;
-  // rmsnorm over one head (n = WG = 128: each partial is one fma32(x, x, 0))
-  const float x = src[t];
-  const float sum = block128_tree_sum(ffma(x, x, 0.0f), red);
-  const float scale = rsqrt_f64r(fadd(fdiv(sum, (float)hd), a.eps));
-  y[t] = fmul(fmul(x, scale), gain[t]);
-  __syncthreads();
-  // RoPE at absolute position pos0 + tok
-  const int half = hd / 2;
-  float* dst = is_q ? a.qn + ((size_t)tok * a.n_heads + hv) * hd
-                    : a.kcache + ((size_t)(pos0 + tok) * a.n_kv_heads + kvh) * hd;
-  if (t < half) {
-    const int j = t;
-    const float theta = fmul((float)(pos0 + tok), a.inv_freq[j]);
-    const float c = __double2float_rn(cos((double)theta));
-    const float s = __double2float_rn(sin((double)theta));
-    const int ia = a.neox ? j : 2 * j, ib = a.neox ? j + half : 2 * j + 1;
-    const float av = y[ia], bv = y[ib];
-    dst[ia] = ffma(-bv, s, fmul(av, c));
-    dst[ib] = ffma(bv, c, fmul(av, s));
-  }
-  if (!is_q) {
-    a.vcache[((size_t)(pos0 + tok) * a.n_kv_heads + kvh) * hd + t] =
-        a.v[((size_t)tok * a.n_kv_heads + kvh) * hd + t];
+  const int pos = a.ctl[0] + tok;
+  if (is_q) {
+    norm_rope_warp(a.q + ((size_t)tok * a.n_heads + hv) * hd, a.q_norm, a.eps, pos, a.inv_freq,
+                   a.neox, a.qn + ((size_t)tok * a.n_heads + hv) * hd, lane);
+  } else {
+    const size_t row = ((size_t)pos * a.n_kv_heads + kvh) * hd;
+    norm_rope_warp(a.k + ((size_t)tok * a.n_kv_heads + kvh) * hd, a.k_norm, a.eps, pos, a.inv_freq,
+                   a.neox, a.kcache + row, lane);
+    const float* v = a.v + ((size_t)tok * a.n_kv_heads + kvh) * hd;
+#pragma unroll
+    for (int q = 0; q < 4; q++) a.vcache[row + lane + 32 * q] = v[lane + 32 * q];
   }
 }
 
