@@ -358,28 +358,13 @@ def main():
     print(json.dumps(out), flush=True)
 
 
-def stage_layers(n_layers: int, world: int) -> list[tuple[int, int]]:
-    """4 layers on rank 0, the remaining split evenly (earlier ranks take the
-    remainder), as BASELINE config 2 asks."""
-    if world == 1:
-        return [(0, n_layers)]
-    first = min(4, n_layers - (world - 1))
-    rest = n_layers - first
-    base, extra = divmod(rest, world - 1)
-    out, at = [(0, first)], first
-    for r in range(world - 1):
-        c = base + (1 if r < extra else 0)
-        out.append((at, at + c))
-        at += c
-    return out
-
-
 def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     import ctypes
     import torch.distributed as dist
     from datetime import timedelta
     from flock_b200 import _abi
     from flock_b200.layer import upload_layer
+    from flock_b200.pipeline import stage_ranges
     from flock_b200.lib import GpuTensor
     from flock_b200.model import Model
 
@@ -393,7 +378,7 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     comm = ctypes.c_void_p()
     _abi.call("flock_comm_init", dev.handle, world, rank, _abi.ptr(uid, _abi._u8p), 60000,
               ctypes.byref(comm))
-    a, b = stage_layers(shape.n_layers, world)[rank]
+    a, b = stage_ranges(shape.n_layers, world)[rank]
     layer_ts = [upload_layer(dev, m.layers[i]) for i in range(a, b)]
     if rank == 0:
         embd = GpuTensor.from_packed(dev, m.embd["packed"], m.embd["rows"], m.embd["cols"])
@@ -448,16 +433,24 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     ms_e2e = float(tt[0])
     if rank == 0:
         tok_s = args.steps / (ms_max / 1000.0)
+        avg_keys = PROMPT + (args.steps - 1) / 2.0 + 1
+        tok_bytes = bytes_per_token(shape, avg_keys)
+        token_gbs = tok_bytes * tok_s / 1e9
         out = {
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": "config 2 pipelined: contiguous layer ranges "
-                                   f"{stage_layers(shape.n_layers, world)}, hidden state over "
+                                   f"{stage_ranges(shape.n_layers, world)}, hidden state over "
                                    "NCCL send/recv", "seed": SEED, "prompt": PROMPT,
                        "attention": args.attention, "parallelism": f"pp{world}",
                        "l2": "inputs larger than L2"},
+            # batch 1 keeps one stage busy at a time: the roofline is one GPU's
+            "roofline": {"bound": "hbm", "achieved": token_gbs, "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": token_gbs / pk["hbm_gbs"], "traffic": None,
+                         "kernel": "whole token across the pipeline stages",
+                         "bytes_per_launch": tok_bytes, "peak_src": pk["src"]},
             "clocks": clocks,
             "e2e": {"value": args.steps / (ms_e2e / 1000.0), "unit": "tok/s",
                     "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},

@@ -387,7 +387,8 @@ struct Nccl {
     SYM(AllGather);
     SYM(GetErrorString);
 #undef SYM
-    if (!GetUniqueId || !CommInitRankConfig || !Send || !Recv || !AllReduce || !AllGather) {
+    if (!GetUniqueId || !CommInitRankConfig || !Send || !Recv || !AllReduce || !AllGather ||
+        !CommGetAsyncError || !CommAbort || !CommDestroy || !GetErrorString) {
       set_error("libnccl.so.2 lacks required symbols");
       return false;
     }
@@ -444,6 +445,38 @@ int comm_wait(flock_comm* c) {
       return FLOCK_E_NCCL;                                                             \
     }                                                                                  \
   } while (0)
+
+// A communicator created non-blocking may answer an enqueue with
+// ncclInProgress; it takes the next call only once ncclCommGetAsyncError
+// reports ncclSuccess.  Bounded by the communicator's timeout (then aborted).
+static int nccl_settle(flock_comm* c, ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return FLOCK_OK;
+  if (r != ncclInProgress) {
+    set_error("NCCL error %s at %s", g_nccl.GetErrorString(r), what);
+    return FLOCK_E_NCCL;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclInProgress;
+    g_nccl.CommGetAsyncError(c->comm, &st);
+    if (st == ncclSuccess) return FLOCK_OK;
+    if (st != ncclInProgress) {
+      set_error("NCCL error %s after %s", g_nccl.GetErrorString(st), what);
+      g_nccl.CommAbort(c->comm);
+      c->comm = nullptr;
+      return FLOCK_E_NCCL;
+    }
+    if (std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count() >
+        c->timeout_ms) {
+      set_error("%s still in progress after %d ms (a peer rank is gone?)", what, c->timeout_ms);
+      g_nccl.CommAbort(c->comm);
+      c->comm = nullptr;
+      return FLOCK_E_NCCL;
+    }
+    std::this_thread::yield();
+  }
+}
+#define NCCL_ISSUE(c, call) FLOCK_TRY(nccl_settle((c), (call), #call))
 
 extern "C" {
 
@@ -524,7 +557,7 @@ int flock_comm_allreduce_f32(flock_comm* c, const float* in, float* out, int64_t
   FLOCK_TRY(c->tmp_in.alloc(n * 4));
   FLOCK_TRY(c->tmp_out.alloc(n * 4));
   FLOCK_CK(cudaMemcpyAsync(c->tmp_in.p, in, n * 4, cudaMemcpyHostToDevice, c->dev->stream));
-  NCCL_CK(g_nccl.AllReduce(c->tmp_in.p, c->tmp_out.p, (size_t)n, ncclFloat32, ncclSum, c->comm,
+  NCCL_ISSUE(c, g_nccl.AllReduce(c->tmp_in.p, c->tmp_out.p, (size_t)n, ncclFloat32, ncclSum, c->comm,
                            c->dev->stream));
   FLOCK_CK(cudaMemcpyAsync(out, c->tmp_out.p, n * 4, cudaMemcpyDeviceToHost, c->dev->stream));
   return comm_wait(c);
@@ -536,7 +569,7 @@ int flock_comm_allgather_bytes(flock_comm* c, const void* in, void* out, int64_t
   FLOCK_TRY(c->tmp_in.alloc(bytes));
   FLOCK_TRY(c->tmp_out.alloc(bytes * c->n_ranks));
   FLOCK_CK(cudaMemcpyAsync(c->tmp_in.p, in, bytes, cudaMemcpyHostToDevice, c->dev->stream));
-  NCCL_CK(g_nccl.AllGather(c->tmp_in.p, c->tmp_out.p, (size_t)bytes, ncclUint8, c->comm,
+  NCCL_ISSUE(c, g_nccl.AllGather(c->tmp_in.p, c->tmp_out.p, (size_t)bytes, ncclUint8, c->comm,
                            c->dev->stream));
   FLOCK_CK(cudaMemcpyAsync(out, c->tmp_out.p, bytes * c->n_ranks, cudaMemcpyDeviceToHost,
                            c->dev->stream));
@@ -549,7 +582,8 @@ int flock_comm_allgather_bytes(flock_comm* c, const void* in, void* out, int64_t
 // its workspace); see flock_model.cu.
 namespace flock {
 int comm_send(flock_comm* c, const void* p, size_t n_f32, int peer) {
-  NCCL_CK(g_nccl.Send(p, n_f32, ncclFloat32, peer, c->comm, c->dev->stream));
+  if (!c->comm) return FLOCK_E_NCCL;
+  NCCL_ISSUE(c, g_nccl.Send(p, n_f32, ncclFloat32, peer, c->comm, c->dev->stream));
   return FLOCK_OK;
 }
 int comm_rank(const flock_comm* c, int* rank, int* n_ranks) {
@@ -558,7 +592,8 @@ int comm_rank(const flock_comm* c, int* rank, int* n_ranks) {
   return c->comm ? FLOCK_OK : FLOCK_E_NCCL;
 }
 int comm_recv(flock_comm* c, void* p, size_t n_f32, int peer) {
-  NCCL_CK(g_nccl.Recv(p, n_f32, ncclFloat32, peer, c->comm, c->dev->stream));
+  if (!c->comm) return FLOCK_E_NCCL;
+  NCCL_ISSUE(c, g_nccl.Recv(p, n_f32, ncclFloat32, peer, c->comm, c->dev->stream));
   return FLOCK_OK;
 }
 }  // namespace flock
