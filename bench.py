@@ -112,8 +112,11 @@ def peaks() -> dict:
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": d["hbm_gbs"], "src": "measured"}
-    return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d.get("bf16_tflops", 1590.0),
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", 1400.0),
+                "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "src": "fallback"}
 
 
 def traffic_from_profile(name: str = "gemv_lm_head_traffic.txt") -> float | None:
@@ -238,6 +241,8 @@ def main():
                     help="one cooperative kernel per token, or the per-op kernel graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the config 3 (512-token prefill) measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -350,12 +355,49 @@ def main():
     }
     if e2e:
         out["e2e"] = e2e
+    if not args.no_prefill:
+        out["prefill"] = prefill_ttft(dev, m, shape, pk)
     if not args.no_cpu_baseline:
         try:
             out["cpu_baseline"] = cpu_baseline(m, shape)
         except Exception as e:  # reported, not fatal
             out["cpu_baseline"] = {"value": None, "error": str(e)}
     print(json.dumps(out), flush=True)
+
+
+def prefill_ttft(dev, m, shape, pk, n_prompt: int = 512) -> dict:
+    """time to first token of a 512-token prompt on the same
+    28-layer model through the bf16 tensor-core prefill (tcgen05 GEMMs and
+    attention), device-timed; the weight GEMMs' FLOPs over the TTFT give a
+    lower bound on tensor-pipe use."""
+    from flock_b200.layer import QWEN3_06B
+    from flock_b200.model import Model
+    from flock_b200 import synth
+    cfg = QWEN3_06B.with_(attention="fast", prefill="bf16", max_keys=n_prompt + 64,
+                          max_prefill=n_prompt)
+    M = Model.create(dev, m, cfg)
+    prompt = synth.uniform_ids(SEED, "prompt512", n_prompt, shape.vocab).tolist()
+    M.step(prompt[:64])  # kernels loaded, workspaces touched
+    M.reset()
+    dev.sync()
+    best = None
+    for _ in range(3):
+        dev.timer_start()
+        first = M.step(prompt)
+        ms = dev.timer_stop()
+        M.reset()
+        best = ms if best is None else min(best, ms)
+    h, f = shape.hidden, shape.ffn
+    q, kv = shape.n_heads * shape.head_dim, shape.n_kv_heads * shape.head_dim
+    gemm_flops = 2.0 * n_prompt * shape.n_layers * (h * (q + 2 * kv) + q * h + 2 * h * f + f * h)
+    tf = gemm_flops / (best * 1e-3) / 1e12
+    M.free()
+    return {"workload": "config 3: 512-token prompt, 28 layers, bf16 tcgen05 prefill "
+                        "(GEMMs + causal attention), first token greedy",
+            "ttft_ms": best, "prompt_tok_s": n_prompt / (best * 1e-3), "first_id": first,
+            "gemm_tflops_over_ttft": tf, "peak_tflops": pk["bf16_tflops"],
+            "frac_of_peak": tf / pk["bf16_tflops"],
+            "timing": "CUDA events, best of 3 prefills"}
 
 
 def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):

@@ -423,12 +423,17 @@ static __global__ void __launch_bounds__(ACT_IMG_THREADS) k_act_image(const ActI
     v = __shfl_sync(0xffffffffu, v, 0);
     scale = rsqrt_f64r(fadd(fdiv(v, (float)a.K), a.eps));
   }
+#pragma unroll 4
   for (int i = lane; i < a.K / 8; i += 32) {
-    float v[8];
+    const float4 x0 = reinterpret_cast<const float4*>(xr)[2 * i];
+    const float4 x1 = reinterpret_cast<const float4*>(xr)[2 * i + 1];
+    float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    if (a.gain) {
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gain) + 2 * i);
+      const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gain) + 2 * i + 1);
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
-      const int k = 8 * i + e;
-      v[e] = a.gain ? fmul(fmul(xr[k], scale), __ldg(a.gain + k)) : xr[k];
+      for (int e = 0; e < 8; e++) v[e] = fmul(fmul(v[e], scale), g[e]);
     }
     *reinterpret_cast<uint4*>(base + (size_t)(i >> 3) * a.Nt * 128 + sw128_off(r, i & 7)) =
         make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]), bf16x2(v[6], v[7]));
