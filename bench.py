@@ -367,13 +367,13 @@ def main():
 
 def prefill_ttft(dev, m, shape, pk, n_prompt: int = 512) -> dict:
     """time to first token of a 512-token prompt on the same
-    28-layer model through the bf16 tensor-core prefill (tcgen05 GEMMs and
+    28-layer model through the tensor-core prefill (tcgen05 f16 GEMMs and
     attention), device-timed; the weight GEMMs' FLOPs over the TTFT give a
     lower bound on tensor-pipe use."""
     from flock_b200.layer import QWEN3_06B
     from flock_b200.model import Model
     from flock_b200 import synth
-    cfg = QWEN3_06B.with_(attention="fast", prefill="bf16", max_keys=n_prompt + 64,
+    cfg = QWEN3_06B.with_(attention="fast", prefill="tensor", max_keys=n_prompt + 64,
                           max_prefill=n_prompt)
     M = Model.create(dev, m, cfg)
     prompt = synth.uniform_ids(SEED, "prompt512", n_prompt, shape.vocab).tolist()
@@ -392,7 +392,7 @@ def prefill_ttft(dev, m, shape, pk, n_prompt: int = 512) -> dict:
     gemm_flops = 2.0 * n_prompt * shape.n_layers * (h * (q + 2 * kv) + q * h + 2 * h * f + f * h)
     tf = gemm_flops / (best * 1e-3) / 1e12
     M.free()
-    return {"workload": "config 3: 512-token prompt, 28 layers, bf16 tcgen05 prefill "
+    return {"workload": "config 3: 512-token prompt, 28 layers, tcgen05 f16 prefill "
                         "(GEMMs + causal attention), first token greedy",
             "ttft_ms": best, "prompt_tok_s": n_prompt / (best * 1e-3), "first_id": first,
             "gemm_tflops_over_ttft": tf, "peak_tflops": pk["bf16_tflops"],

@@ -26,7 +26,7 @@ FLOCK_Q8_0, FLOCK_Q4_0, FLOCK_F32 = 8, 4, 32
 FLOCK_ROPE_NEOX, FLOCK_ROPE_NORM = 0, 1
 FLOCK_ATTN_EXACT, FLOCK_ATTN_FAST = 0, 1
 FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT = 0, 1
-FLOCK_PREFILL_EXACT, FLOCK_PREFILL_BF16 = 0, 1
+FLOCK_PREFILL_EXACT, FLOCK_PREFILL_TENSOR = 0, 1
 
 
 class FlockError(RuntimeError):

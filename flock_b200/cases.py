@@ -2,11 +2,18 @@
 
     python -m flock_b200.cases layer [--time]   # one decode layer (config 0 shape, 256-key cache)
     python -m flock_b200.cases head  [--time]   # the 151936 x 1024 Q8_0 head matvec
-    python -m flock_b200.cases gemv  [--time]   # the config 1 matvec sweep (M = 1)
+    python -m flock_b200.cases gemv  [--time] [--8b]
+                                                # the config 1 matvec sweep (M = 1), or the
+                                                # 8B shapes (config 4)
     python -m flock_b200.cases sweep [--time]   # config 1: Q8_0/Q4_0 x shapes x M in {1,16,128,512}
     python -m flock_b200.cases gemm  [--time] [rows cols [M]]
                                                 # one tensor-core GEMM (default 3072 x 1024, M 512)
     python -m flock_b200.cases model [--time] [--kernels] [--trace]
+    python -m flock_b200.cases model8b [--time] [--prompt P] [--decode N] [--persistent]
+                                                # config 4 on one GPU: Qwen3-8B shape, 36
+                                                # layers, untied head; 4096-token prompt
+                                                # (tensor-core prefill, 512-token chunks), then
+                                                # N (default 512) greedy decode tokens
     python -m flock_b200.cases prefill [--time] [--exact]
                                                 # config 3: 512-token prompt TTFT on the
                                                 # 28-layer model, tensor-core (default) or
@@ -28,6 +35,7 @@ from . import lib as flib
 from .layer import QWEN3_06B, Layer
 
 SWEEP = [(2048, 1024), (1024, 1024), (1024, 2048), (3072, 1024), (1024, 3072), (151936, 1024)]
+SWEEP_8B = [(4096, 4096), (1024, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]
 
 
 def layer_case(timed: bool, attention: str = "fast") -> None:
@@ -58,8 +66,9 @@ def head_case(timed: bool) -> None:
 
 def gemv_case(timed: bool) -> None:
     dev = flib.get_device(0)
-    for q8 in (True, False):
-        for rows, cols in SWEEP:
+    shapes = SWEEP_8B if "--8b" in sys.argv else SWEEP
+    for q8 in ((True,) if "--8b" in sys.argv else (True, False)):
+        for rows, cols in shapes:
             make = synth.q8_tensor if q8 else synth.q4_tensor
             t = flib.GpuTensor.from_packed(dev, make(2, "t", rows, cols), rows, cols,
                                            flib.FLOCK_Q8_0 if q8 else flib.FLOCK_Q4_0)
@@ -92,7 +101,7 @@ def sweep_case(timed: bool) -> None:
                 if timed:
                     b = rows * cols * bpw + 4 * cols * m + 4 * rows * m
                     tf = 2.0 * m * rows * cols / (ms * 1e-3) / 1e12
-                    extra = f" (+{img * 1000:.1f} us x->bf16)" if img else ""
+                    extra = f" (+{img * 1000:.1f} us x->f16)" if img else ""
                     print(f"| {'Q8_0' if q8 else 'Q4_0'} | {cols} x {rows} | {m} | {eng} | "
                           f"{ms * 1000:.1f}{extra} | {b / ms / 1e6:.0f} | {tf:.1f} |")
             t.free()
@@ -115,7 +124,7 @@ def prefill_case(timed: bool) -> None:
     m = synth.model(300)
     exact = "--exact" in sys.argv
     cfg = QWEN3_06B.with_(attention="fast", max_keys=1024,
-                          prefill="exact" if exact else "bf16")
+                          prefill="exact" if exact else "tensor")
     M = Model.create(dev, m, cfg)
     prompt = synth.uniform_ids(300, "p512", 512, synth.QWEN3_06B.vocab).tolist()
     M.step(prompt[:64])  # warm-up: kernels loaded, workspaces touched
@@ -128,9 +137,58 @@ def prefill_case(timed: bool) -> None:
     M.decode_device(32)
     dec = dev.timer_stop()
     if timed:
-        print(f"prefill ({'exact' if exact else 'bf16 tensor cores'}): TTFT {ttft:.2f} ms for 512 "
+        print(f"prefill ({'exact' if exact else 'tensor cores'}): TTFT {ttft:.2f} ms for 512 "
               f"tokens ({512 / ttft * 1000:.0f} tok/s), first id {first}; 32 decode tokens "
               f"{dec / 32 * 1000:.1f} us/token")
+
+
+def model8b_case(timed: bool) -> None:
+    import time
+    from .layer import LayerConfig
+    from .model import Model
+    s = synth.QWEN3_8B
+    n_prompt = 4096
+    n_dec = 512
+    if "--decode" in sys.argv:
+        n_dec = int(sys.argv[sys.argv.index("--decode") + 1])
+    if "--prompt" in sys.argv:
+        n_prompt = int(sys.argv[sys.argv.index("--prompt") + 1])
+    dev = flib.get_device(0)
+    t0 = time.perf_counter()
+    m = synth.model(400, s)
+    cfg = LayerConfig(hidden=s.hidden, n_heads=s.n_heads, n_kv_heads=s.n_kv_heads,
+                      head_dim=s.head_dim, ffn=s.ffn, max_keys=n_prompt + n_dec + 64,
+                      max_prefill=512, attention="fast", prefill="tensor")
+    M = Model.create(dev, m, cfg)
+    if "--persistent" in sys.argv:
+        M.decode_mode = "persistent"
+    t_load = time.perf_counter() - t0
+    prompt = synth.uniform_ids(400, "p4096", n_prompt, s.vocab).tolist()
+    M.step(prompt[:min(512, n_prompt)])  # warm-up
+    M.reset()
+    dev.sync()
+    dev.timer_start()
+    first = M.step(prompt)
+    ttft = dev.timer_stop()
+    M.decode_device(8)
+    M.rewind(n_prompt)
+    M.set_token(first)
+    dev.sync()
+    dev.timer_start()
+    ids = M.decode_device(n_dec)
+    ms = dev.timer_stop()
+    if timed:
+        q, kv = s.n_heads * s.head_dim, s.n_kv_heads * s.head_dim
+        layer_w = (q * s.hidden + 2 * kv * s.hidden + s.hidden * q + 3 * s.ffn * s.hidden) * 1.0625
+        keys = n_prompt + (n_dec + 1) / 2.0
+        tok_bytes = s.n_layers * (layer_w + 2 * kv * 4 * keys) + s.vocab * s.hidden * 1.0625
+        tok_s = n_dec / (ms * 1e-3)
+        print(f"config 4 (8B shape, 1 GPU, {M.decode_mode}): synthetic weights + upload "
+              f"{t_load:.1f} s; "
+              f"TTFT {ttft:.1f} ms for {n_prompt} tokens; decode {n_dec} tokens "
+              f"{ms / n_dec * 1000:.1f} us/token = {tok_s:.1f} tok/s = "
+              f"{tok_bytes * tok_s / 1e9:.0f} GB/s ({tok_bytes / 1e9:.2f} GB/token); "
+              f"first ids {first} {ids[:4].tolist()}")
 
 
 PHASES = ("qkv", "attention", "o_proj", "gate/up", "down")
@@ -192,5 +250,6 @@ if __name__ == "__main__":
     case = sys.argv[1] if len(sys.argv) > 1 else "layer"
     timed = "--time" in sys.argv
     {"layer": layer_case, "head": head_case, "gemv": gemv_case, "model": model_case,
-     "sweep": sweep_case, "gemm": gemm_case, "prefill": prefill_case}[case](timed)
+     "sweep": sweep_case, "gemm": gemm_case, "prefill": prefill_case,
+     "model8b": model8b_case}[case](timed)
     print("ok")

@@ -1,19 +1,19 @@
-// Causal GQA prefill attention on the tcgen05 tensor cores, for the bf16
-// prefill path -- kernels/attention_prefill.wgsl:75 / head_ref.ts:99
+// Causal GQA prefill attention on the tcgen05 tensor cores, for the tensor-
+// core prefill path -- kernels/attention_prefill.wgsl:75 / head_ref.ts:99
 // attnPrefillRef (queries at positions pos0 .. pos0+n-1, query i sees keys
 // 0 .. pos0+i, scale 1/sqrt(head_dim), max-subtracted softmax), re-designed:
 //
 //  * one CTA per (128-query tile, query head); 4 warps; thread t owns query
 //    row t of the tile, which is TMEM lane t of every accumulator, so a row's
 //    max and sum need no cross-thread reduction (tcgen05.ld 32x32b);
-//  * q is staged as bf16 in the K-major 128-byte-swizzled layout (head_dim
-//    128 = two 64-wide swizzle chunks); K and V come from a bf16 image of the
+//  * q is staged as f16 in the K-major 128-byte-swizzled layout (head_dim
+//    128 = two 64-wide swizzle chunks); K and V come from an f16 image of the
 //    cache that k_kv_image builds once per step (per kv head, 128-key tiles
 //    of K and of V transposed to [head_dim][keys], already in that layout),
 //    one bulk copy per tile, so both products read K-major operands;
 //  * pass 1: S = q K^T per 128-key tile (tcgen05.mma 128x128x16, f32 in
 //    TMEM) -> exact row max m;  pass 2: S again, P = e^(S*scale - m) written
-//    as bf16 into shared memory, O += P V^T accumulated in TMEM, l += sum P;
+//    as f16 into shared memory, O += P V^T accumulated in TMEM, l += sum P;
 //    the extra q K^T replaces any rescaling of O;
 //  * out = O / l in f32.
 //
@@ -28,7 +28,7 @@ constexpr int ATC_Q = 128;        // queries per CTA
 constexpr int ATC_K = 128;        // keys per tile
 constexpr int ATC_HD = 128;       // head_dim (two 64-wide swizzle chunks)
 constexpr int ATC_THREADS = 128;
-constexpr int ATC_OPND = ATC_Q * ATC_HD * 2;  // bytes of one 128 x 128 bf16 operand (32 KiB)
+constexpr int ATC_OPND = ATC_Q * ATC_HD * 2;  // bytes of one 128 x 128 f16 operand (32 KiB)
 
 struct AttnTcArgs {
   const float* q;  // [n][nH][hd] normalised + rotated
@@ -46,7 +46,7 @@ FLOCK_DEV uint32_t atc_off(int r, int chunk16) {
   return (uint32_t)(chunk16 >> 3) * (ATC_Q * 128) + sw128_off(r, chunk16 & 7);
 }
 
-// Row r of a 128 x 128 bf16 operand from 128 f32 values at `src` (global),
+// Row r of a 128 x 128 f16 operand from 128 f32 values at `src` (global),
 // or zeros.
 FLOCK_DEV void atc_stage_row(uint8_t* op, int r, const float* src) {
 #pragma unroll 4
@@ -55,20 +55,20 @@ FLOCK_DEV void atc_stage_row(uint8_t* op, int r, const float* src) {
     if (src) {
       const float4 a = __ldg(reinterpret_cast<const float4*>(src) + 2 * c);
       const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 2 * c + 1);
-      o = make_uint4(bf16x2(a.x, a.y), bf16x2(a.z, a.w), bf16x2(b.x, b.y), bf16x2(b.z, b.w));
+      o = make_uint4(h2(a.x, a.y), h2(a.z, a.w), h2(b.x, b.y), h2(b.z, b.w));
     }
     *reinterpret_cast<uint4*>(op + atc_off(r, c)) = o;
   }
 }
 
 // D (TMEM, 128 lanes x 128 columns) (+)= A . B^T over 128 K elements, both
-// 128 x 128 bf16 operands in the two-chunk swizzled layout.
+// 128 x 128 f16 operands in the two-chunk swizzled layout.
 FLOCK_DEV void atc_mma(uint32_t d, uint32_t a, uint32_t b, bool accumulate) {
-  const uint32_t idesc = umma_idesc_bf16(128, 128);
+  const uint32_t idesc = umma_idesc_f16(128, 128);
 #pragma unroll
   for (int k16 = 0; k16 < 8; k16++) {
     const uint32_t off = (uint32_t)(k16 >> 2) * (ATC_Q * 128) + (uint32_t)(k16 & 3) * 32;
-    umma_bf16(d, umma_desc_sw128(a + off), umma_desc_sw128(b + off), idesc,
+    umma_f16(d, umma_desc_sw128(a + off), umma_desc_sw128(b + off), idesc,
               (accumulate || k16 > 0) ? 1u : 0u);
   }
 }
@@ -186,9 +186,9 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
 #pragma unroll
       for (int half = 0; half < 2; half++)
         *reinterpret_cast<uint4*>(sP + atc_off(t, (c0 >> 3) + half)) =
-            make_uint4(bf16x2(p[8 * half], p[8 * half + 1]), bf16x2(p[8 * half + 2], p[8 * half + 3]),
-                       bf16x2(p[8 * half + 4], p[8 * half + 5]),
-                       bf16x2(p[8 * half + 6], p[8 * half + 7]));
+            make_uint4(h2(p[8 * half], p[8 * half + 1]), h2(p[8 * half + 2], p[8 * half + 3]),
+                       h2(p[8 * half + 4], p[8 * half + 5]),
+                       h2(p[8 * half + 6], p[8 * half + 7]));
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -233,7 +233,7 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
 
 inline size_t attn_tc_smem_bytes() { return 4 * (size_t)ATC_OPND + 24 + 1024; }
 
-// The bf16 image of keys [0, kend) of the cache for k_attn_prefill_tc, kend =
+// The f16 image of keys [0, kend) of the cache for k_attn_prefill_tc, kend =
 // ctl[0] + n (the position block already advanced for this step): per (key
 // tile, kv head) one CTA writes the K tile ([key][head_dim], rows past kend
 // zero) and the V^T tile ([head_dim][key]), transposed through shared memory
@@ -267,7 +267,7 @@ static __global__ void __launch_bounds__(ATC_THREADS) k_kv_image(const float* kc
 #pragma unroll
     for (int e = 0; e < 8; e++) v[e] = vbuf[(8 * c + e) * KVI_STRIDE + t];
     *reinterpret_cast<uint4*>(vdst + atc_off(t, c)) =
-        make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]), bf16x2(v[6], v[7]));
+        make_uint4(h2(v[0], v[1]), h2(v[2], v[3]), h2(v[4], v[5]), h2(v[6], v[7]));
   }
 }
 

@@ -263,51 +263,8 @@ struct ConsumerSync {
   FLOCK_DEV void operator()() const { consumers_sync(); }
 };
 
-// x in shared memory: 32-float blocks padded to XPAD floats (lane l reading
-// block l touches distinct banks), and inside each 8-float group the pairs
-// (x_k, x_k+4) adjacent, so one 128-bit read yields two f32x2 operands for
-// fold_q8_packed.  The norm gains are staged in the same layout.
-FLOCK_DEV int xperm(int i) {
-  const int j = i & 31;
-  return (i >> 5) * XPAD + (j & ~7) + 2 * (j & 3) + ((j >> 2) & 1);
-}
-
-// One Q8_0 block against x in packed pairs: xp[4g + k] = (x[8g+k], x[8g+4+k]).
-// The two dot4 chains of a group (weights 8g..8g+3 and 8g+4..8g+7) run as
-// the halves of one f32x2 chain: the same rounded product and three FMAs
-// each (lib.ts:196), then acc = fma(scale, d0 + d1, acc) as fold_block.
-FLOCK_DEV float fold_q8_packed(const BlockW<QT_Q8>& bw, const uint64_t (&xp)[16], float acc) {
-  const float s = scale_f16(bw.s);
-  const uint32_t w[8] = {bw.w0.x, bw.w0.y, bw.w0.z, bw.w0.w, bw.w1.x, bw.w1.y, bw.w1.z, bw.w1.w};
-  const uint64_t k2 = pack2(8388736.0f, 8388736.0f);  // 2^23 + 128
-#pragma unroll
-  for (int g = 0; g < 4; g++) {
-    const uint32_t ua = w[2 * g] ^ 0x80808080u, uc = w[2 * g + 1] ^ 0x80808080u;
-    uint64_t q[4];
-#pragma unroll
-    for (int k = 0; k < 4; k++)
-      q[k] = fsub2(pack2(__uint_as_float(__byte_perm(ua, 0x4B000000u, 0x7540u + k)),
-                         __uint_as_float(__byte_perm(uc, 0x4B000000u, 0x7540u + k))),
-                   k2);
-    uint64_t d = fmul2(q[0], xp[4 * g]);
-    d = ffma2(q[1], xp[4 * g + 1], d);
-    d = ffma2(q[2], xp[4 * g + 2], d);
-    d = ffma2(q[3], xp[4 * g + 3], d);
-    const float2 dd = unpack2(d);
-    acc = ffma(s, fadd(dd.x, dd.y), acc);
-  }
-  return acc;
-}
-
-FLOCK_DEV void load_pairs(const float* xs, int b, uint64_t (&xp)[16]) {
-  const ulonglong2* q = reinterpret_cast<const ulonglong2*>(xs + b * XPAD);
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const ulonglong2 v = q[j];
-    xp[2 * j] = v.x;
-    xp[2 * j + 1] = v.y;
-  }
-}
+// x lives in shared memory in gemv.cuh's packed-pair layout (xperm<QT_Q8>),
+// folded with fold_block_packed; the norm gains are staged the same way.
 
 // x for a GEMV phase: one round trip of 128-bit loads into the packed shared
 // layout, then each lane's block 0 of x into registers (xp).  With `gain`,
@@ -345,7 +302,7 @@ FLOCK_DEV void mk_stage(const float* src, bool src_shared, int K, const float* g
 #pragma unroll
   for (int q = 0; q < 4; q++)
     for (int i = lane + 32 * q; i < K; i += 128) {
-      const float v = xs[xperm(i)];
+      const float v = xs[xperm<QT_Q8>(i)];
       p[q] = ffma(v, v, p[q]);
     }
   float v = fadd(fadd(p[0], p[2]), fadd(p[1], p[3]));
@@ -367,7 +324,7 @@ FLOCK_DEV void mk_stage(const float* src, bool src_shared, int K, const float* g
   }
   consumers_sync();  // every warp has read the unscaled copy
   for (int i = t; i < K; i += MK_CONSUMERS * 32) {
-    const int o = xperm(i);
+    const int o = xperm<QT_Q8>(i);
     xs[o] = fmul(fmul(xs[o], scale), gs[o]);
   }
   consumers_sync();
@@ -382,7 +339,7 @@ FLOCK_DEV void mk_stage_attn(const MkArgs& a, int pos, float* xs, uint64_t (&xp)
   const int splits = attn_splits_for(pos + 1, a.splits);
   for (int h = warp; h < a.nH; h += MK_CONSUMERS)
     attn_combine_warp(a.attn_part + (size_t)h * a.splits * (a.hd + 2), splits, a.hd, lane,
-                      [&](int i, float v) { xs[xperm(h * a.hd + i)] = v; });
+                      [&](int i, float v) { xs[xperm<QT_Q8>(h * a.hd + i)] = v; });
   consumers_sync();
   if (lane < a.nH * a.hd / 32) load_pairs(xs, lane, xp);
 }
@@ -406,16 +363,16 @@ FLOCK_DEV void mk_rows_dot(const uint8_t* const* rq, const uint16_t* const* rs, 
     for (int r = 0; r < R; r++) load_block_smem(bw[r], rq[r], rs[r], b);
     if (m == 0) {
 #pragma unroll
-      for (int r = 0; r < R; r++) accA[r] = fold_q8_packed(bw[r], xp, accA[r]);
+      for (int r = 0; r < R; r++) accA[r] = fold_block_packed<QT_Q8>(bw[r], xp, accA[r]);
     } else {
       uint64_t xb[16];
       load_pairs(xs, b, xb);
       if (m & 1) {
 #pragma unroll
-        for (int r = 0; r < R; r++) accB[r] = fold_q8_packed(bw[r], xb, accB[r]);
+        for (int r = 0; r < R; r++) accB[r] = fold_block_packed<QT_Q8>(bw[r], xb, accB[r]);
       } else {
 #pragma unroll
-        for (int r = 0; r < R; r++) accA[r] = fold_q8_packed(bw[r], xb, accA[r]);
+        for (int r = 0; r < R; r++) accA[r] = fold_block_packed<QT_Q8>(bw[r], xb, accA[r]);
       }
     }
   }

@@ -7,7 +7,7 @@
 #include <cstring>
 #include <string>
 #include <mutex>
-#include <set>
+#include <map>
 #include <vector>
 
 #include "attn_fast.cuh"
@@ -58,14 +58,15 @@ const char* const kTensorNames[W_COUNT] = {
 
 int kernel_setup(const void* func, int max_dyn_smem) {
   static std::mutex mu;
-  static std::set<std::pair<const void*, int>> done;
+  static std::map<std::pair<const void*, int>, int> opted;  // largest opt-in so far
   int dev = 0;
   FLOCK_CK(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lock(mu);
-  if (done.count({func, dev})) return FLOCK_OK;
+  auto it = opted.find({func, dev});
+  if (it != opted.end() && it->second >= max_dyn_smem) return FLOCK_OK;
   if (max_dyn_smem > 0)
     FLOCK_CK(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn_smem));
-  done.insert({func, dev});
+  opted[{func, dev}] = max_dyn_smem;
   return FLOCK_OK;
 }
 
@@ -85,9 +86,9 @@ static cudaError_t launch_ex(cudaStream_t st, void (*k)(KArgs...), dim3 grid, di
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
 
-template <int QT, int R, int EPI, int MX>
+template <int QT, int R, int EPI, int MX, int LA = 1>
 static cudaError_t gemv_go(flock_dev* d, const GemvArgs& a, int ctas, bool pdl) {
-  auto k = k_gemv<QT, R, EPI, MX>;
+  auto k = k_gemv<QT, R, EPI, MX, LA>;
   const size_t smem = gemv_smem_bytes(a.K, a.norm_gain != nullptr);
   if (kernel_setup((const void*)k, 200 * 1024)) return cudaErrorInvalidValue;
   return launch_ex(d->stream, k, dim3(ctas, a.n_tokens), dim3(GEMV_THREADS), smem, pdl, a);
@@ -122,7 +123,11 @@ int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl) {
   }
   const int ctas = gemv_grid(d, groups);
   cudaError_t e = cudaErrorInvalidValue;
-#define GO(qt, r, epi, mx) e = gemv_go<qt, r, epi, mx>(d, a, ctas, pdl)
+// long rows (two or more column blocks per lane) keep one x block in
+// registers and two steps of weights in flight; short rows keep the x
+// blocks and one step
+#define GO(qt, r, epi, mx) \
+  e = (mx) == 1 ? gemv_go<qt, r, epi, 1, 1>(d, a, ctas, pdl) : gemv_go<qt, r, epi, 1, 2>(d, a, ctas, pdl)
   if (QT == QT_Q8) {
     switch (EPI) {
       case EPI_STORE:
@@ -215,7 +220,7 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count) {
   FLOCK_TRY(attn_part.alloc((size_t)nH * attn_split_cap * (hd + 2) * f));
   FLOCK_TRY(attn_count.alloc((size_t)nKV * 4));
   FLOCK_CK(cudaMemset(attn_count.p, 0, attn_count.bytes));
-  if (c.prefill == FLOCK_PREFILL_BF16) {
+  if (c.prefill == FLOCK_PREFILL_TENSOR) {
     size_t ib = act_image_bytes(P, H);
     const size_t iq = act_image_bytes(P, nH * hd), iff = act_image_bytes(P, F);
     ib = ib > iq ? ib : iq;
@@ -253,13 +258,13 @@ static int check_cfg(const flock_layer_config& c) {
     set_error("max_keys and max_prefill must be >= 1");
     return FLOCK_E_ARG;
   }
-  if (c.prefill != FLOCK_PREFILL_EXACT && c.prefill != FLOCK_PREFILL_BF16) {
-    set_error("prefill mode %d is neither FLOCK_PREFILL_EXACT nor FLOCK_PREFILL_BF16", c.prefill);
+  if (c.prefill != FLOCK_PREFILL_EXACT && c.prefill != FLOCK_PREFILL_TENSOR) {
+    set_error("prefill mode %d is neither FLOCK_PREFILL_EXACT nor FLOCK_PREFILL_TENSOR", c.prefill);
     return FLOCK_E_ARG;
   }
-  if (c.prefill == FLOCK_PREFILL_BF16 &&
+  if (c.prefill == FLOCK_PREFILL_TENSOR &&
       (c.hidden % 64 || c.ffn % 64 || c.hidden > 12288 || c.ffn > 12288)) {
-    set_error("bf16 prefill needs hidden %d and ffn %d multiples of 64, at most 12288", c.hidden,
+    set_error("tensor-core prefill needs hidden %d and ffn %d multiples of 64, at most 12288", c.hidden,
               c.ffn);
     return FLOCK_E_UNSUPPORTED;
   }
@@ -341,7 +346,7 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   aa.head_dim = c.head_dim;
   pf_add(aa.pf, L->w[W_UP]);
   if (n > 1 && tensor_cores) {
-    // the bf16 image of keys [0, ctl[0] + n) (pos0 is read on the device)
+    // the f16 image of keys [0, ctl[0] + n) (pos0 is read on the device)
     const int img_tiles = (c.max_keys + ATC_K - 1) / ATC_K;
     FLOCK_TRY(kernel_setup((const void*)k_kv_image, (int)kv_image_smem_bytes()));
     k_kv_image<<<dim3(img_tiles, c.n_kv_heads), ATC_THREADS, kv_image_smem_bytes(),
@@ -384,7 +389,7 @@ static __global__ void k_swiglu_rows(const float* gu, float* act, int n, int F) 
 }
 
 // One prefill step of n > 1 tokens with the four weight matmuls on the
-// tcgen05 tensor cores (FLOCK_PREFILL_BF16); norms, RoPE, attention and the
+// tcgen05 tensor cores (FLOCK_PREFILL_TENSOR); norms, RoPE, attention and the
 // residual adds keep their f32 arithmetic.
 static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
   flock_dev* d = L->dev;
@@ -475,7 +480,7 @@ int ws_check_errors(Workspace* ws) {
 }
 
 int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_next, bool pdl) {
-  if (n > 1 && L->cfg.prefill == FLOCK_PREFILL_BF16) return layer_enqueue_tc(L, n, advance);
+  if (n > 1 && L->cfg.prefill == FLOCK_PREFILL_TENSOR) return layer_enqueue_tc(L, n, advance);
   flock_dev* d = L->dev;
   Workspace* ws = L->ws;
   const flock_layer_config& c = L->cfg;

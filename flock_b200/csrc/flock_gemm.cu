@@ -10,10 +10,16 @@
 
 namespace flock {
 
-size_t act_image_bytes(int M, int K) {
+// The image proper, then one int (the row's scale exponent) per image row.
+static size_t act_image_only_bytes(int M, int K) {
   const int nt = tc_token_tile(M);
   const size_t n_mb = (size_t)(M + nt - 1) / nt;
   return n_mb * (size_t)(K / TC_KT) * (size_t)nt * 128;
+}
+
+size_t act_image_bytes(int M, int K) {
+  const int nt = tc_token_tile(M);
+  return act_image_only_bytes(M, K) + (size_t)((M + nt - 1) / nt) * nt * 4;
 }
 
 int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float* gain, float eps,
@@ -31,6 +37,7 @@ int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float
   a.K = K;
   a.Nt = tc_token_tile(M);
   a.img = img;
+  a.row_exp = reinterpret_cast<int*>(img + act_image_only_bytes(M, K));
   const int rows = (M + a.Nt - 1) / a.Nt * a.Nt;
   const size_t smem = (size_t)ACT_IMG_ROWS * K * 4;
   FLOCK_TRY(kernel_setup((const void*)k_act_image, ACT_IMG_ROWS * 12288 * 4));
@@ -86,6 +93,7 @@ int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a, int sm_count,
                     size_t part_floats) {
   if (a.K % TC_KT || a.M < 1 || a.nseg < 1 || a.nseg > 3) return FLOCK_E_ARG;
   a.Nt = tc_token_tile(a.M);
+  a.row_exp = reinterpret_cast<const int*>(a.img + act_image_only_bytes(a.M, a.K));
   tc_finish_tiles(a);
   a.ksplit = 1;
   const int ctas = a.tile0[a.nseg] * ((a.M + a.Nt - 1) / a.Nt);

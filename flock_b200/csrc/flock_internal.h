@@ -89,9 +89,9 @@ struct Workspace {
   DBuf attn_part, attn_count;  // fast decode attention partials
   int attn_splits = 16;         // splits: SMs / kv heads, so one wave covers them
   int attn_split_cap = 32;      // partial slots allocated per head (attn_max_splits' bound)
-  DBuf img, gu, tc_err, part;   // bf16 prefill: activation image, gate|up rows, error word,
+  DBuf img, gu, tc_err, part;   // tensor-core prefill: activation image, gate|up rows, error word,
                                 // split-K partials
-  DBuf kv_img;                  // bf16 prefill: bf16 K / V^T tiles of the cache
+  DBuf kv_img;                  // tensor-core prefill: f16 K / V^T tiles of the cache
   int alloc(const flock_layer_config& c, int sm_count);
 };
 
@@ -110,7 +110,7 @@ int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float
 int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a, int sm_count,
                     size_t part_floats);
 TcSeg tc_seg_of(const flock_tensor* t, float* out, int out_stride);
-// bf16 prefill's device error word: FLOCK_E_CUDA (and cleared) if a tensor-core
+// tensor-core prefill's device error word: FLOCK_E_CUDA (and cleared) if a tensor-core
 // GEMM gave up waiting since the last check; call after a synchronisation.
 int ws_check_errors(Workspace* ws);
 int gemv_grid(flock_dev* d, int total_groups);

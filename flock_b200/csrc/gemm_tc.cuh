@@ -2,21 +2,28 @@
 // weights -- kernels/q8_coop.wgsl:76 / q4_coop.wgsl:48 at M > 1 tokens
 // (layer.ts:685 encodePrefill), re-designed for B200:
 //
-//   Y[m][n] = sum_k X[m][k] * W[n][k],  X f32 -> bf16, W = s * q -> bf16,
-//   f32 accumulation in tensor memory.
+//   Y[m][n] = sum_k X[m][k] * W[n][k],  X f32 -> f16 (a power-of-two scale
+//   per token row), W = s * q -> f16, f32 accumulation in tensor memory.
+//
+//  * 16-bit operands are f16, not bf16: kind::f16 runs both at the same rate
+//    and f16's 11-bit significand rounds 8x more finely (per-GEMM error
+//    ~3e-4 instead of ~2e-3 at K = 4096-12288).  Each activation row is
+//    scaled by 2^-e so its largest magnitude lies in [2^13, 2^14) before the
+//    rounding (no overflow, full precision), and the epilogue multiplies by
+//    2^e, which is exact.  Weights q * s are exact in f32 and rounded once.
 //
 //  * Operands are swapped for small M: 128 weight rows form the MMA's M and
 //    up to 256 tokens its N, so a 16-token prefill still issues full-height
 //    tcgen05.mma.cta_group::1.kind::f16 (128 x Nt x 16) instructions.
 //  * Producers (8 warps, two threads per weight row: one 32-weight block each
 //    per K-tile) keep 6 K-tiles of raw int8 / nibble weights in flight in
-//    registers, dequantise q * s in f32 (packed f32x2), round to bf16 and
+//    registers, dequantise q * s in f32 (packed f32x2), round to f16 and
 //    write the K-major 128-byte-swizzled layout the UMMA
 //    shared-memory descriptor names (8-row x 128-byte atoms, 16-byte chunk
-//    c of row r at (c ^ r % 8)).  int8 values are exact in bf16, so the only
-//    weight rounding is that of the scaled value.
+//    c of row r at (c ^ r % 8)).  The only weight rounding is that of the
+//    scaled value.
 //  * Activations come from an image the caller builds once per GEMM
-//    (k_act_image: RMSNorm fused, bf16, same swizzled layout, Nt rows per
+//    (k_act_image: RMSNorm fused, f16, same swizzled layout, Nt rows per
 //    K-tile contiguous), so each stage's B tile is one bulk copy.
 //  * One thread issues the MMAs; tcgen05.commit returns each stage to the
 //    producers through an mbarrier and signals the epilogue after the last
@@ -28,7 +35,7 @@
 // Every wait is bounded (mbar_wait); on a timeout the kernel sets *err,
 // still releases its tensor memory and returns.  No multicast is used.
 #pragma once
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "gemv.cuh"
@@ -37,12 +44,12 @@
 namespace flock {
 
 constexpr int TC_ROWS = 128;              // weight rows per CTA: the MMA's M
-constexpr int TC_KT = 64;                 // K per stage: one 128-byte bf16 swizzle atom row
+constexpr int TC_KT = 64;                 // K per stage: one 128-byte f16 swizzle atom row
 constexpr int TC_STAGES = 4;
 constexpr int TC_MAX_NT = 256;            // tokens per CTA: the MMA's N
 constexpr int TC_PRODUCERS = 256;         // 8 warps: producers, then the epilogue
 constexpr int TC_THREADS = TC_PRODUCERS + 32;  // + the MMA warp
-constexpr int TC_A_BYTES = TC_ROWS * TC_KT * 2;  // 16 KiB of bf16 per stage
+constexpr int TC_A_BYTES = TC_ROWS * TC_KT * 2;  // 16 KiB of f16 per stage
 constexpr int TC_PREFETCH = 6;            // K-tiles of raw weights in flight per thread
 
 struct TcSeg {
@@ -59,7 +66,8 @@ struct TcArgs {
   int nseg;
   int tile0[4];      // first 128-row tile of each segment; tile0[nseg] = all tiles
   int K, M, Nt;      // Nt: tokens per CTA (multiple of 16, <= 256)
-  const uint8_t* img;  // activation image: [M / Nt][K / 64][Nt][128 B] bf16, swizzled
+  const uint8_t* img;  // activation image: [M / Nt][K / 64][Nt][128 B] f16, swizzled
+  const int* row_exp;  // e of each image row: the row was scaled by 2^-e
   const float* res;    // EPI_RESIDUAL: y += res[m][n] (res may alias the output)
   int res_stride;
   int* err;
@@ -85,8 +93,8 @@ FLOCK_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
                : "memory");
 }
-// D[tmem] (+)= A[smem desc] . B[smem desc]^T, bf16 inputs, f32 accumulator.
-FLOCK_DEV void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+// D[tmem] (+)= A[smem desc] . B[smem desc]^T, f16 inputs, f32 accumulator.
+FLOCK_DEV void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                          uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
@@ -126,21 +134,32 @@ FLOCK_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) |
          ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// Instruction descriptor, kind::f16: f32 D (bits 4-5 = 1), bf16 A and B
-// (bits 7-9, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-FLOCK_DEV uint32_t umma_idesc_bf16(int m, int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
-         ((uint32_t)(m >> 4) << 24);
+// Instruction descriptor, kind::f16: f32 D (bits 4-5 = 1), f16 A and B
+// (bits 7-9, 10-12 = 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+FLOCK_DEV uint32_t umma_idesc_f16(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-// Byte offset of 16-byte chunk c (8 bf16, K elements 8c..8c+7 of a K-tile)
+// Byte offset of 16-byte chunk c (8 f16, K elements 8c..8c+7 of a K-tile)
 // of row r inside a K-tile block of 128-byte rows.
 FLOCK_DEV uint32_t sw128_off(int r, int c) { return (uint32_t)r * 128u + (uint32_t)((c ^ (r & 7)) << 4); }
 
-FLOCK_DEV uint32_t bf16x2(float lo, float hi) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+// Two f32 -> f16 (round to nearest even), lo in the low half.
+FLOCK_DEV uint32_t h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
+
+// e with max_abs in [2^(e+13), 2^(e+14)): scaling a row by 2^-e puts its
+// largest magnitude in [2^13, 2^14).  0 for an all-zero row; clamped to
+// [-120, 120] so 2^e and 2^-e are normal floats.
+FLOCK_DEV int row_exponent(float max_abs) {
+  const int biased = (int)((__float_as_uint(max_abs) >> 23) & 0xFFu);
+  const int e = biased == 0 ? 0 : biased - 127 - 13;
+  return e < -120 ? -120 : (e > 120 ? 120 : e);
+}
+// 2^e for e in [-126, 127], exactly.
+FLOCK_DEV float pow2f(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 
 // Raw weights of one block (32 weights) of a row for one K-tile.
 struct TcRaw {
@@ -163,7 +182,7 @@ FLOCK_DEV void tc_load_raw(TcRaw& r, const TcSeg& sg, int K, int row, int half, 
   r.s = __ldg(sg.sc + (size_t)row * sg.sc_stride + kt * 2 + half);
 }
 
-// bf16(q * s) for the four int8 / nibble values of word u, two per packed op.
+// f16(q * s) for the four int8 / nibble values of word u, two per packed op.
 FLOCK_DEV uint2 tc_dequant4(uint32_t u, uint64_t bias2, uint64_t s2) {
   const uint64_t a = fmul2(fsub2(pack2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u)),
                                        __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541u))),
@@ -174,12 +193,13 @@ FLOCK_DEV uint2 tc_dequant4(uint32_t u, uint64_t bias2, uint64_t s2) {
                                  bias2),
                            s2);
   const float2 fa = unpack2(a), fb = unpack2(b);
-  return make_uint2(bf16x2(fa.x, fa.y), bf16x2(fb.x, fb.y));
+  return make_uint2(h2(fa.x, fa.y), h2(fb.x, fb.y));
 }
 
 // Dequantise one block into chunks 4*half .. 4*half+3 of row t's swizzled
 // 128-byte row of the A stage.  The integers come out exact (2^23 + bias
-// trick), then q * s rounds once in f32 and once to bf16.
+// trick), q * s is exact in f32 (8 x 11 significant bits) and rounds once to
+// f16.
 template <int QT>
 FLOCK_DEV void tc_store_block(const TcRaw& r, uint8_t* A, int t, int half) {
   const float s = scale_f16((uint16_t)(r.s & 0xFFFFu));
@@ -315,6 +335,7 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
         for (int j = 0; j < 16; j++) {
           const int m = m0 + c0 + j;
           if (m < a.M) {
+            v[j] = v[j] * pow2f(a.row_exp[m]);  // undo the row's power-of-two scale (exact)
             if (split) {
               a.part[((size_t)blockIdx.z * a.M + m) * sg.rows + row] = v[j];
             } else {
@@ -327,7 +348,7 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
     }
   } else if (lane == 0) {
     // ----------------------------------------------------------- MMA issuer
-    const uint32_t idesc = umma_idesc_bf16(TC_ROWS, Nt);
+    const uint32_t idesc = umma_idesc_f16(TC_ROWS, Nt);
     for (int kt = 0; kt < KT; kt++) {
       const int st = kt % TC_STAGES;
       if (!mbar_wait(&full[st], (uint32_t)((kt / TC_STAGES) & 1), a.err)) {
@@ -338,7 +359,7 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
       const uint32_t A = smem_u32(tsm + (size_t)st * stage_bytes), B = A + TC_A_BYTES;
 #pragma unroll
       for (int k16 = 0; k16 < TC_KT / 16; k16++)
-        umma_bf16(tmem, umma_desc_sw128(A + 32 * k16), umma_desc_sw128(B + 32 * k16), idesc,
+        umma_f16(tmem, umma_desc_sw128(A + 32 * k16), umma_desc_sw128(B + 32 * k16), idesc,
                   (kt | k16) != 0);
       umma_commit(&empty[st]);
     }
@@ -376,12 +397,14 @@ inline size_t gemm_tc_smem_bytes(int nt) {
 }
 
 // ------------------------------------------------------- activation image
-// X (f32 [M][x_stride]) -> bf16 image [M / Nt][K / 64][Nt][128 B] in the
+// X (f32 [M][x_stride]) -> f16 image [M / Nt][K / 64][Nt][128 B] in the
 // swizzled K-major layout, RMSNorm fused when `gain` is set (ops_ref.ts:20
 // order: WG = 128 strided partials -- lane l of the warp folds partials l,
 // l+32, l+64, l+96 -- the pairwise tree, 1/sqrt in f64 rounded once, then
-// x * scale * gain rounded per multiply).  One warp per image row, no block
-// barriers; rows >= M are written as zeros.
+// x * scale * gain rounded per multiply); each row is scaled by 2^-e
+// (row_exponent of its largest magnitude) before rounding to f16 and e is
+// stored in row_exp.  One warp per image row, no block barriers; rows >= M
+// are written as zeros.
 struct ActImgArgs {
   const float* x;
   int x_stride;
@@ -389,6 +412,7 @@ struct ActImgArgs {
   float eps;
   int M, K, Nt;
   uint8_t* img;
+  int* row_exp;
 };
 
 constexpr int ACT_IMG_THREADS = 128;
@@ -406,6 +430,7 @@ static __global__ void __launch_bounds__(ACT_IMG_THREADS) k_act_image(const ActI
     for (int i = lane; i < a.K / 8; i += 32)
       *reinterpret_cast<uint4*>(base + (size_t)(i >> 3) * a.Nt * 128 + sw128_off(r, i & 7)) =
           make_uint4(0, 0, 0, 0);
+    if (lane == 0) a.row_exp[m] = 0;
     return;
   }
   float* xr = xrows + (size_t)warp * a.K;
@@ -423,20 +448,39 @@ static __global__ void __launch_bounds__(ACT_IMG_THREADS) k_act_image(const ActI
     v = __shfl_sync(0xffffffffu, v, 0);
     scale = rsqrt_f64r(fadd(fdiv(v, (float)a.K), a.eps));
   }
+  // pass 1: the row's final values (in place) and their largest magnitude
+  float mx = 0.0f;
+#pragma unroll 4
+  for (int i = lane; i < a.K / 8; i += 32) {
+    float4* p = reinterpret_cast<float4*>(xr) + 2 * i;
+    float4 x0 = p[0], x1 = p[1];
+    if (a.gain) {
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gain) + 2 * i);
+      const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gain) + 2 * i + 1);
+      x0 = make_float4(fmul(fmul(x0.x, scale), g0.x), fmul(fmul(x0.y, scale), g0.y),
+                       fmul(fmul(x0.z, scale), g0.z), fmul(fmul(x0.w, scale), g0.w));
+      x1 = make_float4(fmul(fmul(x1.x, scale), g1.x), fmul(fmul(x1.y, scale), g1.y),
+                       fmul(fmul(x1.z, scale), g1.z), fmul(fmul(x1.w, scale), g1.w));
+      p[0] = x0;
+      p[1] = x1;
+    }
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x0.x), fabsf(x0.y)), fmaxf(fabsf(x0.z), fabsf(x0.w))));
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x1.x), fabsf(x1.y)), fmaxf(fabsf(x1.z), fabsf(x1.w))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int e = row_exponent(mx);
+  if (lane == 0) a.row_exp[m] = e;
+  __syncwarp();
+  // pass 2: x * 2^-e (exact) rounded to f16, swizzled
+  const float sc = pow2f(-e);
 #pragma unroll 4
   for (int i = lane; i < a.K / 8; i += 32) {
     const float4 x0 = reinterpret_cast<const float4*>(xr)[2 * i];
     const float4 x1 = reinterpret_cast<const float4*>(xr)[2 * i + 1];
-    float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-    if (a.gain) {
-      const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gain) + 2 * i);
-      const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gain) + 2 * i + 1);
-      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-#pragma unroll
-      for (int e = 0; e < 8; e++) v[e] = fmul(fmul(v[e], scale), g[e]);
-    }
     *reinterpret_cast<uint4*>(base + (size_t)(i >> 3) * a.Nt * 128 + sw128_off(r, i & 7)) =
-        make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]), bf16x2(v[6], v[7]));
+        make_uint4(h2(x0.x * sc, x0.y * sc), h2(x0.z * sc, x0.w * sc), h2(x1.x * sc, x1.y * sc),
+                   h2(x1.z * sc, x1.w * sc));
   }
 }
 

@@ -139,6 +139,98 @@ FLOCK_DEV float fold_block<QT_Q4>(const BlockW<QT_Q4>& bw, const float4* xb, flo
 constexpr int XPAD = 36;
 FLOCK_DEV int xpad(int i) { return (i >> 5) * XPAD + (i & 31); }
 
+// The packed-pair layout the f32x2 folds (persistent decode kernel) read:
+// inside each padded 32-float
+// block, u64 element 4g + k holds the two x values that weight pair k of
+// group g multiplies -- Q8_0 (x[8g+k], x[8g+4+k]), Q4_0 (x[4g+k],
+// x[16+4g+k]) -- so a 128-bit shared read yields two f32x2 operands.
+template <int QT>
+FLOCK_DEV int xperm(int i) {
+  const int j = i & 31;
+  const int p = QT == QT_Q8 ? (j & ~7) + 2 * (j & 3) + ((j >> 2) & 1) : 2 * (j & 15) + (j >> 4);
+  return (i >> 5) * XPAD + p;
+}
+
+// n floats of src (global or shared) into xs in the packed-pair layout.
+template <int QT>
+FLOCK_DEV void stage_x_packed(const float* src, int n, float* xs, int tid, int nthreads) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  for (int i = tid; i < n / 8; i += nthreads) {
+    const int b = i >> 2, q = i & 3;
+    // Q8_0: the 8-float group i; Q4_0: floats 4q.. and 16+4q.. of block b
+    const float4 lo = QT == QT_Q8 ? s4[2 * i] : s4[b * 8 + q];
+    const float4 hi = QT == QT_Q8 ? s4[2 * i + 1] : s4[b * 8 + 4 + q];
+    float4* d = reinterpret_cast<float4*>(xs + b * XPAD + q * 8);
+    d[0] = make_float4(lo.x, hi.x, lo.y, hi.y);
+    d[1] = make_float4(lo.z, hi.z, lo.w, hi.w);
+  }
+}
+
+// Block b of packed x as 16 pairs.
+FLOCK_DEV void load_pairs(const float* xs, int b, uint64_t (&xp)[16]) {
+  const ulonglong2* q = reinterpret_cast<const ulonglong2*>(xs + b * XPAD);
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const ulonglong2 v = q[j];
+    xp[2 * j] = v.x;
+    xp[2 * j + 1] = v.y;
+  }
+}
+
+// fold_block on packed pairs: the two dot4 chains of a group run as the
+// halves of one f32x2 chain (each half rounds as the scalar instruction),
+// then acc = fma(scale, d0 + d1, acc) -- fold_block's arithmetic exactly.
+template <int QT>
+FLOCK_DEV float fold_block_packed(const BlockW<QT>& bw, const uint64_t (&xp)[16], float acc);
+template <>
+FLOCK_DEV float fold_block_packed<QT_Q8>(const BlockW<QT_Q8>& bw, const uint64_t (&xp)[16],
+                                         float acc) {
+  const float s = scale_f16(bw.s);
+  const uint32_t w[8] = {bw.w0.x, bw.w0.y, bw.w0.z, bw.w0.w, bw.w1.x, bw.w1.y, bw.w1.z, bw.w1.w};
+  const uint64_t k2 = pack2(8388736.0f, 8388736.0f);  // 2^23 + 128
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    const uint32_t ua = w[2 * g] ^ 0x80808080u, uc = w[2 * g + 1] ^ 0x80808080u;
+    uint64_t q[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+      q[k] = fsub2(pack2(__uint_as_float(__byte_perm(ua, 0x4B000000u, 0x7540u + k)),
+                         __uint_as_float(__byte_perm(uc, 0x4B000000u, 0x7540u + k))),
+                   k2);
+    uint64_t d = fmul2(q[0], xp[4 * g]);
+    d = ffma2(q[1], xp[4 * g + 1], d);
+    d = ffma2(q[2], xp[4 * g + 2], d);
+    d = ffma2(q[3], xp[4 * g + 3], d);
+    const float2 dd = unpack2(d);
+    acc = ffma(s, fadd(dd.x, dd.y), acc);
+  }
+  return acc;
+}
+template <>
+FLOCK_DEV float fold_block_packed<QT_Q4>(const BlockW<QT_Q4>& bw, const uint64_t (&xp)[16],
+                                         float acc) {
+  const float s = scale_f16(bw.s);
+  const uint32_t w[4] = {bw.w.x, bw.w.y, bw.w.z, bw.w.w};
+  const uint64_t k2 = pack2(8388616.0f, 8388616.0f);  // 2^23 + 8
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    const uint32_t lo = w[g] & 0x0F0F0F0Fu, hi = (w[g] >> 4) & 0x0F0F0F0Fu;
+    uint64_t q[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+      q[k] = fsub2(pack2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7540u + k)),
+                         __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7540u + k))),
+                   k2);
+    uint64_t d = fmul2(q[0], xp[4 * g]);
+    d = ffma2(q[1], xp[4 * g + 1], d);
+    d = ffma2(q[2], xp[4 * g + 2], d);
+    d = ffma2(q[3], xp[4 * g + 3], d);
+    const float2 dd = unpack2(d);
+    acc = ffma(s, fadd(dd.x, dd.y), acc);
+  }
+  return acc;
+}
+
 // kernels/argmax.wgsl:57 better(): strictly larger, or equal with lower index.
 FLOCK_DEV bool am_better(float va, uint32_t ia, float vb, uint32_t ib) {
   return va > vb || (va == vb && ia < ib);
@@ -226,7 +318,10 @@ FLOCK_DEV void rows_of(const GemvArgs& a, int g, Rows<R>& rs) {
 
 // MX: how many of each thread's x blocks (lane + 32m, m < MX) stay in
 // registers; the rest are read from shared memory.
-template <int QT, int R, int EPI, int MX>
+// LA: steps in flight ahead of the one being folded (1, or 2 for long rows,
+// where each warp walks several column blocks per row and one step of
+// lookahead leaves HBM latency exposed).
+template <int QT, int R, int EPI, int MX, int LA = 1>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(16) float smem[];
   const bool norm = a.norm_gain != nullptr;
@@ -267,6 +362,26 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
         if (rs.ok[r]) load_block<QT>(cur[r], a.seg[rs.seg[r]], rs.row[r], lane, a.K);
     }
   }
+  // LA = 2: the following step is in flight too
+  int g1 = g, m1 = 0;
+  bool have1 = false;
+  Rows<R> rs1 = rs;
+  BlockW<QT> nx1[R];
+  if (LA == 2) {
+    m1 = m + 1;
+    if (m1 == M) {
+      m1 = 0;
+      g1 = g + nwarps;
+    }
+    have1 = have && g1 < n_groups;
+    if (have1 && m1 == 0) rows_of<R, EPI>(a, g1, rs1);
+    const int b1 = lane + 32 * m1;
+    if (have1 && b1 < nb) {
+#pragma unroll
+      for (int r = 0; r < R; r++)
+        if (rs1.ok[r]) load_block<QT>(nx1[r], a.seg[rs1.seg[r]], rs1.row[r], b1, a.K);
+    }
+  }
 
   issue_prefetch(a.pf);
   pdl_launch_dependents();
@@ -305,14 +420,15 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   uint32_t best_i = 0xFFFFFFFFu;
 
   while (have) {
-    // issue the next step's loads before folding this one
-    int g2 = g, m2 = m + 1;
+    // issue the loads of the step LA ahead before folding this one
+    const int gb = LA == 2 ? g1 : g, mb = LA == 2 ? m1 : m;
+    int g2 = gb, m2 = mb + 1;
     if (m2 == M) {
       m2 = 0;
-      g2 = g + nwarps;
+      g2 = gb + nwarps;
     }
-    const bool have2 = g2 < n_groups;
-    Rows<R> rs2 = rs;
+    const bool have2 = (LA == 2 ? have1 : true) && g2 < n_groups;
+    Rows<R> rs2 = LA == 2 ? rs1 : rs;
     if (have2 && m2 == 0) rows_of<R, EPI>(a, g2, rs2);
     BlockW<QT> nxt[R];
     const int b2 = lane + 32 * m2;
@@ -334,14 +450,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
             accA[r] = fold_block<QT>(cur[r], xb, accA[r]);
         }
       };
-      if constexpr (MX >= 2) {
-        if (m == 0) fold_all(xr[0]);
-        else if (m == 1) fold_all(xr[MX >= 2 ? 1 : 0]);
-        else fold_all(xs4 + b * (XPAD / 4));
-      } else {
-        if (m == 0) fold_all(xr[0]);
-        else fold_all(xs4 + b * (XPAD / 4));
-      }
+      if (m < MX)
+        fold_all(xr[MX >= 2 && m == 1 ? 1 : 0]);
+      else
+        fold_all(xs4 + b * (XPAD / 4));
     }
 
     if (m == M - 1) {
@@ -382,12 +494,28 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
       }
     }
 
+    if (LA == 2) {
 #pragma unroll
-    for (int r = 0; r < R; r++) cur[r] = nxt[r];
-    g = g2;
-    m = m2;
-    rs = rs2;
-    have = have2;
+      for (int r = 0; r < R; r++) {
+        cur[r] = nx1[r];
+        nx1[r] = nxt[r];
+      }
+      g = g1;
+      m = m1;
+      rs = rs1;
+      have = have1;
+      g1 = g2;
+      m1 = m2;
+      rs1 = rs2;
+      have1 = have2;
+    } else {
+#pragma unroll
+      for (int r = 0; r < R; r++) cur[r] = nxt[r];
+      g = g2;
+      m = m2;
+      rs = rs2;
+      have = have2;
+    }
   }
 
   if (EPI == EPI_ARGMAX) {

@@ -42,7 +42,7 @@ class LayerConfig:
     # "fast": split-K flash-decode, uncapped keys, 1e-5 relative tolerance.
     attention: str = "exact"
     # multi-token steps: "exact" (the reference's f32 order, bit-comparable) or
-    # "bf16" (tcgen05 tensor cores, bf16 operands, 1e-2 relative tolerance)
+    # "tensor" (tcgen05 tensor cores, f16 operands, 1e-2 relative tolerance)
     prefill: str = "exact"
 
     def to_c(self) -> _abi.LayerConfigC:
@@ -51,7 +51,7 @@ class LayerConfig:
             self.rope_base, self.max_keys, self.max_prefill,
             _abi.FLOCK_ROPE_NEOX if self.rope_pairing == "neox" else _abi.FLOCK_ROPE_NORM,
             _abi.FLOCK_ATTN_EXACT if self.attention == "exact" else _abi.FLOCK_ATTN_FAST,
-            _abi.FLOCK_PREFILL_BF16 if self.prefill == "bf16" else _abi.FLOCK_PREFILL_EXACT)
+            _abi.FLOCK_PREFILL_TENSOR if self.prefill == "tensor" else _abi.FLOCK_PREFILL_EXACT)
 
     def with_(self, **kw) -> "LayerConfig":
         return replace(self, **kw)

@@ -45,7 +45,7 @@ def matvec_timed(dev: Device, w: GpuTensor, n_tokens: int = 1, iters: int = 50) 
 
 
 def gemm(dev: Device, w: GpuTensor, x: np.ndarray, m: int) -> np.ndarray:
-    """[m][cols] x W^T on the tensor cores (bf16 operands, f32 accumulation)."""
+    """[m][cols] x W^T on the tensor cores (f16 operands, f32 accumulation)."""
     x = _f32(x)
     if x.size != m * w.cols:
         raise ValueError(f"x is {x.size} floats, want {m * w.cols}")

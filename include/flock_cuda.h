@@ -55,9 +55,10 @@ extern "C" {
 #define FLOCK_ATTN_EXACT 0 /* decode attention in attnRef's exact order (ops_ref.ts:135) */
 #define FLOCK_ATTN_FAST 1  /* split-K flash-decode; no key cap; tolerance 1e-5 rel */
 
-#define FLOCK_PREFILL_EXACT 0 /* prefill matmuls in the reference's f32 order (bit-exact) */
-#define FLOCK_PREFILL_BF16 1  /* prefill matmuls on the tcgen05 tensor cores: bf16 operands,
-                                 f32 accumulation, max relative error 1e-2 */
+#define FLOCK_PREFILL_EXACT 0  /* prefill in the reference's f32 order (bit-exact) */
+#define FLOCK_PREFILL_TENSOR 1 /* prefill matmuls and attention on the tcgen05 tensor cores:
+                                  16-bit (f16) operands, f32 accumulation, max relative
+                                  error 1e-2 */
 
 typedef struct flock_dev flock_dev;
 typedef struct flock_tensor flock_tensor;
@@ -80,7 +81,7 @@ typedef struct flock_layer_config {
   int32_t max_prefill;  /* largest prefill batch (sizes activations) */
   int32_t rope_pairing; /* FLOCK_ROPE_NEOX | FLOCK_ROPE_NORM */
   int32_t attention;    /* FLOCK_ATTN_EXACT | FLOCK_ATTN_FAST */
-  int32_t prefill;      /* FLOCK_PREFILL_EXACT | FLOCK_PREFILL_BF16 (multi-token steps) */
+  int32_t prefill;      /* FLOCK_PREFILL_EXACT | FLOCK_PREFILL_TENSOR (multi-token steps) */
 } flock_layer_config;
 
 /* ------------------------------------------------------------- errors/dev */
@@ -143,8 +144,9 @@ FLOCK_API int flock_op_matvec_timed(flock_dev* dev, const flock_tensor* w, int n
                                     float* ms_per_call);
 /* The prefill matmul of layer.ts:685 encodePrefill (q8_coop.wgsl:76 /
  * q4_coop.wgsl:48 over M tokens) on the tcgen05 tensor cores: y[m][r] =
- * W x[m] with x and s * q rounded to bf16 and f32 accumulation (the bf16
- * prefill path: max relative error <= 1e-2).  x is [M][cols],
+ * W x[m] with s * q and x (scaled per row by a power of two) rounded to f16
+ * and f32 accumulation (the tensor-core prefill path: max relative error
+ * <= 1e-2).  x is [M][cols],
  * y [M][rows]; cols must be a multiple of 64 and at most 12288. */
 FLOCK_API int flock_op_gemm(flock_dev* dev, const flock_tensor* w, const float* x, int M, float* y);
 /* Device-resident timing of flock_op_gemm over `iters` calls on a seeded

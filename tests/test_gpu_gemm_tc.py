@@ -2,10 +2,12 @@
 references of the same matmul:
 
 * exact math (dequantised weights, f32 activations): max relative error
-  <= 1e-2, the bf16 prefill bound, as absErrScaled (ops_ref.ts:206);
-* the same product of bf16-rounded operands (x and s * q rounded to nearest
-  even): agreement to 1e-4, which leaves room only for f32 accumulation order
-  and pins the operand layouts, swizzle and descriptors.
+  <= 1e-2, the tensor-core prefill bound, as absErrScaled (ops_ref.ts:206);
+* the same product of the f16 operands the kernel forms (s * q rounded to
+  f16; each x row scaled by the power of two that puts its largest magnitude
+  in [2^13, 2^14), rounded to f16, scaled back): agreement to 1e-4, which
+  leaves room only for f32 accumulation order and pins the operand layouts,
+  swizzle, descriptors and row scaling.
 """
 import numpy as np
 import pytest
@@ -38,11 +40,20 @@ def dequant(packed: np.ndarray, rows: int, cols: int, q8: bool) -> np.ndarray:
     return (q * s[:, :, None]).reshape(rows, cols)
 
 
-def bf16(a: np.ndarray) -> np.ndarray:
-    """Round f32 values to bf16 (nearest even), returned as f64."""
-    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
-    u = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
-    return u.astype(np.uint32).view(np.float32).astype(np.float64)
+def f16w(w: np.ndarray) -> np.ndarray:
+    """s * q (exact in f32) rounded to f16, as f64."""
+    return np.asarray(w, np.float32).astype(np.float16).astype(np.float64)
+
+
+def f16x(x: np.ndarray) -> np.ndarray:
+    """Each row scaled by 2^-e (e = exponent of its largest magnitude - 13),
+    rounded to f16, scaled back, as f64."""
+    x = np.asarray(x, np.float32)
+    mx = np.abs(x).max(axis=1)
+    _, ex = np.frexp(mx)                   # mx = f * 2^ex, f in [0.5, 1)
+    e = np.clip(np.where(mx > 0, ex - 1 - 13, 0), -120, 120)
+    sc = np.ldexp(np.ones_like(mx, dtype=np.float64), -e)[:, None]
+    return (x.astype(np.float64) * sc).astype(np.float16).astype(np.float64) / sc
 
 
 CASES = [
@@ -68,7 +79,7 @@ def test_gemm_matches_references(dev, q8, rows, cols, m):
     w = dequant(packed, rows, cols, q8)
     exact = x.reshape(m, cols).astype(np.float64) @ w.T
     assert abs_err_scaled(y, exact) <= 1e-2
-    rounded = bf16(x.reshape(m, cols)) @ bf16(w.astype(np.float32)).T
+    rounded = f16x(x.reshape(m, cols)) @ f16w(w).T
     assert abs_err_scaled(y, rounded) <= 1e-4
 
 
@@ -80,7 +91,7 @@ def test_gemm_lm_head_rows(dev):
     x = synth.normal(13, "xh", m * cols).astype(np.float32)
     y = ops.gemm(dev, t, x, m).reshape(m, rows).astype(np.float64)
     w = dequant(packed, rows, cols, True)
-    rounded = bf16(x.reshape(m, cols)) @ bf16(w.astype(np.float32)).T
+    rounded = f16x(x.reshape(m, cols)) @ f16w(w).T
     assert abs_err_scaled(y, rounded) <= 1e-4
 
 

@@ -147,3 +147,72 @@ def test_full_06b_model_greedy_ids(dev, oracle):
         got.append(M.step([got[-1]]))
         want.append(ref.step([want[-1]]))
     assert got == want
+
+
+S8 = synth.QWEN3_8B
+CFG8 = dict(hidden=S8.hidden, n_heads=S8.n_heads, n_kv_heads=S8.n_kv_heads,
+            head_dim=S8.head_dim, ffn=S8.ffn)
+
+
+@pytest.fixture(scope="module")
+def small8b():
+    return synth.model(210, S8, n_layers=2, vocab=4096)
+
+
+def _cfg8(**kw):
+    from flock_b200.layer import LayerConfig
+    return LayerConfig(hidden=S8.hidden, n_heads=S8.n_heads, n_kv_heads=S8.n_kv_heads,
+                       head_dim=S8.head_dim, ffn=S8.ffn, **kw)
+
+
+def test_8b_shape_greedy_ids(dev, oracle, small8b):
+    """Config 4's layer shape (hidden 4096, GQA group 4, ffn 12288, untied
+    head) on 2 layers: greedy ids equal the oracle's, exact attention."""
+    m = small8b
+    M = Model.create(dev, m, _cfg8())
+    oracle.set_fma_mode(True)
+    try:
+        layers = [oracle.RefLayer(w, CFG8, 256) for w in m.layers]
+
+        def ref_step(ids):
+            n = len(ids)
+            h = oracle.embed(m.embd["packed"], ids, S8.hidden)
+            for L in layers:
+                h = L.forward(h, n)
+            tok, _, _ = oracle.head(h[(n - 1) * S8.hidden:], m.output_norm, m.output["packed"],
+                                    m.vocab, S8.hidden)
+            return int(tok)
+
+        prompt = [5, 4000, 17, 123]
+        got = [M.step(prompt)]
+        want = [ref_step(prompt)]
+        for _ in range(3):
+            got.append(M.step([got[-1]]))
+            want.append(ref_step([want[-1]]))
+    finally:
+        oracle.set_fma_mode(False)
+    assert got == want
+
+
+def test_8b_shape_persistent_equals_kernels(dev, small8b):
+    """The persistent decode kernel at the 8B shape (K = 4096 / 12288 staging
+    through shared memory, GQA group 4) is bit-identical to the kernel graph."""
+    a = Model.create(dev, small8b, _cfg8(attention="fast"))
+    b = Model.create(dev, small8b, _cfg8(attention="fast"))
+    a.decode_mode = "persistent"
+    if a.decode_mode != "persistent":
+        pytest.skip("persistent kernel does not fit this shape")
+    for M in (a, b):
+        M.step([9, 8, 7, 6, 5])
+    la, lb = a.logits([a.current_token()]), b.logits([b.current_token()])
+    assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    assert a.decode_device(6).tolist() == b.decode_device(6).tolist()
+
+
+def test_8b_shape_tensor_prefill(dev, small8b):
+    """Tensor-core prefill at the 8B shape (K up to 12288) within 1e-2."""
+    from gpu_util import abs_err_scaled
+    a = Model.create(dev, small8b, _cfg8(prefill="tensor"))
+    b = Model.create(dev, small8b, _cfg8())
+    prompt = synth.uniform_ids(8, "p8", 300, 4096).tolist()
+    assert abs_err_scaled(a.logits(prompt), b.logits(prompt)) <= 1e-2
