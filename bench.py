@@ -243,6 +243,13 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the config 3 (512-token prefill) measurement")
+    ap.add_argument("--parallel", default="pipeline", choices=["pipeline", "tensor"],
+                    help="N > 1 (or --parallel tensor at N = 1): layer-range pipeline stages "
+                         "(config 2 / 4a) or tensor-sharded layers and head (config 4b)")
+    ap.add_argument("--shape", default="0.6b", choices=["0.6b", "8b"],
+                    help="Qwen3-0.6B shape (configs 1-3) or Qwen3-8B shape (config 4)")
+    ap.add_argument("--prompt", type=int, default=None,
+                    help="prompt tokens before the timed decode (default 64; 4096 for 8b)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -261,15 +268,23 @@ def main():
     from flock_b200.model import Model
     from flock_b200 import ops
 
-    shape = synth.QWEN3_06B
+    shape = synth.QWEN3_8B if args.shape == "8b" else synth.QWEN3_06B
+    dev = get_device(local)
+    pk = peaks()
+    if args.parallel == "tensor":
+        run_tensor(args, rank, world, local, dev, shape, pk)
+        return
+    if args.shape == "8b" and world == 1:
+        raise SystemExit("--shape 8b runs as config 4: give --parallel tensor, or --gpus N > 1")
     t_gen = time.perf_counter()
-    m = synth.model(SEED, shape)
+    m = synth.model(SEED, shape, lazy=args.shape == "8b")
     log(f"[rank {rank}] synthetic model generated in {time.perf_counter() - t_gen:.1f}s")
     max_keys = PROMPT + args.warmup + args.steps + 8
     cfg = QWEN3_06B.with_(max_keys=max(max_keys, 512), attention=args.attention)
+    if args.shape == "8b":
+        cfg = cfg.with_(hidden=shape.hidden, n_heads=shape.n_heads, n_kv_heads=shape.n_kv_heads,
+                        ffn=shape.ffn)
     prompt = synth.uniform_ids(SEED, "prompt", PROMPT, shape.vocab)
-    dev = get_device(local)
-    pk = peaks()
 
     if world > 1:
         run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk)
@@ -400,6 +415,118 @@ def prefill_ttft(dev, m, shape, pk, n_prompt: int = 512) -> dict:
             "timing": "CUDA events, best of 3 prefills"}
 
 
+def _max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0])
+
+
+def run_tensor(args, rank, world, local, dev, shape, pk):
+    """Config 4b (and the 0.6B shape likewise): every layer and the head
+    sharded over the N GPUs (flock_model_create_tp) -- QKV / gate / up by
+    output rows, o_proj / down by input columns with an NCCL all-gather and a
+    rank-order sum per projection, the head by vocab rows with an 8-byte
+    (value, index) all-gather per token.  Decode steps replay one captured
+    graph per rank, NCCL inside."""
+    from datetime import timedelta
+    import torch.distributed as dist
+    from flock_b200 import synth
+    from flock_b200.comm import Comm
+    from flock_b200.layer import LayerConfig
+    from flock_b200.model import Model
+
+    n_prompt = args.prompt if args.prompt is not None else (4096 if args.shape == "8b" else PROMPT)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=timedelta(seconds=600))
+    uid = Comm.unique_id() if rank == 0 else None
+    if world > 1:
+        obj = [uid]
+        dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+    comm = Comm(dev, world, rank, uid, 120000)
+    cfg = LayerConfig(hidden=shape.hidden, n_heads=shape.n_heads, n_kv_heads=shape.n_kv_heads,
+                      head_dim=shape.head_dim, ffn=shape.ffn,
+                      max_keys=n_prompt + args.warmup + args.steps + 8, max_prefill=512,
+                      attention=args.attention, prefill="tensor")
+    t0 = time.perf_counter()
+    m = synth.model(SEED, shape, lazy=True)
+    M = Model.create_tp(dev, m, cfg, comm, rank, world)
+    t_load = time.perf_counter() - t0
+    log(f"[rank {rank}] tensor-parallel rank built in {t_load:.1f}s")
+    prompt = synth.uniform_ids(SEED, "prompt", n_prompt, shape.vocab)
+    if world > 1:
+        dist.barrier()
+    dev.timer_start()
+    first = M.step(prompt)                 # prefill on the tensor cores (untimed for value)
+    ttft = _max_over_ranks(dev.timer_stop(), world)
+    M.decode_device(args.warmup)
+    M.rewind(n_prompt)
+    M.set_token(first)
+    dev.sync()
+    if world > 1:
+        dist.barrier()
+    clk = Clocks(gpu_index(local))
+    clk.start()
+    dev.timer_start()
+    ids_dev = M.decode_device(args.steps)
+    ms = _max_over_ranks(dev.timer_stop(), world)
+    clocks = clk.stop()
+    # e2e: the public API's host loop, the id read back on every rank each token
+    M.rewind(n_prompt)
+    M.set_token(first)
+    if world > 1:
+        dist.barrier()
+    dev.timer_start()
+    prev, ids_api = first, []
+    for _ in range(args.steps):
+        prev = M.step([prev])
+        ids_api.append(prev)
+    ms_e2e = _max_over_ranks(dev.timer_stop(), world)
+    if rank == 0:
+        tok_s = args.steps / (ms / 1000.0)
+        avg_keys = n_prompt + (args.steps - 1) / 2.0 + 1
+        tok_bytes = bytes_per_token(shape, avg_keys)
+        per_gpu = tok_bytes / world * tok_s / 1e9
+        out = {
+            "metric": METRIC.replace("0.6B", "8B") if args.shape == "8b" else METRIC,
+            "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"config 4b: Qwen3-{'8B' if args.shape == '8b' else '0.6B'}"
+                                   f"-shape Q8_0, {shape.n_layers} layers, tensor-sharded over "
+                                   f"{world} GPU(s): QKV/gate/up by rows, o_proj/down by "
+                                   "columns with an NCCL all-gather + rank-order sum, head by "
+                                   "vocab rows with a (value, index) all-gather",
+                       "seed": SEED, "prompt": n_prompt, "attention": args.attention,
+                       "parallelism": f"tp{world}",
+                       "collectives_per_token": 2 * shape.n_layers + 1,
+                       "l2": "inputs larger than L2: weights streamed per token",
+                       "timing": "CUDA events around K device-fed decode steps, max over ranks"},
+            "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": per_gpu / pk["hbm_gbs"], "traffic": None,
+                         "kernel": "whole token per GPU: its 1/N of every weight and KV byte",
+                         "bytes_per_launch": tok_bytes / world, "peak_src": pk["src"]},
+            "clocks": clocks,
+            "e2e": {"value": args.steps / (ms_e2e / 1000.0), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                    "ids_match_device_loop": ids_api == ids_dev.tolist()},
+            "prefill": {"ttft_ms": ttft, "prompt": n_prompt, "path": "tcgen05 f16, tensor-sharded"},
+            "gpu_launches": (1 + shape.n_layers * ((5 if args.attention == "fast" else 6) + 2) + 4)
+            * args.steps,
+            "load_s": t_load,
+        }
+        print(json.dumps(out), flush=True)
+    M.free()  # the captured graph holds NCCL calls: release it before the communicator
+    comm.free()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     import ctypes
     import torch.distributed as dist
@@ -425,7 +552,11 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     if rank == 0:
         embd = GpuTensor.from_packed(dev, m.embd["packed"], m.embd["rows"], m.embd["cols"])
         onorm = GpuTensor.from_f32(dev, m.output_norm)
-        M = Model.from_tensors(dev, cfg, shape.vocab, b - a, layer_ts, embd, onorm)
+        head = None
+        if m.output is not None:
+            head = GpuTensor.from_packed(dev, m.output["packed"], m.output["rows"],
+                                         m.output["cols"])
+        M = Model.from_tensors(dev, cfg, shape.vocab, b - a, layer_ts, embd, onorm, head)
     else:
         M = Model.from_tensors(dev, cfg, shape.vocab, b - a, layer_ts, None, None)
     nxt = ctypes.c_int32()
@@ -479,11 +610,13 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
         tok_bytes = bytes_per_token(shape, avg_keys)
         token_gbs = tok_bytes * tok_s / 1e9
         out = {
-            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world,
+            "metric": METRIC.replace("0.6B", "8B") if shape.n_layers == 36 else METRIC,
+            "value": tok_s, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": "config 2 pipelined: contiguous layer ranges "
+            "config": {"workload": f"config {'4a (8B shape)' if shape.n_layers == 36 else '2'} "
+                                   "pipelined: contiguous layer ranges "
                                    f"{stage_ranges(shape.n_layers, world)}, hidden state over "
                                    "NCCL send/recv", "seed": SEED, "prompt": PROMPT,
                        "attention": args.attention, "parallelism": f"pp{world}",

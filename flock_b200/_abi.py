@@ -25,7 +25,7 @@ FLOCK_E_UNSUPPORTED = -8
 FLOCK_Q8_0, FLOCK_Q4_0, FLOCK_F32 = 8, 4, 32
 FLOCK_ROPE_NEOX, FLOCK_ROPE_NORM = 0, 1
 FLOCK_ATTN_EXACT, FLOCK_ATTN_FAST = 0, 1
-FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT = 0, 1
+FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT, FLOCK_DECODE_EAGER = 0, 1, 2
 FLOCK_PREFILL_EXACT, FLOCK_PREFILL_TENSOR = 0, 1
 
 
@@ -100,6 +100,7 @@ SIGNATURES = {
     "flock_layer_write_cache": [_vp, _fp, _fp, _i],
     "flock_range_forward": [_pp, _i, _fp, _i, _i, _i, _fp],
     "flock_model_create": [_vp, _cfgp, _i, _i, _pp, _vp, _vp, _vp, _i, _pp],
+    "flock_model_create_tp": [_vp, _cfgp, _i, _i, _pp, _vp, _vp, _vp, _vp, _pp],
     "flock_model_free": [_vp],
     "flock_model_step": [_vp, _i32p, _i, _i32p],
     "flock_model_logits": [_vp, _i32p, _i, _fp],

@@ -201,7 +201,7 @@ void dev_release(flock_dev* d) {
 
 // ------------------------------------------------------------- workspace
 
-int Workspace::alloc(const flock_layer_config& c, int sm_count) {
+int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
   P = c.max_prefill < 1 ? 1 : c.max_prefill;
   attn_splits = attn_max_splits(sm_count, c.n_kv_heads);
   H = c.hidden;
@@ -231,6 +231,10 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count) {
     FLOCK_CK(cudaMemset(tc_err.p, 0, 16));
     FLOCK_TRY(part.alloc((size_t)8 * P * H * f));
     FLOCK_TRY(kv_img.alloc(kv_image_bytes(c.max_keys, nKV)));
+  }
+  if (tp_ranks > 1) {
+    FLOCK_TRY(tp_part.alloc((size_t)P * H * f));
+    FLOCK_TRY(tp_all.alloc((size_t)tp_ranks * P * H * f));
   }
   return FLOCK_OK;
 }
@@ -388,6 +392,28 @@ static __global__ void k_swiglu_rows(const float* gu, float* act, int n, int F) 
   act[i] = fmul(fdiv(g, fadd(1.0f, exp_f64r(-g))), u);
 }
 
+// Tensor parallel: h[i] += (p_0[i] + p_1[i] + ... + p_{N-1}[i]), the ranks'
+// partials summed serially in rank order (shard_ref.ts / shard_reduce.wgsl:47
+// order), then added to the residual as the unsharded epilogue adds o.
+static __global__ void k_tp_reduce_residual(float* h, const float* parts, int n_ranks,
+                                            int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float acc = parts[i];
+  for (int r = 1; r < n_ranks; r++) acc = fadd(acc, parts[(int64_t)r * n + i]);
+  h[i] = fadd(h[i], acc);
+}
+
+static int tp_sum_into_h(flock_layer* L, int n) {
+  Workspace* ws = L->ws;
+  const int64_t count = (int64_t)n * L->cfg.hidden;
+  FLOCK_TRY(comm_allgather_dev(L->tp, ws->tp_part.p, ws->tp_all.p, (size_t)count * 4));
+  k_tp_reduce_residual<<<(unsigned)((count + 255) / 256), 256, 0, L->dev->stream>>>(
+      ws->h.as<float>(), ws->tp_all.as<float>(), L->tp_n, count);
+  FLOCK_CK(cudaGetLastError());
+  return FLOCK_OK;
+}
+
 // One prefill step of n > 1 tokens with the four weight matmuls on the
 // tcgen05 tensor cores (FLOCK_PREFILL_TENSOR); norms, RoPE, attention and the
 // residual adds keep their f32 arithmetic.
@@ -422,7 +448,7 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
   {  // o_proj + residual on h
     FLOCK_TRY(act_image_enqueue(st, ws->attn.as<float>(), qw, nullptr, 0.0f, n, qw, img));
     TcArgs a = {};
-    a.seg[0] = tc_seg_of(L->w[W_O], ws->h.as<float>(), H);
+    a.seg[0] = tc_seg_of(L->w[W_O], L->tp ? ws->tp_part.as<float>() : ws->h.as<float>(), H);
     a.nseg = 1;
     a.K = qw;
     a.M = n;
@@ -431,7 +457,9 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.res_stride = H;
     a.err = err;
     a.part = ws->part.as<float>();
-    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_RESIDUAL, a, d->sm_count, ws->part.bytes / 4));
+    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, L->tp ? EPI_STORE : EPI_RESIDUAL, a, d->sm_count,
+                              ws->part.bytes / 4));
+    if (L->tp) FLOCK_TRY(tp_sum_into_h(L, n));
   }
   {  // ffn_norm + gate | up, SwiGLU
     FLOCK_TRY(act_image_enqueue(st, ws->h.as<float>(), H, L->w[W_FFN_NORM]->data.as<float>(),
@@ -453,7 +481,7 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
   {  // down + residual on h
     FLOCK_TRY(act_image_enqueue(st, ws->act.as<float>(), F, nullptr, 0.0f, n, F, img));
     TcArgs a = {};
-    a.seg[0] = tc_seg_of(L->w[W_DOWN], ws->h.as<float>(), H);
+    a.seg[0] = tc_seg_of(L->w[W_DOWN], L->tp ? ws->tp_part.as<float>() : ws->h.as<float>(), H);
     a.nseg = 1;
     a.K = F;
     a.M = n;
@@ -462,7 +490,9 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.res_stride = H;
     a.err = err;
     a.part = ws->part.as<float>();
-    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_RESIDUAL, a, d->sm_count, ws->part.bytes / 4));
+    FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, L->tp ? EPI_STORE : EPI_RESIDUAL, a, d->sm_count,
+                              ws->part.bytes / 4));
+    if (L->tp) FLOCK_TRY(tp_sum_into_h(L, n));
   }
   return FLOCK_OK;
 }
@@ -541,10 +571,11 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
   } else {
     FLOCK_TRY(enqueue_qk_attn(L, n, pdl, false));
   }
-  // 4. o_proj + residual, in place on h
+  // 4. o_proj + residual, in place on h (tensor parallel: a partial, summed
+  // across ranks, then added)
   {
     GemvArgs a = {};
-    a.seg[0] = seg_of(L->w[W_O], ws->h.as<float>(), c.hidden);
+    a.seg[0] = seg_of(L->w[W_O], L->tp ? ws->tp_part.as<float>() : ws->h.as<float>(), c.hidden);
     a.nseg = 1;
     a.K = qw;
     a.n_tokens = n;
@@ -553,7 +584,8 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.res = ws->h.as<float>();
     a.res_stride = c.hidden;
     pf_add(a.pf, L->w[W_DOWN]);
-    FLOCK_TRY(launch_gemv(d, QT_Q8, EPI_RESIDUAL, a, pdl));
+    FLOCK_TRY(launch_gemv(d, QT_Q8, L->tp ? EPI_STORE : EPI_RESIDUAL, a, pdl));
+    if (L->tp) FLOCK_TRY(tp_sum_into_h(L, n));
   }
   // 5. ffn_norm + gate/up + SwiGLU
   {
@@ -570,10 +602,11 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.pf = pf_next;
     FLOCK_TRY(launch_gemv(d, QT_Q8, EPI_SWIGLU, a, pdl));
   }
-  // 6. down + residual, in place on h
+  // 6. down + residual, in place on h (tensor parallel as o_proj)
   {
     GemvArgs a = {};
-    a.seg[0] = seg_of(L->w[W_DOWN], ws->h.as<float>(), c.hidden);
+    a.seg[0] = seg_of(L->w[W_DOWN], L->tp ? ws->tp_part.as<float>() : ws->h.as<float>(),
+                      c.hidden);
     a.nseg = 1;
     a.K = c.ffn;
     a.n_tokens = n;
@@ -581,7 +614,8 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.x_stride = c.ffn;
     a.res = ws->h.as<float>();
     a.res_stride = c.hidden;
-    FLOCK_TRY(launch_gemv(d, QT_Q8, EPI_RESIDUAL, a, pdl));
+    FLOCK_TRY(launch_gemv(d, QT_Q8, L->tp ? EPI_STORE : EPI_RESIDUAL, a, pdl));
+    if (L->tp) FLOCK_TRY(tp_sum_into_h(L, n));
   }
   return FLOCK_OK;
 }

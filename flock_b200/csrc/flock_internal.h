@@ -92,7 +92,9 @@ struct Workspace {
   DBuf img, gu, tc_err, part;   // tensor-core prefill: activation image, gate|up rows, error word,
                                 // split-K partials
   DBuf kv_img;                  // tensor-core prefill: f16 K / V^T tiles of the cache
-  int alloc(const flock_layer_config& c, int sm_count);
+  DBuf tp_part, tp_all;         // tensor parallel: this rank's partial [P][H], all ranks
+  // tp_ranks > 1: also the tensor-parallel partial / all-gather buffers
+  int alloc(const flock_layer_config& c, int sm_count, int tp_ranks = 1);
 };
 
 enum { W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_ATTN_NORM, W_Q_NORM, W_K_NORM, W_FFN_NORM,
@@ -124,6 +126,10 @@ struct flock_layer {
   flock::DBuf kcache, vcache, ctl_own, inv_freq;
   int* ctl = nullptr;          // {pos, n_last} on the device (own or the model's)
   int n_keys = 0;              // host mirror
+  // tensor parallel: this layer is one rank's slice; o_proj and down give
+  // partial sums that are all-gathered over `tp` and added in rank order
+  flock_comm* tp = nullptr;
+  int tp_n = 1;
   flock::Workspace* ws = nullptr;
   flock::Workspace ws_own;     // standalone layers own their workspace
   bool owns_ws = false;
@@ -139,7 +145,11 @@ int layer_init(flock_layer* L, flock_dev* dev, const flock_layer_config& cfg, Wo
 int comm_send(flock_comm* c, const void* p, size_t n_f32, int peer);
 int comm_recv(flock_comm* c, void* p, size_t n_f32, int peer);
 int comm_wait(flock_comm* c);
+// NCCL all-gather of `bytes` per rank between device buffers on the
+// communicator's stream (out is [n_ranks][bytes], rank order).
+int comm_allgather_dev(flock_comm* c, const void* in, void* out, size_t bytes);
 int comm_rank(const flock_comm* c, int* rank, int* n_ranks);
+flock_dev* comm_device(const flock_comm* c);
 int layer_build(flock_dev* dev, const flock_layer_config* cfg, int n_tensors,
                 const char* const* names, flock_tensor* const* tensors, Workspace* ws, int* ctl,
                 flock_layer** out);

@@ -38,6 +38,12 @@ struct flock_model {
   MkArgs mk{};
   size_t mk_smem = 0;
   int mk_grid = 0;
+  // tensor parallel: this rank holds vocab rows [tp_start[r], tp_start[r+1])
+  // of the head; layers exchange partials over `tp`
+  flock_comm* tp = nullptr;
+  int tp_rank = 0, tp_n = 1, tp_chunk = 0;
+  std::vector<int64_t> tp_start;
+  DBuf tp_best, tp_bests, tp_logits;
 };
 
 namespace {
@@ -92,13 +98,34 @@ int enqueue_layers(flock_model* m, int n) {
   return FLOCK_OK;
 }
 
-// output_norm + lm-head + argmax on row `row` of ws.h.
+// Tensor parallel: the ranks' (value, global index) maxima in rank order ->
+// the token, by reduceShardArgmax's rule (shard_ref.ts:437; greater value,
+// or equal value and lower index), into ids[0].
+static __global__ void k_tp_argmax(const uint32_t* bests, int n_ranks, int32_t* ids) {
+  if (threadIdx.x != 0) return;
+  float bv = __uint_as_float(bests[0]);
+  uint32_t bi = bests[1];
+  for (int r = 1; r < n_ranks; r++) {
+    const float v = __uint_as_float(bests[2 * r]);
+    const uint32_t ix = bests[2 * r + 1];
+    if (am_better(v, ix, bv, bi)) {
+      bv = v;
+      bi = ix;
+    }
+  }
+  ids[0] = (int32_t)bi;
+}
+
+// output_norm + lm-head + argmax on row `row` of ws.h.  Tensor parallel: the
+// head is this rank's vocab rows; its (value, index) maximum is all-gathered
+// and reduced, so every rank ends with the same id.
 int enqueue_head(flock_model* m, int row) {
   GemvArgs a = {};
   GemvSeg s;
   s.qs = m->head->qs.as<uint8_t>();
   s.sc = m->head->sc.as<uint16_t>();
-  s.out = m->logits.as<float>();
+  s.out = m->tp ? m->tp_logits.as<float>() + (size_t)m->tp_rank * m->tp_chunk
+                : m->logits.as<float>();
   s.rows = (int)m->head->rows;
   s.sc_stride = m->head->sc_stride;
   s.out_stride = (int)m->head->rows;
@@ -115,7 +142,24 @@ int enqueue_head(flock_model* m, int row) {
   a.am_count = m->am_count.as<uint32_t>();
   a.am_best_val = m->am_best_val.as<float>();
   a.am_best_idx = m->ids.as<int32_t>();
-  return launch_gemv(m->dev, QT_Q8, EPI_ARGMAX, a, true);
+  if (!m->tp) return launch_gemv(m->dev, QT_Q8, EPI_ARGMAX, a, true);
+  a.am_row_offset = (int)m->tp_start[m->tp_rank];
+  a.am_best_val = m->tp_best.as<float>();
+  a.am_best_idx = m->tp_best.as<int32_t>() + 1;
+  FLOCK_TRY(launch_gemv(m->dev, QT_Q8, EPI_ARGMAX, a, true));
+  FLOCK_TRY(comm_allgather_dev(m->tp, m->tp_best.p, m->tp_bests.p, 8));
+  k_tp_argmax<<<1, 32, 0, m->dev->stream>>>(m->tp_bests.as<uint32_t>(), m->tp_n,
+                                            m->ids.as<int32_t>());
+  FLOCK_CK(cudaGetLastError());
+  return FLOCK_OK;
+}
+
+// Wait for the model's stream: bounded by the communicator's deadline (which
+// aborts it) when the step holds collectives.
+int sync_model(flock_model* m) {
+  if (m->tp) return comm_wait(m->tp);
+  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  return FLOCK_OK;
 }
 
 // Copy ids[0] (the chosen token) into hist[pos_last] on the device.
@@ -183,7 +227,7 @@ int mk_prepare(flock_model* m) {
   const flock_layer_config& c = m->cfg;
   m->mk_ok = false;
   if (c.attention != FLOCK_ATTN_FAST || !m->embd || !m->head || m->held < 1 || c.head_dim != 128 ||
-      c.n_heads / c.n_kv_heads > 4 || c.hidden > 4096)
+      c.n_heads / c.n_kv_heads > 4 || c.hidden > 4096 || m->tp)
     return FLOCK_OK;
   int dev = m->dev->ordinal, coop = 0, smem_optin = 0;
   FLOCK_CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
@@ -340,6 +384,12 @@ int capture_decode(flock_model* m) {
 // kernel) or the captured kernel graph.
 int launch_decode(flock_model* m) {
   if (m->decode_mode == FLOCK_DECODE_PERSISTENT && m->mk_ok) return enqueue_mk(m);
+  if (m->decode_mode == FLOCK_DECODE_EAGER) {
+    FLOCK_TRY(enqueue_embed(m, 1));
+    FLOCK_TRY(enqueue_layers(m, 1));
+    FLOCK_TRY(enqueue_head(m, 0));
+    return enqueue_record(m);
+  }
   FLOCK_TRY(capture_decode(m));
   FLOCK_CK(cudaGraphLaunch(m->decode_graph, m->dev->stream));
   return FLOCK_OK;
@@ -353,14 +403,11 @@ int need_head(flock_model* m) {
   return FLOCK_OK;
 }
 
-}  // namespace
-
-extern "C" {
-
-int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_layers,
-                       flock_tensor* const* lt, const flock_tensor* embd,
-                       const flock_tensor* output_norm, const flock_tensor* output, int cut,
-                       flock_model** out) {
+// Model.create body; tp != nullptr builds one rank of the tensor-parallel
+// model (cfg is the rank's slice, `output` its vocab rows of the head).
+int model_build(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_layers,
+                flock_tensor* const* lt, const flock_tensor* embd, const flock_tensor* output_norm,
+                const flock_tensor* output, int cut, flock_comm* tp, flock_model** out) {
   if (!dev || !cfg || !out || n_layers < 0 || (n_layers > 0 && !lt)) return FLOCK_E_ARG;
   if (cut < 0) cut = n_layers;
   if (cut > n_layers) {
@@ -389,7 +436,21 @@ int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab,
     flock_model_free(m);
     return r;
   };
-  if ((rc = m->ws.alloc(*cfg, dev->sm_count))) return fail(rc);
+  int64_t head_rows = vocab;
+  if (tp) {
+    m->tp = tp;
+    if ((rc = comm_rank(tp, &m->tp_rank, &m->tp_n))) return fail(rc);
+    // the head's vocab rows per rank: shard_ref.ts:97 shardRanges(vocab, n, 1)
+    const int64_t base = vocab / m->tp_n, extra = vocab % m->tp_n;
+    m->tp_start.assign(m->tp_n + 1, 0);
+    for (int r = 0; r < m->tp_n; r++) m->tp_start[r + 1] = m->tp_start[r] + base + (r < extra);
+    m->tp_chunk = (int)(base + (extra > 0));
+    head_rows = m->tp_start[m->tp_rank + 1] - m->tp_start[m->tp_rank];
+    if ((rc = m->tp_best.alloc(16)) || (rc = m->tp_bests.alloc((size_t)m->tp_n * 8)) ||
+        (rc = m->tp_logits.alloc((size_t)m->tp_n * m->tp_chunk * 4)))
+      return fail(rc);
+  }
+  if ((rc = m->ws.alloc(*cfg, dev->sm_count, m->tp_n))) return fail(rc);
   if ((rc = m->ctl.alloc(16))) return fail(rc);
   if (cudaMemset(m->ctl.p, 0, 16) != cudaSuccess) return fail(FLOCK_E_CUDA);
   if ((rc = m->ids.alloc((size_t)m->ws.P * 4 + 16))) return fail(rc);
@@ -400,9 +461,10 @@ int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab,
       (rc = m->am_count.alloc(16)) || (rc = m->am_best_val.alloc(16)))
     return fail(rc);
   if (cudaMemset(m->am_count.p, 0, 16) != cudaSuccess) return fail(FLOCK_E_CUDA);
-  if (m->head && (m->head->cols != cfg->hidden || m->head->rows != vocab)) {
-    set_error("lm-head is %lldx%lld, want %dx%d", (long long)m->head->rows,
-              (long long)m->head->cols, vocab, cfg->hidden);
+  if (m->head && (m->head->cols != cfg->hidden || m->head->rows != head_rows)) {
+    set_error("lm-head%s is %lldx%lld, want %lldx%d", tp ? " slice" : "",
+              (long long)m->head->rows, (long long)m->head->cols, (long long)head_rows,
+              cfg->hidden);
     return fail(FLOCK_E_ARG);
   }
   for (int i = 0; i < cut; i++) {
@@ -416,6 +478,8 @@ int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab,
     // all held layers share the model's workspace and position block
     if ((rc = layer_build(dev, cfg, W_COUNT, names, ts, &m->ws, m->ctl.as<int>(), &L)))
       return fail(rc);
+    L->tp = tp;
+    L->tp_n = m->tp_n;
     m->layers.push_back(L);
   }
   m->held = cut;
@@ -424,8 +488,44 @@ int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab,
   return FLOCK_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_layers,
+                       flock_tensor* const* lt, const flock_tensor* embd,
+                       const flock_tensor* output_norm, const flock_tensor* output, int cut,
+                       flock_model** out) {
+  return model_build(dev, cfg, vocab, n_layers, lt, embd, output_norm, output, cut, nullptr, out);
+}
+
+int flock_model_create_tp(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_layers,
+                          flock_tensor* const* lt, const flock_tensor* embd,
+                          const flock_tensor* output_norm, const flock_tensor* output_slice,
+                          flock_comm* comm, flock_model** out) {
+  if (!comm || !dev || !cfg) return FLOCK_E_ARG;
+  int rank = 0, n = 1;
+  FLOCK_TRY(comm_rank(comm, &rank, &n));
+  if (comm_device(comm) != dev) {
+    set_error("the communicator belongs to another device");
+    return FLOCK_E_ARG;
+  }
+  if (!embd || !output_norm || !output_slice) {
+    set_error("a tensor-parallel rank holds the embedding, output_norm and its head slice");
+    return FLOCK_E_MISSING;
+  }
+  if (vocab < n) {
+    set_error("vocab %d cannot be cut into %d head slices", vocab, n);
+    return FLOCK_E_ARG;
+  }
+  return model_build(dev, cfg, vocab, n_layers, lt, embd, output_norm, output_slice, -1, comm,
+                     out);
+}
+
 int flock_model_set_decode_mode(flock_model* m, int mode) {
-  if (!m || (mode != FLOCK_DECODE_KERNELS && mode != FLOCK_DECODE_PERSISTENT)) return FLOCK_E_ARG;
+  if (!m || (mode != FLOCK_DECODE_KERNELS && mode != FLOCK_DECODE_PERSISTENT &&
+             mode != FLOCK_DECODE_EAGER))
+    return FLOCK_E_ARG;
   if (mode != m->decode_mode && m->decode_graph) {
     cudaStreamSynchronize(m->dev->stream);
     cudaGraphExecDestroy(m->decode_graph);
@@ -457,15 +557,15 @@ int flock_model_trace_read(flock_model* m, uint64_t* out, int64_t cap, int* n_ct
   const int64_t n = (int64_t)m->mk_grid * *stride;
   if (!m->mk_trace.p) return FLOCK_E_STATE;
   if (!out || cap < n) return FLOCK_E_LIMIT;
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   FLOCK_CK(cudaMemcpy(out, m->mk_trace.p, (size_t)n * 8, cudaMemcpyDeviceToHost));
   return FLOCK_OK;
 }
 
 int flock_model_get_decode_mode(const flock_model* m, int* mode) {
   if (!m || !mode) return FLOCK_E_ARG;
-  *mode = (m->decode_mode == FLOCK_DECODE_PERSISTENT && m->mk_ok) ? FLOCK_DECODE_PERSISTENT
-                                                                  : FLOCK_DECODE_KERNELS;
+  *mode = (m->decode_mode == FLOCK_DECODE_PERSISTENT && !m->mk_ok) ? FLOCK_DECODE_KERNELS
+                                                                   : m->decode_mode;
   return FLOCK_OK;
 }
 
@@ -487,7 +587,7 @@ int flock_model_rewind(flock_model* m, int n_keys) {
   if (!m || n_keys < 0 || n_keys > m->cfg.max_keys) return FLOCK_E_ARG;
   int ctl[4] = {n_keys, 0, 0, 0};
   FLOCK_CK(cudaMemcpyAsync(m->ctl.p, ctl, sizeof ctl, cudaMemcpyHostToDevice, m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   m->pos = n_keys;
   for (auto* L : m->layers) L->n_keys = n_keys;
   return FLOCK_OK;
@@ -520,7 +620,7 @@ int flock_model_step(flock_model* m, const int32_t* ids, int n, int32_t* next_id
   }
   for (auto* L : m->layers) L->n_keys = m->pos;
   FLOCK_CK(cudaMemcpyAsync(next_id, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   return check_device_errors(m);
 }
 
@@ -537,7 +637,7 @@ int flock_model_decode_device(flock_model* m, int n_steps, int32_t* out_ids) {
   if (n_steps)
     FLOCK_CK(cudaMemcpyAsync(out_ids, m->hist.as<int32_t>() + start, (size_t)n_steps * 4,
                              cudaMemcpyDeviceToHost, m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   return check_device_errors(m);
 }
 
@@ -561,8 +661,20 @@ int flock_model_generate(flock_model* m, const int32_t* prompt, int n_prompt, in
 int flock_model_logits(flock_model* m, const int32_t* ids, int n, float* logits) {
   int32_t tok;
   FLOCK_TRY(flock_model_step(m, ids, n, &tok));
-  FLOCK_CK(cudaMemcpy(logits, m->logits.p, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost));
-  return FLOCK_OK;
+  if (!m->tp) {
+    FLOCK_CK(cudaMemcpy(logits, m->logits.p, (size_t)m->vocab * 4, cudaMemcpyDeviceToHost));
+    return FLOCK_OK;
+  }
+  // tensor parallel: gather the ranks' slices (in place, one padded slot per
+  // rank) and lay them out contiguously; a collective like the step itself
+  float* slots = m->tp_logits.as<float>();
+  FLOCK_TRY(comm_allgather_dev(m->tp, slots + (size_t)m->tp_rank * m->tp_chunk, slots,
+                               (size_t)m->tp_chunk * 4));
+  for (int r = 0; r < m->tp_n; r++)
+    FLOCK_CK(cudaMemcpyAsync(logits + m->tp_start[r], slots + (size_t)r * m->tp_chunk,
+                             (size_t)(m->tp_start[r + 1] - m->tp_start[r]) * 4,
+                             cudaMemcpyDeviceToHost, m->dev->stream));
+  return sync_model(m);
 }
 
 int flock_model_hidden_state(flock_model* m, const int32_t* ids, int n, float* out) {
@@ -574,7 +686,7 @@ int flock_model_hidden_state(flock_model* m, const int32_t* ids, int n, float* o
   for (auto* L : m->layers) L->n_keys = m->pos;
   FLOCK_CK(cudaMemcpyAsync(out, m->ws.h.as<float>() + (size_t)(last - 1) * m->cfg.hidden,
                            (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost, m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   return check_device_errors(m);
 }
 
@@ -592,7 +704,7 @@ int flock_model_normed_state(flock_model* m, const int32_t* ids, int n, float* o
   FLOCK_TRY(enqueue_head(m, last - 1));
   FLOCK_CK(cudaMemcpyAsync(out, m->normed.p, (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost,
                            m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   return check_device_errors(m);
 }
 
@@ -604,7 +716,7 @@ int flock_model_embed(flock_model* m, const int32_t* ids, int n, float* out) {
   FLOCK_TRY(enqueue_embed(m, n));
   FLOCK_CK(cudaMemcpyAsync(out, m->ws.h.p, (size_t)n * m->cfg.hidden * 4, cudaMemcpyDeviceToHost,
                            m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   return check_device_errors(m);
 }
 
@@ -625,7 +737,7 @@ int flock_model_encode_partial(flock_model* m, const int32_t* ids, int n, int of
   for (auto* L : m->layers) L->n_keys = m->pos;
   FLOCK_CK(cudaMemcpyAsync(out, m->ws.h.p, (size_t)n * m->cfg.hidden * 4, cudaMemcpyDeviceToHost,
                            m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   return check_device_errors(m);
 }
 
@@ -637,20 +749,20 @@ int flock_model_project_hidden(flock_model* m, const float* flat, int seq, int32
                            (size_t)m->cfg.hidden * 4, cudaMemcpyHostToDevice, m->dev->stream));
   FLOCK_TRY(enqueue_head(m, 0));
   FLOCK_CK(cudaMemcpyAsync(next_id, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   return check_device_errors(m);
 }
 
 int flock_model_set_token(flock_model* m, int32_t id) {
   if (!m || id < 0 || id >= m->vocab) return FLOCK_E_ARG;
   FLOCK_CK(cudaMemcpyAsync(m->ids.p, &id, 4, cudaMemcpyHostToDevice, m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   return check_device_errors(m);
 }
 
 int flock_model_current_token(flock_model* m, int32_t* out) {
   FLOCK_CK(cudaMemcpyAsync(out, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   return check_device_errors(m);
 }
 
@@ -720,7 +832,7 @@ int flock_model_history(flock_model* m, int start, int n, int32_t* out) {
   if (n)
     FLOCK_CK(cudaMemcpyAsync(out, m->hist.as<int32_t>() + start, (size_t)n * 4,
                              cudaMemcpyDeviceToHost, m->dev->stream));
-  FLOCK_CK(cudaStreamSynchronize(m->dev->stream));
+  FLOCK_TRY(sync_model(m));
   return check_device_errors(m);
 }
 

@@ -581,11 +581,17 @@ int flock_comm_allgather_bytes(flock_comm* c, const void* in, void* out, int64_t
 // The hidden-state hops of the layer pipeline live with the model (they need
 // its workspace); see flock_model.cu.
 namespace flock {
+int comm_allgather_dev(flock_comm* c, const void* in, void* out, size_t bytes) {
+  if (!c->comm) return FLOCK_E_NCCL;
+  NCCL_ISSUE(c, g_nccl.AllGather(in, out, bytes, ncclUint8, c->comm, c->dev->stream));
+  return FLOCK_OK;
+}
 int comm_send(flock_comm* c, const void* p, size_t n_f32, int peer) {
   if (!c->comm) return FLOCK_E_NCCL;
   NCCL_ISSUE(c, g_nccl.Send(p, n_f32, ncclFloat32, peer, c->comm, c->dev->stream));
   return FLOCK_OK;
 }
+flock_dev* comm_device(const flock_comm* c) { return c->dev; }
 int comm_rank(const flock_comm* c, int* rank, int* n_ranks) {
   *rank = c->rank;
   *n_ranks = c->n_ranks;

@@ -63,6 +63,31 @@ class Model:
                   output.handle if output else None, cut, ctypes.byref(h))
         return Model(dev, h, cfg, vocab, n_layers, [layer_ts, embd, out_norm, output])
 
+    @staticmethod
+    def create_tp(dev: Device, m, cfg: LayerConfig, comm, rank: int, world: int) -> "Model":
+        """One rank of the tensor-parallel model over an NCCL communicator
+        (flock_model_create_tp): this rank's slices of every layer, the
+        whole embedding and output_norm, its vocab rows of the head."""
+        from .tensor_parallel import local_config, slice_head, slice_layer
+        lcfg = local_config(cfg, world)
+        layer_ts = [upload_layer(dev, slice_layer(w, cfg, rank, world)) for w in m.layers]
+        embd = GpuTensor.from_packed(dev, m.embd["packed"], m.embd["rows"], m.embd["cols"])
+        onorm = GpuTensor.from_f32(dev, m.output_norm)
+        head = getattr(m, "output", None) or m.embd
+        hs = slice_head(head, rank, world)
+        out = GpuTensor.from_packed(dev, hs["packed"], hs["rows"], hs["cols"])
+        flat = [t[name].handle for t in layer_ts for name in TENSOR_NAMES]
+        arr = (ctypes.c_void_p * max(1, len(flat)))(*flat)
+        h = ctypes.c_void_p()
+        cfg_c = lcfg[rank].to_c()
+        _abi.call("flock_model_create_tp", dev.handle, ctypes.byref(cfg_c), m.vocab,
+                  len(layer_ts), arr, embd.handle, onorm.handle, out.handle,
+                  comm.handle if hasattr(comm, "handle") else comm, ctypes.byref(h))
+        # the model holds the communicator: it is freed after the model (and
+        # its captured graph with NCCL calls)
+        return Model(dev, h, lcfg[rank], m.vocab, len(m.layers),
+                     [layer_ts, embd, onorm, out, comm])
+
     def free(self) -> None:
         if self.handle:
             _abi.lib().flock_model_free(self.handle)
@@ -180,17 +205,22 @@ class Model:
         _abi.call("flock_model_held", self.handle, ctypes.byref(n))
         return n.value
 
+    _MODES = {"kernels": _abi.FLOCK_DECODE_KERNELS, "persistent": _abi.FLOCK_DECODE_PERSISTENT,
+              "eager": _abi.FLOCK_DECODE_EAGER}
+
     @property
     def decode_mode(self) -> str:
-        """"persistent" (one cooperative kernel per token) or "kernels"."""
+        """"kernels" (the captured kernel graph), "persistent" (one cooperative
+        kernel per token) or "eager" (the kernels launched from the host)."""
         n = ctypes.c_int()
         _abi.call("flock_model_get_decode_mode", self.handle, ctypes.byref(n))
-        return "persistent" if n.value == _abi.FLOCK_DECODE_PERSISTENT else "kernels"
+        return {v: k for k, v in self._MODES.items()}[n.value]
 
     @decode_mode.setter
     def decode_mode(self, mode: str) -> None:
-        _abi.call("flock_model_set_decode_mode", self.handle,
-                  _abi.FLOCK_DECODE_PERSISTENT if mode == "persistent" else _abi.FLOCK_DECODE_KERNELS)
+        if mode not in self._MODES:
+            raise ValueError(f"decode mode {mode!r} is not one of {sorted(self._MODES)}")
+        _abi.call("flock_model_set_decode_mode", self.handle, self._MODES[mode])
 
     def trace(self, enable: bool = True) -> None:
         """Record per-CTA phase timestamps in the persistent decode kernel."""

@@ -152,12 +152,33 @@ class SynthModel:
         return len(self.layers)
 
 
+class LazyLayers:
+    """The layers of a synthetic model, each generated when it is indexed (the
+    same bytes as layer_weights), so a loader that uploads or slices one layer
+    at a time never holds the whole model in host memory."""
+
+    def __init__(self, seed: int, s: Shape, n: int):
+        self.seed, self.s, self.n = seed, s, n
+
+    def __len__(self) -> int:
+        return self.n
+
+    def __getitem__(self, i: int) -> dict:
+        if not -self.n <= i < self.n:
+            raise IndexError(i)
+        return layer_weights(self.seed, i % self.n, self.s)
+
+    def __iter__(self):
+        return (self[i] for i in range(self.n))
+
+
 def model(seed: int, s: Shape = QWEN3_06B, n_layers: int | None = None,
-          vocab: int | None = None) -> SynthModel:
-    """A whole synthetic model.  ``n_layers``/``vocab`` shrink it for tests."""
+          vocab: int | None = None, lazy: bool = False) -> SynthModel:
+    """A whole synthetic model.  ``n_layers``/``vocab`` shrink it for tests;
+    ``lazy`` generates each layer when it is read."""
     nl = s.n_layers if n_layers is None else n_layers
     V = s.vocab if vocab is None else vocab
-    layers = [layer_weights(seed, i, s) for i in range(nl)]
+    layers = LazyLayers(seed, s, nl) if lazy else [layer_weights(seed, i, s) for i in range(nl)]
     embd = {"rows": V, "cols": s.hidden, "packed": q8_tensor(seed, "token_embd.weight", V, s.hidden)}
     out = None
     if not s.tied:

@@ -237,6 +237,25 @@ FLOCK_API int flock_model_create(flock_dev* dev, const flock_layer_config* cfg, 
                        flock_tensor* const* layer_tensors, const flock_tensor* embd,
                        const flock_tensor* output_norm, const flock_tensor* output, int cut,
                        flock_model** out);
+/* One rank of a tensor-parallel model over `comm` (one rank per GPU, NCCL;
+ * no counterpart in the reference, which validates shard.ts on one device).
+ * The layers are this rank's slices in the shard.ts directions: `cfg` is the
+ * rank-local shape (n_heads, n_kv_heads and ffn divided among the ranks),
+ * attn_q/k/v, ffn_gate/up carry the rank's output rows ("row" shards),
+ * attn_output and ffn_down its input columns ("col" shards), whose partial
+ * products are all-gathered and summed in rank order (shardReduceRef) before
+ * the residual add.  `embd` and output_norm are whole on every rank;
+ * `output_slice` is the rank's rows shardRanges(vocab, n_ranks, 1)[rank] of
+ * the lm-head (of embd when tied); each rank's (value, index) maximum is
+ * all-gathered and reduced by reduceShardArgmax.  Every step, logits and
+ * head call is a collective: all ranks make it with the same arguments.
+ * Both prefill paths shard the same way; the persistent decode kernel is not
+ * used (single-token steps replay the kernel graph, NCCL included). */
+FLOCK_API int flock_model_create_tp(flock_dev* dev, const flock_layer_config* cfg, int vocab,
+                                   int n_layers, flock_tensor* const* layer_tensors,
+                                   const flock_tensor* embd, const flock_tensor* output_norm,
+                                   const flock_tensor* output_slice, flock_comm* comm,
+                                   flock_model** out);
 FLOCK_API int flock_model_free(flock_model* m);
 /* kernels/model.ts:387 step(ids): prefill/decode ids, return the greedy id. */
 FLOCK_API int flock_model_step(flock_model* m, const int32_t* ids, int n, int32_t* next_id);
@@ -267,6 +286,7 @@ FLOCK_API int flock_model_pos(const flock_model* m, int* out);
 FLOCK_API int flock_model_held(const flock_model* m, int* out);
 #define FLOCK_DECODE_KERNELS 0    /* one kernel per op, CUDA graph + PDL */
 #define FLOCK_DECODE_PERSISTENT 1 /* one cooperative persistent kernel per token */
+#define FLOCK_DECODE_EAGER 2      /* one kernel per op, launched from the host each step */
 /* Choose the decode engine for single-token steps (default: the kernel
  * graph).  The persistent kernel needs fast attention, Q8_0 weights, head_dim
  * 128 and a resident embedding/head; otherwise the kernel graph runs and

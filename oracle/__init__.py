@@ -94,6 +94,8 @@ def lib():
                                         _f32p]),
             "fo_layer_prefill": (_int, [_f32p, _int, ctypes.c_void_p, ctypes.c_void_p,
                                         ctypes.c_void_p, _f32p]),
+            "fo_layer_prefill_tp": (_int, [_f32p, _int, ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_void_p, _int, _f32p]),
             "fo_head": (_i64, [_f32p, _f32p, _u8p, _i64, _int, _dbl, _f32p, _f32p]),
             "fo_shard_ranges": (_int, [_i64, _int, _i64, _i64p, _i64p]),
             "fo_slice_rows": (None, [_u8p, _u8p, _i64, _i64, _i64, _i64, _u8p, _u8p]),
@@ -311,9 +313,12 @@ F32_NAMES = {"attn_norm.weight": "attn_norm", "attn_q_norm.weight": "q_norm",
 
 
 class RefLayer:
-    """layer_ref.ts layerForwardRef / layerPrefillRef with a RefCache (:24)."""
+    """layer_ref.ts layerForwardRef / layerPrefillRef with a RefCache (:24).
+    tp > 1: o_proj and down become tp-shard input-split matvecs
+    (shard_ref.ts:353), the arithmetic of a tensor-parallel layer."""
 
-    def __init__(self, weights: dict, cfg: dict, max_keys: int = 4096):
+    def __init__(self, weights: dict, cfg: dict, max_keys: int = 4096, tp: int = 1):
+        self.tp = int(tp)
         self._keep = {}
         w = _W()
         for name, field in Q8_NAMES.items():
@@ -360,8 +365,11 @@ class RefLayer:
     def forward(self, hidden: np.ndarray, n_tokens: int = 1) -> np.ndarray:
         hidden = _f32(hidden)
         out = np.empty(n_tokens * self.cfg["hidden"], np.float32)
-        rc = lib().fo_layer_prefill(_p(hidden, _f32p), n_tokens, ctypes.byref(self._w),
-                                    ctypes.byref(self._c), self._cache, _p(out, _f32p))
+        rc = lib().fo_layer_prefill_tp(_p(hidden, _f32p), n_tokens, ctypes.byref(self._w),
+                                       ctypes.byref(self._c), self._cache, self.tp,
+                                       _p(out, _f32p))
+        if rc == -2:
+            raise ValueError(f"cannot cut this layer into {self.tp} shards")
         if rc != 0:
             raise ValueError("reference cache overflow")
         return out

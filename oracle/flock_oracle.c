@@ -518,15 +518,41 @@ int fo_layer_forward(const float* hidden, const fo_layer_w* w, const fo_layer_cf
   return fo_layer_prefill(hidden, 1, w, cfg, cache, out);
 }
 
+/* o_proj / down of one layer: the plain matmul, or (tp > 1) the input-split
+ * composition of shard_ref.ts:353 shardedColMatvecRef over tp shards (column
+ * ranges of shardRanges(cols, tp, 32), partials summed serially in shard
+ * order), token by token. */
+static int layer_proj(const uint8_t* packed, const float* x, int64_t rows, int64_t cols, int n,
+                      int tp, float* out) {
+  if (tp <= 1) {
+    fo_matmul_q8_batched(packed, x, rows, cols, n, COOP_LANES, out);
+    return 0;
+  }
+  for (int t = 0; t < n; t++) {
+    int rc = fo_sharded_col_matvec(packed, x + (int64_t)t * cols, rows, cols, tp, COOP_LANES,
+                                   out + (int64_t)t * rows);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
 /* layer_ref.ts:103 layerPrefillRef (n_tokens == 1 is exactly layerForwardRef,
  * whose only difference is attnRef in place of attnPrefillRef). */
 int fo_layer_prefill(const float* hidden, int n, const fo_layer_w* w, const fo_layer_cfg* cfg,
                      fo_cache* cache, float* out) {
+  return fo_layer_prefill_tp(hidden, n, w, cfg, cache, 1, out);
+}
+
+/* layerPrefillRef with o_proj and down replaced by their tp-shard input-split
+ * forms (the tensor-parallel layer; tp == 1 is layerPrefillRef itself). */
+int fo_layer_prefill_tp(const float* hidden, int n, const fo_layer_w* w, const fo_layer_cfg* cfg,
+                        fo_cache* cache, int tp, float* out) {
   const int H = cfg->hidden, nH = cfg->n_heads, nKV = cfg->n_kv_heads, hd = cfg->head_dim,
             F = cfg->ffn;
   const int qw = nH * hd, kvw = nKV * hd;
   if (cache->kvw != kvw) return -1;
   if (cache->n + n > cache->cap) return -1;
+  if (tp < 1 || (tp > 1 && ((qw / 32) < tp || (F / 32) < tp))) return -2;
   float inv_freq[512];
   fo_rope_inv_freq(hd, cfg->rope_base, inv_freq);
   int pos0 = cache->n;
@@ -557,13 +583,13 @@ int fo_layer_prefill(const float* hidden, int n, const fo_layer_w* w, const fo_l
     fo_attn(q, cache->k, cache->v, nH, nKV, hd, cache->n, attn);
   else
     fo_attn_prefill(q, cache->k, cache->v, nH, nKV, hd, n, pos0, 64, 128, attn);
-  fo_matmul_q8_batched(w->o, attn, H, qw, n, COOP_LANES, proj);
+  layer_proj(w->o, attn, H, qw, n, tp, proj);
   fo_add(hidden, proj, N * H, h2);
   fo_rmsnorm(h2, w->ffn_norm, H, n, cfg->eps, 128, nh);
   fo_matmul_q8_batched(w->gate, nh, F, H, n, COOP_LANES, gate);
   fo_matmul_q8_batched(w->up, nh, F, H, n, COOP_LANES, up);
   fo_swiglu(gate, up, N * F, act);
-  fo_matmul_q8_batched(w->down, act, H, F, n, COOP_LANES, proj);
+  layer_proj(w->down, act, H, F, n, tp, proj);
   fo_add(h2, proj, N * H, out);
 
   free(nh); free(q); free(k); free(v); free(qn); free(kn); free(attn);

@@ -131,6 +131,10 @@ int fo_layer_forward(const float* hidden, const fo_layer_w* w, const fo_layer_cf
                      fo_cache* cache, float* out);
 int fo_layer_prefill(const float* hidden, int n_tokens, const fo_layer_w* w,
                      const fo_layer_cfg* cfg, fo_cache* cache, float* out);
+/* The tensor-parallel layer: o_proj and down as tp-shard input-split matvecs
+ * (shardedColMatvecRef); tp == 1 is fo_layer_prefill. */
+int fo_layer_prefill_tp(const float* hidden, int n_tokens, const fo_layer_w* w,
+                        const fo_layer_cfg* cfg, fo_cache* cache, int tp, float* out);
 
 /* model.ts encodeHead :307: rmsnorm(output_norm) -> tied head coop(64) -> argmax. */
 int64_t fo_head(const float* last_row, const float* out_norm, const uint8_t* embd_packed,
