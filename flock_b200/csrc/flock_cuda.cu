@@ -232,7 +232,7 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
     FLOCK_TRY(part.alloc((size_t)8 * P * H * f));
     FLOCK_TRY(kv_img.alloc(kv_image_bytes(c.max_keys, nKV)));
   }
-  if (tp_ranks > 1) {
+  if (tp_ranks >= 1) {
     FLOCK_TRY(tp_part.alloc((size_t)P * H * f));
     FLOCK_TRY(tp_all.alloc((size_t)tp_ranks * P * H * f));
   }
@@ -406,6 +406,10 @@ static __global__ void k_tp_reduce_residual(float* h, const float* parts, int n_
 
 static int tp_sum_into_h(flock_layer* L, int n) {
   Workspace* ws = L->ws;
+  if (!ws->tp_part.p || !ws->tp_all.p || n > ws->P) {
+    set_error("tensor-parallel layer without its exchange buffers");
+    return FLOCK_E_STATE;
+  }
   const int64_t count = (int64_t)n * L->cfg.hidden;
   FLOCK_TRY(comm_allgather_dev(L->tp, ws->tp_part.p, ws->tp_all.p, (size_t)count * 4));
   k_tp_reduce_residual<<<(unsigned)((count + 255) / 256), 256, 0, L->dev->stream>>>(

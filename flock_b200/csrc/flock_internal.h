@@ -93,8 +93,9 @@ struct Workspace {
                                 // split-K partials
   DBuf kv_img;                  // tensor-core prefill: f16 K / V^T tiles of the cache
   DBuf tp_part, tp_all;         // tensor parallel: this rank's partial [P][H], all ranks
-  // tp_ranks > 1: also the tensor-parallel partial / all-gather buffers
-  int alloc(const flock_layer_config& c, int sm_count, int tp_ranks = 1);
+  // tp_ranks >= 1 (a tensor-parallel model, one rank included): also the
+  // partial / all-gather buffers; 0 = no tensor parallelism
+  int alloc(const flock_layer_config& c, int sm_count, int tp_ranks = 0);
 };
 
 enum { W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN, W_ATTN_NORM, W_Q_NORM, W_K_NORM, W_FFN_NORM,

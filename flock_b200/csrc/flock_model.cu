@@ -450,7 +450,7 @@ int model_build(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_
         (rc = m->tp_logits.alloc((size_t)m->tp_n * m->tp_chunk * 4)))
       return fail(rc);
   }
-  if ((rc = m->ws.alloc(*cfg, dev->sm_count, m->tp_n))) return fail(rc);
+  if ((rc = m->ws.alloc(*cfg, dev->sm_count, tp ? m->tp_n : 0))) return fail(rc);
   if ((rc = m->ctl.alloc(16))) return fail(rc);
   if (cudaMemset(m->ctl.p, 0, 16) != cudaSuccess) return fail(FLOCK_E_CUDA);
   if ((rc = m->ids.alloc((size_t)m->ws.P * 4 + 16))) return fail(rc);
