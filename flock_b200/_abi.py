@@ -101,6 +101,17 @@ SIGNATURES = {
     "flock_range_forward": [_pp, _i, _fp, _i, _i, _i, _fp],
     "flock_model_create": [_vp, _cfgp, _i, _i, _pp, _vp, _vp, _vp, _i, _pp],
     "flock_model_create_tp": [_vp, _cfgp, _i, _i, _pp, _vp, _vp, _vp, _vp, _pp],
+    "flock_gguf_open": [ctypes.c_char_p, _pp],
+    "flock_gguf_free": [_vp],
+    "flock_gguf_info": [_vp, _i64p, _i64p, _ip, _ip],
+    "flock_gguf_tensor_info": [_vp, _i64, ctypes.c_char_p, _i, _ip, _i64p, _i64p, _i64p, _i64p],
+    "flock_gguf_find": [_vp, ctypes.c_char_p, _i64p],
+    "flock_gguf_meta_int": [_vp, ctypes.c_char_p, _i64p],
+    "flock_gguf_meta_f64": [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)],
+    "flock_gguf_meta_str": [_vp, ctypes.c_char_p, ctypes.c_char_p, _i],
+    "flock_gguf_layer_ranges": [_vp, _i, _i, _i64, _i64p, _i64p, _i, _ip],
+    "flock_gguf_load_tensor": [_vp, _vp, ctypes.c_char_p, _i64, _pp],
+    "flock_gguf_split_host": [_vp, ctypes.c_char_p, _i64, _u8p, _u8p],
     "flock_model_free": [_vp],
     "flock_model_step": [_vp, _i32p, _i, _i32p],
     "flock_model_logits": [_vp, _i32p, _i, _fp],

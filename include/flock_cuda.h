@@ -309,6 +309,47 @@ FLOCK_API int flock_model_set_token(flock_model* m, int32_t id);
 /* kernels/model.ts:541 currentToken(). */
 FLOCK_API int flock_model_current_token(flock_model* m, int32_t* out);
 
+/* ----------------------------------------------------------------- GGUF */
+
+/* A GGUF model file opened on the host (web/js/gguf-dir.mjs:187
+ * readDirectory / server/gguf.mjs:48 readModel): the directory is parsed at
+ * open (version 2 or 3; dataStart = header end rounded up to
+ * general.alignment, default 32); tensor bytes are read on demand. */
+typedef struct flock_gguf flock_gguf;
+FLOCK_API int flock_gguf_open(const char* path, flock_gguf** out);
+FLOCK_API int flock_gguf_free(flock_gguf* g);
+/* tensor count, dataStart, version, `<general.architecture>.block_count` (-1 if absent) */
+FLOCK_API int flock_gguf_info(const flock_gguf* g, int64_t* n_tensors, int64_t* data_start,
+                              int* version, int* n_layers);
+/* tensor i: name (NUL-terminated, cut to name_cap), ggml type (0 F32, 1 F16,
+ * 2 Q4_0, 8 Q8_0, ...), rows (product of shape[1:]), cols (shape[0]; GGUF
+ * shapes are [in, out]), offset from dataStart, bytes (gguf.mjs:37
+ * tensorBytes; -1 for a type without block geometry). */
+FLOCK_API int flock_gguf_tensor_info(const flock_gguf* g, int64_t i, char* name, int name_cap,
+                                     int* dtype, int64_t* rows, int64_t* cols, int64_t* offset,
+                                     int64_t* bytes);
+FLOCK_API int flock_gguf_find(const flock_gguf* g, const char* name, int64_t* index);
+/* metadata by key: integers and bools (arrays: their length), numbers, strings */
+FLOCK_API int flock_gguf_meta_int(const flock_gguf* g, const char* key, int64_t* out);
+FLOCK_API int flock_gguf_meta_f64(const flock_gguf* g, const char* key, double* out);
+FLOCK_API int flock_gguf_meta_str(const flock_gguf* g, const char* key, char* out, int cap);
+/* server/gguf.mjs:78 byteRanges: absolute byte ranges covering the blk.<first..last>.*
+ * tensors, merged where the gap is at most `gap` bytes; *n = the count
+ * (FLOCK_E_LIMIT when it exceeds cap). */
+FLOCK_API int flock_gguf_layer_ranges(const flock_gguf* g, int first, int last, int64_t gap,
+                                      int64_t* starts, int64_t* ends, int cap, int* n);
+/* web/js/gguf-stream.mjs:281 streamTensorToGPU: the tensor's bytes read
+ * `staging` bytes at a time (<= 0: 4 MiB), Q8_0 / Q4_0 blocks split into the
+ * qs and scale planes as they arrive (SplitStreamer, :132) and copied to the
+ * device from two pinned staging buffers in turn; F32 / F16 tensors (norm
+ * gains) become f32 data. */
+FLOCK_API int flock_gguf_load_tensor(flock_dev* dev, const flock_gguf* g, const char* name,
+                                     int64_t staging, flock_tensor** out);
+/* The same incremental split into host planes in block order (qs: 32 / 16
+ * bytes per block, scales: 2), reading `chunk` bytes at a time. */
+FLOCK_API int flock_gguf_split_host(const flock_gguf* g, const char* name, int64_t chunk,
+                                    uint8_t* qs, uint8_t* scales);
+
 /* --------------------------------------------------------------- shards */
 
 /* kernels/shard.ts:214 ShardedMatvec.create over a Q8_0 tensor given in the
