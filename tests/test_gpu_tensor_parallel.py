@@ -97,6 +97,13 @@ def test_one_rank_tensor_prefill_equals_single_gpu():
 
 
 def _rank(rank, world, q_uid, q_out):
+    try:
+        q_out.put((rank, _rank_body(rank, world, q_uid)))
+    except Exception as e:  # report instead of leaving the parent waiting
+        q_out.put((rank, f"rank {rank} failed: {e!r}"))
+
+
+def _rank_body(rank, world, q_uid):
     from flock_b200 import lib as flib
     from flock_b200 import synth
     from flock_b200.comm import Comm
@@ -110,10 +117,12 @@ def _rank(rank, world, q_uid, q_out):
             q_uid.put(uid)
     else:
         uid = q_uid.get(timeout=60)
+    # one communicator per rank (a unique id bootstraps exactly one), shared
+    # by the models built one after another
+    comm = Comm(dev, world, rank, uid, 30000)
     res = {}
     for attention in ("exact", "fast"):
-        M = Model.create_tp(dev, m, QWEN3_06B.with_(attention=attention),
-                            Comm(dev, world, rank, uid, 30000), rank, world)
+        M = Model.create_tp(dev, m, QWEN3_06B.with_(attention=attention), comm, rank, world)
         M.decode_mode = "eager"
         ids = [M.step(PROMPT)]
         for _ in range(N_DECODE - 1):
@@ -124,11 +133,11 @@ def _rank(rank, world, q_uid, q_out):
         graph = [M.step(PROMPT)] + M.decode_device(N_DECODE - 1).tolist()
         res[attention] = (ids, lg, graph)
         M.free()
-    M = Model.create_tp(dev, m, QWEN3_06B.with_(prefill="tensor"),
-                        Comm(dev, world, rank, uid, 30000), rank, world)
+    M = Model.create_tp(dev, m, QWEN3_06B.with_(prefill="tensor"), comm, rank, world)
     res["tensor_prefill"] = M.logits(LONG)
     M.free()
-    q_out.put((rank, res))
+    comm.free()
+    return res
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
@@ -144,6 +153,7 @@ def test_two_rank_tp_matches_oracle(oracle):
         for _ in range(2):
             r, v = q_out.get(timeout=600)
             res[r] = v
+            assert not isinstance(v, str), v
     finally:
         for p in procs:
             p.join(timeout=60)
