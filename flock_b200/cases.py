@@ -216,11 +216,6 @@ def trace_summary(tr, n_layers: int) -> str:
     lines.append(f"     head: compute {np.mean(t[:, h] - t[:, h - 1]):6.2f} us "
                  f"(slowest {np.max(t[:, h] - t[:, h - 1]):.2f}), argmax "
                  f"{np.max(t[:, h + 1] - t[:, h]):.2f} us")
-    w = tr[:, 4 + 10 * n_layers:].astype(np.float64) / 1000.0
-    lines.append("weight waits (warp 0, per token): " + ", ".join(
-        f"{n} {w[:, i].mean():.1f} us" for i, n in enumerate(("qkv", "o_proj", "gate/up", "down",
-                                                                "head"))) +
-        f"; producer waited for free stages {w[:, 5].mean():.1f} us")
     return "\n".join(lines)
 
 

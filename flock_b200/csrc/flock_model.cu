@@ -238,14 +238,8 @@ int mk_prepare(flock_model* m) {
   if (splits != m->ws.attn_splits) return FLOCK_OK;
   MkArgs& a = m->mk;
   a = MkArgs{};
-  a.n_stages = 4;
-  a.stage_bytes = 32 * 1024;
-  const size_t smem = mk_smem_bytes(a.stage_bytes, a.n_stages, c.hidden, c.n_heads * c.head_dim,
-                                    c.ffn) + 1024;  // + static shared
+  const size_t smem = mk_smem_bytes(c.hidden, c.n_heads * c.head_dim, c.ffn) + 1024;  // + static
   if (smem > (size_t)smem_optin) return FLOCK_OK;
-  // every unit of every phase must fit one stage
-  const int kmax = c.hidden > c.ffn ? c.hidden : c.ffn;
-  if (2 * (kmax + ((kmax / 32 + 7) / 8 * 8) * 2) > a.stage_bytes) return FLOCK_OK;
   if (m->embd->dtype != FLOCK_Q8_0 || m->head->dtype != FLOCK_Q8_0) return FLOCK_OK;
   for (int i = 0; i < m->held; i++)
     for (int t = 0; t < 7; t++)
@@ -309,12 +303,17 @@ int mk_prepare(flock_model* m) {
   a.ctl = m->ctl.as<int>();
   a.bar = m->mk_bar.as<unsigned>();
   a.err = m->mk_err.as<int>();
+  // the last layer streams the head's first rows into L2 (it exceeds L2)
+  a.head_prefetch = (int64_t)48 << 20;
   FLOCK_TRY(kernel_setup((const void*)k_decode_mk, (int)smem));
   int per_sm = 0;
   FLOCK_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mk, MK_THREADS, smem));
   if (per_sm < 1) return FLOCK_OK;
+  // every CTA must be resident (cooperative launch); two per SM when they fit,
+  // as the graph's GEMVs run, and never fewer than the attention items
   m->mk_smem = smem;
-  m->mk_grid = grid;
+  m->mk_grid = (per_sm >= 2 ? 2 : 1) * grid;
+  if (m->mk_grid < c.n_kv_heads * splits || m->mk_grid > 4096) return FLOCK_OK;
   m->mk_ok = true;
   return FLOCK_OK;
 }
@@ -335,8 +334,8 @@ int enqueue_mk(flock_model* m) {
   return FLOCK_OK;
 }
 
-// The device error words of the persistent kernel and the bf16 prefill
-// GEMMs; call after a synchronisation.
+// The device error words of the persistent kernel and the tensor-core
+// prefill GEMMs; call after a synchronisation.
 int check_device_errors(flock_model* m) {
   FLOCK_TRY(ws_check_errors(&m->ws));
   if (!m->mk_ok || m->decode_mode != FLOCK_DECODE_PERSISTENT) return FLOCK_OK;

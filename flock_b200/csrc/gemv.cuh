@@ -321,20 +321,17 @@ FLOCK_DEV void rows_of(const GemvArgs& a, int g, Rows<R>& rs) {
 // LA: steps in flight ahead of the one being folded (1, or 2 for long rows,
 // where each warp walks several column blocks per row and one step of
 // lookahead leaves HBM latency exposed).
-template <int QT, int R, int EPI, int MX, int LA = 1>
-__global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
-  extern __shared__ __align__(16) float smem[];
-  const bool norm = a.norm_gain != nullptr;
-  const int kpad = a.K / 32 * XPAD;
-  float* xs = smem;                          // [K/32][36] the (normalised) input
-  float* gs = smem + kpad;                   // [K] gain staging (norm only)
-  float* red = gs + (norm ? a.K : 0);        // [136] reduction scratch
-  float* cta_val = red + 136;                // [GEMV_WARPS]
-  uint32_t* cta_idx = (uint32_t*)(cta_val + GEMV_WARPS);
-
+//
+// gemv_run: the matvec of CTA `cta` of `n_ctas` (warps stride over row groups
+// across the CTAs) for token `tok`.  The first step's weight loads are issued,
+// then `pre()` runs -- it must leave x (padded layout) in xs and synchronise
+// the block -- then the rows are folded and the epilogue applied.  EPI_ARGMAX
+// leaves this thread's best (value, index) in best_v / best_i.
+template <int QT, int R, int EPI, int MX, int LA, class Pre>
+FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const float* xs,
+                        Pre&& pre, float& best_v, uint32_t& best_i) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int tok = blockIdx.y;
   const int nb = a.K / 32;
   const int M = (nb + 31) / 32;
 
@@ -345,12 +342,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     n_groups = 0;
     for (int s = 0; s < a.nseg; s++) n_groups += (a.seg[s].rows + R - 1) / R;
   }
-  const int nwarps = gridDim.x * GEMV_WARPS;
+  const int nwarps = n_ctas * GEMV_WARPS;
 
   // The warp walks steps (g, m): row group g = gwarp, gwarp + nwarps, ...,
   // column block m = 0..M-1.  Weights do not depend on any earlier kernel,
   // so the first step's loads are issued before griddepcontrol.wait.
-  int g = blockIdx.x * GEMV_WARPS + warp, m = 0;
+  int g = cta * GEMV_WARPS + warp, m = 0;
   bool have = g < n_groups;
   Rows<R> rs;
   BlockW<QT> cur[R];
@@ -383,25 +380,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
     }
   }
 
-  issue_prefetch(a.pf);
-  pdl_launch_dependents();
-  pdl_wait();
-
-  if (a.ctl && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
-    a.ctl[0] += a.ctl[1];
-    a.ctl[1] = a.ctl_n;
-  }
-
-  // ---- x into shared memory (optionally normalised) ----
-  if (norm) {
-    rmsnorm_to_smem(a.x + (size_t)tok * a.x_stride, a.norm_gain, a.K, a.eps, xs, gs, red);
-  } else {
-    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)tok * a.x_stride);
-#pragma unroll 4
-    for (int i = threadIdx.x; i < a.K / 4; i += GEMV_THREADS)
-      reinterpret_cast<float4*>(xs)[(i >> 3) * (XPAD / 4) + (i & 7)] = src[i];
-  }
-  __syncthreads();
+  pre();
 
   const float4* xs4 = reinterpret_cast<const float4*>(xs);
   float4 xr[MX][8];
@@ -416,8 +395,6 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
   float accA[R], accB[R];
 #pragma unroll
   for (int r = 0; r < R; r++) accA[r] = accB[r] = 0.0f;
-  float best_v = -FLT_MAX;
-  uint32_t best_i = 0xFFFFFFFFu;
 
   while (have) {
     // issue the loads of the step LA ahead before folding this one
@@ -517,71 +494,118 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv(const GemvArgs a) {
       have = have2;
     }
   }
+}
 
-  if (EPI == EPI_ARGMAX) {
-    // CTA reduction of the per-warp bests, then the last CTA to arrive
-    // reduces the per-CTA partials (kernels/argmax.wgsl pass1/pass2 fused).
+// x for token `tok` into xs (padded layout), RMSNorm-ed when a.norm_gain is
+// set; the caller synchronises the block afterwards.
+FLOCK_DEV void gemv_stage_x(const GemvArgs& a, int tok, float* xs, float* gs, float* red) {
+  if (a.norm_gain) {
+    rmsnorm_to_smem(a.x + (size_t)tok * a.x_stride, a.norm_gain, a.K, a.eps, xs, gs, red);
+  } else {
+    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)tok * a.x_stride);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < a.K / 4; i += GEMV_THREADS)
+      reinterpret_cast<float4*>(xs)[(i >> 3) * (XPAD / 4) + (i & 7)] = src[i];
+  }
+}
+
+// EPI_ARGMAX: CTA reduction of the per-warp bests, then the last CTA to
+// arrive reduces the per-CTA partials (kernels/argmax.wgsl pass1/pass2
+// fused) into *am_best_val / *am_best_idx and re-arms the counter.  Returns
+// true in every thread of that last CTA.
+FLOCK_DEV bool gemv_argmax_finish(const GemvArgs& a, float best_v, uint32_t best_i,
+                                  float* cta_val, uint32_t* cta_idx) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    cta_val[warp] = best_v;
+    cta_idx[warp] = best_i;
+  }
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) {
+    float bv = cta_val[0];
+    uint32_t bi = cta_idx[0];
+    for (int w = 1; w < GEMV_WARPS; w++)
+      if (am_better(cta_val[w], cta_idx[w], bv, bi)) {
+        bv = cta_val[w];
+        bi = cta_idx[w];
+      }
+    a.am_val[blockIdx.x] = bv;
+    a.am_idx[blockIdx.x] = bi;
+    __threadfence();
+    const uint32_t prev = atomicAdd(a.am_count, 1u);
+    last = (prev == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (last) {
+    __threadfence();
+    float bv = -FLT_MAX;
+    uint32_t bi = 0xFFFFFFFFu;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += GEMV_THREADS) {
+      const float v = ((volatile float*)a.am_val)[i];
+      const uint32_t ix = ((volatile uint32_t*)a.am_idx)[i];
+      if (am_better(v, ix, bv, bi)) {
+        bv = v;
+        bi = ix;
+      }
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+      const float ov = __shfl_down_sync(0xffffffffu, bv, s);
+      const uint32_t oi = __shfl_down_sync(0xffffffffu, bi, s);
+      if (am_better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
     if (lane == 0) {
-      cta_val[warp] = best_v;
-      cta_idx[warp] = best_i;
+      cta_val[warp] = bv;
+      cta_idx[warp] = bi;
     }
     __syncthreads();
-    __shared__ bool last;
     if (threadIdx.x == 0) {
-      float bv = cta_val[0];
-      uint32_t bi = cta_idx[0];
+      bv = cta_val[0];
+      bi = cta_idx[0];
       for (int w = 1; w < GEMV_WARPS; w++)
         if (am_better(cta_val[w], cta_idx[w], bv, bi)) {
           bv = cta_val[w];
           bi = cta_idx[w];
         }
-      a.am_val[blockIdx.x] = bv;
-      a.am_idx[blockIdx.x] = bi;
-      __threadfence();
-      const uint32_t prev = atomicAdd(a.am_count, 1u);
-      last = (prev == gridDim.x - 1);
-    }
-    __syncthreads();
-    if (last) {
-      __threadfence();
-      float bv = -FLT_MAX;
-      uint32_t bi = 0xFFFFFFFFu;
-      for (int i = threadIdx.x; i < (int)gridDim.x; i += GEMV_THREADS) {
-        const float v = ((volatile float*)a.am_val)[i];
-        const uint32_t ix = ((volatile uint32_t*)a.am_idx)[i];
-        if (am_better(v, ix, bv, bi)) {
-          bv = v;
-          bi = ix;
-        }
-      }
-#pragma unroll
-      for (int s = 16; s > 0; s >>= 1) {
-        const float ov = __shfl_down_sync(0xffffffffu, bv, s);
-        const uint32_t oi = __shfl_down_sync(0xffffffffu, bi, s);
-        if (am_better(ov, oi, bv, bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      if (lane == 0) {
-        cta_val[warp] = bv;
-        cta_idx[warp] = bi;
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        bv = cta_val[0];
-        bi = cta_idx[0];
-        for (int w = 1; w < GEMV_WARPS; w++)
-          if (am_better(cta_val[w], cta_idx[w], bv, bi)) {
-            bv = cta_val[w];
-            bi = cta_idx[w];
-          }
-        *a.am_best_val = bv;
-        *a.am_best_idx = (int32_t)bi;
-        *a.am_count = 0;  // re-arm for the next launch
-      }
+      *a.am_best_val = bv;
+      *a.am_best_idx = (int32_t)bi;
+      *a.am_count = 0;  // re-arm for the next launch
     }
   }
+  return last;
+}
+
+// MINB: resident CTAs per SM the register budget is sized for.
+template <int QT, int R, int EPI, int MX, int LA = 1, int MINB = 2>
+__global__ void __launch_bounds__(GEMV_THREADS, MINB) k_gemv(const GemvArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  const bool norm = a.norm_gain != nullptr;
+  const int kpad = a.K / 32 * XPAD;
+  float* xs = smem;                          // [K/32][36] the (normalised) input
+  float* gs = smem + kpad;                   // [K] gain staging (norm only)
+  float* red = gs + (norm ? a.K : 0);        // [136] reduction scratch
+  float* cta_val = red + 136;                // [GEMV_WARPS]
+  uint32_t* cta_idx = (uint32_t*)(cta_val + GEMV_WARPS);
+  float best_v = -FLT_MAX;
+  uint32_t best_i = 0xFFFFFFFFu;
+  // weights do not depend on any earlier kernel: their first loads go out
+  // before griddepcontrol.wait, overlapping the previous kernel's tail
+  gemv_run<QT, R, EPI, MX, LA>(a, blockIdx.y, blockIdx.x, gridDim.x, xs, [&] {
+    issue_prefetch(a.pf);
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.ctl && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+      a.ctl[0] += a.ctl[1];
+      a.ctl[1] = a.ctl_n;
+    }
+    gemv_stage_x(a, blockIdx.y, xs, gs, red);
+    __syncthreads();
+  }, best_v, best_i);
+  if (EPI == EPI_ARGMAX) gemv_argmax_finish(a, best_v, best_i, cta_val, cta_idx);
 }
 
 // Shared-memory bytes a k_gemv launch needs.

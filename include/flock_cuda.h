@@ -298,9 +298,8 @@ FLOCK_API int flock_model_get_decode_mode(const flock_model* m, int* mode);
  * global-timer nanosecond values per token -- stamps at start, embedded, then
  * for every layer and each of its 5 phases (QKV, attention, o_proj, gate/up,
  * down) "computed" and "released by the grid barrier", head computed and
- * done; then the time warp 0 waited for weights in the 5 GEMV phase kinds
- * and the time the weight producer waited for a free stage.  trace_read
- * copies the last token's [n_ctas][stride] entries. */
+ * done; then 6 words kept zero.  trace_read copies the last token's
+ * [n_ctas][stride] entries. */
 FLOCK_API int flock_model_trace(flock_model* m, int enable);
 FLOCK_API int flock_model_trace_read(flock_model* m, uint64_t* out, int64_t cap, int* n_ctas,
                                      int* stride);
