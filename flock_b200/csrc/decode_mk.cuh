@@ -131,6 +131,8 @@ FLOCK_DEV bool grid_barrier(const MkArgs& a, unsigned& epoch) {
 
 // L2 prefetch of one layer's weight planes (qs, scales) and the K/V rows of
 // keys 0..n_keys-1, spread over the grid in 32 KiB pieces (issue_prefetch).
+// Planes above 24 MiB (the 8B shape's gate / up / down) stream on demand, so
+// what is prefetched stays well inside the 126 MB L2.
 FLOCK_DEV void mk_prefetch_layer(const MkArgs& a, int l, int n_keys) {
   const MkLayer& L = a.layers[l];
   const int rows[7] = {a.nH * a.hd, a.nKV * a.hd, a.nKV * a.hd, a.H, a.F, a.F, a.H};
@@ -144,8 +146,11 @@ FLOCK_DEV void mk_prefetch_layer(const MkArgs& a, int l, int n_keys) {
       pf.n = 0;
     }
   };
-  for (int t = 0; t < 7; t++) add(L.qs[t], (uint64_t)rows[t] * cols[t]);
-  for (int t = 0; t < 7; t++) add(L.sc[t], (uint64_t)rows[t] * L.sc_stride[t] * 2);
+  constexpr uint64_t kMax = 24ull << 20;
+  for (int t = 0; t < 7; t++)
+    if ((uint64_t)rows[t] * cols[t] <= kMax) add(L.qs[t], (uint64_t)rows[t] * cols[t]);
+  for (int t = 0; t < 7; t++)
+    if ((uint64_t)rows[t] * cols[t] <= kMax) add(L.sc[t], (uint64_t)rows[t] * L.sc_stride[t] * 2);
   const uint64_t kv = (uint64_t)n_keys * a.nKV * a.hd * 4;
   add(L.kcache, kv);
   add(L.vcache, kv);
@@ -153,19 +158,24 @@ FLOCK_DEV void mk_prefetch_layer(const MkArgs& a, int l, int n_keys) {
 }
 
 // Runs a GEMV phase: the row-group walk of a k_gemv launch over this grid,
-// x staged (and normalised) by gemv_stage_x.  Not inlined: each phase gets
-// the registers of its own loop instead of sharing the kernel's allocation.
-template <int R, int EPI>
-__device__ __noinline__ void mk_gemv(const GemvArgs& g, float* xs, float* gs, float* red, float& best_v,
-                       uint32_t& best_i) {
-  auto pre = [&] {
+// x staged (and normalised) by gemv_stage_x.  One non-inlined function per
+// shape: each phase gets the registers of its own loop, as its k_gemv
+// launch would, instead of sharing the kernel's allocation.
+template <int R, int EPI, int LA>
+__device__ __noinline__ void mk_gemv_la(const GemvArgs& g, float* xs, float* gs, float* red,
+                                        float& best_v, uint32_t& best_i) {
+  gemv_run<QT_Q8, R, EPI, 1, LA>(g, 0, blockIdx.x, gridDim.x, xs, [&] {
     gemv_stage_x(g, 0, xs, gs, red);
     __syncthreads();
-  };
+  }, best_v, best_i);
+}
+template <int R, int EPI>
+FLOCK_DEV void mk_gemv(const GemvArgs& g, float* xs, float* gs, float* red, float& best_v,
+                       uint32_t& best_i) {
   if ((g.K / 32 + 31) / 32 >= 2)
-    gemv_run<QT_Q8, R, EPI, 1, 2>(g, 0, blockIdx.x, gridDim.x, xs, pre, best_v, best_i);
+    mk_gemv_la<R, EPI, 2>(g, xs, gs, red, best_v, best_i);
   else
-    gemv_run<QT_Q8, R, EPI, 1, 1>(g, 0, blockIdx.x, gridDim.x, xs, pre, best_v, best_i);
+    mk_gemv_la<R, EPI, 1>(g, xs, gs, red, best_v, best_i);
 }
 
 FLOCK_DEV GemvSeg mk_seg(const MkLayer& L, int t, float* out, int rows) {
@@ -197,7 +207,7 @@ struct MkShared {
   float* att;
 };
 
-static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs a) {
+static __global__ void __launch_bounds__(MK_THREADS, 2) k_decode_mk(const MkArgs a) {
   extern __shared__ __align__(128) float mk_smem[];
   const int kmax = max(a.H, max(a.nH * a.hd, a.F));
   MkShared sm;

@@ -171,8 +171,13 @@ static GemvSeg seg_of(const flock_tensor* t, float* out, int out_stride) {
   return s;
 }
 
+// L2 prefetch hints for the next kernel's weights.  A tensor larger than
+// kPrefetchMax is left to stream on demand: prefetching it would compete with
+// the running kernel's own HBM stream and could be evicted before its use
+// (the 8B shape's 50 MB gate / up / down planes next to a 126 MB L2).
+constexpr uint64_t kPrefetchMax = 24ull << 20;
 static void pf_add(PrefetchList& pf, const flock_tensor* t) {
-  if (!t) return;
+  if (!t || t->qs.bytes > kPrefetchMax) return;
   if (pf.n + 2 > 4) return;
   pf.ptr[pf.n] = t->qs.as<uint8_t>();
   pf.bytes[pf.n] = t->qs.bytes & ~(uint64_t)15;

@@ -131,7 +131,7 @@ def test_phase_trace(dev, small):
     tr = a.read_trace().astype(np.int64)
     a.trace(False)
     assert got.tolist() == b.decode_device(3).tolist()
-    assert tr.shape == (dev.sm_count, 10 + 10 * a.held)
+    assert tr.shape[1] == 10 + 10 * a.held and tr.shape[0] % dev.sm_count == 0  # 1-2 CTAs per SM
     tr = tr[:, :4 + 10 * a.held]                      # the stamps
     assert (tr > 0).all()
     assert (np.diff(tr, axis=1) >= 0).all()          # stamps in program order per CTA
