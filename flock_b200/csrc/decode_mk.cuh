@@ -81,6 +81,12 @@ struct MkArgs {
   unsigned* bar;   // grid barrier counter, zero at launch
   int* err;        // set non-zero on a timed-out wait
   int64_t head_prefetch;  // bytes of the head's planes prefetched during the last layer
+  // per-phase launch arguments built by the host, read from global memory by
+  // every thread (a private copy per thread would be local-memory traffic):
+  // gemv[4 * l + {0 QKV, 1 o_proj, 2 gate/up, 3 down}], gemv[4 * n_layers] the
+  // head; attn[l] the attention phase of layer l
+  const GemvArgs* gemv;
+  const AttnFastArgs* attn_args;
   // optional phase trace: per CTA, mk_trace_stride(n_layers) entries of
   // global-timer nanoseconds -- stamps (start, embedded, then per layer and
   // phase: computed, released; head computed, done), then 6 zero words
@@ -162,36 +168,30 @@ FLOCK_DEV void mk_prefetch_layer(const MkArgs& a, int l, int n_keys) {
 // shape: each phase gets the registers of its own loop, as its k_gemv
 // launch would, instead of sharing the kernel's allocation.
 template <int R, int EPI, int LA>
-__device__ __noinline__ void mk_gemv_la(const GemvArgs& g, float* xs, float* gs, float* red,
-                                        float& best_v, uint32_t& best_i) {
+__device__ __noinline__ void mk_gemv_la(const GemvArgs* __restrict__ gp, const float* from,
+                                        float* xs, float* gs, float* red, float& best_v,
+                                        uint32_t& best_i) {
+  const GemvArgs& g = *gp;
   gemv_run<QT_Q8, R, EPI, 1, LA>(g, 0, blockIdx.x, gridDim.x, xs, [&] {
-    gemv_stage_x(g, 0, xs, gs, red);
+    gemv_stage_x(g, 0, xs, gs, red, from);
     __syncthreads();
   }, best_v, best_i);
 }
+// `from`: the source row when it is not g->x (layer 0's embedded row in
+// shared memory).
 template <int R, int EPI>
-FLOCK_DEV void mk_gemv(const GemvArgs& g, float* xs, float* gs, float* red, float& best_v,
-                       uint32_t& best_i) {
-  if ((g.K / 32 + 31) / 32 >= 2)
-    mk_gemv_la<R, EPI, 2>(g, xs, gs, red, best_v, best_i);
+FLOCK_DEV void mk_gemv(const GemvArgs* gp, const float* from, float* xs, float* gs, float* red,
+                       float& best_v, uint32_t& best_i) {
+  if ((gp->K / 32 + 31) / 32 >= 2)
+    mk_gemv_la<R, EPI, 2>(gp, from, xs, gs, red, best_v, best_i);
   else
-    mk_gemv_la<R, EPI, 1>(g, xs, gs, red, best_v, best_i);
-}
-
-FLOCK_DEV GemvSeg mk_seg(const MkLayer& L, int t, float* out, int rows) {
-  GemvSeg s;
-  s.qs = L.qs[t];
-  s.sc = L.sc[t];
-  s.out = out;
-  s.rows = rows;
-  s.sc_stride = L.sc_stride[t];
-  s.out_stride = rows;
-  return s;
+    mk_gemv_la<R, EPI, 1>(gp, from, xs, gs, red, best_v, best_i);
 }
 
 // The attention phase: work item (kv head, split) = (CTA / splits, CTA % splits).
-__device__ __noinline__ void mk_attention(const AttnFastArgs& aa, int pos, float* att,
-                                          bool* last) {
+__device__ __noinline__ void mk_attention(const AttnFastArgs* __restrict__ ap, int pos,
+                                          float* att, bool* last) {
+  const AttnFastArgs& aa = *ap;
   attn_fast_item(aa, blockIdx.x / aa.splits, blockIdx.x % aa.splits, pos, att, last, BlockSync{});
 }
 
@@ -207,7 +207,7 @@ struct MkShared {
   float* att;
 };
 
-static __global__ void __launch_bounds__(MK_THREADS, 2) k_decode_mk(const MkArgs a) {
+static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs a) {
   extern __shared__ __align__(128) float mk_smem[];
   const int kmax = max(a.H, max(a.nH * a.hd, a.F));
   MkShared sm;
@@ -252,29 +252,11 @@ static __global__ void __launch_bounds__(MK_THREADS, 2) k_decode_mk(const MkArgs
     for (int i = threadIdx.x; i < a.H; i += MK_THREADS) a.h[i] = sm.raw[i];
   stamp(1);
 
-  AttnFastArgs aa = {};
-  aa.q = a.q;
-  aa.k = a.k;
-  aa.v = a.v;
-  aa.inv_freq = a.inv_freq;
-  aa.out = a.attn;
-  aa.part = a.attn_part;
-  aa.count = a.attn_count;
-  aa.n_heads = a.nH;
-  aa.n_kv_heads = a.nKV;
-  aa.head_dim = a.hd;
-  aa.splits = a.splits;
-  aa.eps = a.eps;
-  aa.neox = a.neox;
-  aa.combine = 1;  // the last split of a group combines, as in the kernel graph
-
-  const int qw = a.nH * a.hd, kvw = a.nKV * a.hd;
   float best_v = -FLT_MAX;
   uint32_t best_i = 0xFFFFFFFFu;
   unsigned epoch = 0;
   bool ok = true;
   for (int l = 0; l < a.n_layers && ok; l++) {
-    const MkLayer& L = a.layers[l];
     if (l + 1 < a.n_layers) {
       mk_prefetch_layer(a, l + 1, pos + 1);
     } else if (a.head_prefetch > 0 && threadIdx.x == 0) {
@@ -284,103 +266,39 @@ static __global__ void __launch_bounds__(MK_THREADS, 2) k_decode_mk(const MkArgs
       pf.n = 1;
       issue_prefetch(pf);
     }
-    {  // QKV (attn_norm fused): k_gemv<Q8, 2, STORE> over q | k | v
-      GemvArgs g = {};
-      g.seg[0] = mk_seg(L, 0, a.q, qw);
-      g.seg[1] = mk_seg(L, 1, a.k, kvw);
-      g.seg[2] = mk_seg(L, 2, a.v, kvw);
-      g.nseg = 3;
-      g.K = a.H;
-      g.n_tokens = 1;
-      g.x = l == 0 ? sm.raw : a.h;
-      g.x_stride = a.H;
-      g.norm_gain = L.attn_norm;
-      g.eps = a.eps;
-      mk_gemv<2, EPI_STORE>(g, sm.xs, sm.gs, sm.red, best_v, best_i);
-    }
+    const GemvArgs* G = a.gemv + 4 * l;
+    // QKV (attn_norm fused): k_gemv<Q8, 2, STORE> over q | k | v
+    mk_gemv<2, EPI_STORE>(G + 0, l == 0 ? sm.raw : nullptr, sm.xs, sm.gs, sm.red, best_v, best_i);
     stamp(2 + l * 10 + 0);
     if (!(ok = grid_barrier(a, epoch))) break;
     stamp(2 + l * 10 + 1);
-    // attention (q/k norm + RoPE + KV append fused)
-    aa.q_norm = L.q_norm;
-    aa.k_norm = L.k_norm;
-    aa.kcache = L.kcache;
-    aa.vcache = L.vcache;
-    if ((int)blockIdx.x < a.nKV * a.splits) mk_attention(aa, pos, sm.att, &att_last);
+    // attention (q/k norm + RoPE + KV append fused; the last split combines)
+    if ((int)blockIdx.x < a.nKV * a.splits) mk_attention(a.attn_args + l, pos, sm.att, &att_last);
     stamp(2 + l * 10 + 2);
     if (!(ok = grid_barrier(a, epoch))) break;
     stamp(2 + l * 10 + 3);
-    {  // o_proj + residual, in place on h
-      GemvArgs g = {};
-      g.seg[0] = mk_seg(L, 3, a.h, a.H);
-      g.nseg = 1;
-      g.K = qw;
-      g.n_tokens = 1;
-      g.x = a.attn;
-      g.x_stride = qw;
-      g.res = a.h;
-      g.res_stride = a.H;
-      mk_gemv<1, EPI_RESIDUAL>(g, sm.xs, sm.gs, sm.red, best_v, best_i);
-    }
+    // o_proj + residual, in place on h
+    mk_gemv<1, EPI_RESIDUAL>(G + 1, nullptr, sm.xs, sm.gs, sm.red, best_v, best_i);
     stamp(2 + l * 10 + 4);
     if (!(ok = grid_barrier(a, epoch))) break;
     stamp(2 + l * 10 + 5);
-    {  // gate/up + SwiGLU (ffn_norm fused)
-      GemvArgs g = {};
-      g.seg[0] = mk_seg(L, 4, a.act, a.F);
-      g.seg[1] = mk_seg(L, 5, a.act, a.F);
-      g.nseg = 2;
-      g.K = a.H;
-      g.n_tokens = 1;
-      g.x = a.h;
-      g.x_stride = a.H;
-      g.norm_gain = L.ffn_norm;
-      g.eps = a.eps;
-      mk_gemv<2, EPI_SWIGLU>(g, sm.xs, sm.gs, sm.red, best_v, best_i);
-    }
+    // gate/up + SwiGLU (ffn_norm fused)
+    mk_gemv<2, EPI_SWIGLU>(G + 2, nullptr, sm.xs, sm.gs, sm.red, best_v, best_i);
     stamp(2 + l * 10 + 6);
     if (!(ok = grid_barrier(a, epoch))) break;
     stamp(2 + l * 10 + 7);
-    {  // down + residual, in place on h
-      GemvArgs g = {};
-      g.seg[0] = mk_seg(L, 6, a.h, a.H);
-      g.nseg = 1;
-      g.K = a.F;
-      g.n_tokens = 1;
-      g.x = a.act;
-      g.x_stride = a.F;
-      g.res = a.h;
-      g.res_stride = a.H;
-      mk_gemv<1, EPI_RESIDUAL>(g, sm.xs, sm.gs, sm.red, best_v, best_i);
-    }
+    // down + residual, in place on h
+    mk_gemv<1, EPI_RESIDUAL>(G + 3, nullptr, sm.xs, sm.gs, sm.red, best_v, best_i);
     stamp(2 + l * 10 + 8);
     ok = grid_barrier(a, epoch);
     stamp(2 + l * 10 + 9);
   }
   if (!ok) return;
   // output_norm + head + argmax: k_gemv<Q8, 2, ARGMAX> over the vocab
-  GemvArgs g = {};
-  g.seg[0].qs = a.head_qs;
-  g.seg[0].sc = a.head_sc;
-  g.seg[0].out = a.logits;
-  g.seg[0].rows = a.vocab;
-  g.seg[0].sc_stride = a.head_sc_stride;
-  g.seg[0].out_stride = a.vocab;
-  g.nseg = 1;
-  g.K = a.H;
-  g.n_tokens = 1;
-  g.x = a.h;
-  g.x_stride = a.H;
-  g.norm_gain = a.out_norm;
-  g.eps = a.eps;
-  g.am_val = a.am_val;
-  g.am_idx = a.am_idx;
-  g.am_count = a.am_count;
-  g.am_best_val = a.am_best_val;
-  g.am_best_idx = a.ids;
-  mk_gemv<2, EPI_ARGMAX>(g, sm.xs, sm.gs, sm.red, best_v, best_i);
+  const GemvArgs* hg = a.gemv + 4 * a.n_layers;
+  mk_gemv<2, EPI_ARGMAX>(hg, nullptr, sm.xs, sm.gs, sm.red, best_v, best_i);
   stamp(2 + a.n_layers * 10);
-  if (gemv_argmax_finish(g, best_v, best_i, sm.cta_val, sm.cta_idx) && threadIdx.x == 0) {
+  if (gemv_argmax_finish(*hg, best_v, best_i, sm.cta_val, sm.cta_idx) && threadIdx.x == 0) {
     // the chosen id (just written by this thread), its history slot, the position
     if (pos >= 0 && pos < a.hist_cap) a.hist[pos] = a.ids[0];
     a.ctl[0] = pos;

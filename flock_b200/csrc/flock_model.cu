@@ -34,7 +34,7 @@ struct flock_model {
   // persistent decode kernel
   int decode_mode = FLOCK_DECODE_KERNELS;
   bool mk_ok = false;       // shape fits the persistent kernel
-  DBuf mk_layers, mk_bar, mk_err, mk_trace;
+  DBuf mk_layers, mk_bar, mk_err, mk_trace, mk_gemv, mk_attn;
   MkArgs mk{};
   size_t mk_smem = 0;
   int mk_grid = 0;
@@ -305,6 +305,111 @@ int mk_prepare(flock_model* m) {
   a.err = m->mk_err.as<int>();
   // the last layer streams the head's first rows into L2 (it exceeds L2)
   a.head_prefetch = (int64_t)48 << 20;
+  // per-phase arguments: what each phase's kernel-graph launch would get
+  // (n = 1, no step-control advance, no prefetch list)
+  {
+    auto seg = [](const flock_tensor* t, float* out, int out_stride) {
+      GemvSeg s;
+      s.qs = t->qs.as<uint8_t>();
+      s.sc = t->sc.as<uint16_t>();
+      s.out = out;
+      s.rows = (int)t->rows;
+      s.sc_stride = t->sc_stride;
+      s.out_stride = out_stride;
+      return s;
+    };
+    Workspace& ws = m->ws;
+    const int qw = c.n_heads * c.head_dim, kvw = c.n_kv_heads * c.head_dim;
+    std::vector<GemvArgs> gv((size_t)4 * m->held + 1);
+    std::vector<AttnFastArgs> at((size_t)m->held);
+    for (int i = 0; i < m->held; i++) {
+      flock_layer* L = m->layers[i];
+      GemvArgs* g = &gv[(size_t)4 * i];
+      g[0] = GemvArgs{};
+      g[0].seg[0] = seg(L->w[W_Q], ws.q.as<float>(), qw);
+      g[0].seg[1] = seg(L->w[W_K], ws.k.as<float>(), kvw);
+      g[0].seg[2] = seg(L->w[W_V], ws.v.as<float>(), kvw);
+      g[0].nseg = 3;
+      g[0].K = c.hidden;
+      g[0].n_tokens = 1;
+      g[0].x = ws.h.as<float>();
+      g[0].x_stride = c.hidden;
+      g[0].norm_gain = L->w[W_ATTN_NORM]->data.as<float>();
+      g[0].eps = c.eps;
+      g[1] = GemvArgs{};
+      g[1].seg[0] = seg(L->w[W_O], ws.h.as<float>(), c.hidden);
+      g[1].nseg = 1;
+      g[1].K = qw;
+      g[1].n_tokens = 1;
+      g[1].x = ws.attn.as<float>();
+      g[1].x_stride = qw;
+      g[1].res = ws.h.as<float>();
+      g[1].res_stride = c.hidden;
+      g[2] = GemvArgs{};
+      g[2].seg[0] = seg(L->w[W_GATE], ws.act.as<float>(), c.ffn);
+      g[2].seg[1] = seg(L->w[W_UP], ws.act.as<float>(), c.ffn);
+      g[2].nseg = 2;
+      g[2].K = c.hidden;
+      g[2].n_tokens = 1;
+      g[2].x = ws.h.as<float>();
+      g[2].x_stride = c.hidden;
+      g[2].norm_gain = L->w[W_FFN_NORM]->data.as<float>();
+      g[2].eps = c.eps;
+      g[3] = GemvArgs{};
+      g[3].seg[0] = seg(L->w[W_DOWN], ws.h.as<float>(), c.hidden);
+      g[3].nseg = 1;
+      g[3].K = c.ffn;
+      g[3].n_tokens = 1;
+      g[3].x = ws.act.as<float>();
+      g[3].x_stride = c.ffn;
+      g[3].res = ws.h.as<float>();
+      g[3].res_stride = c.hidden;
+      AttnFastArgs& aa = at[(size_t)i];
+      aa = AttnFastArgs{};
+      aa.q = ws.q.as<float>();
+      aa.k = ws.k.as<float>();
+      aa.v = ws.v.as<float>();
+      aa.q_norm = L->w[W_Q_NORM]->data.as<float>();
+      aa.k_norm = L->w[W_K_NORM]->data.as<float>();
+      aa.inv_freq = L->inv_freq.as<float>();
+      aa.kcache = L->kcache.as<float>();
+      aa.vcache = L->vcache.as<float>();
+      aa.out = ws.attn.as<float>();
+      aa.part = ws.attn_part.as<float>();
+      aa.count = ws.attn_count.as<uint32_t>();
+      aa.n_heads = c.n_heads;
+      aa.n_kv_heads = c.n_kv_heads;
+      aa.head_dim = c.head_dim;
+      aa.splits = splits;
+      aa.eps = c.eps;
+      aa.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
+      aa.chunk_cap = (c.max_keys + splits - 1) / splits;
+      aa.combine = 1;
+    }
+    GemvArgs& hg = gv[(size_t)4 * m->held];
+    hg = GemvArgs{};
+    hg.seg[0] = seg(m->head, m->logits.as<float>(), (int)m->head->rows);
+    hg.nseg = 1;
+    hg.K = c.hidden;
+    hg.n_tokens = 1;
+    hg.x = ws.h.as<float>();
+    hg.x_stride = c.hidden;
+    hg.norm_gain = m->out_norm->data.as<float>();
+    hg.eps = c.eps;
+    hg.am_val = m->am_val.as<float>();
+    hg.am_idx = m->am_idx.as<uint32_t>();
+    hg.am_count = m->am_count.as<uint32_t>();
+    hg.am_best_val = m->am_best_val.as<float>();
+    hg.am_best_idx = m->ids.as<int32_t>();
+    FLOCK_TRY(m->mk_gemv.alloc(gv.size() * sizeof(GemvArgs)));
+    FLOCK_CK(cudaMemcpy(m->mk_gemv.p, gv.data(), gv.size() * sizeof(GemvArgs),
+                        cudaMemcpyHostToDevice));
+    FLOCK_TRY(m->mk_attn.alloc(at.size() * sizeof(AttnFastArgs)));
+    FLOCK_CK(cudaMemcpy(m->mk_attn.p, at.data(), at.size() * sizeof(AttnFastArgs),
+                        cudaMemcpyHostToDevice));
+    a.gemv = m->mk_gemv.as<GemvArgs>();
+    a.attn_args = m->mk_attn.as<AttnFastArgs>();
+  }
   FLOCK_TRY(kernel_setup((const void*)k_decode_mk, (int)smem));
   int per_sm = 0;
   FLOCK_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mk, MK_THREADS, smem));

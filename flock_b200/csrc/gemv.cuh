@@ -497,12 +497,15 @@ FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const f
 }
 
 // x for token `tok` into xs (padded layout), RMSNorm-ed when a.norm_gain is
-// set; the caller synchronises the block afterwards.
-FLOCK_DEV void gemv_stage_x(const GemvArgs& a, int tok, float* xs, float* gs, float* red) {
+// set; `from` (if given) replaces a.x + tok * x_stride as the source row.
+// The caller synchronises the block afterwards.
+FLOCK_DEV void gemv_stage_x(const GemvArgs& a, int tok, float* xs, float* gs, float* red,
+                            const float* from = nullptr) {
+  const float* x = from ? from : a.x + (size_t)tok * a.x_stride;
   if (a.norm_gain) {
-    rmsnorm_to_smem(a.x + (size_t)tok * a.x_stride, a.norm_gain, a.K, a.eps, xs, gs, red);
+    rmsnorm_to_smem(x, a.norm_gain, a.K, a.eps, xs, gs, red);
   } else {
-    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)tok * a.x_stride);
+    const float4* src = reinterpret_cast<const float4*>(x);
 #pragma unroll 4
     for (int i = threadIdx.x; i < a.K / 4; i += GEMV_THREADS)
       reinterpret_cast<float4*>(xs)[(i >> 3) * (XPAD / 4) + (i & 7)] = src[i];
