@@ -248,6 +248,9 @@ def main():
                          "(config 2 / 4a) or tensor-sharded layers and head (config 4b)")
     ap.add_argument("--shape", default="0.6b", choices=["0.6b", "8b"],
                     help="Qwen3-0.6B shape (configs 1-3) or Qwen3-8B shape (config 4)")
+    ap.add_argument("--allocate", action="store_true",
+                    help="pipeline stages from the makespan allocator fed by each GPU's measured "
+                         "bytes/ms (rank 0 charged for its head), instead of config 2's 4 + even")
     ap.add_argument("--prompt", type=int, default=None,
                     help="prompt tokens before the timed decode (default 64; 4096 for 8b)")
     args = ap.parse_args()
@@ -547,7 +550,23 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     comm = ctypes.c_void_p()
     _abi.call("flock_comm_init", dev.handle, world, rank, _abi.ptr(uid, _abi._u8p), 60000,
               ctypes.byref(comm))
-    a, b = stage_ranges(shape.n_layers, world)[rank]
+    ranges = stage_ranges(shape.n_layers, world)
+    if args.allocate:
+        # server/allocate.js fed by measurement: every rank's streaming rate,
+        # rank 0 charged the time of the head it also runs
+        from flock_b200.allocate import Device, allocate, layer_plan, measure_rate
+        from flock_b200 import ops
+        rate = measure_rate(dev)
+        reserved = 0.0
+        if rank == 0:
+            ht = GpuTensor.from_packed(dev, m.embd["packed"], m.embd["rows"], m.embd["cols"])
+            reserved = ops.matvec_timed(dev, ht, 1, 20)
+            ht.free()
+        got = [None] * world
+        dist.all_gather_object(got, (rate, reserved))
+        devs = [Device(f"gpu{r}", rate=got[r][0], reserved_ms=got[r][1]) for r in range(world)]
+        ranges = allocate(layer_plan(m), devs).ranges()
+    a, b = ranges[rank]
     layer_ts = [upload_layer(dev, m.layers[i]) for i in range(a, b)]
     if rank == 0:
         embd = GpuTensor.from_packed(dev, m.embd["packed"], m.embd["rows"], m.embd["cols"])
@@ -617,7 +636,8 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
             "data": "synthetic",
             "config": {"workload": f"config {'4a (8B shape)' if shape.n_layers == 36 else '2'} "
                                    "pipelined: contiguous layer ranges "
-                                   f"{stage_ranges(shape.n_layers, world)}, hidden state over "
+                                   f"{ranges}{' (allocator)' if args.allocate else ''}, "
+                                   "hidden state over "
                                    "NCCL send/recv", "seed": SEED, "prompt": PROMPT,
                        "attention": args.attention, "parallelism": f"pp{world}",
                        "l2": "inputs larger than L2"},
