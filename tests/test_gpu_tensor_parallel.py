@@ -35,7 +35,7 @@ def _oracle_run(oracle, m, tp, prompt, n_decode):
     """Greedy ids and last logits of the oracle model with tp-shard layers."""
     oracle.set_fma_mode(True)
     try:
-        layers = [oracle.RefLayer(w, CFG, 64, tp=tp) for w in m.layers]
+        layers = [oracle.RefLayer(w, CFG, 256, tp=tp) for w in m.layers]
         ids, out, lg = list(prompt), [], None
         for _ in range(1 + n_decode):
             n = len(ids)
