@@ -461,6 +461,9 @@ def run_tensor(args, rank, world, local, dev, shape, pk):
     t_load = time.perf_counter() - t0
     log(f"[rank {rank}] tensor-parallel rank built in {t_load:.1f}s")
     prompt = synth.uniform_ids(SEED, "prompt", n_prompt, shape.vocab)
+    # warm-up prefill: NCCL connects its channels on the first collectives
+    M.step(prompt[:min(64, n_prompt)])
+    M.reset()
     if world > 1:
         dist.barrier()
     dev.timer_start()
