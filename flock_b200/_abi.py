@@ -27,6 +27,7 @@ FLOCK_ROPE_NEOX, FLOCK_ROPE_NORM = 0, 1
 FLOCK_ATTN_EXACT, FLOCK_ATTN_FAST = 0, 1
 FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT, FLOCK_DECODE_EAGER = 0, 1, 2
 FLOCK_PREFILL_EXACT, FLOCK_PREFILL_TENSOR = 0, 1
+FLOCK_TP_NCCL, FLOCK_TP_PEER = 0, 1
 
 
 class FlockError(RuntimeError):
@@ -101,6 +102,8 @@ SIGNATURES = {
     "flock_range_forward": [_pp, _i, _fp, _i, _i, _i, _fp],
     "flock_model_create": [_vp, _cfgp, _i, _i, _pp, _vp, _vp, _vp, _i, _pp],
     "flock_model_create_tp": [_vp, _cfgp, _i, _i, _pp, _vp, _vp, _vp, _vp, _pp],
+    "flock_model_set_tp_exchange": [_vp, _i],
+    "flock_model_get_tp_exchange": [_vp, _ip],
     "flock_gguf_open": [ctypes.c_char_p, _pp],
     "flock_gguf_free": [_vp],
     "flock_gguf_info": [_vp, _i64p, _i64p, _ip, _ip],

@@ -416,6 +416,9 @@ static int tp_sum_into_h(flock_layer* L, int n) {
     return FLOCK_E_STATE;
   }
   const int64_t count = (int64_t)n * L->cfg.hidden;
+  if (L->xchg && n == 1)  // decode: the fused peer-memory exchange, same sum
+    return peer_xchg_run(L->xchg, L->dev->stream, ws->h.as<float>(), ws->tp_part.as<float>(),
+                         count);
   FLOCK_TRY(comm_allgather_dev(L->tp, ws->tp_part.p, ws->tp_all.p, (size_t)count * 4));
   k_tp_reduce_residual<<<(unsigned)((count + 255) / 256), 256, 0, L->dev->stream>>>(
       ws->h.as<float>(), ws->tp_all.as<float>(), L->tp_n, count);

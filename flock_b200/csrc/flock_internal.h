@@ -107,6 +107,7 @@ int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl);
 // tensor-core prefill GEMM (flock_gemm.cu)
 struct TcArgs;
 struct TcSeg;
+struct PeerXchg;
 size_t act_image_bytes(int M, int K);
 int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float* gain, float eps,
                       int M, int K, uint8_t* img);
@@ -131,6 +132,7 @@ struct flock_layer {
   // partial sums that are all-gathered over `tp` and added in rank order
   flock_comm* tp = nullptr;
   int tp_n = 1;
+  flock::PeerXchg* xchg = nullptr;  // decode steps: the fused peer exchange (else NCCL)
   flock::Workspace* ws = nullptr;
   flock::Workspace ws_own;     // standalone layers own their workspace
   bool owns_ws = false;
@@ -149,6 +151,13 @@ int comm_wait(flock_comm* c);
 // NCCL all-gather of `bytes` per rank between device buffers on the
 // communicator's stream (out is [n_ranks][bytes], rank order).
 int comm_allgather_dev(flock_comm* c, const void* in, void* out, size_t bytes);
+// Fused peer-memory exchange (flock_peer.cu): h[i] += sum over ranks of the
+// ranks' part[i], rank order; `cap` floats per exchange.  init and free are
+// collectives over the communicator.
+int peer_xchg_init(flock_comm* c, int64_t cap, PeerXchg** out);
+int peer_xchg_run(PeerXchg* x, cudaStream_t st, float* h, const float* part, int64_t n);
+int peer_xchg_check(PeerXchg* x);
+int peer_xchg_free(PeerXchg* x);
 int comm_rank(const flock_comm* c, int* rank, int* n_ranks);
 flock_dev* comm_device(const flock_comm* c);
 int layer_build(flock_dev* dev, const flock_layer_config* cfg, int n_tensors,

@@ -41,6 +41,8 @@ struct flock_model {
   // tensor parallel: this rank holds vocab rows [tp_start[r], tp_start[r+1])
   // of the head; layers exchange partials over `tp`
   flock_comm* tp = nullptr;
+  PeerXchg* xchg = nullptr;   // fused peer exchange for decode steps (null: NCCL)
+  int tp_exchange = FLOCK_TP_PEER;
   int tp_rank = 0, tp_n = 1, tp_chunk = 0;
   std::vector<int64_t> tp_start;
   DBuf tp_best, tp_bests, tp_logits;
@@ -443,6 +445,7 @@ int enqueue_mk(flock_model* m) {
 // prefill GEMMs; call after a synchronisation.
 int check_device_errors(flock_model* m) {
   FLOCK_TRY(ws_check_errors(&m->ws));
+  FLOCK_TRY(peer_xchg_check(m->xchg));
   if (!m->mk_ok || m->decode_mode != FLOCK_DECODE_PERSISTENT) return FLOCK_OK;
   int err = 0;
   FLOCK_CK(cudaMemcpy(&err, m->mk_err.p, 4, cudaMemcpyDeviceToHost));
@@ -587,6 +590,12 @@ int model_build(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_
     m->layers.push_back(L);
   }
   m->held = cut;
+  if (tp) {
+    // decode exchanges through peer memory when every rank maps every peer;
+    // otherwise (the ranks agree) they stay on NCCL
+    if (peer_xchg_init(tp, cfg->hidden, &m->xchg) != FLOCK_OK) m->xchg = nullptr;
+    for (auto* L : m->layers) L->xchg = m->xchg;
+  }
   if ((rc = mk_prepare(m))) return fail(rc);
   *out = m;
   return FLOCK_OK;
@@ -666,6 +675,32 @@ int flock_model_trace_read(flock_model* m, uint64_t* out, int64_t cap, int* n_ct
   return FLOCK_OK;
 }
 
+int flock_model_set_tp_exchange(flock_model* m, int mode) {
+  if (!m || (mode != FLOCK_TP_NCCL && mode != FLOCK_TP_PEER)) return FLOCK_E_ARG;
+  if (!m->tp) {
+    set_error("not a tensor-parallel model");
+    return FLOCK_E_STATE;
+  }
+  if (mode == FLOCK_TP_PEER && !m->xchg) {
+    set_error("the ranks could not map each other's memory; decode exchanges stay on NCCL");
+    return FLOCK_E_UNSUPPORTED;
+  }
+  if (m->decode_graph) {
+    cudaStreamSynchronize(m->dev->stream);
+    cudaGraphExecDestroy(m->decode_graph);
+    m->decode_graph = nullptr;
+  }
+  m->tp_exchange = mode;
+  for (auto* L : m->layers) L->xchg = mode == FLOCK_TP_PEER ? m->xchg : nullptr;
+  return FLOCK_OK;
+}
+
+int flock_model_get_tp_exchange(const flock_model* m, int* mode) {
+  if (!m || !mode) return FLOCK_E_ARG;
+  *mode = (m->tp && m->xchg && m->tp_exchange == FLOCK_TP_PEER) ? FLOCK_TP_PEER : FLOCK_TP_NCCL;
+  return FLOCK_OK;
+}
+
 int flock_model_get_decode_mode(const flock_model* m, int* mode) {
   if (!m || !mode) return FLOCK_E_ARG;
   *mode = (m->decode_mode == FLOCK_DECODE_PERSISTENT && !m->mk_ok) ? FLOCK_DECODE_KERNELS
@@ -680,6 +715,7 @@ int flock_model_free(flock_model* m) {
   cudaStreamSynchronize(d->stream);
   if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
   for (auto* L : m->layers) flock_layer_free(L);
+  peer_xchg_free(m->xchg);  // a collective: every rank frees its model
   delete m;
   dev_release(d);
   return FLOCK_OK;

@@ -1,0 +1,227 @@
+// Fused peer-memory exchange for tensor-parallel decode: the o_proj / down
+// partials of every rank summed in rank order, without NCCL.
+//
+// Each rank exports one buffer and one flag array (cudaIpcGetMemHandle) and
+// maps every peer's (cudaIpcOpenMemHandle, NVLink).  One exchange is one
+// kernel on each rank:
+//   1. push: write this rank's partial [n] into slot [parity][rank] of every
+//      rank's buffer (plain stores over NVLink; no TMA, no multicast);
+//   2. publish: system-scope fence, then a release store of the exchange's
+//      epoch into flag [parity][rank] of every rank;
+//   3. wait: acquire-poll this rank's own flags until every rank has
+//      published this epoch (bounded by the global timer: a peer that never
+//      arrives sets the error word and the kernel returns);
+//   4. reduce: h += p_0 + p_1 + ... + p_{N-1} summed serially in rank order
+//      (shard_ref.ts:327 shardReduceRef's order), the arithmetic of the NCCL
+//      path's k_tp_reduce_residual, so both paths give identical bits.
+// Two parity slots: a rank can run at most one exchange ahead of a peer (its
+// next exchange needs that peer's next partial, which the peer publishes only
+// after it has reduced the current one), so the slot it writes is never the
+// one the peer is still reading.
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "flock_internal.h"
+#include "mbar.cuh"
+
+namespace flock {
+
+struct PeerXchg {
+  flock_comm* comm = nullptr;
+  int rank = 0, n = 1;
+  int64_t cap = 0;                 // floats per (slot, rank)
+  float* buf = nullptr;            // this rank's [2][n][cap]
+  uint32_t* flag = nullptr;        // this rank's [2][n]
+  std::vector<void*> opened;       // peers' mapped buffers / flags (closed at free)
+  float** d_bufs = nullptr;        // [n] device pointers (own or mapped)
+  uint32_t** d_flags = nullptr;    // [n]
+  uint32_t* epoch = nullptr;       // exchanges completed by this rank
+  int* err = nullptr;              // 3 = a peer never published
+};
+
+namespace {
+
+FLOCK_DEV void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+FLOCK_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(256) k_peer_xchg(const float* __restrict__ part, float* h, int n,
+                                                   int rank, int n_ranks, int64_t cap,
+                                                   float* const* bufs, uint32_t* const* flags,
+                                                   uint32_t* epoch_p, int* err) {
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_ok;
+  const int t = threadIdx.x;
+  if (t == 0) s_epoch = *epoch_p + 1u;
+  __syncthreads();
+  const uint32_t e = s_epoch, slot = e & 1u;
+  for (int i = t; i < n; i += blockDim.x) {
+    const float v = part[i];
+    for (int r = 0; r < n_ranks; r++) bufs[r][((int64_t)slot * n_ranks + rank) * cap + i] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (t == 0) {
+    for (int r = 0; r < n_ranks; r++) st_release_sys(flags[r] + slot * n_ranks + rank, e);
+    const uint32_t* mine = flags[rank] + slot * n_ranks;
+    int ok = 1;
+    uint64_t t0 = 0;
+    for (int r = 0; r < n_ranks && ok; r++) {
+      for (uint32_t i = 0; (int32_t)(ld_acquire_sys(mine + r) - e) < 0; i++) {
+        if ((i & 63) != 63) continue;
+        const uint64_t now = globaltimer_ns();
+        if (!t0) t0 = now;
+        if (now - t0 > WAIT_NS || i >= WAIT_MAX_POLLS) {
+          atomicExch(err, 3);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const float* own = bufs[rank] + (int64_t)slot * n_ranks * cap;
+  for (int i = t; i < n; i += blockDim.x) {
+    float acc = __ldcg(own + i);
+    for (int r = 1; r < n_ranks; r++) acc = fadd(acc, __ldcg(own + (int64_t)r * cap + i));
+    h[i] = fadd(h[i], acc);
+  }
+  if (t == 0) *epoch_p = e;
+}
+
+}  // namespace
+
+int peer_xchg_free(PeerXchg* x) {
+  if (!x) return FLOCK_OK;
+  // every rank must be done with every buffer before any is released
+  if (x->comm && x->n > 1) {
+    float one = 1.0f, sum = 0.0f;
+    flock_comm_allreduce_f32(x->comm, &one, &sum, 1);
+  }
+  for (void* p : x->opened) cudaIpcCloseMemHandle(p);
+  cudaFree(x->buf);
+  cudaFree(x->flag);
+  cudaFree(x->d_bufs);
+  cudaFree(x->d_flags);
+  cudaFree(x->epoch);
+  cudaFree(x->err);
+  delete x;
+  return FLOCK_OK;
+}
+
+int peer_xchg_init(flock_comm* c, int64_t cap, PeerXchg** out) {
+  *out = nullptr;
+  int rank = 0, n = 1;
+  FLOCK_TRY(comm_rank(c, &rank, &n));
+  flock_dev* dev = comm_device(c);
+  FLOCK_CK(cudaSetDevice(dev->ordinal));
+  PeerXchg* x = new PeerXchg();
+  x->comm = c;
+  x->rank = rank;
+  x->n = n;
+  x->cap = cap;
+  auto fail = [&](int rc) {
+    peer_xchg_free(x);
+    return rc;
+  };
+  if (cudaMalloc(&x->buf, (size_t)2 * n * cap * 4) != cudaSuccess ||
+      cudaMalloc(&x->flag, (size_t)2 * n * 4) != cudaSuccess ||
+      cudaMalloc(&x->d_bufs, (size_t)n * sizeof(float*)) != cudaSuccess ||
+      cudaMalloc(&x->d_flags, (size_t)n * sizeof(uint32_t*)) != cudaSuccess ||
+      cudaMalloc(&x->epoch, 16) != cudaSuccess || cudaMalloc(&x->err, 16) != cudaSuccess) {
+    set_error("peer exchange: device allocation failed");
+    x->comm = nullptr;  // no collective on this path: the peers may not have got here
+    return fail(FLOCK_E_NOMEM);
+  }
+  FLOCK_CK(cudaMemset(x->flag, 0, (size_t)2 * n * 4));
+  FLOCK_CK(cudaMemset(x->epoch, 0, 16));
+  FLOCK_CK(cudaMemset(x->err, 0, 16));
+  std::vector<float*> bufs(n, nullptr);
+  std::vector<uint32_t*> flags(n, nullptr);
+  bufs[rank] = x->buf;
+  flags[rank] = x->flag;
+  if (n > 1) {
+    cudaIpcMemHandle_t mine[2];
+    if (cudaIpcGetMemHandle(&mine[0], x->buf) != cudaSuccess ||
+        cudaIpcGetMemHandle(&mine[1], x->flag) != cudaSuccess) {
+      set_error("peer exchange: cudaIpcGetMemHandle failed");
+      x->comm = nullptr;
+      return fail(FLOCK_E_CUDA);
+    }
+    std::vector<cudaIpcMemHandle_t> all((size_t)2 * n);
+    int rc = flock_comm_allgather_bytes(c, mine, all.data(), (int64_t)sizeof(mine));
+    if (rc) {
+      x->comm = nullptr;
+      return fail(rc);
+    }
+    int bad = -1;
+    for (int r = 0; r < n && bad < 0; r++) {
+      if (r == rank) continue;
+      void* pb = nullptr;
+      void* pf = nullptr;
+      if (cudaIpcOpenMemHandle(&pb, all[(size_t)2 * r], cudaIpcMemLazyEnablePeerAccess) !=
+          cudaSuccess) {
+        bad = r;
+        break;
+      }
+      x->opened.push_back(pb);
+      if (cudaIpcOpenMemHandle(&pf, all[(size_t)2 * r + 1], cudaIpcMemLazyEnablePeerAccess) !=
+          cudaSuccess) {
+        bad = r;
+        break;
+      }
+      x->opened.push_back(pf);
+      bufs[r] = (float*)pb;
+      flags[r] = (uint32_t*)pf;
+    }
+    cudaGetLastError();
+    // every rank learns whether every rank mapped every peer
+    float failed = bad >= 0 ? 1.0f : 0.0f, any = 0.0f;
+    rc = flock_comm_allreduce_f32(c, &failed, &any, 1);
+    if (rc || any > 0.0f) {
+      if (bad >= 0) set_error("peer exchange: cannot map rank %d's memory (no peer access?)", bad);
+      else if (!rc) set_error("peer exchange: another rank could not map its peers");
+      x->comm = nullptr;  // the ranks agreed; no further collective here
+      return fail(rc ? rc : FLOCK_E_UNSUPPORTED);
+    }
+  }
+  FLOCK_CK(cudaMemcpy(x->d_bufs, bufs.data(), (size_t)n * sizeof(float*), cudaMemcpyHostToDevice));
+  FLOCK_CK(cudaMemcpy(x->d_flags, flags.data(), (size_t)n * sizeof(uint32_t*),
+                      cudaMemcpyHostToDevice));
+  *out = x;
+  return FLOCK_OK;
+}
+
+int peer_xchg_run(PeerXchg* x, cudaStream_t st, float* h, const float* part, int64_t n) {
+  if (n > x->cap) {
+    set_error("peer exchange of %lld floats exceeds its %lld-float slots", (long long)n,
+              (long long)x->cap);
+    return FLOCK_E_LIMIT;
+  }
+  k_peer_xchg<<<1, 256, 0, st>>>(part, h, (int)n, x->rank, x->n, x->cap, x->d_bufs, x->d_flags,
+                                 x->epoch, x->err);
+  FLOCK_CK(cudaGetLastError());
+  return FLOCK_OK;
+}
+
+int peer_xchg_check(PeerXchg* x) {
+  if (!x) return FLOCK_OK;
+  int e = 0;
+  FLOCK_CK(cudaMemcpy(&e, x->err, 4, cudaMemcpyDeviceToHost));
+  if (e) {
+    set_error("tensor-parallel peer exchange gave up waiting for a rank");
+    cudaMemset(x->err, 0, 4);
+    return FLOCK_E_CUDA;
+  }
+  return FLOCK_OK;
+}
+
+}  // namespace flock

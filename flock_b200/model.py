@@ -222,6 +222,20 @@ class Model:
             raise ValueError(f"decode mode {mode!r} is not one of {sorted(self._MODES)}")
         _abi.call("flock_model_set_decode_mode", self.handle, self._MODES[mode])
 
+    @property
+    def tp_exchange(self) -> str:
+        """Tensor-parallel decode exchange: "peer" (NVLink peer memory) or "nccl"."""
+        n = ctypes.c_int()
+        _abi.call("flock_model_get_tp_exchange", self.handle, ctypes.byref(n))
+        return "peer" if n.value == _abi.FLOCK_TP_PEER else "nccl"
+
+    @tp_exchange.setter
+    def tp_exchange(self, mode: str) -> None:
+        if mode not in ("peer", "nccl"):
+            raise ValueError(f"tp exchange {mode!r} is neither 'peer' nor 'nccl'")
+        _abi.call("flock_model_set_tp_exchange", self.handle,
+                  _abi.FLOCK_TP_PEER if mode == "peer" else _abi.FLOCK_TP_NCCL)
+
     def trace(self, enable: bool = True) -> None:
         """Record per-CTA phase timestamps in the persistent decode kernel."""
         _abi.call("flock_model_trace", self.handle, 1 if enable else 0)

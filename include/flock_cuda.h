@@ -256,6 +256,17 @@ FLOCK_API int flock_model_create_tp(flock_dev* dev, const flock_layer_config* cf
                                    const flock_tensor* embd, const flock_tensor* output_norm,
                                    const flock_tensor* output_slice, flock_comm* comm,
                                    flock_model** out);
+/* How a tensor-parallel model's decode steps exchange the o_proj / down
+ * partials: FLOCK_TP_PEER (default when every rank can map every peer's
+ * memory) -- one kernel per exchange pushes this rank's partial into every
+ * rank's buffer over NVLink, publishes an epoch flag and sums the ranks'
+ * partials in rank order once all flags arrived (bounded wait); or
+ * FLOCK_TP_NCCL -- an NCCL all-gather and the same ordered sum.  Both give
+ * identical bits.  Multi-token steps always use NCCL. */
+#define FLOCK_TP_NCCL 0
+#define FLOCK_TP_PEER 1
+FLOCK_API int flock_model_set_tp_exchange(flock_model* m, int mode);
+FLOCK_API int flock_model_get_tp_exchange(const flock_model* m, int* mode);
 FLOCK_API int flock_model_free(flock_model* m);
 /* kernels/model.ts:387 step(ids): prefill/decode ids, return the greedy id. */
 FLOCK_API int flock_model_step(flock_model* m, const int32_t* ids, int n, int32_t* next_id);

@@ -4,7 +4,8 @@
   rank-order sum of one partial is the partial itself, so logits and ids are
   bit-identical to the single-GPU model, in every decode mode;
 * two ranks on two GPUs (skipped with fewer): the o_proj / down partials are
-  all-gathered and summed in rank order and the head's maxima reduced, so the
+  exchanged (NVLink peer memory for decode steps, or an NCCL all-gather) and
+  summed in rank order and the head's maxima reduced, so the
   gathered logits equal the oracle's tensor-parallel model (RefLayer(tp=2),
   shardedColMatvecRef per projection) bit for bit, and the ids follow; the
   device-fed decode graph (NCCL inside the captured graph) gives the ids of
@@ -74,6 +75,10 @@ def test_one_rank_equals_single_gpu_model():
         assert T.decode_mode == "eager"
         nxt = [ref.step([want[-1]])]
         assert T.step([want[-1]]) == nxt[0]
+        assert T.tp_exchange == "peer"
+        T.tp_exchange = "nccl"
+        assert T.tp_exchange == "nccl"
+        assert T.step([nxt[0]]) == ref.step([nxt[0]])
         T.free()
         ref.free()
 
@@ -136,6 +141,15 @@ def _rank_body(rank, world, q_uid):
     M = Model.create_tp(dev, m, QWEN3_06B.with_(prefill="tensor"), comm, rank, world)
     res["tensor_prefill"] = M.logits(LONG)
     M.free()
+    # the two decode exchanges (NVLink peer memory, NCCL) give the same bits
+    M = Model.create_tp(dev, m, QWEN3_06B.with_(attention="fast"), comm, rank, world)
+    res["default_exchange"] = M.tp_exchange
+    for mode in ("peer", "nccl"):
+        M.tp_exchange = mode
+        M.reset()
+        ids = [M.step(PROMPT)] + M.decode_device(N_DECODE - 1).tolist()
+        res[f"xchg_{mode}"] = (ids, M.logits([ids[-1]]))
+    M.free()
     comm.free()
     return res
 
@@ -172,6 +186,11 @@ def test_two_rank_tp_matches_oracle(oracle):
             assert np.array_equal(lg0.view(np.uint32), want_lg.view(np.uint32))
         else:  # fast attention: 1e-5 relative tolerance per step
             assert ids0 == want[:N_DECODE]
+    for r in (0, 1):
+        assert res[r]["default_exchange"] == "peer"
+        (ip, lp), (inc, lnc) = res[r]["xchg_peer"], res[r]["xchg_nccl"]
+        assert ip == inc == res[0]["fast"][2]
+        assert np.array_equal(lp.view(np.uint32), lnc.view(np.uint32))
     from gpu_util import abs_err_scaled
     _, want_long = _oracle_run(oracle, m, 2, LONG, 0)
     assert abs_err_scaled(res[0]["tensor_prefill"], want_long) <= 1e-2
