@@ -509,6 +509,7 @@ def run_tensor(args, rank, world, local, dev, shape, pk):
                                    "vocab rows with a (value, index) all-gather",
                        "seed": SEED, "prompt": n_prompt, "attention": args.attention,
                        "parallelism": f"tp{world}",
+                       "tp_exchange": M.tp_exchange,
                        "collectives_per_token": 2 * shape.n_layers + 1,
                        "l2": "inputs larger than L2: weights streamed per token",
                        "timing": "CUDA events around K device-fed decode steps, max over ranks"},

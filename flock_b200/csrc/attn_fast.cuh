@@ -67,7 +67,10 @@ __host__ __device__ inline int attn_max_splits(int sm_count, int n_kv_heads) {
 // Splits a step over n_keys keys uses: one per ATTN_SPLIT_KEYS keys, at most
 // max_splits.  Both decode engines use this rule, so their partials and
 // results are identical.
-constexpr int ATTN_SPLIT_KEYS = 16;
+#ifndef FLOCK_ATTN_SPLIT_KEYS
+#define FLOCK_ATTN_SPLIT_KEYS 16
+#endif
+constexpr int ATTN_SPLIT_KEYS = FLOCK_ATTN_SPLIT_KEYS;
 FLOCK_DEV int attn_splits_for(int n_keys, int max_splits) {
   const int s = (n_keys + ATTN_SPLIT_KEYS - 1) / ATTN_SPLIT_KEYS;
   return s < 1 ? 1 : (s > max_splits ? max_splits : s);

@@ -61,11 +61,18 @@ __global__ void __launch_bounds__(256) k_peer_xchg(const float* __restrict__ par
   if (t == 0) s_epoch = *epoch_p + 1u;
   __syncthreads();
   const uint32_t e = s_epoch, slot = e & 1u;
+  if (n_ranks == 1) {  // nothing to exchange: the one partial is the sum
+    for (int i = t; i < n; i += blockDim.x) h[i] = fadd(h[i], part[i]);
+    if (t == 0) *epoch_p = e;
+    return;
+  }
   for (int i = t; i < n; i += blockDim.x) {
     const float v = part[i];
     for (int r = 0; r < n_ranks; r++) bufs[r][((int64_t)slot * n_ranks + rank) * cap + i] = v;
   }
-  __threadfence_system();
+  // the CTA barrier orders every thread's pushes before thread 0's release
+  // stores, and a release is cumulative: one system-scope release per flag
+  // publishes the whole CTA's data
   __syncthreads();
   if (t == 0) {
     for (int r = 0; r < n_ranks; r++) st_release_sys(flags[r] + slot * n_ranks + rank, e);
