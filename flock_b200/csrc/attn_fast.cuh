@@ -59,8 +59,11 @@ constexpr int ATTN_TILE = 64;  // keys staged in shared memory per pass
 
 // Most splits a decode step may use: one wave of CTAs over the kv heads, and
 // at most 32 so a warp holds one split per lane when combining.
+#ifndef FLOCK_ATTN_CTAS_PER_SM
+#define FLOCK_ATTN_CTAS_PER_SM 1
+#endif
 __host__ __device__ inline int attn_max_splits(int sm_count, int n_kv_heads) {
-  int s = n_kv_heads > 0 ? sm_count / n_kv_heads : 1;
+  int s = n_kv_heads > 0 ? sm_count * FLOCK_ATTN_CTAS_PER_SM / n_kv_heads : 1;
   return s < 1 ? 1 : (s > 32 ? 32 : s);
 }
 

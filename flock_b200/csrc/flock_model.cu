@@ -593,7 +593,8 @@ int model_build(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_
   if (tp) {
     // decode exchanges through peer memory when every rank maps every peer;
     // otherwise (the ranks agree) they stay on NCCL
-    if (peer_xchg_init(tp, cfg->hidden, &m->xchg) != FLOCK_OK) m->xchg = nullptr;
+    if (cfg->hidden > 16 * 1024 || peer_xchg_init(tp, cfg->hidden, &m->xchg) != FLOCK_OK)
+      m->xchg = nullptr;
     for (auto* L : m->layers) L->xchg = m->xchg;
   }
   if ((rc = mk_prepare(m))) return fail(rc);

@@ -32,11 +32,11 @@ struct PeerXchg {
   int rank = 0, n = 1;
   int64_t cap = 0;                 // floats per (slot, rank)
   float* buf = nullptr;            // this rank's [2][n][cap]
-  uint32_t* flag = nullptr;        // this rank's [2][n]
+  uint32_t* flag = nullptr;        // this rank's [2][n][XCHG_MAX_CTAS]
   std::vector<void*> opened;       // peers' mapped buffers / flags (closed at free)
   float** d_bufs = nullptr;        // [n] device pointers (own or mapped)
   uint32_t** d_flags = nullptr;    // [n]
-  uint32_t* epoch = nullptr;       // exchanges completed by this rank
+  uint32_t* epoch = nullptr;       // exchanges completed, per exchange CTA
   int* err = nullptr;              // 3 = a peer never published
 };
 
@@ -51,40 +51,55 @@ FLOCK_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-__global__ void __launch_bounds__(256) k_peer_xchg(const float* __restrict__ part, float* h, int n,
-                                                   int rank, int n_ranks, int64_t cap,
-                                                   float* const* bufs, uint32_t* const* flags,
-                                                   uint32_t* epoch_p, int* err) {
+// CTA c exchanges elements [c * XCHG_CHUNK, (c + 1) * XCHG_CHUNK): four per
+// thread as one 128-bit load / store, its own flag and epoch slots, so CTAs
+// need not run at the same time.
+constexpr int XCHG_THREADS = 256, XCHG_CHUNK = 4 * XCHG_THREADS, XCHG_MAX_CTAS = 16;
+
+__global__ void __launch_bounds__(XCHG_THREADS) k_peer_xchg(const float* __restrict__ part,
+                                                            float* h, int n, int rank,
+                                                            int n_ranks, int64_t cap,
+                                                            float* const* bufs,
+                                                            uint32_t* const* flags,
+                                                            uint32_t* epochs, int* err) {
   __shared__ uint32_t s_epoch;
   __shared__ int s_ok;
-  const int t = threadIdx.x;
-  if (t == 0) s_epoch = *epoch_p + 1u;
+  const int t = threadIdx.x, c = blockIdx.x;
+  const int i = c * XCHG_CHUNK + 4 * t;  // n is a multiple of 4
+  if (t == 0) s_epoch = epochs[c] + 1u;
   __syncthreads();
   const uint32_t e = s_epoch, slot = e & 1u;
+  const bool mine = i < n;
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (mine) v = *reinterpret_cast<const float4*>(part + i);
   if (n_ranks == 1) {  // nothing to exchange: the one partial is the sum
-    for (int i = t; i < n; i += blockDim.x) h[i] = fadd(h[i], part[i]);
-    if (t == 0) *epoch_p = e;
+    if (mine) {
+      float4 hv = *reinterpret_cast<float4*>(h + i);
+      hv = make_float4(fadd(hv.x, v.x), fadd(hv.y, v.y), fadd(hv.z, v.z), fadd(hv.w, v.w));
+      *reinterpret_cast<float4*>(h + i) = hv;
+    }
+    if (t == 0) epochs[c] = e;
     return;
   }
-  for (int i = t; i < n; i += blockDim.x) {
-    const float v = part[i];
-    for (int r = 0; r < n_ranks; r++) bufs[r][((int64_t)slot * n_ranks + rank) * cap + i] = v;
-  }
+  if (mine)
+    for (int r = 0; r < n_ranks; r++)
+      *reinterpret_cast<float4*>(bufs[r] + ((int64_t)slot * n_ranks + rank) * cap + i) = v;
   // the CTA barrier orders every thread's pushes before thread 0's release
   // stores, and a release is cumulative: one system-scope release per flag
   // publishes the whole CTA's data
   __syncthreads();
   if (t == 0) {
-    for (int r = 0; r < n_ranks; r++) st_release_sys(flags[r] + slot * n_ranks + rank, e);
-    const uint32_t* mine = flags[rank] + slot * n_ranks;
+    const int fo = (int)(slot * n_ranks + rank) * XCHG_MAX_CTAS + c;
+    for (int r = 0; r < n_ranks; r++) st_release_sys(flags[r] + fo, e);
+    const uint32_t* own = flags[rank] + (int)slot * n_ranks * XCHG_MAX_CTAS + c;
     int ok = 1;
     uint64_t t0 = 0;
     for (int r = 0; r < n_ranks && ok; r++) {
-      for (uint32_t i = 0; (int32_t)(ld_acquire_sys(mine + r) - e) < 0; i++) {
-        if ((i & 63) != 63) continue;
+      for (uint32_t k = 0; (int32_t)(ld_acquire_sys(own + r * XCHG_MAX_CTAS) - e) < 0; k++) {
+        if ((k & 63) != 63) continue;
         const uint64_t now = globaltimer_ns();
         if (!t0) t0 = now;
-        if (now - t0 > WAIT_NS || i >= WAIT_MAX_POLLS) {
+        if (now - t0 > WAIT_NS || k >= WAIT_MAX_POLLS) {
           atomicExch(err, 3);
           ok = 0;
           break;
@@ -95,13 +110,18 @@ __global__ void __launch_bounds__(256) k_peer_xchg(const float* __restrict__ par
   }
   __syncthreads();
   if (!s_ok) return;
-  const float* own = bufs[rank] + (int64_t)slot * n_ranks * cap;
-  for (int i = t; i < n; i += blockDim.x) {
-    float acc = __ldcg(own + i);
-    for (int r = 1; r < n_ranks; r++) acc = fadd(acc, __ldcg(own + (int64_t)r * cap + i));
-    h[i] = fadd(h[i], acc);
+  if (mine) {
+    const float* own = bufs[rank] + (int64_t)slot * n_ranks * cap + i;
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(own));
+    for (int r = 1; r < n_ranks; r++) {
+      const float4 p = __ldcg(reinterpret_cast<const float4*>(own + (int64_t)r * cap));
+      acc = make_float4(fadd(acc.x, p.x), fadd(acc.y, p.y), fadd(acc.z, p.z), fadd(acc.w, p.w));
+    }
+    float4 hv = *reinterpret_cast<float4*>(h + i);
+    hv = make_float4(fadd(hv.x, acc.x), fadd(hv.y, acc.y), fadd(hv.z, acc.z), fadd(hv.w, acc.w));
+    *reinterpret_cast<float4*>(h + i) = hv;
   }
-  if (t == 0) *epoch_p = e;
+  if (t == 0) epochs[c] = e;
 }
 
 }  // namespace
@@ -140,16 +160,16 @@ int peer_xchg_init(flock_comm* c, int64_t cap, PeerXchg** out) {
     return rc;
   };
   if (cudaMalloc(&x->buf, (size_t)2 * n * cap * 4) != cudaSuccess ||
-      cudaMalloc(&x->flag, (size_t)2 * n * 4) != cudaSuccess ||
+      cudaMalloc(&x->flag, (size_t)2 * n * 16 * 4) != cudaSuccess ||
       cudaMalloc(&x->d_bufs, (size_t)n * sizeof(float*)) != cudaSuccess ||
       cudaMalloc(&x->d_flags, (size_t)n * sizeof(uint32_t*)) != cudaSuccess ||
-      cudaMalloc(&x->epoch, 16) != cudaSuccess || cudaMalloc(&x->err, 16) != cudaSuccess) {
+      cudaMalloc(&x->epoch, 16 * 4) != cudaSuccess || cudaMalloc(&x->err, 16) != cudaSuccess) {
     set_error("peer exchange: device allocation failed");
     x->comm = nullptr;  // no collective on this path: the peers may not have got here
     return fail(FLOCK_E_NOMEM);
   }
-  FLOCK_CK(cudaMemset(x->flag, 0, (size_t)2 * n * 4));
-  FLOCK_CK(cudaMemset(x->epoch, 0, 16));
+  FLOCK_CK(cudaMemset(x->flag, 0, (size_t)2 * n * 16 * 4));
+  FLOCK_CK(cudaMemset(x->epoch, 0, 16 * 4));
   FLOCK_CK(cudaMemset(x->err, 0, 16));
   std::vector<float*> bufs(n, nullptr);
   std::vector<uint32_t*> flags(n, nullptr);
@@ -208,13 +228,14 @@ int peer_xchg_init(flock_comm* c, int64_t cap, PeerXchg** out) {
 }
 
 int peer_xchg_run(PeerXchg* x, cudaStream_t st, float* h, const float* part, int64_t n) {
-  if (n > x->cap) {
-    set_error("peer exchange of %lld floats exceeds its %lld-float slots", (long long)n,
-              (long long)x->cap);
+  const int64_t ctas = (n + XCHG_CHUNK - 1) / XCHG_CHUNK;
+  if (n > x->cap || n % 4 || ctas > XCHG_MAX_CTAS) {
+    set_error("peer exchange of %lld floats: at most %lld (and %d per CTA x %d), a multiple of 4",
+              (long long)n, (long long)x->cap, XCHG_CHUNK, XCHG_MAX_CTAS);
     return FLOCK_E_LIMIT;
   }
-  k_peer_xchg<<<1, 256, 0, st>>>(part, h, (int)n, x->rank, x->n, x->cap, x->d_bufs, x->d_flags,
-                                 x->epoch, x->err);
+  k_peer_xchg<<<(unsigned)ctas, XCHG_THREADS, 0, st>>>(part, h, (int)n, x->rank, x->n, x->cap,
+                                                       x->d_bufs, x->d_flags, x->epoch, x->err);
   FLOCK_CK(cudaGetLastError());
   return FLOCK_OK;
 }
