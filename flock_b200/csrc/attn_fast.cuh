@@ -9,10 +9,11 @@
 //    row is read from HBM once per token, not once per query head;
 //  * per split: scores by warp-parallel dot products, local max m_s, local
 //    sum l_s and unnormalised output o_s (online-softmax partials);
-//  * the splits are combined, one warp per query head:
-//    out = sum_s o_s e^(m_s-M) / sum_s l_s e^(m_s-M), by the last CTA of a
-//    group to finish (arrival counter) -- or, inside the persistent decode
-//    kernel, by every CTA of the next phase after a grid barrier;
+//  * the splits are combined by the last CTA of a group to finish (arrival
+//    counter), in both decode engines: out = sum_s o_s e^(m_s-M) /
+//    sum_s l_s e^(m_s-M), both sums in split order; one warp per query head
+//    derives the weights, then each thread sums one output element's splits
+//    with all of their loads in flight;
 //  * a step over n keys uses ceil(n / 16) splits, at most
 //    attn_max_splits(SMs, kv heads): short contexts keep few partials;
 //  * scores: one thread per (key, query head), a 128-long dot product over
@@ -77,46 +78,6 @@ constexpr int ATTN_SPLIT_KEYS = FLOCK_ATTN_SPLIT_KEYS;
 FLOCK_DEV int attn_splits_for(int n_keys, int max_splits) {
   const int s = (n_keys + ATTN_SPLIT_KEYS - 1) / ATTN_SPLIT_KEYS;
   return s < 1 ? 1 : (s > max_splits ? max_splits : s);
-}
-
-// One query head's output from its split partials ([splits][hd + 2]:
-// unnormalised o, running max m, sum l) by one warp; lane s holds split s's
-// (m, l).  out = sum_s o_s w_s / sum_s l_s w_s with w_s = e^(m_s - M), both
-// sums in split order.  store(i, value) receives element i.
-template <typename Store>
-FLOCK_DEV void attn_combine_warp(const float* pp, int splits, int hd, int lane, Store store) {
-  const float m = lane < splits ? __ldcg(pp + lane * (hd + 2) + hd) : -INFINITY;
-  const float l = lane < splits ? __ldcg(pp + lane * (hd + 2) + hd + 1) : 0.0f;
-  float M = m;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  const float w = lane < splits ? expf(m - M) : 0.0f;
-  float L = 0.0f;
-  for (int sp = 0; sp < splits; sp++)
-    L = fmaf(__shfl_sync(0xffffffffu, l, sp), __shfl_sync(0xffffffffu, w, sp), L);
-  constexpr int B = 8;  // splits whose loads are in flight together
-  for (int i0 = 0; i0 < hd; i0 += 128) {
-    float O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int sp0 = 0; sp0 < splits; sp0 += B) {
-      float ov[B][4];
-#pragma unroll
-      for (int u = 0; u < B; u++) {
-        const float* o = pp + (sp0 + u) * (hd + 2) + i0 + lane;
-#pragma unroll
-        for (int e = 0; e < 4; e++) ov[u][e] = sp0 + u < splits ? __ldcg(o + 32 * e) : 0.0f;
-      }
-#pragma unroll
-      for (int u = 0; u < B; u++) {
-        const float ws = __shfl_sync(0xffffffffu, w, (sp0 + u) & 31);
-        if (sp0 + u < splits) {
-#pragma unroll
-          for (int e = 0; e < 4; e++) O[e] = fmaf(ov[u][e], ws, O[e]);
-        }
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < 4; e++) store(i0 + lane + 32 * e, O[e] / L);
-  }
 }
 
 // Shared-memory layout (floats): raw q [4][128], raw k/v [2][128], gains
@@ -312,11 +273,38 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   sync();
   if (!*last_flag) return;
   __threadfence();
+  // the combine spread over the whole CTA: warp hq derives
+  // head hq's split weights w_s = e^(m_s - M) and L (lane s = split s), then
+  // every thread owns one (head, element) and sums its splits in order, all
+  // of the split loads in flight at once
+  float* cw = dsm + AF_SC;  // [G][32] split weights
+  float* cl = dsm + AF_ML;  // [G] L
   if (warp < G) {
-    const int h = g * G + warp;
-    float* out = a.out + (size_t)h * hd;
-    attn_combine_warp(a.part + (size_t)h * a.splits * (hd + 2), splits, hd, lane,
-                      [&](int i, float v) { out[i] = v; });
+    const float* pp = a.part + (size_t)(g * G + warp) * a.splits * (hd + 2);
+    const float m = lane < splits ? __ldcg(pp + lane * (hd + 2) + hd) : -INFINITY;
+    const float l = lane < splits ? __ldcg(pp + lane * (hd + 2) + hd + 1) : 0.0f;
+    float M = m;
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+    const float w = lane < splits ? expf(m - M) : 0.0f;
+    float L = 0.0f;
+    for (int sp = 0; sp < splits; sp++)
+      L = fmaf(__shfl_sync(0xffffffffu, l, sp), __shfl_sync(0xffffffffu, w, sp), L);
+    cw[warp * 32 + lane] = w;
+    if (lane == 0) cl[warp] = L;
+  }
+  sync();
+  for (int oi = t; oi < G * hd; oi += ATTN_FAST_THREADS) {
+    const int hq = oi / hd, i = oi - hq * hd;
+    const float* pp = a.part + (size_t)(g * G + hq) * a.splits * (hd + 2) + i;
+    float ov[32];
+#pragma unroll
+    for (int sp = 0; sp < 32; sp++) ov[sp] = sp < splits ? __ldcg(pp + sp * (hd + 2)) : 0.0f;
+    float O = 0.0f;
+#pragma unroll
+    for (int sp = 0; sp < 32; sp++)
+      if (sp < splits) O = fmaf(ov[sp], cw[hq * 32 + sp], O);
+    a.out[(size_t)(g * G + hq) * hd + i] = O / cl[hq];
   }
   if (t == 0) a.count[g] = 0;
 }

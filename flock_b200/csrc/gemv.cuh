@@ -166,6 +166,21 @@ FLOCK_DEV void stage_x_packed(const float* src, int n, float* xs, int tid, int n
   }
 }
 
+// One padded 32-float block of x (8 float4) as the 16 pairs fold_block_packed
+// multiplies: Q8_0 (x[8g+k], x[8g+4+k]), Q4_0 (x[4g+k], x[16+4g+k]).
+template <int QT>
+FLOCK_DEV void pairs_of(const float4 (&v)[8], uint64_t (&xp)[16]) {
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    const float4 lo = QT == QT_Q8 ? v[2 * g] : v[g];
+    const float4 hi = QT == QT_Q8 ? v[2 * g + 1] : v[4 + g];
+    xp[4 * g + 0] = pack2(lo.x, hi.x);
+    xp[4 * g + 1] = pack2(lo.y, hi.y);
+    xp[4 * g + 2] = pack2(lo.z, hi.z);
+    xp[4 * g + 3] = pack2(lo.w, hi.w);
+  }
+}
+
 // Block b of packed x as 16 pairs.
 FLOCK_DEV void load_pairs(const float* xs, int b, uint64_t (&xp)[16]) {
   const ulonglong2* q = reinterpret_cast<const ulonglong2*>(xs + b * XPAD);
@@ -327,7 +342,10 @@ FLOCK_DEV void rows_of(const GemvArgs& a, int g, Rows<R>& rs) {
 // then `pre()` runs -- it must leave x (padded layout) in xs and synchronise
 // the block -- then the rows are folded and the epilogue applied.  EPI_ARGMAX
 // leaves this thread's best (value, index) in best_v / best_i.
-template <int QT, int R, int EPI, int MX, int LA, class Pre>
+// PK (rows of one block per lane, K <= 1024): x lives in registers as f32x2
+// pairs and blocks fold with fold_block_packed -- the same arithmetic in
+// about a quarter fewer instructions.
+template <int QT, int R, int EPI, int MX, int LA, bool PK = false, class Pre>
 FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const float* xs,
                         Pre&& pre, float& best_v, uint32_t& best_i) {
   const int lane = threadIdx.x & 31;
@@ -383,13 +401,22 @@ FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const f
   pre();
 
   const float4* xs4 = reinterpret_cast<const float4*>(xs);
-  float4 xr[MX][8];
-#pragma unroll
-  for (int mm = 0; mm < MX; mm++) {
-    const int b = lane + 32 * mm;
+  float4 xr[PK ? 1 : MX][8];
+  uint64_t xp[PK ? 16 : 1];
+  if (PK) {
+    float4 v[8];
 #pragma unroll
     for (int j = 0; j < 8; j++)
-      xr[mm][j] = (b < nb) ? xs4[b * (XPAD / 4) + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[j] = lane < nb ? xs4[lane * (XPAD / 4) + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    pairs_of<QT>(v, reinterpret_cast<uint64_t(&)[16]>(xp));
+  } else {
+#pragma unroll
+    for (int mm = 0; mm < MX; mm++) {
+      const int b = lane + 32 * mm;
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        xr[mm][j] = (b < nb) ? xs4[b * (XPAD / 4) + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
 
   float accA[R], accB[R];
@@ -427,10 +454,16 @@ FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const f
             accA[r] = fold_block<QT>(cur[r], xb, accA[r]);
         }
       };
-      if (m < MX)
+      if (PK) {  // M == 1: the lane's only block, logical lane `lane`
+#pragma unroll
+        for (int r = 0; r < R; r++)
+          if (rs.ok[r])
+            accA[r] = fold_block_packed<QT>(cur[r], reinterpret_cast<uint64_t(&)[16]>(xp), accA[r]);
+      } else if (m < MX) {
         fold_all(xr[MX >= 2 && m == 1 ? 1 : 0]);
-      else
+      } else {
         fold_all(xs4 + b * (XPAD / 4));
+      }
     }
 
     if (m == M - 1) {
@@ -583,7 +616,7 @@ FLOCK_DEV bool gemv_argmax_finish(const GemvArgs& a, float best_v, uint32_t best
 }
 
 // MINB: resident CTAs per SM the register budget is sized for.
-template <int QT, int R, int EPI, int MX, int LA = 1, int MINB = 2>
+template <int QT, int R, int EPI, int MX, int LA = 1, int MINB = 2, bool PK = false>
 __global__ void __launch_bounds__(GEMV_THREADS, MINB) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(16) float smem[];
   const bool norm = a.norm_gain != nullptr;
@@ -597,7 +630,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB) k_gemv(const GemvArgs a) {
   uint32_t best_i = 0xFFFFFFFFu;
   // weights do not depend on any earlier kernel: their first loads go out
   // before griddepcontrol.wait, overlapping the previous kernel's tail
-  gemv_run<QT, R, EPI, MX, LA>(a, blockIdx.y, blockIdx.x, gridDim.x, xs, [&] {
+  gemv_run<QT, R, EPI, MX, LA, PK>(a, blockIdx.y, blockIdx.x, gridDim.x, xs, [&] {
     issue_prefetch(a.pf);
     pdl_launch_dependents();
     pdl_wait();
