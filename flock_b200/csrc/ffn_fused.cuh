@@ -55,12 +55,12 @@ inline size_t ffn_smem_bytes(int H, int F) {
 
 // Kernel shape rule: gate/up rows of one block per lane, and each logical
 // lane owning at most FFN_MAX_OWN act blocks.
-constexpr int FFN_MAX_OWN = 2;
+constexpr int FFN_MAX_OWN = 4;
 inline bool ffn_fused_fits(int H, int F) {
   return H % 32 == 0 && H <= 1024 && F % 32 == 0 && F / 32 <= FFN_CTAS * FFN_MAX_OWN;
 }
 
-static __global__ void __launch_bounds__(FFN_THREADS, 1) k_ffn_fused(const FfnArgs a) {
+static __global__ void __launch_bounds__(FFN_THREADS) k_ffn_fused(const FfnArgs a) {
   extern __shared__ __align__(16) float smem[];
   float* xs = smem;
   float* gs = xs + a.H / 32 * XPAD;
@@ -70,45 +70,6 @@ static __global__ void __launch_bounds__(FFN_THREADS, 1) k_ffn_fused(const FfnAr
   const int l = blockIdx.x;
   const int nbH = a.H / 32, nbF = a.F / 32;
 
-  // 2. act blocks b = l + 64k (at most FFN_MAX_OWN): warp w takes row pairs
-  //    (gate, up) 4w .. 4w+3 of each block; one row dot = lane folds block
-  //    `lane`, then the tree.  Every weight load of the warp is issued first.
-  BlockW<QT_Q8> wg[FFN_MAX_OWN][4], wu[FFN_MAX_OWN][4];
-#pragma unroll
-  for (int j = 0; j < FFN_MAX_OWN; j++) {
-    const int b = l + FFN_CTAS * j;
-    if (b >= nbF || lane >= nbH) continue;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const size_t row = (size_t)(32 * b + 4 * warp + k);
-      const uint8_t* pg = a.gate_qs + row * a.H + (size_t)lane * 32;
-      const uint8_t* pu = a.up_qs + row * a.H + (size_t)lane * 32;
-      wg[j][k].w0 = ldg_stream(pg);
-      wg[j][k].w1 = ldg_stream(pg + 16);
-      wg[j][k].s = __ldg(a.gate_sc + row * a.gu_sc_stride + lane);
-      wu[j][k].w0 = ldg_stream(pu);
-      wu[j][k].w1 = ldg_stream(pu + 16);
-      wu[j][k].s = __ldg(a.up_sc + row * a.gu_sc_stride + lane);
-    }
-  }
-  // the down rows of step 3 (rows t, t + 256, ...; this lane's blocks), too
-  constexpr int RPT = 4;  // rows per thread: H <= 4 * FFN_THREADS
-  BlockW<QT_Q8> wd[RPT][FFN_MAX_OWN];
-#pragma unroll
-  for (int q = 0; q < RPT; q++) {
-    const int r = t + q * FFN_THREADS;
-#pragma unroll
-    for (int j = 0; j < FFN_MAX_OWN; j++) {
-      const int b = l + FFN_CTAS * j;
-      if (r >= a.H || b >= nbF) continue;
-      const uint8_t* p = a.down_qs + (size_t)r * a.F + (size_t)b * 32;
-      wd[q][j].w0 = ldg_stream(p);
-      wd[q][j].w1 = ldg_stream(p + 16);
-      wd[q][j].s = __ldg(a.down_sc + (size_t)r * a.down_sc_stride + b);
-    }
-  }
-  // weights do not depend on the previous kernel: their loads above are in
-  // flight before griddepcontrol.wait
   pdl_wait();
   // 1. x = RMSNorm(h) * ffn_norm (k_gemv's fused prologue)
   rmsnorm_to_smem(a.h, a.ffn_norm, a.H, a.eps, xs, gs, red);
@@ -119,16 +80,31 @@ static __global__ void __launch_bounds__(FFN_THREADS, 1) k_ffn_fused(const FfnAr
     xr[j] = lane < nbH ? reinterpret_cast<const float4*>(xs)[lane * (XPAD / 4) + j]
                        : make_float4(0.f, 0.f, 0.f, 0.f);
 
+  // 2. act blocks b = l + 64k: warp w takes row pairs (gate, up) 4w .. 4w+3
+  //    of each block; one row dot = lane folds block `lane`, then the tree
+  for (int b = l; b < nbF; b += FFN_CTAS) {
+    const int r0 = 32 * b + 4 * warp;
+    BlockW<QT_Q8> wg[4], wu[4];
+    if (lane < nbH) {
 #pragma unroll
-  for (int j = 0; j < FFN_MAX_OWN; j++) {
-    const int b = l + FFN_CTAS * j;
-    if (b >= nbF) break;  // uniform over the CTA
+      for (int k = 0; k < 4; k++) {
+        const size_t row = (size_t)(r0 + k);
+        const uint8_t* pg = a.gate_qs + row * a.H + (size_t)lane * 32;
+        const uint8_t* pu = a.up_qs + row * a.H + (size_t)lane * 32;
+        wg[k].w0 = ldg_stream(pg);
+        wg[k].w1 = ldg_stream(pg + 16);
+        wg[k].s = __ldg(a.gate_sc + row * a.gu_sc_stride + lane);
+        wu[k].w0 = ldg_stream(pu);
+        wu[k].w1 = ldg_stream(pu + 16);
+        wu[k].s = __ldg(a.up_sc + row * a.gu_sc_stride + lane);
+      }
+    }
 #pragma unroll
     for (int k = 0; k < 4; k++) {
       float ag = 0.0f, au = 0.0f;
       if (lane < nbH) {
-        ag = fold_block<QT_Q8>(wg[j][k], xr, 0.0f);
-        au = fold_block<QT_Q8>(wu[j][k], xr, 0.0f);
+        ag = fold_block<QT_Q8>(wg[k], xr, 0.0f);
+        au = fold_block<QT_Q8>(wu[k], xr, 0.0f);
       }
       // k_gemv: y = tree(accA + accB) with accB = 0 for one-block rows
       const float gt = warp_tree_sum(fadd(ag, 0.0f));
@@ -143,16 +119,15 @@ static __global__ void __launch_bounds__(FFN_THREADS, 1) k_ffn_fused(const FfnAr
   __syncthreads();
 
   // 3. this lane's partial of every down row: blocks l, l + 64, ... in order
-#pragma unroll
-  for (int q = 0; q < RPT; q++) {
-    const int r = t + q * FFN_THREADS;
-    if (r >= a.H) break;
+  for (int r = t; r < a.H; r += FFN_THREADS) {
     float acc = 0.0f;
-#pragma unroll
-    for (int j = 0; j < FFN_MAX_OWN; j++) {
-      const int b = l + FFN_CTAS * j;
-      if (b >= nbF) break;
-      acc = fold_block<QT_Q8>(wd[q][j], reinterpret_cast<const float4*>(act + 32 * b), acc);
+    for (int b = l; b < nbF; b += FFN_CTAS) {
+      BlockW<QT_Q8> w;
+      const uint8_t* p = a.down_qs + (size_t)r * a.F + (size_t)b * 32;
+      w.w0 = ldg_stream(p);
+      w.w1 = ldg_stream(p + 16);
+      w.s = __ldg(a.down_sc + (size_t)r * a.down_sc_stride + b);
+      acc = fold_block<QT_Q8>(w, reinterpret_cast<const float4*>(act + 32 * b), acc);
     }
     a.part[(size_t)l * a.H + r] = acc;
   }
