@@ -14,7 +14,6 @@
 #include "attn_tc.cuh"
 #include "gemm_tc.cuh"
 #include "flock_internal.h"
-#include "ffn_fused.cuh"
 #include "gemv.cuh"
 #include "ops.cuh"
 
@@ -239,13 +238,6 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
     FLOCK_CK(cudaMemset(tc_err.p, 0, 16));
     FLOCK_TRY(part.alloc((size_t)8 * P * H * f));
     FLOCK_TRY(kv_img.alloc(kv_image_bytes(c.max_keys, nKV)));
-  }
-  if (ffn_fused_fits(H, F)) {
-    FLOCK_TRY(ffn_part.alloc((size_t)FFN_CTAS * H * f));
-    FLOCK_TRY(ffn_ticket.alloc(16));
-    FLOCK_TRY(ffn_err.alloc(16));
-    FLOCK_CK(cudaMemset(ffn_ticket.p, 0, 16));
-    FLOCK_CK(cudaMemset(ffn_err.p, 0, 16));
   }
   if (tp_ranks >= 1) {
     FLOCK_TRY(tp_part.alloc((size_t)P * H * f));
@@ -520,15 +512,6 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
 }
 
 int ws_check_errors(Workspace* ws) {
-  if (ws->ffn_err.p) {
-    int e = 0;
-    FLOCK_CK(cudaMemcpy(&e, ws->ffn_err.p, 4, cudaMemcpyDeviceToHost));
-    if (e) {
-      cudaMemset(ws->ffn_err.p, 0, 4);
-      set_error("fused decode FFN gave up waiting at its grid barrier (code %d)", e);
-      return FLOCK_E_CUDA;
-    }
-  }
   if (!ws->tc_err.p) return FLOCK_OK;
   int e = 0;
   FLOCK_CK(cudaMemcpy(&e, ws->tc_err.p, 4, cudaMemcpyDeviceToHost));
@@ -595,7 +578,6 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.chunk_cap = (c.max_keys + a.splits - 1) / a.splits;
     a.combine = 1;
     pf_add(a.pf, L->w[W_GATE]);
-    pf_add(a.pf, L->w[W_UP]);
     const size_t smem = attn_fast_smem(a.chunk_cap);
     FLOCK_TRY(kernel_setup((const void*)k_attn_decode_fast, 200 * 1024));
     FLOCK_CK(launch_ex(d->stream, k_attn_decode_fast, dim3(c.n_kv_heads, a.splits),
@@ -618,33 +600,6 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     pf_add(a.pf, L->w[W_DOWN]);
     FLOCK_TRY(launch_gemv(d, QT_Q8, L->tp ? EPI_STORE : EPI_RESIDUAL, a, pdl));
     if (L->tp) FLOCK_TRY(tp_sum_into_h(L, n));
-  }
-  // 5-6. decode of a small shape: ffn_norm, gate/up, SwiGLU, down and the
-  // residual in one kernel (same arithmetic, one kernel boundary fewer)
-  if (n == 1 && !L->tp && ws->ffn_part.p && L->w[W_GATE]->dtype == FLOCK_Q8_0 &&
-      L->w[W_UP]->dtype == FLOCK_Q8_0 && L->w[W_DOWN]->dtype == FLOCK_Q8_0) {
-    FfnArgs f = {};
-    f.gate_qs = L->w[W_GATE]->qs.as<uint8_t>();
-    f.gate_sc = L->w[W_GATE]->sc.as<uint16_t>();
-    f.up_qs = L->w[W_UP]->qs.as<uint8_t>();
-    f.up_sc = L->w[W_UP]->sc.as<uint16_t>();
-    f.down_qs = L->w[W_DOWN]->qs.as<uint8_t>();
-    f.down_sc = L->w[W_DOWN]->sc.as<uint16_t>();
-    f.gu_sc_stride = L->w[W_GATE]->sc_stride;
-    f.down_sc_stride = L->w[W_DOWN]->sc_stride;
-    f.H = c.hidden;
-    f.F = c.ffn;
-    f.ffn_norm = g_ffn;
-    f.eps = c.eps;
-    f.h = ws->h.as<float>();
-    f.part = ws->ffn_part.as<float>();
-    f.ticket = ws->ffn_ticket.as<unsigned long long>();
-    f.err = ws->ffn_err.as<int>();
-    f.pf = pf_next;
-    const size_t smem = ffn_smem_bytes(c.hidden, c.ffn);
-    FLOCK_TRY(kernel_setup((const void*)k_ffn_fused, (int)smem));
-    FLOCK_CK(launch_ex(d->stream, k_ffn_fused, dim3(FFN_CTAS), dim3(FFN_THREADS), smem, pdl, f));
-    return FLOCK_OK;
   }
   // 5. ffn_norm + gate/up + SwiGLU
   {

@@ -93,7 +93,6 @@ struct Workspace {
                                 // split-K partials
   DBuf kv_img;                  // tensor-core prefill: f16 K / V^T tiles of the cache
   DBuf tp_part, tp_all;         // tensor parallel: this rank's partial [P][H], all ranks
-  DBuf ffn_part, ffn_ticket, ffn_err;  // fused decode FFN: lane partials [64][H], barrier, error
   // tp_ranks >= 1 (a tensor-parallel model, one rank included): also the
   // partial / all-gather buffers; 0 = no tensor parallelism
   int alloc(const flock_layer_config& c, int sm_count, int tp_ranks = 0);
