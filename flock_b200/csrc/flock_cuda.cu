@@ -578,6 +578,7 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.chunk_cap = (c.max_keys + a.splits - 1) / a.splits;
     a.combine = 1;
     pf_add(a.pf, L->w[W_GATE]);
+    pf_add(a.pf, L->w[W_UP]);
     const size_t smem = attn_fast_smem(a.chunk_cap);
     FLOCK_TRY(kernel_setup((const void*)k_attn_decode_fast, 200 * 1024));
     FLOCK_CK(launch_ex(d->stream, k_attn_decode_fast, dim3(c.n_kv_heads, a.splits),
