@@ -88,9 +88,13 @@ static cudaError_t launch_ex(cudaStream_t st, void (*k)(KArgs...), dim3 grid, di
 
 template <int QT, int R, int EPI, int MX, int LA = 1>
 static cudaError_t gemv_go(flock_dev* d, const GemvArgs& a, int ctas, bool pdl) {
-  // rows of one 32-weight block per lane fold on f32x2 pairs
-  auto k = (a.K <= 1024 && LA == 1) ? k_gemv<QT, R, EPI, MX, LA, 2, true>
-                                    : k_gemv<QT, R, EPI, MX, LA>;
+  // blocks fold on f32x2 pairs (x staged in the packed-pair layout): held in
+  // registers for one-block rows, read per step for single-row groups; two
+  // rows with two steps in flight keep the scalar fold (the pairs would spill)
+  auto k = a.K <= 1024 ? (LA == 1 ? k_gemv<QT, R, EPI, MX, LA, 2, 1>
+                                  : k_gemv<QT, R, EPI, MX, LA, 2, 0>)
+                       : (R == 1 ? k_gemv<QT, R, EPI, MX, LA, 2, 2>
+                                 : k_gemv<QT, R, EPI, MX, LA, 2, 0>);
   const size_t smem = gemv_smem_bytes(a.K, a.norm_gain != nullptr);
   if (kernel_setup((const void*)k, 200 * 1024)) return cudaErrorInvalidValue;
   return launch_ex(d->stream, k, dim3(ctas, a.n_tokens), dim3(GEMV_THREADS), smem, pdl, a);

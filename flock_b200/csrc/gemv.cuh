@@ -166,21 +166,6 @@ FLOCK_DEV void stage_x_packed(const float* src, int n, float* xs, int tid, int n
   }
 }
 
-// One padded 32-float block of x (8 float4) as the 16 pairs fold_block_packed
-// multiplies: Q8_0 (x[8g+k], x[8g+4+k]), Q4_0 (x[4g+k], x[16+4g+k]).
-template <int QT>
-FLOCK_DEV void pairs_of(const float4 (&v)[8], uint64_t (&xp)[16]) {
-#pragma unroll
-  for (int g = 0; g < 4; g++) {
-    const float4 lo = QT == QT_Q8 ? v[2 * g] : v[g];
-    const float4 hi = QT == QT_Q8 ? v[2 * g + 1] : v[4 + g];
-    xp[4 * g + 0] = pack2(lo.x, hi.x);
-    xp[4 * g + 1] = pack2(lo.y, hi.y);
-    xp[4 * g + 2] = pack2(lo.z, hi.z);
-    xp[4 * g + 3] = pack2(lo.w, hi.w);
-  }
-}
-
 // Block b of packed x as 16 pairs.
 FLOCK_DEV void load_pairs(const float* xs, int b, uint64_t (&xp)[16]) {
   const ulonglong2* q = reinterpret_cast<const ulonglong2*>(xs + b * XPAD);
@@ -256,7 +241,13 @@ FLOCK_DEV bool am_better(float va, uint32_t ia, float vb, uint32_t ib) {
 // scale = fr(1/sqrt(fr(fr(sum/n) + eps))); y = fr(fr(x*scale)*g).
 // x and the gain are staged into shared memory with ONE round trip of
 // 128-bit loads (all issued before any is consumed); the rest runs on chip.
-// Called by all GEMV_THREADS threads; leaves y in xs (padded layout).
+// Called by all GEMV_THREADS threads; leaves y in xs in layout LAYOUT
+// (xidx: 0 padded, 1 / 2 the Q8_0 / Q4_0 packed-pair layouts).
+template <int LAYOUT>
+FLOCK_DEV int xidx(int i) {
+  return LAYOUT == 0 ? xpad(i) : xperm<LAYOUT - 1>(i);
+}
+template <int LAYOUT = 0>
 FLOCK_DEV void rmsnorm_to_smem(const float* __restrict__ src, const float* __restrict__ gain,
                                int n, float eps, float* xs, float* gs, float* red) {
   const int t = threadIdx.x;
@@ -266,14 +257,21 @@ FLOCK_DEV void rmsnorm_to_smem(const float* __restrict__ src, const float* __res
   for (int i = t; i < n / 4; i += GEMV_THREADS) {
     const float4 v = s4[i];
     const float4 g = g4[i];
-    reinterpret_cast<float4*>(xs)[(i >> 3) * (XPAD / 4) + (i & 7)] = v;
+    if (LAYOUT == 0) {
+      reinterpret_cast<float4*>(xs)[(i >> 3) * (XPAD / 4) + (i & 7)] = v;
+    } else {
+      xs[xidx<LAYOUT>(4 * i)] = v.x;
+      xs[xidx<LAYOUT>(4 * i + 1)] = v.y;
+      xs[xidx<LAYOUT>(4 * i + 2)] = v.z;
+      xs[xidx<LAYOUT>(4 * i + 3)] = v.w;
+    }
     reinterpret_cast<float4*>(gs)[i] = g;
   }
   __syncthreads();
   if (t < 128) {
     float acc = 0.0f;
     for (int i = t; i < n; i += 128) {
-      const float v = xs[xpad(i)];
+      const float v = xs[xidx<LAYOUT>(i)];
       acc = ffma(v, v, acc);
     }
     red[t] = acc;
@@ -288,7 +286,8 @@ FLOCK_DEV void rmsnorm_to_smem(const float* __restrict__ src, const float* __res
   }
   __syncthreads();
   const float scale = red[128];
-  for (int i = t; i < n; i += GEMV_THREADS) xs[xpad(i)] = fmul(fmul(xs[xpad(i)], scale), gs[i]);
+  for (int i = t; i < n; i += GEMV_THREADS)
+    xs[xidx<LAYOUT>(i)] = fmul(fmul(xs[xidx<LAYOUT>(i)], scale), gs[i]);
 }
 
 // The R rows a row group covers.
@@ -342,10 +341,12 @@ FLOCK_DEV void rows_of(const GemvArgs& a, int g, Rows<R>& rs) {
 // then `pre()` runs -- it must leave x (padded layout) in xs and synchronise
 // the block -- then the rows are folded and the epilogue applied.  EPI_ARGMAX
 // leaves this thread's best (value, index) in best_v / best_i.
-// PK (rows of one block per lane, K <= 1024): x lives in registers as f32x2
-// pairs and blocks fold with fold_block_packed -- the same arithmetic in
-// about a quarter fewer instructions.
-template <int QT, int R, int EPI, int MX, int LA, bool PK = false, class Pre>
+// PK != 0: x is staged in the packed-pair layout (pre() must do so:
+// gemv_stage_x with layout 1 + QT) and blocks fold with fold_block_packed --
+// the same arithmetic in about a quarter fewer instructions.  PK 1: rows of
+// one block per lane (K <= 1024), whose pairs stay in registers; PK 2: any
+// row length, the pairs read from shared memory per step.
+template <int QT, int R, int EPI, int MX, int LA, int PK = 0, class Pre>
 FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const float* xs,
                         Pre&& pre, float& best_v, uint32_t& best_i) {
   const int lane = threadIdx.x & 31;
@@ -402,14 +403,15 @@ FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const f
 
   const float4* xs4 = reinterpret_cast<const float4*>(xs);
   float4 xr[PK ? 1 : MX][8];
-  uint64_t xp[PK ? 16 : 1];
-  if (PK) {
-    float4 v[8];
+  uint64_t xp[PK == 1 ? 16 : 1];
+  if (PK == 1) {
+    if (lane < nb) {
+      load_pairs(xs, lane, reinterpret_cast<uint64_t(&)[16]>(xp));
+    } else {
 #pragma unroll
-    for (int j = 0; j < 8; j++)
-      v[j] = lane < nb ? xs4[lane * (XPAD / 4) + j] : make_float4(0.f, 0.f, 0.f, 0.f);
-    pairs_of<QT>(v, reinterpret_cast<uint64_t(&)[16]>(xp));
-  } else {
+      for (int j = 0; j < (PK == 1 ? 16 : 1); j++) xp[j] = 0;
+    }
+  } else if (PK == 0) {
 #pragma unroll
     for (int mm = 0; mm < MX; mm++) {
       const int b = lane + 32 * mm;
@@ -454,11 +456,22 @@ FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const f
             accA[r] = fold_block<QT>(cur[r], xb, accA[r]);
         }
       };
-      if (PK) {  // M == 1: the lane's only block, logical lane `lane`
+      if (PK == 1) {  // the lane's only block (M == 1): pairs held in registers
 #pragma unroll
         for (int r = 0; r < R; r++)
           if (rs.ok[r])
             accA[r] = fold_block_packed<QT>(cur[r], reinterpret_cast<uint64_t(&)[16]>(xp), accA[r]);
+      } else if (PK == 2) {
+        uint64_t xq[16];
+        load_pairs(xs, b, xq);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          if (!rs.ok[r]) continue;
+          if (m & 1)
+            accB[r] = fold_block_packed<QT>(cur[r], xq, accB[r]);
+          else
+            accA[r] = fold_block_packed<QT>(cur[r], xq, accA[r]);
+        }
       } else if (m < MX) {
         fold_all(xr[MX >= 2 && m == 1 ? 1 : 0]);
       } else {
@@ -529,14 +542,18 @@ FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const f
   }
 }
 
-// x for token `tok` into xs (padded layout), RMSNorm-ed when a.norm_gain is
-// set; `from` (if given) replaces a.x + tok * x_stride as the source row.
-// The caller synchronises the block afterwards.
+// x for token `tok` into xs in layout LAYOUT (0 padded, 1 + QT packed
+// pairs), RMSNorm-ed when a.norm_gain is set; `from` (if given) replaces
+// a.x + tok * x_stride as the source row.  The caller synchronises the block
+// afterwards.
+template <int LAYOUT = 0>
 FLOCK_DEV void gemv_stage_x(const GemvArgs& a, int tok, float* xs, float* gs, float* red,
                             const float* from = nullptr) {
   const float* x = from ? from : a.x + (size_t)tok * a.x_stride;
   if (a.norm_gain) {
-    rmsnorm_to_smem(x, a.norm_gain, a.K, a.eps, xs, gs, red);
+    rmsnorm_to_smem<LAYOUT>(x, a.norm_gain, a.K, a.eps, xs, gs, red);
+  } else if (LAYOUT != 0) {
+    stage_x_packed<LAYOUT - 1>(x, a.K, xs, threadIdx.x, GEMV_THREADS);
   } else {
     const float4* src = reinterpret_cast<const float4*>(x);
 #pragma unroll 4
@@ -616,7 +633,7 @@ FLOCK_DEV bool gemv_argmax_finish(const GemvArgs& a, float best_v, uint32_t best
 }
 
 // MINB: resident CTAs per SM the register budget is sized for.
-template <int QT, int R, int EPI, int MX, int LA = 1, int MINB = 2, bool PK = false>
+template <int QT, int R, int EPI, int MX, int LA = 1, int MINB = 2, int PK = 0>
 __global__ void __launch_bounds__(GEMV_THREADS, MINB) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(16) float smem[];
   const bool norm = a.norm_gain != nullptr;
@@ -638,7 +655,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, MINB) k_gemv(const GemvArgs a) {
       a.ctl[0] += a.ctl[1];
       a.ctl[1] = a.ctl_n;
     }
-    gemv_stage_x(a, blockIdx.y, xs, gs, red);
+    gemv_stage_x<PK ? 1 + QT : 0>(a, blockIdx.y, xs, gs, red);
     __syncthreads();
   }, best_v, best_i);
   if (EPI == EPI_ARGMAX) gemv_argmax_finish(a, best_v, best_i, cta_val, cta_idx);
