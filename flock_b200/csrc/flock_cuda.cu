@@ -89,12 +89,12 @@ static cudaError_t launch_ex(cudaStream_t st, void (*k)(KArgs...), dim3 grid, di
 template <int QT, int R, int EPI, int MX, int LA = 1>
 static cudaError_t gemv_go(flock_dev* d, const GemvArgs& a, int ctas, bool pdl) {
   // blocks fold on f32x2 pairs (x staged in the packed-pair layout): held in
-  // registers for one-block rows, read per step for single-row groups; two
-  // rows with two steps in flight keep the scalar fold (the pairs would spill)
+  // registers for one-block rows, read per step otherwise; two rows with two
+  // steps in flight keep the scalar fold (the pairs would spill)
   auto k = a.K <= 1024 ? (LA == 1 ? k_gemv<QT, R, EPI, MX, LA, 2, 1>
                                   : k_gemv<QT, R, EPI, MX, LA, 2, 0>)
-                       : (R == 1 ? k_gemv<QT, R, EPI, MX, LA, 2, 2>
-                                 : k_gemv<QT, R, EPI, MX, LA, 2, 0>);
+                       : ((R == 1 || LA == 1) ? k_gemv<QT, R, EPI, MX, LA, 2, 2>
+                                              : k_gemv<QT, R, EPI, MX, LA, 2, 0>);
   const size_t smem = gemv_smem_bytes(a.K, a.norm_gain != nullptr);
   if (kernel_setup((const void*)k, 200 * 1024)) return cudaErrorInvalidValue;
   return launch_ex(d->stream, k, dim3(ctas, a.n_tokens), dim3(GEMV_THREADS), smem, pdl, a);
@@ -113,13 +113,18 @@ int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl) {
     return FLOCK_E_ARG;
   }
   const int M = (a.K / 32 + 31) / 32;
-  const int MX = M >= 2 ? 2 : 1;
   int rows = 0;
   for (int s = 0; s < a.nseg; s++) rows += a.seg[s].rows;
+  // large matrices with long rows (the 8B shape): two rows per warp step and
+  // one step of lookahead on the f32x2 fold measured fastest (4096 x 12288:
+  // 16.4 us against 20.7 for one row with two steps in flight)
+  const bool big = a.K > 1024 && rows >= 4096;
+  // steps of weights in flight: two for long rows, else one
+  const int MX = (M >= 2 && !big) ? 2 : 1;
   // rows per warp step: 2 where that keeps one wave of <= 2 CTAs per SM busy
   // with about one row group per warp, 1 for the small matrices
   int R = 1;
-  if (EPI == EPI_SWIGLU || EPI == EPI_ARGMAX) R = 2;
+  if (EPI == EPI_SWIGLU || EPI == EPI_ARGMAX || big) R = 2;
   else if (EPI == EPI_STORE && rows > 2 * GEMV_WARPS * d->sm_count) R = 2;
   int groups;
   if (EPI == EPI_SWIGLU) groups = a.seg[0].rows;
@@ -141,7 +146,8 @@ int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl) {
         else { if (MX == 1) GO(QT_Q8, 1, EPI_STORE, 1); else GO(QT_Q8, 1, EPI_STORE, 2); }
         break;
       case EPI_RESIDUAL:
-        if (MX == 1) GO(QT_Q8, 1, EPI_RESIDUAL, 1); else GO(QT_Q8, 1, EPI_RESIDUAL, 2);
+        if (R == 2) { if (MX == 1) GO(QT_Q8, 2, EPI_RESIDUAL, 1); else GO(QT_Q8, 2, EPI_RESIDUAL, 2); }
+        else { if (MX == 1) GO(QT_Q8, 1, EPI_RESIDUAL, 1); else GO(QT_Q8, 1, EPI_RESIDUAL, 2); }
         break;
       case EPI_SWIGLU:
         if (MX == 1) GO(QT_Q8, 2, EPI_SWIGLU, 1); else GO(QT_Q8, 2, EPI_SWIGLU, 2);
