@@ -13,7 +13,9 @@ EPS = 9.999999974752427e-7
 VOCAB = 151936
 # kernels/test_coop.ts:113-121 shapes, plus the model's other projections
 SHAPES = [(64, 32), (30, 1024), (128, 1024), (1024, 1024), (2048, 1024), (3072, 1024),
-          (1024, 3072), (1024, 2048), (37, 96), (5, 4096)]
+          (1024, 3072), (1024, 2048), (37, 96), (5, 4096),
+          # the 8B shape's large-matrix path (two rows per step, packed fold)
+          (4096, 4096), (4097, 2048), (4096, 12288)]
 
 
 @pytest.fixture(scope="module")
