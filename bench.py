@@ -166,7 +166,17 @@ def cpu_baseline(m, shape, n_tokens: int = 2) -> dict:
             h = L.forward(h, 1)
         tok, _, _ = oracle.head(h, m.output_norm, m.embd["packed"], shape.vocab, shape.hidden)
     dt = time.perf_counter() - t0
+    # the reference's JS engine runs one thread: the same path on one core
+    oracle.set_threads(1)
+    t1 = time.perf_counter()
+    h = oracle.embed(m.embd["packed"], [tok], shape.hidden)
+    for L in layers:
+        h = L.forward(h, 1)
+    oracle.head(h, m.output_norm, m.embd["packed"], shape.vocab, shape.hidden)
+    single = 1.0 / (time.perf_counter() - t1)
+    oracle.set_threads(cores)
     return {"value": n_tokens / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "single_thread_value": single,
             "sample": f"{n_tokens} decode tokens of the 28-layer model at position {PROMPT} "
                       f"(oracle/flock_oracle.c, OpenMP over rows, {cores} threads)"}
 

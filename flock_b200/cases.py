@@ -48,11 +48,18 @@ def layer_case(timed: bool, attention: str = "fast") -> None:
         L.encode(x if i == 0 else None)
     dev.sync()
     if timed:
+        # config 0: one layer's decode step from position 261 on, 1000 steps
+        # (the cache grows to 1260 keys); bytes = weights + the K/V rows read
+        n = 1000
         dev.timer_start()
-        for _ in range(50):
+        for _ in range(n):
             L.encode(None)
         ms = dev.timer_stop()
-        print(f"layer decode ({attention}): {ms / 50 * 1000:.2f} us/step")
+        keys = 261 + (n - 1) / 2.0 + 1
+        b = 15728640 * 1.0625 + 2 * keys * 1024 * 4
+        us = ms / n * 1000
+        print(f"layer decode ({attention}): {us:.2f} us/step, {b / us / 1e3:.1f} GB/s "
+              f"({b / 1e6:.2f} MB/step at {keys:.0f} keys on average)")
 
 
 def head_case(timed: bool) -> None:
