@@ -249,10 +249,9 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
     FLOCK_TRY(part.alloc((size_t)8 * P * H * f));
     FLOCK_TRY(kv_img.alloc(kv_image_bytes(c.max_keys, nKV)));
   }
-  if (tp_ranks >= 1) {
+  if (tp_ranks >= 1 || H >= 4096)  // also the large shape's split residual
     FLOCK_TRY(tp_part.alloc((size_t)P * H * f));
-    FLOCK_TRY(tp_all.alloc((size_t)tp_ranks * P * H * f));
-  }
+  if (tp_ranks >= 1) FLOCK_TRY(tp_all.alloc((size_t)tp_ranks * P * H * f));
   return FLOCK_OK;
 }
 
@@ -438,6 +437,20 @@ static int tp_sum_into_h(flock_layer* L, int n) {
   return FLOCK_OK;
 }
 
+// Large decode shapes (hidden >= 4096): o_proj / down store their result and
+// a separate kernel adds it to h -- the residual epilogue's fadd(h, y) --
+// which measured faster than the in-epilogue residual at these sizes.
+static bool split_residual(const flock_layer* L, int n) {
+  return !L->tp && n == 1 && L->cfg.hidden >= 4096 && L->ws->tp_part.p;
+}
+static int add_split_residual(flock_layer* L, int n) {
+  const int64_t count = (int64_t)n * L->cfg.hidden;
+  k_tp_reduce_residual<<<(unsigned)((count + 255) / 256), 256, 0, L->dev->stream>>>(
+      L->ws->h.as<float>(), L->ws->tp_part.as<float>(), 1, count);
+  FLOCK_CK(cudaGetLastError());
+  return FLOCK_OK;
+}
+
 // One prefill step of n > 1 tokens with the four weight matmuls on the
 // tcgen05 tensor cores (FLOCK_PREFILL_TENSOR); norms, RoPE, attention and the
 // residual adds keep their f32 arithmetic.
@@ -600,7 +613,9 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
   // across ranks, then added)
   {
     GemvArgs a = {};
-    a.seg[0] = seg_of(L->w[W_O], L->tp ? ws->tp_part.as<float>() : ws->h.as<float>(), c.hidden);
+    const bool split = split_residual(L, n);
+    a.seg[0] = seg_of(L->w[W_O], (L->tp || split) ? ws->tp_part.as<float>() : ws->h.as<float>(),
+                      c.hidden);
     a.nseg = 1;
     a.K = qw;
     a.n_tokens = n;
@@ -609,8 +624,9 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.res = ws->h.as<float>();
     a.res_stride = c.hidden;
     pf_add(a.pf, L->w[W_DOWN]);
-    FLOCK_TRY(launch_gemv(d, QT_Q8, L->tp ? EPI_STORE : EPI_RESIDUAL, a, pdl));
+    FLOCK_TRY(launch_gemv(d, QT_Q8, (L->tp || split) ? EPI_STORE : EPI_RESIDUAL, a, pdl));
     if (L->tp) FLOCK_TRY(tp_sum_into_h(L, n));
+    if (split) FLOCK_TRY(add_split_residual(L, n));
   }
   // 5. ffn_norm + gate/up + SwiGLU
   {
@@ -630,7 +646,8 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
   // 6. down + residual, in place on h (tensor parallel as o_proj)
   {
     GemvArgs a = {};
-    a.seg[0] = seg_of(L->w[W_DOWN], L->tp ? ws->tp_part.as<float>() : ws->h.as<float>(),
+    const bool split = split_residual(L, n);
+    a.seg[0] = seg_of(L->w[W_DOWN], (L->tp || split) ? ws->tp_part.as<float>() : ws->h.as<float>(),
                       c.hidden);
     a.nseg = 1;
     a.K = c.ffn;
@@ -639,8 +656,9 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.x_stride = c.ffn;
     a.res = ws->h.as<float>();
     a.res_stride = c.hidden;
-    FLOCK_TRY(launch_gemv(d, QT_Q8, L->tp ? EPI_STORE : EPI_RESIDUAL, a, pdl));
+    FLOCK_TRY(launch_gemv(d, QT_Q8, (L->tp || split) ? EPI_STORE : EPI_RESIDUAL, a, pdl));
     if (L->tp) FLOCK_TRY(tp_sum_into_h(L, n));
+    if (split) FLOCK_TRY(add_split_residual(L, n));
   }
   return FLOCK_OK;
 }
