@@ -10,6 +10,11 @@
 #include <map>
 #include <vector>
 
+// decode o_proj / down: store + separate residual add from this hidden size up
+#ifndef FLOCK_SPLIT_RESIDUAL_MIN_HIDDEN
+#define FLOCK_SPLIT_RESIDUAL_MIN_HIDDEN 4096
+#endif
+
 #include "attn_fast.cuh"
 #include "attn_tc.cuh"
 #include "gemm_tc.cuh"
@@ -249,7 +254,7 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
     FLOCK_TRY(part.alloc((size_t)8 * P * H * f));
     FLOCK_TRY(kv_img.alloc(kv_image_bytes(c.max_keys, nKV)));
   }
-  if (tp_ranks >= 1 || H >= 4096)  // also the large shape's split residual
+  if (tp_ranks >= 1 || H >= FLOCK_SPLIT_RESIDUAL_MIN_HIDDEN)  // also the split residual
     FLOCK_TRY(tp_part.alloc((size_t)P * H * f));
   if (tp_ranks >= 1) FLOCK_TRY(tp_all.alloc((size_t)tp_ranks * P * H * f));
   return FLOCK_OK;
@@ -441,7 +446,7 @@ static int tp_sum_into_h(flock_layer* L, int n) {
 // a separate kernel adds it to h -- the residual epilogue's fadd(h, y) --
 // which measured faster than the in-epilogue residual at these sizes.
 static bool split_residual(const flock_layer* L, int n) {
-  return !L->tp && n == 1 && L->cfg.hidden >= 4096 && L->ws->tp_part.p;
+  return !L->tp && n == 1 && L->cfg.hidden >= FLOCK_SPLIT_RESIDUAL_MIN_HIDDEN && L->ws->tp_part.p;
 }
 static int add_split_residual(flock_layer* L, int n) {
   const int64_t count = (int64_t)n * L->cfg.hidden;
