@@ -104,6 +104,10 @@ SIGNATURES = {
     "flock_model_create_tp": [_vp, _cfgp, _i, _i, _pp, _vp, _vp, _vp, _vp, _pp],
     "flock_model_set_tp_exchange": [_vp, _i],
     "flock_model_get_tp_exchange": [_vp, _ip],
+    "flock_wire_pack": [_fp, _i64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                        ctypes.c_uint32, _u8p, _i64, _i64p],
+    "flock_wire_unpack": [_u8p, _i64, _fp, _i64, ctypes.POINTER(ctypes.c_uint32)],
+    "flock_range_forward_wire": [_pp, _i, _u8p, _i64, _u8p, _i64, _i64p],
     "flock_gguf_open": [ctypes.c_char_p, _pp],
     "flock_gguf_free": [_vp],
     "flock_gguf_info": [_vp, _i64p, _i64p, _ip, _ip],

@@ -93,6 +93,7 @@ struct Workspace {
                                 // split-K partials
   DBuf kv_img;                  // tensor-core prefill: f16 K / V^T tiles of the cache
   DBuf tp_part, tp_all;         // tensor parallel: this rank's partial [P][H], all ranks
+  DBuf wire;                    // FLK1 frames: the f16 payload on the device
   // tp_ranks >= 1 (a tensor-parallel model, one rank included): also the
   // partial / all-gather buffers; 0 = no tensor parallelism
   int alloc(const flock_layer_config& c, int sm_count, int tp_ranks = 0);

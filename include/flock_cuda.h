@@ -319,6 +319,28 @@ FLOCK_API int flock_model_set_token(flock_model* m, int32_t id);
 /* kernels/model.ts:541 currentToken(). */
 FLOCK_API int flock_model_current_token(flock_model* m, int32_t* out);
 
+/* ------------------------------------------------------------ FLK1 frames */
+
+/* web/js/wire.mjs FLK1 frames: "FLK1" | seq | hidden | offset | flags (u32 LE,
+ * flags bit 0 reset, bit 1 replay) | f16 payload.  pack (wire.mjs:54) rounds
+ * f32 to f16 to nearest even (subnormals, overflow to inf, NaN -> 0x7e00 |
+ * sign) and needs 20 + 2n bytes (*out_len, FLOCK_E_LIMIT if cap is short);
+ * unpack (wire.mjs:79) widens exactly (NaN canonical) and fills meta = {seq,
+ * hidden, offset, reset, replay}; out == NULL reads the header only. */
+FLOCK_API int flock_wire_pack(const float* x, int64_t n, uint32_t seq, uint32_t hidden,
+                              uint32_t offset, uint32_t flags, uint8_t* out, int64_t cap,
+                              int64_t* out_len);
+FLOCK_API int flock_wire_unpack(const uint8_t* frame, int64_t len, float* out, int64_t cap,
+                                uint32_t meta[5]);
+/* web/bird.html:544 runFrame for a held layer range: the frame's f16 payload is
+ * widened on the device, a reset flag clears the caches first, the offset must
+ * equal the caches' position ("cache holds X positions, frame is at Y"), the
+ * layers run in order and the output frame (same header) carries the last
+ * layer's output rounded to f16 as pack() would. */
+FLOCK_API int flock_range_forward_wire(flock_layer* const* layers, int n_layers,
+                                       const uint8_t* frame, int64_t frame_len, uint8_t* out,
+                                       int64_t out_cap, int64_t* out_len);
+
 /* ----------------------------------------------------------------- GGUF */
 
 /* A GGUF model file opened on the host (web/js/gguf-dir.mjs:187
