@@ -7,10 +7,11 @@
 // attn_fast_item, gemv_argmax_finish), so logits and ids are bit-identical
 // to the multi-kernel path.  Laid out for batch-1 latency on B200:
 //
-//  * grid = up to 2 CTAs per SM (all co-resident: cooperative launch) of
-//    8 warps; in a GEMV phase every warp walks row groups across the grid
-//    exactly as in a k_gemv launch of the same grid, reading weights straight
-//    from global memory with its register lookahead;
+//  * grid = one CTA of 8 warps per SM (all co-resident: cooperative launch;
+//    each phase function is compiled on its own, with up to 255 registers,
+//    so no loop spills); in a GEMV phase every warp walks row groups across
+//    the grid exactly as in a k_gemv launch of the same grid, reading weights
+//    straight from global memory with its register lookahead;
 //  * weights and KV rows do not depend on activations, so at the start of
 //    each layer the grid issues L2 bulk prefetches of the NEXT layer's
 //    weight and scale planes and KV rows (one 32 KiB piece per CTA at a

@@ -517,15 +517,9 @@ int flock_gguf_split_host(const flock_gguf* g, const char* name, int64_t chunk, 
   s.flush = HostSink::flush;
   s.ctx = &h;
   // host sink: blocks land in the caller's planes directly; the window moves per flush
-  const int64_t nbytes = t->bytes;
   std::vector<uint8_t> buf;
-  int64_t written = 0;
-  FLOCK_TRY(read_range(g->fd, g->data_start + t->offset, nbytes, chunk, buf,
-                       [&](const uint8_t* p, int64_t n) {
-                         written += n;
-                         return s.push(p, n);
-                       }));
-  (void)written;
+  FLOCK_TRY(read_range(g->fd, g->data_start + t->offset, t->bytes, chunk, buf,
+                       [&](const uint8_t* p, int64_t n) { return s.push(p, n); }));
   return s.end();
 }
 

@@ -168,9 +168,12 @@ int peer_xchg_init(flock_comm* c, int64_t cap, PeerXchg** out) {
     x->comm = nullptr;  // no collective on this path: the peers may not have got here
     return fail(FLOCK_E_NOMEM);
   }
-  FLOCK_CK(cudaMemset(x->flag, 0, (size_t)2 * n * 16 * 4));
-  FLOCK_CK(cudaMemset(x->epoch, 0, 16 * 4));
-  FLOCK_CK(cudaMemset(x->err, 0, 16));
+  if (cudaMemset(x->flag, 0, (size_t)2 * n * 16 * 4) != cudaSuccess ||
+      cudaMemset(x->epoch, 0, 16 * 4) != cudaSuccess || cudaMemset(x->err, 0, 16) != cudaSuccess) {
+    set_error("peer exchange: cudaMemset failed");
+    x->comm = nullptr;
+    return fail(FLOCK_E_CUDA);
+  }
   std::vector<float*> bufs(n, nullptr);
   std::vector<uint32_t*> flags(n, nullptr);
   bufs[rank] = x->buf;
@@ -220,9 +223,13 @@ int peer_xchg_init(flock_comm* c, int64_t cap, PeerXchg** out) {
       return fail(rc ? rc : FLOCK_E_UNSUPPORTED);
     }
   }
-  FLOCK_CK(cudaMemcpy(x->d_bufs, bufs.data(), (size_t)n * sizeof(float*), cudaMemcpyHostToDevice));
-  FLOCK_CK(cudaMemcpy(x->d_flags, flags.data(), (size_t)n * sizeof(uint32_t*),
-                      cudaMemcpyHostToDevice));
+  if (cudaMemcpy(x->d_bufs, bufs.data(), (size_t)n * sizeof(float*), cudaMemcpyHostToDevice) !=
+          cudaSuccess ||
+      cudaMemcpy(x->d_flags, flags.data(), (size_t)n * sizeof(uint32_t*),
+                 cudaMemcpyHostToDevice) != cudaSuccess) {
+    set_error("peer exchange: pointer table upload failed");
+    return fail(FLOCK_E_CUDA);  // every rank got here: the free's barrier is collective
+  }
   *out = x;
   return FLOCK_OK;
 }
