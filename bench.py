@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Decode throughput of the Qwen3-0.6B-shaped Q8_0 model on B200.
 
-Workload: the full 28-layer model with a tied
+Workload (benchmark config 2): the full 28-layer model with a tied
 151936 x 1024 Q8_0 embedding/head and seeded synthetic Q8_0 weights, a
 64-token prompt (ids uniform in [0, 151936)), then greedy batch-1 decode.  A
 step is one decode token (embedding -> 28 layers -> output_norm -> head ->
@@ -394,7 +394,7 @@ def main():
 
 
 def prefill_ttft(dev, m, shape, pk, n_prompt: int = 512) -> dict:
-    """time to first token of a 512-token prompt on the same
+    """benchmark config 3: time to first token of a 512-token prompt on the same
     28-layer model through the tensor-core prefill (tcgen05 f16 GEMMs and
     attention), device-timed; the weight GEMMs' FLOPs over the TTFT give a
     lower bound on tensor-pipe use."""

@@ -3,7 +3,7 @@ Model.create({cut}) + the bird layer ranges of web/bird.html:544-620 and
 server/gguf.mjs:102 splitLayers), with the hidden state passed between
 stages by NCCL send/recv (flock_pipeline_step) instead of the WebRTC hop.
 
-stage_ranges() is the partition BASELINE config 2 names: the first stage
+stage_ranges() is the partition benchmark config 2 names: the first stage
 (which also holds the embedding, output norm and head, as the reference's
 coordinator does) takes `first` layers, the rest are split evenly with the
 remainder going to the earlier stages.

@@ -1,5 +1,5 @@
 """One Qwen3 layer on the GPU vs layer_ref.ts (kernels/test_layer.ts,
-test_prefill.ts, test_frombuffers.ts), including BASELINE config 0: decode at
+test_prefill.ts, test_frombuffers.ts), including benchmark config 0: decode at
 position 256 over a 256-key N(0,1) cache."""
 import numpy as np
 import pytest

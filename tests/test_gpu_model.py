@@ -136,7 +136,7 @@ def test_objects_outlive_device_close(small):
 
 
 def test_full_06b_model_greedy_ids(dev, oracle):
-    """BASELINE config 2 shape (28 layers, vocab 151936, tied head), short run."""
+    """benchmark config 2 shape (28 layers, vocab 151936, tied head), short run."""
     m = synth.model(300)
     M = Model.create(dev, m, QWEN3_06B)
     ref = OracleModel(oracle, m, ieee=False)
