@@ -2,11 +2,11 @@
 flock_b200.tensor_parallel against the oracle's shardRanges /
 shardedColMatvecRef, and the whole per-token protocol of
 flock_model_create_tp -- every rank runs its slice of a layer, the o_proj and
-down partials are all-gathered (gloo, world size 2, 127.0.0.1) and summed in
-rank order, the head's (value, index) maxima are reduced by
-reduceShardArgmax -- with the oracle as the compute.  The rank-0 hidden
-states must equal the oracle's tensor-parallel layer (RefLayer(tp=2)) bit for
-bit, and the ids the whole model's."""
+down partials are all-gathered (gloo, world size 2 and 4, 127.0.0.1) and
+summed in rank order, the head's (value, index) maxima are reduced by
+reduceShardArgmax -- with the oracle as the compute.  Every rank's hidden
+states must equal the oracle's tensor-parallel layer (RefLayer(tp=N)) bit
+for bit, and the ids the whole model's."""
 import multiprocessing as mp
 import socket
 
@@ -52,6 +52,35 @@ def test_local_config_shapes():
     assert head_ranges(QWEN3_06B, 4) == [(0, 2), (2, 2), (4, 2), (6, 2)]
     with pytest.raises(ValueError):
         local_config(QWEN3_06B, 3)  # 8 KV heads over 3 ranks
+
+
+def test_8b_shape_slices():
+    """Config 4b's shape over 2 / 4 / 8 ranks: whole KV heads with their GQA
+    groups, ffn cut in 32-aligned pieces, and the slices reassemble the layer."""
+    s8 = synth.QWEN3_8B
+    cfg = QWEN3_06B.with_(hidden=s8.hidden, n_heads=s8.n_heads, n_kv_heads=s8.n_kv_heads,
+                          ffn=s8.ffn)
+    for world in (2, 4, 8):
+        cs = local_config(cfg, world)
+        assert all(c.n_heads == 4 * c.n_kv_heads for c in cs)
+        assert sum(c.n_kv_heads for c in cs) == 8 and sum(c.ffn for c in cs) == 12288
+        assert all(c.ffn % 32 == 0 for c in cs)
+    # reassembly on a small layer of the same head structure
+    small = QWEN3_06B.with_(hidden=256, n_heads=8, n_kv_heads=2, head_dim=128, ffn=512)
+    w = {}
+    for name, (rows, cols) in {"attn_q.weight": (1024, 256), "attn_k.weight": (256, 256),
+                               "attn_v.weight": (256, 256), "attn_output.weight": (256, 1024),
+                               "ffn_gate.weight": (512, 256), "ffn_up.weight": (512, 256),
+                               "ffn_down.weight": (256, 512)}.items():
+        w[name] = {"rows": rows, "cols": cols, "packed": synth.q8_tensor(5, name, rows, cols)}
+    parts = [slice_layer(w, small, r, 2) for r in range(2)]
+    for name in ("attn_q.weight", "attn_k.weight", "attn_v.weight", "ffn_gate.weight",
+                 "ffn_up.weight"):
+        assert np.array_equal(np.concatenate([p[name]["packed"] for p in parts]), w[name]["packed"])
+    for name in ("attn_output.weight", "ffn_down.weight"):
+        rows = w[name]["rows"]
+        glued = np.concatenate([p[name]["packed"].reshape(rows, -1) for p in parts], axis=1)
+        assert np.array_equal(glued.reshape(-1), w[name]["packed"])
 
 
 def test_col_slices_sum_to_sharded_matvec(oracle):
@@ -197,10 +226,11 @@ def _run(target, world):
     return res
 
 
-def test_tp_protocol_two_ranks(oracle):
-    res = _run(_tp_worker, 2)
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_protocol(oracle, world):
+    res = _run(_tp_worker, world)
     m = synth.model(200, n_layers=2, vocab=4096)
-    layers = [oracle.RefLayer(w, CFG, 16, tp=2) for w in m.layers]
+    layers = [oracle.RefLayer(w, CFG, 16, tp=world) for w in m.layers]
     ids, want, want_h = list(PROMPT), [], []
     for _ in range(1 + N_DECODE):
         n = len(ids)
@@ -211,7 +241,7 @@ def test_tp_protocol_two_ranks(oracle):
         tok, _, _ = oracle.head(h[(n - 1) * 1024:], m.output_norm, m.embd["packed"], m.vocab, 1024)
         want.append(int(tok))
         ids = [int(tok)]
-    for r in (0, 1):
+    for r in range(world):
         got, hidden = res[r]
         assert got == want
         for a, b in zip(hidden, want_h):
