@@ -131,14 +131,15 @@ def traffic_from_profile(name: str = "gemv_lm_head_traffic.txt") -> float | None
 
 
 # ----------------------------------------------------------------- bytes
-def bytes_per_token(shape, keys: float) -> float:
+def bytes_per_token(shape, keys: float, kv_elem: int = 4) -> float:
     """Algorithmic HBM bytes of one decode token: every Q8_0 weight byte
-    (1.0625 B/weight), the f32 K/V rows read, plus the token's small vectors."""
+    (1.0625 B/weight) and the K/V rows read (kv_elem bytes per element: 4 for
+    the f32 cache, 2 for bf16)."""
     h, f, q, kv = shape.hidden, shape.ffn, shape.n_heads * shape.head_dim, \
         shape.n_kv_heads * shape.head_dim
     layer_w = (q * h + 2 * kv * h + h * q + 2 * f * h + h * f) * 1.0625
     head_w = shape.vocab * h * 1.0625
-    kv_bytes = 2 * kv * 4 * keys
+    kv_bytes = 2 * kv * kv_elem * keys
     return shape.n_layers * (layer_w + kv_bytes) + head_w
 
 
@@ -262,7 +263,11 @@ def main():
                     help="pipeline stages from the makespan allocator fed by each GPU's measured "
                          "bytes/ms (rank 0 charged for its head), instead of config 2's 4 + even")
     ap.add_argument("--prompt", type=int, default=None,
-                    help="prompt tokens before the timed decode (default 64; 4096 for 8b)")
+                    help="prompt tokens before the timed decode (default 64; 4096 for 8b); "
+                         "longer prompts prefill on the tensor cores")
+    ap.add_argument("--kv", default="f32", choices=["f32", "bf16"],
+                    help="KV cache element type (bf16: half the KV bytes per token; the "
+                         "tensor-core prefill and split-K decode attention)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -292,12 +297,15 @@ def main():
     t_gen = time.perf_counter()
     m = synth.model(SEED, shape, lazy=args.shape == "8b")
     log(f"[rank {rank}] synthetic model generated in {time.perf_counter() - t_gen:.1f}s")
-    max_keys = PROMPT + args.warmup + args.steps + 8
+    n_prompt = args.prompt if args.prompt is not None else PROMPT
+    max_keys = n_prompt + args.warmup + args.steps + 8
     cfg = QWEN3_06B.with_(max_keys=max(max_keys, 512), attention=args.attention)
+    if args.kv == "bf16" or n_prompt > 512:
+        cfg = cfg.with_(prefill="tensor", kv=args.kv)
     if args.shape == "8b":
         cfg = cfg.with_(hidden=shape.hidden, n_heads=shape.n_heads, n_kv_heads=shape.n_kv_heads,
                         ffn=shape.ffn)
-    prompt = synth.uniform_ids(SEED, "prompt", PROMPT, shape.vocab)
+    prompt = synth.uniform_ids(SEED, "prompt", n_prompt, shape.vocab)
 
     if world > 1:
         run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk)
@@ -308,7 +316,7 @@ def main():
     decode = M.decode_mode                # "kernels" when the shape rules the persistent kernel out
     first = M.step(prompt)                # prefill (untimed)
     M.decode_device(args.warmup)          # warm-up steps
-    M.rewind(PROMPT)
+    M.rewind(n_prompt)
     M.set_token(first)
     dev.sync()
 
@@ -324,7 +332,7 @@ def main():
     # end to end through the public API, host loop
     e2e = None
     if not args.no_e2e:
-        M.rewind(PROMPT)
+        M.rewind(n_prompt)
         prev = first
         ids_api = []
         dev.timer_start()
@@ -343,8 +351,9 @@ def main():
     head_ms = ops.matvec_timed(dev, embd_t, 1, 50)
     head_bytes = shape.vocab * shape.hidden * 1.0625 + 4 * shape.hidden + 4 * shape.vocab
     head_gbs = head_bytes / (head_ms / 1000.0) / 1e9
-    avg_keys = PROMPT + (args.steps - 1) / 2.0 + 1
-    tok_bytes = bytes_per_token(shape, avg_keys)
+    avg_keys = n_prompt + (args.steps - 1) / 2.0 + 1
+    kv_elem = 2 if args.kv == "bf16" else 4
+    tok_bytes = bytes_per_token(shape, avg_keys, kv_elem)
     token_gbs = tok_bytes * tok_s / 1e9
     if decode == "persistent":
         # one k_decode_mk launch per token: its algorithmic bytes are the token's
@@ -366,10 +375,14 @@ def main():
         "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config 2: Qwen3-0.6B-shape Q8_0, 28 layers, tied 151936x1024 "
-                               "head, prompt 64 then greedy bs1 decode at positions 64..",
-                   "seed": SEED, "prompt": PROMPT, "attention": args.attention,
-                   "decode": decode,
+        "config": {"workload": ("config 2: Qwen3-0.6B-shape Q8_0, 28 layers, tied 151936x1024 "
+                                "head, prompt 64 then greedy bs1 decode at positions 64.."
+                                if n_prompt == PROMPT and args.kv == "f32" else
+                                f"long-context decode: Qwen3-0.6B-shape Q8_0, 28 layers, tied "
+                                f"head, {args.kv} KV cache, prompt {n_prompt} then greedy bs1 "
+                                f"decode at positions {n_prompt}.."),
+                   "seed": SEED, "prompt": n_prompt, "attention": args.attention,
+                   "kv": args.kv, "decode": decode,
                    "l2": "inputs larger than L2: 692 MB of weights streamed per token",
                    "timing": "CUDA events around K device-fed decode steps"},
         "roofline": roofline,
@@ -464,7 +477,7 @@ def run_tensor(args, rank, world, local, dev, shape, pk):
     cfg = LayerConfig(hidden=shape.hidden, n_heads=shape.n_heads, n_kv_heads=shape.n_kv_heads,
                       head_dim=shape.head_dim, ffn=shape.ffn,
                       max_keys=n_prompt + args.warmup + args.steps + 8, max_prefill=512,
-                      attention=args.attention, prefill="tensor")
+                      attention=args.attention, prefill="tensor", kv=args.kv)
     t0 = time.perf_counter()
     m = synth.model(SEED, shape, lazy=True)
     M = Model.create_tp(dev, m, cfg, comm, rank, world)
@@ -505,7 +518,7 @@ def run_tensor(args, rank, world, local, dev, shape, pk):
     if rank == 0:
         tok_s = args.steps / (ms / 1000.0)
         avg_keys = n_prompt + (args.steps - 1) / 2.0 + 1
-        tok_bytes = bytes_per_token(shape, avg_keys)
+        tok_bytes = bytes_per_token(shape, avg_keys, 2 if args.kv == "bf16" else 4)
         per_gpu = tok_bytes / world * tok_s / 1e9
         out = {
             "metric": METRIC.replace("0.6B", "8B") if args.shape == "8b" else METRIC,
@@ -518,7 +531,7 @@ def run_tensor(args, rank, world, local, dev, shape, pk):
                                    "columns with an NCCL all-gather + rank-order sum, head by "
                                    "vocab rows with a (value, index) all-gather",
                        "seed": SEED, "prompt": n_prompt, "attention": args.attention,
-                       "parallelism": f"tp{world}",
+                       "kv": args.kv, "parallelism": f"tp{world}",
                        "tp_exchange": M.tp_exchange,
                        "collectives_per_token": 2 * shape.n_layers + 1,
                        "l2": "inputs larger than L2: weights streamed per token",

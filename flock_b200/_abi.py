@@ -27,6 +27,7 @@ FLOCK_ROPE_NEOX, FLOCK_ROPE_NORM = 0, 1
 FLOCK_ATTN_EXACT, FLOCK_ATTN_FAST = 0, 1
 FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT, FLOCK_DECODE_EAGER = 0, 1, 2
 FLOCK_PREFILL_EXACT, FLOCK_PREFILL_TENSOR = 0, 1
+FLOCK_KV_F32, FLOCK_KV_BF16 = 0, 1
 FLOCK_TP_NCCL, FLOCK_TP_PEER = 0, 1
 
 
@@ -44,7 +45,7 @@ class LayerConfigC(ctypes.Structure):
                 ("ffn", ctypes.c_int32), ("eps", ctypes.c_float), ("rope_base", ctypes.c_double),
                 ("max_keys", ctypes.c_int32), ("max_prefill", ctypes.c_int32),
                 ("rope_pairing", ctypes.c_int32), ("attention", ctypes.c_int32),
-                ("prefill", ctypes.c_int32)]
+                ("prefill", ctypes.c_int32), ("kv_dtype", ctypes.c_int32)]
 
 
 _vp = ctypes.c_void_p

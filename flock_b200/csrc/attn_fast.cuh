@@ -41,8 +41,8 @@ struct AttnFastArgs {
   const float* q_norm;
   const float* k_norm;
   const float* inv_freq;
-  float* kcache;
-  float* vcache;
+  void* kcache;    // [maxKeys][nKV][hd], f32 or (kv_bf16) bf16
+  void* vcache;
   const int* ctl;  // ctl[0] = pos of this token
   float* out;      // [nH][hd]
   float* part;     // [nH][splits][hd + 2]
@@ -52,6 +52,7 @@ struct AttnFastArgs {
   int neox;
   int chunk_cap;   // max keys per split (informational; tiles of 64 are staged)
   int combine;     // 1: the last split of a group combines into out; 0: leave partials
+  int kv_bf16;     // 1: the cache holds bf16 (widened into the f32 tiles as staged)
   PrefetchList pf;
 };
 
@@ -114,11 +115,26 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   // ---- one round trip: the token's raw q/k/v, gains, and the first K/V tile
   auto stage_tile = [&](int t0, int nt) {
     // keys [t0, t0 + nt) of kv head g; position pos is filled from knew/vnew
+    if (a.kv_bf16) {
+      // 16 x 128-bit loads per 256-byte bf16 row, widened to f32 in the tiles
+      for (int i = t; i < nt * 16; i += ATTN_FAST_THREADS) {
+        const int j = i >> 4, c8 = i & 15, key = t0 + j;
+        if (key == pos) continue;
+        const size_t off = (size_t)key * kvs + (size_t)g * hd;
+        const uint4 kw = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.kcache) + off)[c8];
+        const uint4 vw = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.vcache) + off)[c8];
+        bf16x8_widen(kw, dsm + AF_KT + j * AF_KSTRIDE + 8 * c8);
+        bf16x8_widen(vw, dsm + AF_VT + j * 128 + 8 * c8);
+      }
+      return;
+    }
     for (int i = t; i < nt * 32; i += ATTN_FAST_THREADS) {
       const int j = i >> 5, c4 = i & 31, key = t0 + j;
       if (key == pos) continue;
-      const float4* kr = reinterpret_cast<const float4*>(a.kcache + key * kvs + (size_t)g * hd);
-      const float4* vr = reinterpret_cast<const float4*>(a.vcache + key * kvs + (size_t)g * hd);
+      const float4* kr = reinterpret_cast<const float4*>(static_cast<const float*>(a.kcache) +
+                                                         key * kvs + (size_t)g * hd);
+      const float4* vr = reinterpret_cast<const float4*>(static_cast<const float*>(a.vcache) +
+                                                         key * kvs + (size_t)g * hd);
       reinterpret_cast<float4*>(dsm + AF_KT)[j * (AF_KSTRIDE / 4) + c4] = kr[c4];
       reinterpret_cast<float4*>(dsm + AF_VT)[i] = vr[c4];
     }
@@ -138,11 +154,20 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
         if (t < 16)
           reinterpret_cast<float4*>(dsm + AF_INV)[t] =
               reinterpret_cast<const float4*>(a.inv_freq)[t];
+      } else if (a.kv_bf16) {
+        const size_t off = (size_t)pos * kvs + (size_t)g * hd;
+        if (t < 16) {
+          bf16x8_widen(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.kcache) + off)[t],
+                       dsm + AF_KNEW + 8 * t);
+          bf16x8_widen(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.vcache) + off)[t],
+                       dsm + AF_VNEW + 8 * t);
+        }
       } else {
+        const size_t off = (size_t)pos * kvs + (size_t)g * hd;
         reinterpret_cast<float4*>(dsm + AF_KNEW)[t] =
-            reinterpret_cast<const float4*>(a.kcache + (size_t)pos * kvs + (size_t)g * hd)[t];
+            reinterpret_cast<const float4*>(static_cast<const float*>(a.kcache) + off)[t];
         reinterpret_cast<float4*>(dsm + AF_VNEW)[t] =
-            reinterpret_cast<const float4*>(a.vcache + (size_t)pos * kvs + (size_t)g * hd)[t];
+            reinterpret_cast<const float4*>(static_cast<const float*>(a.vcache) + off)[t];
       }
     }
     stage_tile(k0, min(nk, ATTN_TILE));
@@ -163,9 +188,23 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
     else if (warp == G + 1)
       for (int i = lane; i < 128; i += 32) vnew[i] = dsm[AF_VRAW + i];
     sync();
-    if (s == 0 && t < 128) {
-      a.kcache[(size_t)pos * kvs + (size_t)g * hd + t] = knew[t];
-      a.vcache[(size_t)pos * kvs + (size_t)g * hd + t] = vnew[t];
+    const size_t off = (size_t)pos * kvs + (size_t)g * hd + t;
+    if (a.kv_bf16) {
+      // every split rounds its own copy of the new key/value, so the scores
+      // see the value the cache keeps; split 0 appends it
+      if (t < 128) {
+        const uint16_t kb = bf16_bits(knew[t]), vb = bf16_bits(vnew[t]);
+        knew[t] = __uint_as_float((uint32_t)kb << 16);
+        vnew[t] = __uint_as_float((uint32_t)vb << 16);
+        if (s == 0) {
+          static_cast<uint16_t*>(a.kcache)[off] = kb;
+          static_cast<uint16_t*>(a.vcache)[off] = vb;
+        }
+      }
+      sync();
+    } else if (s == 0 && t < 128) {
+      static_cast<float*>(a.kcache)[off] = knew[t];
+      static_cast<float*>(a.vcache)[off] = vnew[t];
     }
   } else {
     for (int i = t; i < G * 128; i += ATTN_FAST_THREADS) qv[i] = dsm[AF_QRAW + i];

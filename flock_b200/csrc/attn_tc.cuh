@@ -238,10 +238,12 @@ inline size_t attn_tc_smem_bytes() { return 4 * (size_t)ATC_OPND + 24 + 1024; }
 // tile, kv head) one CTA writes the K tile ([key][head_dim], rows past kend
 // zero) and the V^T tile ([head_dim][key]), transposed through shared memory
 // so every global load is a coalesced row.  The grid covers the cache's
-// capacity; tiles past kend return at once.
+// capacity; tiles past kend return at once.  BF16: the cache holds bf16,
+// widened exactly before the f16 rounding.
 constexpr int KVI_STRIDE = 132;  // f32 row stride of the transposition buffer
-static __global__ void __launch_bounds__(ATC_THREADS) k_kv_image(const float* kcache,
-                                                                const float* vcache,
+template <bool BF16>
+static __global__ void __launch_bounds__(ATC_THREADS) k_kv_image(const void* kcache,
+                                                                const void* vcache,
                                                                 int n_kv_heads, const int* ctl,
                                                                 int n, int img_tiles,
                                                                 uint8_t* img) {
@@ -251,14 +253,41 @@ static __global__ void __launch_bounds__(ATC_THREADS) k_kv_image(const float* kc
   if (kt * ATC_K >= kend) return;
   const size_t kvs = (size_t)n_kv_heads * ATC_HD;
   const int key = kt * ATC_K + t;
+  const size_t off = (size_t)key * kvs + (size_t)g * ATC_HD;
   uint8_t* kdst = img + ((size_t)g * img_tiles + kt) * 2 * ATC_OPND;
   uint8_t* vdst = kdst + ATC_OPND;
-  atc_stage_row(kdst, t, key < kend ? kcache + (size_t)key * kvs + (size_t)g * ATC_HD : nullptr);
-  const float4* vr = reinterpret_cast<const float4*>(vcache + (size_t)key * kvs + (size_t)g * ATC_HD);
+  if constexpr (BF16) {
+    const uint4* kr = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(kcache) + off);
+    const uint4* vr = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(vcache) + off);
+    float kf[8];
+#pragma unroll 4
+    for (int c = 0; c < 16; c++) {
+      uint4 o = make_uint4(0, 0, 0, 0);
+      if (key < kend) {
+        bf16x8_widen(__ldg(kr + c), kf);
+        o = make_uint4(h2(kf[0], kf[1]), h2(kf[2], kf[3]), h2(kf[4], kf[5]), h2(kf[6], kf[7]));
+      }
+      *reinterpret_cast<uint4*>(kdst + atc_off(t, c)) = o;
+    }
+#pragma unroll 4
+    for (int c = 0; c < 16; c++) {
+      float* dst = vbuf + t * KVI_STRIDE + 8 * c;
+      if (key < kend) {
+        bf16x8_widen(__ldg(vr + c), dst);
+      } else {
+        reinterpret_cast<float4*>(dst)[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  } else {
+    const float* kc = static_cast<const float*>(kcache);
+    atc_stage_row(kdst, t, key < kend ? kc + off : nullptr);
+    const float4* vr = reinterpret_cast<const float4*>(static_cast<const float*>(vcache) + off);
 #pragma unroll 8
-  for (int c = 0; c < 32; c++)
-    reinterpret_cast<float4*>(vbuf + t * KVI_STRIDE)[c] =
-        key < kend ? __ldg(vr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c = 0; c < 32; c++)
+      reinterpret_cast<float4*>(vbuf + t * KVI_STRIDE)[c] =
+          key < kend ? __ldg(vr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   __syncthreads();
   // thread t = head_dim column t of the tile
 #pragma unroll 4

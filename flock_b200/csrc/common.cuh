@@ -11,6 +11,7 @@
 // functions and rounding once to f32.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <float.h>
@@ -29,6 +30,25 @@ FLOCK_DEV float fdiv(float a, float b) { return __fdiv_rn(a, b); }
 FLOCK_DEV float exp_f64r(float x) { return __double2float_rn(exp((double)x)); }
 // fr(1 / Math.sqrt(v)) for an f32 v: IEEE f64 sqrt and divide, one f32 round.
 FLOCK_DEV float rsqrt_f64r(float v) { return __double2float_rn(1.0 / sqrt((double)v)); }
+
+// bf16 KV cache elements (FLOCK_KV_BF16): a key or value is rounded to the
+// nearest bf16 (ties to even) once, when it is appended, and widened exactly
+// (the bf16 bits are the high half of the f32) whenever attention reads it.
+FLOCK_DEV uint16_t bf16_bits(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+FLOCK_DEV float bf16_round(float x) { return __uint_as_float((uint32_t)bf16_bits(x) << 16); }
+// Two bf16 packed in a word (element 0 in the low half) -> two f32.
+FLOCK_DEV float2 bf16x2_widen(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+// Eight bf16 (one 128-bit load) -> eight f32 at dst (16-byte aligned).
+FLOCK_DEV void bf16x8_widen(uint4 w, float* dst) {
+  const float2 a = bf16x2_widen(w.x), b = bf16x2_widen(w.y), c = bf16x2_widen(w.z),
+               d = bf16x2_widen(w.w);
+  reinterpret_cast<float4*>(dst)[0] = make_float4(a.x, a.y, b.x, b.y);
+  reinterpret_cast<float4*>(dst)[1] = make_float4(c.x, c.y, d.x, d.y);
+}
 
 // kernels/lib.ts:30 halfToF32: f16 -> f32 exactly, with inf/nan clamped to
 // the largest finite f32 (the reference clamps e == 31 regardless of mantissa).

@@ -43,14 +43,15 @@ struct MkLayer {
   const float* q_norm;
   const float* k_norm;
   const float* ffn_norm;
-  float* kcache;
-  float* vcache;
+  const void* kcache;  // prefetched only; attention reads through attn_args
+  const void* vcache;
 };
 
 struct MkArgs {
   const MkLayer* layers;
   int n_layers;
   int H, nH, nKV, hd, F, vocab;
+  int kv_bytes;  // bytes per cached key/value element: 4 (f32) or 2 (bf16)
   float eps;
   int neox;
   const float* inv_freq;
@@ -158,7 +159,7 @@ FLOCK_DEV void mk_prefetch_layer(const MkArgs& a, int l, int n_keys) {
     if ((uint64_t)rows[t] * cols[t] <= kMax) add(L.qs[t], (uint64_t)rows[t] * cols[t]);
   for (int t = 0; t < 7; t++)
     if ((uint64_t)rows[t] * cols[t] <= kMax) add(L.sc[t], (uint64_t)rows[t] * L.sc_stride[t] * 2);
-  const uint64_t kv = (uint64_t)n_keys * a.nKV * a.hd * 4;
+  const uint64_t kv = (uint64_t)n_keys * a.nKV * a.hd * a.kv_bytes;
   add(L.kcache, kv);
   add(L.vcache, kv);
   if (pf.n) issue_prefetch(pf);

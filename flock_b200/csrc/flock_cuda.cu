@@ -293,6 +293,16 @@ static int check_cfg(const flock_layer_config& c) {
               c.ffn);
     return FLOCK_E_UNSUPPORTED;
   }
+  if (c.kv_dtype != FLOCK_KV_F32 && c.kv_dtype != FLOCK_KV_BF16) {
+    set_error("kv_dtype %d is neither FLOCK_KV_F32 nor FLOCK_KV_BF16", c.kv_dtype);
+    return FLOCK_E_ARG;
+  }
+  if (c.kv_dtype == FLOCK_KV_BF16 &&
+      (c.attention != FLOCK_ATTN_FAST || c.prefill != FLOCK_PREFILL_TENSOR)) {
+    set_error("a bf16 KV cache needs FLOCK_ATTN_FAST and FLOCK_PREFILL_TENSOR (the exact "
+              "kernels read f32)");
+    return FLOCK_E_UNSUPPORTED;
+  }
   if (c.attention == FLOCK_ATTN_EXACT && c.max_keys > 48 * 1024) {
     set_error("exact decode attention holds every score on chip: max_keys %d > 49152; use "
               "FLOCK_ATTN_FAST", c.max_keys);
@@ -306,7 +316,7 @@ int layer_init(flock_layer* L, flock_dev* dev, const flock_layer_config& cfg, Wo
   FLOCK_TRY(check_cfg(cfg));
   L->dev = dev_retain(dev);
   L->cfg = cfg;
-  const size_t kv = (size_t)cfg.max_keys * cfg.n_kv_heads * cfg.head_dim * sizeof(float);
+  const size_t kv = (size_t)cfg.max_keys * cfg.n_kv_heads * cfg.head_dim * kv_elem_bytes(cfg);
   FLOCK_TRY(L->kcache.alloc(kv));
   FLOCK_TRY(L->vcache.alloc(kv));
   std::vector<float> inv(cfg.head_dim / 2);
@@ -347,8 +357,8 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   qa.k_norm = L->w[W_K_NORM]->data.as<float>();
   qa.inv_freq = L->inv_freq.as<float>();
   qa.qn = ws->qn.as<float>();
-  qa.kcache = L->kcache.as<float>();
-  qa.vcache = L->vcache.as<float>();
+  qa.kcache = L->kcache.p;
+  qa.vcache = L->vcache.p;
   qa.ctl = L->ctl;
   qa.n_tokens = n;
   qa.n_heads = c.n_heads;
@@ -357,7 +367,12 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   qa.eps = c.eps;
   qa.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
   pf_add(qa.pf, L->w[W_GATE]);
-  FLOCK_CK(launch_ex(d->stream, k_qk_norm_rope_append,
+  const bool kv_bf16 = c.kv_dtype == FLOCK_KV_BF16;
+  if (kv_bf16 && !(n > 1 && tensor_cores)) {
+    set_error("a bf16 KV cache runs decode on FLOCK_ATTN_FAST and prefill on the tensor cores");
+    return FLOCK_E_UNSUPPORTED;
+  }
+  FLOCK_CK(launch_ex(d->stream, kv_bf16 ? k_qk_norm_rope_append<true> : k_qk_norm_rope_append<false>,
                      dim3((n * (c.n_heads + c.n_kv_heads) + 7) / 8), dim3(256), 0, pdl, qa));
   AttnArgs aa = {};
   aa.q = ws->qn.as<float>();
@@ -373,10 +388,10 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   if (n > 1 && tensor_cores) {
     // the f16 image of keys [0, ctl[0] + n) (pos0 is read on the device)
     const int img_tiles = (c.max_keys + ATC_K - 1) / ATC_K;
-    FLOCK_TRY(kernel_setup((const void*)k_kv_image, (int)kv_image_smem_bytes()));
-    k_kv_image<<<dim3(img_tiles, c.n_kv_heads), ATC_THREADS, kv_image_smem_bytes(),
-                 d->stream>>>(L->kcache.as<float>(), L->vcache.as<float>(), c.n_kv_heads, L->ctl,
-                              n, img_tiles, ws->kv_img.as<uint8_t>());
+    auto* kvi = kv_bf16 ? k_kv_image<true> : k_kv_image<false>;
+    FLOCK_TRY(kernel_setup((const void*)kvi, (int)kv_image_smem_bytes()));
+    kvi<<<dim3(img_tiles, c.n_kv_heads), ATC_THREADS, kv_image_smem_bytes(), d->stream>>>(
+        L->kcache.p, L->vcache.p, c.n_kv_heads, L->ctl, n, img_tiles, ws->kv_img.as<uint8_t>());
     FLOCK_CK(cudaGetLastError());
     AttnTcArgs ta = {};
     ta.q = ws->qn.as<float>();
@@ -591,8 +606,9 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.q_norm = g_q;
     a.k_norm = g_k;
     a.inv_freq = L->inv_freq.as<float>();
-    a.kcache = L->kcache.as<float>();
-    a.vcache = L->vcache.as<float>();
+    a.kcache = L->kcache.p;
+    a.vcache = L->vcache.p;
+    a.kv_bf16 = c.kv_dtype == FLOCK_KV_BF16;
     a.ctl = L->ctl;
     a.out = ws->attn.as<float>();
     a.part = ws->attn_part.as<float>();
@@ -1076,8 +1092,8 @@ int flock_op_attention(flock_dev* d, const float* q, const float* k, const float
     FLOCK_CK(cudaMemset(tcount.b.p, 0, tcount.b.bytes));
     AttnFastArgs a = {};
     a.q = tq.b.as<float>();
-    a.kcache = tk.b.as<float>();
-    a.vcache = tv.b.as<float>();
+    a.kcache = tk.b.p;
+    a.vcache = tv.b.p;
     a.ctl = tc.b.as<int>();
     a.out = to.b.as<float>();
     a.part = tp.b.as<float>();
@@ -1326,22 +1342,59 @@ int flock_layer_n_keys(const flock_layer* L, int* out) {
 }
 
 int flock_layer_read_cache(flock_layer* L, float* k, float* v) {
-  const size_t bytes = (size_t)L->n_keys * L->cfg.n_kv_heads * L->cfg.head_dim * 4;
-  if (bytes) {
-    FLOCK_CK(cudaMemcpyAsync(k, L->kcache.p, bytes, cudaMemcpyDeviceToHost, L->dev->stream));
-    FLOCK_CK(cudaMemcpyAsync(v, L->vcache.p, bytes, cudaMemcpyDeviceToHost, L->dev->stream));
+  if (!L || !k || !v) return FLOCK_E_ARG;
+  const size_t count = (size_t)L->n_keys * L->cfg.n_kv_heads * L->cfg.head_dim;
+  if (count && L->cfg.kv_dtype == FLOCK_KV_BF16) {
+    // bf16 -> f32 exactly: the stored bits become the high half
+    std::vector<uint16_t> kb(count), vb(count);
+    FLOCK_CK(cudaMemcpyAsync(kb.data(), L->kcache.p, count * 2, cudaMemcpyDeviceToHost,
+                             L->dev->stream));
+    FLOCK_CK(cudaMemcpyAsync(vb.data(), L->vcache.p, count * 2, cudaMemcpyDeviceToHost,
+                             L->dev->stream));
+    FLOCK_CK(cudaStreamSynchronize(L->dev->stream));
+    for (size_t i = 0; i < count; i++) {
+      const uint32_t kw = (uint32_t)kb[i] << 16, vw = (uint32_t)vb[i] << 16;
+      memcpy(k + i, &kw, 4);
+      memcpy(v + i, &vw, 4);
+    }
+  } else if (count) {
+    FLOCK_CK(cudaMemcpyAsync(k, L->kcache.p, count * 4, cudaMemcpyDeviceToHost, L->dev->stream));
+    FLOCK_CK(cudaMemcpyAsync(v, L->vcache.p, count * 4, cudaMemcpyDeviceToHost, L->dev->stream));
   }
   FLOCK_CK(cudaStreamSynchronize(L->dev->stream));
   return ws_check_errors(L->ws);
 }
 
+// f32 -> bf16 bits, rounded to nearest with ties to even (NaN stays a quiet NaN).
+static uint16_t host_bf16_bits(float x) {
+  uint32_t w;
+  memcpy(&w, &x, 4);
+  if ((w & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((w >> 16) | 0x40u);
+  return (uint16_t)((w + 0x7fffu + ((w >> 16) & 1u)) >> 16);
+}
+
 int flock_layer_write_cache(flock_layer* L, const float* k, const float* v, int n_keys) {
   if (!L || !k || !v || n_keys < 0 || L->n_keys + n_keys > L->cfg.max_keys) return FLOCK_E_ARG;
-  const size_t row = (size_t)L->cfg.n_kv_heads * L->cfg.head_dim * 4;
-  FLOCK_CK(cudaMemcpyAsync(L->kcache.as<uint8_t>() + L->n_keys * row, k, n_keys * row,
-                           cudaMemcpyHostToDevice, L->dev->stream));
-  FLOCK_CK(cudaMemcpyAsync(L->vcache.as<uint8_t>() + L->n_keys * row, v, n_keys * row,
-                           cudaMemcpyHostToDevice, L->dev->stream));
+  const size_t elems = (size_t)L->cfg.n_kv_heads * L->cfg.head_dim;
+  const size_t row = elems * kv_elem_bytes(L->cfg);
+  if (L->cfg.kv_dtype == FLOCK_KV_BF16) {
+    const size_t count = elems * (size_t)n_keys;
+    std::vector<uint16_t> kb(count), vb(count);
+    for (size_t i = 0; i < count; i++) {
+      kb[i] = host_bf16_bits(k[i]);
+      vb[i] = host_bf16_bits(v[i]);
+    }
+    FLOCK_CK(cudaMemcpyAsync(L->kcache.as<uint8_t>() + L->n_keys * row, kb.data(), n_keys * row,
+                             cudaMemcpyHostToDevice, L->dev->stream));
+    FLOCK_CK(cudaMemcpyAsync(L->vcache.as<uint8_t>() + L->n_keys * row, vb.data(), n_keys * row,
+                             cudaMemcpyHostToDevice, L->dev->stream));
+    FLOCK_CK(cudaStreamSynchronize(L->dev->stream));  // before the host copies go
+  } else {
+    FLOCK_CK(cudaMemcpyAsync(L->kcache.as<uint8_t>() + L->n_keys * row, k, n_keys * row,
+                             cudaMemcpyHostToDevice, L->dev->stream));
+    FLOCK_CK(cudaMemcpyAsync(L->vcache.as<uint8_t>() + L->n_keys * row, v, n_keys * row,
+                             cudaMemcpyHostToDevice, L->dev->stream));
+  }
   return flock_layer_rewind(L, L->n_keys + n_keys);
 }
 

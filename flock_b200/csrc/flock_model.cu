@@ -258,8 +258,8 @@ int mk_prepare(flock_model* m) {
     tab[i].q_norm = L->w[W_Q_NORM]->data.as<float>();
     tab[i].k_norm = L->w[W_K_NORM]->data.as<float>();
     tab[i].ffn_norm = L->w[W_FFN_NORM]->data.as<float>();
-    tab[i].kcache = L->kcache.as<float>();
-    tab[i].vcache = L->vcache.as<float>();
+    tab[i].kcache = L->kcache.p;
+    tab[i].vcache = L->vcache.p;
   }
   FLOCK_TRY(m->mk_layers.alloc(tab.size() * sizeof(MkLayer)));
   FLOCK_CK(cudaMemcpy(m->mk_layers.p, tab.data(), tab.size() * sizeof(MkLayer),
@@ -273,6 +273,7 @@ int mk_prepare(flock_model* m) {
   a.nH = c.n_heads;
   a.nKV = c.n_kv_heads;
   a.hd = c.head_dim;
+  a.kv_bytes = (int)kv_elem_bytes(c);
   a.F = c.ffn;
   a.vocab = m->vocab;
   a.eps = c.eps;
@@ -374,8 +375,9 @@ int mk_prepare(flock_model* m) {
       aa.q_norm = L->w[W_Q_NORM]->data.as<float>();
       aa.k_norm = L->w[W_K_NORM]->data.as<float>();
       aa.inv_freq = L->inv_freq.as<float>();
-      aa.kcache = L->kcache.as<float>();
-      aa.vcache = L->vcache.as<float>();
+      aa.kcache = L->kcache.p;
+      aa.vcache = L->vcache.p;
+      aa.kv_bf16 = c.kv_dtype == FLOCK_KV_BF16;
       aa.out = ws.attn.as<float>();
       aa.part = ws.attn_part.as<float>();
       aa.count = ws.attn_count.as<uint32_t>();

@@ -65,8 +65,8 @@ struct QkArgs {
   const float* k_norm;
   const float* inv_freq;  // [hd/2]
   float* qn;        // [n][nH][hd] out
-  float* kcache;    // [maxKeys][nKV][hd]
-  float* vcache;
+  void* kcache;     // [maxKeys][nKV][hd], f32 (or bf16 for k_qk_norm_rope_append<true>)
+  void* vcache;
   const int* ctl;   // ctl[0] = pos0
   int n_tokens, n_heads, n_kv_heads, head_dim;
   float eps;
@@ -120,8 +120,12 @@ FLOCK_DEV void norm_rope_warp(const float* src, const float* gain, float eps, in
 
 // One warp per 128-vector (8 per CTA): q heads -> qn, k heads -> the cache at
 // position pos0 + token with v copied beside it.  norm_rope_warp's arithmetic
-// is the WG = 128 RMSNorm and RoPE above, bit for bit.
+// is the WG = 128 RMSNorm and RoPE above, bit for bit.  BF16: the cache holds
+// bf16; the rotated key is staged in shared memory and stored rounded to
+// nearest even, as is v.
+template <bool BF16>
 static __global__ void __launch_bounds__(256) k_qk_norm_rope_append(const QkArgs a) {
+  __shared__ __align__(16) float kstage[BF16 ? 8 * 128 : 4];
   issue_prefetch(a.pf);
   pdl_launch_dependents();
   pdl_wait();
@@ -138,11 +142,26 @@ static __global__ void __launch_bounds__(256) k_qk_norm_rope_append(const QkArgs
                    a.neox, a.qn + ((size_t)tok * a.n_heads + hv) * hd, lane);
   } else {
     const size_t row = ((size_t)pos * a.n_kv_heads + kvh) * hd;
-    norm_rope_warp(a.k + ((size_t)tok * a.n_kv_heads + kvh) * hd, a.k_norm, a.eps, pos, a.inv_freq,
-                   a.neox, a.kcache + row, lane);
+    const float* k = a.k + ((size_t)tok * a.n_kv_heads + kvh) * hd;
     const float* v = a.v + ((size_t)tok * a.n_kv_heads + kvh) * hd;
+    if constexpr (BF16) {
+      float* ks = kstage + warp * 128;
+      norm_rope_warp(k, a.k_norm, a.eps, pos, a.inv_freq, a.neox, ks, lane);
+      __syncwarp();
+      uint16_t* kc = static_cast<uint16_t*>(a.kcache) + row;
+      uint16_t* vc = static_cast<uint16_t*>(a.vcache) + row;
 #pragma unroll
-    for (int q = 0; q < 4; q++) a.vcache[row + lane + 32 * q] = v[lane + 32 * q];
+      for (int q = 0; q < 4; q++) {
+        kc[lane + 32 * q] = bf16_bits(ks[lane + 32 * q]);
+        vc[lane + 32 * q] = bf16_bits(v[lane + 32 * q]);
+      }
+    } else {
+      norm_rope_warp(k, a.k_norm, a.eps, pos, a.inv_freq, a.neox,
+                     static_cast<float*>(a.kcache) + row, lane);
+      float* vc = static_cast<float*>(a.vcache) + row;
+#pragma unroll
+      for (int q = 0; q < 4; q++) vc[lane + 32 * q] = v[lane + 32 * q];
+    }
   }
 }
 

@@ -44,14 +44,21 @@ class LayerConfig:
     # multi-token steps: "exact" (the reference's f32 order, bit-comparable) or
     # "tensor" (tcgen05 tensor cores, f16 operands, 1e-2 relative tolerance)
     prefill: str = "exact"
+    # KV cache element type: "f32" (the reference's) or "bf16" (half the bytes
+    # per key; appends round to nearest even; needs attention="fast" and
+    # prefill="tensor")
+    kv: str = "f32"
 
     def to_c(self) -> _abi.LayerConfigC:
+        if self.kv not in ("f32", "bf16"):
+            raise ValueError(f"kv must be 'f32' or 'bf16', not {self.kv!r}")
         return _abi.LayerConfigC(
             self.hidden, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn, self.eps,
             self.rope_base, self.max_keys, self.max_prefill,
             _abi.FLOCK_ROPE_NEOX if self.rope_pairing == "neox" else _abi.FLOCK_ROPE_NORM,
             _abi.FLOCK_ATTN_EXACT if self.attention == "exact" else _abi.FLOCK_ATTN_FAST,
-            _abi.FLOCK_PREFILL_TENSOR if self.prefill == "tensor" else _abi.FLOCK_PREFILL_EXACT)
+            _abi.FLOCK_PREFILL_TENSOR if self.prefill == "tensor" else _abi.FLOCK_PREFILL_EXACT,
+            _abi.FLOCK_KV_BF16 if self.kv == "bf16" else _abi.FLOCK_KV_F32)
 
     def with_(self, **kw) -> "LayerConfig":
         return replace(self, **kw)

@@ -60,6 +60,12 @@ extern "C" {
                                   16-bit (f16) operands, f32 accumulation, max relative
                                   error 1e-2 */
 
+#define FLOCK_KV_F32 0  /* f32 KV cache, the reference's (layer.ts:394-397 kcache/vcache) */
+#define FLOCK_KV_BF16 1 /* bf16 KV cache: half the bytes per key; each appended key and
+                           value is rounded to nearest even once and every attention
+                           read widens it exactly.  Needs FLOCK_ATTN_FAST and
+                           FLOCK_PREFILL_TENSOR (the exact kernels are f32 only). */
+
 typedef struct flock_dev flock_dev;
 typedef struct flock_tensor flock_tensor;
 typedef struct flock_layer flock_layer;
@@ -82,6 +88,7 @@ typedef struct flock_layer_config {
   int32_t rope_pairing; /* FLOCK_ROPE_NEOX | FLOCK_ROPE_NORM */
   int32_t attention;    /* FLOCK_ATTN_EXACT | FLOCK_ATTN_FAST */
   int32_t prefill;      /* FLOCK_PREFILL_EXACT | FLOCK_PREFILL_TENSOR (multi-token steps) */
+  int32_t kv_dtype;     /* FLOCK_KV_F32 (0, the default) | FLOCK_KV_BF16 */
 } flock_layer_config;
 
 /* ------------------------------------------------------------- errors/dev */
@@ -214,9 +221,11 @@ FLOCK_API int flock_layer_reset(flock_layer* layer);
 FLOCK_API int flock_layer_n_keys(const flock_layer* layer, int* out);
 /* Drop the cache back to n_keys (model.ts:529 rewind, per layer). */
 FLOCK_API int flock_layer_rewind(flock_layer* layer, int n_keys);
-/* kernels/layer.ts:792 cacheBuffers(): copy keys/values [n_keys][nKV][hd]. */
+/* kernels/layer.ts:792 cacheBuffers(): copy keys/values [n_keys][nKV][hd] as f32
+ * (a bf16 cache is widened exactly). */
 FLOCK_API int flock_layer_read_cache(flock_layer* layer, float* k_out, float* v_out);
-/* Preload keys/values at the current position (a synthetic cache). */
+/* Preload keys/values at the current position (a synthetic cache); a bf16
+ * cache stores them rounded to nearest even. */
 FLOCK_API int flock_layer_write_cache(flock_layer* layer, const float* k, const float* v, int n_keys);
 
 /* web/bird.html:544-620 runFrame / tools/sim_bird.mjs:326-340: run `x`

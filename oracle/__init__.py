@@ -90,6 +90,8 @@ def lib():
             "fo_cache_k": (_f32p, [ctypes.c_void_p]),
             "fo_cache_v": (_f32p, [ctypes.c_void_p]),
             "fo_cache_fill": (_int, [ctypes.c_void_p, _f32p, _f32p, _int]),
+            "fo_cache_set_bf16": (None, [ctypes.c_void_p, _int]),
+            "fo_bf16_round": (ctypes.c_float, [ctypes.c_float]),
             "fo_layer_forward": (_int, [_f32p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                         _f32p]),
             "fo_layer_prefill": (_int, [_f32p, _int, ctypes.c_void_p, ctypes.c_void_p,
@@ -315,9 +317,14 @@ F32_NAMES = {"attn_norm.weight": "attn_norm", "attn_q_norm.weight": "q_norm",
 class RefLayer:
     """layer_ref.ts layerForwardRef / layerPrefillRef with a RefCache (:24).
     tp > 1: o_proj and down become tp-shard input-split matvecs
-    (shard_ref.ts:353), the arithmetic of a tensor-parallel layer."""
+    (shard_ref.ts:353), the arithmetic of a tensor-parallel layer.
+    kv="bf16": every appended key/value is rounded to bf16 (nearest even), the
+    cache a FLOCK_KV_BF16 layer keeps; attention then reads the rounded values."""
 
-    def __init__(self, weights: dict, cfg: dict, max_keys: int = 4096, tp: int = 1):
+    def __init__(self, weights: dict, cfg: dict, max_keys: int = 4096, tp: int = 1,
+                 kv: str = "f32"):
+        if kv not in ("f32", "bf16"):
+            raise ValueError(f"kv must be 'f32' or 'bf16', not {kv!r}")
         self.tp = int(tp)
         self._keep = {}
         w = _W()
@@ -336,6 +343,7 @@ class RefLayer:
                        1 if cfg.get("rope_pairing", "neox") == "neox" else 0)
         self.kvw = cfg["n_kv_heads"] * cfg["head_dim"]
         self._cache = lib().fo_cache_new(max_keys, self.kvw)
+        lib().fo_cache_set_bf16(self._cache, 1 if kv == "bf16" else 0)
 
     def __del__(self):
         try:

@@ -502,10 +502,31 @@ void fo_cache_reset(fo_cache* c) { c->n = 0; }
 int fo_cache_len(const fo_cache* c) { return c->n; }
 const float* fo_cache_k(const fo_cache* c) { return c->k; }
 const float* fo_cache_v(const fo_cache* c) { return c->v; }
+void fo_cache_set_bf16(fo_cache* c, int on) { c->bf16 = on != 0; }
+float fo_bf16_round(float x) {
+  uint32_t w;
+  memcpy(&w, &x, 4);
+  if ((w & 0x7fffffffu) > 0x7f800000u) {
+    w |= 0x00400000u; /* quiet NaN */
+  } else {
+    w += 0x7fffu + ((w >> 16) & 1u); /* round to nearest, ties to even */
+  }
+  w &= 0xffff0000u;
+  memcpy(&x, &w, 4);
+  return x;
+}
 int fo_cache_fill(fo_cache* c, const float* k, const float* v, int n) {
   if (c->n + n > c->cap) return -1;
-  memcpy(c->k + (int64_t)c->n * c->kvw, k, sizeof(float) * (size_t)n * c->kvw);
-  memcpy(c->v + (int64_t)c->n * c->kvw, v, sizeof(float) * (size_t)n * c->kvw);
+  float* kd = c->k + (int64_t)c->n * c->kvw;
+  float* vd = c->v + (int64_t)c->n * c->kvw;
+  const size_t count = (size_t)n * c->kvw;
+  memcpy(kd, k, sizeof(float) * count);
+  memcpy(vd, v, sizeof(float) * count);
+  if (c->bf16)
+    for (size_t i = 0; i < count; i++) {
+      kd[i] = fo_bf16_round(kd[i]);
+      vd[i] = fo_bf16_round(vd[i]);
+    }
   c->n += n;
   return 0;
 }

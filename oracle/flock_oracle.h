@@ -115,6 +115,7 @@ typedef struct fo_cache {
   int n;   /* keys held */
   int cap; /* capacity in keys */
   int kvw; /* nKV*hd */
+  int bf16; /* 1: every key/value is rounded to bf16 (nearest even) as it is stored */
 } fo_cache;
 
 fo_cache* fo_cache_new(int cap, int kvw);
@@ -123,6 +124,11 @@ void fo_cache_reset(fo_cache* c);
 int fo_cache_len(const fo_cache* c);
 const float* fo_cache_k(const fo_cache* c);
 const float* fo_cache_v(const fo_cache* c);
+/* A bf16 KV cache (FLOCK_KV_BF16 in flock_cuda.h; beyond the reference, which
+ * keeps f32): from now on fo_cache_fill stores each value rounded to bf16. */
+void fo_cache_set_bf16(fo_cache* c, int on);
+/* f32 -> the nearest bf16 value (ties to even), as an f32. */
+float fo_bf16_round(float x);
 /* Preload n keys (e.g. a synthetic cache); returns 0 or -1 if over capacity. */
 int fo_cache_fill(fo_cache* c, const float* k, const float* v, int n);
 
