@@ -46,6 +46,26 @@ def test_python_binding_covers_the_abi(built):
         assert hasattr(lib, name)
 
 
+def test_config_struct_matches_the_header(tmp_path):
+    """The ctypes mirror of flock_layer_config has the C compiler's layout."""
+    fields = [f[0] for f in _abi.LayerConfigC._fields_]
+    prog = tmp_path / "layout.c"
+    prog.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "flock_cuda.h"\n'
+                    "int main(void) {\n"
+                    '  printf("%zu", sizeof(flock_layer_config));\n'
+                    + "".join(f'  printf(" %zu", offsetof(flock_layer_config, {f}));\n'
+                              for f in fields)
+                    + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", f"-I{os.path.dirname(HEADER)}", str(prog), "-o", str(exe)],
+                   check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    want = [ctypes.sizeof(_abi.LayerConfigC)] + [getattr(_abi.LayerConfigC, f).offset
+                                                 for f in fields]
+    assert got == want
+
+
 def test_version_and_error_strings(built):
     assert b"sm_100a" in _abi.lib().flock_version()
     assert isinstance(_abi.last_error(), str)
