@@ -15,7 +15,8 @@
 //    derives the weights, then each thread sums one output element's splits
 //    with all of their loads in flight;
 //  * a step over n keys uses ceil(n / 16) splits, at most
-//    attn_max_splits(SMs, kv heads): short contexts keep few partials;
+//    attn_max_splits(SMs, kv heads, cache capacity): short contexts keep few
+//    partials, caches over 2048 keys run up to 3 CTAs per SM;
 //  * scores: one thread per (key, query head), a 128-long dot product over
 //    a K tile whose rows are padded to 132 floats (conflict-free 128-bit
 //    reads).
@@ -59,14 +60,26 @@ struct AttnFastArgs {
 constexpr int ATTN_FAST_THREADS = 256;
 constexpr int ATTN_TILE = 64;  // keys staged in shared memory per pass
 
-// Most splits a decode step may use: one wave of CTAs over the kv heads, and
-// at most 32 so a warp holds one split per lane when combining.
+// Most splits a decode step may use: one wave of CTAs over the kv heads --
+// one CTA per SM, at most 32 splits, for caches of up to ATTN_LONG_KEYS keys
+// (short steps are latency-bound: fewer partials combine sooner); for longer
+// caches several CTAs per SM, so that one CTA's K/V loads overlap another's
+// arithmetic, and at most ATTN_MAX_SPLITS (a combining lane holds two).
 #ifndef FLOCK_ATTN_CTAS_PER_SM
 #define FLOCK_ATTN_CTAS_PER_SM 1
 #endif
-__host__ __device__ inline int attn_max_splits(int sm_count, int n_kv_heads) {
-  int s = n_kv_heads > 0 ? sm_count * FLOCK_ATTN_CTAS_PER_SM / n_kv_heads : 1;
-  return s < 1 ? 1 : (s > 32 ? 32 : s);
+#ifndef FLOCK_ATTN_LONG_CTAS_PER_SM
+#define FLOCK_ATTN_LONG_CTAS_PER_SM 3
+#endif
+constexpr int ATTN_LONG_KEYS = 2048;
+constexpr int ATTN_MAX_SPLITS = 64;
+static_assert(4 * ATTN_MAX_SPLITS <= 4 * ATTN_TILE, "combine weights live in the score tile");
+__host__ __device__ inline int attn_max_splits(int sm_count, int n_kv_heads, int max_keys) {
+  const bool long_cache = max_keys > ATTN_LONG_KEYS;
+  const int per_sm = long_cache ? FLOCK_ATTN_LONG_CTAS_PER_SM : FLOCK_ATTN_CTAS_PER_SM;
+  const int cap = long_cache ? ATTN_MAX_SPLITS : 32;
+  int s = n_kv_heads > 0 ? sm_count * per_sm / n_kv_heads : 1;
+  return s < 1 ? 1 : (s > cap ? cap : s);
 }
 
 // Splits a step over n_keys keys uses: one per ATTN_SPLIT_KEYS keys, at most
@@ -313,36 +326,49 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   if (!*last_flag) return;
   __threadfence();
   // the combine spread over the whole CTA: warp hq derives
-  // head hq's split weights w_s = e^(m_s - M) and L (lane s = split s), then
-  // every thread owns one (head, element) and sums its splits in order, all
-  // of the split loads in flight at once
-  float* cw = dsm + AF_SC;  // [G][32] split weights
+  // head hq's split weights w_s = e^(m_s - M) and L (lane s holds splits s
+  // and s + 32), then every thread owns one (head, element) and sums its
+  // splits in order, 32 split loads in flight at a time
+  float* cw = dsm + AF_SC;  // [G][ATTN_MAX_SPLITS] split weights
   float* cl = dsm + AF_ML;  // [G] L
   if (warp < G) {
     const float* pp = a.part + (size_t)(g * G + warp) * a.splits * (hd + 2);
-    const float m = lane < splits ? __ldcg(pp + lane * (hd + 2) + hd) : -INFINITY;
-    const float l = lane < splits ? __ldcg(pp + lane * (hd + 2) + hd + 1) : 0.0f;
-    float M = m;
+    const bool has0 = lane < splits, has1 = lane + 32 < splits;
+    const float m0 = has0 ? __ldcg(pp + lane * (hd + 2) + hd) : -INFINITY;
+    const float l0 = has0 ? __ldcg(pp + lane * (hd + 2) + hd + 1) : 0.0f;
+    const float m1 = has1 ? __ldcg(pp + (lane + 32) * (hd + 2) + hd) : -INFINITY;
+    const float l1 = has1 ? __ldcg(pp + (lane + 32) * (hd + 2) + hd + 1) : 0.0f;
+    float M = fmaxf(m0, m1);
 #pragma unroll
     for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-    const float w = lane < splits ? expf(m - M) : 0.0f;
+    const float w0 = has0 ? expf(m0 - M) : 0.0f;
+    const float w1 = has1 ? expf(m1 - M) : 0.0f;
     float L = 0.0f;
-    for (int sp = 0; sp < splits; sp++)
-      L = fmaf(__shfl_sync(0xffffffffu, l, sp), __shfl_sync(0xffffffffu, w, sp), L);
-    cw[warp * 32 + lane] = w;
+    for (int sp = 0; sp < splits; sp++) {
+      const bool hi = sp >= 32;  // uniform over the warp
+      L = fmaf(__shfl_sync(0xffffffffu, hi ? l1 : l0, sp & 31),
+               __shfl_sync(0xffffffffu, hi ? w1 : w0, sp & 31), L);
+    }
+    cw[warp * ATTN_MAX_SPLITS + lane] = w0;
+    cw[warp * ATTN_MAX_SPLITS + lane + 32] = w1;
     if (lane == 0) cl[warp] = L;
   }
   sync();
   for (int oi = t; oi < G * hd; oi += ATTN_FAST_THREADS) {
     const int hq = oi / hd, i = oi - hq * hd;
     const float* pp = a.part + (size_t)(g * G + hq) * a.splits * (hd + 2) + i;
-    float ov[32];
-#pragma unroll
-    for (int sp = 0; sp < 32; sp++) ov[sp] = sp < splits ? __ldcg(pp + sp * (hd + 2)) : 0.0f;
     float O = 0.0f;
 #pragma unroll
-    for (int sp = 0; sp < 32; sp++)
-      if (sp < splits) O = fmaf(ov[sp], cw[hq * 32 + sp], O);
+    for (int s0 = 0; s0 < ATTN_MAX_SPLITS; s0 += 32) {
+      if (s0 >= splits) break;
+      float ov[32];
+#pragma unroll
+      for (int sp = 0; sp < 32; sp++)
+        ov[sp] = s0 + sp < splits ? __ldcg(pp + (s0 + sp) * (hd + 2)) : 0.0f;
+#pragma unroll
+      for (int sp = 0; sp < 32; sp++)
+        if (s0 + sp < splits) O = fmaf(ov[sp], cw[hq * ATTN_MAX_SPLITS + s0 + sp], O);
+    }
     a.out[(size_t)(g * G + hq) * hd + i] = O / cl[hq];
   }
   if (t == 0) a.count[g] = 0;

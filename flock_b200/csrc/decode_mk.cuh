@@ -190,11 +190,16 @@ FLOCK_DEV void mk_gemv(const GemvArgs* gp, const float* from, float* xs, float* 
     mk_gemv_la<R, EPI, 1>(gp, from, xs, gs, red, best_v, best_i);
 }
 
-// The attention phase: work item (kv head, split) = (CTA / splits, CTA % splits).
+// The attention phase: work items (kv head, split) = (item / splits, item %
+// splits), item = CTA, CTA + grid, ... (more items than CTAs when a long
+// cache runs several splits per SM); all threads of the CTA work on each item.
 __device__ __noinline__ void mk_attention(const AttnFastArgs* __restrict__ ap, int pos,
                                           float* att, bool* last) {
   const AttnFastArgs& aa = *ap;
-  attn_fast_item(aa, blockIdx.x / aa.splits, blockIdx.x % aa.splits, pos, att, last, BlockSync{});
+  for (int item = blockIdx.x; item < aa.n_kv_heads * aa.splits; item += gridDim.x) {
+    attn_fast_item(aa, item / aa.splits, item % aa.splits, pos, att, last, BlockSync{});
+    __syncthreads();  // the next item reuses the shared tiles
+  }
 }
 
 // Shared memory: x (padded) | gain staging | reduction scratch | CTA argmax
@@ -275,7 +280,7 @@ static __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const MkArgs
     if (!(ok = grid_barrier(a, epoch))) break;
     stamp(2 + l * 10 + 1);
     // attention (q/k norm + RoPE + KV append fused; the last split combines)
-    if ((int)blockIdx.x < a.nKV * a.splits) mk_attention(a.attn_args + l, pos, sm.att, &att_last);
+    mk_attention(a.attn_args + l, pos, sm.att, &att_last);
     stamp(2 + l * 10 + 2);
     if (!(ok = grid_barrier(a, epoch))) break;
     stamp(2 + l * 10 + 3);

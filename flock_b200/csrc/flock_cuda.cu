@@ -61,7 +61,7 @@ const char* const kTensorNames[W_COUNT] = {
 
 // ------------------------------------------------------------- launching
 
-int kernel_setup(const void* func, int max_dyn_smem) {
+int kernel_setup(const void* func, int max_dyn_smem, int carveout) {
   static std::mutex mu;
   static std::map<std::pair<const void*, int>, int> opted;  // largest opt-in so far
   int dev = 0;
@@ -71,6 +71,8 @@ int kernel_setup(const void* func, int max_dyn_smem) {
   if (it != opted.end() && it->second >= max_dyn_smem) return FLOCK_OK;
   if (max_dyn_smem > 0)
     FLOCK_CK(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn_smem));
+  if (carveout >= 0)
+    FLOCK_CK(cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, carveout));
   opted[{func, dev}] = max_dyn_smem;
   return FLOCK_OK;
 }
@@ -225,7 +227,7 @@ void dev_release(flock_dev* d) {
 
 int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
   P = c.max_prefill < 1 ? 1 : c.max_prefill;
-  attn_splits = attn_max_splits(sm_count, c.n_kv_heads);
+  attn_splits = attn_max_splits(sm_count, c.n_kv_heads, c.max_keys);
   H = c.hidden;
   nH = c.n_heads;
   nKV = c.n_kv_heads;
@@ -239,7 +241,7 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
   FLOCK_TRY(qn.alloc((size_t)P * nH * hd * f));
   FLOCK_TRY(attn.alloc((size_t)P * nH * hd * f));
   FLOCK_TRY(act.alloc((size_t)P * F * f));
-  FLOCK_TRY(attn_part.alloc((size_t)nH * attn_split_cap * (hd + 2) * f));
+  FLOCK_TRY(attn_part.alloc((size_t)nH * attn_splits * (hd + 2) * f));  // stride: attn_splits
   FLOCK_TRY(attn_count.alloc((size_t)nKV * 4));
   FLOCK_CK(cudaMemset(attn_count.p, 0, attn_count.bytes));
   if (c.prefill == FLOCK_PREFILL_TENSOR) {
@@ -624,7 +626,9 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     pf_add(a.pf, L->w[W_GATE]);
     pf_add(a.pf, L->w[W_UP]);
     const size_t smem = attn_fast_smem(a.chunk_cap);
-    FLOCK_TRY(kernel_setup((const void*)k_attn_decode_fast, 200 * 1024));
+    // all shared memory: a long cache's splits run three 75 KB CTAs per SM
+    FLOCK_TRY(kernel_setup((const void*)k_attn_decode_fast, 200 * 1024,
+                           cudaSharedmemCarveoutMaxShared));
     FLOCK_CK(launch_ex(d->stream, k_attn_decode_fast, dim3(c.n_kv_heads, a.splits),
                        dim3(ATTN_FAST_THREADS), smem, pdl, a));
   } else {

@@ -19,7 +19,9 @@ void set_error(const char* fmt, ...);
 // Per (kernel, current device), once: when max_dyn_smem > 0, opt in to that
 // much dynamic shared memory (the attribute is per device, so a process
 // driving several GPUs needs it on each).
-int kernel_setup(const void* func, int max_dyn_smem);
+// Opt `func` in to max_dyn_smem bytes of dynamic shared memory (once per
+// device); carveout >= 0 also sets its preferred shared-memory carveout (%).
+int kernel_setup(const void* func, int max_dyn_smem, int carveout = -1);
 
 // Device references (see flock_dev): retain returns its argument.
 flock_dev* dev_retain(flock_dev* d);
@@ -87,8 +89,7 @@ struct Workspace {
   int P = 0, H = 0, nH = 0, nKV = 0, hd = 0, F = 0;
   DBuf h, q, k, v, qn, attn, act;
   DBuf attn_part, attn_count;  // fast decode attention partials
-  int attn_splits = 16;         // splits: SMs / kv heads, so one wave covers them
-  int attn_split_cap = 32;      // partial slots allocated per head (attn_max_splits' bound)
+  int attn_splits = 16;         // splits (attn_max_splits); partial slots per query head
   DBuf img, gu, tc_err, part;   // tensor-core prefill: activation image, gate|up rows, error word,
                                 // split-K partials
   DBuf kv_img;                  // tensor-core prefill: f16 K / V^T tiles of the cache

@@ -236,7 +236,7 @@ int mk_prepare(flock_model* m) {
   FLOCK_CK(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
   if (!coop) return FLOCK_OK;
   const int grid = m->dev->sm_count;
-  const int splits = attn_max_splits(grid, c.n_kv_heads);  // = the kernel graph's
+  const int splits = attn_max_splits(grid, c.n_kv_heads, c.max_keys);  // = the kernel graph's
   if (splits != m->ws.attn_splits) return FLOCK_OK;
   MkArgs& a = m->mk;
   a = MkArgs{};

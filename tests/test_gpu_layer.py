@@ -71,6 +71,24 @@ def test_config0_decode_at_256(dev, oracle, weights, mode):
     assert n_mismatch(k[256 * kvw:], rk[256 * kvw:]) <= 2
 
 
+def test_fast_decode_over_long_cache(dev, oracle, weights):
+    """8192 keys: past 2048 keys of capacity the split-K attention runs up to 64
+    splits (three CTAs per SM), combined two splits per lane."""
+    kvw = S.n_kv_heads * S.head_dim
+    kc = synth.normal(107, "k8k", 8192 * kvw)
+    vc = synth.normal(107, "v8k", 8192 * kvw)
+    L = Layer.create(dev, weights, QWEN3_06B.with_(attention="fast", max_keys=8200))
+    L.write_cache(kc, vc)
+    ref = _ref(oracle, weights, cap=8200)
+    ref.fill_cache(kc, vc)
+    for step in range(2):
+        x = synth.normal(107, f"x{step}", S.hidden)
+        got = L.forward(x)
+        want = _fwd(oracle, ref, x, 1, False)
+        assert abs_err_scaled(got, want) < 1e-5
+    assert L.n_keys == 8194
+
+
 @pytest.mark.parametrize("mode", ["exact", "fast"])
 def test_four_decode_steps(dev, oracle, weights, mode):
     L = Layer.create(dev, weights, QWEN3_06B.with_(attention=mode))

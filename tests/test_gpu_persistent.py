@@ -82,6 +82,21 @@ def test_persistent_long_context(dev, small):
     assert np.array_equal(_bits(la), _bits(lb))
 
 
+def test_persistent_long_cache_splits(dev, small):
+    """A cache of over 2048 keys: up to 64 splits, several per SM, which the
+    persistent kernel's CTAs take in turn."""
+    a, b = _pair(dev, small, FAST.with_(max_keys=4200, prefill="tensor"))
+    ids = synth.uniform_ids(9, "long4k", 4000, 4096).tolist()
+    for M in (a, b):
+        for i in range(0, 4000, 500):
+            M.step(ids[i:i + 500])
+    got = a.decode_device(8)
+    want = b.decode_device(8)
+    assert got.tolist() == want.tolist()
+    la, lb = a.logits([int(got[-1])]), b.logits([int(want[-1])])
+    assert np.array_equal(_bits(la), _bits(lb))
+
+
 def test_persistent_decode_device_history(dev, small):
     a, b = _pair(dev, small)
     for M in (a, b):
