@@ -419,10 +419,10 @@ int mk_prepare(flock_model* m) {
   FLOCK_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mk, MK_THREADS, smem));
   if (per_sm < 1) return FLOCK_OK;
   // every CTA must be resident (cooperative launch); two per SM when they fit,
-  // as the graph's GEMVs run, and never fewer than the attention items
+  // as the graph's GEMVs run (the attention phase loops CTAs over its items)
   m->mk_smem = smem;
   m->mk_grid = (per_sm >= 2 ? 2 : 1) * grid;
-  if (m->mk_grid < c.n_kv_heads * splits || m->mk_grid > 4096) return FLOCK_OK;
+  if (m->mk_grid > 4096) return FLOCK_OK;
   m->mk_ok = true;
   return FLOCK_OK;
 }
