@@ -567,6 +567,7 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     from flock_b200.lib import GpuTensor
     from flock_b200.model import Model
 
+    n_prompt = len(prompt)
     dist.init_process_group("gloo", timeout=timedelta(seconds=120))
     uid = np.zeros(128, np.uint8)
     if rank == 0:
@@ -615,12 +616,12 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
             p = _abi.ptr(arr, _abi._i32p)
         _abi.call("flock_pipeline_step", M.handle, comm, p, n, sync, ctypes.byref(nxt))
 
-    pstep(prompt if rank == 0 else None, PROMPT, 1)
+    pstep(prompt if rank == 0 else None, n_prompt, 1)
     first = nxt.value
     for _ in range(args.warmup):
         pstep(None, 1, 0)
     dev.sync()
-    M.rewind(PROMPT)
+    M.rewind(n_prompt)
     if rank == 0:
         M.set_token(first)
     dist.barrier()
@@ -637,7 +638,7 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms_max = float(tt[0])
     # e2e: host loop through the API, id read back on rank 0 every token
-    M.rewind(PROMPT)
+    M.rewind(n_prompt)
     if rank == 0:
         M.set_token(first)
     dist.barrier()
@@ -652,8 +653,8 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     ms_e2e = float(tt[0])
     if rank == 0:
         tok_s = args.steps / (ms_max / 1000.0)
-        avg_keys = PROMPT + (args.steps - 1) / 2.0 + 1
-        tok_bytes = bytes_per_token(shape, avg_keys)
+        avg_keys = n_prompt + (args.steps - 1) / 2.0 + 1
+        tok_bytes = bytes_per_token(shape, avg_keys, 2 if args.kv == "bf16" else 4)
         token_gbs = tok_bytes * tok_s / 1e9
         out = {
             "metric": METRIC.replace("0.6B", "8B") if shape.n_layers == 36 else METRIC,
@@ -665,9 +666,9 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
                                    "pipelined: contiguous layer ranges "
                                    f"{ranges}{' (allocator)' if args.allocate else ''}, "
                                    "hidden state over "
-                                   "NCCL send/recv", "seed": SEED, "prompt": PROMPT,
-                       "attention": args.attention, "parallelism": f"pp{world}",
-                       "l2": "inputs larger than L2"},
+                                   "NCCL send/recv", "seed": SEED, "prompt": n_prompt,
+                       "attention": args.attention, "kv": args.kv,
+                       "parallelism": f"pp{world}", "l2": "inputs larger than L2"},
             # batch 1 keeps one stage busy at a time: the roofline is one GPU's
             "roofline": {"bound": "hbm", "achieved": token_gbs, "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": token_gbs / pk["hbm_gbs"], "traffic": None,
