@@ -182,6 +182,74 @@ def cpu_baseline(m, shape, n_tokens: int = 2) -> dict:
                       f"(oracle/flock_oracle.c, OpenMP over rows, {cores} threads)"}
 
 
+def oracle_ids(m, shape, prompt, n: int) -> list:
+    """The oracle's first n greedy ids for `prompt` (kernels/model.ts:387 step
+    composed from layer_ref.ts / head_ref.ts): the checker for the timed run."""
+    import oracle
+    oracle.set_threads(len(os.sched_getaffinity(0)))
+    cfg = dict(hidden=shape.hidden, n_heads=shape.n_heads, n_kv_heads=shape.n_kv_heads,
+               head_dim=shape.head_dim, ffn=shape.ffn)
+    layers = [oracle.RefLayer(w, cfg, len(prompt) + n + 1) for w in m.layers]
+    ids, cur = [], [int(t) for t in prompt]
+    for _ in range(n):
+        h = oracle.embed(m.embd["packed"], cur, shape.hidden)
+        for L in layers:
+            h = L.forward(h, len(cur))
+        tok, _, _ = oracle.head(h[(len(cur) - 1) * shape.hidden:], m.output_norm,
+                                m.embd["packed"], shape.vocab, shape.hidden)
+        ids.append(int(tok))
+        cur = [int(tok)]
+    return ids
+
+
+def config1_sweep(dev, pk) -> dict:
+    """Benchmark config 1: the Q8_0 / Q4_0 matmul over the model's projection
+    shapes.  M = 1 (and 16) through the decode GEMV, M in {16, 128, 512}
+    through the tcgen05 GEMM (f16 operands, f32 accumulation; the activation
+    conversion is timed apart); every launch timed alone after a 256 MiB L2
+    eviction, so the weights stream from HBM."""
+    from flock_b200 import lib as flib
+    from flock_b200 import ops, synth
+    from flock_b200 import _abi
+    import ctypes
+    shapes = [(2048, 1024), (1024, 1024), (1024, 2048), (3072, 1024), (1024, 3072),
+              (151936, 1024)]   # (rows N, cols K)
+    rows_out = []
+    for q8 in (True, False):
+        for n, k in shapes:
+            make = synth.q8_tensor if q8 else synth.q4_tensor
+            t = flib.GpuTensor.from_packed(dev, make(2, "t", n, k), n, k,
+                                           flib.FLOCK_Q8_0 if q8 else flib.FLOCK_Q4_0)
+            bpw = 1.0625 if q8 else 0.5625
+            for m_tok, eng in ((1, "gemv"), (16, "gemv"), (16, "tcgen05"), (128, "tcgen05"),
+                               (512, "tcgen05")):
+                ms = ctypes.c_float()
+                img = ctypes.c_float()
+                if eng == "gemv":
+                    _abi.call("flock_op_matvec_timed_cold", dev.handle, t.handle, m_tok, 10,
+                              ctypes.byref(ms))
+                else:
+                    _abi.call("flock_op_gemm_timed_cold", dev.handle, t.handle, m_tok, 10,
+                              ctypes.byref(ms), ctypes.byref(img))
+                b = n * k * bpw + 4 * k * m_tok + 4 * n * m_tok
+                gbs = b / (ms.value * 1e-3) / 1e9
+                tf = 2.0 * m_tok * n * k / (ms.value * 1e-3) / 1e12
+                r = {"wt": "Q8_0" if q8 else "Q4_0", "KxN": f"{k}x{n}", "M": m_tok,
+                     "engine": eng, "us": round(ms.value * 1000, 2), "GB_s": round(gbs, 1),
+                     "frac_hbm": round(gbs / pk["hbm_gbs"], 3), "TFLOP_s": round(tf, 2)}
+                if eng == "tcgen05":
+                    r["frac_bf16_peak"] = round(tf / pk["bf16_tflops"], 3)
+                    r["act_image_us"] = round(img.value * 1000, 2)
+                rows_out.append(r)
+            t.free()
+    return {"workload": "config 1: Q8_0/Q4_0 matmul sweep, K x N over the 0.6B projections "
+                        "and the 1024 x 151936 head, M in {1, 16} (GEMV) and {16, 128, 512} "
+                        "(tcgen05)",
+            "timing": "each launch alone after a 256 MiB L2 eviction, CUDA events, mean of 10",
+            "peak_hbm_gbs": pk["hbm_gbs"], "peak_bf16_tflops": pk["bf16_tflops"],
+            "rows": rows_out}
+
+
 def run_reference(args, rank: int, world: int) -> None:
     """--impl reference: the reference's CPU path (its strict-f32 TS oracle,
     restated in C: Deno is absent) on this config, on the host cores."""
@@ -248,8 +316,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="flock", choices=["flock", "reference"])
     ap.add_argument("--attention", default="fast", choices=["fast", "exact"])
-    ap.add_argument("--decode", default="kernels", choices=["persistent", "kernels"],
-                    help="one cooperative kernel per token, or the per-op kernel graph")
+    ap.add_argument("--decode", default="stream", choices=["stream", "persistent", "kernels"],
+                    help="stream: one cooperative kernel per token with the weights streamed "
+                         "through shared-memory rings (default); persistent: the kernel "
+                         "graph's kernels as phases of one cooperative kernel; kernels: the "
+                         "per-op kernel graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",
@@ -265,6 +336,14 @@ def main():
     ap.add_argument("--prompt", type=int, default=None,
                     help="prompt tokens before the timed decode (default 64; 4096 for 8b); "
                          "longer prompts prefill on the tensor cores")
+    ap.add_argument("--min-timed-s", type=float, default=1.5,
+                    help="repeat the K-step window (untimed rewind between) until the timed "
+                         "windows add up to this many seconds")
+    ap.add_argument("--no-oracle-ids", action="store_true",
+                    help="skip checking the first decode ids against the CPU oracle")
+    ap.add_argument("--sweep", action=argparse.BooleanOptionalAction, default=True,
+                    help="config 1: the Q8_0/Q4_0 GEMV and tensor-core GEMM sweep (L2 flushed "
+                         "before every timed launch)")
     ap.add_argument("--kv", default="f32", choices=["f32", "bf16"],
                     help="KV cache element type (bf16: half the KV bytes per token; the "
                          "tensor-core prefill and split-K decode attention)")
@@ -313,21 +392,42 @@ def main():
 
     M = Model.create(dev, m, cfg)
     M.decode_mode = args.decode
-    decode = M.decode_mode                # "kernels" when the shape rules the persistent kernel out
+    decode = M.decode_mode                # "kernels" when the shape rules the chosen engine out
     first = M.step(prompt)                # prefill (untimed)
     M.decode_device(args.warmup)          # warm-up steps
     M.rewind(n_prompt)
     M.set_token(first)
     dev.sync()
 
+    # The timed region: windows of exactly K device-fed steps (positions
+    # n_prompt .. n_prompt+K-1), each bracketed by CUDA events, repeated after
+    # an untimed rewind until the windows add up to >= min_timed_s, so the
+    # 200 ms clock sampler sees the GPU under load.
     clk = Clocks(gpu_index(local))
     clk.start()
-    dev.timer_start()
-    ids_dev = M.decode_device(args.steps)
-    ms = dev.timer_stop()
+    window_ms, ids_dev = [], None
+    while True:
+        dev.timer_start()
+        ids_w = M.decode_device(args.steps)
+        window_ms.append(dev.timer_stop())
+        if ids_dev is None:
+            ids_dev = ids_w
+        windows_same = bool(np.array_equal(ids_w, ids_dev))
+        if not windows_same or sum(window_ms) >= 1000.0 * args.min_timed_s:
+            break
+        M.rewind(n_prompt)
+        M.set_token(first)
     clocks = clk.stop()
+    ms = sum(window_ms) / len(window_ms)   # per K-step window
     tok_s = args.steps / (ms / 1000.0)
-    log(f"decode: {args.steps} tokens in {ms:.2f} ms -> {tok_s:.1f} tok/s; clocks {clocks}")
+    log(f"decode: {len(window_ms)} windows of {args.steps} tokens, {ms:.3f} ms per window -> "
+        f"{tok_s:.1f} tok/s; clocks {clocks}")
+    ids_oracle = None
+    if not args.no_oracle_ids:
+        n_chk = min(4, args.steps)
+        ids_oracle = oracle_ids(m, shape, prompt, n_chk + 1)
+        ids_match = ids_oracle == [first] + ids_dev[:n_chk].tolist()
+        log(f"oracle ids {ids_oracle}: match {ids_match}")
 
     # end to end through the public API, host loop
     e2e = None
@@ -355,21 +455,26 @@ def main():
     kv_elem = 2 if args.kv == "bf16" else 4
     tok_bytes = bytes_per_token(shape, avg_keys, kv_elem)
     token_gbs = tok_bytes * tok_s / 1e9
-    if decode == "persistent":
-        # one k_decode_mk launch per token: its algorithmic bytes are the token's
+    # roofline: the whole decode token -- every weight byte and K/V row it
+    # reads (bytes_per_token) over the measured time per token; for the
+    # single-launch engines that is exactly one kernel launch
+    if decode in ("stream", "persistent"):
         launches_per_token = 1
-        roofline = {"bound": "hbm", "achieved": token_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                    "frac": token_gbs / pk["hbm_gbs"],
-                    "traffic": traffic_from_profile("decode_persistent_traffic.txt"),
-                    "kernel": "k_decode_mk, one cooperative launch per token",
-                    "bytes_per_launch": tok_bytes, "ms_per_launch": ms / args.steps,
-                    "peak_src": pk["src"]}
+        kernel = ("k_decode_stream, one cooperative launch per token (weights streamed "
+                  "through shared-memory rings)" if decode == "stream" else
+                  "k_decode_mk, one cooperative launch per token")
+        traffic = traffic_from_profile(f"decode_{decode}_traffic.txt")
     else:
         launches_per_token = 1 + shape.n_layers * (5 if args.attention == "fast" else 6) + 2
-        roofline = {"bound": "hbm", "achieved": head_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                    "frac": head_gbs / pk["hbm_gbs"], "traffic": traffic_from_profile(),
-                    "kernel": "k_gemv<Q8,R2,STORE> on the 151936x1024 head, 165.3 MB per launch",
-                    "ms_per_launch": head_ms, "peak_src": pk["src"]}
+        kernel = (f"the kernel graph's {launches_per_token} launches per token (k_embed, "
+                  "per layer 4 k_gemv + attention, head k_gemv + argmax, k_record)")
+        traffic = None
+    roofline = {"bound": "hbm", "achieved": token_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": token_gbs / pk["hbm_gbs"], "traffic": traffic, "kernel": kernel,
+                "bytes_per_launch": tok_bytes / launches_per_token if launches_per_token == 1
+                else None,
+                "bytes_per_token": tok_bytes, "ms_per_token": ms / args.steps,
+                "peak_src": pk["src"], "peak_note": "measured copy bandwidth (burst)"}
 
     out = {
         "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
@@ -384,16 +489,26 @@ def main():
                    "seed": SEED, "prompt": n_prompt, "attention": args.attention,
                    "kv": args.kv, "decode": decode,
                    "l2": "inputs larger than L2: 692 MB of weights streamed per token",
-                   "timing": "CUDA events around K device-fed decode steps"},
+                   "timing": f"CUDA events around each window of K device-fed decode "
+                             f"steps; {len(window_ms)} windows (untimed rewind between) so the "
+                             f"timed region spans {sum(window_ms) / 1000:.2f} s",
+                   "windows": len(window_ms), "windows_same_ids": windows_same},
         "roofline": roofline,
         "head_gemv": {"achieved": head_gbs, "unit": "GB/s", "ms_per_launch": head_ms,
-                      "frac": head_gbs / pk["hbm_gbs"]},
+                      "frac": head_gbs / pk["hbm_gbs"],
+                      "traffic": traffic_from_profile(),
+                      "kernel": "k_gemv<Q8,R2,ARGMAX> on the 151936x1024 head timed alone"},
         "token_roofline": {"achieved": token_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                            "frac": token_gbs / pk["hbm_gbs"],
                            "bytes_per_token": tok_bytes, "avg_keys": avg_keys},
         "clocks": clocks,
-        "gpu_launches": launches_per_token * args.steps,
+        "gpu_launches": launches_per_token * args.steps * len(window_ms),
     }
+    if ids_oracle is not None:
+        out["ids_match_oracle"] = ids_match
+        out["ids_checked"] = len(ids_oracle)
+    if args.sweep:
+        out["config1_sweep"] = config1_sweep(dev, pk)
     if e2e:
         out["e2e"] = e2e
     if not args.no_prefill:

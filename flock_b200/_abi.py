@@ -80,8 +80,10 @@ SIGNATURES = {
     "flock_tensor_bytes": [_vp, _i64p],
     "flock_op_matvec": [_vp, _vp, _fp, _i, _fp],
     "flock_op_matvec_timed": [_vp, _vp, _i, _i, _fp],
+    "flock_op_matvec_timed_cold": [_vp, _vp, _i, _i, _fp],
     "flock_op_gemm": [_vp, _vp, _fp, _i, _fp],
     "flock_op_gemm_timed": [_vp, _vp, _i, _i, _fp, _fp],
+    "flock_op_gemm_timed_cold": [_vp, _vp, _i, _i, _fp, _fp],
     "flock_op_rmsnorm": [_vp, _fp, _fp, _i, _i, _f, _fp],
     "flock_op_rope": [_vp, _fp, _i, _i, _i, _i, _fp, _i, _fp],
     "flock_op_swiglu": [_vp, _fp, _fp, _i64, _fp],

@@ -930,8 +930,8 @@ int flock_op_matvec(flock_dev* d, const flock_tensor* w, const float* x, int n_t
   return FLOCK_OK;
 }
 
-int flock_op_matvec_timed(flock_dev* d, const flock_tensor* w, int n_tokens, int iters,
-                          float* ms_per_call) {
+static int matvec_timed(flock_dev* d, const flock_tensor* w, int n_tokens, int iters, bool cold,
+                        float* ms_per_call) {
   if (!d || !w || n_tokens < 1 || iters < 1 || !ms_per_call || w->dtype == FLOCK_F32)
     return FLOCK_E_ARG;
   FLOCK_CK(cudaSetDevice(d->ordinal));
@@ -955,14 +955,42 @@ int flock_op_matvec_timed(flock_dev* d, const flock_tensor* w, int n_tokens, int
   a.x_stride = (int)w->cols;
   const int qt = w->dtype == FLOCK_Q8_0 ? QT_Q8 : QT_Q4;
   FLOCK_TRY(launch_gemv(d, qt, EPI_STORE, a, false));  // warm-up
-  FLOCK_CK(cudaEventRecord(d->t0, d->stream));
-  for (int i = 0; i < iters; i++) FLOCK_TRY(launch_gemv(d, qt, EPI_STORE, a, true));
-  FLOCK_CK(cudaEventRecord(d->t1, d->stream));
-  FLOCK_CK(cudaEventSynchronize(d->t1));
-  float ms = 0;
-  FLOCK_CK(cudaEventElapsedTime(&ms, d->t0, d->t1));
-  *ms_per_call = ms / iters;
+  if (!cold) {
+    FLOCK_CK(cudaEventRecord(d->t0, d->stream));
+    for (int i = 0; i < iters; i++) FLOCK_TRY(launch_gemv(d, qt, EPI_STORE, a, true));
+    FLOCK_CK(cudaEventRecord(d->t1, d->stream));
+    FLOCK_CK(cudaEventSynchronize(d->t1));
+    float ms = 0;
+    FLOCK_CK(cudaEventElapsedTime(&ms, d->t0, d->t1));
+    *ms_per_call = ms / iters;
+    return FLOCK_OK;
+  }
+  // cold: evict L2 with a 256 MiB write before each launch, time each alone
+  DBuf flush;
+  FLOCK_TRY(flush.alloc((size_t)256 << 20));
+  float total = 0;
+  for (int i = 0; i < iters; i++) {
+    FLOCK_CK(cudaMemsetAsync(flush.p, i & 0xff, flush.bytes, d->stream));
+    FLOCK_CK(cudaEventRecord(d->t0, d->stream));
+    FLOCK_TRY(launch_gemv(d, qt, EPI_STORE, a, false));
+    FLOCK_CK(cudaEventRecord(d->t1, d->stream));
+    FLOCK_CK(cudaEventSynchronize(d->t1));
+    float ms = 0;
+    FLOCK_CK(cudaEventElapsedTime(&ms, d->t0, d->t1));
+    total += ms;
+  }
+  *ms_per_call = total / iters;
   return FLOCK_OK;
+}
+
+int flock_op_matvec_timed(flock_dev* d, const flock_tensor* w, int n_tokens, int iters,
+                          float* ms_per_call) {
+  return matvec_timed(d, w, n_tokens, iters, false, ms_per_call);
+}
+
+int flock_op_matvec_timed_cold(flock_dev* d, const flock_tensor* w, int n_tokens, int iters,
+                               float* ms_per_call) {
+  return matvec_timed(d, w, n_tokens, iters, true, ms_per_call);
 }
 
 int flock_op_rmsnorm(flock_dev* d, const float* x, const float* g, int n, int n_vecs, float eps,

@@ -149,6 +149,12 @@ FLOCK_API int flock_op_matvec(flock_dev* dev, const flock_tensor* w, const float
  * writes the mean milliseconds per launch. */
 FLOCK_API int flock_op_matvec_timed(flock_dev* dev, const flock_tensor* w, int n_tokens, int iters,
                                     float* ms_per_call);
+/* The same launch timed cold: before each of the `iters` launches a 256 MiB
+ * device write evicts L2 (126 MB), so the weights stream from HBM; each
+ * launch is CUDA-event timed alone; writes the mean milliseconds.  (A
+ * measurement aid like bench.ts:195; allocates its scratch.) */
+FLOCK_API int flock_op_matvec_timed_cold(flock_dev* dev, const flock_tensor* w, int n_tokens,
+                                         int iters, float* ms_per_call);
 /* The prefill matmul of layer.ts:685 encodePrefill (q8_coop.wgsl:76 /
  * q4_coop.wgsl:48 over M tokens) on the tcgen05 tensor cores: y[m][r] =
  * W x[m] with s * q and x (scaled per row by a power of two) rounded to f16
@@ -161,6 +167,10 @@ FLOCK_API int flock_op_gemm(flock_dev* dev, const flock_tensor* w, const float* 
  * kernel and of the activation conversion before it. */
 FLOCK_API int flock_op_gemm_timed(flock_dev* dev, const flock_tensor* w, int M, int iters,
                                   float* ms_per_call, float* ms_image);
+/* flock_op_gemm_timed with L2 evicted (256 MiB device write) before each
+ * call, as flock_op_matvec_timed_cold. */
+FLOCK_API int flock_op_gemm_timed_cold(flock_dev* dev, const flock_tensor* w, int M, int iters,
+                                       float* ms_per_call, float* ms_image);
 /* kernels/rmsnorm.wgsl:41: n_vecs vectors of width n. */
 FLOCK_API int flock_op_rmsnorm(flock_dev* dev, const float* x, const float* g, int n, int n_vecs, float eps,
                      float* out);

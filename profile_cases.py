@@ -1,20 +1,20 @@
 """Small, fixed GPU workloads for profiling one kernel family at a time.
 
-    python -m flock_b200.cases layer [--time]   # one decode layer (config 0 shape, 256-key cache)
-    python -m flock_b200.cases head  [--time]   # the 151936 x 1024 Q8_0 head matvec
-    python -m flock_b200.cases gemv  [--time] [--8b]
+    python profile_cases.py layer [--time]   # one decode layer (config 0 shape, 256-key cache)
+    python profile_cases.py head  [--time]   # the 151936 x 1024 Q8_0 head matvec
+    python profile_cases.py gemv  [--time] [--8b]
                                                 # the config 1 matvec sweep (M = 1), or the
                                                 # 8B shapes (config 4)
-    python -m flock_b200.cases sweep [--time]   # config 1: Q8_0/Q4_0 x shapes x M in {1,16,128,512}
-    python -m flock_b200.cases gemm  [--time] [rows cols [M]]
+    python profile_cases.py sweep [--time]   # config 1: Q8_0/Q4_0 x shapes x M in {1,16,128,512}
+    python profile_cases.py gemm  [--time] [rows cols [M]]
                                                 # one tensor-core GEMM (default 3072 x 1024, M 512)
-    python -m flock_b200.cases model [--time] [--kernels] [--trace]
-    python -m flock_b200.cases model8b [--time] [--prompt P] [--decode N] [--persistent]
+    python profile_cases.py model [--time] [--kernels] [--trace]
+    python profile_cases.py model8b [--time] [--prompt P] [--decode N] [--persistent]
                                                 # config 4 on one GPU: Qwen3-8B shape, 36
                                                 # layers, untied head; 4096-token prompt
                                                 # (tensor-core prefill, 512-token chunks), then
                                                 # N (default 512) greedy decode tokens
-    python -m flock_b200.cases prefill [--time] [--exact]
+    python profile_cases.py prefill [--time] [--exact]
                                                 # config 3: 512-token prompt TTFT on the
                                                 # 28-layer model, tensor-core (default) or
                                                 # exact prefill, then 32 decode tokens
@@ -30,9 +30,13 @@ from __future__ import annotations
 
 import sys
 
-from . import ops, synth
-from . import lib as flib
-from .layer import QWEN3_06B, Layer
+import os
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+from flock_b200 import ops, synth  # noqa: E402
+from flock_b200 import lib as flib  # noqa: E402
+from flock_b200.layer import QWEN3_06B, Layer  # noqa: E402
 
 SWEEP = [(2048, 1024), (1024, 1024), (1024, 2048), (3072, 1024), (1024, 3072), (151936, 1024)]
 SWEEP_8B = [(4096, 4096), (1024, 4096), (12288, 4096), (4096, 12288), (151936, 4096)]
@@ -126,7 +130,7 @@ def gemm_case(timed: bool) -> None:
 
 
 def prefill_case(timed: bool) -> None:
-    from .model import Model
+    from flock_b200.model import Model
     dev = flib.get_device(0)
     m = synth.model(300)
     exact = "--exact" in sys.argv
@@ -151,8 +155,8 @@ def prefill_case(timed: bool) -> None:
 
 def model8b_case(timed: bool) -> None:
     import time
-    from .layer import LayerConfig
-    from .model import Model
+    from flock_b200.layer import LayerConfig
+    from flock_b200.model import Model
     s = synth.QWEN3_8B
     n_prompt = 4096
     n_dec = 512
@@ -227,7 +231,7 @@ def trace_summary(tr, n_layers: int) -> str:
 
 
 def model_case(timed: bool) -> None:
-    from .model import Model
+    from flock_b200.model import Model
     dev = flib.get_device(0)
     m = synth.model(300)
     M = Model.create(dev, m, QWEN3_06B.with_(attention="fast"))
