@@ -25,7 +25,8 @@ FLOCK_E_UNSUPPORTED = -8
 FLOCK_Q8_0, FLOCK_Q4_0, FLOCK_F32 = 8, 4, 32
 FLOCK_ROPE_NEOX, FLOCK_ROPE_NORM = 0, 1
 FLOCK_ATTN_EXACT, FLOCK_ATTN_FAST = 0, 1
-FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT, FLOCK_DECODE_EAGER = 0, 1, 2
+FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT, FLOCK_DECODE_EAGER, FLOCK_DECODE_STREAM = \
+    0, 1, 2, 3
 FLOCK_PREFILL_EXACT, FLOCK_PREFILL_TENSOR = 0, 1
 FLOCK_KV_F32, FLOCK_KV_BF16 = 0, 1
 FLOCK_TP_NCCL, FLOCK_TP_PEER = 0, 1

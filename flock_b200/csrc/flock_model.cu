@@ -14,6 +14,7 @@
 
 #include "decode_mk.cuh"
 #include "flock_internal.h"
+#include "stream_engine.h"
 #include "gemv.cuh"
 #include "ops.cuh"
 
@@ -38,6 +39,8 @@ struct flock_model {
   MkArgs mk{};
   size_t mk_smem = 0;
   int mk_grid = 0;
+  // streaming persistent decode kernel (weights through shared-memory rings)
+  StEngine st;
   // tensor parallel: this rank holds vocab rows [tp_start[r], tp_start[r+1])
   // of the head; layers exchange partials over `tp`
   flock_comm* tp = nullptr;
@@ -427,6 +430,47 @@ int mk_prepare(flock_model* m) {
   return FLOCK_OK;
 }
 
+// The streaming engine's description of this model (once per model).
+int st_prepare(flock_model* m) {
+  const flock_layer_config& c = m->cfg;
+  if (c.attention != FLOCK_ATTN_FAST) {
+    m->st.why = "needs fast (split-K) attention";
+    return FLOCK_OK;
+  }
+  if (m->tp || !m->embd || !m->head || m->held < 1 || m->held != m->n_layers) {
+    m->st.why = "needs a whole single-GPU model with its embedding and head";
+    return FLOCK_OK;
+  }
+  StModelDesc d;
+  d.H = c.hidden;
+  d.nH = c.n_heads;
+  d.nKV = c.n_kv_heads;
+  d.hd = c.head_dim;
+  d.F = c.ffn;
+  d.vocab = m->vocab;
+  d.n_layers = m->held;
+  d.eps = c.eps;
+  d.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
+  d.kv_bf16 = c.kv_dtype == FLOCK_KV_BF16;
+  for (int i = 0; i < m->held; i++) {
+    flock_layer* L = m->layers[i];
+    for (int t = 0; t < W_COUNT; t++) d.w.push_back(L->w[t]);
+    d.kcache.push_back(L->kcache.p);
+    d.vcache.push_back(L->vcache.p);
+  }
+  d.embd = m->embd;
+  d.head = m->head;
+  d.out_norm = m->out_norm;
+  d.inv_freq = m->layers[0]->inv_freq.as<float>();
+  d.h_out = m->ws.h.as<float>();
+  d.logits = m->logits.as<float>();
+  d.ids = m->ids.as<int32_t>();
+  d.hist = m->hist.as<int32_t>();
+  d.hist_cap = c.max_keys;
+  d.ctl = m->ctl.as<int>();
+  return stream_prepare(m->dev, d, &m->st);
+}
+
 int enqueue_mk(flock_model* m) {
   FLOCK_CK(cudaMemsetAsync(m->mk_bar.p, 0, 4, m->dev->stream));
   cudaLaunchConfig_t cfg = {};
@@ -448,6 +492,7 @@ int enqueue_mk(flock_model* m) {
 int check_device_errors(flock_model* m) {
   FLOCK_TRY(ws_check_errors(&m->ws));
   FLOCK_TRY(peer_xchg_check(m->xchg));
+  if (m->decode_mode == FLOCK_DECODE_STREAM) return stream_check(&m->st);
   if (!m->mk_ok || m->decode_mode != FLOCK_DECODE_PERSISTENT) return FLOCK_OK;
   int err = 0;
   FLOCK_CK(cudaMemcpy(&err, m->mk_err.p, 4, cudaMemcpyDeviceToHost));
@@ -492,6 +537,7 @@ int capture_decode(flock_model* m) {
 // barrier reset plus one cooperative launch; no graph, so profilers see the
 // kernel) or the captured kernel graph.
 int launch_decode(flock_model* m) {
+  if (m->decode_mode == FLOCK_DECODE_STREAM && m->st.ok) return stream_launch(&m->st, m->dev->stream);
   if (m->decode_mode == FLOCK_DECODE_PERSISTENT && m->mk_ok) return enqueue_mk(m);
   if (m->decode_mode == FLOCK_DECODE_EAGER) {
     FLOCK_TRY(enqueue_embed(m, 1));
@@ -600,6 +646,7 @@ int model_build(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_
     for (auto* L : m->layers) L->xchg = m->xchg;
   }
   if ((rc = mk_prepare(m))) return fail(rc);
+  if ((rc = st_prepare(m))) return fail(rc);
   *out = m;
   return FLOCK_OK;
 }
@@ -640,7 +687,7 @@ int flock_model_create_tp(flock_dev* dev, const flock_layer_config* cfg, int voc
 
 int flock_model_set_decode_mode(flock_model* m, int mode) {
   if (!m || (mode != FLOCK_DECODE_KERNELS && mode != FLOCK_DECODE_PERSISTENT &&
-             mode != FLOCK_DECODE_EAGER))
+             mode != FLOCK_DECODE_EAGER && mode != FLOCK_DECODE_STREAM))
     return FLOCK_E_ARG;
   if (mode != m->decode_mode && m->decode_graph) {
     cudaStreamSynchronize(m->dev->stream);
@@ -653,6 +700,7 @@ int flock_model_set_decode_mode(flock_model* m, int mode) {
 
 int flock_model_trace(flock_model* m, int enable) {
   if (!m) return FLOCK_E_ARG;
+  if (m->decode_mode == FLOCK_DECODE_STREAM && m->st.ok) return stream_trace(&m->st, enable != 0);
   if (!m->mk_ok) {
     set_error("phase tracing needs the persistent decode kernel, which this model cannot run");
     return FLOCK_E_UNSUPPORTED;
@@ -668,6 +716,16 @@ int flock_model_trace(flock_model* m, int enable) {
 
 int flock_model_trace_read(flock_model* m, uint64_t* out, int64_t cap, int* n_ctas, int* stride) {
   if (!m || !n_ctas || !stride) return FLOCK_E_ARG;
+  if (m->decode_mode == FLOCK_DECODE_STREAM && m->st.ok) {
+    *n_ctas = m->st.grid;
+    *stride = stream_trace_stride(&m->st);
+    const int64_t n = (int64_t)*n_ctas * *stride;
+    if (!m->st.trace.p) return FLOCK_E_STATE;
+    if (!out || cap < n) return FLOCK_E_LIMIT;
+    FLOCK_TRY(sync_model(m));
+    FLOCK_CK(cudaMemcpy(out, m->st.trace.p, (size_t)n * 8, cudaMemcpyDeviceToHost));
+    return FLOCK_OK;
+  }
   *n_ctas = m->mk_grid;
   *stride = mk_trace_stride(m->held);
   const int64_t n = (int64_t)m->mk_grid * *stride;
@@ -706,8 +764,10 @@ int flock_model_get_tp_exchange(const flock_model* m, int* mode) {
 
 int flock_model_get_decode_mode(const flock_model* m, int* mode) {
   if (!m || !mode) return FLOCK_E_ARG;
-  *mode = (m->decode_mode == FLOCK_DECODE_PERSISTENT && !m->mk_ok) ? FLOCK_DECODE_KERNELS
-                                                                   : m->decode_mode;
+  *mode = ((m->decode_mode == FLOCK_DECODE_PERSISTENT && !m->mk_ok) ||
+           (m->decode_mode == FLOCK_DECODE_STREAM && !m->st.ok))
+              ? FLOCK_DECODE_KERNELS
+              : m->decode_mode;
   return FLOCK_OK;
 }
 

@@ -206,12 +206,14 @@ class Model:
         return n.value
 
     _MODES = {"kernels": _abi.FLOCK_DECODE_KERNELS, "persistent": _abi.FLOCK_DECODE_PERSISTENT,
-              "eager": _abi.FLOCK_DECODE_EAGER}
+              "eager": _abi.FLOCK_DECODE_EAGER, "stream": _abi.FLOCK_DECODE_STREAM}
 
     @property
     def decode_mode(self) -> str:
         """"kernels" (the captured kernel graph), "persistent" (one cooperative
-        kernel per token) or "eager" (the kernels launched from the host)."""
+        kernel per token), "stream" (one cooperative kernel per token with the
+        weights streamed through shared-memory rings) or "eager" (the kernels
+        launched from the host)."""
         n = ctypes.c_int()
         _abi.call("flock_model_get_decode_mode", self.handle, ctypes.byref(n))
         return {v: k for k, v in self._MODES.items()}[n.value]

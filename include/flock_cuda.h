@@ -317,10 +317,16 @@ FLOCK_API int flock_model_held(const flock_model* m, int* out);
 #define FLOCK_DECODE_KERNELS 0    /* one kernel per op, CUDA graph + PDL */
 #define FLOCK_DECODE_PERSISTENT 1 /* one cooperative persistent kernel per token */
 #define FLOCK_DECODE_EAGER 2      /* one kernel per op, launched from the host each step */
+#define FLOCK_DECODE_STREAM 3     /* one cooperative kernel per token, weights streamed
+                                     through shared-memory rings */
 /* Choose the decode engine for single-token steps (default: the kernel
- * graph).  The persistent kernel needs fast attention, Q8_0 weights, head_dim
- * 128 and a resident embedding/head; otherwise the kernel graph runs and
- * flock_model_get_decode_mode reports it.  Both give bit-identical results. */
+ * graph).  The persistent and streaming kernels need fast attention, Q8_0
+ * weights, head_dim 128, a GQA group of at most 4 and a whole single-GPU
+ * model with its embedding/head; otherwise the kernel graph runs and
+ * flock_model_get_decode_mode reports it.  The persistent kernel is
+ * bit-identical to the graph; the streaming kernel's matvecs are too (same
+ * coop(64) order), its split-K attention uses 32-key splits (a different
+ * reassociation of the softmax, within the same tolerance of attnRef). */
 FLOCK_API int flock_model_set_decode_mode(flock_model* m, int mode);
 FLOCK_API int flock_model_get_decode_mode(const flock_model* m, int* mode);
 /* Phase trace of the persistent decode kernel (a profiling aid with no

