@@ -316,11 +316,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="flock", choices=["flock", "reference"])
     ap.add_argument("--attention", default="fast", choices=["fast", "exact"])
-    ap.add_argument("--decode", default="stream", choices=["stream", "persistent", "kernels"],
-                    help="stream: one cooperative kernel per token with the weights streamed "
-                         "through shared-memory rings (default); persistent: the kernel "
-                         "graph's kernels as phases of one cooperative kernel; kernels: the "
-                         "per-op kernel graph")
+    ap.add_argument("--decode", default="kernels", choices=["stream", "persistent", "kernels"],
+                    help="kernels: the per-op kernel graph (default, the fastest measured); "
+                         "stream: one cooperative kernel per token for the layers with the "
+                         "weights streamed through shared-memory rings, then the head GEMV; "
+                         "persistent: the kernel graph's kernels as phases of one cooperative "
+                         "kernel")
+    ap.add_argument("--also-stream", action=argparse.BooleanOptionalAction, default=True,
+                    help="also time the streaming engine on the same workload (its own key)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",
@@ -422,6 +425,33 @@ def main():
     tok_s = args.steps / (ms / 1000.0)
     log(f"decode: {len(window_ms)} windows of {args.steps} tokens, {ms:.3f} ms per window -> "
         f"{tok_s:.1f} tok/s; clocks {clocks}")
+    stream_line = None
+    if args.also_stream and decode != "stream":
+        # the streaming engine on the same model and positions, its own windows
+        M.decode_mode = "stream"
+        if M.decode_mode == "stream":
+            M.rewind(n_prompt)
+            M.set_token(first)
+            M.decode_device(args.warmup)
+            sw = []
+            ids_s = None
+            while sum(sw) < 1000.0 * args.min_timed_s / 2:
+                M.rewind(n_prompt)
+                M.set_token(first)
+                dev.timer_start()
+                ids_w = M.decode_device(args.steps)
+                sw.append(dev.timer_stop())
+                ids_s = ids_w if ids_s is None else ids_s
+            ms_s = sum(sw) / len(sw)
+            stream_line = {"value": args.steps / (ms_s / 1000.0), "unit": "tok/s",
+                           "ms_per_step": ms_s / args.steps, "windows": len(sw),
+                           "ids_match_kernels": bool(np.array_equal(ids_s, ids_dev)),
+                           "engine": "k_decode_stream (28 layers, one cooperative launch) + "
+                                     "the head k_gemv launch"}
+            log(f"stream engine: {stream_line}")
+        M.decode_mode = decode
+        M.rewind(n_prompt)
+        M.set_token(first)
     ids_oracle = None
     if not args.no_oracle_ids:
         n_chk = min(4, args.steps)
@@ -504,6 +534,8 @@ def main():
         "clocks": clocks,
         "gpu_launches": launches_per_token * args.steps * len(window_ms),
     }
+    if stream_line:
+        out["stream_engine"] = stream_line
     if ids_oracle is not None:
         out["ids_match_oracle"] = ids_match
         out["ids_checked"] = len(ids_oracle)

@@ -85,6 +85,7 @@ SIGNATURES = {
     "flock_op_gemm": [_vp, _vp, _fp, _i, _fp],
     "flock_op_gemm_timed": [_vp, _vp, _i, _i, _fp, _fp],
     "flock_op_gemm_timed_cold": [_vp, _vp, _i, _i, _fp, _fp],
+    "flock_op_peer_exchange_lone": [_vp, _i, ctypes.c_int64, _i, _i, ctypes.POINTER(ctypes.c_int)],
     "flock_op_rmsnorm": [_vp, _fp, _fp, _i, _i, _f, _fp],
     "flock_op_rope": [_vp, _fp, _i, _i, _i, _i, _fp, _i, _fp],
     "flock_op_swiglu": [_vp, _fp, _fp, _i64, _fp],

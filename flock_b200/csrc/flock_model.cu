@@ -467,6 +467,7 @@ int st_prepare(flock_model* m) {
   d.ids = m->ids.as<int32_t>();
   d.hist = m->hist.as<int32_t>();
   d.hist_cap = c.max_keys;
+  d.max_keys = c.max_keys;
   d.ctl = m->ctl.as<int>();
   return stream_prepare(m->dev, d, &m->st);
 }
@@ -537,7 +538,14 @@ int capture_decode(flock_model* m) {
 // barrier reset plus one cooperative launch; no graph, so profilers see the
 // kernel) or the captured kernel graph.
 int launch_decode(flock_model* m) {
-  if (m->decode_mode == FLOCK_DECODE_STREAM && m->st.ok) return stream_launch(&m->st, m->dev->stream);
+  if (m->decode_mode == FLOCK_DECODE_STREAM && m->st.ok) {
+    // the layers in one streaming launch, then the graph's head GEMV (its
+    // 296-CTA register-pipelined stream beats the persistent grid's 148 CTAs
+    // on the 165 MB head) with the fused argmax, and the history record
+    FLOCK_TRY(stream_launch(&m->st, m->dev->stream));
+    FLOCK_TRY(enqueue_head(m, 0));
+    return enqueue_record(m);
+  }
   if (m->decode_mode == FLOCK_DECODE_PERSISTENT && m->mk_ok) return enqueue_mk(m);
   if (m->decode_mode == FLOCK_DECODE_EAGER) {
     FLOCK_TRY(enqueue_embed(m, 1));

@@ -37,7 +37,9 @@ struct PeerXchg {
   float** d_bufs = nullptr;        // [n] device pointers (own or mapped)
   uint32_t** d_flags = nullptr;    // [n]
   uint32_t* epoch = nullptr;       // exchanges completed, per exchange CTA
-  int* err = nullptr;              // 3 = a peer never published
+  int* err = nullptr;              // 3 = a peer never published (sticky: never cleared)
+  uint64_t wait_ns = WAIT_NS;      // how long a CTA waits for the peers' flags
+  bool failed = false;             // a wait ran out: every later exchange is refused
 };
 
 namespace {
@@ -61,13 +63,21 @@ __global__ void __launch_bounds__(XCHG_THREADS) k_peer_xchg(const float* __restr
                                                             int n_ranks, int64_t cap,
                                                             float* const* bufs,
                                                             uint32_t* const* flags,
-                                                            uint32_t* epochs, int* err) {
+                                                            uint32_t* epochs, int* err,
+                                                            uint64_t wait_ns) {
   __shared__ uint32_t s_epoch;
   __shared__ int s_ok;
   const int t = threadIdx.x, c = blockIdx.x;
   const int i = c * XCHG_CHUNK + 4 * t;  // n is a multiple of 4
-  if (t == 0) s_epoch = epochs[c] + 1u;
+  if (t == 0) {
+    s_epoch = epochs[c] + 1u;
+    // after a timeout this rank's epochs no longer match its peers': stop
+    // exchanging for good (graph replays included) rather than sum partials
+    // of another step
+    s_ok = *(volatile int*)err == 0;
+  }
   __syncthreads();
+  if (!s_ok) return;
   const uint32_t e = s_epoch, slot = e & 1u;
   const bool mine = i < n;
   float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -99,7 +109,7 @@ __global__ void __launch_bounds__(XCHG_THREADS) k_peer_xchg(const float* __restr
         if ((k & 63) != 63) continue;
         const uint64_t now = globaltimer_ns();
         if (!t0) t0 = now;
-        if (now - t0 > WAIT_NS || k >= WAIT_MAX_POLLS) {
+        if (now - t0 > wait_ns || k >= WAIT_MAX_POLLS) {
           atomicExch(err, 3);
           ok = 0;
           break;
@@ -235,6 +245,11 @@ int peer_xchg_init(flock_comm* c, int64_t cap, PeerXchg** out) {
 }
 
 int peer_xchg_run(PeerXchg* x, cudaStream_t st, float* h, const float* part, int64_t n) {
+  if (x->failed) {
+    set_error("tensor-parallel peer exchange failed earlier (a rank gave up waiting); free the "
+              "model and set the exchange up again");
+    return FLOCK_E_CUDA;
+  }
   const int64_t ctas = (n + XCHG_CHUNK - 1) / XCHG_CHUNK;
   if (n > x->cap || n % 4 || ctas > XCHG_MAX_CTAS) {
     set_error("peer exchange of %lld floats: at most %lld (and %d per CTA x %d), a multiple of 4",
@@ -242,21 +257,92 @@ int peer_xchg_run(PeerXchg* x, cudaStream_t st, float* h, const float* part, int
     return FLOCK_E_LIMIT;
   }
   k_peer_xchg<<<(unsigned)ctas, XCHG_THREADS, 0, st>>>(part, h, (int)n, x->rank, x->n, x->cap,
-                                                       x->d_bufs, x->d_flags, x->epoch, x->err);
+                                                       x->d_bufs, x->d_flags, x->epoch, x->err,
+                                                       x->wait_ns);
   FLOCK_CK(cudaGetLastError());
   return FLOCK_OK;
 }
 
+// The device error word is sticky: once a wait ran out, this rank is an
+// exchange behind (or ahead of) its peers, so every later check (and every
+// later exchange) fails until the exchange is freed and set up again.
 int peer_xchg_check(PeerXchg* x) {
   if (!x) return FLOCK_OK;
-  int e = 0;
-  FLOCK_CK(cudaMemcpy(&e, x->err, 4, cudaMemcpyDeviceToHost));
-  if (e) {
-    set_error("tensor-parallel peer exchange gave up waiting for a rank");
-    cudaMemset(x->err, 0, 4);
+  if (!x->failed) {
+    int e = 0;
+    FLOCK_CK(cudaMemcpy(&e, x->err, 4, cudaMemcpyDeviceToHost));
+    x->failed = e != 0;
+  }
+  if (x->failed) {
+    set_error("tensor-parallel peer exchange gave up waiting for a rank; it stays failed until "
+              "the model is freed and the exchange set up again");
     return FLOCK_E_CUDA;
   }
   return FLOCK_OK;
 }
+
+}  // namespace flock
+
+using namespace flock;
+
+extern "C" {
+
+// One rank of an n_ranks exchange whose peers never publish (their buffers
+// and flags are local allocations nothing writes): `calls` exchanges of n
+// floats with a wait limit of wait_ms, each followed by the host check.
+// Returns the last call's status (its message in flock_last_error): the
+// first call gives up waiting, every later one is refused.  A test of the
+// bounded wait and of the sticky failure that needs no second GPU.
+int flock_op_peer_exchange_lone(flock_dev* d, int n_ranks, int64_t n, int wait_ms, int calls,
+                                int* first_status) {
+  if (!d || n_ranks < 2 || n_ranks > 8 || n < 4 || n % 4 || n > XCHG_CHUNK * XCHG_MAX_CTAS ||
+      wait_ms < 1 || wait_ms > 2000 || calls < 1 || calls > 8)
+    return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  PeerXchg x;
+  x.rank = 0;
+  x.n = n_ranks;
+  x.cap = n;
+  x.wait_ns = (uint64_t)wait_ms * 1000000ull;
+  DBuf bufs, flags, tab, epoch, err, part, h;
+  const size_t buf_bytes = (size_t)2 * n_ranks * n * 4;
+  const size_t flag_bytes = (size_t)2 * n_ranks * XCHG_MAX_CTAS * 4;
+  FLOCK_TRY(bufs.alloc(buf_bytes * n_ranks));
+  FLOCK_TRY(flags.alloc(flag_bytes * n_ranks));
+  FLOCK_TRY(tab.alloc((size_t)2 * n_ranks * sizeof(void*)));
+  FLOCK_TRY(epoch.alloc(16 * 4));
+  FLOCK_TRY(err.alloc(16));
+  FLOCK_TRY(part.alloc((size_t)n * 4));
+  FLOCK_TRY(h.alloc((size_t)n * 4));
+  FLOCK_CK(cudaMemset(flags.p, 0, flag_bytes * n_ranks));
+  FLOCK_CK(cudaMemset(epoch.p, 0, 16 * 4));
+  FLOCK_CK(cudaMemset(err.p, 0, 16));
+  FLOCK_CK(cudaMemset(part.p, 0, (size_t)n * 4));
+  FLOCK_CK(cudaMemset(h.p, 0, (size_t)n * 4));
+  std::vector<void*> ptrs(2 * (size_t)n_ranks);
+  for (int r = 0; r < n_ranks; r++) {
+    ptrs[r] = bufs.as<uint8_t>() + (size_t)r * buf_bytes;
+    ptrs[n_ranks + r] = flags.as<uint8_t>() + (size_t)r * flag_bytes;
+  }
+  FLOCK_CK(cudaMemcpy(tab.p, ptrs.data(), ptrs.size() * sizeof(void*), cudaMemcpyHostToDevice));
+  x.d_bufs = tab.as<float*>();
+  x.d_flags = reinterpret_cast<uint32_t**>(tab.as<void*>() + n_ranks);
+  x.epoch = epoch.as<uint32_t>();
+  x.err = err.as<int>();
+  int rc = FLOCK_OK;
+  for (int i = 0; i < calls; i++) {
+    rc = peer_xchg_run(&x, d->stream, h.as<float>(), part.as<float>(), n);
+    if (rc == FLOCK_OK) {
+      FLOCK_CK(cudaStreamSynchronize(d->stream));
+      rc = peer_xchg_check(&x);
+    }
+    if (i == 0 && first_status) *first_status = rc;
+  }
+  return rc;
+}
+
+}  // extern "C"
+
+namespace flock {
 
 }  // namespace flock

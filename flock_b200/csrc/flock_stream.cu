@@ -34,8 +34,8 @@ void emit(std::vector<StPiece>& v, const flock_tensor* a, const flock_tensor* b,
       p.qs[1] = b->qs.as<uint8_t>() + r * K;
       p.sc[1] = b->sc.as<uint16_t>() + r * b->sc_stride;
     }
-    p.qs_bytes = (uint32_t)(n * K);
-    p.sc_bytes = (uint32_t)(n * scb);
+    p.row_bytes = (uint32_t)K;
+    p.sc_row = (uint16_t)scb;
     p.out_row = (uint32_t)(out0 + (r - r0));
     p.nrows = (uint16_t)n;
     p.flags = b ? ST_PAIR : 0;
@@ -96,7 +96,7 @@ int stream_prepare(flock_dev* d, const StModelDesc& m, StEngine* e) {
       if (w->dtype != FLOCK_Q8_0) return no("a layer matrix is not Q8_0");
       if (!fits_slot(w, (t == W_GATE || t == W_UP) ? 2 : 1)) return no("row exceeds a ring slot");
     }
-  if (!fits_slot(m.head, 1)) return no("head row exceeds a ring slot");
+  if (m.head_in_kernel && !fits_slot(m.head, 1)) return no("head row exceeds a ring slot");
   int dev = d->ordinal, coop = 0, optin = 0;
   FLOCK_CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
   FLOCK_CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
@@ -105,8 +105,9 @@ int stream_prepare(flock_dev* d, const StModelDesc& m, StEngine* e) {
   const size_t fixed = st_fixed_bytes(m.H, m.nH * m.hd, m.F, &xbytes);
   const size_t per_slot = st_smem_bytes(1, 0);
   const int64_t room = (int64_t)optin - (int64_t)fixed - 1024;
-  const int slots = room > 0 ? (int)(room / (int64_t)per_slot) : 0;
+  int slots = room > 0 ? (int)(room / (int64_t)per_slot) : 0;
   if (slots < 4) return no("shared memory leaves fewer than 4 ring slots");
+  if (slots > 32) slots = 32;  // one producer lane per slot
   const size_t smem = st_smem_bytes(slots, fixed);
   const int grid = d->sm_count;
 
@@ -136,10 +137,12 @@ int stream_prepare(flock_dev* d, const StModelDesc& m, StEngine* e) {
       emit(v, w[W_DOWN], nullptr, r0, r1, r0);
       end_phase(v, st);
     }
-    size_t st = v.size();
-    share(m.head->rows, c, grid, &r0, &r1);
-    emit(v, m.head, nullptr, r0, r1, r0);
-    end_phase(v, st);
+    if (m.head_in_kernel) {
+      size_t st = v.size();
+      share(m.head->rows, c, grid, &r0, &r1);
+      emit(v, m.head, nullptr, r0, r1, r0);
+      end_phase(v, st);
+    }
   }
   size_t maxp = 0;
   for (auto& v : lists) maxp = std::max(maxp, v.size());
@@ -189,6 +192,12 @@ int stream_prepare(flock_dev* d, const StModelDesc& m, StEngine* e) {
   FLOCK_TRY(e->am_count.alloc(16));
   FLOCK_CK(cudaMemset(e->am_count.p, 0, 16));
 
+  // RoPE (cos, sin) for every position the cache holds
+  const int rope_rows = std::max(1, m.max_keys);
+  FLOCK_TRY(e->rope.alloc((size_t)rope_rows * 64 * sizeof(float2)));
+  k_rope_table<<<(rope_rows * 64 + 255) / 256, 256>>>(m.inv_freq, rope_rows, e->rope.as<float2>());
+  FLOCK_CK(cudaGetLastError());
+  FLOCK_CK(cudaDeviceSynchronize());
   if (!e->args) e->args = new StArgs();
   StArgs& a = *e->args;
   a = StArgs{};
@@ -204,6 +213,8 @@ int stream_prepare(flock_dev* d, const StModelDesc& m, StEngine* e) {
   a.eps = m.eps;
   a.neox = m.neox;
   a.inv_freq = m.inv_freq;
+  a.rope_cs = e->rope.as<float2>();
+  a.rope_rows = rope_rows;
   a.embd_qs = m.embd->qs.as<uint8_t>();
   a.embd_sc = m.embd->sc.as<uint16_t>();
   a.embd_sc_stride = m.embd->sc_stride;
@@ -230,11 +241,15 @@ int stream_prepare(flock_dev* d, const StModelDesc& m, StEngine* e) {
   a.err = e->err.as<int>();
   a.trace = nullptr;
   a.splits_max = std::max(1, std::min(ST_MAX_SPLITS, grid / m.nKV));
+  a.head = m.head_in_kernel ? 1 : 0;
+  a.l2_rounds = 3;
   a.ring_slots = slots;
   a.xbytes = xbytes;
-  FLOCK_TRY(kernel_setup((const void*)k_decode_stream, (int)smem));
+  const void* kfn = m.H <= 1024 ? (const void*)k_decode_stream<true>
+                                 : (const void*)k_decode_stream<false>;
+  FLOCK_TRY(kernel_setup(kfn, (int)smem));
   int per_sm = 0;
-  FLOCK_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_stream, ST_THREADS,
+  FLOCK_CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, ST_THREADS,
                                                          smem));
   if (per_sm < 1) return no("the kernel does not fit an SM");
   e->smem = smem;
@@ -259,7 +274,10 @@ int stream_launch(StEngine* e, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FLOCK_CK(cudaLaunchKernelEx(&cfg, k_decode_stream, *e->args));
+  if (e->args->H <= 1024)
+    FLOCK_CK(cudaLaunchKernelEx(&cfg, k_decode_stream<true>, *e->args));
+  else
+    FLOCK_CK(cudaLaunchKernelEx(&cfg, k_decode_stream<false>, *e->args));
   return FLOCK_OK;
 }
 

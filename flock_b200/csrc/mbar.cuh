@@ -79,6 +79,22 @@ FLOCK_DEV bool mbar_wait(uint64_t* b, uint32_t parity, const int* err, bool watc
   }
   return false;
 }
+// Bounded wait that never asks the hardware to suspend the thread for long:
+// for latency-critical pipelines where a late wake-up costs more than the
+// issue slots of polling (a producer that must refill a ring slot as soon as
+// it drains, consumers that must start on a slot as soon as it fills).
+FLOCK_DEV bool mbar_wait_poll(uint64_t* b, uint32_t parity, const int* err, bool watch_err = true) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; i++) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((i & 63) == 63) {
+      if (watch_err && *(volatile const int*)err) return false;
+      const uint64_t now = globaltimer_ns();
+      if (!t0) t0 = now;
+      else if (now - t0 > WAIT_NS) return false;
+    }
+  }
+}
 // Orders this thread's generic shared-memory writes before later async-proxy
 // reads of them (bulk copies, tensor-core operand reads).
 FLOCK_DEV void fence_proxy_async_smem() {

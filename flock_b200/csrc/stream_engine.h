@@ -29,6 +29,11 @@ struct StModelDesc {
   int32_t* ids = nullptr;
   int32_t* hist = nullptr;
   int hist_cap = 0;
+  int max_keys = 0;  // positions the RoPE table covers
+  // true: the LM head and its argmax run inside the streaming kernel; false:
+  // the kernel ends with the last layer's hidden state (h_out) and the caller
+  // launches the head GEMV (the kernel still advances the position)
+  bool head_in_kernel = false;
   int* ctl = nullptr;
 };
 
@@ -37,7 +42,7 @@ struct StEngine {
   std::string why;  // why the engine is unavailable for this model
   StArgs* args = nullptr;
   DBuf layers, pieces, n_pieces, t_qkv, t_part, t_att, t_ho, t_act, t_hd, seq, err, am_val,
-      am_idx, am_count, trace;
+      am_idx, am_count, trace, rope;
   size_t smem = 0;
   int grid = 0;
   int n_layers = 0;

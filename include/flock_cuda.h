@@ -171,6 +171,15 @@ FLOCK_API int flock_op_gemm_timed(flock_dev* dev, const flock_tensor* w, int M, 
  * call, as flock_op_matvec_timed_cold. */
 FLOCK_API int flock_op_gemm_timed_cold(flock_dev* dev, const flock_tensor* w, int M, int iters,
                                        float* ms_per_call, float* ms_image);
+/* One rank of an n_ranks tensor-parallel peer exchange whose peers never
+ * publish (local buffers nothing writes), run `calls` times with a wait
+ * limit of wait_ms, each followed by the host's error check.  *first_status
+ * gets the first call's status (FLOCK_E_CUDA: the bounded wait ran out),
+ * the return value the last call's (FLOCK_E_CUDA: the exchange stays failed).
+ * A test of the exchange's failure detection (flock_peer.cu) that needs no
+ * second GPU; no counterpart in the reference. */
+FLOCK_API int flock_op_peer_exchange_lone(flock_dev* dev, int n_ranks, int64_t n, int wait_ms,
+                                          int calls, int* first_status);
 /* kernels/rmsnorm.wgsl:41: n_vecs vectors of width n. */
 FLOCK_API int flock_op_rmsnorm(flock_dev* dev, const float* x, const float* g, int n, int n_vecs, float eps,
                      float* out);

@@ -8,7 +8,7 @@
     python profile_cases.py sweep [--time]   # config 1: Q8_0/Q4_0 x shapes x M in {1,16,128,512}
     python profile_cases.py gemm  [--time] [rows cols [M]]
                                                 # one tensor-core GEMM (default 3072 x 1024, M 512)
-    python profile_cases.py model [--time] [--kernels] [--trace]
+    python profile_cases.py model [--time] [--kernels | --persistent] [--trace]
     python profile_cases.py model8b [--time] [--prompt P] [--decode N] [--persistent]
                                                 # config 4 on one GPU: Qwen3-8B shape, 36
                                                 # layers, untied head; 4096-token prompt
@@ -18,8 +18,9 @@
                                                 # config 3: 512-token prompt TTFT on the
                                                 # 28-layer model, tensor-core (default) or
                                                 # exact prefill, then 32 decode tokens
-                                                # 28-layer 0.6B-shape decode, persistent
-                                                # kernel (default) or per-op kernel graph
+                                                # 28-layer 0.6B-shape decode: streaming
+                                                # kernel (default), persistent kernel or
+                                                # per-op kernel graph
 
 Each case builds seeded synthetic weights, runs a few warm launches and, with
 --time, prints CUDA-event timings.  They are small enough (< 1 GB on the
@@ -230,12 +231,81 @@ def trace_summary(tr, n_layers: int) -> str:
     return "\n".join(lines)
 
 
+def stream_trace_summary(tr, n_layers: int) -> str:
+    """The streaming decode kernel's trace: per step of a layer, the median
+    and slowest CTA's time since the previous step (averaged over layers),
+    the token time and the ring's wait totals."""
+    import numpy as np
+    t = (tr.astype(np.int64) - int(tr[:, 0].min())) / 1000.0
+    names = ["h polled", "QKV rows", "q/k/v polled", "attention", "attn polled", "o_proj rows",
+             "h polled", "gate/up rows", "act polled", "down rows"]
+    L = n_layers
+    head_in = bool((tr[:, 4 + 10 * L] > 0).any())
+    end = t[:, 4 + 10 * L].max() if head_in else t[:, 1 + 10 * L].max()
+    lines = [f"{'token' if head_in else 'layers (head launched after)'}: {end:.1f} us; "
+             f"embed {np.median(t[:, 1]):.2f} us"]
+    for k, name in enumerate(names):
+        med, mx = [], []
+        for l in range(1, L):
+            c = 2 + 10 * l + k
+            prev = c - 1 if k != 3 else c - 2   # attention: from the QKV rows
+            if k == 2:
+                sel = tr[:, c] > 0
+                if not sel.any():
+                    continue
+                d = t[sel, c] - t[sel, c - 1]
+            elif k == 4:
+                d = t[:, c] - np.max(t[:, c - 1])   # after the slowest attention
+            else:
+                d = t[:, c] - t[:, prev]
+            med.append(np.median(d))
+            mx.append(np.max(d))
+        if med:
+            lines.append(f"{name:>14}: median {np.mean(med):6.2f} us, slowest CTA {np.mean(mx):6.2f} us")
+    h = 2 + 10 * L
+    if head_in:
+        lines.append(f"head: input polled {np.median(t[:, h] - t[:, h - 1]):.2f} us, rows "
+                     f"{np.median(t[:, h + 1] - t[:, h]):.2f} us (slowest "
+                     f"{np.max(t[:, h + 1] - t[:, h]):.2f}), argmax "
+                     f"{np.max(t[:, h + 2]) - np.max(t[:, h + 1]):.2f} us")
+    det = tr[:, 8 + 10 * L: 20 + 10 * L].astype(np.int64)
+    rows = det[:, 0] > 0
+    if rows.any():
+        steps = ["q/k/v polled", "q/k rotated", "key appended", "tile staged", "scores",
+                 "softmax", "P.V", "published / weights", "combined"]
+        d = (det[rows] - det[rows, :1]) / 1000.0
+        parts = []
+        for k in range(1, len(steps)):
+            col = d[:, k][det[rows, k] > 0]
+            if col.size:
+                parts.append(f"{steps[k]} +{np.median(col):.2f}/{col.max():.2f}")
+        lines.append("last layer's attention item (median/max us after its q/k/v poll): "
+                     + ", ".join(parts))
+    for off, name in ((0, "QKV"), (9, "gate/up"), (18, "down")):
+        pd = tr[:, 20 + 10 * L + off: 29 + 10 * L + off].astype(np.int64)
+        if (pd[:, 0] > 0).any():
+            d = (pd - pd[:, :1]) / 1000.0
+            parts = []
+            for k in range(4):
+                w, r = pd[:, 1 + 2 * k] > 0, pd[:, 2 + 2 * k] > 0
+                if w.any():
+                    parts.append(f"piece {k}: full +{np.median(d[w, 1 + 2 * k]):.2f}, rows "
+                                 f"+{np.median(d[r, 2 + 2 * k]):.2f}")
+            lines.append(f"last layer's {name} phase (median us after its start): "
+                         + "; ".join(parts))
+    lines.append(f"ring: consumers waited {np.median(tr[:, 5 + 10 * L]) / 1e3:.1f} us a token "
+                 f"(median CTA), producer waited {np.median(tr[:, 6 + 10 * L]) / 1e3:.1f} us; "
+                 f"{int(np.median(tr[:, 7 + 10 * L]))} pieces per CTA")
+    return "\n".join(lines)
+
+
 def model_case(timed: bool) -> None:
     from flock_b200.model import Model
     dev = flib.get_device(0)
     m = synth.model(300)
     M = Model.create(dev, m, QWEN3_06B.with_(attention="fast"))
-    M.decode_mode = "kernels" if "--kernels" in sys.argv else "persistent"
+    M.decode_mode = ("kernels" if "--kernels" in sys.argv else
+                     "persistent" if "--persistent" in sys.argv else "stream")
     M.step(synth.uniform_ids(300, "prompt", 64, synth.QWEN3_06B.vocab).tolist())
     M.decode_device(3)
     dev.sync()
@@ -248,7 +318,8 @@ def model_case(timed: bool) -> None:
     if "--trace" in sys.argv:
         M.trace(True)
         M.decode_device(4)
-        print(trace_summary(M.read_trace(), M.held))
+        summary = stream_trace_summary if M.decode_mode == "stream" else trace_summary
+        print(summary(M.read_trace(), M.held))
         M.trace(False)
 
 

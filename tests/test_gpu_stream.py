@@ -102,15 +102,25 @@ def test_stream_rewind_repeats(dev, small):
 
 def test_stream_long_context(dev, small):
     """1500 cached keys: the split count is capped at SMs / kv heads, so each
-    split walks several 32-key tiles."""
+    split walks several 32-key tiles.  Over this many keys the two split-K
+    reassociations drift apart by a few 1e-5, so both engines are held to
+    the exact-attention engine (attnRef's order): within max relative error
+    1e-3 (floor 1e-3 * max|ref|), the stream engine no further off than
+    twice the graph's own fast path (+1e-6)."""
     cfg = FAST.with_(max_keys=2048)
     a, b = _pair(dev, small, cfg)
+    c = Model.create(dev, small, QWEN3_06B.with_(max_keys=2048))
     ids = synth.uniform_ids(7, "long", 1500, 4096).tolist()
-    for M in (a, b):
+    for M in (a, b, c):
         for i in range(0, 1500, 500):
             M.step(ids[i:i + 500])
-    assert a.decode_device(12).tolist() == b.decode_device(12).tolist()
-    _close(a.logits([3]), b.logits([3]))
+    want = c.decode_device(12).tolist()
+    assert a.decode_device(12).tolist() == b.decode_device(12).tolist() == want
+    la, lb, lc = a.logits([3]), b.logits([3]), c.logits([3])
+    ea, eb = abs_err_scaled(la, lc), abs_err_scaled(lb, lc)
+    print(f"1500 keys: absErrScaled vs exact: stream {ea:.2e}, graph fast {eb:.2e}")
+    assert rel_err(la, lc, floor=1e-3 * float(np.abs(lc).max())) <= 1e-3
+    assert ea <= 2 * eb + 1e-6
 
 
 def test_stream_kv_bf16(dev, small):
@@ -142,10 +152,18 @@ def test_stream_trace(dev, small):
     a.step([a.current_token()])
     tr = a.read_trace()
     n_layers = 2
-    assert tr.shape == (dev.sm_count, 4 + 6 * n_layers)
+    assert tr.shape == (dev.sm_count, 47 + 10 * n_layers)
     t0 = tr[:, 0].astype(np.int64)
-    done = tr[:, 3 + 6 * n_layers].astype(np.int64)
+    done = tr[:, 4 + 10 * n_layers].astype(np.int64)
     assert np.all(t0 > 0) and np.all(done >= t0)
+    # every CTA's stamps of one layer are in order (the attention stamp is
+    # 0 on CTAs without an attention item)
+    for l in range(n_layers):
+        cols = [2 + 10 * l + k for k in (0, 1, 3, 4, 5, 6, 7, 8, 9)]
+        seq = tr[:, cols].astype(np.int64)
+        assert np.all(np.diff(seq, axis=1) >= 0)
+    # pieces issued = pieces consumed: every CTA streamed its whole list
+    assert np.all(tr[:, 7 + 10 * n_layers] > 0)
     a.trace(False)
 
 
