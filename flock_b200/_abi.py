@@ -79,6 +79,10 @@ SIGNATURES = {
     "flock_tensor_from_f32": [_vp, _fp, _i64, _pp],
     "flock_tensor_free": [_vp],
     "flock_tensor_bytes": [_vp, _i64p],
+    "flock_tensor_from_bytes": [_vp, _vp, _i64, _pp],
+    "flock_tensor_read": [_vp, _i64, _i64, _vp],
+    "flock_quant_q8": [_fp, _i64, _i64, _u8p],
+    "flock_quant_q4": [_fp, _i64, _i64, _u8p],
     "flock_op_matvec": [_vp, _vp, _fp, _i, _fp],
     "flock_op_matvec_timed": [_vp, _vp, _i, _i, _fp],
     "flock_op_matvec_timed_cold": [_vp, _vp, _i, _i, _fp],

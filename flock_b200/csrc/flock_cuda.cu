@@ -876,6 +876,43 @@ int flock_tensor_from_f32(flock_dev* dev, const float* data, int64_t n, flock_te
   return FLOCK_OK;
 }
 
+int flock_tensor_from_bytes(flock_dev* dev, const void* data, int64_t bytes, flock_tensor** out) {
+  if (!dev || bytes < 1 || !out) return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(dev->ordinal));
+  const int64_t padded = (bytes + 3) & ~(int64_t)3;
+  flock_tensor* t = new flock_tensor();
+  t->dev = flock::dev_retain(dev);
+  t->dtype = FLOCK_F32;
+  t->rows = 1;
+  t->cols = padded / 4;
+  int rc = t->data.alloc(padded);
+  if (rc) {
+    flock_tensor_free(t);
+    return rc;
+  }
+  FLOCK_CK(cudaMemset(t->data.p, 0, padded));
+  if (data) FLOCK_CK(cudaMemcpy(t->data.p, data, bytes, cudaMemcpyHostToDevice));
+  *out = t;
+  return FLOCK_OK;
+}
+
+int flock_tensor_read(const flock_tensor* t, int64_t offset, int64_t bytes, void* out) {
+  if (!t || !out || offset < 0 || bytes < 0) return FLOCK_E_ARG;
+  if (t->dtype != FLOCK_F32) {
+    set_error("readBack: only f32/raw tensors are readable (quantized planes stay on the device)");
+    return FLOCK_E_ARG;
+  }
+  if (offset + bytes > (int64_t)t->data.bytes) {
+    set_error("readBack: range [%lld, %lld) is outside the %lld-byte buffer", (long long)offset,
+              (long long)(offset + bytes), (long long)t->data.bytes);
+    return FLOCK_E_LIMIT;
+  }
+  if (!bytes) return FLOCK_OK;
+  FLOCK_CK(cudaSetDevice(t->dev->ordinal));
+  FLOCK_CK(cudaMemcpy(out, (const uint8_t*)t->data.p + offset, bytes, cudaMemcpyDeviceToHost));
+  return FLOCK_OK;
+}
+
 int flock_tensor_free(flock_tensor* t) {
   if (t) {
     flock_dev* d = t->dev;

@@ -8,7 +8,9 @@
 // reach the CUDA allocator at all (an FFI caller given raw device pointers).
 // flock_op_argmax needs per-CTA scratch and takes it from its device handle,
 // whose creation allocates; this entry point instead keeps that scratch in a
-// fixed file-scope device array, sized for NOALLOC_MAX_CTAS partials.
+// fixed file-scope device array, sized for NOALLOC_MAX_CTAS partials.  The
+// first call on a device loads the module (the runtime's lazy loading), so it
+// must not be made while a stream is being captured.
 //
 // The array lives for as long as the library is loaded, on every GPU that
 // loads it (8 KiB + 256 B).  All calls share it: two calls whose kernels
@@ -24,36 +26,49 @@
 
 namespace {
 
-constexpr int NOALLOC_MAX_CTAS = 1024;      // partial (value, index) slots
-constexpr int NOALLOC_PER_CTA = 4096;       // logits one CTA reduces at most
-constexpr int64_t NOALLOC_MAX_N = (int64_t)NOALLOC_MAX_CTAS * NOALLOC_PER_CTA;
+// k_argmax walks its input with a grid stride, so the kernel itself handles
+// any n whose indices fit its uint32 slots with up to NOALLOC_MAX_CTAS CTAs.
+// NOALLOC_MAX_N is a bound this entry point chooses, not one the kernel
+// needs: it covers every vocabulary (151,936 for Qwen3) with a wide margin
+// and keeps the documented contract small.
+constexpr int NOALLOC_MAX_CTAS = 1024;            // partial (value, index) slots
+constexpr int64_t NOALLOC_MAX_N = 4194304;        // chosen bound (see above)
 
 // [0, 4 KiB) partial values, [4 KiB, 8 KiB) partial indices, then the counter.
 constexpr size_t OFF_VAL = 0, OFF_IDX = 4096, OFF_COUNT = 8192, SCRATCH_BYTES = 8192 + 256;
 static __device__ __align__(256) unsigned char g_argmax_scratch[SCRATCH_BYTES];
 
-// Device address of g_argmax_scratch per device ordinal, resolved once.
+// SM count per device ordinal (a property of the GPU, not of its context).
 std::mutex g_mu;
-void* g_addr[64] = {};
+int g_sms[64] = {};
 
-int scratch_address(int dev, void** out) {
-  std::lock_guard<std::mutex> lock(g_mu);
+int sm_count(int dev, int* out) {
   if (dev < 0 || dev >= 64) {
     flock::set_error("device ordinal %d out of range", dev);
     return FLOCK_E_ARG;
   }
-  if (!g_addr[dev]) {
-    // The symbol's host-side name is not a device address: ask the runtime for
-    // the address on the current device.
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_argmax_scratch);
-    if (e != cudaSuccess || !p) {
-      flock::set_error("cudaGetSymbolAddress(argmax scratch) failed: %s", cudaGetErrorString(e));
-      return FLOCK_E_CUDA;
-    }
-    g_addr[dev] = p;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_sms[dev]) {
+    int n = 0;
+    FLOCK_CK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    g_sms[dev] = n > 0 ? n : 1;
   }
-  *out = g_addr[dev];
+  *out = g_sms[dev];
+  return FLOCK_OK;
+}
+
+// The scratch array's device address in the current context, asked for on
+// every call: an address cached across calls would go stale if the primary
+// context were torn down and made again (cudaDeviceReset).  Once the module
+// is loaded the query is a table lookup in the runtime.
+int scratch_address(void** out) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_argmax_scratch);
+  if (e != cudaSuccess || !p) {
+    flock::set_error("cudaGetSymbolAddress(argmax scratch) failed: %s", cudaGetErrorString(e));
+    return FLOCK_E_CUDA;
+  }
+  *out = p;
   return FLOCK_OK;
 }
 
@@ -68,23 +83,22 @@ int flock_argmax_noalloc(const float* x, int64_t n, int32_t* index_out, float* v
     return FLOCK_E_ARG;
   }
   if (n > NOALLOC_MAX_N) {
-    flock::set_error("argmax_noalloc: n = %lld exceeds the maximum %lld (%d scratch slots x %d "
-                     "logits per slot); use flock_op_argmax", (long long)n,
-                     (long long)NOALLOC_MAX_N, NOALLOC_MAX_CTAS, NOALLOC_PER_CTA);
+    flock::set_error("argmax_noalloc: n = %lld exceeds the maximum %lld this entry point "
+                     "accepts; use flock_op_argmax", (long long)n, (long long)NOALLOC_MAX_N);
     return FLOCK_E_LIMIT;
   }
   int dev = 0;
   FLOCK_CK(cudaGetDevice(&dev));
   void* base = nullptr;
-  FLOCK_TRY(scratch_address(dev, &base));
+  FLOCK_TRY(scratch_address(&base));
   unsigned char* s = static_cast<unsigned char*>(base);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int sms = 148;
-  FLOCK_CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  int sms = 0;
+  FLOCK_TRY(sm_count(dev, &sms));
+  // two CTAs per SM at most (the grid stride covers the rest), one per 256
+  // logits for small inputs
   int64_t ctas = (n + 255) / 256;
-  const int64_t need = (n + NOALLOC_PER_CTA - 1) / NOALLOC_PER_CTA;  // <= NOALLOC_MAX_CTAS
-  if (ctas > 2 * sms) ctas = 2 * sms;
-  if (ctas < need) ctas = need;
+  if (ctas > 2 * (int64_t)sms) ctas = 2 * (int64_t)sms;
   if (ctas > NOALLOC_MAX_CTAS) ctas = NOALLOC_MAX_CTAS;
   FLOCK_CK(cudaMemsetAsync(s + OFF_COUNT, 0, sizeof(uint32_t), st));
   flock::k_argmax<<<(unsigned)ctas, 256, 0, st>>>(

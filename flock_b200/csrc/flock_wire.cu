@@ -13,8 +13,12 @@
 //   clears their caches first; the frame's offset must equal the caches'
 //   position), the last layer's output is rounded to f16 by a kernel with
 //   the same rounding as f32to16 and only the f16 payload comes back.
+// * flock_quant_q8 / flock_quant_q4: the host quantizers (kernels/lib.ts:40,
+//   :64), which store their block scales with the same f16 rounding.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cmath>
 #include <cstring>
 
 #include "flock_internal.h"
@@ -200,6 +204,73 @@ int flock_range_forward_wire(flock_layer* const* layers, int n_layers, const uin
                            d->stream));
   FLOCK_CK(cudaStreamSynchronize(d->stream));
   return ws_check_errors(wo);
+}
+
+
+// kernels/lib.ts:40 quantRowQ8 over every row.  JS numbers are f64: amax and
+// d = amax/127 are f64, the stored scale is f32(d) rounded to f16 nearest-even
+// (wire.mjs f32to16 takes an f32), and Math.round(x/d) sends halves toward
+// +infinity.
+static inline double js_round(double x) {
+  const double r = std::floor(x);
+  return x - r >= 0.5 ? r + 1.0 : r;
+}
+
+int flock_quant_q8(const float* w, int64_t rows, int64_t cols, uint8_t* out) {
+  if (!w || !out || rows < 1 || cols < 32 || cols % 32) {
+    set_error("quantMatrixQ8: cols %lld must be a positive multiple of 32", (long long)cols);
+    return FLOCK_E_ARG;
+  }
+  const int64_t blocks = rows * (cols / 32);
+  for (int64_t b = 0; b < blocks; b++) {
+    const float* v = w + b * 32;
+    uint8_t* o = out + b * 34;
+    double amax = 0.0;
+    for (int i = 0; i < 32; i++) amax = std::max(amax, std::fabs((double)v[i]));
+    const double d = amax / 127.0;
+    const uint16_t h = f32_to_f16_rne((float)d);
+    o[0] = (uint8_t)(h & 0xff);
+    o[1] = (uint8_t)(h >> 8);
+    for (int i = 0; i < 32; i++) {
+      const double q = d == 0.0 ? 0.0 : js_round((double)v[i] / d);
+      o[2 + i] = (uint8_t)((int)std::max(-128.0, std::min(127.0, q)) & 0xff);
+    }
+  }
+  return FLOCK_OK;
+}
+
+// kernels/lib.ts:64 quantRowQ4 over every row: the scale comes from the first
+// value of largest magnitude (strict > scan) so its sign survives.
+int flock_quant_q4(const float* w, int64_t rows, int64_t cols, uint8_t* out) {
+  if (!w || !out || rows < 1 || cols < 32 || cols % 32) {
+    set_error("quantMatrixQ4: cols %lld must be a positive multiple of 32", (long long)cols);
+    return FLOCK_E_ARG;
+  }
+  const int64_t blocks = rows * (cols / 32);
+  for (int64_t b = 0; b < blocks; b++) {
+    const float* v = w + b * 32;
+    uint8_t* o = out + b * 18;
+    double amax = 0.0, mx = 0.0;
+    for (int i = 0; i < 32; i++) {
+      const double a = std::fabs((double)v[i]);
+      if (a > amax) {
+        amax = a;
+        mx = v[i];
+      }
+    }
+    const double d = mx / -8.0;
+    const double id = d == 0.0 ? 0.0 : 1.0 / d;
+    const uint16_t h = f32_to_f16_rne((float)d);
+    o[0] = (uint8_t)(h & 0xff);
+    o[1] = (uint8_t)(h >> 8);
+    for (int i = 0; i < 16; i++) {
+      const double x0 = (double)v[i] * id + 8.5, x1 = (double)v[i + 16] * id + 8.5;
+      const int q0 = (int)std::min(15.0, std::max(0.0, std::floor(x0)));
+      const int q1 = (int)std::min(15.0, std::max(0.0, std::floor(x1)));
+      o[2 + i] = (uint8_t)(q0 | (q1 << 4));
+    }
+  }
+  return FLOCK_OK;
 }
 
 }  // extern "C"

@@ -118,6 +118,15 @@ FLOCK_API int flock_repack_q8(const uint8_t* packed, int64_t rows, int64_t cols,
 /* kernels/lib.ts:142 splitQ4: 18-byte blocks -> qs [rows*cols/2] + scales. */
 FLOCK_API int flock_repack_q4(const uint8_t* packed, int64_t rows, int64_t cols, uint8_t* qs_out,
                     uint8_t* scales_out);
+/* kernels/lib.ts:94 quantMatrixQ8 (each row as lib.ts:40 quantRowQ8): f32
+ * [rows][cols] -> Q8_0 blocks [rows*cols/32][34] on the host; cols a multiple
+ * of 32.  Per block d = amax/127 in f64, the scale is f32(d) rounded to f16
+ * (nearest even), q = round-half-up(x/d) clamped to [-128, 127]. */
+FLOCK_API int flock_quant_q8(const float* w, int64_t rows, int64_t cols, uint8_t* out);
+/* kernels/lib.ts:103 quantMatrixQ4 (rows as lib.ts:64 quantRowQ4): d = the
+ * first value of largest magnitude / -8, q = clamp(floor(x/d + 8.5), 0, 15),
+ * byte i = q[i] | q[i+16] << 4. */
+FLOCK_API int flock_quant_q4(const float* w, int64_t rows, int64_t cols, uint8_t* out);
 
 /* -------------------------------------------------------------- tensors */
 
@@ -134,6 +143,14 @@ FLOCK_API int flock_tensor_from_f32(flock_dev* dev, const float* data, int64_t n
 FLOCK_API int flock_tensor_free(flock_tensor* t);
 /* Bytes resident on the device for the tensor (qs + scales, or data). */
 FLOCK_API int flock_tensor_bytes(const flock_tensor* t, int64_t* out);
+/* kernels/lib.ts:548 storageBuffer / :569 uniformBuffer: a raw device buffer
+ * of `bytes` (rounded up to 4) holding a copy of `data` (NULL: zeros), typed
+ * FLOCK_F32 so the ops that take an f32 tensor accept it. */
+FLOCK_API int flock_tensor_from_bytes(flock_dev* dev, const void* data, int64_t bytes,
+                                      flock_tensor** out);
+/* kernels/lib.ts:576 readBack: copy [offset, offset+bytes) of an f32/raw
+ * tensor's device buffer to the host (synchronous). */
+FLOCK_API int flock_tensor_read(const flock_tensor* t, int64_t offset, int64_t bytes, void* out);
 
 /* ---------------------------------------------------- op-level kernels
  * The individually validated kernels, with host inputs/outputs, as the
@@ -212,10 +229,13 @@ FLOCK_API int flock_op_argmax(flock_dev* dev, const float* x, int64_t n, int64_t
  * value_out are device pointers; stream may be NULL (the default stream).
  * Nothing is allocated: the per-CTA partials live in a fixed 8.25 KiB
  * device array inside the library, present on every GPU that loads it
- * until exit.  n must be <= 4194304 (FLOCK_E_LIMIT otherwise).  The first
- * call on a device resolves that array's address (cudaGetSymbolAddress) --
- * make it before any stream capture.  Calls share the array: calls whose
- * kernels overlap on the GPU race, so order them on one stream. */
+ * until exit.  n must be <= 4194304 (FLOCK_E_LIMIT otherwise), a bound
+ * this entry point chooses -- the kernel walks any n with a grid stride.
+ * Every call asks the runtime for the array's address in the current
+ * context, so a device reset between calls is safe; the first call on a
+ * device loads the module, so make it before any stream capture.  Calls
+ * share the array: calls whose kernels overlap on the GPU race, so order
+ * them on one stream. */
 FLOCK_API int flock_argmax_noalloc(const float* x, int64_t n, int32_t* index_out, float* value_out,
                                    void* stream);
 

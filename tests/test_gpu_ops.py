@@ -222,3 +222,25 @@ def test_argmax_ties_negative_random(dev, oracle):
     for n in (256, 1000, 4096, VOCAB):
         r = synth.normal(14, f"a{n}", n) * 10
         assert ops.argmax(dev, r)[0] == oracle.argmax(r)
+
+
+def test_raw_buffer_roundtrip(dev):
+    """kernels/lib.ts:548 storageBuffer / :576 readBack through the C ABI: a
+    34-byte (not 4-aligned) upload reads back byte-for-byte, the pad is zero,
+    and a range past the end is refused."""
+    import ctypes
+
+    from flock_b200 import _abi
+    data = np.arange(34, dtype=np.uint8)
+    h = ctypes.c_void_p()
+    _abi.call("flock_tensor_from_bytes", dev.handle, data.ctypes.data, 34, ctypes.byref(h))
+    try:
+        out = np.zeros(36, np.uint8)
+        _abi.call("flock_tensor_read", h, 0, 36, out.ctypes.data)
+        assert np.array_equal(out[:34], data) and not out[34:].any()
+        part = np.zeros(8, np.uint8)
+        _abi.call("flock_tensor_read", h, 10, 8, part.ctypes.data)
+        assert np.array_equal(part, data[10:18])
+        assert _abi.lib().flock_tensor_read(h, 30, 8, part.ctypes.data) == _abi.FLOCK_E_LIMIT
+    finally:
+        _abi.lib().flock_tensor_free(h)
