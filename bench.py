@@ -324,6 +324,9 @@ def main():
                          "kernel")
     ap.add_argument("--also-stream", action=argparse.BooleanOptionalAction, default=True,
                     help="also time the streaming engine on the same workload (its own key)")
+    ap.add_argument("--also-tp", action=argparse.BooleanOptionalAction, default=True,
+                    help="N > 1 pipeline runs: also time the tensor-parallel path on the same "
+                         "GPUs and report it as the line's tensor_parallel key")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-prefill", action="store_true",
@@ -598,13 +601,16 @@ def _max_over_ranks(v: float, world: int) -> float:
     return float(t[0])
 
 
-def run_tensor(args, rank, world, local, dev, shape, pk):
+def run_tensor(args, rank, world, local, dev, shape, pk, emit: bool = True,
+               pg_ready: bool = False):
     """Config 4b (and the 0.6B shape likewise): every layer and the head
     sharded over the N GPUs (flock_model_create_tp) -- QKV / gate / up by
     output rows, o_proj / down by input columns with an NCCL all-gather and a
     rank-order sum per projection, the head by vocab rows with an 8-byte
     (value, index) all-gather per token.  Decode steps replay one captured
-    graph per rank, NCCL inside."""
+    graph per rank, NCCL inside.  emit=False returns rank 0's line instead
+    of printing it (the pipeline line carries it as a key); pg_ready: the
+    caller owns the gloo process group."""
     from datetime import timedelta
     import torch.distributed as dist
     from flock_b200 import synth
@@ -613,7 +619,7 @@ def run_tensor(args, rank, world, local, dev, shape, pk):
     from flock_b200.model import Model
 
     n_prompt = args.prompt if args.prompt is not None else (4096 if args.shape == "8b" else PROMPT)
-    if world > 1:
+    if world > 1 and not pg_ready:
         dist.init_process_group("gloo", timeout=timedelta(seconds=600))
     uid = Comm.unique_id() if rank == 0 else None
     if world > 1:
@@ -691,17 +697,21 @@ def run_tensor(args, rank, world, local, dev, shape, pk):
             "e2e": {"value": args.steps / (ms_e2e / 1000.0), "unit": "tok/s",
                     "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                     "ids_match_device_loop": ids_api == ids_dev.tolist()},
+            "ids": ids_dev.tolist(),
             "prefill": {"ttft_ms": ttft, "prompt": n_prompt, "path": "tcgen05 f16, tensor-sharded"},
             "gpu_launches": (1 + shape.n_layers * ((5 if args.attention == "fast" else 6) + 2) + 4)
             * args.steps,
             "load_s": t_load,
         }
-        print(json.dumps(out), flush=True)
+        if emit:
+            print(json.dumps(out), flush=True)
     M.free()  # the captured graph holds NCCL calls: release it before the communicator
     comm.free()
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
+        if not pg_ready:
+            dist.destroy_process_group()
+    return out if rank == 0 else None
 
 
 def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
@@ -772,18 +782,35 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     if rank == 0:
         M.set_token(first)
     dist.barrier()
+    import torch
+    # windows of exactly K device-fed steps (the chosen id stays on rank 0's
+    # device; no rank waits on its host inside a window), repeated after an
+    # untimed rewind until they add up to min_timed_s; each window's time is
+    # the max over ranks, so every rank takes the same decision to go on
     clk = Clocks(gpu_index(local))
     clk.start()
-    dev.timer_start()
-    for _ in range(args.steps):
-        pstep(None, 1, 0)
-    ms = dev.timer_stop()
+    window_ms, ids_dev = [], None
+    while True:
+        dev.timer_start()
+        for _ in range(args.steps):
+            pstep(None, 1, 0)
+        w_ms = dev.timer_stop()
+        tt = torch.tensor([w_ms], dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        window_ms.append(float(tt[0]))
+        if ids_dev is None and rank == 0:
+            ids_dev = np.zeros(args.steps, np.int32)
+            _abi.call("flock_model_history", M.handle, n_prompt, args.steps,
+                      _abi.ptr(ids_dev, _abi._i32p))
+        if sum(window_ms) >= 1000.0 * args.min_timed_s:
+            break
+        M.rewind(n_prompt)
+        if rank == 0:
+            M.set_token(first)
+        dist.barrier()
     clocks = clk.stop()
-    t = np.array([ms], np.float64)
-    import torch
-    tt = torch.tensor(t)
-    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    ms_max = float(tt[0])
+    ms_max = sum(window_ms) / len(window_ms)
+
     # e2e: host loop through the API, id read back on rank 0 every token
     M.rewind(n_prompt)
     if rank == 0:
@@ -798,7 +825,51 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
     tt = torch.tensor([ms_e2e], dtype=torch.float64)
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms_e2e = float(tt[0])
+    ids_api = []
     if rank == 0:
+        ids_api = np.zeros(args.steps, np.int32)
+        _abi.call("flock_model_history", M.handle, n_prompt, args.steps,
+                  _abi.ptr(ids_api, _abi._i32p))
+    dist.barrier()
+    _abi.lib().flock_comm_free(comm)
+    M.free()
+    for lt in layer_ts:
+        for t in lt.values():
+            t.free()
+
+    # the same decode on one GPU (rank 0, the whole model, same positions):
+    # the ids the pipeline must reproduce, and the per-token time the hops add to
+    one_gpu = None
+    if rank == 0:
+        M1 = Model.create(dev, m, cfg)
+        f1 = M1.step(prompt)
+        M1.decode_device(args.warmup)
+        M1.rewind(n_prompt)
+        M1.set_token(f1)
+        dev.sync()
+        dev.timer_start()
+        ids_1 = M1.decode_device(args.steps)
+        ms_1 = dev.timer_stop()
+        M1.free()
+        hop_us = (ms_max - ms_1) / args.steps * 1000.0 / world
+        one_gpu = {"ms_per_step": ms_1 / args.steps, "first_id": int(f1),
+                   "ids_match": f1 == first and ids_1.tolist() == ids_dev.tolist(),
+                   "hop_us_est": hop_us}
+        log(f"one GPU: {one_gpu}")
+    dist.barrier()
+
+    # the tensor-parallel path on the same N GPUs (config 4b's form at this
+    # shape), reported as a key of this line
+    tp_line = None
+    if args.also_tp and shape.n_layers == 28:
+        tp_line = run_tensor(args, rank, world, local, dev, shape, pk, emit=False, pg_ready=True)
+    if rank == 0:
+        ids_oracle, ids_match = None, None
+        if not args.no_oracle_ids:
+            n_chk = min(4, args.steps)
+            ids_oracle = oracle_ids(m, shape, prompt, n_chk + 1)
+            ids_match = ids_oracle == [first] + ids_dev[:n_chk].tolist()
+            log(f"oracle ids {ids_oracle}: match {ids_match}")
         tok_s = args.steps / (ms_max / 1000.0)
         avg_keys = n_prompt + (args.steps - 1) / 2.0 + 1
         tok_bytes = bytes_per_token(shape, avg_keys, 2 if args.kv == "bf16" else 4)
@@ -815,7 +886,19 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
                                    "hidden state over "
                                    "NCCL send/recv", "seed": SEED, "prompt": n_prompt,
                        "attention": args.attention, "kv": args.kv,
-                       "parallelism": f"pp{world}", "l2": "inputs larger than L2"},
+                       "parallelism": f"pp{world}", "l2": "inputs larger than L2",
+                       "timing": f"CUDA events around each window of K device-fed steps, max "
+                                 f"over ranks; {len(window_ms)} windows (untimed rewind between)",
+                       "windows": len(window_ms)},
+            "limit": {"collective": "NCCL send/recv of one token's hidden state, one hop per "
+                                    "stage boundary and one back to rank 0 (N hops per token); "
+                                    "batch 1 keeps one stage busy at a time",
+                      "hops_per_token": world,
+                      "hop_us_est": one_gpu["hop_us_est"],
+                      "hop_share": world * one_gpu["hop_us_est"] / 1000.0 / (ms_max / args.steps),
+                      "how": "(pipeline ms/token - one GPU's ms/token on the same model and "
+                             "positions, rank 0) / hops"},
+            "one_gpu": one_gpu,
             # batch 1 keeps one stage busy at a time: the roofline is one GPU's
             "roofline": {"bound": "hbm", "achieved": token_gbs, "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": token_gbs / pk["hbm_gbs"], "traffic": None,
@@ -823,13 +906,26 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
                          "bytes_per_launch": tok_bytes, "peak_src": pk["src"]},
             "clocks": clocks,
             "e2e": {"value": args.steps / (ms_e2e / 1000.0), "unit": "tok/s",
-                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                    "ids_match_device_loop": ids_api.tolist() == ids_dev.tolist()},
             "gpu_launches": (1 + shape.n_layers * (5 if args.attention == "fast" else 6) + 2)
-            * args.steps,
+            * args.steps * len(window_ms),
         }
+        if ids_oracle is not None:
+            out["ids_match_oracle"] = ids_match
+            out["ids_checked"] = len(ids_oracle)
+        if tp_line:
+            out["tensor_parallel"] = {k: tp_line[k] for k in
+                                      ("value", "unit", "ms_per_step", "e2e", "roofline",
+                                       "prefill") if k in tp_line}
+            out["tensor_parallel"]["parallelism"] = tp_line["config"]["parallelism"]
+            out["tensor_parallel"]["tp_exchange"] = tp_line["config"]["tp_exchange"]
+            # tensor parallelism sums the o_proj / down partials in rank order
+            # (shardReduceRef), so its bits differ from one GPU's fold: equal
+            # greedy ids are expected, not guaranteed
+            out["tensor_parallel"]["ids_match_pipeline"] = tp_line.get("ids") == ids_dev.tolist()
         print(json.dumps(out), flush=True)
     dist.barrier()
-    _abi.lib().flock_comm_free(comm)
     dist.destroy_process_group()
 
 

@@ -552,6 +552,9 @@ FLOCK_DEV int st_phase(const StArgs& a, int pi, int ph, uint32_t tag, bool last_
         }
       }
     }
+    // order this lane's generic reads of the slot before the producer's next
+    // bulk copy (async proxy) into it, then release the slot for the warp
+    fence_proxy_async_smem();
     __syncwarp();
     if (pd && k < 4) pd[2 + 2 * k] = globaltimer_ns();
     if (lane == 0) mbar_arrive(&c.empty[slot]);

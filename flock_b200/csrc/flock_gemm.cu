@@ -1,8 +1,12 @@
 // Host side of the tensor-core prefill GEMM (gemm_tc.cuh): the activation
 // image, launches, and the op-level entry points that the M > 1 sweep and
 // the parity tests call.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <vector>
 
 #include "flock_internal.h"
@@ -68,7 +72,7 @@ void tc_finish_tiles(TcArgs& a) {
 
 template <int QT, int EPI>
 static int launch_tc(cudaStream_t st, const TcArgs& a) {
-  FLOCK_TRY(kernel_setup((const void*)k_gemm_tc<QT, EPI>, (int)gemm_tc_smem_bytes(TC_MAX_NT)));
+  FLOCK_TRY(kernel_setup((const void*)k_gemm_tc<QT, EPI>, TC_SMEM_MAX));
   const size_t smem = gemm_tc_smem_bytes(a.Nt);
   const dim3 grid((unsigned)a.tile0[a.nseg], (unsigned)((a.M + a.Nt - 1) / a.Nt),
                   (unsigned)a.ksplit);
@@ -85,6 +89,47 @@ static int launch_tc(cudaStream_t st, const TcArgs& a) {
   return FLOCK_OK;
 }
 
+// The TMA tensor map of a qs plane ([rows][row_bytes] uint8, row_bytes = K
+// for Q8_0 and K / 2 for Q4_0): box {64 / 32 bytes, 128 rows} with the
+// matching 64- / 32-byte swizzle (gemm_tc.cuh tc_read_raw), L2 promotion of
+// 256 bytes, zeros past the last row.  Encoded once per (plane, shape) and
+// cached: the map is a pure function of those, so a cached entry stays right
+// even if a freed plane's address comes back for another tensor.
+static int qs_tensor_map(CUtensorMap* out, const uint8_t* qs, int rows, int row_bytes, int qt) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, int, int>, CUtensorMap> cache;
+  const auto key = std::make_tuple((const void*)qs, rows, row_bytes, qt);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return FLOCK_OK;
+  }
+  if (((uintptr_t)qs & 15) || row_bytes % 16 || rows < 1) {
+    set_error("tensor-core GEMM: weight plane %p (%d rows of %d bytes) is not TMA-addressable",
+              (const void*)qs, rows, row_bytes);
+    return FLOCK_E_ARG;
+  }
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)(qt == QT_Q8 ? TC_KT : TC_KT / 2), (cuuint32_t)TC_ROWS};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = cuTensorMapEncodeTiled(
+      &m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(qs), dims, strides, box, estr,
+      CU_TENSOR_MAP_INTERLEAVE_NONE,
+      qt == QT_Q8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
+      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for a %d x %d weight plane", (int)r, rows,
+              row_bytes);
+    return FLOCK_E_CUDA;
+  }
+  cache.emplace(key, m);
+  *out = m;
+  return FLOCK_OK;
+}
+
 // Y = X . W^T for the segments of `a` on the tensor cores; `a.img` must hold
 // the activation image of the same M and K.  With `part` (room for
 // part_floats) and one segment, a grid too small for the GPU is split along
@@ -92,9 +137,20 @@ static int launch_tc(cudaStream_t st, const TcArgs& a) {
 int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a, int sm_count,
                     size_t part_floats) {
   if (a.K % TC_KT || a.M < 1 || a.nseg < 1 || a.nseg > 3) return FLOCK_E_ARG;
-  a.Nt = tc_token_tile(a.M);
+  for (int i = 0; i < a.nseg; i++)
+    FLOCK_TRY(qs_tensor_map(&a.tmap[i], a.seg[i].qs, a.seg[i].rows,
+                            qt == QT_Q8 ? a.K : a.K / 2, qt));
+  a.img_nt = tc_token_tile(a.M);
   a.row_exp = reinterpret_cast<const int*>(a.img + act_image_only_bytes(a.M, a.K));
   tc_finish_tiles(a);
+  // Tokens per CTA: the image tile, or half of it when that still fits the
+  // grid in one wave -- twice the CTAs on the small weight matrices, each
+  // dequantising its weight tile for half as many tokens.
+  a.Nt = a.img_nt;
+  if (a.img_nt >= 128 && a.img_nt % 32 == 0 &&
+      a.tile0[a.nseg] * ((a.M + a.img_nt / 2 - 1) / (a.img_nt / 2)) <= sm_count)
+    a.Nt = a.img_nt / 2;
+  a.raw_stages = tc_raw_stages(a.Nt);
   a.ksplit = 1;
   const int ctas = a.tile0[a.nseg] * ((a.M + a.Nt - 1) / a.Nt);
   const int KT = a.K / TC_KT;

@@ -15,19 +15,27 @@
 //  * Operands are swapped for small M: 128 weight rows form the MMA's M and
 //    up to 256 tokens its N, so a 16-token prefill still issues full-height
 //    tcgen05.mma.cta_group::1.kind::f16 (128 x Nt x 16) instructions.
-//  * Producers (8 warps, two threads per weight row: one 32-weight block each
-//    per K-tile) keep 6 K-tiles of raw int8 / nibble weights in flight in
-//    registers, dequantise q * s in f32 (packed f32x2), round to f16 and
-//    write the K-major 128-byte-swizzled layout the UMMA
-//    shared-memory descriptor names (8-row x 128-byte atoms, 16-byte chunk
-//    c of row r at (c ^ r % 8)).  The only weight rounding is that of the
-//    scaled value.
+//  * Raw weight tiles arrive by TMA: one thread of a loader warp issues a
+//    2-D cp.async.bulk.tensor per K-tile (128 rows x 64 int8 bytes, or x 32
+//    nibble bytes) from the weight's tensor map into a ring of 4-12
+//    shared-memory stages (all the shared memory the A/B stages leave) (the map's 64-/32-byte swizzle spreads the rows
+//    over all banks), completing on the stage's mbarrier by transaction
+//    count.  The map always describes this GPU's own weight plane; there is
+//    no multicast.
+//  * Converters (8 warps, two threads per weight row: one 32-weight block
+//    each per K-tile) read their block from the raw stage, release it,
+//    form q * s in packed f16 arithmetic (exact integers, one correctly
+//    rounded multiply by the stored f16 scale; the scales come from global
+//    memory a few K-tiles ahead) and write the K-major
+//    128-byte-swizzled layout the UMMA shared-memory descriptor names
+//    (8-row x 128-byte atoms, 16-byte chunk c of row r at (c ^ r % 8)).  The
+//    only weight rounding is that of the scaled value.
 //  * Activations come from an image the caller builds once per GEMM
 //    (k_act_image: RMSNorm fused, f16, same swizzled layout, Nt rows per
 //    K-tile contiguous), so each stage's B tile is one bulk copy.
 //  * One thread issues the MMAs; tcgen05.commit returns each stage to the
-//    producers through an mbarrier and signals the epilogue after the last
-//    K-tile.  The 8 producer warps then read the accumulator with tcgen05.ld
+//    converters through an mbarrier and signals the epilogue after the last
+//    K-tile.  The 8 converter warps then read the accumulator with tcgen05.ld
 //    (32 lanes x 32 bit: one weight row per thread, one token per column;
 //    warps w and w+4 share a lane quarter and split the columns) and store
 //    coalesced rows of Y, optionally adding a residual.
@@ -35,6 +43,7 @@
 // Every wait is bounded (mbar_wait); on a timeout the kernel sets *err,
 // still releases its tensor memory and returns.  No multicast is used.
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -45,12 +54,15 @@ namespace flock {
 
 constexpr int TC_ROWS = 128;              // weight rows per CTA: the MMA's M
 constexpr int TC_KT = 64;                 // K per stage: one 128-byte f16 swizzle atom row
-constexpr int TC_STAGES = 4;
+constexpr int TC_STAGES = 4;              // f16 A / image B stages
+constexpr int TC_RAW_MAX = 12;            // raw weight stages (TMA ring), at most
+constexpr int TC_SMEM_MAX = 232448;       // dynamic shared memory per CTA on sm_100
 constexpr int TC_MAX_NT = 256;            // tokens per CTA: the MMA's N
-constexpr int TC_PRODUCERS = 256;         // 8 warps: producers, then the epilogue
-constexpr int TC_THREADS = TC_PRODUCERS + 32;  // + the MMA warp
+constexpr int TC_PRODUCERS = 256;         // 8 warps: converters, then the epilogue
+constexpr int TC_THREADS = TC_PRODUCERS + 96;  // + the MMA warp + the weight and image loaders
 constexpr int TC_A_BYTES = TC_ROWS * TC_KT * 2;  // 16 KiB of f16 per stage
-constexpr int TC_PREFETCH = 6;            // K-tiles of raw weights in flight per thread
+constexpr int TC_RAW_BYTES = TC_ROWS * TC_KT;    // 8 KiB of int8 per raw stage (Q4: half used)
+constexpr int TC_SC_AHEAD = 4;            // K-tiles of scales loaded ahead per thread
 
 struct TcSeg {
   const uint8_t* qs;
@@ -62,11 +74,15 @@ struct TcSeg {
 };
 
 struct TcArgs {
+  // 2-D tensor map of each segment's qs plane: {row bytes, rows}, box
+  // {64 (Q8) / 32 (Q4) bytes, 128 rows}, 64-/32-byte swizzle (host-encoded)
+  CUtensorMap tmap[3];
   TcSeg seg[3];
   int nseg;
   int tile0[4];      // first 128-row tile of each segment; tile0[nseg] = all tiles
   int K, M, Nt;      // Nt: tokens per CTA (multiple of 16, <= 256)
-  const uint8_t* img;  // activation image: [M / Nt][K / 64][Nt][128 B] f16, swizzled
+  int img_nt;        // token rows per image tile (Nt divides it)
+  const uint8_t* img;  // activation image: [M / img_nt][K / 64][img_nt][128 B] f16, swizzled
   const int* row_exp;  // e of each image row: the row was scaled by 2^-e
   const float* res;    // EPI_RESIDUAL: y += res[m][n] (res may alias the output)
   int res_stride;
@@ -75,6 +91,7 @@ struct TcArgs {
   // and writes its partial to part[z][m][row]; k_splitk_reduce sums them
   int ksplit;
   float* part;
+  int raw_stages;    // depth of the raw weight ring (tc_raw_stages)
 };
 
 // ------------------------------------------------------------------ tcgen05
@@ -167,53 +184,69 @@ struct TcRaw {
   uint32_t s;   // the f16 scale (low 16 bits)
 };
 
-// Block `half` (0/1) of row `row` in K-tile kt.
+// Block `half` (0/1) of row t from a raw stage the TMA wrote.  Q8 rows are
+// 64 bytes with the 64-byte swizzle (16-byte chunk c of row t at
+// c ^ ((t >> 1) & 3)); Q4 rows are 32 bytes with the 32-byte swizzle (chunk
+// c at c ^ ((t >> 2) & 1)).  Either way the 8 threads of an LDS.128 phase
+// (four rows, both halves) hit 8 distinct 4-bank groups.
 template <int QT>
-FLOCK_DEV void tc_load_raw(TcRaw& r, const TcSeg& sg, int K, int row, int half, int kt) {
+FLOCK_DEV void tc_read_raw(TcRaw& r, const uint8_t* raw, int t, int half) {
   if (QT == QT_Q8) {
-    const uint4* p = reinterpret_cast<const uint4*>(sg.qs + (size_t)row * K + (size_t)kt * TC_KT +
-                                                    half * 32);
-    r.q[0] = ldg_stream(p);
-    r.q[1] = ldg_stream(p + 1);
+    const int x = (t >> 1) & 3;
+    const uint8_t* row = raw + t * 64;
+    r.q[0] = *reinterpret_cast<const uint4*>(row + (((2 * half) ^ x) << 4));
+    r.q[1] = *reinterpret_cast<const uint4*>(row + (((2 * half + 1) ^ x) << 4));
   } else {
-    r.q[0] = ldg_stream(reinterpret_cast<const uint4*>(sg.qs + (size_t)row * (K / 2) +
-                                                       (size_t)kt * (TC_KT / 2) + half * 16));
+    r.q[0] = *reinterpret_cast<const uint4*>(raw + t * 32 + ((half ^ ((t >> 2) & 1)) << 4));
   }
-  r.s = __ldg(sg.sc + (size_t)row * sg.sc_stride + kt * 2 + half);
 }
 
-// f16(q * s) for the four int8 / nibble values of word u, two per packed op.
-FLOCK_DEV uint2 tc_dequant4(uint32_t u, uint64_t bias2, uint64_t s2) {
-  const uint64_t a = fmul2(fsub2(pack2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u)),
-                                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541u))),
-                                 bias2),
-                           s2);
-  const uint64_t b = fmul2(fsub2(pack2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542u)),
-                                       __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543u))),
-                                 bias2),
-                           s2);
-  const float2 fa = unpack2(a), fb = unpack2(b);
-  return make_uint2(h2(fa.x, fa.y), h2(fb.x, fb.y));
+// 2-D tiled TMA load of box {x, y} into shared memory, completing on `bar`
+// by transaction bytes.  `tmap` is the generic address of a tensor map in
+// kernel parameter space (__grid_constant__).
+FLOCK_DEV void tma_load_2d(void* dst, const CUtensorMap* tmap, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+FLOCK_DEV void tma_prefetch_desc(const CUtensorMap* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+// f16(q * s) for the four 8-bit values of word u (bytes v = q + bias, v in
+// [0, 255]), two per packed f16 op: __byte_perm places each byte under the
+// exponent 0x64 (f16 1024 + v, exact), one HSUB2 removes 1024 + bias
+// (exact: the values are integers below 2048) and one HMUL2 by the block's
+// f16 scale rounds q * s to f16 once, to nearest even -- the same bits as
+// rounding the exact f32 product.
+FLOCK_DEV uint2 tc_dequant4(uint32_t u, __half2 bias2, __half2 s2) {
+  const uint32_t lo = __byte_perm(u, 0x64646464u, 0x5140u);  // (v0, v1) + 1024
+  const uint32_t hi = __byte_perm(u, 0x64646464u, 0x7362u);  // (v2, v3) + 1024
+  const __half2 a = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&lo), bias2), s2);
+  const __half2 b = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&hi), bias2), s2);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
 }
 
 // Dequantise one block into chunks 4*half .. 4*half+3 of row t's swizzled
-// 128-byte row of the A stage.  The integers come out exact (2^23 + bias
-// trick), q * s is exact in f32 (8 x 11 significant bits) and rounds once to
-// f16.
+// 128-byte row of the A stage: q * s rounded once to f16 (q exact, s the
+// block's f16 scale as stored).
 template <int QT>
 FLOCK_DEV void tc_store_block(const TcRaw& r, uint8_t* A, int t, int half) {
-  const float s = scale_f16((uint16_t)(r.s & 0xFFFFu));
-  const uint64_t s2 = pack2(s, s);
+  const uint16_t sb = (uint16_t)(r.s & 0xFFFFu);
+  const __half2 s2 = __halves2half2(__ushort_as_half(sb), __ushort_as_half(sb));
+  // 1024 + 128 (Q8: int8 -> u8 by flipping the sign bit) or 1024 + 8 (Q4)
+  const __half2 bias2 = QT == QT_Q8 ? __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480))
+                                    : __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
 #pragma unroll
   for (int cc = 0; cc < 4; cc++) {
     uint32_t w0, w1;
-    uint64_t bias2;
     if (QT == QT_Q8) {
-      // weights 8cc..8cc+7 of the block; int8 -> u8 by flipping the sign bit
+      // weights 8cc..8cc+7 of the block
       const uint4 w = r.q[cc >> 1];
       w0 = ((cc & 1) ? w.z : w.x) ^ 0x80808080u;
       w1 = ((cc & 1) ? w.w : w.y) ^ 0x80808080u;
-      bias2 = pack2(8388736.0f, 8388736.0f);  // 2^23 + 128
     } else {
       // q4_coop.wgsl: byte i holds weights i (low nibble) and i+16 (high);
       // weights 8cc..8cc+7 are nibbles of bytes 8(cc&1).. , high for cc >= 2
@@ -221,7 +254,6 @@ FLOCK_DEV void tc_store_block(const TcRaw& r, uint8_t* A, int t, int half) {
       const int sh = cc < 2 ? 0 : 4;
       w0 = (((cc & 1) ? w.z : w.x) >> sh) & 0x0F0F0F0Fu;
       w1 = (((cc & 1) ? w.w : w.y) >> sh) & 0x0F0F0F0Fu;
-      bias2 = pack2(8388616.0f, 8388616.0f);  // 2^23 + 8
     }
     const uint2 lo = tc_dequant4(w0, bias2, s2), hi = tc_dequant4(w1, bias2, s2);
     *reinterpret_cast<uint4*>(A + sw128_off(t, 4 * half + cc)) = make_uint4(lo.x, lo.y, hi.x, hi.y);
@@ -235,7 +267,8 @@ FLOCK_DEV int tc_tmem_cols(int nt) {
 }
 
 template <int QT, int EPI>
-static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a) {
+static __global__ void __launch_bounds__(TC_THREADS, 1)
+    k_gemm_tc(const __grid_constant__ TcArgs a) {
   extern __shared__ __align__(16) uint8_t tsm_raw[];
   // the swizzle atoms must sit on 1024-byte boundaries: round the dynamic
   // shared memory up (the launch reserves 1 KiB of slack for this)
@@ -243,16 +276,28 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
   const int Nt = a.Nt;
   const int b_bytes = Nt * 128;
   const int stage_bytes = TC_A_BYTES + b_bytes;  // a multiple of 1024
-  uint64_t* full = reinterpret_cast<uint64_t*>(tsm + TC_STAGES * stage_bytes);
-  uint64_t* empty = full + TC_STAGES;
-  uint64_t* done = empty + TC_STAGES;
+  const int R = a.raw_stages;
+  uint8_t* rawbase = tsm + TC_STAGES * stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(rawbase + R * TC_RAW_BYTES);
+  uint64_t* bfull = full + TC_STAGES;    // the image tile's bulk copy landed
+  uint64_t* empty = bfull + TC_STAGES;   // the MMAs reading the stage completed
+  uint64_t* rfull = empty + TC_STAGES;   // a raw weight tile landed (TMA)
+  uint64_t* rempty = rfull + TC_RAW_MAX; // every converter read its raw block
+  uint64_t* done = rempty + TC_RAW_MAX;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int RAW_ROW = QT == QT_Q8 ? TC_KT : TC_KT / 2;  // raw bytes per row per K-tile
+  constexpr uint32_t RAW_TX = (uint32_t)(TC_ROWS * RAW_ROW);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; s++) {
       mbar_init(&full[s], TC_PRODUCERS);
+      mbar_init(&bfull[s], 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < R; s++) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], TC_PRODUCERS);
     }
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -277,38 +322,44 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
   const int kt_base = (int)blockIdx.z * KT;     // its first K-tile
 
   if (warp < TC_PRODUCERS / 32) {
-    // ------------------------------------------------------------ producers
+    // ----------------------------------------------------------- converters
     const int t = threadIdx.x & (TC_ROWS - 1), half = threadIdx.x >> 7;
     const int row = row0 + t;
     const bool rv = row < sg.rows;
-    const int lrow = rv ? row : sg.rows - 1;  // rows past the end load a real row, store nothing
-    TcRaw ring[TC_PREFETCH];
+    const int lrow = rv ? row : sg.rows - 1;  // rows past the end read a real scale, store nothing
+    const uint16_t* scp = sg.sc + (size_t)lrow * sg.sc_stride + half;
+    uint32_t scr[TC_SC_AHEAD];
 #pragma unroll
-    for (int j = 0; j < TC_PREFETCH; j++)
-      if (j < KT) tc_load_raw<QT>(ring[j], sg, a.K, lrow, half, kt_base + j);
+    for (int j = 0; j < TC_SC_AHEAD; j++)
+      if (j < KT) scr[j] = __ldg(scp + (kt_base + j) * 2);
     bool ok = true;
-    for (int kt0 = 0; kt0 < KT && ok; kt0 += TC_PREFETCH) {
+    for (int kt0 = 0; kt0 < KT && ok; kt0 += TC_SC_AHEAD) {
 #pragma unroll
-      for (int j = 0; j < TC_PREFETCH; j++) {
+      for (int j = 0; j < TC_SC_AHEAD; j++) {
         const int kt = kt0 + j;
         if (kt >= KT || !ok) break;
-        const int st = kt % TC_STAGES;
+        const int st = kt % TC_STAGES, rs = kt % R;
         if (kt >= TC_STAGES &&
-            !mbar_wait(&empty[st], (uint32_t)(((kt / TC_STAGES) - 1) & 1), a.err)) {
+            !mbar_wait_poll(&empty[st], (uint32_t)(((kt / TC_STAGES) - 1) & 1), a.err)) {
           atomicCAS(a.err, 0, 1);
           ok = false;
           break;
         }
         uint8_t* A = tsm + (size_t)st * stage_bytes;
-        if (threadIdx.x == 0) {
-          mbar_expect_tx_only(&full[st], (uint32_t)b_bytes);
-          bulk_g2s(A + TC_A_BYTES,
-                   a.img + ((size_t)mb * (a.K / TC_KT) + kt_base + kt) * (size_t)b_bytes,
-                   (uint32_t)b_bytes, &full[st]);
+        if (!mbar_wait_poll(&rfull[rs], (uint32_t)((kt / R) & 1), a.err)) {
+          atomicCAS(a.err, 0, 1);
+          ok = false;
+          break;
         }
-        tc_store_block<QT>(ring[j], A, t, half);
-        if (kt + TC_PREFETCH < KT)
-          tc_load_raw<QT>(ring[j], sg, a.K, lrow, half, kt_base + kt + TC_PREFETCH);
+        TcRaw r;
+        tc_read_raw<QT>(r, rawbase + rs * TC_RAW_BYTES, t, half);
+        r.s = scr[j];
+        // the block is in registers: order these generic reads before the
+        // loader's next (async-proxy) TMA write of the stage, then release it
+        fence_proxy_async_smem();
+        mbar_arrive(&rempty[rs]);
+        if (kt + TC_SC_AHEAD < KT) scr[j] = __ldg(scp + (kt_base + kt + TC_SC_AHEAD) * 2);
+        tc_store_block<QT>(r, A, t, half);
         fence_proxy_async_smem();
         mbar_arrive(&full[st]);
       }
@@ -346,24 +397,81 @@ static __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const TcArgs a
         }
       }
     }
-  } else if (lane == 0) {
+  } else if (warp == TC_PRODUCERS / 32) {
     // ----------------------------------------------------------- MMA issuer
-    const uint32_t idesc = umma_idesc_f16(TC_ROWS, Nt);
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(TC_ROWS, Nt);
+      for (int kt = 0; kt < KT; kt++) {
+        const int st = kt % TC_STAGES;
+        const uint32_t par = (uint32_t)((kt / TC_STAGES) & 1);
+        if (!mbar_wait_poll(&full[st], par, a.err) || !mbar_wait_poll(&bfull[st], par, a.err)) {
+          atomicCAS(a.err, 0, 1);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t A = smem_u32(tsm + (size_t)st * stage_bytes), B = A + TC_A_BYTES;
+#pragma unroll
+        for (int k16 = 0; k16 < TC_KT / 16; k16++)
+          umma_f16(tmem, umma_desc_sw128(A + 32 * k16), umma_desc_sw128(B + 32 * k16), idesc,
+                    (kt | k16) != 0);
+        umma_commit(&empty[st]);
+      }
+      umma_commit(done);
+    }
+  } else if (warp == TC_PRODUCERS / 32 + 2) {
+    // --------------------------------------------------------- image loader
+    // the B tile of K-tile kt goes into stage kt % TC_STAGES as soon as the
+    // MMAs of kt - TC_STAGES have released it
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      for (int kt = 0; kt < KT; kt++) {
+        const int st = kt % TC_STAGES;
+        if (kt >= TC_STAGES &&
+            !mbar_wait_poll(&empty[st], (uint32_t)(((kt / TC_STAGES) - 1) & 1), a.err)) {
+          atomicCAS(a.err, 0, 1);
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&bfull[st], (uint32_t)b_bytes);
+        // this CTA's Nt rows of the image tile that holds token m0 (an Nt
+        // subset of an image tile keeps the row swizzle: Nt is a multiple of 8)
+        bulk_g2s(tsm + (size_t)st * stage_bytes + TC_A_BYTES,
+                 a.img + ((size_t)(m0 / a.img_nt) * (a.K / TC_KT) + kt_base + kt) *
+                             (size_t)a.img_nt * 128 + (size_t)(m0 % a.img_nt) * 128,
+                 (uint32_t)b_bytes, &bfull[st]);
+        issued = kt + 1;
+      }
+      if (!ok) {
+        // let the copies still in flight land before the CTA can exit
+        for (int kt = issued > TC_STAGES ? issued - TC_STAGES : 0; kt < issued; kt++)
+          mbar_wait(&bfull[kt % TC_STAGES], (uint32_t)((kt / TC_STAGES) & 1), a.err, false);
+      }
+    }
+  } else if (lane == 0) {
+    // ----------------------------------------------------------- TMA loader
+    const CUtensorMap* map = &a.tmap[sgi];
+    tma_prefetch_desc(map);
+    int issued = 0;
+    bool ok = true;
     for (int kt = 0; kt < KT; kt++) {
-      const int st = kt % TC_STAGES;
-      if (!mbar_wait(&full[st], (uint32_t)((kt / TC_STAGES) & 1), a.err)) {
+      const int rs = kt % R;
+      if (kt >= R && !mbar_wait_poll(&rempty[rs], (uint32_t)(((kt / R) - 1) & 1), a.err)) {
         atomicCAS(a.err, 0, 1);
+        ok = false;
         break;
       }
-      tc_fence_after();
-      const uint32_t A = smem_u32(tsm + (size_t)st * stage_bytes), B = A + TC_A_BYTES;
-#pragma unroll
-      for (int k16 = 0; k16 < TC_KT / 16; k16++)
-        umma_f16(tmem, umma_desc_sw128(A + 32 * k16), umma_desc_sw128(B + 32 * k16), idesc,
-                  (kt | k16) != 0);
-      umma_commit(&empty[st]);
+      mbar_expect_tx(&rfull[rs], RAW_TX);
+      // x: the K-tile's first byte of the row (a multiple of 32 or 64 bytes);
+      // y: the tile's first row (rows past the end read as zeros)
+      tma_load_2d(rawbase + rs * TC_RAW_BYTES, map, (kt_base + kt) * RAW_ROW, row0, &rfull[rs]);
+      issued = kt + 1;
     }
-    umma_commit(done);
+    if (!ok) {
+      // let the copies still in flight land before the CTA can exit
+      for (int kt = issued > R ? issued - R : 0; kt < issued; kt++)
+        mbar_wait(&rfull[kt % R], (uint32_t)((kt / R) & 1), a.err, false);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -392,8 +500,22 @@ static __global__ void k_splitk_reduce(const float* part, int ksplit, int M, int
   out[m * out_stride + n] = s;
 }
 
+// Shared memory besides the raw ring: A/B stages, barriers, the TMEM slot,
+// and 1 KiB of alignment slack.
+inline size_t gemm_tc_fixed_smem(int nt) {
+  return (size_t)TC_STAGES * (TC_A_BYTES + nt * 128) + (3 * TC_STAGES + 2 * TC_RAW_MAX + 1) * 8 +
+         16 + 1024;
+}
+// Raw weight stages (8 KiB each).  Four: a 12-stage ring (all the shared
+// memory a 128-token tile leaves) measured slower on B200 -- 24.7 against
+// 20.9 us for the M = 512 q/k/v GEMM -- and at M = 16 it halves the CTAs an
+// SM holds.
+inline int tc_raw_stages(int nt) {
+  (void)nt;
+  return 4;
+}
 inline size_t gemm_tc_smem_bytes(int nt) {
-  return (size_t)TC_STAGES * (TC_A_BYTES + nt * 128) + (2 * TC_STAGES + 1) * 8 + 16 + 1024;
+  return gemm_tc_fixed_smem(nt) + (size_t)tc_raw_stages(nt) * TC_RAW_BYTES;
 }
 
 // ------------------------------------------------------- activation image
