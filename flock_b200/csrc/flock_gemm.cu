@@ -110,12 +110,30 @@ static int qs_tensor_map(CUtensorMap* out, const uint8_t* qs, int rows, int row_
               (const void*)qs, rows, row_bytes);
     return FLOCK_E_ARG;
   }
+  // the driver's encoder, looked up through the runtime so that loading this
+  // library needs no libcuda at link time (the CPU-only build host has none)
+  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn) {
+      set_error("cuTensorMapEncodeTiled is not available from the driver");
+      return FLOCK_E_CUDA;
+    }
+    encode = reinterpret_cast<EncodeFn>(fn);
+  }
   CUtensorMap m;
   const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
   const cuuint32_t box[2] = {(cuuint32_t)(qt == QT_Q8 ? TC_KT : TC_KT / 2), (cuuint32_t)TC_ROWS};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = cuTensorMapEncodeTiled(
+  const CUresult r = encode(
       &m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(qs), dims, strides, box, estr,
       CU_TENSOR_MAP_INTERLEAVE_NONE,
       qt == QT_Q8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
