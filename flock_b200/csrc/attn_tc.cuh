@@ -13,9 +13,19 @@
 //    one bulk copy per tile, so both products read K-major operands;
 //  * pass 1: S = q K^T per 128-key tile (tcgen05.mma 128x128x16, f32 in
 //    TMEM) -> exact row max m;  pass 2: S again, P = e^(S*scale - m) written
-//    as f16 into shared memory, O += P V^T accumulated in TMEM, l += sum P;
-//    the extra q K^T replaces any rescaling of O;
+//    as f16 into shared memory (over the K tile), O += P V^T accumulated in
+//    TMEM, l += sum P; the extra q K^T replaces any rescaling of O.  A range
+//    of one key tile needs one S only: its K and V^T copies are issued
+//    before the q staging and it runs a single pass;
 //  * out = O / l in f32.
+//  * the keys of a query tile are cut into gridDim.z contiguous ranges of
+//    whole key tiles, one CTA each (the two passes run over the CTA's own
+//    range); with more than one range every CTA writes its unnormalised O,
+//    its row max m and its sum l, and the o_proj activation image
+//    (k_act_image) merges the ranges in order as it reads them (out =
+//    sum_z e^(m_z - m) O_z / sum_z e^(m_z - m) l_z), so no extra pass over
+//    the output runs.  A 512-token prompt then runs one key tile per CTA
+//    over 160 CTAs with work instead of up to four tiles in turn over 64.
 //
 // Waits are bounded (mbar_wait); on a timeout the kernel sets *err, frees its
 // tensor memory and returns.  No multicast is used.
@@ -38,6 +48,7 @@ struct AttnTcArgs {
   const int* ctl;  // ctl[0] = pos0 (keys before this batch)
   int n_tokens, n_heads, n_kv_heads;
   int* err;
+  float* part;     // gridDim.z > 1: [z][n][nH][hd] unnormalised O, then [z][n][nH][2] (m, l)
 };
 
 // Byte offset of element (row r, column c) -- c < 128 -- in a 128-row operand
@@ -73,14 +84,17 @@ FLOCK_DEV void atc_mma(uint32_t d, uint32_t a, uint32_t b, bool accumulate) {
   }
 }
 
-static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const AttnTcArgs a) {
+static __global__ void __launch_bounds__(ATC_THREADS, 2) k_attn_prefill_tc(const AttnTcArgs a) {
   extern __shared__ __align__(16) uint8_t asm_raw[];
   uint8_t* base = asm_raw + ((1024u - (smem_u32(asm_raw) & 1023u)) & 1023u);
   uint8_t* sQ = base;
   uint8_t* sK = sQ + ATC_OPND;
   uint8_t* sV = sK + ATC_OPND;  // V^T: [head_dim][keys]
-  uint8_t* sP = sV + ATC_OPND;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + ATC_OPND);
+  // P is written over K: S = q K^T has completed (its commit was waited for)
+  // before any P store, and the next K lands only after P V^T completed --
+  // three operands of shared memory, so two CTAs fit an SM
+  uint8_t* sP = sK;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sV + ATC_OPND);
   uint64_t* ldbar = bar + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 2);
   __shared__ int s_stop;
@@ -95,12 +109,36 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
   const int kend = pos0 + last_q + 1;      // keys any query of the tile sees
   const int n_tiles = (kend + ATC_K - 1) / ATC_K;
   const float scale = __double2float_rn(1.0 / sqrt((double)ATC_HD));
+  // this CTA's key tiles [t0, t1)
+  const int nz = gridDim.z, z = blockIdx.z;
+  const int t0 = z * n_tiles / nz, t1 = (z + 1) * n_tiles / nz;
+  const bool single = t1 - t0 == 1;        // one tile: one S, one pass
+  float* const part_o = a.part + ((size_t)z * a.n_tokens + qi) * a.n_heads * ATC_HD +
+                        (size_t)h * ATC_HD;
+  float* const part_ml = a.part + (size_t)nz * a.n_tokens * a.n_heads * ATC_HD +
+                         (((size_t)z * a.n_tokens + qi) * a.n_heads + h) * 2;
+  if (t0 == t1) {  // no key tile in this range: an empty partial (the merge skips it)
+    if (qi < a.n_tokens) {
+      part_ml[0] = -INFINITY;
+      part_ml[1] = 0.0f;
+    }
+    return;
+  }
 
+  bool inflight = false;  // thread 0: copies issued on ldbar that no wait has seen land
+  auto issue = [&](int kt, bool with_v) {  // thread 0: K tile kt (and its V^T) by bulk copy
+    inflight = true;
+    const uint8_t* src = a.kv_img + ((size_t)g * a.img_tiles + kt) * 2 * ATC_OPND;
+    mbar_expect_tx(ldbar, (uint32_t)(with_v ? 2 : 1) * ATC_OPND);
+    bulk_g2s(sK, src, ATC_OPND, ldbar);
+    if (with_v) bulk_g2s(sV, src + ATC_OPND, ATC_OPND, ldbar);
+  };
   if (t == 0) {
     mbar_init(bar, 1);
     mbar_init(ldbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_stop = 0;
+    issue(t0, single);  // the first tile's copies overlap the q staging
   }
   if (warp == 0) {
     tmem_alloc(tslot, 256);
@@ -118,19 +156,18 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
   uint32_t phase = 0, ldphase = 0;
   bool ok = true;
 
-  // K tile kt (and its V^T tile) from the image by bulk copy; everyone waits
-  auto stage = [&](int kt, bool with_v) {
-    if (t == 0) {
-      const uint8_t* src = a.kv_img + ((size_t)g * a.img_tiles + kt) * 2 * ATC_OPND;
-      mbar_expect_tx(ldbar, (uint32_t)(with_v ? 2 : 1) * ATC_OPND);
-      bulk_g2s(sK, src, ATC_OPND, ldbar);
-      if (with_v) bulk_g2s(sV, src + ATC_OPND, ATC_OPND, ldbar);
-    }
+  auto land = [&]() {  // everyone: the copies issued on ldbar have landed
     if (!mbar_wait(ldbar, ldphase, a.err)) {
       atomicCAS(a.err, 0, 1);
       s_stop = 1;
+    } else {
+      inflight = false;
+      ldphase ^= 1;
     }
-    ldphase ^= 1;
+  };
+  auto stage = [&](int kt, bool with_v) {
+    if (t == 0) issue(kt, with_v);
+    land();
   };
   // issue S = q K^T (thread 0) and wait for it (everyone)
   auto scores = [&]() {
@@ -146,56 +183,42 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
     phase ^= 1;
     tc_fence_after();
   };
-
-  // ---------------------------------------------------------------- pass 1
-  float m = -INFINITY;
-  for (int kt = 0; kt < n_tiles && ok; kt++) {
+  // the row max of S over this thread's visible keys of tile kt
+  auto tile_max = [&](int kt, float m) {
     const int k0 = kt * ATC_K;
-    stage(kt, false);
-    tc_fence_before();
-    __syncthreads();
-    scores();
     for (int c0 = 0; c0 < ATC_K; c0 += 16) {
-      float s[16];
-      tmem_ld16(tS + lane_base + (uint32_t)c0, s);
+      float sv[16];
+      tmem_ld16(tS + lane_base + (uint32_t)c0, sv);
 #pragma unroll
       for (int j = 0; j < 16; j++)
-        if (k0 + c0 + j <= qpos) m = fmaxf(m, s[j] * scale);
+        if (k0 + c0 + j <= qpos) m = fmaxf(m, sv[j] * scale);
     }
-    tc_fence_before();
-    __syncthreads();
-    ok = !s_stop;
-  }
-  // ---------------------------------------------------------------- pass 2
-  float l = 0.0f;
-  for (int kt = 0; kt < n_tiles && ok; kt++) {
+    return m;
+  };
+  // P = e^(S scale - m) into sP (f16), l += sum P, then O (+)= P V^T
+  auto tile_pv = [&](int kt, float m, float& l) {
     const int k0 = kt * ATC_K;
-    stage(kt, true);
-    tc_fence_before();
-    __syncthreads();
-    scores();
     for (int c0 = 0; c0 < ATC_K; c0 += 16) {
-      float s[16];
-      tmem_ld16(tS + lane_base + (uint32_t)c0, s);
+      float sv[16];
+      tmem_ld16(tS + lane_base + (uint32_t)c0, sv);
       float p[16];
 #pragma unroll
       for (int j = 0; j < 16; j++) {
-        p[j] = k0 + c0 + j <= qpos ? expf(s[j] * scale - m) : 0.0f;
+        p[j] = k0 + c0 + j <= qpos ? expf(sv[j] * scale - m) : 0.0f;
         l += p[j];
       }
 #pragma unroll
-      for (int half = 0; half < 2; half++)
-        *reinterpret_cast<uint4*>(sP + atc_off(t, (c0 >> 3) + half)) =
-            make_uint4(h2(p[8 * half], p[8 * half + 1]), h2(p[8 * half + 2], p[8 * half + 3]),
-                       h2(p[8 * half + 4], p[8 * half + 5]),
-                       h2(p[8 * half + 6], p[8 * half + 7]));
+      for (int hf = 0; hf < 2; hf++)
+        *reinterpret_cast<uint4*>(sP + atc_off(t, (c0 >> 3) + hf)) =
+            make_uint4(h2(p[8 * hf], p[8 * hf + 1]), h2(p[8 * hf + 2], p[8 * hf + 3]),
+                       h2(p[8 * hf + 4], p[8 * hf + 5]), h2(p[8 * hf + 6], p[8 * hf + 7]));
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     if (t == 0) {
       tc_fence_after();
-      atc_mma(tO, smem_u32(sP), smem_u32(sV), kt > 0);
+      atc_mma(tO, smem_u32(sP), smem_u32(sV), kt > t0);
       umma_commit(bar);
     }
     if (!mbar_wait(bar, phase, a.err)) {
@@ -205,13 +228,54 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
     phase ^= 1;
     tc_fence_after();
     __syncthreads();
+  };
+
+  float m = -INFINITY, l = 0.0f;
+  if (single) {
+    // K and V^T were issued together: one S, its max, then P and P V^T
+    land();
+    tc_fence_before();
+    __syncthreads();
     ok = !s_stop;
+    if (ok) {
+      scores();
+      m = tile_max(t0, m);
+      tile_pv(t0, m, l);
+      ok = !s_stop;
+    }
+  } else {
+    // pass 1: the exact row max over the range (K only; the first K was issued)
+    for (int kt = t0; kt < t1 && ok; kt++) {
+      if (kt == t0) land();
+      else stage(kt, false);
+      tc_fence_before();
+      __syncthreads();
+      scores();
+      m = tile_max(kt, m);
+      tc_fence_before();
+      __syncthreads();
+      ok = !s_stop;
+    }
+    // pass 2: S again, P and O += P V^T (no rescaling of O)
+    for (int kt = t0; kt < t1 && ok; kt++) {
+      stage(kt, true);
+      tc_fence_before();
+      __syncthreads();
+      scores();
+      tile_pv(kt, m, l);
+      ok = !s_stop;
+    }
   }
   // --------------------------------------------------------------- epilogue
   if (ok) {
     // every lane takes part in the warp-collective loads; rows past n store nothing
-    float* dst = a.out + ((size_t)qi * a.n_heads + h) * ATC_HD;
-    const float inv = 1.0f / l;
+    const bool whole = nz == 1;
+    float* dst = whole ? a.out + ((size_t)qi * a.n_heads + h) * ATC_HD : part_o;
+    const float inv = whole ? 1.0f / l : 1.0f;  // a range keeps O unnormalised
+    if (!whole && qi < a.n_tokens) {
+      part_ml[0] = m;
+      part_ml[1] = l;
+    }
     for (int c0 = 0; c0 < ATC_HD; c0 += 16) {
       float o[16];
       tmem_ld16(tO + lane_base + (uint32_t)c0, o);
@@ -222,6 +286,9 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
               make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
       }
     }
+  } else if (t == 0 && inflight) {
+    // a wait gave up: let the copies still in flight land before the exit
+    mbar_wait(ldbar, ldphase, a.err, false);
   }
   tc_fence_before();
   __syncthreads();
@@ -231,7 +298,19 @@ static __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_prefill_tc(const
   }
 }
 
-inline size_t attn_tc_smem_bytes() { return 4 * (size_t)ATC_OPND + 24 + 1024; }
+inline size_t attn_tc_smem_bytes() { return 3 * (size_t)ATC_OPND + 24 + 1024; }
+
+constexpr int ATC_MAX_SPLITS = 8;  // key ranges per query tile, at most
+static_assert(ATC_MAX_SPLITS <= ATC_MAX_SPLITS_IMG, "the o_proj image merges every range");
+
+// Key ranges per query tile for n queries after pos0 cached keys: one key
+// tile per CTA as far as ATC_MAX_SPLITS allows (the last query tile sees
+// the most tiles).
+inline int attn_tc_splits(int pos0_max, int n) {
+  const int tiles = (pos0_max + n + ATC_K - 1) / ATC_K;
+  return tiles < 1 ? 1 : (tiles > ATC_MAX_SPLITS ? ATC_MAX_SPLITS : tiles);
+}
+
 
 // The f16 image of keys [0, kend) of the cache for k_attn_prefill_tc, kend =
 // ctl[0] + n (the position block already advanced for this step): per (key

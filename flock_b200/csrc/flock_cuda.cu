@@ -255,6 +255,7 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
     FLOCK_CK(cudaMemset(tc_err.p, 0, 16));
     FLOCK_TRY(part.alloc((size_t)8 * P * H * f));
     FLOCK_TRY(kv_img.alloc(kv_image_bytes(c.max_keys, nKV)));
+    FLOCK_TRY(atc_part.alloc((size_t)ATC_MAX_SPLITS * P * nH * (hd + 2) * f));
   }
   if (tp_ranks >= 1 || H >= FLOCK_SPLIT_RESIDUAL_MIN_HIDDEN)  // also the split residual
     FLOCK_TRY(tp_part.alloc((size_t)P * H * f));
@@ -405,10 +406,17 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
     ta.n_heads = c.n_heads;
     ta.n_kv_heads = c.n_kv_heads;
     ta.err = ws->tc_err.as<int>();
+    ta.part = ws->atc_part.as<float>();
+    // key ranges: sized from the host's count of cached keys (the kernel
+    // reads pos0 on the device; a range past its query tile's keys is empty)
+    const int nz = attn_tc_splits(L->n_keys, n);
     FLOCK_TRY(kernel_setup((const void*)k_attn_prefill_tc, (int)attn_tc_smem_bytes()));
-    k_attn_prefill_tc<<<dim3((n + ATC_Q - 1) / ATC_Q, c.n_heads), ATC_THREADS,
+    k_attn_prefill_tc<<<dim3((n + ATC_Q - 1) / ATC_Q, c.n_heads, nz), ATC_THREADS,
                         attn_tc_smem_bytes(), d->stream>>>(ta);
     FLOCK_CK(cudaGetLastError());
+    // with several key ranges the o_proj activation image merges them
+    // (act_image_enqueue); ws->attn is then not written
+    ws->atc_nz = nz;
   } else if (n == 1) {
     const size_t smem = (size_t)c.max_keys * sizeof(float);
     FLOCK_TRY(kernel_setup((const void*)k_attn_decode_exact, 200 * 1024));
@@ -419,15 +427,6 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
                        aa));
   }
   return FLOCK_OK;
-}
-
-// SwiGLU over rows of [gate | up] (ops_ref.ts:103 swigluRef order).
-static __global__ void k_swiglu_rows(const float* gu, float* act, int n, int F) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)n * F) return;
-  const int64_t m = i / F, f = i - m * F;
-  const float g = gu[m * 2 * F + f], u = gu[m * 2 * F + F + f];
-  act[i] = fmul(fdiv(g, fadd(1.0f, exp_f64r(-g))), u);
 }
 
 // Tensor parallel: h[i] += (p_0[i] + p_1[i] + ... + p_{N-1}[i]), the ranks'
@@ -485,6 +484,7 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
             F = c.ffn;
   uint8_t* img = ws->img.as<uint8_t>();
   int* err = ws->tc_err.as<int>();
+  int o_split = 1;  // K-splits of the o_proj GEMM whose partials the ffn image sums
   if (advance) {
     k_ctl_advance<<<1, 1, 0, st>>>(L->ctl, n);
     FLOCK_CK(cudaGetLastError());
@@ -505,7 +505,10 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
   }
   FLOCK_TRY(enqueue_qk_attn(L, n, false, true));
   {  // o_proj + residual on h
-    FLOCK_TRY(act_image_enqueue(st, ws->attn.as<float>(), qw, nullptr, 0.0f, n, qw, img));
+    FLOCK_TRY(ws->atc_nz > 1 ? act_image_enqueue(st, nullptr, qw, nullptr, 0.0f, n, qw, img,
+                                                 ws->atc_part.as<float>(), ws->atc_nz, c.n_heads)
+                             : act_image_enqueue(st, ws->attn.as<float>(), qw, nullptr, 0.0f, n,
+                                                 qw, img));
     TcArgs a = {};
     a.seg[0] = tc_seg_of(L->w[W_O], L->tp ? ws->tp_part.as<float>() : ws->h.as<float>(), H);
     a.nseg = 1;
@@ -516,13 +519,20 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.res_stride = H;
     a.err = err;
     a.part = ws->part.as<float>();
+    // a split-K o_proj leaves its partials for the ffn_norm image to sum
     FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, L->tp ? EPI_STORE : EPI_RESIDUAL, a, d->sm_count,
-                              ws->part.bytes / 4));
+                              ws->part.bytes / 4, !L->tp));
     if (L->tp) FLOCK_TRY(tp_sum_into_h(L, n));
+    o_split = L->tp ? 1 : a.ksplit;
   }
-  {  // ffn_norm + gate | up, SwiGLU
-    FLOCK_TRY(act_image_enqueue(st, ws->h.as<float>(), H, L->w[W_FFN_NORM]->data.as<float>(),
-                                c.eps, n, H, img));
+  {  // ffn_norm (h = residual + o_proj, when split) + gate | up
+    if (o_split > 1)
+      FLOCK_TRY(act_image_reduce_enqueue(st, ws->h.as<float>(), ws->part.as<float>(), o_split,
+                                         ws->h.as<float>(),
+                                         L->w[W_FFN_NORM]->data.as<float>(), c.eps, n, H, img));
+    else
+      FLOCK_TRY(act_image_enqueue(st, ws->h.as<float>(), H,
+                                  L->w[W_FFN_NORM]->data.as<float>(), c.eps, n, H, img));
     TcArgs a = {};
     a.seg[0] = tc_seg_of(L->w[W_GATE], ws->gu.as<float>(), 2 * F);
     a.seg[1] = tc_seg_of(L->w[W_UP], ws->gu.as<float>() + F, 2 * F);
@@ -532,13 +542,9 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.img = img;
     a.err = err;
     FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_STORE, a, d->sm_count, ws->part.bytes / 4));
-    const int64_t total = (int64_t)n * F;
-    k_swiglu_rows<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(ws->gu.as<float>(),
-                                                                    ws->act.as<float>(), n, F);
-    FLOCK_CK(cudaGetLastError());
   }
-  {  // down + residual on h
-    FLOCK_TRY(act_image_enqueue(st, ws->act.as<float>(), F, nullptr, 0.0f, n, F, img));
+  {  // SwiGLU (in the image pass) + down + residual on h
+    FLOCK_TRY(act_image_swiglu_enqueue(st, ws->gu.as<float>(), n, F, img));
     TcArgs a = {};
     a.seg[0] = tc_seg_of(L->w[W_DOWN], L->tp ? ws->tp_part.as<float>() : ws->h.as<float>(), H);
     a.nseg = 1;

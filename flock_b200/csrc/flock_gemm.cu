@@ -26,10 +26,18 @@ size_t act_image_bytes(int M, int K) {
   return act_image_only_bytes(M, K) + (size_t)((M + nt - 1) / nt) * nt * 4;
 }
 
+static int act_image_launch(cudaStream_t st, ActImgArgs& a);
+
 int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float* gain, float eps,
-                      int M, int K, uint8_t* img) {
+                      int M, int K, uint8_t* img, const float* atc_part, int atc_nz,
+                      int n_heads) {
   if (K % TC_KT || K > 12288 || M < 1) {
     set_error("tensor-core GEMM needs K a multiple of 64 and at most 12288 (K = %d)", K);
+    return FLOCK_E_ARG;
+  }
+  if (atc_part && (atc_nz < 1 || atc_nz > ATC_MAX_SPLITS_IMG || n_heads < 1 || n_heads > 32 ||
+                   K % (4 * n_heads))) {
+    set_error("attention range merge: %d ranges over %d heads", atc_nz, n_heads);
     return FLOCK_E_ARG;
   }
   ActImgArgs a = {};
@@ -39,13 +47,49 @@ int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float
   a.eps = eps;
   a.M = M;
   a.K = K;
-  a.Nt = tc_token_tile(M);
   a.img = img;
-  a.row_exp = reinterpret_cast<int*>(img + act_image_only_bytes(M, K));
-  const int rows = (M + a.Nt - 1) / a.Nt * a.Nt;
-  const size_t smem = (size_t)ACT_IMG_ROWS * K * 4;
-  FLOCK_TRY(kernel_setup((const void*)k_act_image, ACT_IMG_ROWS * 12288 * 4));
-  k_act_image<<<(rows + ACT_IMG_ROWS - 1) / ACT_IMG_ROWS, ACT_IMG_THREADS, smem, st>>>(a);
+  a.part = atc_part;
+  a.nz = atc_nz;
+  a.n_heads = n_heads;
+  return act_image_launch(st, a);
+}
+
+int act_image_reduce_enqueue(cudaStream_t st, const float* res, const float* red_part, int red_nz,
+                             float* x_out, const float* gain, float eps, int M, int K,
+                             uint8_t* img) {
+  if (K % TC_KT || K > 12288 || M < 1 || red_nz < 1) return FLOCK_E_ARG;
+  ActImgArgs a = {};
+  a.x = res;
+  a.x_stride = K;
+  a.gain = gain;
+  a.eps = eps;
+  a.M = M;
+  a.K = K;
+  a.img = img;
+  a.red_part = red_part;
+  a.red_nz = red_nz;
+  a.x_out = x_out;
+  return act_image_launch(st, a);
+}
+
+int act_image_swiglu_enqueue(cudaStream_t st, const float* gu, int M, int K, uint8_t* img) {
+  if (K % TC_KT || K > 12288 || M < 1) return FLOCK_E_ARG;
+  ActImgArgs a = {};
+  a.x_stride = K;
+  a.M = M;
+  a.K = K;
+  a.img = img;
+  a.gu = gu;
+  return act_image_launch(st, a);
+}
+
+static int act_image_launch(cudaStream_t st, ActImgArgs& a) {
+  const int M = a.M, K = a.K;
+  a.Nt = tc_token_tile(M);
+  a.row_exp = reinterpret_cast<int*>(a.img + act_image_only_bytes(M, K));
+  const int rows = (M + a.Nt - 1) / a.Nt * a.Nt;  // image rows, zero past M
+  FLOCK_TRY(kernel_setup((const void*)k_act_image, (int)act_image_smem_bytes(12288)));
+  k_act_image<<<rows, ACT_IMG_THREADS, act_image_smem_bytes(K), st>>>(a);
   FLOCK_CK(cudaGetLastError());
   return FLOCK_OK;
 }
@@ -71,14 +115,14 @@ void tc_finish_tiles(TcArgs& a) {
 }
 
 template <int QT, int EPI>
-static int launch_tc(cudaStream_t st, const TcArgs& a) {
+static int launch_tc(cudaStream_t st, const TcArgs& a, bool defer_reduce) {
   FLOCK_TRY(kernel_setup((const void*)k_gemm_tc<QT, EPI>, TC_SMEM_MAX));
   const size_t smem = gemm_tc_smem_bytes(a.Nt);
   const dim3 grid((unsigned)a.tile0[a.nseg], (unsigned)((a.M + a.Nt - 1) / a.Nt),
                   (unsigned)a.ksplit);
   k_gemm_tc<QT, EPI><<<grid, TC_THREADS, smem, st>>>(a);
   FLOCK_CK(cudaGetLastError());
-  if (a.ksplit > 1) {
+  if (a.ksplit > 1 && !defer_reduce) {
     const TcSeg& s = a.seg[0];
     const int64_t total = (int64_t)a.M * s.rows;
     k_splitk_reduce<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
@@ -151,9 +195,11 @@ static int qs_tensor_map(CUtensorMap* out, const uint8_t* qs, int rows, int row_
 // Y = X . W^T for the segments of `a` on the tensor cores; `a.img` must hold
 // the activation image of the same M and K.  With `part` (room for
 // part_floats) and one segment, a grid too small for the GPU is split along
-// K (at least 8 K-tiles per CTA) and reduced by k_splitk_reduce.
+// K (at least 8 K-tiles per CTA) and reduced by k_splitk_reduce -- or, with
+// defer_reduce, left as partials in a.part (a.ksplit of them) for the
+// caller's next activation image to sum (act_image_reduce_enqueue).
 int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a, int sm_count,
-                    size_t part_floats) {
+                    size_t part_floats, bool defer_reduce) {
   if (a.K % TC_KT || a.M < 1 || a.nseg < 1 || a.nseg > 3) return FLOCK_E_ARG;
   for (int i = 0; i < a.nseg; i++)
     FLOCK_TRY(qs_tensor_map(&a.tmap[i], a.seg[i].qs, a.seg[i].rows,
@@ -182,10 +228,10 @@ int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a, int sm_count,
     }
   }
   if (qt == QT_Q8)
-    return epi == EPI_RESIDUAL ? launch_tc<QT_Q8, EPI_RESIDUAL>(st, a)
-                               : launch_tc<QT_Q8, EPI_STORE>(st, a);
-  return epi == EPI_RESIDUAL ? launch_tc<QT_Q4, EPI_RESIDUAL>(st, a)
-                             : launch_tc<QT_Q4, EPI_STORE>(st, a);
+    return epi == EPI_RESIDUAL ? launch_tc<QT_Q8, EPI_RESIDUAL>(st, a, defer_reduce)
+                               : launch_tc<QT_Q8, EPI_STORE>(st, a, defer_reduce);
+  return epi == EPI_RESIDUAL ? launch_tc<QT_Q4, EPI_RESIDUAL>(st, a, defer_reduce)
+                             : launch_tc<QT_Q4, EPI_STORE>(st, a, defer_reduce);
 }
 
 }  // namespace flock

@@ -93,6 +93,8 @@ struct Workspace {
   DBuf img, gu, tc_err, part;   // tensor-core prefill: activation image, gate|up rows, error word,
                                 // split-K partials
   DBuf kv_img;                  // tensor-core prefill: f16 K / V^T tiles of the cache
+  DBuf atc_part;                // tensor-core prefill attention: per key range O, m, l
+  int atc_nz = 1;               // key ranges of the last tensor-core attention launch
   DBuf tp_part, tp_all;         // tensor parallel: this rank's partial [P][H], all ranks
   DBuf wire;                    // FLK1 frames: the f16 payload on the device
   // tp_ranks >= 1 (a tensor-parallel model, one rank included): also the
@@ -112,9 +114,18 @@ struct TcSeg;
 struct PeerXchg;
 size_t act_image_bytes(int M, int K);
 int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float* gain, float eps,
-                      int M, int K, uint8_t* img);
+                      int M, int K, uint8_t* img, const float* atc_part = nullptr, int atc_nz = 0,
+                      int n_heads = 0);
+// The activation image of x = res + the split-K partials [red_nz][M][K]
+// (summed as k_splitk_reduce sums them; x is also written to x_out), or of
+// the SwiGLU of [gate | up] rows [M][2K] -- the reduce and SwiGLU kernels
+// folded into the image pass.
+int act_image_reduce_enqueue(cudaStream_t st, const float* res, const float* red_part, int red_nz,
+                             float* x_out, const float* gain, float eps, int M, int K,
+                             uint8_t* img);
+int act_image_swiglu_enqueue(cudaStream_t st, const float* gu, int M, int K, uint8_t* img);
 int gemm_tc_enqueue(cudaStream_t st, int qt, int epi, TcArgs& a, int sm_count,
-                    size_t part_floats);
+                    size_t part_floats, bool defer_reduce = false);
 TcSeg tc_seg_of(const flock_tensor* t, float* out, int out_stride);
 // tensor-core prefill's device error word: FLOCK_E_CUDA (and cleared) if a tensor-core
 // GEMM gave up waiting since the last check; call after a synchronisation.

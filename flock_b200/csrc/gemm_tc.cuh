@@ -521,12 +521,15 @@ inline size_t gemm_tc_smem_bytes(int nt) {
 // ------------------------------------------------------- activation image
 // X (f32 [M][x_stride]) -> f16 image [M / Nt][K / 64][Nt][128 B] in the
 // swizzled K-major layout, RMSNorm fused when `gain` is set (ops_ref.ts:20
-// order: WG = 128 strided partials -- lane l of the warp folds partials l,
-// l+32, l+64, l+96 -- the pairwise tree, 1/sqrt in f64 rounded once, then
-// x * scale * gain rounded per multiply); each row is scaled by 2^-e
-// (row_exponent of its largest magnitude) before rounding to f16 and e is
-// stored in row_exp.  One warp per image row, no block barriers; rows >= M
-// are written as zeros.
+// order: thread t of the row's 128 folds the strided partial t = sum over
+// i = t, t+128, ... of x_i^2 with fma in order, then the pairwise tree over
+// the 128 partials, 1/sqrt in f64 rounded once, then x * scale * gain rounded
+// per multiply); each row is scaled by 2^-e (row_exponent of its largest
+// magnitude) before rounding to f16 and e is stored in row_exp.  One CTA of
+// 128 threads per image row, the row staged in shared memory; rows >= M
+// are written as zeros.  The row can also be formed on the way in: merged
+// from the attention's key ranges, summed from split-K partials plus the
+// residual (and written back), or the SwiGLU of [gate | up].
 struct ActImgArgs {
   const float* x;
   int x_stride;
@@ -535,71 +538,146 @@ struct ActImgArgs {
   int M, K, Nt;
   uint8_t* img;
   int* row_exp;
+  // instead of x: the key ranges of the tensor-core prefill attention
+  // ([nz][M][K] unnormalised O, then [nz][M][n_heads][2] (m, l)), merged here
+  const float* part;
+  int nz, n_heads;
+  // x = res + sum of split-K partials ([red_nz][M][K], the order of
+  // k_splitk_reduce), also written back to x_out (the residual stream)
+  const float* red_part;
+  int red_nz;
+  float* x_out;
+  // x = SwiGLU of [gate | up] rows ([M][2K], ops_ref.ts:103 order)
+  const float* gu;
 };
 
-constexpr int ACT_IMG_THREADS = 128;
-constexpr int ACT_IMG_ROWS = ACT_IMG_THREADS / 32;  // rows per CTA
+constexpr int ACT_IMG_THREADS = 128;                // one CTA per row: the RMSNorm's WG
+constexpr int ATC_MAX_SPLITS_IMG = 8;               // attention key ranges the merge takes
+
+// shared memory: the row [K], the 128 partials / maxima, the merge weights
+inline size_t act_image_smem_bytes(int K) {
+  return ((size_t)K + ACT_IMG_THREADS + ATC_MAX_SPLITS_IMG * 32 + 32) * 4;
+}
 
 static __global__ void __launch_bounds__(ACT_IMG_THREADS) k_act_image(const ActImgArgs a) {
-  extern __shared__ __align__(16) float xrows[];  // [ACT_IMG_ROWS][K]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = blockIdx.x * ACT_IMG_ROWS + warp;
-  const int n_mb = (a.M + a.Nt - 1) / a.Nt;
-  if (m >= n_mb * a.Nt) return;
+  extern __shared__ __align__(16) float xr[];  // [K] row, then scratch
+  float* red = xr + a.K;                       // [128]
+  float* w = red + ACT_IMG_THREADS;            // [ATC_MAX_SPLITS_IMG][32] merge weights
+  float* winv = w + ATC_MAX_SPLITS_IMG * 32;   // [32]
+  const int t = threadIdx.x;
+  const int m = blockIdx.x;
   const int r = m % a.Nt, mb = m / a.Nt, KT = a.K / TC_KT;
   uint8_t* base = a.img + (size_t)mb * KT * a.Nt * 128;
   if (m >= a.M) {
-    for (int i = lane; i < a.K / 8; i += 32)
+    for (int i = t; i < a.K / 8; i += ACT_IMG_THREADS)
       *reinterpret_cast<uint4*>(base + (size_t)(i >> 3) * a.Nt * 128 + sw128_off(r, i & 7)) =
           make_uint4(0, 0, 0, 0);
-    if (lane == 0) a.row_exp[m] = 0;
+    if (t == 0) a.row_exp[m] = 0;
     return;
   }
-  float* xr = xrows + (size_t)warp * a.K;
-  const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)m * a.x_stride);
-  for (int i = lane; i < a.K / 4; i += 32) reinterpret_cast<float4*>(xr)[i] = src[i];
-  __syncwarp();
+  float4* x4 = reinterpret_cast<float4*>(xr);
+  const int K4 = a.K / 4;
+  if (a.part) {
+    // merge the attention's key ranges (k_attn_prefill_tc): thread hh derives
+    // head hh's range weights e^(m_z - m) and 1 / l, l = sum_z e^(m_z - m) l_z,
+    // then every element is the weighted sum of its ranges in order
+    const float* ml = a.part + (size_t)a.nz * a.M * a.K;
+    if (t < a.n_heads) {
+      float mx = -INFINITY, l = 0.0f;
+      for (int z = 0; z < a.nz; z++) {
+        const float* p = ml + (((size_t)z * a.M + m) * a.n_heads + t) * 2;
+        if (p[1] > 0.0f) mx = fmaxf(mx, p[0]);
+      }
+      for (int z = 0; z < a.nz; z++) {
+        const float* p = ml + (((size_t)z * a.M + m) * a.n_heads + t) * 2;
+        const float e = p[1] > 0.0f ? expf(p[0] - mx) : 0.0f;
+        w[z * 32 + t] = e;
+        l += e * p[1];
+      }
+      winv[t] = 1.0f / l;
+    }
+    __syncthreads();
+    const int hd4 = K4 / a.n_heads;  // float4s per head
+    for (int i = t; i < K4; i += ACT_IMG_THREADS) {
+      const int hh = i / hd4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int z = 0; z < a.nz; z++) {
+        const float wz = w[z * 32 + hh];
+        if (wz != 0.0f) {
+          const float4 o = reinterpret_cast<const float4*>(a.part + ((size_t)z * a.M + m) * a.K)[i];
+          acc = make_float4(fmaf(wz, o.x, acc.x), fmaf(wz, o.y, acc.y), fmaf(wz, o.z, acc.z),
+                            fmaf(wz, o.w, acc.w));
+        }
+      }
+      const float inv = winv[hh];
+      x4[i] = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    }
+  } else if (a.red_part) {
+    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)m * a.x_stride);
+    float4* dst = reinterpret_cast<float4*>(a.x_out + (size_t)m * a.x_stride);
+    const size_t plane4 = (size_t)a.M * a.K / 4;
+    for (int i = t; i < K4; i += ACT_IMG_THREADS) {
+      const float4* p = reinterpret_cast<const float4*>(a.red_part + (size_t)m * a.K) + i;
+      float4 v = p[0];
+      for (int z = 1; z < a.red_nz; z++) {
+        const float4 u = p[z * plane4];
+        v = make_float4(fadd(v.x, u.x), fadd(v.y, u.y), fadd(v.z, u.z), fadd(v.w, u.w));
+      }
+      const float4 rr = src[i];
+      v = make_float4(fadd(rr.x, v.x), fadd(rr.y, v.y), fadd(rr.z, v.z), fadd(rr.w, v.w));
+      x4[i] = v;
+      dst[i] = v;
+    }
+  } else if (a.gu) {
+    const float4* g4 = reinterpret_cast<const float4*>(a.gu + (size_t)m * 2 * a.K);
+    const float4* u4 = reinterpret_cast<const float4*>(a.gu + (size_t)m * 2 * a.K + a.K);
+    auto sw = [](float g, float u) { return fmul(fdiv(g, fadd(1.0f, exp_f64r(-g))), u); };
+    for (int i = t; i < K4; i += ACT_IMG_THREADS) {
+      const float4 g = g4[i], u = u4[i];
+      x4[i] = make_float4(sw(g.x, u.x), sw(g.y, u.y), sw(g.z, u.z), sw(g.w, u.w));
+    }
+  } else {
+    const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)m * a.x_stride);
+    for (int i = t; i < K4; i += ACT_IMG_THREADS) x4[i] = src[i];
+  }
+  __syncthreads();
   float scale = 1.0f;
   if (a.gain) {
-    float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int q = 0; q < 4; q++)
-      for (int i = lane + 32 * q; i < a.K; i += 128) p[q] = ffma(xr[i], xr[i], p[q]);
-    float v = fadd(fadd(p[0], p[2]), fadd(p[1], p[3]));
-    v = warp_tree_sum(v);
-    v = __shfl_sync(0xffffffffu, v, 0);
-    scale = rsqrt_f64r(fadd(fdiv(v, (float)a.K), a.eps));
-  }
-  // pass 1: the row's final values (in place) and their largest magnitude
-  float mx = 0.0f;
-#pragma unroll 4
-  for (int i = lane; i < a.K / 8; i += 32) {
-    float4* p = reinterpret_cast<float4*>(xr) + 2 * i;
-    float4 x0 = p[0], x1 = p[1];
-    if (a.gain) {
-      const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gain) + 2 * i);
-      const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gain) + 2 * i + 1);
-      x0 = make_float4(fmul(fmul(x0.x, scale), g0.x), fmul(fmul(x0.y, scale), g0.y),
-                       fmul(fmul(x0.z, scale), g0.z), fmul(fmul(x0.w, scale), g0.w));
-      x1 = make_float4(fmul(fmul(x1.x, scale), g1.x), fmul(fmul(x1.y, scale), g1.y),
-                       fmul(fmul(x1.z, scale), g1.z), fmul(fmul(x1.w, scale), g1.w));
-      p[0] = x0;
-      p[1] = x1;
+    // ops_ref.ts:20: partial t over i = t, t+128, ... in order, then the tree
+    float p = 0.0f;
+    for (int i = t; i < a.K; i += ACT_IMG_THREADS) p = ffma(xr[i], xr[i], p);
+    red[t] = p;
+    __syncthreads();
+    for (int s = ACT_IMG_THREADS / 2; s > 0; s >>= 1) {
+      if (t < s) red[t] = fadd(red[t], red[t + s]);
+      __syncthreads();
     }
-    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x0.x), fabsf(x0.y)), fmaxf(fabsf(x0.z), fabsf(x0.w))));
-    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x1.x), fabsf(x1.y)), fmaxf(fabsf(x1.z), fabsf(x1.w))));
+    scale = rsqrt_f64r(fadd(fdiv(red[0], (float)a.K), a.eps));
+    __syncthreads();  // red is reused for the maxima
+  }
+  // the row's final values (in place) and their largest magnitude
+  float mx = 0.0f;
+  for (int i = t; i < K4; i += ACT_IMG_THREADS) {
+    float4 x = x4[i];
+    if (a.gain) {
+      const float4 g = __ldg(reinterpret_cast<const float4*>(a.gain) + i);
+      x = make_float4(fmul(fmul(x.x, scale), g.x), fmul(fmul(x.y, scale), g.y),
+                      fmul(fmul(x.z, scale), g.z), fmul(fmul(x.w, scale), g.w));
+      x4[i] = x;
+    }
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((t & 31) == 0) red[t >> 5] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   const int e = row_exponent(mx);
-  if (lane == 0) a.row_exp[m] = e;
-  __syncwarp();
-  // pass 2: x * 2^-e (exact) rounded to f16, swizzled
+  if (t == 0) a.row_exp[m] = e;
+  // x * 2^-e (exact) rounded to f16, swizzled
   const float sc = pow2f(-e);
-#pragma unroll 4
-  for (int i = lane; i < a.K / 8; i += 32) {
-    const float4 x0 = reinterpret_cast<const float4*>(xr)[2 * i];
-    const float4 x1 = reinterpret_cast<const float4*>(xr)[2 * i + 1];
+  for (int i = t; i < a.K / 8; i += ACT_IMG_THREADS) {
+    const float4 x0 = x4[2 * i], x1 = x4[2 * i + 1];
     *reinterpret_cast<uint4*>(base + (size_t)(i >> 3) * a.Nt * 128 + sw128_off(r, i & 7)) =
         make_uint4(h2(x0.x * sc, x0.y * sc), h2(x0.z * sc, x0.w * sc), h2(x1.x * sc, x1.y * sc),
                    h2(x1.z * sc, x1.w * sc));
