@@ -312,13 +312,17 @@ inline int attn_tc_splits(int pos0_max, int n) {
 }
 
 
-// The f16 image of keys [0, kend) of the cache for k_attn_prefill_tc, kend =
-// ctl[0] + n (the position block already advanced for this step): per (key
-// tile, kv head) one CTA writes the K tile ([key][head_dim], rows past kend
-// zero) and the V^T tile ([head_dim][key]), transposed through shared memory
-// so every global load is a coalesced row.  The grid covers the cache's
-// capacity; tiles past kend return at once.  BF16: the cache holds bf16,
-// widened exactly before the f16 rounding.
+// The f16 image of the cached keys [0, pos0) for k_attn_prefill_tc (pos0 =
+// ctl[0]; the step's n new keys are written into the image by
+// k_qk_norm_rope_append as it appends them): per (key tile, kv head) one CTA
+// writes the K tile ([key][head_dim], rows past kend = pos0 + n zero) and
+// the V^T tile ([head_dim][key]), transposed through shared memory so every
+// global load is a coalesced row.  The grid covers the tiles holding keys
+// before pos0; tiles of new keys only return at once.  BF16: the cache holds
+// bf16, widened exactly before the f16 rounding.  Image entries past kend in
+// a tile the append wrote hold zeros (the buffer is cleared when allocated)
+// or finite values of earlier steps: those keys are masked out of S, and
+// their V^T columns meet P = 0.
 constexpr int KVI_STRIDE = 132;  // f32 row stride of the transposition buffer
 template <bool BF16>
 static __global__ void __launch_bounds__(ATC_THREADS) k_kv_image(const void* kcache,
@@ -329,7 +333,9 @@ static __global__ void __launch_bounds__(ATC_THREADS) k_kv_image(const void* kca
   extern __shared__ __align__(16) float vbuf[];  // [128 keys][KVI_STRIDE]
   const int kt = blockIdx.x, g = blockIdx.y, t = threadIdx.x;
   const int kend = ctl[0] + n;
-  if (kt * ATC_K >= kend) return;
+  // tiles of new keys only: k_qk_norm_rope_append wrote them (and the tile
+  // holding pos0 is rebuilt here whole, its new keys included)
+  if (kt * ATC_K >= kend || kt * ATC_K >= ctl[0]) return;
   const size_t kvs = (size_t)n_kv_heads * ATC_HD;
   const int key = kt * ATC_K + t;
   const size_t off = (size_t)key * kvs + (size_t)g * ATC_HD;

@@ -255,6 +255,7 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
     FLOCK_CK(cudaMemset(tc_err.p, 0, 16));
     FLOCK_TRY(part.alloc((size_t)8 * P * H * f));
     FLOCK_TRY(kv_img.alloc(kv_image_bytes(c.max_keys, nKV)));
+    FLOCK_CK(cudaMemset(kv_img.p, 0, kv_img.bytes));  // entries past a step's keys stay finite
     FLOCK_TRY(atc_part.alloc((size_t)ATC_MAX_SPLITS * P * nH * (hd + 2) * f));
   }
   if (tp_ranks >= 1 || H >= FLOCK_SPLIT_RESIDUAL_MIN_HIDDEN)  // also the split residual
@@ -370,6 +371,11 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   qa.eps = c.eps;
   qa.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
   pf_add(qa.pf, L->w[W_GATE]);
+  const int img_tiles = (c.max_keys + ATC_K - 1) / ATC_K;
+  if (n > 1 && tensor_cores) {
+    qa.kv_img = ws->kv_img.as<uint8_t>();
+    qa.img_tiles = img_tiles;
+  }
   const bool kv_bf16 = c.kv_dtype == FLOCK_KV_BF16;
   if (kv_bf16 && !(n > 1 && tensor_cores)) {
     set_error("a bf16 KV cache runs decode on FLOCK_ATTN_FAST and prefill on the tensor cores");
@@ -389,13 +395,18 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   aa.head_dim = c.head_dim;
   pf_add(aa.pf, L->w[W_UP]);
   if (n > 1 && tensor_cores) {
-    // the f16 image of keys [0, ctl[0] + n) (pos0 is read on the device)
-    const int img_tiles = (c.max_keys + ATC_K - 1) / ATC_K;
-    auto* kvi = kv_bf16 ? k_kv_image<true> : k_kv_image<false>;
-    FLOCK_TRY(kernel_setup((const void*)kvi, (int)kv_image_smem_bytes()));
-    kvi<<<dim3(img_tiles, c.n_kv_heads), ATC_THREADS, kv_image_smem_bytes(), d->stream>>>(
-        L->kcache.p, L->vcache.p, c.n_kv_heads, L->ctl, n, img_tiles, ws->kv_img.as<uint8_t>());
-    FLOCK_CK(cudaGetLastError());
+    // the f16 image of the keys cached before this step (pos0 is read on
+    // the device; the new keys went into the image with the append); a
+    // step from an empty cache has none
+    if (L->n_keys > 0) {
+      auto* kvi = kv_bf16 ? k_kv_image<true> : k_kv_image<false>;
+      FLOCK_TRY(kernel_setup((const void*)kvi, (int)kv_image_smem_bytes()));
+      const int old_tiles = (L->n_keys + ATC_K - 1) / ATC_K;
+      kvi<<<dim3(old_tiles < img_tiles ? old_tiles : img_tiles, c.n_kv_heads), ATC_THREADS,
+            kv_image_smem_bytes(), d->stream>>>(L->kcache.p, L->vcache.p, c.n_kv_heads, L->ctl,
+                                                n, img_tiles, ws->kv_img.as<uint8_t>());
+      FLOCK_CK(cudaGetLastError());
+    }
     AttnTcArgs ta = {};
     ta.q = ws->qn.as<float>();
     ta.kv_img = ws->kv_img.as<uint8_t>();

@@ -83,7 +83,12 @@ int enqueue_embed(flock_model* m, int n) {
 }
 
 // Layers over ws.h ([n][hidden]); layer 0 advances the shared position.
+// Each layer's host key count is set to the model's position first: a
+// multi-token step sizes host-side work by it (the tensor-core attention's
+// image of earlier keys), and the chunks of one prompt advance m->pos
+// between calls.
 int enqueue_layers(flock_model* m, int n) {
+  for (int i = 0; i < m->held; i++) m->layers[i]->n_keys = m->pos;
   for (int i = 0; i < m->held; i++) {
     PrefetchList pf = {};
     if (i + 1 < m->held) {

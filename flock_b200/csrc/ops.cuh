@@ -13,6 +13,7 @@
 //                          op-level API (rmsnorm.wgsl, elementwise.wgsl,
 //                          argmax.wgsl).
 #pragma once
+#include <cuda_fp16.h>
 #include "common.cuh"
 
 namespace flock {
@@ -72,7 +73,34 @@ struct QkArgs {
   float eps;
   int neox;
   PrefetchList pf;
+  // tensor-core prefill: the f16 K / V^T tile image of the cache (attn_tc.cuh
+  // layout, img_tiles 128-key tiles per kv head) gets each new key too
+  uint8_t* kv_img;
+  int img_tiles;
 };
+
+// Byte offset of element (row, 8-element chunk c16) of a 128 x 128 f16
+// operand of the tensor-core attention: two 64-column halves of 128-byte
+// rows, 16-byte chunk c of row r at c ^ (r % 8) (attn_tc.cuh atc_off).
+FLOCK_DEV uint32_t kvimg_off(int row, int c16) {
+  return (uint32_t)(c16 >> 3) * (128u * 128u) + (uint32_t)row * 128u +
+         (uint32_t)(((c16 & 7) ^ (row & 7)) << 4);
+}
+
+// This key's row of the K tile and column of the V^T tile, from the values
+// the cache holds (lane l: elements l, l+32, l+64, l+96), rounded to f16.
+FLOCK_DEV void kvimg_put(uint8_t* kv_img, int img_tiles, int kvh, int pos, const float (&kf)[4],
+                         const float (&vf)[4], int lane) {
+  const int kt = pos >> 7, r = pos & 127;
+  uint8_t* kdst = kv_img + ((size_t)kvh * img_tiles + kt) * 2 * (128 * 128 * 2);
+  uint8_t* vdst = kdst + 128 * 128 * 2;
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    const int e = lane + 32 * q;
+    *reinterpret_cast<__half*>(kdst + kvimg_off(r, e >> 3) + (e & 7) * 2) = __float2half_rn(kf[q]);
+    *reinterpret_cast<__half*>(vdst + kvimg_off(e, r >> 3) + (r & 7) * 2) = __float2half_rn(vf[q]);
+  }
+}
 
 // One block of 128 threads per (token, head-vector); head_dim must be 128.
 // Exact RMSNorm (WG = 128) + RoPE of one 128-vector by one warp, with no
@@ -144,6 +172,7 @@ static __global__ void __launch_bounds__(256) k_qk_norm_rope_append(const QkArgs
     const size_t row = ((size_t)pos * a.n_kv_heads + kvh) * hd;
     const float* k = a.k + ((size_t)tok * a.n_kv_heads + kvh) * hd;
     const float* v = a.v + ((size_t)tok * a.n_kv_heads + kvh) * hd;
+    float kf[4], vf[4];  // the values the cache now holds (for the f16 image)
     if constexpr (BF16) {
       float* ks = kstage + warp * 128;
       norm_rope_warp(k, a.k_norm, a.eps, pos, a.inv_freq, a.neox, ks, lane);
@@ -152,16 +181,24 @@ static __global__ void __launch_bounds__(256) k_qk_norm_rope_append(const QkArgs
       uint16_t* vc = static_cast<uint16_t*>(a.vcache) + row;
 #pragma unroll
       for (int q = 0; q < 4; q++) {
-        kc[lane + 32 * q] = bf16_bits(ks[lane + 32 * q]);
-        vc[lane + 32 * q] = bf16_bits(v[lane + 32 * q]);
+        const uint16_t kb = bf16_bits(ks[lane + 32 * q]), vb = bf16_bits(v[lane + 32 * q]);
+        kc[lane + 32 * q] = kb;
+        vc[lane + 32 * q] = vb;
+        kf[q] = __uint_as_float((uint32_t)kb << 16);
+        vf[q] = __uint_as_float((uint32_t)vb << 16);
       }
     } else {
-      norm_rope_warp(k, a.k_norm, a.eps, pos, a.inv_freq, a.neox,
-                     static_cast<float*>(a.kcache) + row, lane);
+      float* kc = static_cast<float*>(a.kcache) + row;
+      norm_rope_warp(k, a.k_norm, a.eps, pos, a.inv_freq, a.neox, kc, lane);
       float* vc = static_cast<float*>(a.vcache) + row;
 #pragma unroll
-      for (int q = 0; q < 4; q++) vc[lane + 32 * q] = v[lane + 32 * q];
+      for (int q = 0; q < 4; q++) {
+        vf[q] = v[lane + 32 * q];
+        vc[lane + 32 * q] = vf[q];
+        kf[q] = kc[lane + 32 * q];  // this lane's own elements of the rotated key
+      }
     }
+    if (a.kv_img) kvimg_put(a.kv_img, a.img_tiles, kvh, pos, kf, vf, lane);
   }
 }
 
