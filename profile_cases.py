@@ -240,7 +240,11 @@ def stream_trace_summary(tr, n_layers: int) -> str:
     names = ["h polled", "QKV rows", "q/k/v polled", "attention", "attn polled", "o_proj rows",
              "h polled", "gate/up rows", "act polled", "down rows"]
     L = n_layers
-    head_in = bool((tr[:, 4 + 10 * L] > 0).any())
+    # head stamps exist only when the head runs inside the kernel; otherwise
+    # the slots hold whatever an earlier launch left (outside this token)
+    t0 = int(tr[:, 0].min())
+    hs = tr[:, 2 + 10 * L: 5 + 10 * L].astype(np.int64) - t0
+    head_in = bool(((hs > 0) & (hs < 10**9)).all())
     end = t[:, 4 + 10 * L].max() if head_in else t[:, 1 + 10 * L].max()
     lines = [f"{'token' if head_in else 'layers (head launched after)'}: {end:.1f} us; "
              f"embed {np.median(t[:, 1]):.2f} us"]
