@@ -55,6 +55,11 @@ struct AttnFastArgs {
   int combine;     // 1: the last split of a group combines into out; 0: leave partials
   int kv_bf16;     // 1: the cache holds bf16 (widened into the f32 tiles as staged)
   PrefetchList pf;
+  // RoPE (cos, sin) per position and frequency, [rope_rows][hd / 2], the
+  // values norm_rope_warp evaluates in f64 (k_rope_table); positions past
+  // rope_rows (or no table) evaluate them in place
+  const float2* rope_cs;
+  int rope_rows;
 };
 
 constexpr int ATTN_FAST_THREADS = 256;
@@ -95,14 +100,16 @@ FLOCK_DEV int attn_splits_for(int n_keys, int max_splits) {
 }
 
 // Shared-memory layout (floats): raw q [4][128], raw k/v [2][128], gains
-// [2][128], inv_freq [64], normalised q [4][128], new k/v [2][128], norm
-// scratch tmp [2][128] + red [2][132], scores/probabilities [4][TILE],
-// running softmax state [4][4], K tile [TILE][AF_KSTRIDE], V tile [TILE][128].
+// [2][128], inv_freq [64], normalised q [4][128], new k/v [2][128],
+// scores/probabilities [4][TILE], running softmax state [4][4], this
+// position's RoPE (cos, sin) [64][2], K tile [TILE][AF_KSTRIDE], V tile
+// [TILE][128].
 constexpr int AF_KSTRIDE = 132;
 constexpr int AF_QRAW = 0, AF_KRAW = 512, AF_VRAW = 640, AF_GQ = 768, AF_GK = 896,
               AF_INV = 1024, AF_QV = 1088, AF_KNEW = 1600, AF_VNEW = 1728,
-              AF_SC = 1856, AF_ML = AF_SC + 4 * ATTN_TILE, AF_KT = AF_ML + 16,
-              AF_VT = AF_KT + ATTN_TILE * AF_KSTRIDE, AF_END = AF_VT + ATTN_TILE * 128;
+              AF_SC = 1856, AF_ML = AF_SC + 4 * ATTN_TILE, AF_CS = AF_ML + 16,
+              AF_KT = AF_CS + 128, AF_VT = AF_KT + ATTN_TILE * AF_KSTRIDE,
+              AF_END = AF_VT + ATTN_TILE * 128;
 
 // One (kv head g, split s) work item, run by ATTN_FAST_THREADS threads that
 // synchronise with `sync()`; `dsm` holds AF_END floats; `last` is a shared
@@ -124,6 +131,7 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   const int k1 = min(n_keys, k0 + chunk);
   const int nk = max(0, k1 - k0);
   const bool fused = a.q_norm != nullptr;
+  const bool table = fused && a.rope_cs != nullptr && pos < a.rope_rows;
 
   // ---- one round trip: the token's raw q/k/v, gains, and the first K/V tile
   auto stage_tile = [&](int t0, int nt) {
@@ -167,6 +175,9 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
         if (t < 16)
           reinterpret_cast<float4*>(dsm + AF_INV)[t] =
               reinterpret_cast<const float4*>(a.inv_freq)[t];
+        if (table)  // 64 (cos, sin) pairs: 32 float4
+          reinterpret_cast<float4*>(dsm + AF_CS)[t] =
+              reinterpret_cast<const float4*>(a.rope_cs + (size_t)pos * 64)[t];
       } else if (a.kv_bf16) {
         const size_t off = (size_t)pos * kvs + (size_t)g * hd;
         if (t < 16) {
@@ -193,11 +204,22 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   if (fused) {
     // exact per-head RMSNorm + RoPE (k_qk_norm_rope_append's arithmetic):
     // warps 0..G-1 the query heads, warp G the new key, warp G+1 copies v
-    if (warp < G)
-      norm_rope_warp(dsm + AF_QRAW + warp * 128, dsm + AF_GQ, a.eps, pos, dsm + AF_INV, a.neox,
-                     qv + warp * 128, lane);
-    else if (warp == G)
-      norm_rope_warp(dsm + AF_KRAW, dsm + AF_GK, a.eps, pos, dsm + AF_INV, a.neox, knew, lane);
+    // with the table the (cos, sin) pairs are the values norm_rope_warp
+    // would evaluate in f64: the same bits without the f64 sin and cos
+    const float2* cs = reinterpret_cast<const float2*>(dsm + AF_CS);
+    if (warp < G) {
+      if (table)
+        norm_rope_warp_cs(dsm + AF_QRAW + warp * 128, dsm + AF_GQ, a.eps, cs, a.neox,
+                          qv + warp * 128, lane);
+      else
+        norm_rope_warp(dsm + AF_QRAW + warp * 128, dsm + AF_GQ, a.eps, pos, dsm + AF_INV, a.neox,
+                       qv + warp * 128, lane);
+    } else if (warp == G) {
+      if (table)
+        norm_rope_warp_cs(dsm + AF_KRAW, dsm + AF_GK, a.eps, cs, a.neox, knew, lane);
+      else
+        norm_rope_warp(dsm + AF_KRAW, dsm + AF_GK, a.eps, pos, dsm + AF_INV, a.neox, knew, lane);
+    }
     else if (warp == G + 1)
       for (int i = lane; i < 128; i += 32) vnew[i] = dsm[AF_VRAW + i];
     sync();
@@ -325,51 +347,46 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   sync();
   if (!*last_flag) return;
   __threadfence();
-  // the combine spread over the whole CTA: warp hq derives
-  // head hq's split weights w_s = e^(m_s - M) and L (lane s holds splits s
-  // and s + 32), then every thread owns one (head, element) and sums its
-  // splits in order, 32 split loads in flight at a time
-  float* cw = dsm + AF_SC;  // [G][ATTN_MAX_SPLITS] split weights
-  float* cl = dsm + AF_ML;  // [G] L
-  if (warp < G) {
-    const float* pp = a.part + (size_t)(g * G + warp) * a.splits * (hd + 2);
-    const bool has0 = lane < splits, has1 = lane + 32 < splits;
-    const float m0 = has0 ? __ldcg(pp + lane * (hd + 2) + hd) : -INFINITY;
-    const float l0 = has0 ? __ldcg(pp + lane * (hd + 2) + hd + 1) : 0.0f;
-    const float m1 = has1 ? __ldcg(pp + (lane + 32) * (hd + 2) + hd) : -INFINITY;
-    const float l1 = has1 ? __ldcg(pp + (lane + 32) * (hd + 2) + hd + 1) : 0.0f;
-    float M = fmaxf(m0, m1);
-#pragma unroll
-    for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-    const float w0 = has0 ? expf(m0 - M) : 0.0f;
-    const float w1 = has1 ? expf(m1 - M) : 0.0f;
-    float L = 0.0f;
-    for (int sp = 0; sp < splits; sp++) {
-      const bool hi = sp >= 32;  // uniform over the warp
-      L = fmaf(__shfl_sync(0xffffffffu, hi ? l1 : l0, sp & 31),
-               __shfl_sync(0xffffffffu, hi ? w1 : w0, sp & 31), L);
-    }
-    cw[warp * ATTN_MAX_SPLITS + lane] = w0;
-    cw[warp * ATTN_MAX_SPLITS + lane + 32] = w1;
-    if (lane == 0) cl[warp] = L;
-  }
-  sync();
+  // the combine spread over the whole CTA: every thread owns one (head,
+  // element) and issues the loads of its element and of its head's (m, l)
+  // for every split together (one round trip where a warp used to derive
+  // the weights first), then derives M = max_s m_s, w_s = e^(m_s - M) and
+  // L = sum_s l_s w_s itself -- the same operations in the same split
+  // order for every thread of a head -- and O = sum_s o_s w_s in split
+  // order, out = O / L
   for (int oi = t; oi < G * hd; oi += ATTN_FAST_THREADS) {
     const int hq = oi / hd, i = oi - hq * hd;
-    const float* pp = a.part + (size_t)(g * G + hq) * a.splits * (hd + 2) + i;
-    float O = 0.0f;
-#pragma unroll
-    for (int s0 = 0; s0 < ATTN_MAX_SPLITS; s0 += 32) {
-      if (s0 >= splits) break;
-      float ov[32];
+    const float* pp = a.part + (size_t)(g * G + hq) * a.splits * (hd + 2);
+    float M = -INFINITY;
+    for (int s0 = 0; s0 < splits; s0 += 32) {
+      float mv[32];
 #pragma unroll
       for (int sp = 0; sp < 32; sp++)
-        ov[sp] = s0 + sp < splits ? __ldcg(pp + (s0 + sp) * (hd + 2)) : 0.0f;
+        mv[sp] = s0 + sp < splits ? __ldcg(pp + (s0 + sp) * (hd + 2) + hd) : -INFINITY;
 #pragma unroll
-      for (int sp = 0; sp < 32; sp++)
-        if (s0 + sp < splits) O = fmaf(ov[sp], cw[hq * ATTN_MAX_SPLITS + s0 + sp], O);
+      for (int sp = 0; sp < 32; sp++) M = fmaxf(M, mv[sp]);
     }
-    a.out[(size_t)(g * G + hq) * hd + i] = O / cl[hq];
+    float O = 0.0f, L = 0.0f;
+    for (int s0 = 0; s0 < splits; s0 += 16) {
+      float ov[16], mv[16], lv[16];
+#pragma unroll
+      for (int sp = 0; sp < 16; sp++) {
+        const bool has = s0 + sp < splits;
+        const float* q = pp + (s0 + sp) * (hd + 2);
+        ov[sp] = has ? __ldcg(q + i) : 0.0f;
+        mv[sp] = has ? __ldcg(q + hd) : -INFINITY;
+        lv[sp] = has ? __ldcg(q + hd + 1) : 0.0f;
+      }
+#pragma unroll
+      for (int sp = 0; sp < 16; sp++) {
+        if (s0 + sp < splits) {
+          const float w = expf(mv[sp] - M);
+          L = fmaf(lv[sp], w, L);
+          O = fmaf(ov[sp], w, O);
+        }
+      }
+    }
+    a.out[(size_t)(g * G + hq) * hd + i] = O / L;
   }
   if (t == 0) a.count[g] = 0;
 }
@@ -383,6 +400,28 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
   __shared__ bool last;
   issue_prefetch(a.pf);
   pdl_launch_dependents();
+  {
+    // before the wait: bring this split's first key tile into L2.  The
+    // position is read before the previous kernel may have advanced it (a
+    // prefetch of a neighbouring range is harmless: L2 stays coherent with
+    // the later loads); the rows are rows earlier steps wrote.
+    const int pos_guess = *(volatile const int*)a.ctl;
+    const int n_keys = pos_guess + 1;
+    const int splits = attn_splits_for(n_keys, a.splits);
+    const int s = blockIdx.y;
+    if (s < splits) {
+      const int chunk = (n_keys + splits - 1) / splits;
+      const int k0 = s * chunk, k1 = min(n_keys, k0 + chunk);
+      const int t = threadIdx.x;
+      const uint32_t row = a.kv_bf16 ? 256u : 512u;
+      const size_t kvs = (size_t)a.n_kv_heads * 128;
+      if (t < 2 * ATTN_TILE && k0 + (t >> 1) < min(k1, k0 + ATTN_TILE)) {
+        const int key = k0 + (t >> 1);
+        const size_t off = ((size_t)key * kvs + (size_t)blockIdx.x * 128) * (a.kv_bf16 ? 2 : 4);
+        prefetch_l2(static_cast<const uint8_t*>((t & 1) ? a.vcache : a.kcache) + off, row);
+      }
+    }
+  }
   pdl_wait();
   attn_fast_item(a, blockIdx.x, blockIdx.y, a.ctl[0], dsm, &last, BlockSync{});
 }

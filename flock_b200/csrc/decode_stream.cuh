@@ -568,55 +568,6 @@ FLOCK_DEV int st_phase(const StArgs& a, int pi, int ph, uint32_t tag, bool last_
   return pi;
 }
 
-// norm_rope_warp (k_qk_norm_rope_append's arithmetic, bit for bit) with the
-// (cos, sin) of this position read from a staged table row instead of
-// evaluated in f64: the same rounded values.
-FLOCK_DEV void st_norm_rope_warp(const float* src, const float* gain, float eps,
-                                 const float2* cs, int neox, float* dst, int lane) {
-  float x[4], y[4];
-#pragma unroll
-  for (int q = 0; q < 4; q++) x[q] = src[lane + 32 * q];
-  float v = fadd(fadd(ffma(x[0], x[0], 0.0f), ffma(x[2], x[2], 0.0f)),
-                 fadd(ffma(x[1], x[1], 0.0f), ffma(x[3], x[3], 0.0f)));
-  v = warp_tree_sum(v);
-  v = __shfl_sync(0xffffffffu, v, 0);
-  const float scale = rsqrt_f64r(fadd(fdiv(v, 128.0f), eps));
-#pragma unroll
-  for (int q = 0; q < 4; q++) y[q] = fmul(fmul(x[q], scale), gain[lane + 32 * q]);
-  if (neox) {
-#pragma unroll
-    for (int q = 0; q < 2; q++) {
-      const int i = lane + 32 * q;
-      const float2 t = cs[i];
-      const float av = y[q], bv = y[q + 2];
-      dst[i] = ffma(-bv, t.y, fmul(av, t.x));
-      dst[i + 64] = ffma(bv, t.x, fmul(av, t.y));
-    }
-  } else {
-    const bool odd = lane & 1;
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int e = lane + 32 * q;
-      const float other = __shfl_xor_sync(0xffffffffu, y[q], 1);
-      const float av = odd ? other : y[q], bv = odd ? y[q] : other;
-      const float2 t = cs[e >> 1];
-      dst[e] = odd ? ffma(bv, t.x, fmul(av, t.y)) : ffma(-bv, t.y, fmul(av, t.x));
-    }
-  }
-}
-
-// (cos, sin) of fr(pos * inv_freq[i]) for i < 64, as norm_rope_warp rounds them.
-FLOCK_DEV float2 st_rope_cs(int pos, float inv_freq_i) {
-  const float theta = fmul((float)pos, inv_freq_i);
-  return make_float2(__double2float_rn(cos((double)theta)), __double2float_rn(sin((double)theta)));
-}
-
-// Builds the RoPE table: rows [0, n_pos) x 64 frequencies.
-static __global__ void k_rope_table(const float* inv_freq, int n_pos, float2* out) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n_pos * 64) out[i] = st_rope_cs(i >> 6, inv_freq[i & 63]);
-}
-
 // Attention shared-memory layout (floats, inside the x region).
 constexpr int SA_QRAW = 0, SA_KRAW = SA_QRAW + ST_MAX_G * 128, SA_VRAW = SA_KRAW + 128,
               SA_GQ = SA_VRAW + 128, SA_GK = SA_GQ + 128, SA_CS = SA_GK + 128,
@@ -720,7 +671,7 @@ FLOCK_DEV bool st_attention_item(const StArgs& a, const StLayer& L, int g, int s
   }
   if (t < 64) {
     float2* cs = reinterpret_cast<float2*>(xs + SA_CS);
-    cs[t] = pos < rope_rows ? rope_cs[(size_t)pos * 64 + t] : st_rope_cs(pos, inv_freq[t]);
+    cs[t] = pos < rope_rows ? rope_cs[(size_t)pos * 64 + t] : rope_cs_at(pos, inv_freq[t]);
   }
   // q heads g*G .. g*G+G-1, k head g, v head g of the QKV output
   {
@@ -759,11 +710,11 @@ FLOCK_DEV bool st_attention_item(const StArgs& a, const StLayer& L, int g, int s
   float* knew = xs + SA_KNEW;
   float* vnew = xs + SA_VNEW;
   if (warp < G)
-    st_norm_rope_warp(xs + SA_QRAW + warp * 128, xs + SA_GQ, eps,
+    norm_rope_warp_cs(xs + SA_QRAW + warp * 128, xs + SA_GQ, eps,
                       reinterpret_cast<const float2*>(xs + SA_CS), neox,
                    qv + warp * 128, lane);
   else if (warp == G)
-    st_norm_rope_warp(xs + SA_KRAW, xs + SA_GK, eps, reinterpret_cast<const float2*>(xs + SA_CS),
+    norm_rope_warp_cs(xs + SA_KRAW, xs + SA_GK, eps, reinterpret_cast<const float2*>(xs + SA_CS),
                       neox, knew, lane);
   else if (warp == G + 1)
     for (int i = lane; i < 128; i += 32) vnew[i] = xs[SA_VRAW + i];

@@ -244,6 +244,23 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
   FLOCK_TRY(attn_part.alloc((size_t)nH * attn_splits * (hd + 2) * f));  // stride: attn_splits
   FLOCK_TRY(attn_count.alloc((size_t)nKV * 4));
   FLOCK_CK(cudaMemset(attn_count.p, 0, attn_count.bytes));
+  if (hd == 128) {
+    // the RoPE (cos, sin) of every position the cache holds, the values
+    // norm_rope_warp evaluates in f64 (layer.ts:180 inv_freq, as layer_init
+    // computes it)
+    std::vector<float> inv(hd / 2);
+    for (int j = 0; j < hd / 2; j++)
+      inv[j] = (float)(1.0 / std::pow(c.rope_base, (double)(2 * j) / (double)hd));
+    DBuf dinv;
+    FLOCK_TRY(dinv.alloc(inv.size() * sizeof(float)));
+    FLOCK_CK(cudaMemcpy(dinv.p, inv.data(), inv.size() * sizeof(float), cudaMemcpyHostToDevice));
+    rope_rows = c.max_keys < 1 ? 1 : c.max_keys;
+    FLOCK_TRY(rope.alloc((size_t)rope_rows * 64 * sizeof(float2)));
+    k_rope_table<<<(rope_rows * 64 + 255) / 256, 256>>>(dinv.as<float>(), rope_rows,
+                                                        rope.as<float2>());
+    FLOCK_CK(cudaGetLastError());
+    FLOCK_CK(cudaDeviceSynchronize());
+  }
   if (c.prefill == FLOCK_PREFILL_TENSOR) {
     size_t ib = act_image_bytes(P, H);
     const size_t iq = act_image_bytes(P, nH * hd), iff = act_image_bytes(P, F);
@@ -640,6 +657,8 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
     a.chunk_cap = (c.max_keys + a.splits - 1) / a.splits;
     a.combine = 1;
+    a.rope_cs = ws->rope.as<float2>();
+    a.rope_rows = ws->rope_rows;
     pf_add(a.pf, L->w[W_GATE]);
     pf_add(a.pf, L->w[W_UP]);
     const size_t smem = attn_fast_smem(a.chunk_cap);

@@ -92,6 +92,8 @@ struct Workspace {
   int attn_splits = 16;         // splits (attn_max_splits); partial slots per query head
   DBuf img, gu, tc_err, part;   // tensor-core prefill: activation image, gate|up rows, error word,
                                 // split-K partials
+  DBuf rope;                    // RoPE (cos, sin) [rope_rows][hd / 2] (k_rope_table)
+  int rope_rows = 0;
   DBuf kv_img;                  // tensor-core prefill: f16 K / V^T tiles of the cache
   DBuf atc_part;                // tensor-core prefill attention: per key range O, m, l
   int atc_nz = 1;               // key ranges of the last tensor-core attention launch

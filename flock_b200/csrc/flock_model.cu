@@ -397,6 +397,8 @@ int mk_prepare(flock_model* m) {
       aa.neox = c.rope_pairing == FLOCK_ROPE_NEOX;
       aa.chunk_cap = (c.max_keys + splits - 1) / splits;
       aa.combine = 1;
+      aa.rope_cs = ws.rope.as<float2>();
+      aa.rope_rows = ws.rope_rows;
     }
     GemvArgs& hg = gv[(size_t)4 * m->held];
     hg = GemvArgs{};

@@ -146,6 +146,55 @@ FLOCK_DEV void norm_rope_warp(const float* src, const float* gain, float eps, in
   }
 }
 
+// norm_rope_warp (k_qk_norm_rope_append's arithmetic, bit for bit) with the
+// (cos, sin) of this position read from a staged table row instead of
+// evaluated in f64: the same rounded values.
+FLOCK_DEV void norm_rope_warp_cs(const float* src, const float* gain, float eps,
+                                 const float2* cs, int neox, float* dst, int lane) {
+  float x[4], y[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++) x[q] = src[lane + 32 * q];
+  float v = fadd(fadd(ffma(x[0], x[0], 0.0f), ffma(x[2], x[2], 0.0f)),
+                 fadd(ffma(x[1], x[1], 0.0f), ffma(x[3], x[3], 0.0f)));
+  v = warp_tree_sum(v);
+  v = __shfl_sync(0xffffffffu, v, 0);
+  const float scale = rsqrt_f64r(fadd(fdiv(v, 128.0f), eps));
+#pragma unroll
+  for (int q = 0; q < 4; q++) y[q] = fmul(fmul(x[q], scale), gain[lane + 32 * q]);
+  if (neox) {
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const int i = lane + 32 * q;
+      const float2 t = cs[i];
+      const float av = y[q], bv = y[q + 2];
+      dst[i] = ffma(-bv, t.y, fmul(av, t.x));
+      dst[i + 64] = ffma(bv, t.x, fmul(av, t.y));
+    }
+  } else {
+    const bool odd = lane & 1;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int e = lane + 32 * q;
+      const float other = __shfl_xor_sync(0xffffffffu, y[q], 1);
+      const float av = odd ? other : y[q], bv = odd ? y[q] : other;
+      const float2 t = cs[e >> 1];
+      dst[e] = odd ? ffma(bv, t.x, fmul(av, t.y)) : ffma(-bv, t.y, fmul(av, t.x));
+    }
+  }
+}
+
+// (cos, sin) of fr(pos * inv_freq[i]) for i < 64, as norm_rope_warp rounds them.
+FLOCK_DEV float2 rope_cs_at(int pos, float inv_freq_i) {
+  const float theta = fmul((float)pos, inv_freq_i);
+  return make_float2(__double2float_rn(cos((double)theta)), __double2float_rn(sin((double)theta)));
+}
+
+// Builds the RoPE table: rows [0, n_pos) x 64 frequencies.
+static __global__ void k_rope_table(const float* inv_freq, int n_pos, float2* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n_pos * 64) out[i] = rope_cs_at(i >> 6, inv_freq[i & 63]);
+}
+
 // One warp per 128-vector (8 per CTA): q heads -> qn, k heads -> the cache at
 // position pos0 + token with v copied beside it.  norm_rope_warp's arithmetic
 // is the WG = 128 RMSNorm and RoPE above, bit for bit.  BF16: the cache holds
