@@ -98,6 +98,8 @@ static __global__ void __launch_bounds__(ATC_THREADS, 2) k_attn_prefill_tc(const
   uint64_t* ldbar = bar + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 2);
   __shared__ int s_stop;
+  pdl_launch_dependents();
+  pdl_wait();
 
   const int t = threadIdx.x, warp = t >> 5;
   const int h = blockIdx.y, q0 = blockIdx.x * ATC_Q;
@@ -331,6 +333,8 @@ static __global__ void __launch_bounds__(ATC_THREADS) k_kv_image(const void* kca
                                                                 int n, int img_tiles,
                                                                 uint8_t* img) {
   extern __shared__ __align__(16) float vbuf[];  // [128 keys][KVI_STRIDE]
+  pdl_launch_dependents();
+  pdl_wait();
   const int kt = blockIdx.x, g = blockIdx.y, t = threadIdx.x;
   const int kend = ctl[0] + n;
   // tiles of new keys only: k_qk_norm_rope_append wrote them (and the tile

@@ -77,21 +77,6 @@ int kernel_setup(const void* func, int max_dyn_smem, int carveout) {
   return FLOCK_OK;
 }
 
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_ex(cudaStream_t st, void (*k)(KArgs...), dim3 grid, dim3 block,
-                             size_t smem, bool pdl, Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
-}
 
 template <int QT, int R, int EPI, int MX, int LA = 1>
 static cudaError_t gemv_go(flock_dev* d, const GemvArgs& a, int ctas, bool pdl) {
@@ -419,10 +404,11 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
       auto* kvi = kv_bf16 ? k_kv_image<true> : k_kv_image<false>;
       FLOCK_TRY(kernel_setup((const void*)kvi, (int)kv_image_smem_bytes()));
       const int old_tiles = (L->n_keys + ATC_K - 1) / ATC_K;
-      kvi<<<dim3(old_tiles < img_tiles ? old_tiles : img_tiles, c.n_kv_heads), ATC_THREADS,
-            kv_image_smem_bytes(), d->stream>>>(L->kcache.p, L->vcache.p, c.n_kv_heads, L->ctl,
-                                                n, img_tiles, ws->kv_img.as<uint8_t>());
-      FLOCK_CK(cudaGetLastError());
+      FLOCK_CK(launch_ex(d->stream, kvi,
+                         dim3(old_tiles < img_tiles ? old_tiles : img_tiles, c.n_kv_heads),
+                         dim3(ATC_THREADS), kv_image_smem_bytes(), true,
+                         (const void*)L->kcache.p, (const void*)L->vcache.p, c.n_kv_heads,
+                         (const int*)L->ctl, n, img_tiles, ws->kv_img.as<uint8_t>()));
     }
     AttnTcArgs ta = {};
     ta.q = ws->qn.as<float>();
@@ -439,9 +425,8 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
     // reads pos0 on the device; a range past its query tile's keys is empty)
     const int nz = attn_tc_splits(L->n_keys, n);
     FLOCK_TRY(kernel_setup((const void*)k_attn_prefill_tc, (int)attn_tc_smem_bytes()));
-    k_attn_prefill_tc<<<dim3((n + ATC_Q - 1) / ATC_Q, c.n_heads, nz), ATC_THREADS,
-                        attn_tc_smem_bytes(), d->stream>>>(ta);
-    FLOCK_CK(cudaGetLastError());
+    FLOCK_CK(launch_ex(d->stream, k_attn_prefill_tc, dim3((n + ATC_Q - 1) / ATC_Q, c.n_heads, nz),
+                       dim3(ATC_THREADS), attn_tc_smem_bytes(), true, ta));
     // with several key ranges the o_proj activation image merges them
     // (act_image_enqueue); ws->attn is then not written
     ws->atc_nz = nz;
@@ -531,7 +516,7 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.err = err;
     FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, EPI_STORE, a, d->sm_count, ws->part.bytes / 4));
   }
-  FLOCK_TRY(enqueue_qk_attn(L, n, false, true));
+  FLOCK_TRY(enqueue_qk_attn(L, n, true, true));
   {  // o_proj + residual on h
     FLOCK_TRY(ws->atc_nz > 1 ? act_image_enqueue(st, nullptr, qw, nullptr, 0.0f, n, qw, img,
                                                  ws->atc_part.as<float>(), ws->atc_nz, c.n_heads)

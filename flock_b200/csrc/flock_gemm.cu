@@ -89,8 +89,8 @@ static int act_image_launch(cudaStream_t st, ActImgArgs& a) {
   a.row_exp = reinterpret_cast<int*>(a.img + act_image_only_bytes(M, K));
   const int rows = (M + a.Nt - 1) / a.Nt * a.Nt;  // image rows, zero past M
   FLOCK_TRY(kernel_setup((const void*)k_act_image, (int)act_image_smem_bytes(12288)));
-  k_act_image<<<rows, ACT_IMG_THREADS, act_image_smem_bytes(K), st>>>(a);
-  FLOCK_CK(cudaGetLastError());
+  FLOCK_CK(launch_ex(st, k_act_image, dim3(rows), dim3(ACT_IMG_THREADS), act_image_smem_bytes(K),
+                     true, a));
   return FLOCK_OK;
 }
 
@@ -120,15 +120,13 @@ static int launch_tc(cudaStream_t st, const TcArgs& a, bool defer_reduce) {
   const size_t smem = gemm_tc_smem_bytes(a.Nt);
   const dim3 grid((unsigned)a.tile0[a.nseg], (unsigned)((a.M + a.Nt - 1) / a.Nt),
                   (unsigned)a.ksplit);
-  k_gemm_tc<QT, EPI><<<grid, TC_THREADS, smem, st>>>(a);
-  FLOCK_CK(cudaGetLastError());
+  FLOCK_CK(launch_ex(st, k_gemm_tc<QT, EPI>, grid, dim3(TC_THREADS), smem, true, a));
   if (a.ksplit > 1 && !defer_reduce) {
     const TcSeg& s = a.seg[0];
     const int64_t total = (int64_t)a.M * s.rows;
-    k_splitk_reduce<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
-        a.part, a.ksplit, a.M, s.rows, EPI == EPI_RESIDUAL ? a.res : nullptr, a.res_stride, s.out,
-        s.out_stride);
-    FLOCK_CK(cudaGetLastError());
+    FLOCK_CK(launch_ex(st, k_splitk_reduce, dim3((unsigned)((total + 255) / 256)), dim3(256), 0,
+                       true, (const float*)a.part, a.ksplit, a.M, s.rows,
+                       EPI == EPI_RESIDUAL ? a.res : nullptr, a.res_stride, s.out, s.out_stride));
   }
   return FLOCK_OK;
 }

@@ -2,6 +2,8 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <utility>
+
 #include <atomic>
 
 #include <cstdint>
@@ -115,6 +117,26 @@ struct TcArgs;
 struct TcSeg;
 struct PeerXchg;
 size_t act_image_bytes(int M, int K);
+// A kernel launch on `st`; with `pdl` the launch may begin while the
+// previous kernel of the stream still runs (programmatic dependent launch):
+// the kernel must call griddepcontrol.wait before it touches anything that
+// kernel writes or reads.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_ex(cudaStream_t st, void (*k)(KArgs...), dim3 grid, dim3 block,
+                             size_t smem, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
 int act_image_enqueue(cudaStream_t st, const float* x, int x_stride, const float* gain, float eps,
                       int M, int K, uint8_t* img, const float* atc_part = nullptr, int atc_nz = 0,
                       int n_heads = 0);

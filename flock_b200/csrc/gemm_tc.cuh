@@ -17,11 +17,14 @@
 //    tcgen05.mma.cta_group::1.kind::f16 (128 x Nt x 16) instructions.
 //  * Raw weight tiles arrive by TMA: one thread of a loader warp issues a
 //    2-D cp.async.bulk.tensor per K-tile (128 rows x 64 int8 bytes, or x 32
-//    nibble bytes) from the weight's tensor map into a ring of 4-12
-//    shared-memory stages (all the shared memory the A/B stages leave) (the map's 64-/32-byte swizzle spreads the rows
+//    nibble bytes) from the weight's tensor map into a ring of 4
+//    shared-memory stages (the map's 64-/32-byte swizzle spreads the rows
 //    over all banks), completing on the stage's mbarrier by transaction
 //    count.  The map always describes this GPU's own weight plane; there is
-//    no multicast.
+//    no multicast.  The kernel is launched with programmatic dependent
+//    launch: these weight loads may start while the previous kernel (the
+//    activation image) still runs; everything that kernel writes is read
+//    after griddepcontrol.wait.
 //  * Converters (8 warps, two threads per weight row: one 32-weight block
 //    each per K-tile) read their block from the raw stage, release it,
 //    form q * s in packed f16 arithmetic (exact integers, one correctly
@@ -287,6 +290,11 @@ static __global__ void __launch_bounds__(TC_THREADS, 1)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int RAW_ROW = QT == QT_Q8 ? TC_KT : TC_KT / 2;  // raw bytes per row per K-tile
+  // launched with programmatic dependent launch: the next kernel may start
+  // its own prologue now; this one reads the previous kernel's output (the
+  // activation image, row scales, residual) only after griddepcontrol.wait
+  // -- the weight loads before it touch nothing any kernel writes
+  pdl_launch_dependents();
   constexpr uint32_t RAW_TX = (uint32_t)(TC_ROWS * RAW_ROW);
 
   if (threadIdx.x == 0) {
@@ -366,6 +374,7 @@ static __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     // ------------------------------------------------------------- epilogue
     if (!mbar_wait(done, 0, a.err)) atomicCAS(a.err, 0, 1);
+    pdl_wait();  // row scales, residual and outputs belong to the previous kernels' step
     tc_fence_after();
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     const bool split = a.ksplit > 1;
@@ -423,6 +432,7 @@ static __global__ void __launch_bounds__(TC_THREADS, 1)
     // the B tile of K-tile kt goes into stage kt % TC_STAGES as soon as the
     // MMAs of kt - TC_STAGES have released it
     if (lane == 0) {
+      pdl_wait();  // the image is the previous kernel's output
       int issued = 0;
       bool ok = true;
       for (int kt = 0; kt < KT; kt++) {
@@ -485,6 +495,8 @@ static __global__ void __launch_bounds__(TC_THREADS, 1)
 static __global__ void k_splitk_reduce(const float* part, int ksplit, int M, int N,
                                        const float* res, int res_stride, float* out,
                                        int out_stride) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)M * N) return;
   const int64_t m = i / N, n = i - m * N;
@@ -561,6 +573,8 @@ inline size_t act_image_smem_bytes(int K) {
 
 static __global__ void __launch_bounds__(ACT_IMG_THREADS) k_act_image(const ActImgArgs a) {
   extern __shared__ __align__(16) float xr[];  // [K] row, then scratch
+  pdl_launch_dependents();
+  pdl_wait();
   float* red = xr + a.K;                       // [128]
   float* w = red + ACT_IMG_THREADS;            // [ATC_MAX_SPLITS_IMG][32] merge weights
   float* winv = w + ATC_MAX_SPLITS_IMG * 32;   // [32]
