@@ -502,9 +502,16 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     k_ctl_advance<<<1, 1, 0, st>>>(L->ctl, n);
     FLOCK_CK(cudaGetLastError());
   }
-  {  // attn_norm + q/k/v
-    FLOCK_TRY(act_image_enqueue(st, ws->h.as<float>(), H, L->w[W_ATTN_NORM]->data.as<float>(),
-                                c.eps, n, H, img));
+  {  // attn_norm (h = residual + the previous layer's down partials, when it
+     // left them) + q/k/v
+    if (ws->down_pending > 1)
+      FLOCK_TRY(act_image_reduce_enqueue(st, ws->h.as<float>(), ws->part.as<float>(),
+                                         ws->down_pending, ws->h.as<float>(),
+                                         L->w[W_ATTN_NORM]->data.as<float>(), c.eps, n, H, img));
+    else
+      FLOCK_TRY(act_image_enqueue(st, ws->h.as<float>(), H,
+                                  L->w[W_ATTN_NORM]->data.as<float>(), c.eps, n, H, img));
+    ws->down_pending = 0;
     TcArgs a = {};
     a.seg[0] = tc_seg_of(L->w[W_Q], ws->q.as<float>(), qw);
     a.seg[1] = tc_seg_of(L->w[W_K], ws->k.as<float>(), kvw);
@@ -568,8 +575,12 @@ static int layer_enqueue_tc(flock_layer* L, int n, bool advance) {
     a.res_stride = H;
     a.err = err;
     a.part = ws->part.as<float>();
+    // with a next layer in the same pass (ws->defer_down), a split-K down
+    // leaves its partials for that layer's attn_norm image to sum
+    const bool defer = !L->tp && ws->defer_down;
     FLOCK_TRY(gemm_tc_enqueue(st, QT_Q8, L->tp ? EPI_STORE : EPI_RESIDUAL, a, d->sm_count,
-                              ws->part.bytes / 4));
+                              ws->part.bytes / 4, defer));
+    if (defer && a.ksplit > 1) ws->down_pending = a.ksplit;
     if (L->tp) FLOCK_TRY(tp_sum_into_h(L, n));
   }
   return FLOCK_OK;

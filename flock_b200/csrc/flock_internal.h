@@ -99,6 +99,11 @@ struct Workspace {
   DBuf kv_img;                  // tensor-core prefill: f16 K / V^T tiles of the cache
   DBuf atc_part;                // tensor-core prefill attention: per key range O, m, l
   int atc_nz = 1;               // key ranges of the last tensor-core attention launch
+  // tensor-core prefill across the layers of one pass: the enqueuer sets
+  // defer_down when another layer follows, and down_pending is the number of
+  // split-K partials of h in `part` that the next layer's first image sums
+  bool defer_down = false;
+  int down_pending = 0;
   DBuf tp_part, tp_all;         // tensor parallel: this rank's partial [P][H], all ranks
   DBuf wire;                    // FLK1 frames: the f16 payload on the device
   // tp_ranks >= 1 (a tensor-parallel model, one rank included): also the

@@ -103,7 +103,13 @@ int enqueue_layers(flock_model* m, int n) {
       pf.bytes[2] = v->qs.bytes & ~(uint64_t)15;
       pf.n = 3;
     }
-    FLOCK_TRY(layer_enqueue(m->layers[i], n, i == 0, pf, true));
+    m->ws.defer_down = i + 1 < m->held;
+    const int rc = layer_enqueue(m->layers[i], n, i == 0, pf, true);
+    m->ws.defer_down = false;
+    if (rc) {
+      m->ws.down_pending = 0;
+      return rc;
+    }
   }
   return FLOCK_OK;
 }
