@@ -49,6 +49,11 @@ struct AttnTcArgs {
   int n_tokens, n_heads, n_kv_heads;
   int* err;
   float* part;     // gridDim.z > 1: [z][n][nH][hd] unnormalised O, then [z][n][nH][2] (m, l)
+  // the f16 image of the rotated queries written by the append kernel
+  // ([nH][q_tiles] 128-token tiles, the operand layout), or null: q staged
+  // from `q` by the threads
+  const uint8_t* q_img;
+  int q_tiles;
 };
 
 // Byte offset of element (row r, column c) -- c < 128 -- in a 128-row operand
@@ -96,9 +101,9 @@ static __global__ void __launch_bounds__(ATC_THREADS, 2) k_attn_prefill_tc(const
   uint8_t* sP = sK;
   uint64_t* bar = reinterpret_cast<uint64_t*>(sV + ATC_OPND);
   uint64_t* ldbar = bar + 1;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 2);
+  uint64_t* qbar = bar + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 3);
   __shared__ int s_stop;
-  pdl_launch_dependents();
   pdl_wait();
 
   const int t = threadIdx.x, warp = t >> 5;
@@ -135,28 +140,52 @@ static __global__ void __launch_bounds__(ATC_THREADS, 2) k_attn_prefill_tc(const
     bulk_g2s(sK, src, ATC_OPND, ldbar);
     if (with_v) bulk_g2s(sV, src + ATC_OPND, ATC_OPND, ldbar);
   };
+  const bool qcopy = a.q_img != nullptr;
+  bool qinflight = false;  // thread 0: the q copy not yet seen landing
   if (t == 0) {
     mbar_init(bar, 1);
     mbar_init(ldbar, 1);
+    mbar_init(qbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     s_stop = 0;
+    if (qcopy) {  // the query tile, one bulk copy
+      qinflight = true;
+      mbar_expect_tx(qbar, (uint32_t)ATC_OPND);
+      bulk_g2s(sQ, a.q_img + ((size_t)h * a.q_tiles + blockIdx.x) * ATC_OPND, ATC_OPND, qbar);
+    }
     issue(t0, single);  // the first tile's copies overlap the q staging
   }
   if (warp == 0) {
     tmem_alloc(tslot, 256);
     tmem_relinquish();
   }
-  // q tile (rows past n are zeros)
-  atc_stage_row(sQ, t, qi < a.n_tokens ? a.q + ((size_t)qi * a.n_heads + h) * ATC_HD : nullptr);
-  fence_proxy_async_smem();
+  if (!qcopy) {
+    // q tile (rows past n are zeros)
+    atc_stage_row(sQ, t, qi < a.n_tokens ? a.q + ((size_t)qi * a.n_heads + h) * ATC_HD : nullptr);
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
-  __syncthreads();
+  __syncthreads();  // the barriers are initialised, the tensor memory allocated
   tc_fence_after();
+  // every CTA holds its tensor memory: a dependent kernel that allocates
+  // some may start now without this grid ever waiting on it
+  pdl_launch_dependents();
+  if (qcopy) {
+    // rows past n hold zeros or an earlier step's finite values: their
+    // outputs are not stored and rows do not mix in either product
+    if (!mbar_wait(qbar, 0, a.err)) {
+      atomicCAS(a.err, 0, 1);
+      s_stop = 1;
+    } else if (t == 0) {
+      qinflight = false;
+    }
+    __syncthreads();  // s_stop agreed on
+  }
   const uint32_t tmem = *tslot;
   const uint32_t tS = tmem, tO = tmem + 128;
   const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
   uint32_t phase = 0, ldphase = 0;
-  bool ok = true;
+  bool ok = !s_stop;  // the q copy's wait may have given up
 
   auto land = [&]() {  // everyone: the copies issued on ldbar have landed
     if (!mbar_wait(ldbar, ldphase, a.err)) {
@@ -288,9 +317,10 @@ static __global__ void __launch_bounds__(ATC_THREADS, 2) k_attn_prefill_tc(const
               make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
       }
     }
-  } else if (t == 0 && inflight) {
+  } else if (t == 0) {
     // a wait gave up: let the copies still in flight land before the exit
-    mbar_wait(ldbar, ldphase, a.err, false);
+    if (inflight) mbar_wait(ldbar, ldphase, a.err, false);
+    if (qinflight) mbar_wait(qbar, 0, a.err, false);
   }
   tc_fence_before();
   __syncthreads();
@@ -300,7 +330,7 @@ static __global__ void __launch_bounds__(ATC_THREADS, 2) k_attn_prefill_tc(const
   }
 }
 
-inline size_t attn_tc_smem_bytes() { return 3 * (size_t)ATC_OPND + 24 + 1024; }
+inline size_t attn_tc_smem_bytes() { return 3 * (size_t)ATC_OPND + 32 + 1024; }
 
 constexpr int ATC_MAX_SPLITS = 8;  // key ranges per query tile, at most
 static_assert(ATC_MAX_SPLITS <= ATC_MAX_SPLITS_IMG, "the o_proj image merges every range");

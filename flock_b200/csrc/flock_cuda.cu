@@ -259,6 +259,9 @@ int Workspace::alloc(const flock_layer_config& c, int sm_count, int tp_ranks) {
     FLOCK_TRY(kv_img.alloc(kv_image_bytes(c.max_keys, nKV)));
     FLOCK_CK(cudaMemset(kv_img.p, 0, kv_img.bytes));  // entries past a step's keys stay finite
     FLOCK_TRY(atc_part.alloc((size_t)ATC_MAX_SPLITS * P * nH * (hd + 2) * f));
+    q_tiles = (P + ATC_Q - 1) / ATC_Q;
+    FLOCK_TRY(q_img.alloc((size_t)nH * q_tiles * ATC_OPND));
+    FLOCK_CK(cudaMemset(q_img.p, 0, q_img.bytes));  // rows past a step's queries stay finite
   }
   if (tp_ranks >= 1 || H >= FLOCK_SPLIT_RESIDUAL_MIN_HIDDEN)  // also the split residual
     FLOCK_TRY(tp_part.alloc((size_t)P * H * f));
@@ -377,7 +380,11 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   if (n > 1 && tensor_cores) {
     qa.kv_img = ws->kv_img.as<uint8_t>();
     qa.img_tiles = img_tiles;
+    qa.q_img = ws->q_img.as<uint8_t>();
+    qa.q_tiles = ws->q_tiles;
   }
+  qa.rope_cs = ws->rope.as<float2>();
+  qa.rope_rows = ws->rope_rows;
   const bool kv_bf16 = c.kv_dtype == FLOCK_KV_BF16;
   if (kv_bf16 && !(n > 1 && tensor_cores)) {
     set_error("a bf16 KV cache runs decode on FLOCK_ATTN_FAST and prefill on the tensor cores");
@@ -421,6 +428,8 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
     ta.n_kv_heads = c.n_kv_heads;
     ta.err = ws->tc_err.as<int>();
     ta.part = ws->atc_part.as<float>();
+    ta.q_img = ws->q_img.as<uint8_t>();
+    ta.q_tiles = ws->q_tiles;
     // key ranges: sized from the host's count of cached keys (the kernel
     // reads pos0 on the device; a range past its query tile's keys is empty)
     const int nz = attn_tc_splits(L->n_keys, n);

@@ -98,6 +98,8 @@ struct Workspace {
   int rope_rows = 0;
   DBuf kv_img;                  // tensor-core prefill: f16 K / V^T tiles of the cache
   DBuf atc_part;                // tensor-core prefill attention: per key range O, m, l
+  DBuf q_img;                   // tensor-core prefill: f16 rotated queries [nH][q_tiles][128 x 128]
+  int q_tiles = 0;
   int atc_nz = 1;               // key ranges of the last tensor-core attention launch
   // tensor-core prefill across the layers of one pass: the enqueuer sets
   // defer_down when another layer follows, and down_pending is the number of

@@ -290,11 +290,10 @@ static __global__ void __launch_bounds__(TC_THREADS, 1)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int RAW_ROW = QT == QT_Q8 ? TC_KT : TC_KT / 2;  // raw bytes per row per K-tile
-  // launched with programmatic dependent launch: the next kernel may start
-  // its own prologue now; this one reads the previous kernel's output (the
-  // activation image, row scales, residual) only after griddepcontrol.wait
-  // -- the weight loads before it touch nothing any kernel writes
-  pdl_launch_dependents();
+  // launched with programmatic dependent launch: this kernel reads the
+  // previous kernel's output (the activation image, row scales, residual)
+  // only after griddepcontrol.wait -- the weight loads before it touch
+  // nothing any kernel writes
   constexpr uint32_t RAW_TX = (uint32_t)(TC_ROWS * RAW_ROW);
 
   if (threadIdx.x == 0) {
@@ -320,6 +319,9 @@ static __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  // every CTA holds its tensor memory: the next kernel may start its
+  // prologue (and allocate tensor memory) without this grid waiting on it
+  pdl_launch_dependents();
 
   int sgi = 0;
   while (sgi + 1 < a.nseg && (int)blockIdx.x >= a.tile0[sgi + 1]) sgi++;

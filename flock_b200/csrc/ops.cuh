@@ -74,9 +74,16 @@ struct QkArgs {
   int neox;
   PrefetchList pf;
   // tensor-core prefill: the f16 K / V^T tile image of the cache (attn_tc.cuh
-  // layout, img_tiles 128-key tiles per kv head) gets each new key too
+  // layout, img_tiles 128-key tiles per kv head) gets each new key too, and
+  // the f16 image of the rotated queries ([nH][q_tiles] 128-token tiles, the
+  // same layout) each query
   uint8_t* kv_img;
   int img_tiles;
+  uint8_t* q_img;
+  int q_tiles;
+  // RoPE (cos, sin) table [rope_rows][hd / 2] (k_rope_table), or null
+  const float2* rope_cs;
+  int rope_rows;
 };
 
 // Byte offset of element (row, 8-element chunk c16) of a 128 x 128 f16
@@ -214,9 +221,27 @@ static __global__ void __launch_bounds__(256) k_qk_norm_rope_append(const QkArgs
   const bool is_q = hv < a.n_heads;
   const int kvh = hv - a.n_heads;
   const int pos = a.ctl[0] + tok;
+  // the table's (cos, sin) are the values norm_rope_warp evaluates in f64
+  const bool table = a.rope_cs != nullptr && pos < a.rope_rows;
+  const float2* cs = table ? a.rope_cs + (size_t)pos * 64 : nullptr;
   if (is_q) {
-    norm_rope_warp(a.q + ((size_t)tok * a.n_heads + hv) * hd, a.q_norm, a.eps, pos, a.inv_freq,
-                   a.neox, a.qn + ((size_t)tok * a.n_heads + hv) * hd, lane);
+    float* qd = a.qn + ((size_t)tok * a.n_heads + hv) * hd;
+    if (table)
+      norm_rope_warp_cs(a.q + ((size_t)tok * a.n_heads + hv) * hd, a.q_norm, a.eps, cs, a.neox, qd,
+                        lane);
+    else
+      norm_rope_warp(a.q + ((size_t)tok * a.n_heads + hv) * hd, a.q_norm, a.eps, pos, a.inv_freq,
+                     a.neox, qd, lane);
+    if (a.q_img) {
+      // this query's row of its 128-token tile, f16 (this lane's own elements)
+      uint8_t* qt = a.q_img + ((size_t)hv * a.q_tiles + (tok >> 7)) * (128 * 128 * 2);
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int e = lane + 32 * q;
+        *reinterpret_cast<__half*>(qt + kvimg_off(tok & 127, e >> 3) + (e & 7) * 2) =
+            __float2half_rn(qd[e]);
+      }
+    }
   } else {
     const size_t row = ((size_t)pos * a.n_kv_heads + kvh) * hd;
     const float* k = a.k + ((size_t)tok * a.n_kv_heads + kvh) * hd;
@@ -224,7 +249,10 @@ static __global__ void __launch_bounds__(256) k_qk_norm_rope_append(const QkArgs
     float kf[4], vf[4];  // the values the cache now holds (for the f16 image)
     if constexpr (BF16) {
       float* ks = kstage + warp * 128;
-      norm_rope_warp(k, a.k_norm, a.eps, pos, a.inv_freq, a.neox, ks, lane);
+      if (table)
+        norm_rope_warp_cs(k, a.k_norm, a.eps, cs, a.neox, ks, lane);
+      else
+        norm_rope_warp(k, a.k_norm, a.eps, pos, a.inv_freq, a.neox, ks, lane);
       __syncwarp();
       uint16_t* kc = static_cast<uint16_t*>(a.kcache) + row;
       uint16_t* vc = static_cast<uint16_t*>(a.vcache) + row;
@@ -238,7 +266,10 @@ static __global__ void __launch_bounds__(256) k_qk_norm_rope_append(const QkArgs
       }
     } else {
       float* kc = static_cast<float*>(a.kcache) + row;
-      norm_rope_warp(k, a.k_norm, a.eps, pos, a.inv_freq, a.neox, kc, lane);
+      if (table)
+        norm_rope_warp_cs(k, a.k_norm, a.eps, cs, a.neox, kc, lane);
+      else
+        norm_rope_warp(k, a.k_norm, a.eps, pos, a.inv_freq, a.neox, kc, lane);
       float* vc = static_cast<float*>(a.vcache) + row;
 #pragma unroll
       for (int q = 0; q < 4; q++) {
