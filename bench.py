@@ -860,9 +860,15 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
 
     # the tensor-parallel path on the same N GPUs (config 4b's form at this
     # shape), reported as a key of this line
-    tp_line = None
+    tp_line, tp_error = None, None
     if args.also_tp and shape.n_layers == 28:
-        tp_line = run_tensor(args, rank, world, local, dev, shape, pk, emit=False, pg_ready=True)
+        try:
+            tp_line = run_tensor(args, rank, world, local, dev, shape, pk, emit=False,
+                                 pg_ready=True)
+        except Exception as e:  # the pipeline line stands on its own
+            tp_error = f"{type(e).__name__}: {e}"[:300]
+            log(f"[rank {rank}] tensor-parallel run failed: {tp_error}")
+        dist.barrier()
     if rank == 0:
         ids_oracle, ids_match = None, None
         if not args.no_oracle_ids:
@@ -914,6 +920,8 @@ def run_pipeline(args, rank, world, local, dev, m, shape, cfg, prompt, pk):
         if ids_oracle is not None:
             out["ids_match_oracle"] = ids_match
             out["ids_checked"] = len(ids_oracle)
+        if tp_error:
+            out["tensor_parallel"] = {"error": tp_error}
         if tp_line:
             out["tensor_parallel"] = {k: tp_line[k] for k in
                                       ("value", "unit", "ms_per_step", "e2e", "roofline",
