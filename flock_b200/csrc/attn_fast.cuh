@@ -341,12 +341,19 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
     }
   }
   if (!a.combine) return;  // combined by the caller after a grid-wide barrier
-  __threadfence();
+  // arrival: the CTA barrier orders every thread's partial stores before
+  // thread 0's release-acquire increment (release is cumulative); the last
+  // arrival's acquire, and the barrier after it, order the other splits'
+  // stores before the combine's loads
   sync();
-  if (t == 0) *last_flag = atomicAdd(a.count + g, 1u) == (uint32_t)(splits - 1);
+  if (t == 0) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.count + g)
+                 : "memory");
+    *last_flag = old == (uint32_t)(splits - 1);
+  }
   sync();
   if (!*last_flag) return;
-  __threadfence();
   // the combine spread over the whole CTA: every thread owns one (head,
   // element) and issues the loads of its element and of its head's (m, l)
   // for every split together (one round trip where a warp used to derive
@@ -357,6 +364,32 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   for (int oi = t; oi < G * hd; oi += ATTN_FAST_THREADS) {
     const int hq = oi / hd, i = oi - hq * hd;
     const float* pp = a.part + (size_t)(g * G + hq) * a.splits * (hd + 2);
+    if (splits <= 16) {
+      // one round trip: every (o, m, l) of the splits in flight together
+      float ov[16], mv[16], lv[16];
+#pragma unroll
+      for (int sp = 0; sp < 16; sp++) {
+        const bool has = sp < splits;
+        const float* q = pp + sp * (hd + 2);
+        ov[sp] = has ? __ldcg(q + i) : 0.0f;
+        mv[sp] = has ? __ldcg(q + hd) : -INFINITY;
+        lv[sp] = has ? __ldcg(q + hd + 1) : 0.0f;
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int sp = 0; sp < 16; sp++) M = fmaxf(M, mv[sp]);
+      float O = 0.0f, L = 0.0f;
+#pragma unroll
+      for (int sp = 0; sp < 16; sp++) {
+        if (sp < splits) {
+          const float w = expf(mv[sp] - M);
+          L = fmaf(lv[sp], w, L);
+          O = fmaf(ov[sp], w, O);
+        }
+      }
+      a.out[(size_t)(g * G + hq) * hd + i] = O / L;
+      continue;
+    }
     float M = -INFINITY;
     for (int s0 = 0; s0 < splits; s0 += 32) {
       float mv[32];
