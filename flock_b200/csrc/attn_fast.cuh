@@ -7,19 +7,22 @@
 //  * grid (kv head g, split s): each CTA owns a contiguous key range of one
 //    kv head and serves all G = nH/nKV query heads of that group, so each K/V
 //    row is read from HBM once per token, not once per query head;
-//  * per split: scores by warp-parallel dot products, local max m_s, local
-//    sum l_s and unnormalised output o_s (online-softmax partials);
+//  * per split: scores, local max m_s, local sum l_s and unnormalised
+//    output o_s (online-softmax partials);
 //  * the splits are combined by the last CTA of a group to finish (arrival
 //    counter), in both decode engines: out = sum_s o_s e^(m_s-M) /
-//    sum_s l_s e^(m_s-M), both sums in split order; one warp per query head
-//    derives the weights, then each thread sums one output element's splits
-//    with all of their loads in flight;
+//    sum_s l_s e^(m_s-M), both sums in split order (af_combine16); each
+//    thread combines one output element with all its splits' loads in
+//    flight;
 //  * a step over n keys uses ceil(n / 16) splits, at most
 //    attn_max_splits(SMs, kv heads, cache capacity): short contexts keep few
 //    partials, caches over 2048 keys run up to 3 CTAs per SM;
 //  * scores: one thread per (key, query head), a 128-long dot product over
 //    a K tile whose rows are padded to 132 floats (conflict-free 128-bit
-//    reads).
+//    reads);
+//  * before its dependency wait a split stages what no earlier kernel of the
+//    step writes (gains, the RoPE row, its first K/V tile), after it only
+//    the projection -- one round trip between the wait and the arithmetic.
 //
 // There is no key cap (the WGSL decode kernel stops at maxKeys = 2048).  The
 // reassociation changes rounding, so parity with attnRef is a tolerance
@@ -60,6 +63,7 @@ struct AttnFastArgs {
   // rope_rows (or no table) evaluate them in place
   const float2* rope_cs;
   int rope_rows;
+  int max_keys;  // cache rows; 0: nothing is staged before the dependency wait
 };
 
 constexpr int ATTN_FAST_THREADS = 256;
@@ -111,99 +115,168 @@ constexpr int AF_QRAW = 0, AF_KRAW = 512, AF_VRAW = 640, AF_GQ = 768, AF_GK = 89
               AF_KT = AF_CS + 128, AF_VT = AF_KT + ATTN_TILE * AF_KSTRIDE,
               AF_END = AF_VT + ATTN_TILE * 128;
 
+// The key range of split s for the token at position pos.
+struct AfRange {
+  int n_keys, splits, k0, k1, nk;
+};
+FLOCK_DEV AfRange af_range(const AttnFastArgs& a, int s, int pos) {
+  AfRange r;
+  r.n_keys = pos + 1;
+  r.splits = attn_splits_for(r.n_keys, a.splits);
+  const int chunk = (r.n_keys + r.splits - 1) / r.splits;
+  r.k0 = s * chunk;
+  r.k1 = min(r.n_keys, r.k0 + chunk);
+  r.nk = max(0, r.k1 - r.k0);
+  return r;
+}
+
+// keys [t0, t0 + nt) of kv head g into the K / V tiles; position pos (this
+// token's key, not yet in the cache) is skipped: its row comes from the
+// projection.  L2-direct loads: the rows are earlier steps' appends.
+FLOCK_DEV void af_stage_tile(const AttnFastArgs& a, int g, int pos, int t0, int nt, float* dsm) {
+  const int t = threadIdx.x;
+  const size_t kvs = (size_t)a.n_kv_heads * 128;
+  if (a.kv_bf16) {
+    // 16 x 128-bit loads per 256-byte bf16 row, widened to f32 in the tiles
+    for (int i = t; i < nt * 16; i += ATTN_FAST_THREADS) {
+      const int j = i >> 4, c8 = i & 15, key = t0 + j;
+      if (key == pos) continue;
+      const size_t off = (size_t)key * kvs + (size_t)g * 128;
+      const uint4 kw = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.kcache) + off) + c8);
+      const uint4 vw = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.vcache) + off) + c8);
+      bf16x8_widen(kw, dsm + AF_KT + j * AF_KSTRIDE + 8 * c8);
+      bf16x8_widen(vw, dsm + AF_VT + j * 128 + 8 * c8);
+    }
+    return;
+  }
+  for (int i = t; i < nt * 32; i += ATTN_FAST_THREADS) {
+    const int j = i >> 5, c4 = i & 31, key = t0 + j;
+    if (key == pos) continue;
+    const float4* kr = reinterpret_cast<const float4*>(static_cast<const float*>(a.kcache) +
+                                                       key * kvs + (size_t)g * 128);
+    const float4* vr = reinterpret_cast<const float4*>(static_cast<const float*>(a.vcache) +
+                                                       key * kvs + (size_t)g * 128);
+    reinterpret_cast<float4*>(dsm + AF_KT)[j * (AF_KSTRIDE / 4) + c4] = __ldcg(kr + c4);
+    reinterpret_cast<float4*>(dsm + AF_VT)[i] = __ldcg(vr + c4);
+  }
+}
+
+// What a split stages that no earlier kernel of the step writes: the q/k
+// gains, inverse frequencies, this position's RoPE (cos, sin) row and the
+// first K/V tile of the split's keys (rows earlier steps appended).  Safe to
+// run before griddepcontrol.wait with a position read there: the step's own
+// rows (position pos) are never read from the cache, and the decode graph
+// cannot keep the kernel that appended row pos - 1 (the same layer one step
+// earlier, ~5 x layers launches back) running while this one starts -- every
+// launch between them would have to be resident at once, waiting.
+FLOCK_DEV void af_stage_static(const AttnFastArgs& a, int g, int s, int pos, float* dsm) {
+  const int t = threadIdx.x;
+  const AfRange r = af_range(a, s, pos);
+  const bool fused = a.q_norm != nullptr;
+  if (t < 32 && fused) {
+    reinterpret_cast<float4*>(dsm + AF_GQ)[t] = reinterpret_cast<const float4*>(a.q_norm)[t];
+    reinterpret_cast<float4*>(dsm + AF_GK)[t] = reinterpret_cast<const float4*>(a.k_norm)[t];
+    if (t < 16)
+      reinterpret_cast<float4*>(dsm + AF_INV)[t] = reinterpret_cast<const float4*>(a.inv_freq)[t];
+    if (a.rope_cs != nullptr && pos < a.rope_rows)  // 64 (cos, sin) pairs: 32 float4
+      reinterpret_cast<float4*>(dsm + AF_CS)[t] =
+          reinterpret_cast<const float4*>(a.rope_cs + (size_t)pos * 64)[t];
+  }
+  af_stage_tile(a, g, pos, r.k0, min(r.nk, ATTN_TILE), dsm);
+}
+
+// What the step's earlier kernels wrote: the raw q/k/v projection (fused
+// norm + RoPE), or the normalised q and the appended k/v row at pos.
+FLOCK_DEV void af_stage_step(const AttnFastArgs& a, int g, int pos, float* dsm) {
+  const int G = a.n_heads / a.n_kv_heads;
+  const int t = threadIdx.x;
+  const float* qsrc = a.q + (size_t)g * G * 128;
+  for (int i = t; i < G * 32; i += ATTN_FAST_THREADS)
+    reinterpret_cast<float4*>(dsm + AF_QRAW)[i] = __ldcg(reinterpret_cast<const float4*>(qsrc) + i);
+  if (t >= 32) return;
+  if (a.q_norm != nullptr) {
+    reinterpret_cast<float4*>(dsm + AF_KRAW)[t] =
+        __ldcg(reinterpret_cast<const float4*>(a.k + (size_t)g * 128) + t);
+    reinterpret_cast<float4*>(dsm + AF_VRAW)[t] =
+        __ldcg(reinterpret_cast<const float4*>(a.v + (size_t)g * 128) + t);
+    return;
+  }
+  const size_t off = (size_t)pos * a.n_kv_heads * 128 + (size_t)g * 128;
+  if (a.kv_bf16) {
+    if (t < 16) {
+      bf16x8_widen(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.kcache) + off) + t),
+                   dsm + AF_KNEW + 8 * t);
+      bf16x8_widen(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.vcache) + off) + t),
+                   dsm + AF_VNEW + 8 * t);
+    }
+  } else {
+    reinterpret_cast<float4*>(dsm + AF_KNEW)[t] =
+        __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(a.kcache) + off) + t);
+    reinterpret_cast<float4*>(dsm + AF_VNEW)[t] =
+        __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(a.vcache) + off) + t);
+  }
+}
+
+// The combine of one output element from its splits' (o, m, l), loaded by
+// `get(split, what)` (what: 0 o, 1 m, 2 l): M = max_s m_s, w_s = e^(m_s - M),
+// L = sum_s l_s w_s, O = sum_s o_s w_s in split order, out = O / L, for up
+// to 16 splits with every load in flight.
+template <typename Get>
+FLOCK_DEV float af_combine16(int splits, Get get) {
+  float ov[16], mv[16], lv[16];
+#pragma unroll
+  for (int sp = 0; sp < 16; sp++) {
+    const bool has = sp < splits;
+    ov[sp] = has ? get(sp, 0) : 0.0f;
+    mv[sp] = has ? get(sp, 1) : -INFINITY;
+    lv[sp] = has ? get(sp, 2) : 0.0f;
+  }
+  float M = -INFINITY;
+#pragma unroll
+  for (int sp = 0; sp < 16; sp++) M = fmaxf(M, mv[sp]);
+  float O = 0.0f, L = 0.0f;
+#pragma unroll
+  for (int sp = 0; sp < 16; sp++) {
+    if (sp < splits) {
+      const float w = expf(mv[sp] - M);
+      L = fmaf(lv[sp], w, L);
+      O = fmaf(ov[sp], w, O);
+    }
+  }
+  return O / L;
+}
+
 // One (kv head g, split s) work item, run by ATTN_FAST_THREADS threads that
 // synchronise with `sync()`; `dsm` holds AF_END floats; `last` is a shared
-// flag.  `pos` is the position of the token being decoded.
+// flag.  `pos` is the position of the token being decoded.  The caller has
+// run af_stage_static and af_stage_step for (g, s, pos) -- the first of them
+// possibly before its dependency wait -- without a barrier after them.
 template <typename Sync>
-FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, float* dsm,
-                              bool* last_flag, Sync sync) {
+FLOCK_DEV void attn_fast_run(const AttnFastArgs& a, int g, int s, int pos, float* dsm,
+                             bool* last_flag, Sync sync) {
   const int G = a.n_heads / a.n_kv_heads;  // <= 4
   const int t = threadIdx.x;
   const int lane = t & 31, warp = t >> 5;
   const int hd = 128;
   const size_t kvs = (size_t)a.n_kv_heads * hd;
 
-  const int n_keys = pos + 1;
-  const int splits = attn_splits_for(n_keys, a.splits);
+  const AfRange r = af_range(a, s, pos);
+  const int splits = r.splits, k0 = r.k0, k1 = r.k1;
   if (s >= splits) return;  // uniform over the CTA, before any synchronisation
-  const int chunk = (n_keys + splits - 1) / splits;
-  const int k0 = s * chunk;
-  const int k1 = min(n_keys, k0 + chunk);
-  const int nk = max(0, k1 - k0);
   const bool fused = a.q_norm != nullptr;
   const bool table = fused && a.rope_cs != nullptr && pos < a.rope_rows;
-
-  // ---- one round trip: the token's raw q/k/v, gains, and the first K/V tile
-  auto stage_tile = [&](int t0, int nt) {
-    // keys [t0, t0 + nt) of kv head g; position pos is filled from knew/vnew
-    if (a.kv_bf16) {
-      // 16 x 128-bit loads per 256-byte bf16 row, widened to f32 in the tiles
-      for (int i = t; i < nt * 16; i += ATTN_FAST_THREADS) {
-        const int j = i >> 4, c8 = i & 15, key = t0 + j;
-        if (key == pos) continue;
-        const size_t off = (size_t)key * kvs + (size_t)g * hd;
-        const uint4 kw = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.kcache) + off)[c8];
-        const uint4 vw = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.vcache) + off)[c8];
-        bf16x8_widen(kw, dsm + AF_KT + j * AF_KSTRIDE + 8 * c8);
-        bf16x8_widen(vw, dsm + AF_VT + j * 128 + 8 * c8);
-      }
-      return;
-    }
-    for (int i = t; i < nt * 32; i += ATTN_FAST_THREADS) {
-      const int j = i >> 5, c4 = i & 31, key = t0 + j;
-      if (key == pos) continue;
-      const float4* kr = reinterpret_cast<const float4*>(static_cast<const float*>(a.kcache) +
-                                                         key * kvs + (size_t)g * hd);
-      const float4* vr = reinterpret_cast<const float4*>(static_cast<const float*>(a.vcache) +
-                                                         key * kvs + (size_t)g * hd);
-      reinterpret_cast<float4*>(dsm + AF_KT)[j * (AF_KSTRIDE / 4) + c4] = kr[c4];
-      reinterpret_cast<float4*>(dsm + AF_VT)[i] = vr[c4];
-    }
-  };
-  {
-    const float* qsrc = a.q + (size_t)g * G * hd;
-    for (int i = t; i < G * 32; i += ATTN_FAST_THREADS)
-      reinterpret_cast<float4*>(dsm + AF_QRAW)[i] = __ldcg(reinterpret_cast<const float4*>(qsrc) + i);
-    if (t < 32) {
-      if (fused) {
-        reinterpret_cast<float4*>(dsm + AF_KRAW)[t] =
-            __ldcg(reinterpret_cast<const float4*>(a.k + (size_t)g * hd) + t);
-        reinterpret_cast<float4*>(dsm + AF_VRAW)[t] =
-            __ldcg(reinterpret_cast<const float4*>(a.v + (size_t)g * hd) + t);
-        reinterpret_cast<float4*>(dsm + AF_GQ)[t] = reinterpret_cast<const float4*>(a.q_norm)[t];
-        reinterpret_cast<float4*>(dsm + AF_GK)[t] = reinterpret_cast<const float4*>(a.k_norm)[t];
-        if (t < 16)
-          reinterpret_cast<float4*>(dsm + AF_INV)[t] =
-              reinterpret_cast<const float4*>(a.inv_freq)[t];
-        if (table)  // 64 (cos, sin) pairs: 32 float4
-          reinterpret_cast<float4*>(dsm + AF_CS)[t] =
-              reinterpret_cast<const float4*>(a.rope_cs + (size_t)pos * 64)[t];
-      } else if (a.kv_bf16) {
-        const size_t off = (size_t)pos * kvs + (size_t)g * hd;
-        if (t < 16) {
-          bf16x8_widen(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.kcache) + off)[t],
-                       dsm + AF_KNEW + 8 * t);
-          bf16x8_widen(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.vcache) + off)[t],
-                       dsm + AF_VNEW + 8 * t);
-        }
-      } else {
-        const size_t off = (size_t)pos * kvs + (size_t)g * hd;
-        reinterpret_cast<float4*>(dsm + AF_KNEW)[t] =
-            reinterpret_cast<const float4*>(static_cast<const float*>(a.kcache) + off)[t];
-        reinterpret_cast<float4*>(dsm + AF_VNEW)[t] =
-            reinterpret_cast<const float4*>(static_cast<const float*>(a.vcache) + off)[t];
-      }
-    }
-    stage_tile(k0, min(nk, ATTN_TILE));
-  }
-  sync();
-
   float* qv = dsm + AF_QV;
   float* knew = dsm + AF_KNEW;
   float* vnew = dsm + AF_VNEW;
+  float* sc = dsm + AF_SC;
+  float* ml = dsm + AF_ML;  // per head: m, l, correction
+  float* kt = dsm + AF_KT;
+  float* vt = dsm + AF_VT;
+  float o[2] = {0.0f, 0.0f};  // outputs oi = t, t + 256 (G * 128 <= 512)
+  sync();
   if (fused) {
     // exact per-head RMSNorm + RoPE (k_qk_norm_rope_append's arithmetic):
-    // warps 0..G-1 the query heads, warp G the new key, warp G+1 copies v
+    // warps 0..G-1 the query heads, warp G the new key, warp G+1 copies v;
     // with the table the (cos, sin) pairs are the values norm_rope_warp
     // would evaluate in f64: the same bits without the f64 sin and cos
     const float2* cs = reinterpret_cast<const float2*>(dsm + AF_CS);
@@ -212,16 +285,16 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
         norm_rope_warp_cs(dsm + AF_QRAW + warp * 128, dsm + AF_GQ, a.eps, cs, a.neox,
                           qv + warp * 128, lane);
       else
-        norm_rope_warp(dsm + AF_QRAW + warp * 128, dsm + AF_GQ, a.eps, pos, dsm + AF_INV, a.neox,
-                       qv + warp * 128, lane);
+        norm_rope_warp(dsm + AF_QRAW + warp * 128, dsm + AF_GQ, a.eps, pos, dsm + AF_INV,
+                       a.neox, qv + warp * 128, lane);
     } else if (warp == G) {
       if (table)
         norm_rope_warp_cs(dsm + AF_KRAW, dsm + AF_GK, a.eps, cs, a.neox, knew, lane);
       else
         norm_rope_warp(dsm + AF_KRAW, dsm + AF_GK, a.eps, pos, dsm + AF_INV, a.neox, knew, lane);
-    }
-    else if (warp == G + 1)
+    } else if (warp == G + 1) {
       for (int i = lane; i < 128; i += 32) vnew[i] = dsm[AF_VRAW + i];
+    }
     sync();
     const size_t off = (size_t)pos * kvs + (size_t)g * hd + t;
     if (a.kv_bf16) {
@@ -247,21 +320,15 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   }
 
   const float scale = __double2float_rn(1.0 / sqrt((double)hd));
-  float* sc = dsm + AF_SC;
-  float* ml = dsm + AF_ML;  // per head: m, l, correction
-  float* kt = dsm + AF_KT;
-  float* vt = dsm + AF_VT;
   if (t < G) {
     ml[4 * t] = -INFINITY;
     ml[4 * t + 1] = 0.0f;
   }
-  float o[2] = {0.0f, 0.0f};  // outputs oi = t, t + 256 (G * 128 <= 512)
-
   for (int t0 = k0; t0 < k1; t0 += ATTN_TILE) {
     const int nt = min(ATTN_TILE, k1 - t0);
     if (t0 != k0) {
       sync();
-      stage_tile(t0, nt);
+      af_stage_tile(a, g, pos, t0, nt, dsm);
     }
     // the new key/value live in shared memory, not (yet) in the cache
     if (pos >= t0 && pos < t0 + nt && t < 128) {
@@ -270,7 +337,9 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
     }
     sync();
     // scores: one thread per (query head, key), four partial sums over the
-    // components of the 128-bit reads
+    // components of the 128-bit reads (a compact loop: what runs after the
+    // dependency wait is mostly instruction-fetch and latency bound, and a
+    // warp-per-dot-product form measured slower)
     for (int idx = t; idx < G * nt; idx += ATTN_FAST_THREADS) {
       const int hq = idx / nt, j = idx - hq * nt;
       const float4* kr = reinterpret_cast<const float4*>(kt + j * AF_KSTRIDE);
@@ -298,9 +367,9 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
       const float m_new = fmaxf(m_old, mt);
       float lt = 0.0f;
       for (int j = lane; j < nt; j += 32) {
-        const float p = expf(sc[hq * ATTN_TILE + j] - m_new);
-        sc[hq * ATTN_TILE + j] = p;
-        lt += p;
+        const float pj = expf(sc[hq * ATTN_TILE + j] - m_new);
+        sc[hq * ATTN_TILE + j] = pj;
+        lt += pj;
       }
 #pragma unroll
       for (int o2 = 16; o2 > 0; o2 >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o2);
@@ -356,38 +425,16 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   if (!*last_flag) return;
   // the combine spread over the whole CTA: every thread owns one (head,
   // element) and issues the loads of its element and of its head's (m, l)
-  // for every split together (one round trip where a warp used to derive
-  // the weights first), then derives M = max_s m_s, w_s = e^(m_s - M) and
-  // L = sum_s l_s w_s itself -- the same operations in the same split
-  // order for every thread of a head -- and O = sum_s o_s w_s in split
-  // order, out = O / L
+  // for every split together, then combines them (af_combine16) -- the same
+  // operations in the same split order for every thread of a head
   for (int oi = t; oi < G * hd; oi += ATTN_FAST_THREADS) {
     const int hq = oi / hd, i = oi - hq * hd;
     const float* pp = a.part + (size_t)(g * G + hq) * a.splits * (hd + 2);
     if (splits <= 16) {
-      // one round trip: every (o, m, l) of the splits in flight together
-      float ov[16], mv[16], lv[16];
-#pragma unroll
-      for (int sp = 0; sp < 16; sp++) {
-        const bool has = sp < splits;
+      a.out[(size_t)(g * G + hq) * hd + i] = af_combine16(splits, [&](int sp, int what) {
         const float* q = pp + sp * (hd + 2);
-        ov[sp] = has ? __ldcg(q + i) : 0.0f;
-        mv[sp] = has ? __ldcg(q + hd) : -INFINITY;
-        lv[sp] = has ? __ldcg(q + hd + 1) : 0.0f;
-      }
-      float M = -INFINITY;
-#pragma unroll
-      for (int sp = 0; sp < 16; sp++) M = fmaxf(M, mv[sp]);
-      float O = 0.0f, L = 0.0f;
-#pragma unroll
-      for (int sp = 0; sp < 16; sp++) {
-        if (sp < splits) {
-          const float w = expf(mv[sp] - M);
-          L = fmaf(lv[sp], w, L);
-          O = fmaf(ov[sp], w, O);
-        }
-      }
-      a.out[(size_t)(g * G + hq) * hd + i] = O / L;
+        return __ldcg(what == 0 ? q + i : q + hd + (what - 1));
+      });
       continue;
     }
     float M = -INFINITY;
@@ -424,39 +471,42 @@ FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, floa
   if (t == 0) a.count[g] = 0;
 }
 
+// The whole item for callers that stage in place (the persistent kernel).
+template <typename Sync>
+FLOCK_DEV void attn_fast_item(const AttnFastArgs& a, int g, int s, int pos, float* dsm,
+                              bool* last_flag, Sync sync) {
+  if (s >= attn_splits_for(pos + 1, a.splits)) return;
+  af_stage_static(a, g, s, pos, dsm);
+  af_stage_step(a, g, pos, dsm);
+  attn_fast_run(a, g, s, pos, dsm, last_flag, sync);
+}
+
 struct BlockSync {
   FLOCK_DEV void operator()() const { __syncthreads(); }
 };
 
+// Graph decode.  Before the dependency wait each split stages what
+// no earlier kernel of the step writes, for the position the step control
+// holds then (the step's position for every layer but the first, whose
+// earlier kernel advances it); after the wait it reads the position with the
+// projection and restages if the position moved.
 static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(const AttnFastArgs a) {
   extern __shared__ __align__(16) float dsm[];
   __shared__ bool last;
   issue_prefetch(a.pf);
   pdl_launch_dependents();
-  {
-    // before the wait: bring this split's first key tile into L2.  The
-    // position is read before the previous kernel may have advanced it (a
-    // prefetch of a neighbouring range is harmless: L2 stays coherent with
-    // the later loads); the rows are rows earlier steps wrote.
-    const int pos_guess = *(volatile const int*)a.ctl;
-    const int n_keys = pos_guess + 1;
-    const int splits = attn_splits_for(n_keys, a.splits);
-    const int s = blockIdx.y;
-    if (s < splits) {
-      const int chunk = (n_keys + splits - 1) / splits;
-      const int k0 = s * chunk, k1 = min(n_keys, k0 + chunk);
-      const int t = threadIdx.x;
-      const uint32_t row = a.kv_bf16 ? 256u : 512u;
-      const size_t kvs = (size_t)a.n_kv_heads * 128;
-      if (t < 2 * ATTN_TILE && k0 + (t >> 1) < min(k1, k0 + ATTN_TILE)) {
-        const int key = k0 + (t >> 1);
-        const size_t off = ((size_t)key * kvs + (size_t)blockIdx.x * 128) * (a.kv_bf16 ? 2 : 4);
-        prefetch_l2(static_cast<const uint8_t*>((t & 1) ? a.vcache : a.kcache) + off, row);
-      }
-    }
-  }
+  const int g = blockIdx.x, s = blockIdx.y;
+  const int guess = *(volatile const int*)a.ctl;
+  const bool pre = guess >= 0 && guess < a.max_keys && s < attn_splits_for(guess + 1, a.splits);
+  if (pre) af_stage_static(a, g, s, guess, dsm);
   pdl_wait();
-  attn_fast_item(a, blockIdx.x, blockIdx.y, a.ctl[0], dsm, &last, BlockSync{});
+  const int pos = __ldcg(a.ctl);
+  const AfRange r = af_range(a, s, pos);
+  if (s < r.splits) {
+    af_stage_step(a, g, pos, dsm);
+    if (!pre || pos != guess) af_stage_static(a, g, s, pos, dsm);
+  }
+  attn_fast_run(a, g, s, pos, dsm, &last, BlockSync{});
 }
 
 inline size_t attn_fast_smem(int /*chunk_cap*/) { return (size_t)AF_END * 4; }

@@ -664,6 +664,7 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.combine = 1;
     a.rope_cs = ws->rope.as<float2>();
     a.rope_rows = ws->rope_rows;
+    a.max_keys = c.max_keys;
     pf_add(a.pf, L->w[W_GATE]);
     pf_add(a.pf, L->w[W_UP]);
     const size_t smem = attn_fast_smem(a.chunk_cap);
