@@ -29,6 +29,7 @@ FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT, FLOCK_DECODE_EAGER, FLOCK_DECODE_
     0, 1, 2, 3
 FLOCK_PREFILL_EXACT, FLOCK_PREFILL_TENSOR = 0, 1
 FLOCK_KV_F32, FLOCK_KV_BF16 = 0, 1
+FLOCK_MATVEC_EXACT, FLOCK_MATVEC_FAST = 0, 1
 FLOCK_TP_NCCL, FLOCK_TP_PEER = 0, 1
 
 
@@ -46,7 +47,8 @@ class LayerConfigC(ctypes.Structure):
                 ("ffn", ctypes.c_int32), ("eps", ctypes.c_float), ("rope_base", ctypes.c_double),
                 ("max_keys", ctypes.c_int32), ("max_prefill", ctypes.c_int32),
                 ("rope_pairing", ctypes.c_int32), ("attention", ctypes.c_int32),
-                ("prefill", ctypes.c_int32), ("kv_dtype", ctypes.c_int32)]
+                ("prefill", ctypes.c_int32), ("kv_dtype", ctypes.c_int32),
+                ("matvec", ctypes.c_int32)]
 
 
 _vp = ctypes.c_void_p
@@ -86,6 +88,8 @@ SIGNATURES = {
     "flock_op_matvec": [_vp, _vp, _fp, _i, _fp],
     "flock_op_matvec_timed": [_vp, _vp, _i, _i, _fp],
     "flock_op_matvec_timed_cold": [_vp, _vp, _i, _i, _fp],
+    "flock_op_matvec_fast": [_vp, _vp, _fp, _fp],
+    "flock_op_matvec_fast_timed": [_vp, _vp, _i, _i, _fp],
     "flock_op_gemm": [_vp, _vp, _fp, _i, _fp],
     "flock_op_gemm_timed": [_vp, _vp, _i, _i, _fp, _fp],
     "flock_op_gemm_timed_cold": [_vp, _vp, _i, _i, _fp, _fp],

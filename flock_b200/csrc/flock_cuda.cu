@@ -20,6 +20,7 @@
 #include "gemm_tc.cuh"
 #include "flock_internal.h"
 #include "gemv.cuh"
+#include "gemv_fast.cuh"
 #include "ops.cuh"
 
 namespace flock {
@@ -159,6 +160,38 @@ int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl) {
 #undef GO
   if (e != cudaSuccess) {
     set_error("matvec launch failed: %s", cudaGetErrorString(e));
+    return FLOCK_E_CUDA;
+  }
+  return FLOCK_OK;
+}
+
+template <int QT, int EPI>
+static cudaError_t gemv_fast_go(flock_dev* d, const GemvArgs& a, int ctas, bool pdl) {
+  auto k = k_gemv_fast<QT, EPI>;
+  const size_t smem = gemv_fast_smem_bytes(a.K, a.norm_gain != nullptr);
+  if (kernel_setup((const void*)k, 200 * 1024)) return cudaErrorInvalidValue;
+  return launch_ex(d->stream, k, dim3(ctas, a.n_tokens), dim3(GEMV_THREADS), smem, pdl, a);
+}
+
+int launch_gemv_fast(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl) {
+  if (a.K % 32 != 0 || a.K > 12288 || a.n_tokens < 1) {
+    set_error("fast matvec cols %d must be a multiple of 32 and <= 12288", a.K);
+    return FLOCK_E_ARG;
+  }
+  int groups = 0;
+  for (int s = 0; s < a.nseg; s++) groups += (a.seg[s].rows + GF_ROWS - 1) / GF_ROWS;
+  const int ctas = gemv_grid(d, groups);
+  cudaError_t e = cudaErrorInvalidValue;
+  if (QT == QT_Q8 && EPI == EPI_STORE) e = gemv_fast_go<QT_Q8, EPI_STORE>(d, a, ctas, pdl);
+  else if (QT == QT_Q8 && EPI == EPI_RESIDUAL) e = gemv_fast_go<QT_Q8, EPI_RESIDUAL>(d, a, ctas, pdl);
+  else if (QT == QT_Q8 && EPI == EPI_ARGMAX) e = gemv_fast_go<QT_Q8, EPI_ARGMAX>(d, a, ctas, pdl);
+  else if (QT == QT_Q4 && EPI == EPI_STORE) e = gemv_fast_go<QT_Q4, EPI_STORE>(d, a, ctas, pdl);
+  else {
+    set_error("the fast matvec has the store, residual and argmax epilogues (Q4_0: store)");
+    return FLOCK_E_UNSUPPORTED;
+  }
+  if (e != cudaSuccess) {
+    set_error("fast matvec launch failed: %s", cudaGetErrorString(e));
     return FLOCK_E_CUDA;
   }
   return FLOCK_OK;
@@ -304,6 +337,10 @@ static int check_cfg(const flock_layer_config& c) {
   }
   if (c.kv_dtype != FLOCK_KV_F32 && c.kv_dtype != FLOCK_KV_BF16) {
     set_error("kv_dtype %d is neither FLOCK_KV_F32 nor FLOCK_KV_BF16", c.kv_dtype);
+    return FLOCK_E_ARG;
+  }
+  if (c.matvec != FLOCK_MATVEC_EXACT && c.matvec != FLOCK_MATVEC_FAST) {
+    set_error("matvec %d is neither FLOCK_MATVEC_EXACT nor FLOCK_MATVEC_FAST", c.matvec);
     return FLOCK_E_ARG;
   }
   if (c.kv_dtype == FLOCK_KV_BF16 &&
@@ -1010,7 +1047,7 @@ int flock_op_matvec(flock_dev* d, const flock_tensor* w, const float* x, int n_t
 }
 
 static int matvec_timed(flock_dev* d, const flock_tensor* w, int n_tokens, int iters, bool cold,
-                        float* ms_per_call) {
+                        float* ms_per_call, bool fast = false) {
   if (!d || !w || n_tokens < 1 || iters < 1 || !ms_per_call || w->dtype == FLOCK_F32)
     return FLOCK_E_ARG;
   FLOCK_CK(cudaSetDevice(d->ordinal));
@@ -1033,10 +1070,13 @@ static int matvec_timed(flock_dev* d, const flock_tensor* w, int n_tokens, int i
   a.x = tx.b.as<float>();
   a.x_stride = (int)w->cols;
   const int qt = w->dtype == FLOCK_Q8_0 ? QT_Q8 : QT_Q4;
-  FLOCK_TRY(launch_gemv(d, qt, EPI_STORE, a, false));  // warm-up
+  auto go = [&](bool pdl) {
+    return fast ? launch_gemv_fast(d, qt, EPI_STORE, a, pdl) : launch_gemv(d, qt, EPI_STORE, a, pdl);
+  };
+  FLOCK_TRY(go(false));  // warm-up
   if (!cold) {
     FLOCK_CK(cudaEventRecord(d->t0, d->stream));
-    for (int i = 0; i < iters; i++) FLOCK_TRY(launch_gemv(d, qt, EPI_STORE, a, true));
+    for (int i = 0; i < iters; i++) FLOCK_TRY(go(true));
     FLOCK_CK(cudaEventRecord(d->t1, d->stream));
     FLOCK_CK(cudaEventSynchronize(d->t1));
     float ms = 0;
@@ -1051,7 +1091,7 @@ static int matvec_timed(flock_dev* d, const flock_tensor* w, int n_tokens, int i
   for (int i = 0; i < iters; i++) {
     FLOCK_CK(cudaMemsetAsync(flush.p, i & 0xff, flush.bytes, d->stream));
     FLOCK_CK(cudaEventRecord(d->t0, d->stream));
-    FLOCK_TRY(launch_gemv(d, qt, EPI_STORE, a, false));
+    FLOCK_TRY(go(false));
     FLOCK_CK(cudaEventRecord(d->t1, d->stream));
     FLOCK_CK(cudaEventSynchronize(d->t1));
     float ms = 0;
@@ -1070,6 +1110,30 @@ int flock_op_matvec_timed(flock_dev* d, const flock_tensor* w, int n_tokens, int
 int flock_op_matvec_timed_cold(flock_dev* d, const flock_tensor* w, int n_tokens, int iters,
                                float* ms_per_call) {
   return matvec_timed(d, w, n_tokens, iters, true, ms_per_call);
+}
+
+int flock_op_matvec_fast(flock_dev* d, const flock_tensor* w, const float* x, float* out) {
+  if (!d || !w || !x || !out || w->dtype == FLOCK_F32) return FLOCK_E_ARG;
+  FLOCK_CK(cudaSetDevice(d->ordinal));
+  Tmp tx, to;
+  FLOCK_TRY(tx.put(x, (size_t)w->cols));
+  FLOCK_TRY(to.put<float>(nullptr, (size_t)w->rows));
+  GemvArgs a = {};
+  a.seg[0] = seg_of(w, to.b.as<float>(), (int)w->rows);
+  a.nseg = 1;
+  a.K = (int)w->cols;
+  a.n_tokens = 1;
+  a.x = tx.b.as<float>();
+  a.x_stride = (int)w->cols;
+  FLOCK_TRY(launch_gemv_fast(d, w->dtype == FLOCK_Q8_0 ? QT_Q8 : QT_Q4, EPI_STORE, a, false));
+  FLOCK_CK(cudaMemcpyAsync(out, to.b.p, (size_t)w->rows * 4, cudaMemcpyDeviceToHost, d->stream));
+  FLOCK_CK(cudaStreamSynchronize(d->stream));
+  return FLOCK_OK;
+}
+
+int flock_op_matvec_fast_timed(flock_dev* d, const flock_tensor* w, int iters, int cold,
+                               float* ms_per_call) {
+  return matvec_timed(d, w, 1, iters, cold != 0, ms_per_call, true);
 }
 
 int flock_op_rmsnorm(flock_dev* d, const float* x, const float* g, int n, int n_vecs, float eps,

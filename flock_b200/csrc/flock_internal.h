@@ -119,6 +119,9 @@ extern const char* const kTensorNames[W_COUNT];
 
 // Launch plan pieces
 int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl);
+// FLOCK_MATVEC_FAST: one token per CTA row on the int8 tensor cores
+// (store, residual and argmax epilogues; Q4_0 store only)
+int launch_gemv_fast(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl);
 // tensor-core prefill GEMM (flock_gemm.cu)
 struct TcArgs;
 struct TcSeg;

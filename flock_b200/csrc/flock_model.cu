@@ -158,11 +158,15 @@ int enqueue_head(flock_model* m, int row) {
   a.am_count = m->am_count.as<uint32_t>();
   a.am_best_val = m->am_best_val.as<float>();
   a.am_best_idx = m->ids.as<int32_t>();
-  if (!m->tp) return launch_gemv(m->dev, QT_Q8, EPI_ARGMAX, a, true);
+  auto go = [&] {
+    return m->cfg.matvec == FLOCK_MATVEC_FAST ? launch_gemv_fast(m->dev, QT_Q8, EPI_ARGMAX, a, true)
+                                              : launch_gemv(m->dev, QT_Q8, EPI_ARGMAX, a, true);
+  };
+  if (!m->tp) return go();
   a.am_row_offset = (int)m->tp_start[m->tp_rank];
   a.am_best_val = m->tp_best.as<float>();
   a.am_best_idx = m->tp_best.as<int32_t>() + 1;
-  FLOCK_TRY(launch_gemv(m->dev, QT_Q8, EPI_ARGMAX, a, true));
+  FLOCK_TRY(go());
   FLOCK_TRY(comm_allgather_dev(m->tp, m->tp_best.p, m->tp_bests.p, 8));
   k_tp_argmax<<<1, 32, 0, m->dev->stream>>>(m->tp_bests.as<uint32_t>(), m->tp_n,
                                             m->ids.as<int32_t>());
@@ -243,7 +247,7 @@ int mk_prepare(flock_model* m) {
   const flock_layer_config& c = m->cfg;
   m->mk_ok = false;
   if (c.attention != FLOCK_ATTN_FAST || !m->embd || !m->head || m->held < 1 || c.head_dim != 128 ||
-      c.n_heads / c.n_kv_heads > 4 || c.hidden > 4096 || m->tp)
+      c.n_heads / c.n_kv_heads > 4 || c.hidden > 4096 || m->tp || c.matvec != FLOCK_MATVEC_EXACT)
     return FLOCK_OK;
   int dev = m->dev->ordinal, coop = 0, smem_optin = 0;
   FLOCK_CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
@@ -448,6 +452,10 @@ int st_prepare(flock_model* m) {
   const flock_layer_config& c = m->cfg;
   if (c.attention != FLOCK_ATTN_FAST) {
     m->st.why = "needs fast (split-K) attention";
+    return FLOCK_OK;
+  }
+  if (c.matvec != FLOCK_MATVEC_EXACT) {
+    m->st.why = "its matvecs are the exact-order ones (FLOCK_MATVEC_EXACT)";
     return FLOCK_OK;
   }
   if (m->tp || !m->embd || !m->head || m->held < 1 || m->held != m->n_layers) {

@@ -48,17 +48,24 @@ class LayerConfig:
     # per key; appends round to nearest even; needs attention="fast" and
     # prefill="tensor")
     kv: str = "f32"
+    # one-token matvecs: "exact" (cpuMatmulQ8F32(coop(64))'s order, bit-identical)
+    # or "fast" (the decode LM head on the int8 tensor cores, reassociated,
+    # 1e-3 relative tolerance)
+    matvec: str = "exact"
 
     def to_c(self) -> _abi.LayerConfigC:
         if self.kv not in ("f32", "bf16"):
             raise ValueError(f"kv must be 'f32' or 'bf16', not {self.kv!r}")
+        if self.matvec not in ("exact", "fast"):
+            raise ValueError(f"matvec must be 'exact' or 'fast', not {self.matvec!r}")
         return _abi.LayerConfigC(
             self.hidden, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn, self.eps,
             self.rope_base, self.max_keys, self.max_prefill,
             _abi.FLOCK_ROPE_NEOX if self.rope_pairing == "neox" else _abi.FLOCK_ROPE_NORM,
             _abi.FLOCK_ATTN_EXACT if self.attention == "exact" else _abi.FLOCK_ATTN_FAST,
             _abi.FLOCK_PREFILL_TENSOR if self.prefill == "tensor" else _abi.FLOCK_PREFILL_EXACT,
-            _abi.FLOCK_KV_BF16 if self.kv == "bf16" else _abi.FLOCK_KV_F32)
+            _abi.FLOCK_KV_BF16 if self.kv == "bf16" else _abi.FLOCK_KV_F32,
+            _abi.FLOCK_MATVEC_FAST if self.matvec == "fast" else _abi.FLOCK_MATVEC_EXACT)
 
     def with_(self, **kw) -> "LayerConfig":
         return replace(self, **kw)

@@ -44,6 +44,26 @@ def matvec_timed(dev: Device, w: GpuTensor, n_tokens: int = 1, iters: int = 50) 
     return ms.value
 
 
+def matvec_fast(dev: Device, w: GpuTensor, x: np.ndarray) -> np.ndarray:
+    """One token's W x on the int8 tensor cores (FLOCK_MATVEC_FAST: x in three
+    int8 digits per 32-block, reassociated; max relative error 1e-3)."""
+    x = _f32(x)
+    if x.size != w.cols:
+        raise ValueError(f"x is {x.size} floats, want {w.cols}")
+    out = np.empty(w.rows, np.float32)
+    _abi.call("flock_op_matvec_fast", dev.handle, w.handle, _abi.ptr(x, _f), _abi.ptr(out, _f))
+    return out
+
+
+def matvec_fast_timed(dev: Device, w: GpuTensor, iters: int = 50, cold: bool = False) -> float:
+    """Mean ms per device-resident FLOCK_MATVEC_FAST launch (CUDA events); cold:
+    L2 evicted before each launch."""
+    ms = ctypes.c_float()
+    _abi.call("flock_op_matvec_fast_timed", dev.handle, w.handle, iters, int(cold),
+              ctypes.byref(ms))
+    return ms.value
+
+
 def gemm(dev: Device, w: GpuTensor, x: np.ndarray, m: int) -> np.ndarray:
     """[m][cols] x W^T on the tensor cores (f16 operands, f32 accumulation)."""
     x = _f32(x)

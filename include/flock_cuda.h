@@ -66,6 +66,13 @@ extern "C" {
                            read widens it exactly.  Needs FLOCK_ATTN_FAST and
                            FLOCK_PREFILL_TENSOR (the exact kernels are f32 only). */
 
+#define FLOCK_MATVEC_EXACT 0 /* one-token matvecs in cpuMatmulQ8F32(coop(64))'s f32 order
+                                (lib.ts:213), bit-identical */
+#define FLOCK_MATVEC_FAST 1  /* the decode LM head (output_norm + matvec + argmax) on the int8
+                                tensor cores: x split into three int8 digits per 32-block,
+                                exact int32 block sums, f32 scaling; reassociated, max
+                                relative error 1e-3 (measured ~1e-6) */
+
 typedef struct flock_dev flock_dev;
 typedef struct flock_tensor flock_tensor;
 typedef struct flock_layer flock_layer;
@@ -89,6 +96,7 @@ typedef struct flock_layer_config {
   int32_t attention;    /* FLOCK_ATTN_EXACT | FLOCK_ATTN_FAST */
   int32_t prefill;      /* FLOCK_PREFILL_EXACT | FLOCK_PREFILL_TENSOR (multi-token steps) */
   int32_t kv_dtype;     /* FLOCK_KV_F32 (0, the default) | FLOCK_KV_BF16 */
+  int32_t matvec;       /* FLOCK_MATVEC_EXACT (0, the default) | FLOCK_MATVEC_FAST */
 } flock_layer_config;
 
 /* ------------------------------------------------------------- errors/dev */
@@ -172,6 +180,14 @@ FLOCK_API int flock_op_matvec_timed(flock_dev* dev, const flock_tensor* w, int n
  * measurement aid like bench.ts:195; allocates its scratch.) */
 FLOCK_API int flock_op_matvec_timed_cold(flock_dev* dev, const flock_tensor* w, int n_tokens,
                                          int iters, float* ms_per_call);
+/* The FLOCK_MATVEC_FAST matvec of one token (int8 tensor cores; the same
+ * rows as flock_op_matvec to max relative error 1e-3), and its device-resident
+ * timing (cold: L2 evicted before each launch, as flock_op_matvec_timed_cold).
+ * Replaces nothing in the reference: its matvecs have one (the f32) order. */
+FLOCK_API int flock_op_matvec_fast(flock_dev* dev, const flock_tensor* w, const float* x,
+                                   float* out);
+FLOCK_API int flock_op_matvec_fast_timed(flock_dev* dev, const flock_tensor* w, int iters,
+                                         int cold, float* ms_per_call);
 /* The prefill matmul of layer.ts:685 encodePrefill (q8_coop.wgsl:76 /
  * q4_coop.wgsl:48 over M tokens) on the tcgen05 tensor cores: y[m][r] =
  * W x[m] with s * q and x (scaled per row by a power of two) rounded to f16

@@ -15,6 +15,8 @@ import {
   FLOCK_ATTN_FAST,
   FLOCK_E_UNSUPPORTED,
   FLOCK_KV_BF16,
+  FLOCK_MATVEC_EXACT,
+  FLOCK_MATVEC_FAST,
   FLOCK_KV_F32,
   FLOCK_PREFILL_EXACT,
   FLOCK_PREFILL_TENSOR,
@@ -66,7 +68,8 @@ export type LayerBuffers = Record<string, GpuTensor>;
  * defaulting to the reference's arithmetic): `attention` "exact" keeps
  * attnRef's order, "fast" is the split-K flash-decode; `prefill` "tensor"
  * runs multi-token steps on the tcgen05 tensor cores; `kvDtype` "bf16"
- * halves the cache.
+ * halves the cache; `matvec` "fast" runs the decode LM head on the int8
+ * tensor cores (reassociated, 1e-3 relative).
  */
 export interface LayerConfig {
   hidden: number;
@@ -82,6 +85,7 @@ export interface LayerConfig {
   attention?: "exact" | "fast";
   prefill?: "exact" | "tensor";
   kvDtype?: "f32" | "bf16";
+  matvec?: "exact" | "fast";
 }
 
 /** layer.ts:119 QWEN3_06B; maxKeys is not capped by workgroup memory here. */
@@ -131,6 +135,7 @@ export function configBytes(cfg: LayerConfig): Uint8Array {
     attention: cfg.attention === "fast" ? FLOCK_ATTN_FAST : FLOCK_ATTN_EXACT,
     prefill: cfg.prefill === "tensor" ? FLOCK_PREFILL_TENSOR : FLOCK_PREFILL_EXACT,
     kv_dtype: cfg.kvDtype === "bf16" ? FLOCK_KV_BF16 : FLOCK_KV_F32,
+    matvec: cfg.matvec === "fast" ? FLOCK_MATVEC_FAST : FLOCK_MATVEC_EXACT,
   });
 }
 

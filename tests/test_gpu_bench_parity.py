@@ -93,12 +93,16 @@ def oracle_run(oracle, model0):
     return prompt, ids, logits, forced, forced_logits
 
 
-@pytest.mark.parametrize("mode", ["kernels", "stream"])
+@pytest.mark.parametrize("mode", ["kernels", "stream", "kernels+fast-matvec"])
 def test_bench_config_greedy_ids_and_logits(dev, model0, oracle_run, mode):
+    """'kernels+fast-matvec': the kernel graph with the LM head on the int8
+    tensor cores (matvec="fast"), held to the same 1e-3 bar."""
     prompt, want_ids, want_logits, forced, forced_logits = oracle_run
+    matvec = "fast" if mode.endswith("+fast-matvec") else "exact"
+    mode = mode.split("+")[0]
     if mode not in Model._MODES:
         pytest.skip(f"decode mode {mode} is not built")
-    M = Model.create(dev, model0, QWEN3_06B.with_(attention="fast",
+    M = Model.create(dev, model0, QWEN3_06B.with_(attention="fast", matvec=matvec,
                                                   max_keys=PROMPT + N_DECODE + 8))
     M.decode_mode = mode
     if M.decode_mode != mode:
