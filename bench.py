@@ -204,7 +204,8 @@ def oracle_ids(m, shape, prompt, n: int) -> list:
 
 def config1_sweep(dev, pk) -> dict:
     """Benchmark config 1: the Q8_0 / Q4_0 matmul over the model's projection
-    shapes.  M = 1 (and 16) through the decode GEMV, M in {16, 128, 512}
+    shapes.  M = 1 (and 16) through the decode GEMV (M = 1 also through the
+    reassociated int8 tensor-core matvec, "gemv_fast"), M in {16, 128, 512}
     through the tcgen05 GEMM (f16 operands, f32 accumulation; the activation
     conversion is timed apart); every launch timed alone after a 256 MiB L2
     eviction, so the weights stream from HBM."""
@@ -221,12 +222,15 @@ def config1_sweep(dev, pk) -> dict:
             t = flib.GpuTensor.from_packed(dev, make(2, "t", n, k), n, k,
                                            flib.FLOCK_Q8_0 if q8 else flib.FLOCK_Q4_0)
             bpw = 1.0625 if q8 else 0.5625
-            for m_tok, eng in ((1, "gemv"), (16, "gemv"), (16, "tcgen05"), (128, "tcgen05"),
-                               (512, "tcgen05")):
+            for m_tok, eng in ((1, "gemv"), (1, "gemv_fast"), (16, "gemv"), (16, "tcgen05"),
+                               (128, "tcgen05"), (512, "tcgen05")):
                 ms = ctypes.c_float()
                 img = ctypes.c_float()
                 if eng == "gemv":
                     _abi.call("flock_op_matvec_timed_cold", dev.handle, t.handle, m_tok, 10,
+                              ctypes.byref(ms))
+                elif eng == "gemv_fast":
+                    _abi.call("flock_op_matvec_fast_timed", dev.handle, t.handle, 10, 1,
                               ctypes.byref(ms))
                 else:
                     _abi.call("flock_op_gemm_timed_cold", dev.handle, t.handle, m_tok, 10,
@@ -243,8 +247,8 @@ def config1_sweep(dev, pk) -> dict:
                 rows_out.append(r)
             t.free()
     return {"workload": "config 1: Q8_0/Q4_0 matmul sweep, K x N over the 0.6B projections "
-                        "and the 1024 x 151936 head, M in {1, 16} (GEMV) and {16, 128, 512} "
-                        "(tcgen05)",
+                        "and the 1024 x 151936 head, M in {1, 16} (GEMV; M = 1 also gemv_fast, "
+                        "the int8 tensor-core matvec) and {16, 128, 512} (tcgen05)",
             "timing": "each launch alone after a 256 MiB L2 eviction, CUDA events, mean of 10",
             "peak_hbm_gbs": pk["hbm_gbs"], "peak_bf16_tflops": pk["bf16_tflops"],
             "rows": rows_out}

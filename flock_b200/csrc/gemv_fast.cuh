@@ -4,12 +4,17 @@
 // Same function as kernels/q8_coop.wgsl:76 / q4_coop.wgsl:48 (y = W x with
 // per-32-weight f16 scales), but not in the reference's f32 order: the
 // parity bar is a relative error (1e-3 by contract, ~1e-6 measured), not
-// bit equality.  It exists because the exact order costs about three
-// instructions per weight (int8 -> f32 decode, product chains, the
-// pairwise tree) and the tall LM-head matvec is issue-bound on them; here
-// the weights go into mma.sync m16n8k32 s8 x s8 -> s32 straight from HBM
-// (no per-weight instruction at all) and the per-block scaling is the only
-// per-block arithmetic.
+// bit equality.  The exact order costs about three instructions per weight
+// (int8 -> f32 decode, product chains, the pairwise tree); here the weights
+// go into mma.sync m16n8k32 s8 x s8 -> s32 as loaded, with no per-weight
+// instruction, and only the per-block scaling runs on the SIMT pipes.
+// Measured on the 151936 x 1024 head it is not faster: 43 us against the
+// exact kernel's 36 (ncu: 21.5 M warp instructions against 26.8 M, about 70
+// per MMA -- the per-(row, block) scaling, its loads and conversions -- and
+// the exact kernel issue-bound at 66 % issue activity, this one waiting on
+// its loads -- long scoreboard the top stall -- at 51 %; an L2 bulk prefetch
+// of the group after next did not change it), so the exact kernel stays the
+// default and this one an option.
 //
 // x as exact integers: per 32-element block b, with sx = max |x| and
 // inv = 127 / sx, r = x * inv is split into three int8 digits

@@ -1,7 +1,9 @@
 """Small, fixed GPU workloads for profiling one kernel family at a time.
 
     python profile_cases.py layer [--time]   # one decode layer (config 0 shape, 256-key cache)
-    python profile_cases.py head  [--time]   # the 151936 x 1024 Q8_0 head matvec
+    python profile_cases.py head  [--time] [--fast]
+                                                # the 151936 x 1024 Q8_0 head matvec (--fast:
+                                                # and the int8 tensor-core matvec after it)
     python profile_cases.py gemv  [--time] [--8b]
                                                 # the config 1 matvec sweep (M = 1), or the
                                                 # 8B shapes (config 4)
@@ -68,12 +70,19 @@ def layer_case(timed: bool, attention: str = "fast") -> None:
 
 
 def head_case(timed: bool) -> None:
+    """--fast: the exact matvec (2 launches untimed) and then the int8
+    tensor-core matvec (FLOCK_MATVEC_FAST, 2 launches untimed)."""
     dev = flib.get_device(0)
     t = flib.GpuTensor.from_packed(dev, synth.q8_tensor(6, "head", 151936, 1024), 151936, 1024)
-    ms = ops.matvec_timed(dev, t, 1, 50 if timed else 3)
+    fast = "--fast" in sys.argv
+    ms = ops.matvec_timed(dev, t, 1, 50 if timed else (1 if fast else 3))
+    b = 151936 * 1024 * 1.0625 + 4 * (1024 + 151936)
     if timed:
-        b = 151936 * 1024 * 1.0625 + 4 * (1024 + 151936)
         print(f"head matvec: {ms * 1000:.2f} us, {b / ms / 1e6:.1f} GB/s")
+    if fast:
+        ms = ops.matvec_fast_timed(dev, t, 50 if timed else 1)
+        if timed:
+            print(f"head matvec (int8 tensor cores): {ms * 1000:.2f} us, {b / ms / 1e6:.1f} GB/s")
 
 
 def gemv_case(timed: bool) -> None:
