@@ -15,8 +15,8 @@
 //    thread combines one output element with all its splits' loads in
 //    flight;
 //  * a step over n keys uses ceil(n / 16) splits, at most
-//    attn_max_splits(SMs, kv heads, cache capacity): short contexts keep few
-//    partials, caches over 2048 keys run up to 3 CTAs per SM;
+//    attn_max_splits(SMs, kv heads, cache capacity): 16 for caches of up to
+//    2048 keys, caches over 2048 keys run up to 3 CTAs per SM;
 //  * scores: one thread per (key, query head), a 128-long dot product over
 //    a K tile whose rows are padded to 132 floats (conflict-free 128-bit
 //    reads);
@@ -70,8 +70,10 @@ constexpr int ATTN_FAST_THREADS = 256;
 constexpr int ATTN_TILE = 64;  // keys staged in shared memory per pass
 
 // Most splits a decode step may use: one wave of CTAs over the kv heads --
-// one CTA per SM, at most 32 splits, for caches of up to ATTN_LONG_KEYS keys
-// (short steps are latency-bound: fewer partials combine sooner); for longer
+// one CTA per SM, at most 16 splits, for caches of up to ATTN_LONG_KEYS keys
+// (short steps are latency-bound: fewer partials combine sooner, and up to
+// 16 combine in one round trip -- 18 splits at 257-320 keys measured 10 us
+// per token slower than 16); for longer
 // caches several CTAs per SM, so that one CTA's K/V loads overlap another's
 // arithmetic, and at most ATTN_MAX_SPLITS (a combining lane holds two).
 #ifndef FLOCK_ATTN_CTAS_PER_SM
@@ -86,7 +88,7 @@ static_assert(4 * ATTN_MAX_SPLITS <= 4 * ATTN_TILE, "combine weights live in the
 __host__ __device__ inline int attn_max_splits(int sm_count, int n_kv_heads, int max_keys) {
   const bool long_cache = max_keys > ATTN_LONG_KEYS;
   const int per_sm = long_cache ? FLOCK_ATTN_LONG_CTAS_PER_SM : FLOCK_ATTN_CTAS_PER_SM;
-  const int cap = long_cache ? ATTN_MAX_SPLITS : 32;
+  const int cap = long_cache ? ATTN_MAX_SPLITS : 16;
   int s = n_kv_heads > 0 ? sm_count * per_sm / n_kv_heads : 1;
   return s < 1 ? 1 : (s > cap ? cap : s);
 }

@@ -424,8 +424,16 @@ FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const f
   float accA[R], accB[R];
 #pragma unroll
   for (int r = 0; r < R; r++) accA[r] = accB[r] = 0.0f;
+  // EPI_RESIDUAL: lane 0 loads the group's residual rows when the group
+  // starts, so the round trip overlaps the fold instead of following it
+  float resv[EPI == EPI_RESIDUAL ? R : 1];
 
   while (have) {
+    if (EPI == EPI_RESIDUAL && m == 0 && lane == 0) {
+#pragma unroll
+      for (int r = 0; r < R; r++)
+        resv[r] = rs.ok[r] ? a.res[(size_t)tok * a.res_stride + rs.row[r]] : 0.0f;
+    }
     // issue the loads of the step LA ahead before folding this one
     const int gb = LA == 2 ? g1 : g, mb = LA == 2 ? m1 : m;
     int g2 = gb, m2 = mb + 1;
@@ -503,7 +511,7 @@ FLOCK_DEV void gemv_run(const GemvArgs& a, int tok, int cta, int n_ctas, const f
             if (!rs.ok[r]) continue;
             const GemvSeg& sg = a.seg[rs.seg[r]];
             float v = y[r];
-            if (EPI == EPI_RESIDUAL) v = fadd(a.res[(size_t)tok * a.res_stride + rs.row[r]], v);
+            if (EPI == EPI_RESIDUAL) v = fadd(resv[EPI == EPI_RESIDUAL ? r : 0], v);
             sg.out[(size_t)tok * sg.out_stride + rs.row[r]] = v;
             if (EPI == EPI_ARGMAX) {
               const uint32_t idx = (uint32_t)(rs.row[r] + a.am_row_offset);
