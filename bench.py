@@ -182,14 +182,15 @@ def cpu_baseline(m, shape, n_tokens: int = 2) -> dict:
                       f"(oracle/flock_oracle.c, OpenMP over rows, {cores} threads)"}
 
 
-def oracle_ids(m, shape, prompt, n: int) -> list:
+def oracle_ids(m, shape, prompt, n: int, kv: str = "f32") -> list:
     """The oracle's first n greedy ids for `prompt` (kernels/model.ts:387 step
-    composed from layer_ref.ts / head_ref.ts): the checker for the timed run."""
+    composed from layer_ref.ts / head_ref.ts): the checker for the timed run;
+    kv: the cache rounding the run uses ("f32", "bf16", "fp8")."""
     import oracle
     oracle.set_threads(len(os.sched_getaffinity(0)))
     cfg = dict(hidden=shape.hidden, n_heads=shape.n_heads, n_kv_heads=shape.n_kv_heads,
                head_dim=shape.head_dim, ffn=shape.ffn)
-    layers = [oracle.RefLayer(w, cfg, len(prompt) + n + 1) for w in m.layers]
+    layers = [oracle.RefLayer(w, cfg, len(prompt) + n + 1, kv=kv) for w in m.layers]
     ids, cur = [], [int(t) for t in prompt]
     for _ in range(n):
         h = oracle.embed(m.embd["packed"], cur, shape.hidden)
@@ -354,9 +355,10 @@ def main():
     ap.add_argument("--sweep", action=argparse.BooleanOptionalAction, default=True,
                     help="config 1: the Q8_0/Q4_0 GEMV and tensor-core GEMM sweep (L2 flushed "
                          "before every timed launch)")
-    ap.add_argument("--kv", default="f32", choices=["f32", "bf16"],
-                    help="KV cache element type (bf16: half the KV bytes per token; the "
-                         "tensor-core prefill and split-K decode attention)")
+    ap.add_argument("--kv", default="f32", choices=["f32", "bf16", "fp8"],
+                    help="KV cache element type (bf16 / fp8: a half / a quarter of the KV "
+                         "bytes per token; the tensor-core prefill and split-K decode "
+                         "attention)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -389,7 +391,7 @@ def main():
     n_prompt = args.prompt if args.prompt is not None else PROMPT
     max_keys = n_prompt + args.warmup + args.steps + 8
     cfg = QWEN3_06B.with_(max_keys=max(max_keys, 512), attention=args.attention)
-    if args.kv == "bf16" or n_prompt > 512:
+    if args.kv != "f32" or n_prompt > 512:
         cfg = cfg.with_(prefill="tensor", kv=args.kv)
     if args.shape == "8b":
         cfg = cfg.with_(hidden=shape.hidden, n_heads=shape.n_heads, n_kv_heads=shape.n_kv_heads,
@@ -462,7 +464,7 @@ def main():
     ids_oracle = None
     if not args.no_oracle_ids:
         n_chk = min(4, args.steps)
-        ids_oracle = oracle_ids(m, shape, prompt, n_chk + 1)
+        ids_oracle = oracle_ids(m, shape, prompt, n_chk + 1, kv=args.kv)
         ids_match = ids_oracle == [first] + ids_dev[:n_chk].tolist()
         log(f"oracle ids {ids_oracle}: match {ids_match}")
 
@@ -489,7 +491,7 @@ def main():
     head_bytes = shape.vocab * shape.hidden * 1.0625 + 4 * shape.hidden + 4 * shape.vocab
     head_gbs = head_bytes / (head_ms / 1000.0) / 1e9
     avg_keys = n_prompt + (args.steps - 1) / 2.0 + 1
-    kv_elem = 2 if args.kv == "bf16" else 4
+    kv_elem = {"bf16": 2, "fp8": 1}.get(args.kv, 4)
     tok_bytes = bytes_per_token(shape, avg_keys, kv_elem)
     token_gbs = tok_bytes * tok_s / 1e9
     # roofline: the whole decode token -- every weight byte and K/V row it

@@ -28,7 +28,7 @@ FLOCK_ATTN_EXACT, FLOCK_ATTN_FAST = 0, 1
 FLOCK_DECODE_KERNELS, FLOCK_DECODE_PERSISTENT, FLOCK_DECODE_EAGER, FLOCK_DECODE_STREAM = \
     0, 1, 2, 3
 FLOCK_PREFILL_EXACT, FLOCK_PREFILL_TENSOR = 0, 1
-FLOCK_KV_F32, FLOCK_KV_BF16 = 0, 1
+FLOCK_KV_F32, FLOCK_KV_BF16, FLOCK_KV_FP8 = 0, 1, 2
 FLOCK_MATVEC_EXACT, FLOCK_MATVEC_FAST = 0, 1
 FLOCK_TP_NCCL, FLOCK_TP_PEER = 0, 1
 

@@ -57,6 +57,7 @@ struct AttnFastArgs {
   int chunk_cap;   // max keys per split (informational; tiles of 64 are staged)
   int combine;     // 1: the last split of a group combines into out; 0: leave partials
   int kv_bf16;     // 1: the cache holds bf16 (widened into the f32 tiles as staged)
+  int kv_fp8;      // 1: the cache holds e4m3 (widened into the f32 tiles as staged)
   PrefetchList pf;
   // RoPE (cos, sin) per position and frequency, [rope_rows][hd / 2], the
   // values norm_rope_warp evaluates in f64 (k_rope_table); positions past
@@ -138,6 +139,19 @@ FLOCK_DEV AfRange af_range(const AttnFastArgs& a, int s, int pos) {
 FLOCK_DEV void af_stage_tile(const AttnFastArgs& a, int g, int pos, int t0, int nt, float* dsm) {
   const int t = threadIdx.x;
   const size_t kvs = (size_t)a.n_kv_heads * 128;
+  if (a.kv_fp8) {
+    // 8 x 128-bit loads per 128-byte e4m3 row, widened to f32 in the tiles
+    for (int i = t; i < nt * 8; i += ATTN_FAST_THREADS) {
+      const int j = i >> 3, c16 = i & 7, key = t0 + j;
+      if (key == pos) continue;
+      const size_t off = (size_t)key * kvs + (size_t)g * 128;
+      const uint4 kw = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.kcache) + off) + c16);
+      const uint4 vw = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.vcache) + off) + c16);
+      fp8x16_widen(kw, dsm + AF_KT + j * AF_KSTRIDE + 16 * c16);
+      fp8x16_widen(vw, dsm + AF_VT + j * 128 + 16 * c16);
+    }
+    return;
+  }
   if (a.kv_bf16) {
     // 16 x 128-bit loads per 256-byte bf16 row, widened to f32 in the tiles
     for (int i = t; i < nt * 16; i += ATTN_FAST_THREADS) {
@@ -204,7 +218,14 @@ FLOCK_DEV void af_stage_step(const AttnFastArgs& a, int g, int pos, float* dsm) 
     return;
   }
   const size_t off = (size_t)pos * a.n_kv_heads * 128 + (size_t)g * 128;
-  if (a.kv_bf16) {
+  if (a.kv_fp8) {
+    if (t < 8) {
+      fp8x16_widen(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.kcache) + off) + t),
+                   dsm + AF_KNEW + 16 * t);
+      fp8x16_widen(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.vcache) + off) + t),
+                   dsm + AF_VNEW + 16 * t);
+    }
+  } else if (a.kv_bf16) {
     if (t < 16) {
       bf16x8_widen(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.kcache) + off) + t),
                    dsm + AF_KNEW + 8 * t);
@@ -299,7 +320,19 @@ FLOCK_DEV void attn_fast_run(const AttnFastArgs& a, int g, int s, int pos, float
     }
     sync();
     const size_t off = (size_t)pos * kvs + (size_t)g * hd + t;
-    if (a.kv_bf16) {
+    if (a.kv_fp8) {
+      // as with bf16: every split rounds its own copy, split 0 appends it
+      if (t < 128) {
+        const uint8_t kb = fp8_bits(knew[t]), vb = fp8_bits(vnew[t]);
+        knew[t] = fp8_widen(kb);
+        vnew[t] = fp8_widen(vb);
+        if (s == 0) {
+          static_cast<uint8_t*>(a.kcache)[off] = kb;
+          static_cast<uint8_t*>(a.vcache)[off] = vb;
+        }
+      }
+      sync();
+    } else if (a.kv_bf16) {
       // every split rounds its own copy of the new key/value, so the scores
       // see the value the cache keeps; split 0 appends it
       if (t < 128) {

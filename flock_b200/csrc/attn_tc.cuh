@@ -350,13 +350,14 @@ inline int attn_tc_splits(int pos0_max, int n) {
 // writes the K tile ([key][head_dim], rows past kend = pos0 + n zero) and
 // the V^T tile ([head_dim][key]), transposed through shared memory so every
 // global load is a coalesced row.  The grid covers the tiles holding keys
-// before pos0; tiles of new keys only return at once.  BF16: the cache holds
-// bf16, widened exactly before the f16 rounding.  Image entries past kend in
+// before pos0; tiles of new keys only return at once.  KV: the cache's element
+// (FLOCK_KV_F32 / _BF16 / _FP8); bf16 and e4m3 are widened exactly before the
+// f16 rounding (e4m3 values are f16 values).  Image entries past kend in
 // a tile the append wrote hold zeros (the buffer is cleared when allocated)
 // or finite values of earlier steps: those keys are masked out of S, and
 // their V^T columns meet P = 0.
 constexpr int KVI_STRIDE = 132;  // f32 row stride of the transposition buffer
-template <bool BF16>
+template <int KV>
 static __global__ void __launch_bounds__(ATC_THREADS) k_kv_image(const void* kcache,
                                                                 const void* vcache,
                                                                 int n_kv_heads, const int* ctl,
@@ -375,7 +376,32 @@ static __global__ void __launch_bounds__(ATC_THREADS) k_kv_image(const void* kca
   const size_t off = (size_t)key * kvs + (size_t)g * ATC_HD;
   uint8_t* kdst = img + ((size_t)g * img_tiles + kt) * 2 * ATC_OPND;
   uint8_t* vdst = kdst + ATC_OPND;
-  if constexpr (BF16) {
+  if constexpr (KV == 2) {
+    const uint4* kr = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(kcache) + off);
+    const uint4* vr = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(vcache) + off);
+    float kf[16];
+#pragma unroll 2
+    for (int c = 0; c < 8; c++) {
+      uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
+      if (key < kend) {
+        fp8x16_widen(__ldg(kr + c), kf);
+        o0 = make_uint4(h2(kf[0], kf[1]), h2(kf[2], kf[3]), h2(kf[4], kf[5]), h2(kf[6], kf[7]));
+        o1 = make_uint4(h2(kf[8], kf[9]), h2(kf[10], kf[11]), h2(kf[12], kf[13]), h2(kf[14], kf[15]));
+      }
+      *reinterpret_cast<uint4*>(kdst + atc_off(t, 2 * c)) = o0;
+      *reinterpret_cast<uint4*>(kdst + atc_off(t, 2 * c + 1)) = o1;
+    }
+#pragma unroll 2
+    for (int c = 0; c < 8; c++) {
+      float* dst = vbuf + t * KVI_STRIDE + 16 * c;
+      if (key < kend) {
+        fp8x16_widen(__ldg(vr + c), dst);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; q++) reinterpret_cast<float4*>(dst)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  } else if constexpr (KV == 1) {
     const uint4* kr = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(kcache) + off);
     const uint4* vr = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(vcache) + off);
     float kf[8];

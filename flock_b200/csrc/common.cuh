@@ -13,6 +13,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <float.h>
 #include <stdint.h>
@@ -38,6 +39,31 @@ FLOCK_DEV uint16_t bf16_bits(float x) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 FLOCK_DEV float bf16_round(float x) { return __uint_as_float((uint32_t)bf16_bits(x) << 16); }
+
+// fp8 KV cache elements (FLOCK_KV_FP8): OCP E4M3FN, a key or value rounded to
+// the nearest e4m3 (ties to even; magnitudes past 448 saturate to 448) once,
+// when it is appended, and widened exactly (e4m3 is a subset of f16) on read.
+FLOCK_DEV uint8_t fp8_bits(float x) {
+  return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+FLOCK_DEV float fp8_widen(uint8_t b) {
+  return __half2float(__half(__nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)b, __NV_E4M3)));
+}
+FLOCK_DEV float fp8_round(float x) { return fp8_widen(fp8_bits(x)); }
+// Two e4m3 in the low 16 bits of w -> two f32.
+FLOCK_DEV float2 fp8x2_widen(uint32_t w) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w & 0xFFFFu), __NV_E4M3);
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+// Sixteen e4m3 (one 128-bit load) -> sixteen f32 at dst (16-byte aligned).
+FLOCK_DEV void fp8x16_widen(uint4 w, float* dst) {
+  const uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const float2 a = fp8x2_widen(v[i]), b = fp8x2_widen(v[i] >> 16);
+    reinterpret_cast<float4*>(dst)[i] = make_float4(a.x, a.y, b.x, b.y);
+  }
+}
 // Two bf16 packed in a word (element 0 in the low half) -> two f32.
 FLOCK_DEV float2 bf16x2_widen(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));

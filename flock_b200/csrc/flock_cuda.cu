@@ -335,18 +335,18 @@ static int check_cfg(const flock_layer_config& c) {
               c.ffn);
     return FLOCK_E_UNSUPPORTED;
   }
-  if (c.kv_dtype != FLOCK_KV_F32 && c.kv_dtype != FLOCK_KV_BF16) {
-    set_error("kv_dtype %d is neither FLOCK_KV_F32 nor FLOCK_KV_BF16", c.kv_dtype);
+  if (c.kv_dtype != FLOCK_KV_F32 && c.kv_dtype != FLOCK_KV_BF16 && c.kv_dtype != FLOCK_KV_FP8) {
+    set_error("kv_dtype %d is not FLOCK_KV_F32, FLOCK_KV_BF16 or FLOCK_KV_FP8", c.kv_dtype);
     return FLOCK_E_ARG;
   }
   if (c.matvec != FLOCK_MATVEC_EXACT && c.matvec != FLOCK_MATVEC_FAST) {
     set_error("matvec %d is neither FLOCK_MATVEC_EXACT nor FLOCK_MATVEC_FAST", c.matvec);
     return FLOCK_E_ARG;
   }
-  if (c.kv_dtype == FLOCK_KV_BF16 &&
+  if (c.kv_dtype != FLOCK_KV_F32 &&
       (c.attention != FLOCK_ATTN_FAST || c.prefill != FLOCK_PREFILL_TENSOR)) {
-    set_error("a bf16 KV cache needs FLOCK_ATTN_FAST and FLOCK_PREFILL_TENSOR (the exact "
-              "kernels read f32)");
+    set_error("a %s KV cache needs FLOCK_ATTN_FAST and FLOCK_PREFILL_TENSOR (the exact "
+              "kernels read f32)", c.kv_dtype == FLOCK_KV_BF16 ? "bf16" : "fp8");
     return FLOCK_E_UNSUPPORTED;
   }
   if (c.attention == FLOCK_ATTN_EXACT && c.max_keys > 48 * 1024) {
@@ -422,12 +422,16 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
   }
   qa.rope_cs = ws->rope.as<float2>();
   qa.rope_rows = ws->rope_rows;
-  const bool kv_bf16 = c.kv_dtype == FLOCK_KV_BF16;
-  if (kv_bf16 && !(n > 1 && tensor_cores)) {
-    set_error("a bf16 KV cache runs decode on FLOCK_ATTN_FAST and prefill on the tensor cores");
+  const int kv = c.kv_dtype;
+  if (kv != FLOCK_KV_F32 && !(n > 1 && tensor_cores)) {
+    set_error("a %s KV cache runs decode on FLOCK_ATTN_FAST and prefill on the tensor cores",
+              kv == FLOCK_KV_BF16 ? "bf16" : "fp8");
     return FLOCK_E_UNSUPPORTED;
   }
-  FLOCK_CK(launch_ex(d->stream, kv_bf16 ? k_qk_norm_rope_append<true> : k_qk_norm_rope_append<false>,
+  FLOCK_CK(launch_ex(d->stream,
+                     kv == FLOCK_KV_FP8 ? k_qk_norm_rope_append<FLOCK_KV_FP8>
+                     : kv == FLOCK_KV_BF16 ? k_qk_norm_rope_append<FLOCK_KV_BF16>
+                                           : k_qk_norm_rope_append<FLOCK_KV_F32>,
                      dim3((n * (c.n_heads + c.n_kv_heads) + 7) / 8), dim3(256), 0, pdl, qa));
   AttnArgs aa = {};
   aa.q = ws->qn.as<float>();
@@ -445,7 +449,8 @@ static int enqueue_qk_attn(flock_layer* L, int n, bool pdl, bool tensor_cores) {
     // the device; the new keys went into the image with the append); a
     // step from an empty cache has none
     if (L->n_keys > 0) {
-      auto* kvi = kv_bf16 ? k_kv_image<true> : k_kv_image<false>;
+      auto* kvi = kv == FLOCK_KV_FP8 ? k_kv_image<FLOCK_KV_FP8>
+                  : kv == FLOCK_KV_BF16 ? k_kv_image<FLOCK_KV_BF16> : k_kv_image<FLOCK_KV_F32>;
       FLOCK_TRY(kernel_setup((const void*)kvi, (int)kv_image_smem_bytes()));
       const int old_tiles = (L->n_keys + ATC_K - 1) / ATC_K;
       FLOCK_CK(launch_ex(d->stream, kvi,
@@ -687,6 +692,7 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     a.kcache = L->kcache.p;
     a.vcache = L->vcache.p;
     a.kv_bf16 = c.kv_dtype == FLOCK_KV_BF16;
+    a.kv_fp8 = c.kv_dtype == FLOCK_KV_FP8;
     a.ctl = L->ctl;
     a.out = ws->attn.as<float>();
     a.part = ws->attn_part.as<float>();
@@ -1516,10 +1522,52 @@ int flock_layer_n_keys(const flock_layer* L, int* out) {
   return FLOCK_OK;
 }
 
+// OCP E4M3FN on the host: code -> value (exact), and value -> the nearest
+// code (ties to even, magnitudes past 448 saturating to 448, NaN to 0x7F),
+// the conversion the device's cvt.rn.satfinite performs.
+static float host_fp8_value(uint8_t b) {
+  const int sgn = b >> 7, e = (b >> 3) & 15, m = b & 7;
+  if (e == 15 && m == 7) return NAN;
+  const float mag = e == 0 ? std::ldexp((float)m, -9) : std::ldexp((float)(8 + m), e - 10);
+  return sgn ? -mag : mag;
+}
+static uint8_t host_fp8_bits(float x) {
+  if (std::isnan(x)) return 0x7F;
+  const uint8_t sgn = std::signbit(x) ? 0x80 : 0;
+  float a = std::fabs(x);
+  if (a >= 448.0f) return sgn | 0x7E;
+  int e2 = 0;
+  std::frexp(a, &e2);            // a = f * 2^e2, f in [0.5, 1)
+  int E = e2 - 1;                // a in [2^E, 2^(E+1))
+  if (E < -6) E = -6;            // subnormals: steps of 2^-9
+  const float step = std::ldexp(1.0f, E - 3);
+  const float q = std::nearbyint(a / step);  // ties to even (the default rounding mode)
+  const float r = q * step;
+  if (r == 0.0f) return sgn;
+  int re = 0;
+  std::frexp(r, &re);
+  const int Er = re - 1;
+  if (Er < -6) return sgn | (uint8_t)(r / std::ldexp(1.0f, -9));  // subnormal code
+  const int mant = (int)(r / std::ldexp(1.0f, Er - 3)) - 8;
+  return sgn | (uint8_t)((Er + 7) << 3) | (uint8_t)mant;
+}
+
 int flock_layer_read_cache(flock_layer* L, float* k, float* v) {
   if (!L || !k || !v) return FLOCK_E_ARG;
   const size_t count = (size_t)L->n_keys * L->cfg.n_kv_heads * L->cfg.head_dim;
-  if (count && L->cfg.kv_dtype == FLOCK_KV_BF16) {
+  if (count && L->cfg.kv_dtype == FLOCK_KV_FP8) {
+    // e4m3 -> f32 exactly
+    std::vector<uint8_t> kb(count), vb(count);
+    FLOCK_CK(cudaMemcpyAsync(kb.data(), L->kcache.p, count, cudaMemcpyDeviceToHost,
+                             L->dev->stream));
+    FLOCK_CK(cudaMemcpyAsync(vb.data(), L->vcache.p, count, cudaMemcpyDeviceToHost,
+                             L->dev->stream));
+    FLOCK_CK(cudaStreamSynchronize(L->dev->stream));
+    for (size_t i = 0; i < count; i++) {
+      k[i] = host_fp8_value(kb[i]);
+      v[i] = host_fp8_value(vb[i]);
+    }
+  } else if (count && L->cfg.kv_dtype == FLOCK_KV_BF16) {
     // bf16 -> f32 exactly: the stored bits become the high half
     std::vector<uint16_t> kb(count), vb(count);
     FLOCK_CK(cudaMemcpyAsync(kb.data(), L->kcache.p, count * 2, cudaMemcpyDeviceToHost,
@@ -1552,7 +1600,19 @@ int flock_layer_write_cache(flock_layer* L, const float* k, const float* v, int 
   if (!L || !k || !v || n_keys < 0 || L->n_keys + n_keys > L->cfg.max_keys) return FLOCK_E_ARG;
   const size_t elems = (size_t)L->cfg.n_kv_heads * L->cfg.head_dim;
   const size_t row = elems * kv_elem_bytes(L->cfg);
-  if (L->cfg.kv_dtype == FLOCK_KV_BF16) {
+  if (L->cfg.kv_dtype == FLOCK_KV_FP8) {
+    const size_t count = elems * (size_t)n_keys;
+    std::vector<uint8_t> kb(count), vb(count);
+    for (size_t i = 0; i < count; i++) {
+      kb[i] = host_fp8_bits(k[i]);
+      vb[i] = host_fp8_bits(v[i]);
+    }
+    FLOCK_CK(cudaMemcpyAsync(L->kcache.as<uint8_t>() + L->n_keys * row, kb.data(), n_keys * row,
+                             cudaMemcpyHostToDevice, L->dev->stream));
+    FLOCK_CK(cudaMemcpyAsync(L->vcache.as<uint8_t>() + L->n_keys * row, vb.data(), n_keys * row,
+                             cudaMemcpyHostToDevice, L->dev->stream));
+    FLOCK_CK(cudaStreamSynchronize(L->dev->stream));  // before the host copies go
+  } else if (L->cfg.kv_dtype == FLOCK_KV_BF16) {
     const size_t count = elems * (size_t)n_keys;
     std::vector<uint16_t> kb(count), vb(count);
     for (size_t i = 0; i < count; i++) {

@@ -188,7 +188,7 @@ struct flock_layer {
 namespace flock {
 // Bytes per cached key/value element: 4 (FLOCK_KV_F32) or 2 (FLOCK_KV_BF16).
 inline size_t kv_elem_bytes(const flock_layer_config& c) {
-  return c.kv_dtype == FLOCK_KV_BF16 ? 2 : 4;
+  return c.kv_dtype == FLOCK_KV_BF16 ? 2 : c.kv_dtype == FLOCK_KV_FP8 ? 1 : 4;
 }
 // Enqueue one layer step over ws->h (in place): n tokens at the layer's pos.
 // `advance` = this launch advances the layer's ctl; pf_next = L2 prefetch

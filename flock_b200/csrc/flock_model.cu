@@ -396,6 +396,7 @@ int mk_prepare(flock_model* m) {
       aa.kcache = L->kcache.p;
       aa.vcache = L->vcache.p;
       aa.kv_bf16 = c.kv_dtype == FLOCK_KV_BF16;
+      aa.kv_fp8 = c.kv_dtype == FLOCK_KV_FP8;
       aa.out = ws.attn.as<float>();
       aa.part = ws.attn_part.as<float>();
       aa.count = ws.attn_count.as<uint32_t>();
@@ -456,6 +457,10 @@ int st_prepare(flock_model* m) {
   }
   if (c.matvec != FLOCK_MATVEC_EXACT) {
     m->st.why = "its matvecs are the exact-order ones (FLOCK_MATVEC_EXACT)";
+    return FLOCK_OK;
+  }
+  if (c.kv_dtype == FLOCK_KV_FP8) {
+    m->st.why = "its attention reads f32 or bf16 caches";
     return FLOCK_OK;
   }
   if (m->tp || !m->embd || !m->head || m->held < 1 || m->held != m->n_layers) {

@@ -66,7 +66,7 @@ struct QkArgs {
   const float* k_norm;
   const float* inv_freq;  // [hd/2]
   float* qn;        // [n][nH][hd] out
-  void* kcache;     // [maxKeys][nKV][hd], f32 (or bf16 for k_qk_norm_rope_append<true>)
+  void* kcache;     // [maxKeys][nKV][hd], f32 (bf16 / e4m3 for k_qk_norm_rope_append<1 / 2>)
   void* vcache;
   const int* ctl;   // ctl[0] = pos0
   int n_tokens, n_heads, n_kv_heads, head_dim;
@@ -204,12 +204,12 @@ static __global__ void k_rope_table(const float* inv_freq, int n_pos, float2* ou
 
 // One warp per 128-vector (8 per CTA): q heads -> qn, k heads -> the cache at
 // position pos0 + token with v copied beside it.  norm_rope_warp's arithmetic
-// is the WG = 128 RMSNorm and RoPE above, bit for bit.  BF16: the cache holds
-// bf16; the rotated key is staged in shared memory and stored rounded to
-// nearest even, as is v.
-template <bool BF16>
+// is the WG = 128 RMSNorm and RoPE above, bit for bit.  KV: the cache's
+// element (FLOCK_KV_F32 / _BF16 / _FP8); for bf16 and e4m3 the rotated key is
+// staged in shared memory and stored rounded to nearest even, as is v.
+template <int KV>
 static __global__ void __launch_bounds__(256) k_qk_norm_rope_append(const QkArgs a) {
-  __shared__ __align__(16) float kstage[BF16 ? 8 * 128 : 4];
+  __shared__ __align__(16) float kstage[KV != 0 ? 8 * 128 : 4];
   issue_prefetch(a.pf);
   pdl_launch_dependents();
   pdl_wait();
@@ -247,7 +247,24 @@ static __global__ void __launch_bounds__(256) k_qk_norm_rope_append(const QkArgs
     const float* k = a.k + ((size_t)tok * a.n_kv_heads + kvh) * hd;
     const float* v = a.v + ((size_t)tok * a.n_kv_heads + kvh) * hd;
     float kf[4], vf[4];  // the values the cache now holds (for the f16 image)
-    if constexpr (BF16) {
+    if constexpr (KV == 2) {
+      float* ks = kstage + warp * 128;
+      if (table)
+        norm_rope_warp_cs(k, a.k_norm, a.eps, cs, a.neox, ks, lane);
+      else
+        norm_rope_warp(k, a.k_norm, a.eps, pos, a.inv_freq, a.neox, ks, lane);
+      __syncwarp();
+      uint8_t* kc = static_cast<uint8_t*>(a.kcache) + row;
+      uint8_t* vc = static_cast<uint8_t*>(a.vcache) + row;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const uint8_t kb = fp8_bits(ks[lane + 32 * q]), vb = fp8_bits(v[lane + 32 * q]);
+        kc[lane + 32 * q] = kb;
+        vc[lane + 32 * q] = vb;
+        kf[q] = fp8_widen(kb);
+        vf[q] = fp8_widen(vb);
+      }
+    } else if constexpr (KV == 1) {
       float* ks = kstage + warp * 128;
       if (table)
         norm_rope_warp_cs(k, a.k_norm, a.eps, cs, a.neox, ks, lane);

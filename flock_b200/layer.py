@@ -44,9 +44,10 @@ class LayerConfig:
     # multi-token steps: "exact" (the reference's f32 order, bit-comparable) or
     # "tensor" (tcgen05 tensor cores, f16 operands, 1e-2 relative tolerance)
     prefill: str = "exact"
-    # KV cache element type: "f32" (the reference's) or "bf16" (half the bytes
-    # per key; appends round to nearest even; needs attention="fast" and
-    # prefill="tensor")
+    # KV cache element type: "f32" (the reference's), "bf16" (half the bytes
+    # per key) or "fp8" (e4m3, a quarter; magnitudes past 448 saturate);
+    # appends round to nearest even; both need attention="fast" and
+    # prefill="tensor"
     kv: str = "f32"
     # one-token matvecs: "exact" (cpuMatmulQ8F32(coop(64))'s order, bit-identical)
     # or "fast" (the decode LM head on the int8 tensor cores, reassociated,
@@ -54,8 +55,8 @@ class LayerConfig:
     matvec: str = "exact"
 
     def to_c(self) -> _abi.LayerConfigC:
-        if self.kv not in ("f32", "bf16"):
-            raise ValueError(f"kv must be 'f32' or 'bf16', not {self.kv!r}")
+        if self.kv not in ("f32", "bf16", "fp8"):
+            raise ValueError(f"kv must be 'f32', 'bf16' or 'fp8', not {self.kv!r}")
         if self.matvec not in ("exact", "fast"):
             raise ValueError(f"matvec must be 'exact' or 'fast', not {self.matvec!r}")
         return _abi.LayerConfigC(
@@ -64,7 +65,7 @@ class LayerConfig:
             _abi.FLOCK_ROPE_NEOX if self.rope_pairing == "neox" else _abi.FLOCK_ROPE_NORM,
             _abi.FLOCK_ATTN_EXACT if self.attention == "exact" else _abi.FLOCK_ATTN_FAST,
             _abi.FLOCK_PREFILL_TENSOR if self.prefill == "tensor" else _abi.FLOCK_PREFILL_EXACT,
-            _abi.FLOCK_KV_BF16 if self.kv == "bf16" else _abi.FLOCK_KV_F32,
+            {"bf16": _abi.FLOCK_KV_BF16, "fp8": _abi.FLOCK_KV_FP8}.get(self.kv, _abi.FLOCK_KV_F32),
             _abi.FLOCK_MATVEC_FAST if self.matvec == "fast" else _abi.FLOCK_MATVEC_EXACT)
 
     def with_(self, **kw) -> "LayerConfig":

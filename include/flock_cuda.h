@@ -65,6 +65,11 @@ extern "C" {
                            value is rounded to nearest even once and every attention
                            read widens it exactly.  Needs FLOCK_ATTN_FAST and
                            FLOCK_PREFILL_TENSOR (the exact kernels are f32 only). */
+#define FLOCK_KV_FP8 2  /* fp8 KV cache (OCP E4M3FN): a quarter of the bytes per key;
+                           each appended key and value is rounded to the nearest e4m3
+                           (ties to even, magnitudes past 448 saturate to 448, no
+                           scale) once and every read widens it exactly.  Needs
+                           FLOCK_ATTN_FAST and FLOCK_PREFILL_TENSOR. */
 
 #define FLOCK_MATVEC_EXACT 0 /* one-token matvecs in cpuMatmulQ8F32(coop(64))'s f32 order
                                 (lib.ts:213), bit-identical */
@@ -95,7 +100,7 @@ typedef struct flock_layer_config {
   int32_t rope_pairing; /* FLOCK_ROPE_NEOX | FLOCK_ROPE_NORM */
   int32_t attention;    /* FLOCK_ATTN_EXACT | FLOCK_ATTN_FAST */
   int32_t prefill;      /* FLOCK_PREFILL_EXACT | FLOCK_PREFILL_TENSOR (multi-token steps) */
-  int32_t kv_dtype;     /* FLOCK_KV_F32 (0, the default) | FLOCK_KV_BF16 */
+  int32_t kv_dtype;     /* FLOCK_KV_F32 (0, the default) | FLOCK_KV_BF16 | FLOCK_KV_FP8 */
   int32_t matvec;       /* FLOCK_MATVEC_EXACT (0, the default) | FLOCK_MATVEC_FAST */
 } flock_layer_config;
 

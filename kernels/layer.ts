@@ -15,6 +15,7 @@ import {
   FLOCK_ATTN_FAST,
   FLOCK_E_UNSUPPORTED,
   FLOCK_KV_BF16,
+  FLOCK_KV_FP8,
   FLOCK_MATVEC_EXACT,
   FLOCK_MATVEC_FAST,
   FLOCK_KV_F32,
@@ -68,7 +69,7 @@ export type LayerBuffers = Record<string, GpuTensor>;
  * defaulting to the reference's arithmetic): `attention` "exact" keeps
  * attnRef's order, "fast" is the split-K flash-decode; `prefill` "tensor"
  * runs multi-token steps on the tcgen05 tensor cores; `kvDtype` "bf16"
- * halves the cache; `matvec` "fast" runs the decode LM head on the int8
+ * halves the cache, "fp8" (e4m3) quarters it; `matvec` "fast" runs the decode LM head on the int8
  * tensor cores (reassociated, 1e-3 relative).
  */
 export interface LayerConfig {
@@ -84,7 +85,7 @@ export interface LayerConfig {
   ropePairing: RopePairing;
   attention?: "exact" | "fast";
   prefill?: "exact" | "tensor";
-  kvDtype?: "f32" | "bf16";
+  kvDtype?: "f32" | "bf16" | "fp8";
   matvec?: "exact" | "fast";
 }
 
@@ -134,7 +135,7 @@ export function configBytes(cfg: LayerConfig): Uint8Array {
     rope_pairing: cfg.ropePairing === "norm" ? FLOCK_ROPE_NORM : FLOCK_ROPE_NEOX,
     attention: cfg.attention === "fast" ? FLOCK_ATTN_FAST : FLOCK_ATTN_EXACT,
     prefill: cfg.prefill === "tensor" ? FLOCK_PREFILL_TENSOR : FLOCK_PREFILL_EXACT,
-    kv_dtype: cfg.kvDtype === "bf16" ? FLOCK_KV_BF16 : FLOCK_KV_F32,
+    kv_dtype: cfg.kvDtype === "bf16" ? FLOCK_KV_BF16 : cfg.kvDtype === "fp8" ? FLOCK_KV_FP8 : FLOCK_KV_F32,
     matvec: cfg.matvec === "fast" ? FLOCK_MATVEC_FAST : FLOCK_MATVEC_EXACT,
   });
 }

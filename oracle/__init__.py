@@ -92,6 +92,8 @@ def lib():
             "fo_cache_fill": (_int, [ctypes.c_void_p, _f32p, _f32p, _int]),
             "fo_cache_set_bf16": (None, [ctypes.c_void_p, _int]),
             "fo_bf16_round": (ctypes.c_float, [ctypes.c_float]),
+            "fo_cache_set_fp8": (None, [ctypes.c_void_p, _int]),
+            "fo_fp8_round": (ctypes.c_float, [ctypes.c_float]),
             "fo_layer_forward": (_int, [_f32p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                         _f32p]),
             "fo_layer_prefill": (_int, [_f32p, _int, ctypes.c_void_p, ctypes.c_void_p,
@@ -319,12 +321,13 @@ class RefLayer:
     tp > 1: o_proj and down become tp-shard input-split matvecs
     (shard_ref.ts:353), the arithmetic of a tensor-parallel layer.
     kv="bf16": every appended key/value is rounded to bf16 (nearest even), the
-    cache a FLOCK_KV_BF16 layer keeps; attention then reads the rounded values."""
+    cache a FLOCK_KV_BF16 layer keeps; kv="fp8": to e4m3 (fo_fp8_round, the
+    FLOCK_KV_FP8 cache); attention then reads the rounded values."""
 
     def __init__(self, weights: dict, cfg: dict, max_keys: int = 4096, tp: int = 1,
                  kv: str = "f32"):
-        if kv not in ("f32", "bf16"):
-            raise ValueError(f"kv must be 'f32' or 'bf16', not {kv!r}")
+        if kv not in ("f32", "bf16", "fp8"):
+            raise ValueError(f"kv must be 'f32', 'bf16' or 'fp8', not {kv!r}")
         self.tp = int(tp)
         self._keep = {}
         w = _W()
@@ -344,6 +347,8 @@ class RefLayer:
         self.kvw = cfg["n_kv_heads"] * cfg["head_dim"]
         self._cache = lib().fo_cache_new(max_keys, self.kvw)
         lib().fo_cache_set_bf16(self._cache, 1 if kv == "bf16" else 0)
+        if kv == "fp8":
+            lib().fo_cache_set_fp8(self._cache, 1)
 
     def __del__(self):
         try:

@@ -515,6 +515,19 @@ float fo_bf16_round(float x) {
   memcpy(&x, &w, 4);
   return x;
 }
+void fo_cache_set_fp8(fo_cache* c, int on) { c->bf16 = on ? 2 : 0; }
+float fo_fp8_round(float x) {
+  if (isnan(x)) return x;
+  const float a = fabsf(x);
+  if (a >= 448.0f) return copysignf(448.0f, x);
+  int e2 = 0;
+  frexpf(a, &e2); /* a = f * 2^e2, f in [0.5, 1): a in [2^(e2-1), 2^e2) */
+  int E = e2 - 1;
+  if (E < -6) E = -6; /* below the smallest normal, 2^-6: subnormal steps of 2^-9 */
+  const float step = ldexpf(1.0f, E - 3); /* three mantissa bits */
+  /* a / step is exact (a power-of-two scale); rintf rounds ties to even */
+  return copysignf(rintf(a / step) * step, x);
+}
 int fo_cache_fill(fo_cache* c, const float* k, const float* v, int n) {
   if (c->n + n > c->cap) return -1;
   float* kd = c->k + (int64_t)c->n * c->kvw;
@@ -522,10 +535,15 @@ int fo_cache_fill(fo_cache* c, const float* k, const float* v, int n) {
   const size_t count = (size_t)n * c->kvw;
   memcpy(kd, k, sizeof(float) * count);
   memcpy(vd, v, sizeof(float) * count);
-  if (c->bf16)
+  if (c->bf16 == 1)
     for (size_t i = 0; i < count; i++) {
       kd[i] = fo_bf16_round(kd[i]);
       vd[i] = fo_bf16_round(vd[i]);
+    }
+  else if (c->bf16 == 2)
+    for (size_t i = 0; i < count; i++) {
+      kd[i] = fo_fp8_round(kd[i]);
+      vd[i] = fo_fp8_round(vd[i]);
     }
   c->n += n;
   return 0;

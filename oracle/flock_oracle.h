@@ -115,7 +115,8 @@ typedef struct fo_cache {
   int n;   /* keys held */
   int cap; /* capacity in keys */
   int kvw; /* nKV*hd */
-  int bf16; /* 1: every key/value is rounded to bf16 (nearest even) as it is stored */
+  int bf16; /* 1: every key/value is rounded to bf16 (nearest even) as it is stored;
+               2: to e4m3 (FLOCK_KV_FP8) */
 } fo_cache;
 
 fo_cache* fo_cache_new(int cap, int kvw);
@@ -129,6 +130,13 @@ const float* fo_cache_v(const fo_cache* c);
 void fo_cache_set_bf16(fo_cache* c, int on);
 /* f32 -> the nearest bf16 value (ties to even), as an f32. */
 float fo_bf16_round(float x);
+/* An e4m3 KV cache (FLOCK_KV_FP8): from now on fo_cache_fill stores each
+ * value rounded with fo_fp8_round. */
+void fo_cache_set_fp8(fo_cache* c, int on);
+/* f32 -> the nearest OCP E4M3FN value (ties to even; magnitudes at or past 448
+ * become 448 with the sign, NaN stays NaN), as an f32: the rounding of the
+ * device's cvt.rn.satfinite.e4m3x2.f32. */
+float fo_fp8_round(float x);
 /* Preload n keys (e.g. a synthetic cache); returns 0 or -1 if over capacity. */
 int fo_cache_fill(fo_cache* c, const float* k, const float* v, int n);
 

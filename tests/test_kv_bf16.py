@@ -120,7 +120,7 @@ def test_layer_config_kv_switch():
     c = QWEN3_06B.with_(attention="fast", prefill="tensor", kv="bf16").to_c()
     assert c.kv_dtype == _abi.FLOCK_KV_BF16 and c.prefill == _abi.FLOCK_PREFILL_TENSOR
     with pytest.raises(ValueError):
-        QWEN3_06B.with_(kv="fp8").to_c()
+        QWEN3_06B.with_(kv="fp16").to_c()
     with pytest.raises(ValueError):
         import oracle as o
-        o.RefLayer({}, {}, 4, kv="fp8")
+        o.RefLayer({}, {}, 4, kv="fp16")
