@@ -79,8 +79,23 @@ int kernel_setup(const void* func, int max_dyn_smem, int carveout) {
 }
 
 
+// SwiGLU (gate/up) rows of one block per lane run three CTAs per SM: its
+// 2 x ffn rows at two per warp step are more row groups than two CTAs per
+// SM have warps, and a warp's second group loads its weights only after the
+// dependency wait; at three (x pairs read per step from shared memory, so
+// the registers fit) every warp has one group (3072 rows: 665 against 678
+// us per 0.6B-shape token)
+constexpr int GEMV_SWIGLU_CTAS_PER_SM = 3;
+static bool gemv_swiglu3(int EPI, int K, int LA) { return EPI == EPI_SWIGLU && K <= 1024 && LA == 1; }
+
 template <int QT, int R, int EPI, int MX, int LA = 1>
 static cudaError_t gemv_go(flock_dev* d, const GemvArgs& a, int ctas, bool pdl) {
+  if (gemv_swiglu3(EPI, a.K, LA)) {
+    auto k3 = k_gemv<QT, R, EPI, MX, LA, GEMV_SWIGLU_CTAS_PER_SM, 2>;
+    const size_t smem3 = gemv_smem_bytes(a.K, a.norm_gain != nullptr);
+    if (kernel_setup((const void*)k3, 200 * 1024)) return cudaErrorInvalidValue;
+    return launch_ex(d->stream, k3, dim3(ctas, a.n_tokens), dim3(GEMV_THREADS), smem3, pdl, a);
+  }
   // blocks fold on f32x2 pairs (x staged in the packed-pair layout): held in
   // registers for one-block rows, read per step otherwise; two rows with two
   // steps in flight keep the scalar fold (the pairs would spill)
@@ -125,7 +140,11 @@ int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl) {
     groups = 0;
     for (int s = 0; s < a.nseg; s++) groups += (a.seg[s].rows + R - 1) / R;
   }
-  const int ctas = gemv_grid(d, groups);
+  int ctas = gemv_grid(d, groups);
+  if (gemv_swiglu3(EPI, a.K, MX == 1 ? 1 : 2)) {
+    ctas = (groups + GEMV_WARPS - 1) / GEMV_WARPS;
+    if (ctas > GEMV_SWIGLU_CTAS_PER_SM * d->sm_count) ctas = GEMV_SWIGLU_CTAS_PER_SM * d->sm_count;
+  }
   cudaError_t e = cudaErrorInvalidValue;
 // long rows (two or more column blocks per lane) keep one x block in
 // registers and two steps of weights in flight; short rows keep the x
