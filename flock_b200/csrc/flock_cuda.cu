@@ -140,6 +140,24 @@ int launch_gemv(flock_dev* d, int QT, int EPI, const GemvArgs& a, bool pdl) {
     groups = 0;
     for (int s = 0; s < a.nseg; s++) groups += (a.seg[s].rows + R - 1) / R;
   }
+  // rows of 2-3 column blocks per lane in small matrices (the 0.6B o_proj,
+  // down): one row per warp pair (k_gemv_pair, the same arithmetic)
+  if (QT == QT_Q8 && (EPI == EPI_STORE || EPI == EPI_RESIDUAL) && a.nseg == 1 && !big &&
+      (M == 2 || M == 3) && a.K <= 12288) {
+    const int pctas = (rows + GEMV_PAIRS - 1) / GEMV_PAIRS;
+    if (pctas <= 2 * d->sm_count) {
+      auto k = EPI == EPI_STORE ? k_gemv_pair<QT_Q8, EPI_STORE> : k_gemv_pair<QT_Q8, EPI_RESIDUAL>;
+      const size_t smem = gemv_pair_smem_bytes(a.K, a.norm_gain != nullptr);
+      if (kernel_setup((const void*)k, 200 * 1024)) return FLOCK_E_CUDA;
+      cudaError_t pe = launch_ex(d->stream, k, dim3(pctas, a.n_tokens), dim3(GEMV_THREADS), smem,
+                                 pdl, a);
+      if (pe != cudaSuccess) {
+        set_error("matvec launch failed: %s", cudaGetErrorString(pe));
+        return FLOCK_E_CUDA;
+      }
+      return FLOCK_OK;
+    }
+  }
   int ctas = gemv_grid(d, groups);
   if (gemv_swiglu3(EPI, a.K, MX == 1 ? 1 : 2)) {
     ctas = (groups + GEMV_WARPS - 1) / GEMV_WARPS;

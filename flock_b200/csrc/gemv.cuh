@@ -674,4 +674,73 @@ inline size_t gemv_smem_bytes(int K, bool norm) {
   return (size_t)(K / 32 * XPAD + (norm ? K : 0) + 136 + GEMV_WARPS * 2) * 4 + 16;
 }
 
+// Rows of two or three column blocks per lane (K = 2048, 3072: the 0.6B
+// o_proj and down), one row per warp PAIR: warp 2p folds the row's even
+// column steps (logical lanes 0..31 of the coop(64) order), warp 2p + 1 its
+// odd steps (logical lanes 32..63), each into its own accumulator in step
+// order as gemv_run does; the odd warp hands its 32 partials over through
+// shared memory and the even warp adds them lane by lane -- the tree's
+// first level, fadd(accA, accB) -- then finishes the tree and the epilogue.
+// The same arithmetic as gemv_run; every weight load of a warp goes out
+// before the dependency wait, and each warp folds half the row.
+constexpr int GEMV_PAIRS = GEMV_WARPS / 2;
+template <int QT, int EPI>
+__global__ void __launch_bounds__(GEMV_THREADS, 2) k_gemv_pair(const GemvArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  const bool norm = a.norm_gain != nullptr;
+  const int kpad = a.K / 32 * XPAD;
+  float* xs = smem;
+  float* gs = smem + kpad;
+  float* red = gs + (norm ? a.K : 0);
+  float* pbuf = red + 136;  // [GEMV_PAIRS][32] the odd warps' partials
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int half = warp & 1;
+  const int row = blockIdx.x * GEMV_PAIRS + (warp >> 1);
+  const int tok = blockIdx.y;
+  const GemvSeg& sg = a.seg[0];
+  const int nb = a.K / 32;
+  const int M = (nb + 31) / 32;  // 2 or 3
+  const bool ok = row < sg.rows;
+  // this warp's steps m = half, half + 2 (< M): weights only, before the wait
+  BlockW<QT> w[2];
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    const int m = half + 2 * i, b = lane + 32 * m;
+    if (ok && m < M && b < nb) load_block<QT>(w[i], sg, row, b, a.K);
+  }
+  issue_prefetch(a.pf);
+  pdl_launch_dependents();
+  pdl_wait();
+  if (a.ctl && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+    a.ctl[0] += a.ctl[1];
+    a.ctl[1] = a.ctl_n;
+  }
+  float resv = 0.0f;
+  if (EPI == EPI_RESIDUAL && ok && half == 0 && lane == 0)
+    resv = a.res[(size_t)tok * a.res_stride + row];
+  gemv_stage_x<0>(a, tok, xs, gs, red);
+  __syncthreads();
+  const float4* xs4 = reinterpret_cast<const float4*>(xs);
+  float acc = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    const int m = half + 2 * i, b = lane + 32 * m;
+    if (ok && m < M && b < nb) acc = fold_block<QT>(w[i], xs4 + b * (XPAD / 4), acc);
+  }
+  if (half == 1) pbuf[(warp >> 1) * 32 + lane] = acc;
+  __syncthreads();
+  if (half == 0 && ok) {
+    const float y = warp_tree_sum(fadd(acc, pbuf[(warp >> 1) * 32 + lane]));
+    if (lane == 0) {
+      float v = y;
+      if (EPI == EPI_RESIDUAL) v = fadd(resv, v);
+      sg.out[(size_t)tok * sg.out_stride + row] = v;
+    }
+  }
+}
+
+inline size_t gemv_pair_smem_bytes(int K, bool norm) {
+  return (size_t)(K / 32 * XPAD + (norm ? K : 0) + 136 + GEMV_PAIRS * 32) * 4 + 16;
+}
+
 }  // namespace flock
