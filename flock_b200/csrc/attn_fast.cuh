@@ -14,7 +14,7 @@
 //    sum_s l_s e^(m_s-M), both sums in split order (af_combine16); each
 //    thread combines one output element with all its splits' loads in
 //    flight;
-//  * a step over n keys uses ceil(n / 16) splits, at most
+//  * a step over n keys uses ceil(n / 32) splits, at most
 //    attn_max_splits(SMs, kv heads, cache capacity): 16 for caches of up to
 //    2048 keys, caches over 2048 keys run up to 3 CTAs per SM;
 //  * scores: one thread per (key, query head), a 128-long dot product over
@@ -96,9 +96,10 @@ __host__ __device__ inline int attn_max_splits(int sm_count, int n_kv_heads, int
 
 // Splits a step over n_keys keys uses: one per ATTN_SPLIT_KEYS keys, at most
 // max_splits.  Both decode engines use this rule, so their partials and
-// results are identical.
+// results are identical.  32 keys per split measured 1-5 us per 0.6B token
+// faster than 16 (8 slower) with the split's tile staged before the wait.
 #ifndef FLOCK_ATTN_SPLIT_KEYS
-#define FLOCK_ATTN_SPLIT_KEYS 16
+#define FLOCK_ATTN_SPLIT_KEYS 32
 #endif
 constexpr int ATTN_SPLIT_KEYS = FLOCK_ATTN_SPLIT_KEYS;
 FLOCK_DEV int attn_splits_for(int n_keys, int max_splits) {
