@@ -97,6 +97,23 @@ def test_persistent_long_cache_splits(dev, small):
     assert np.array_equal(_bits(la), _bits(lb))
 
 
+def test_split_counts_bit_identical(dev, small):
+    """Teacher-forced one-token steps from position 40 to 330 cross every
+    decode-attention split count from 2 to 11 (one split per 32 keys; the
+    first step right after a 40-token prompt, whose position the first layer
+    advances by 40): every step's logits must be bit-identical between the
+    kernel graph and the persistent kernel, which stage, split and combine
+    the attention in their own launches."""
+    a, b = _pair(dev, small)
+    prompt = synth.uniform_ids(11, "ac-prompt", 40, 4096).tolist()
+    forced = synth.uniform_ids(11, "ac-forced", 290, 4096).tolist()
+    assert a.step(prompt) == b.step(prompt)
+    for i, t in enumerate(forced):
+        la, lb = a.logits([t]), b.logits([t])
+        assert np.array_equal(_bits(la), _bits(lb)), f"position {40 + i}"
+    assert a.pos == b.pos == 330
+
+
 def test_persistent_decode_device_history(dev, small):
     a, b = _pair(dev, small)
     for M in (a, b):
