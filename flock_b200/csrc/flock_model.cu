@@ -31,7 +31,10 @@ struct flock_model {
   Workspace ws;
   DBuf ctl, ids, hist, logits, normed, am_val, am_idx, am_count, am_best_val;
   int pos = 0;  // host mirror of ctl[0] after the last step
-  cudaGraphExec_t decode_graph = nullptr;
+  // the kernel graph of one decode step, and of DECODE_GRAPH_TOKENS steps
+  // in a row (device-fed decode runs: no graph boundary, so each step's
+  // first launch overlaps the previous step's last one)
+  cudaGraphExec_t decode_graph = nullptr, decode_graph_run = nullptr;
   // persistent decode kernel
   int decode_mode = FLOCK_DECODE_KERNELS;
   bool mk_ok = false;       // shape fits the persistent kernel
@@ -532,15 +535,22 @@ int check_device_errors(flock_model* m) {
   return FLOCK_OK;
 }
 
-int capture_decode(flock_model* m) {
-  if (m->decode_graph) return FLOCK_OK;
+constexpr int DECODE_GRAPH_TOKENS = 8;
+
+// Captures `tokens` decode steps (embed -> layers -> head -> record each)
+// into one executable graph.
+int capture_decode_steps(flock_model* m, int tokens, cudaGraphExec_t* out) {
+  if (*out) return FLOCK_OK;
   cudaStream_t st = m->dev->stream;
   cudaGraph_t g = nullptr;
   FLOCK_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-  int rc = enqueue_embed(m, 1);
-  if (!rc) rc = enqueue_layers(m, 1);
-  if (!rc) rc = enqueue_head(m, 0);
-  if (!rc) rc = enqueue_record(m);
+  int rc = FLOCK_OK;
+  for (int i = 0; i < tokens && !rc; i++) {
+    rc = enqueue_embed(m, 1);
+    if (!rc) rc = enqueue_layers(m, 1);
+    if (!rc) rc = enqueue_head(m, 0);
+    if (!rc) rc = enqueue_record(m);
+  }
   cudaError_t e = cudaStreamEndCapture(st, &g);
   if (rc) {
     if (g) cudaGraphDestroy(g);
@@ -550,14 +560,27 @@ int capture_decode(flock_model* m) {
     set_error("decode graph capture failed: %s", cudaGetErrorString(e));
     return FLOCK_E_CUDA;
   }
-  e = cudaGraphInstantiate(&m->decode_graph, g, 0);
+  e = cudaGraphInstantiate(out, g, 0);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) {
-    m->decode_graph = nullptr;
+    *out = nullptr;
     set_error("decode graph instantiate failed: %s", cudaGetErrorString(e));
     return FLOCK_E_CUDA;
   }
   return FLOCK_OK;
+}
+
+int capture_decode(flock_model* m) { return capture_decode_steps(m, 1, &m->decode_graph); }
+
+// Drops the captured decode graphs (after the stream drains): the launches
+// they hold change with the decode mode or the tensor-parallel exchange.
+void drop_decode_graphs(flock_model* m) {
+  if (!m->decode_graph && !m->decode_graph_run) return;
+  cudaStreamSynchronize(m->dev->stream);
+  if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
+  if (m->decode_graph_run) cudaGraphExecDestroy(m->decode_graph_run);
+  if (m->decode_graph_run) cudaGraphExecDestroy(m->decode_graph_run);
+  m->decode_graph = m->decode_graph_run = nullptr;
 }
 
 // One single-token decode step on the stream: the persistent kernel (a
@@ -581,6 +604,24 @@ int launch_decode(flock_model* m) {
   }
   FLOCK_TRY(capture_decode(m));
   FLOCK_CK(cudaGraphLaunch(m->decode_graph, m->dev->stream));
+  return FLOCK_OK;
+}
+
+// n device-fed decode steps: the kernel graph of a one-GPU model runs them
+// DECODE_GRAPH_TOKENS to a graph launch (the same kernels in the same order
+// as n single-step launches); the other engines, and tensor-parallel ranks
+// (whose graphs hold collectives), one step at a time.
+int launch_decode_run(flock_model* m, int n) {
+  const bool graph = !m->tp && !(m->decode_mode == FLOCK_DECODE_STREAM && m->st.ok) &&
+                     !(m->decode_mode == FLOCK_DECODE_PERSISTENT && m->mk_ok) &&
+                     m->decode_mode != FLOCK_DECODE_EAGER;
+  int i = 0;
+  if (graph && n >= DECODE_GRAPH_TOKENS) {
+    FLOCK_TRY(capture_decode_steps(m, DECODE_GRAPH_TOKENS, &m->decode_graph_run));
+    for (; i + DECODE_GRAPH_TOKENS <= n; i += DECODE_GRAPH_TOKENS)
+      FLOCK_CK(cudaGraphLaunch(m->decode_graph_run, m->dev->stream));
+  }
+  for (; i < n; i++) FLOCK_TRY(launch_decode(m));
   return FLOCK_OK;
 }
 
@@ -723,11 +764,7 @@ int flock_model_set_decode_mode(flock_model* m, int mode) {
   if (!m || (mode != FLOCK_DECODE_KERNELS && mode != FLOCK_DECODE_PERSISTENT &&
              mode != FLOCK_DECODE_EAGER && mode != FLOCK_DECODE_STREAM))
     return FLOCK_E_ARG;
-  if (mode != m->decode_mode && m->decode_graph) {
-    cudaStreamSynchronize(m->dev->stream);
-    cudaGraphExecDestroy(m->decode_graph);
-    m->decode_graph = nullptr;
-  }
+  if (mode != m->decode_mode) drop_decode_graphs(m);
   m->decode_mode = mode;
   return FLOCK_OK;
 }
@@ -780,11 +817,7 @@ int flock_model_set_tp_exchange(flock_model* m, int mode) {
     set_error("the ranks could not map each other's memory; decode exchanges stay on NCCL");
     return FLOCK_E_UNSUPPORTED;
   }
-  if (m->decode_graph) {
-    cudaStreamSynchronize(m->dev->stream);
-    cudaGraphExecDestroy(m->decode_graph);
-    m->decode_graph = nullptr;
-  }
+  drop_decode_graphs(m);
   m->tp_exchange = mode;
   for (auto* L : m->layers) L->xchg = mode == FLOCK_TP_PEER ? m->xchg : nullptr;
   return FLOCK_OK;
@@ -868,7 +901,7 @@ int flock_model_decode_device(flock_model* m, int n_steps, int32_t* out_ids) {
   FLOCK_TRY(check_room(m, n_steps));
   FLOCK_CK(cudaSetDevice(m->dev->ordinal));
   const int start = m->pos;
-  for (int i = 0; i < n_steps; i++) FLOCK_TRY(launch_decode(m));
+  FLOCK_TRY(launch_decode_run(m, n_steps));
   m->pos += n_steps;
   for (auto* L : m->layers) L->n_keys = m->pos;
   if (n_steps)
