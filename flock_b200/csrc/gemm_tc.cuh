@@ -576,6 +576,18 @@ inline size_t act_image_smem_bytes(int K) {
 static __global__ void __launch_bounds__(ACT_IMG_THREADS) k_act_image(const ActImgArgs a) {
   extern __shared__ __align__(16) float xr[];  // [K] row, then scratch
   pdl_launch_dependents();
+  // the gains are weights (no kernel writes them): this thread's float4s of
+  // them, for rows of up to 4096, load before the dependency wait
+  constexpr int GREG = 8;
+  float4 gr[GREG];
+  const bool greg = a.gain != nullptr && a.K / 4 <= GREG * ACT_IMG_THREADS;
+  if (greg) {
+#pragma unroll
+    for (int j = 0; j < GREG; j++) {
+      const int i = (int)threadIdx.x + j * ACT_IMG_THREADS;
+      if (i < a.K / 4) gr[j] = __ldg(reinterpret_cast<const float4*>(a.gain) + i);
+    }
+  }
   pdl_wait();
   float* red = xr + a.K;                       // [128]
   float* w = red + ACT_IMG_THREADS;            // [ATC_MAX_SPLITS_IMG][32] merge weights
@@ -660,23 +672,36 @@ static __global__ void __launch_bounds__(ACT_IMG_THREADS) k_act_image(const ActI
   float scale = 1.0f;
   if (a.gain) {
     // ops_ref.ts:20: partial t over i = t, t+128, ... in order, then the tree
+    // the pairwise tree: levels 64 and 32 in one step across the warps,
+    // (r[l] + r[l+64]) + (r[l+32] + r[l+96]), the last five in warp 0
     float p = 0.0f;
     for (int i = t; i < a.K; i += ACT_IMG_THREADS) p = ffma(xr[i], xr[i], p);
     red[t] = p;
     __syncthreads();
-    for (int s = ACT_IMG_THREADS / 2; s > 0; s >>= 1) {
-      if (t < s) red[t] = fadd(red[t], red[t + s]);
-      __syncthreads();
+    if (t < 32) {
+      float v = fadd(fadd(red[t], red[t + 64]), fadd(red[t + 32], red[t + 96]));
+      v = warp_tree_sum(v);
+      if (t == 0) red[ACT_IMG_THREADS] = rsqrt_f64r(fadd(fdiv(v, (float)a.K), a.eps));
     }
-    scale = rsqrt_f64r(fadd(fdiv(red[0], (float)a.K), a.eps));
+    __syncthreads();
+    scale = red[ACT_IMG_THREADS];
     __syncthreads();  // red is reused for the maxima
   }
   // the row's final values (in place) and their largest magnitude
   float mx = 0.0f;
-  for (int i = t; i < K4; i += ACT_IMG_THREADS) {
+#pragma unroll 1
+  for (int i = t, j = 0; i < K4; i += ACT_IMG_THREADS, j++) {
     float4 x = x4[i];
     if (a.gain) {
-      const float4 g = __ldg(reinterpret_cast<const float4*>(a.gain) + i);
+      float4 g;
+      if (greg) {
+        g = gr[0];
+#pragma unroll
+        for (int q = 1; q < GREG; q++)
+          if (j == q) g = gr[q];
+      } else {
+        g = __ldg(reinterpret_cast<const float4*>(a.gain) + i);
+      }
       x = make_float4(fmul(fmul(x.x, scale), g.x), fmul(fmul(x.y, scale), g.y),
                       fmul(fmul(x.z, scale), g.z), fmul(fmul(x.w, scale), g.w));
       x4[i] = x;
