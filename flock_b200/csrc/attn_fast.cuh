@@ -536,10 +536,32 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
   const bool pre = guess >= 0 && guess < a.max_keys && s < attn_splits_for(guess + 1, a.splits);
   if (pre) af_stage_static(a, g, s, guess, dsm);
   pdl_wait();
+  // the raw projection's addresses do not depend on the position: with the
+  // fused norm its loads go out together with the position's (one round
+  // trip), and are staged as af_stage_step stages them once the position
+  // says this split has keys
+  const bool fused = a.q_norm != nullptr;
+  const int G = a.n_heads / a.n_kv_heads, t = threadIdx.x;
+  float4 qr = make_float4(0.f, 0.f, 0.f, 0.f), kr = qr, vr = qr;
+  if (fused) {
+    if (t < G * 32) qr = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)g * G * 128) + t);
+    if (t < 32) {
+      kr = __ldcg(reinterpret_cast<const float4*>(a.k + (size_t)g * 128) + t);
+      vr = __ldcg(reinterpret_cast<const float4*>(a.v + (size_t)g * 128) + t);
+    }
+  }
   const int pos = __ldcg(a.ctl);
   const AfRange r = af_range(a, s, pos);
   if (s < r.splits) {
-    af_stage_step(a, g, pos, dsm);
+    if (fused) {
+      if (t < G * 32) reinterpret_cast<float4*>(dsm + AF_QRAW)[t] = qr;
+      if (t < 32) {
+        reinterpret_cast<float4*>(dsm + AF_KRAW)[t] = kr;
+        reinterpret_cast<float4*>(dsm + AF_VRAW)[t] = vr;
+      }
+    } else {
+      af_stage_step(a, g, pos, dsm);
+    }
     if (!pre || pos != guess) af_stage_static(a, g, s, pos, dsm);
   }
   attn_fast_run(a, g, s, pos, dsm, &last, BlockSync{});
