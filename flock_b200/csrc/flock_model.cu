@@ -35,6 +35,9 @@ struct flock_model {
   // in a row (device-fed decode runs: no graph boundary, so each step's
   // first launch overlaps the previous step's last one)
   cudaGraphExec_t decode_graph = nullptr, decode_graph_run = nullptr;
+  // pinned host slots of a one-token step: [0] the id going in, [1] the id
+  // coming back (both copies asynchronous on the model's stream)
+  int32_t* h_io = nullptr;
   // persistent decode kernel
   int decode_mode = FLOCK_DECODE_KERNELS;
   bool mk_ok = false;       // shape fits the persistent kernel
@@ -579,7 +582,6 @@ void drop_decode_graphs(flock_model* m) {
   cudaStreamSynchronize(m->dev->stream);
   if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
   if (m->decode_graph_run) cudaGraphExecDestroy(m->decode_graph_run);
-  if (m->decode_graph_run) cudaGraphExecDestroy(m->decode_graph_run);
   m->decode_graph = m->decode_graph_run = nullptr;
 }
 
@@ -691,6 +693,11 @@ int model_build(flock_dev* dev, const flock_layer_config* cfg, int vocab, int n_
       (rc = m->am_count.alloc(16)) || (rc = m->am_best_val.alloc(16)))
     return fail(rc);
   if (cudaMemset(m->am_count.p, 0, 16) != cudaSuccess) return fail(FLOCK_E_CUDA);
+  if (cudaHostAlloc((void**)&m->h_io, 16, cudaHostAllocDefault) != cudaSuccess) {
+    m->h_io = nullptr;
+    set_error("pinned host slot for the step ids could not be allocated");
+    return fail(FLOCK_E_CUDA);
+  }
   if (m->head && (m->head->cols != cfg->hidden || m->head->rows != head_rows)) {
     set_error("lm-head%s is %lldx%lld, want %lldx%d", tp ? " slice" : "",
               (long long)m->head->rows, (long long)m->head->cols, (long long)head_rows,
@@ -844,6 +851,8 @@ int flock_model_free(flock_model* m) {
   cudaSetDevice(d->ordinal);
   cudaStreamSynchronize(d->stream);
   if (m->decode_graph) cudaGraphExecDestroy(m->decode_graph);
+  if (m->decode_graph_run) cudaGraphExecDestroy(m->decode_graph_run);
+  if (m->h_io) cudaFreeHost(m->h_io);
   for (auto* L : m->layers) flock_layer_free(L);
   peer_xchg_free(m->xchg);  // a collective: every rank frees its model
   delete m;
@@ -878,16 +887,27 @@ int flock_model_step(flock_model* m, const int32_t* ids, int n, int32_t* next_id
   FLOCK_TRY(need_head(m));
   FLOCK_CK(cudaSetDevice(m->dev->ordinal));
   if (n == 1 && m->held > 0) {
+    // one decode step: the id goes up and the next comes back through the
+    // pinned slots (the previous step's copies completed before it returned)
     FLOCK_TRY(check_room(m, 1));
-    FLOCK_TRY(upload_ids(m, ids, 1));
+    if (ids[0] < 0 || ids[0] >= m->vocab) {
+      set_error("token id %d out of range 0..%d", ids[0], m->vocab - 1);
+      return FLOCK_E_ARG;
+    }
+    m->h_io[0] = ids[0];
+    FLOCK_CK(cudaMemcpyAsync(m->ids.p, m->h_io, 4, cudaMemcpyHostToDevice, m->dev->stream));
     FLOCK_TRY(launch_decode(m));
     m->pos += 1;
-  } else {
-    int last = 0;
-    FLOCK_TRY(encode_tokens(m, ids, n, &last));
-    FLOCK_TRY(enqueue_head(m, last - 1));
-    FLOCK_TRY(enqueue_record(m));
+    for (auto* L : m->layers) L->n_keys = m->pos;
+    FLOCK_CK(cudaMemcpyAsync(m->h_io + 1, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
+    FLOCK_TRY(sync_model(m));
+    *next_id = m->h_io[1];
+    return check_device_errors(m);
   }
+  int last = 0;
+  FLOCK_TRY(encode_tokens(m, ids, n, &last));
+  FLOCK_TRY(enqueue_head(m, last - 1));
+  FLOCK_TRY(enqueue_record(m));
   for (auto* L : m->layers) L->n_keys = m->pos;
   FLOCK_CK(cudaMemcpyAsync(next_id, m->ids.p, 4, cudaMemcpyDeviceToHost, m->dev->stream));
   FLOCK_TRY(sync_model(m));

@@ -114,6 +114,30 @@ def test_split_counts_bit_identical(dev, small):
     assert a.pos == b.pos == 330
 
 
+def test_engine_switches_around_multi_step_graphs(dev, small):
+    """Device-fed runs of 8 or more steps launch the kernel graph's 8-step
+    capture; switching the engine drops both captures and a later run
+    captures them again, and freeing the model releases them.  Ids follow a
+    model that stays on the persistent kernel, step for step."""
+    a = Model.create(dev, small, FAST)
+    ref = Model.create(dev, small, FAST)
+    ref.decode_mode = "persistent"
+    for M in (a, ref):
+        M.step([4, 8, 15, 16, 23])
+    got = a.decode_device(10).tolist()          # one 8-step launch + 2 single steps
+    a.decode_mode = "persistent"
+    got += a.decode_device(9).tolist()
+    a.decode_mode = "kernels"
+    got += a.decode_device(16).tolist()         # captured again
+    got.append(a.step([got[-1]]))              # the one-step graph after the run graph
+    want = ref.decode_device(35).tolist()
+    want.append(ref.step([want[-1]]))
+    assert got == want
+    assert a.pos == ref.pos == 5 + 36
+    a.free()
+    ref.free()
+
+
 def test_persistent_decode_device_history(dev, small):
     a, b = _pair(dev, small)
     for M in (a, b):
