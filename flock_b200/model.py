@@ -24,6 +24,12 @@ class Model:
                  keep: list):
         self.dev, self.handle, self.cfg, self.vocab, self.n_layers = dev, handle, cfg, vocab, n_layers
         self._keep = keep
+        # the one-token step's arguments, made once (the per-token loop of a
+        # caller feeding back each id converts no arrays)
+        self._one = (ctypes.c_int32 * 1)()
+        self._next = ctypes.c_int32()
+        self._next_ref = ctypes.byref(self._next)
+        self._step_fn = _abi.lib().flock_model_step
 
     @staticmethod
     def create(dev: Device, m, cfg: LayerConfig = QWEN3_06B, cut: int | None = None) -> "Model":
@@ -106,6 +112,11 @@ class Model:
     # -------------------------------------------------------------- decode
     def step(self, ids) -> int:
         """kernels/model.ts:387 -- feed ids, return the greedy next id."""
+        if (isinstance(ids, (list, tuple)) and len(ids) == 1 and
+                isinstance(ids[0], (int, np.integer)) and -2**31 <= int(ids[0]) < 2**31):
+            self._one[0] = int(ids[0])
+            _abi.check(self._step_fn(self.handle, self._one, 1, self._next_ref))
+            return self._next.value
         ids = self._ids(ids)
         out = ctypes.c_int32()
         _abi.call("flock_model_step", self.handle, _abi.ptr(ids, _abi._i32p), ids.size,

@@ -104,3 +104,20 @@ def test_device_open_without_gpu_is_an_error_not_a_crash(built):
     h = ctypes.c_void_p()
     rc = _abi.lib().flock_dev_open(0, ctypes.byref(h))
     assert rc != 0 and not h.value
+
+
+def test_one_token_step_reaches_the_abi(built):
+    """Model.step([id]) passes its prebuilt one-id argument straight to
+    flock_model_step: with no model behind the handle the library answers
+    with its argument error (raised as FlockError, not a ctypes TypeError);
+    ids outside int32 take the array path, as do longer id lists."""
+    from flock_b200.layer import QWEN3_06B
+    from flock_b200.model import Model
+    M = Model(None, None, QWEN3_06B, 4096, 0, [])
+    for ids in ([5], (7,), [np.int32(3)]):
+        with pytest.raises(_abi.FlockError) as e:
+            M.step(ids)
+        assert e.value.code == _abi.FLOCK_E_ARG
+    for ids in ([2**40], [1, 2]):
+        with pytest.raises(_abi.FlockError):
+            M.step(ids)
