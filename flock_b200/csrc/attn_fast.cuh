@@ -137,10 +137,15 @@ FLOCK_DEV AfRange af_range(const AttnFastArgs& a, int s, int pos) {
 // keys [t0, t0 + nt) of kv head g into the K / V tiles; position pos (this
 // token's key, not yet in the cache) is skipped: its row comes from the
 // projection.  L2-direct loads: the rows are earlier steps' appends.
+// KV: the cache element when known at compile time (0 f32, 1 bf16, 2 e4m3),
+// -1: read from the arguments
+template <int KV = -1>
 FLOCK_DEV void af_stage_tile(const AttnFastArgs& a, int g, int pos, int t0, int nt, float* dsm) {
+  const bool fp8 = KV < 0 ? a.kv_fp8 != 0 : KV == 2;
+  const bool bf16 = KV < 0 ? a.kv_bf16 != 0 : KV == 1;
   const int t = threadIdx.x;
   const size_t kvs = (size_t)a.n_kv_heads * 128;
-  if (a.kv_fp8) {
+  if (fp8) {
     // 8 x 128-bit loads per 128-byte e4m3 row, widened to f32 in the tiles
     for (int i = t; i < nt * 8; i += ATTN_FAST_THREADS) {
       const int j = i >> 3, c16 = i & 7, key = t0 + j;
@@ -153,7 +158,7 @@ FLOCK_DEV void af_stage_tile(const AttnFastArgs& a, int g, int pos, int t0, int 
     }
     return;
   }
-  if (a.kv_bf16) {
+  if (bf16) {
     // 16 x 128-bit loads per 256-byte bf16 row, widened to f32 in the tiles
     for (int i = t; i < nt * 16; i += ATTN_FAST_THREADS) {
       const int j = i >> 4, c8 = i & 15, key = t0 + j;
@@ -186,6 +191,7 @@ FLOCK_DEV void af_stage_tile(const AttnFastArgs& a, int g, int pos, int t0, int 
 // cannot keep the kernel that appended row pos - 1 (the same layer one step
 // earlier, ~5 x layers launches back) running while this one starts -- every
 // launch between them would have to be resident at once, waiting.
+template <int KV = -1>
 FLOCK_DEV void af_stage_static(const AttnFastArgs& a, int g, int s, int pos, float* dsm) {
   const int t = threadIdx.x;
   const AfRange r = af_range(a, s, pos);
@@ -199,12 +205,15 @@ FLOCK_DEV void af_stage_static(const AttnFastArgs& a, int g, int s, int pos, flo
       reinterpret_cast<float4*>(dsm + AF_CS)[t] =
           reinterpret_cast<const float4*>(a.rope_cs + (size_t)pos * 64)[t];
   }
-  af_stage_tile(a, g, pos, r.k0, min(r.nk, ATTN_TILE), dsm);
+  af_stage_tile<KV>(a, g, pos, r.k0, min(r.nk, ATTN_TILE), dsm);
 }
 
 // What the step's earlier kernels wrote: the raw q/k/v projection (fused
 // norm + RoPE), or the normalised q and the appended k/v row at pos.
+template <int KV = -1>
 FLOCK_DEV void af_stage_step(const AttnFastArgs& a, int g, int pos, float* dsm) {
+  const bool fp8 = KV < 0 ? a.kv_fp8 != 0 : KV == 2;
+  const bool bf16 = KV < 0 ? a.kv_bf16 != 0 : KV == 1;
   const int G = a.n_heads / a.n_kv_heads;
   const int t = threadIdx.x;
   const float* qsrc = a.q + (size_t)g * G * 128;
@@ -219,14 +228,14 @@ FLOCK_DEV void af_stage_step(const AttnFastArgs& a, int g, int pos, float* dsm) 
     return;
   }
   const size_t off = (size_t)pos * a.n_kv_heads * 128 + (size_t)g * 128;
-  if (a.kv_fp8) {
+  if (fp8) {
     if (t < 8) {
       fp8x16_widen(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.kcache) + off) + t),
                    dsm + AF_KNEW + 16 * t);
       fp8x16_widen(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.vcache) + off) + t),
                    dsm + AF_VNEW + 16 * t);
     }
-  } else if (a.kv_bf16) {
+  } else if (bf16) {
     if (t < 16) {
       bf16x8_widen(__ldcg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.kcache) + off) + t),
                    dsm + AF_KNEW + 8 * t);
@@ -275,9 +284,11 @@ FLOCK_DEV float af_combine16(int splits, Get get) {
 // flag.  `pos` is the position of the token being decoded.  The caller has
 // run af_stage_static and af_stage_step for (g, s, pos) -- the first of them
 // possibly before its dependency wait -- without a barrier after them.
-template <typename Sync>
+template <typename Sync, int KV = -1>
 FLOCK_DEV void attn_fast_run(const AttnFastArgs& a, int g, int s, int pos, float* dsm,
                              bool* last_flag, Sync sync) {
+  const bool fp8 = KV < 0 ? a.kv_fp8 != 0 : KV == 2;
+  const bool bf16 = KV < 0 ? a.kv_bf16 != 0 : KV == 1;
   const int G = a.n_heads / a.n_kv_heads;  // <= 4
   const int t = threadIdx.x;
   const int lane = t & 31, warp = t >> 5;
@@ -321,7 +332,7 @@ FLOCK_DEV void attn_fast_run(const AttnFastArgs& a, int g, int s, int pos, float
     }
     sync();
     const size_t off = (size_t)pos * kvs + (size_t)g * hd + t;
-    if (a.kv_fp8) {
+    if (fp8) {
       // as with bf16: every split rounds its own copy, split 0 appends it
       if (t < 128) {
         const uint8_t kb = fp8_bits(knew[t]), vb = fp8_bits(vnew[t]);
@@ -333,7 +344,7 @@ FLOCK_DEV void attn_fast_run(const AttnFastArgs& a, int g, int s, int pos, float
         }
       }
       sync();
-    } else if (a.kv_bf16) {
+    } else if (bf16) {
       // every split rounds its own copy of the new key/value, so the scores
       // see the value the cache keeps; split 0 appends it
       if (t < 128) {
@@ -364,7 +375,7 @@ FLOCK_DEV void attn_fast_run(const AttnFastArgs& a, int g, int s, int pos, float
     const int nt = min(ATTN_TILE, k1 - t0);
     if (t0 != k0) {
       sync();
-      af_stage_tile(a, g, pos, t0, nt, dsm);
+      af_stage_tile<KV>(a, g, pos, t0, nt, dsm);
     }
     // the new key/value live in shared memory, not (yet) in the cache
     if (pos >= t0 && pos < t0 + nt && t < 128) {
@@ -526,6 +537,10 @@ struct BlockSync {
 // holds then (the step's position for every layer but the first, whose
 // earlier kernel advances it); after the wait it reads the position with the
 // projection and restages if the position moved.
+// KV: the cache element (0 f32, 1 bf16, 2 e4m3) as a compile-time constant,
+// so each instance holds only its own cache paths (what runs after the wait
+// is bound by instruction fetch; a smaller hot path misses less).
+template <int KV>
 static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(const AttnFastArgs a) {
   extern __shared__ __align__(16) float dsm[];
   __shared__ bool last;
@@ -534,7 +549,7 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
   const int g = blockIdx.x, s = blockIdx.y;
   const int guess = *(volatile const int*)a.ctl;
   const bool pre = guess >= 0 && guess < a.max_keys && s < attn_splits_for(guess + 1, a.splits);
-  if (pre) af_stage_static(a, g, s, guess, dsm);
+  if (pre) af_stage_static<KV>(a, g, s, guess, dsm);
   pdl_wait();
   // the raw projection's addresses do not depend on the position: with the
   // fused norm its loads go out together with the position's (one round
@@ -560,11 +575,11 @@ static __global__ void __launch_bounds__(ATTN_FAST_THREADS) k_attn_decode_fast(c
         reinterpret_cast<float4*>(dsm + AF_VRAW)[t] = vr;
       }
     } else {
-      af_stage_step(a, g, pos, dsm);
+      af_stage_step<KV>(a, g, pos, dsm);
     }
-    if (!pre || pos != guess) af_stage_static(a, g, s, pos, dsm);
+    if (!pre || pos != guess) af_stage_static<KV>(a, g, s, pos, dsm);
   }
-  attn_fast_run(a, g, s, pos, dsm, &last, BlockSync{});
+  attn_fast_run<BlockSync, KV>(a, g, s, pos, dsm, &last, BlockSync{});
 }
 
 inline size_t attn_fast_smem(int /*chunk_cap*/) { return (size_t)AF_END * 4; }

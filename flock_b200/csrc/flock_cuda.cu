@@ -749,9 +749,11 @@ int layer_enqueue(flock_layer* L, int n, bool advance, const PrefetchList& pf_ne
     pf_add(a.pf, L->w[W_UP]);
     const size_t smem = attn_fast_smem(a.chunk_cap);
     // all shared memory: a long cache's splits run three 75 KB CTAs per SM
-    FLOCK_TRY(kernel_setup((const void*)k_attn_decode_fast, 200 * 1024,
-                           cudaSharedmemCarveoutMaxShared));
-    FLOCK_CK(launch_ex(d->stream, k_attn_decode_fast, dim3(c.n_kv_heads, a.splits),
+    auto kaf = c.kv_dtype == FLOCK_KV_FP8    ? k_attn_decode_fast<FLOCK_KV_FP8>
+               : c.kv_dtype == FLOCK_KV_BF16 ? k_attn_decode_fast<FLOCK_KV_BF16>
+                                             : k_attn_decode_fast<FLOCK_KV_F32>;
+    FLOCK_TRY(kernel_setup((const void*)kaf, 200 * 1024, cudaSharedmemCarveoutMaxShared));
+    FLOCK_CK(launch_ex(d->stream, kaf, dim3(c.n_kv_heads, a.splits),
                        dim3(ATTN_FAST_THREADS), smem, pdl, a));
   } else {
     FLOCK_TRY(enqueue_qk_attn(L, n, pdl, false));
@@ -1324,9 +1326,10 @@ int flock_op_attention(flock_dev* d, const float* q, const float* k, const float
     a.combine = 1;
     const size_t smem = attn_fast_smem(a.chunk_cap);
     if (smem > 200 * 1024) return FLOCK_E_UNSUPPORTED;
-    FLOCK_CK(cudaFuncSetAttribute(k_attn_decode_fast, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  200 * 1024));
-    k_attn_decode_fast<<<dim3(n_kv_heads, splits), ATTN_FAST_THREADS, smem, d->stream>>>(a);
+    FLOCK_CK(cudaFuncSetAttribute(k_attn_decode_fast<FLOCK_KV_F32>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    k_attn_decode_fast<FLOCK_KV_F32>
+        <<<dim3(n_kv_heads, splits), ATTN_FAST_THREADS, smem, d->stream>>>(a);
     FLOCK_CK(cudaGetLastError());
   }
   FLOCK_CK(cudaMemcpyAsync(out, to.b.p, (size_t)n_heads * head_dim * 4, cudaMemcpyDeviceToHost,
